@@ -1,0 +1,290 @@
+// Python bindings of the sigma0_b200 CUDA extension (module sigma0_b200._C).
+//
+// Tensor checks, allocation and stream selection live here; the .cu files hold
+// torch-free kernels and raw-pointer launchers (launchers.h).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <vector>
+
+#include "launchers.h"
+
+namespace {
+
+constexpr int M3_N = 128, M3_P = 64, M3_R = 32;
+
+int num_sms(const at::Tensor& t) {
+  return at::cuda::getDeviceProperties(t.device().index())->multiProcessorCount;
+}
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+
+void req(const at::Tensor& t, at::ScalarType dt, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == dt, name, " has the wrong dtype");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+M3Geo m3_geo(const at::Tensor& proj, int64_t B, int64_t L, int64_t nh) {
+  req(proj, at::kBFloat16, "proj");
+  TORCH_CHECK(proj.size(-1) % 8 == 0, "proj row stride must be a multiple of 8");
+  TORCH_CHECK(proj.size(-1) >= 2 * nh * M3_P + 2 * M3_N + 3 * nh + M3_R, "proj too narrow for the layout");
+  TORCH_CHECK(proj.numel() == B * L * proj.size(-1), "proj shape does not match B*L rows");
+  M3Geo g;
+  g.B = (int)B; g.L = (int)L; g.nh = (int)nh; g.ldp = (int)proj.size(-1);
+  return g;
+}
+
+M3Scan m3_scan(const at::Tensor& proj, const std::vector<at::Tensor>& pre, const at::Tensor& Bb,
+               const at::Tensor& Cb, const at::Tensor& D) {
+  M3Scan s;
+  s.proj = proj.data_ptr();
+  s.bc = pre[0].data_ptr();
+  s.dt = pre[1].data_ptr<float>();
+  s.adt = pre[2].data_ptr<float>();
+  s.sig = pre[3].data_ptr<float>();
+  s.rate = pre[4].data_ptr<float>();
+  s.Bb = Bb.data_ptr<float>();
+  s.Cb = Cb.data_ptr<float>();
+  s.D = D.data_ptr<float>();
+  return s;
+}
+
+std::vector<at::Tensor> m3_prep_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh, at::Tensor wB,
+                                    at::Tensor wC, at::Tensor dt_bias, double A_floor, double eps) {
+  c10::cuda::CUDAGuard guard(proj.device());
+  M3Geo g = m3_geo(proj, B, L, nh);
+  auto f32 = proj.options().dtype(at::kFloat);
+  auto bc = at::empty({B * L, 2 * M3_N}, proj.options());
+  auto dt = at::empty({B, nh, L}, f32), adt = at::empty({B, nh, L}, f32), sig = at::empty({B, nh, L}, f32);
+  auto rate = at::empty({B * L, M3_R}, f32);
+  m3_prep_fwd_launch(g, proj.data_ptr(), wB.data_ptr<float>(), wC.data_ptr<float>(), dt_bias.data_ptr<float>(),
+                     (float)A_floor, (float)eps, bc.data_ptr(), dt.data_ptr<float>(), adt.data_ptr<float>(),
+                     sig.data_ptr<float>(), rate.data_ptr<float>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {bc, dt, adt, sig, rate};
+}
+
+std::vector<at::Tensor> m3_ssd_fwd(at::Tensor proj, std::vector<at::Tensor> pre, at::Tensor Bb, at::Tensor Cb,
+                                   at::Tensor D, int64_t B, int64_t L, int64_t nh, bool write_y, bool store) {
+  c10::cuda::CUDAGuard guard(proj.device());
+  M3Geo g = m3_geo(proj, B, L, nh);
+  TORCH_CHECK(write_y || store, "nothing to compute");
+  int nc = m3_nchunks((int)L);
+  at::Tensor y, states, theta0;
+  if (write_y) y = at::empty({B, L, nh * M3_P}, proj.options());
+  if (store) {
+    states = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
+    theta0 = at::empty({B, nh, nc, M3_R}, proj.options().dtype(at::kFloat));
+  }
+  m3_ssd_fwd_launch(g, m3_scan(proj, pre, Bb, Cb, D), write_y ? y.data_ptr() : nullptr,
+                    store ? states.data_ptr() : nullptr, store ? theta0.data_ptr<float>() : nullptr, stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {y, states, theta0};
+}
+
+std::vector<at::Tensor> m3_ssd_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC,
+                                   at::Tensor dt_bias, at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B,
+                                   int64_t L, int64_t nh, double A_floor, double eps) {
+  c10::cuda::CUDAGuard guard(proj.device());
+  M3Geo g = m3_geo(proj, B, L, nh);
+  req(dy, at::kBFloat16, "dy");
+  auto pre = m3_prep_fwd(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
+  auto st = m3_ssd_fwd(proj, pre, Bb, Cb, D, B, L, nh, false, true);
+  auto f32 = proj.options().dtype(at::kFloat);
+  auto dproj = at::empty_like(proj);
+  auto gQ = at::empty({B * L, nh, M3_N}, proj.options());
+  auto gK = at::empty({B * L, nh, M3_N}, proj.options());
+  auto gAng = at::empty({B * L, nh, M3_R}, f32);
+  auto dgam = at::empty({B, nh, L}, f32), dscl = at::empty({B, nh, L}, f32), ddt = at::empty({B, nh, L}, f32),
+       dadt = at::empty({B, nh, L}, f32);
+  auto dD = at::empty({B, nh}, f32), dCb = at::empty({B, nh, M3_N}, f32), dBb = at::empty({B, nh, M3_N}, f32);
+  M3BwdOut o;
+  o.dproj = dproj.data_ptr();
+  o.gQ = gQ.data_ptr();
+  o.gK = gK.data_ptr();
+  o.gAng = gAng.data_ptr<float>();
+  o.dgam = dgam.data_ptr<float>();
+  o.dscl = dscl.data_ptr<float>();
+  o.ddt = ddt.data_ptr<float>();
+  o.dadt = dadt.data_ptr<float>();
+  o.dD = dD.data_ptr<float>();
+  o.dCb = dCb.data_ptr<float>();
+  o.dBb = dBb.data_ptr<float>();
+  m3_ssd_bwd_launch(g, m3_scan(proj, pre, Bb, Cb, D), dy.data_ptr(), st[1].data_ptr(), st[2].data_ptr<float>(), o,
+                    stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  auto dwB = at::zeros({M3_N}, f32), dwC = at::zeros({M3_N}, f32), ddtb = at::zeros({nh}, f32);
+  m3_prep_bwd_launch(g, proj.data_ptr(), wB.data_ptr<float>(), wC.data_ptr<float>(), dt_bias.data_ptr<float>(),
+                     (float)A_floor, (float)eps, gQ.data_ptr(), gK.data_ptr(), gAng.data_ptr<float>(),
+                     dgam.data_ptr<float>(), dscl.data_ptr<float>(), ddt.data_ptr<float>(), dadt.data_ptr<float>(),
+                     dproj.data_ptr(), dwB.data_ptr<float>(), dwC.data_ptr<float>(), ddtb.data_ptr<float>(),
+                     stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dproj, dwB, dwC, ddtb, dD.sum(0), dCb.sum(0), dBb.sum(0)};
+}
+
+// ---- row / elementwise ------------------------------------------------------------------
+std::vector<at::Tensor> ln_fwd(at::Tensor x, at::Tensor w, at::Tensor b, double eps) {
+  req(x, at::kFloat, "x");
+  c10::cuda::CUDAGuard guard(x.device());
+  int64_t D = x.size(-1), T = x.numel() / D;
+  TORCH_CHECK(D <= 2048, "LayerNorm width above 2048 is not supported");
+  auto y = at::empty(x.sizes(), x.options().dtype(at::kBFloat16));
+  auto mean = at::empty({T}, x.options()), rstd = at::empty({T}, x.options());
+  ln_fwd_launch(x.data_ptr<float>(), w.data_ptr<float>(), b.data_ptr<float>(), y.data_ptr(), mean.data_ptr<float>(),
+                rstd.data_ptr<float>(), T, (int)D, (float)eps, num_sms(x), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {y, mean, rstd};
+}
+
+std::vector<at::Tensor> ln_bwd(at::Tensor dy, at::Tensor x, at::Tensor mean, at::Tensor rstd, at::Tensor w,
+                               c10::optional<at::Tensor> dres) {
+  req(dy, at::kBFloat16, "dy");
+  req(x, at::kFloat, "x");
+  c10::cuda::CUDAGuard guard(x.device());
+  int64_t D = x.size(-1), T = x.numel() / D;
+  auto dx = at::empty_like(x);
+  auto dw = at::zeros({D}, x.options()), db = at::zeros({D}, x.options());
+  const float* r = nullptr;
+  if (dres.has_value() && dres->defined()) {
+    req(*dres, at::kFloat, "dres");
+    r = dres->data_ptr<float>();
+  }
+  ln_bwd_launch(dy.data_ptr(), x.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+                w.data_ptr<float>(), r, dx.data_ptr<float>(), dw.data_ptr<float>(), db.data_ptr<float>(), T, (int)D,
+                num_sms(x), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dx, dw, db};
+}
+
+std::vector<at::Tensor> rms_fwd(at::Tensor x, at::Tensor w, double eps) {
+  req(x, at::kBFloat16, "x");
+  c10::cuda::CUDAGuard guard(x.device());
+  int64_t D = x.size(-1), T = x.numel() / D;
+  TORCH_CHECK(D % 8 == 0 && D <= 2048, "RMSNorm width must be a multiple of 8, at most 2048");
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({T}, x.options().dtype(at::kFloat));
+  rms_fwd_launch(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), rstd.data_ptr<float>(), T, (int)D, (float)eps,
+                 num_sms(x), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {y, rstd};
+}
+
+std::vector<at::Tensor> rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd) {
+  req(dy, at::kBFloat16, "dy");
+  req(x, at::kBFloat16, "x");
+  c10::cuda::CUDAGuard guard(x.device());
+  int64_t D = x.size(-1), T = x.numel() / D;
+  auto dx = at::empty_like(x);
+  auto dw = at::zeros({D}, x.options().dtype(at::kFloat));
+  rms_bwd_launch(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
+                 dw.data_ptr<float>(), T, (int)D, num_sms(x), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dx, dw};
+}
+
+at::Tensor gelu_fwd(at::Tensor o) {
+  req(o, at::kBFloat16, "o");
+  TORCH_CHECK(o.numel() % 8 == 0, "numel must be a multiple of 8");
+  c10::cuda::CUDAGuard guard(o.device());
+  auto g = at::empty_like(o);
+  gelu_fwd_launch(o.data_ptr(), g.data_ptr(), o.numel(), num_sms(o), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return g;
+}
+
+at::Tensor glu_res_fwd(at::Tensor x, at::Tensor g, at::Tensor h, at::Tensor b) {
+  req(x, at::kFloat, "x");
+  req(g, at::kBFloat16, "g");
+  req(h, at::kBFloat16, "h");
+  int64_t D = x.size(-1);
+  TORCH_CHECK(D % 8 == 0, "width must be a multiple of 8");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto out = at::empty_like(x);
+  glu_res_fwd_launch(x.data_ptr<float>(), g.data_ptr(), h.data_ptr(), b.data_ptr<float>(), out.data_ptr<float>(),
+                     x.numel(), (int)D, num_sms(x), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+std::vector<at::Tensor> glu_res_bwd(at::Tensor dout, at::Tensor g, at::Tensor h, at::Tensor b) {
+  req(dout, at::kFloat, "dout");
+  int64_t D = dout.size(-1), T = dout.numel() / D;
+  c10::cuda::CUDAGuard guard(dout.device());
+  auto dh = at::empty(dout.sizes(), dout.options().dtype(at::kBFloat16));
+  auto dgp = at::empty_like(dout);
+  auto db = at::zeros({D}, dout.options());
+  glu_res_bwd_launch(dout.data_ptr<float>(), g.data_ptr(), h.data_ptr(), b.data_ptr<float>(), dh.data_ptr(),
+                     dgp.data_ptr<float>(), db.data_ptr<float>(), T, (int)D, num_sms(dout), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dh, dgp, db};
+}
+
+at::Tensor gelu_bwd(at::Tensor o, at::Tensor dgp, at::Tensor dgm) {
+  req(o, at::kBFloat16, "o");
+  req(dgp, at::kFloat, "dgp");
+  req(dgm, at::kBFloat16, "dgm");
+  c10::cuda::CUDAGuard guard(o.device());
+  auto d = at::empty_like(o);
+  gelu_bwd_launch(o.data_ptr(), dgp.data_ptr<float>(), dgm.data_ptr(), d.data_ptr(), o.numel(), num_sms(o),
+                  stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return d;
+}
+
+// logits [T, ld] bf16 (first V columns used) is overwritten with w[row]*(softmax - onehot).
+at::Tensor ce_fwd_bwd(at::Tensor logits, c10::optional<at::Tensor> bias, at::Tensor labels,
+                      c10::optional<at::Tensor> wrow, int64_t V) {
+  req(logits, at::kBFloat16, "logits");
+  req(labels, at::kLong, "labels");
+  c10::cuda::CUDAGuard guard(logits.device());
+  int64_t T = logits.size(0), ld = logits.size(1);
+  auto loss = at::empty({T}, logits.options().dtype(at::kFloat));
+  const float* bp = (bias.has_value() && bias->defined()) ? bias->data_ptr<float>() : nullptr;
+  const float* wp = (wrow.has_value() && wrow->defined()) ? wrow->data_ptr<float>() : nullptr;
+  ce_launch(logits.data_ptr(), bp, labels.data_ptr<int64_t>(), wp, loss.data_ptr<float>(), T, (int)V, (int)ld,
+            stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return loss;
+}
+
+void sumsq(at::Tensor g, at::Tensor out) {
+  req(g, at::kFloat, "g");
+  c10::cuda::CUDAGuard guard(g.device());
+  sumsq_launch(g.data_ptr<float>(), g.numel(), out.data_ptr<float>(), num_sms(g), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void adam(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> pb,
+          c10::optional<at::Tensor> sumsq_t, double max_norm, at::Tensor lr, double b1, double b2, double eps,
+          double wd, double bc1, double bc2) {
+  req(p, at::kFloat, "p");
+  req(g, at::kFloat, "g");
+  c10::cuda::CUDAGuard guard(p.device());
+  void* pbp = (pb.has_value() && pb->defined()) ? pb->data_ptr() : nullptr;
+  const float* ss = (sumsq_t.has_value() && sumsq_t->defined()) ? sumsq_t->data_ptr<float>() : nullptr;
+  adam_launch(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), pbp, p.numel(), ss,
+              (float)max_norm, lr.data_ptr<float>(), (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1,
+              (float)bc2, num_sms(p), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sigma0_b200 sm_100a kernels";
+  m.def("m3_prep_fwd", &m3_prep_fwd);
+  m.def("m3_ssd_fwd", &m3_ssd_fwd);
+  m.def("m3_ssd_bwd", &m3_ssd_bwd);
+  m.def("ln_fwd", &ln_fwd);
+  m.def("ln_bwd", &ln_bwd);
+  m.def("rms_fwd", &rms_fwd);
+  m.def("rms_bwd", &rms_bwd);
+  m.def("gelu_fwd", &gelu_fwd);
+  m.def("glu_res_fwd", &glu_res_fwd);
+  m.def("glu_res_bwd", &glu_res_bwd);
+  m.def("gelu_bwd", &gelu_bwd);
+  m.def("ce_fwd_bwd", &ce_fwd_bwd);
+  m.def("sumsq", &sumsq);
+  m.def("adam", &adam);
+}

@@ -1,0 +1,517 @@
+// Fused row-wise kernels of the residual block, the loss and the optimizer (sm_100a).
+//
+//  ln_fwd / ln_bwd          LayerNorm (fp32 residual in, bf16 out) and its backward fused
+//                           with the residual add; scale/bias grads reduced per block
+//  rms_fwd / rms_bwd        RMSNorm over d_inner (bf16 in/out), the out_norm of Mamba3
+//  gelu_fwd                 tanh-GELU (the reference uses flax's approximate gelu)
+//  glu_res_fwd / _bwd       out = x + g * sigmoid(h + b)  (half_glu1 gate + residual)
+//  gelu_bwd                 d o = (dg_gate + dg_mm) * gelu'(o)
+//  ce_fwd_bwd               per-row log-softmax cross-entropy and its logit gradient,
+//                           written in place over the bf16 logits
+//  sumsq / adam_step        global-norm clip + Adam/AdamW update of a flat fp32 buffer,
+//                           writing the bf16 compute copy in the same pass
+//
+// The GELU tanh approximation uses the published constants of Hendrycks & Gimpel
+// (sqrt(2/pi), 0.044715).  Row kernels are one warp per row; column (parameter)
+// reductions accumulate per warp over a grid-stride row loop, then one atomicAdd
+// per column per warp.
+#include "common.cuh"
+#include "launchers.h"
+
+namespace s0 {
+namespace ops {
+
+using bf16 = __nv_bfloat16;
+constexpr float K_GELU = 0.7978845608028654f;   // sqrt(2/pi)
+constexpr float C_GELU = 0.044715f;
+
+S0_DEV float gelu_t(float x) {
+  float u = K_GELU * (x + C_GELU * x * x * x);
+  return 0.5f * x * (1.f + tanhf(u));
+}
+S0_DEV float gelu_t_grad(float x) {
+  float u = K_GELU * (x + C_GELU * x * x * x);
+  float th = tanhf(u);
+  return 0.5f * (1.f + th) + 0.5f * x * (1.f - th * th) * K_GELU * (1.f + 3.f * C_GELU * x * x);
+}
+
+// Max 64 columns per lane (D <= 2048).
+constexpr int MAXV = 64;
+
+// ---------------------------------------------------------------------------
+// LayerNorm forward: x fp32 [T, D] -> y bf16, mean/rstd fp32 [T]
+// ---------------------------------------------------------------------------
+template <int VPL>
+__global__ void ln_fwd_k(const float* __restrict__ x, const float* __restrict__ w,
+                         const float* __restrict__ b, bf16* __restrict__ y, float* __restrict__ mean,
+                         float* __restrict__ rstd, int T, int D, float eps) {
+  int lane = threadIdx.x & 31;
+  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int row = gw; row < T; row += nw) {
+    const float* xr = x + (size_t)row * D;
+    float v[VPL];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int c = lane + 32 * i;
+      v[i] = c < D ? xr[c] : 0.f;
+      s += v[i];
+    }
+    s = warp_sum(s);
+    float mu = s / D;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int c = lane + 32 * i;
+      float d = c < D ? v[i] - mu : 0.f;
+      q += d * d;
+    }
+    q = warp_sum(q);
+    float r = rsqrtf(q / D + eps);
+    bf16* yr = y + (size_t)row * D;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int c = lane + 32 * i;
+      if (c < D) yr[c] = __float2bfloat16((v[i] - mu) * r * w[c] + b[c]);
+    }
+    if (lane == 0) { mean[row] = mu; rstd[row] = r; }
+  }
+}
+
+// LayerNorm backward fused with the residual: dx = dres + LN'(dy); dw, db accumulated.
+template <int VPL>
+__global__ void ln_bwd_k(const bf16* __restrict__ dy, const float* __restrict__ x,
+                         const float* __restrict__ mean, const float* __restrict__ rstd,
+                         const float* __restrict__ w, const float* __restrict__ dres,
+                         float* __restrict__ dx, float* __restrict__ dw, float* __restrict__ db, int T,
+                         int D) {
+  int lane = threadIdx.x & 31;
+  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  float aw[VPL], ab[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) { aw[i] = 0.f; ab[i] = 0.f; }
+  for (int row = gw; row < T; row += nw) {
+    const float* xr = x + (size_t)row * D;
+    const bf16* gr = dy + (size_t)row * D;
+    float mu = mean[row], r = rstd[row];
+    float xh[VPL], gw_[VPL];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int c = lane + 32 * i;
+      float g = c < D ? __bfloat162float(gr[c]) : 0.f;
+      xh[i] = c < D ? (xr[c] - mu) * r : 0.f;
+      gw_[i] = c < D ? g * w[c] : 0.f;
+      s1 += gw_[i];
+      s2 += gw_[i] * xh[i];
+      aw[i] += g * xh[i];
+      ab[i] += g;
+    }
+    s1 = warp_sum(s1) / D;
+    s2 = warp_sum(s2) / D;
+    float* dxr = dx + (size_t)row * D;
+    const float* rr = dres ? dres + (size_t)row * D : nullptr;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int c = lane + 32 * i;
+      if (c < D) dxr[c] = (rr ? rr[c] : 0.f) + r * (gw_[i] - s1 - xh[i] * s2);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    int c = lane + 32 * i;
+    if (c < D) {
+      atomicAdd(&dw[c], aw[i]);
+      atomicAdd(&db[c], ab[i]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm over bf16 rows (out_norm): y = x * rsqrt(mean(x^2)+eps) * w
+// ---------------------------------------------------------------------------
+__global__ void rms_fwd_k(const bf16* __restrict__ x, const float* __restrict__ w, bf16* __restrict__ y,
+                          float* __restrict__ rstd, int T, int D, float eps) {
+  int lane = threadIdx.x & 31;
+  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int row = gw; row < T; row += nw) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
+    uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * D);
+    int nv = D / 8;
+    float s = 0.f;
+    for (int c = lane; c < nv; c += 32) {
+      uint4 u = xr[c];
+      uint32_t a[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) { float2 f = unpack_bf16(a[k]); s += f.x * f.x + f.y * f.y; }
+    }
+    s = warp_sum(s);
+    float r = rsqrtf(s / D + eps);
+    for (int c = lane; c < nv; c += 32) {
+      uint4 u = xr[c];
+      uint32_t a[4] = {u.x, u.y, u.z, u.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 f = unpack_bf16(a[k]);
+        int col = c * 8 + 2 * k;
+        o[k] = pack_bf16(f.x * r * w[col], f.y * r * w[col + 1]);
+      }
+      yr[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    if (lane == 0) rstd[row] = r;
+  }
+}
+
+template <int PER>
+__global__ void rms_bwd_k(const bf16* __restrict__ dy, const bf16* __restrict__ x, const float* __restrict__ w,
+                          const float* __restrict__ rstd, bf16* __restrict__ dx, float* __restrict__ dw, int T,
+                          int D) {
+  int lane = threadIdx.x & 31;
+  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  int nv = D / 8;   // uint4 chunks per row; lane handles chunks lane + 32*j
+  float aw[PER * 8];
+#pragma unroll
+  for (int i = 0; i < PER * 8; ++i) aw[i] = 0.f;
+  for (int row = gw; row < T; row += nw) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
+    const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * D);
+    float r = rstd[row];
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      int c = lane + 32 * j;
+      if (c < nv) {
+        uint4 ux = xr[c], ug = gr[c];
+        uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          int col = c * 8 + 2 * k;
+          m += fg.x * w[col] * fx.x + fg.y * w[col + 1] * fx.y;
+          aw[j * 8 + 2 * k] += fg.x * fx.x * r;
+          aw[j * 8 + 2 * k + 1] += fg.y * fx.y * r;
+        }
+      }
+    }
+    m = warp_sum(m) / D;
+    uint4* dr = reinterpret_cast<uint4*>(dx + (size_t)row * D);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      int c = lane + 32 * j;
+      if (c < nv) {
+        uint4 ux = xr[c], ug = gr[c];
+        uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w}, o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          int col = c * 8 + 2 * k;
+          float d0 = r * fg.x * w[col] - fx.x * r * r * r * m;
+          float d1 = r * fg.y * w[col + 1] - fx.y * r * r * r * m;
+          o[k] = pack_bf16(d0, d1);
+        }
+        dr[c] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    int c = lane + 32 * j;
+    if (c < nv)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) atomicAdd(&dw[c * 8 + k], aw[j * 8 + k]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// elementwise GELU / gate (vectorised by 8 bf16)
+// ---------------------------------------------------------------------------
+__global__ void gelu_fwd_k(const bf16* __restrict__ o, bf16* __restrict__ g, long n8) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    uint4 u = reinterpret_cast<const uint4*>(o)[i];
+    uint32_t a[4] = {u.x, u.y, u.z, u.w}, r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f = unpack_bf16(a[k]);
+      r[k] = pack_bf16(gelu_t(f.x), gelu_t(f.y));
+    }
+    reinterpret_cast<uint4*>(g)[i] = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+
+// out = x + g * sigmoid(h + b)      (x, out fp32; g, h bf16; b fp32 [D])
+__global__ void glu_res_fwd_k(const float* __restrict__ x, const bf16* __restrict__ g,
+                              const bf16* __restrict__ h, const float* __restrict__ b,
+                              float* __restrict__ out, long n8, int D) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    uint4 ug = reinterpret_cast<const uint4*>(g)[i], uh = reinterpret_cast<const uint4*>(h)[i];
+    uint32_t ag[4] = {ug.x, ug.y, ug.z, ug.w}, ah[4] = {uh.x, uh.y, uh.z, uh.w};
+    float4 x0 = reinterpret_cast<const float4*>(x)[2 * i], x1 = reinterpret_cast<const float4*>(x)[2 * i + 1];
+    float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w}, ov[8];
+    int col = (int)((i * 8) % D);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 fg = unpack_bf16(ag[k]), fh = unpack_bf16(ah[k]);
+      ov[2 * k] = xv[2 * k] + fg.x * sigmoidf_(fh.x + b[col + 2 * k]);
+      ov[2 * k + 1] = xv[2 * k + 1] + fg.y * sigmoidf_(fh.y + b[col + 2 * k + 1]);
+    }
+    reinterpret_cast<float4*>(out)[2 * i] = make_float4(ov[0], ov[1], ov[2], ov[3]);
+    reinterpret_cast<float4*>(out)[2 * i + 1] = make_float4(ov[4], ov[5], ov[6], ov[7]);
+  }
+}
+
+// dh = dout * g * s(1-s) (bf16), dgp = dout * s (fp32), db accumulated; rows of D columns.
+template <int VPL>
+__global__ void glu_res_bwd_k(const float* __restrict__ dout, const bf16* __restrict__ g,
+                              const bf16* __restrict__ h, const float* __restrict__ b,
+                              bf16* __restrict__ dh, float* __restrict__ dgp, float* __restrict__ db,
+                              int T, int D) {
+  int lane = threadIdx.x & 31;
+  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  float ab[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) ab[i] = 0.f;
+  for (int row = gw; row < T; row += nw) {
+    size_t o = (size_t)row * D;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int c = lane + 32 * i;
+      if (c < D) {
+        float gg = __bfloat162float(g[o + c]);
+        float s = sigmoidf_(__bfloat162float(h[o + c]) + b[c]);
+        float d = dout[o + c];
+        float v = d * gg * s * (1.f - s);
+        dh[o + c] = __float2bfloat16(v);
+        dgp[o + c] = d * s;
+        ab[i] += v;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    int c = lane + 32 * i;
+    if (c < D) atomicAdd(&db[c], ab[i]);
+  }
+}
+
+// do = (dgp + dgm) * gelu'(o)  -> bf16
+__global__ void gelu_bwd_k(const bf16* __restrict__ o, const float* __restrict__ dgp,
+                           const bf16* __restrict__ dgm, bf16* __restrict__ dout, long n8) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    uint4 uo = reinterpret_cast<const uint4*>(o)[i], um = reinterpret_cast<const uint4*>(dgm)[i];
+    uint32_t ao[4] = {uo.x, uo.y, uo.z, uo.w}, am[4] = {um.x, um.y, um.z, um.w}, r[4];
+    float4 p0 = reinterpret_cast<const float4*>(dgp)[2 * i], p1 = reinterpret_cast<const float4*>(dgp)[2 * i + 1];
+    float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 fo = unpack_bf16(ao[k]), fm = unpack_bf16(am[k]);
+      r[k] = pack_bf16((pv[2 * k] + fm.x) * gelu_t_grad(fo.x), (pv[2 * k + 1] + fm.y) * gelu_t_grad(fo.y));
+    }
+    reinterpret_cast<uint4*>(dout)[i] = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Cross-entropy over bf16 logits (+ fp32 bias), one block per row.
+// loss[row] = lse - logit[label]; logits <- w[row] * (softmax - onehot) in place.
+// ---------------------------------------------------------------------------
+__global__ void ce_fwd_bwd_k(bf16* __restrict__ logits, const float* __restrict__ bias,
+                             const int64_t* __restrict__ labels, const float* __restrict__ wrow,
+                             float* __restrict__ loss, int V, int ld) {
+  int row = blockIdx.x;
+  bf16* lr = logits + (size_t)row * ld;
+  __shared__ float red[32];
+  int tid = threadIdx.x, nt = blockDim.x;
+  float mx = -INFINITY, se = 0.f;
+  for (int c = tid; c < V; c += nt) {
+    float v = __bfloat162float(lr[c]) + (bias ? bias[c] : 0.f);
+    if (v > mx) { se = se * __expf(mx - v) + 1.f; mx = v; }
+    else se += __expf(v - mx);
+  }
+  // block reduce of (mx, se)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float m2 = __shfl_xor_sync(0xffffffffu, mx, o), s2 = __shfl_xor_sync(0xffffffffu, se, o);
+    float m = fmaxf(mx, m2);
+    se = (mx == -INFINITY ? 0.f : se * __expf(mx - m)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - m));
+    mx = m;
+  }
+  __shared__ float smx[32], sse[32];
+  int w = tid >> 5, lane = tid & 31;
+  if (lane == 0) { smx[w] = mx; sse[w] = se; }
+  __syncthreads();
+  if (w == 0) {
+    int nwarps = nt >> 5;
+    mx = lane < nwarps ? smx[lane] : -INFINITY;
+    se = lane < nwarps ? sse[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float m2 = __shfl_xor_sync(0xffffffffu, mx, o), s2 = __shfl_xor_sync(0xffffffffu, se, o);
+      float m = fmaxf(mx, m2);
+      se = (mx == -INFINITY ? 0.f : se * __expf(mx - m)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - m));
+      mx = m;
+    }
+    if (lane == 0) { red[0] = mx; red[1] = logf(se); }
+  }
+  __syncthreads();
+  float m = red[0], lse = m + red[1];
+  int64_t lab = labels[row];
+  float wr = wrow ? wrow[row] : 1.f;
+  if (tid == 0) {
+    float lv = __bfloat162float(lr[lab]) + (bias ? bias[lab] : 0.f);
+    loss[row] = lse - lv;
+  }
+  __syncthreads();
+  for (int c = tid; c < V; c += nt) {
+    float v = __bfloat162float(lr[c]) + (bias ? bias[c] : 0.f);
+    float p = __expf(v - lse);
+    lr[c] = __float2bfloat16(wr * (p - (c == lab ? 1.f : 0.f)));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Optimizer: sum of squares, then fused clip + Adam(W) + bf16 copy.
+// ---------------------------------------------------------------------------
+__global__ void sumsq_k(const float* __restrict__ g, long n, float* __restrict__ out) {
+  float s = 0.f;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    float v = g[i];
+    s += v * v;
+  }
+  s = warp_sum(s);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    s = warp_sum(s);
+    if (threadIdx.x == 0) atomicAdd(out, s);
+  }
+}
+
+// One group: elements [0, n).  step is 1-based.  sumsq points at the global grad
+// sum of squares; clip scale = max_norm / max(norm, max_norm) (optax clip_by_global_norm).
+__global__ void adam_k(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                       float* __restrict__ v, bf16* __restrict__ pb, long n, const float* __restrict__ sumsq,
+                       float max_norm, const float* __restrict__ lr_ptr, float b1, float b2, float eps,
+                       float wd, float bc1, float bc2) {
+  float scale = 1.f;
+  if (sumsq && max_norm > 0.f) {
+    float nrm = sqrtf(*sumsq);
+    scale = nrm < max_norm ? 1.f : max_norm / nrm;
+  }
+  float lr = *lr_ptr;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    float gi = g[i] * scale;
+    float mi = b1 * m[i] + (1.f - b1) * gi;
+    float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    float mh = mi / bc1, vh = vi / bc2;
+    float pi = p[i];
+    float upd = mh / (sqrtf(vh) + eps) + wd * pi;
+    pi -= lr * upd;
+    p[i] = pi;
+    if (pb) pb[i] = __float2bfloat16(pi);
+  }
+}
+
+}  // namespace ops
+}  // namespace s0
+
+// ---------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------
+using namespace s0::ops;
+
+static int row_grid(long T, int sms) {
+  long warps = T;
+  long blocks = (warps * 32 + 255) / 256;
+  long cap = (long)sms * 8;
+  return (int)(blocks < cap ? blocks : cap);
+}
+static int ew_grid(long n, int sms) {
+  long blocks = (n + 255) / 256;
+  long cap = (long)sms * 16;
+  return (int)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+void ln_fwd_launch(const float* x, const float* w, const float* b, void* y, float* mean, float* rstd, long T,
+                   int D, float eps, int sms, cudaStream_t st) {
+  int gr = row_grid(T, sms);
+  bf16* yp = reinterpret_cast<bf16*>(y);
+  if (D <= 256) ln_fwd_k<8><<<gr, 256, 0, st>>>(x, w, b, yp, mean, rstd, (int)T, D, eps);
+  else if (D <= 512) ln_fwd_k<16><<<gr, 256, 0, st>>>(x, w, b, yp, mean, rstd, (int)T, D, eps);
+  else if (D <= 1024) ln_fwd_k<32><<<gr, 256, 0, st>>>(x, w, b, yp, mean, rstd, (int)T, D, eps);
+  else ln_fwd_k<64><<<gr, 256, 0, st>>>(x, w, b, yp, mean, rstd, (int)T, D, eps);
+}
+void ln_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,
+                   const float* dres, float* dx, float* dw, float* db, long T, int D, int sms, cudaStream_t st) {
+  int gr = row_grid(T, sms);
+  const bf16* g = reinterpret_cast<const bf16*>(dy);
+  if (D <= 256) ln_bwd_k<8><<<gr, 256, 0, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  else if (D <= 512) ln_bwd_k<16><<<gr, 256, 0, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  else if (D <= 1024) ln_bwd_k<32><<<gr, 256, 0, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  else ln_bwd_k<64><<<gr, 256, 0, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+}
+void rms_fwd_launch(const void* x, const float* w, void* y, float* rstd, long T, int D, float eps, int sms,
+                    cudaStream_t st) {
+  rms_fwd_k<<<row_grid(T, sms), 256, 0, st>>>(reinterpret_cast<const bf16*>(x), w, reinterpret_cast<bf16*>(y),
+                                             rstd, (int)T, D, eps);
+}
+void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw, long T,
+                    int D, int sms, cudaStream_t st) {
+  int gr = row_grid(T, sms);
+  const bf16* g = reinterpret_cast<const bf16*>(dy);
+  const bf16* xp = reinterpret_cast<const bf16*>(x);
+  bf16* o = reinterpret_cast<bf16*>(dx);
+  int nv = D / 8;
+  if (nv <= 32) rms_bwd_k<1><<<gr, 256, 0, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+  else if (nv <= 64) rms_bwd_k<2><<<gr, 256, 0, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+  else if (nv <= 128) rms_bwd_k<4><<<gr, 256, 0, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+  else rms_bwd_k<8><<<gr, 256, 0, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+}
+void gelu_fwd_launch(const void* o, void* g, long n, int sms, cudaStream_t st) {
+  gelu_fwd_k<<<ew_grid(n / 8, sms), 256, 0, st>>>(reinterpret_cast<const bf16*>(o), reinterpret_cast<bf16*>(g),
+                                                 n / 8);
+}
+void glu_res_fwd_launch(const float* x, const void* g, const void* h, const float* b, float* out, long n, int D,
+                        int sms, cudaStream_t st) {
+  glu_res_fwd_k<<<ew_grid(n / 8, sms), 256, 0, st>>>(x, reinterpret_cast<const bf16*>(g),
+                                                    reinterpret_cast<const bf16*>(h), b, out, n / 8, D);
+}
+void glu_res_bwd_launch(const float* dout, const void* g, const void* h, const float* b, void* dh, float* dgp,
+                        float* db, long T, int D, int sms, cudaStream_t st) {
+  int gr = row_grid(T, sms);
+  const bf16* gp = reinterpret_cast<const bf16*>(g);
+  const bf16* hp = reinterpret_cast<const bf16*>(h);
+  bf16* dhp = reinterpret_cast<bf16*>(dh);
+  if (D <= 256) glu_res_bwd_k<8><<<gr, 256, 0, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  else if (D <= 512) glu_res_bwd_k<16><<<gr, 256, 0, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  else if (D <= 1024) glu_res_bwd_k<32><<<gr, 256, 0, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  else glu_res_bwd_k<64><<<gr, 256, 0, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+}
+void gelu_bwd_launch(const void* o, const float* dgp, const void* dgm, void* dout, long n, int sms,
+                     cudaStream_t st) {
+  gelu_bwd_k<<<ew_grid(n / 8, sms), 256, 0, st>>>(reinterpret_cast<const bf16*>(o), dgp,
+                                                 reinterpret_cast<const bf16*>(dgm), reinterpret_cast<bf16*>(dout),
+                                                 n / 8);
+}
+void ce_launch(void* logits, const float* bias, const int64_t* labels, const float* wrow, float* loss, long T,
+               int V, int ld, cudaStream_t st) {
+  ce_fwd_bwd_k<<<(unsigned)T, 512, 0, st>>>(reinterpret_cast<bf16*>(logits), bias, labels, wrow, loss, V, ld);
+}
+void sumsq_launch(const float* g, long n, float* out, int sms, cudaStream_t st) {
+  sumsq_k<<<ew_grid(n, sms), 256, 0, st>>>(g, n, out);
+}
+void adam_launch(float* p, const float* g, float* m, float* v, void* pb, long n, const float* sumsq,
+                 float max_norm, const float* lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
+                 int sms, cudaStream_t st) {
+  adam_k<<<ew_grid(n, sms), 256, 0, st>>>(p, g, m, v, reinterpret_cast<bf16*>(pb), n, sumsq, max_norm, lr, b1, b2,
+                                         eps, wd, bc1, bc2);
+}

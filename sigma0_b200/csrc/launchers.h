@@ -1,0 +1,61 @@
+// Raw-pointer launch entry points of the sm_100a kernels.  The CUDA sources
+// include no torch headers (fast, parallel compiles); tensor handling lives in
+// bindings.cpp.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// ---- Mamba3 SSD ----------------------------------------------------------------
+struct M3Geo {
+  int B, L, nh;
+  int ldp;   // row stride (elements) of proj / dproj
+};
+struct M3Scan {
+  const void* proj;
+  const void* bc;
+  const float *dt, *adt, *sig, *rate;
+  const float *Bb, *Cb, *D;
+};
+struct M3BwdOut {
+  void* dproj;
+  void *gQ, *gK;
+  float* gAng;
+  float *dgam, *dscl, *ddt, *dadt;
+  float *dD, *dCb, *dBb;
+};
+int m3_nchunks(int L);
+void m3_prep_fwd_launch(const M3Geo& g, const void* proj, const float* wB, const float* wC,
+                        const float* dt_bias, float A_floor, float eps, void* bc, float* dt, float* adt,
+                        float* sig, float* rate, cudaStream_t st);
+void m3_ssd_fwd_launch(const M3Geo& g, const M3Scan& s, void* y, void* states, float* theta0,
+                       cudaStream_t st);
+void m3_ssd_bwd_launch(const M3Geo& g, const M3Scan& s, const void* dy, const void* states,
+                       const float* theta0, const M3BwdOut& o, cudaStream_t st);
+void m3_prep_bwd_launch(const M3Geo& g, const void* proj, const float* wB, const float* wC,
+                        const float* dt_bias, float A_floor, float eps, const void* gQ, const void* gK,
+                        const float* gAng, const float* dgam, const float* dscl, const float* ddt,
+                        const float* dadt, void* dproj, float* dwB, float* dwC, float* ddt_bias,
+                        cudaStream_t st);
+
+// ---- fused row/elementwise ops, loss and optimizer (fused_ops.cu) -------------------
+void ln_fwd_launch(const float* x, const float* w, const float* b, void* y, float* mean, float* rstd, long T,
+                   int D, float eps, int sms, cudaStream_t st);
+void ln_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,
+                   const float* dres, float* dx, float* dw, float* db, long T, int D, int sms, cudaStream_t st);
+void rms_fwd_launch(const void* x, const float* w, void* y, float* rstd, long T, int D, float eps, int sms,
+                    cudaStream_t st);
+void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw, long T,
+                    int D, int sms, cudaStream_t st);
+void gelu_fwd_launch(const void* o, void* g, long n, int sms, cudaStream_t st);
+void glu_res_fwd_launch(const float* x, const void* g, const void* h, const float* b, float* out, long n, int D,
+                        int sms, cudaStream_t st);
+void glu_res_bwd_launch(const float* dout, const void* g, const void* h, const float* b, void* dh, float* dgp,
+                        float* db, long T, int D, int sms, cudaStream_t st);
+void gelu_bwd_launch(const void* o, const float* dgp, const void* dgm, void* dout, long n, int sms,
+                     cudaStream_t st);
+void ce_launch(void* logits, const float* bias, const int64_t* labels, const float* wrow, float* loss, long T,
+               int V, int ld, cudaStream_t st);
+void sumsq_launch(const float* g, long n, float* out, int sms, cudaStream_t st);
+void adam_launch(float* p, const float* g, float* m, float* v, void* pb, long n, const float* sumsq,
+                 float max_norm, const float* lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
+                 int sms, cudaStream_t st);

@@ -1,0 +1,76 @@
+"""Parameter-holding building blocks named like the reference's Flax modules.
+
+Every parameter lives under the attribute path that the reference's Flax tree
+uses (``Dense`` -> ``kernel``/``bias``, ``LayerNorm`` -> ``scale``/``bias``,
+``Embed`` -> ``embedding``, ``RMSNorm`` -> ``scale``), so a module's
+``named_parameters()`` maps one-to-one onto the reference checkpoint tree
+(``docs/architecture.md:35-39`` of the reference).  Kernels are stored
+``(in, out)`` as in Flax; parameters are float32.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+def lecun_normal_(t: torch.Tensor, fan_in: int, gen=None) -> torch.Tensor:
+    # truncated normal (+-2 std) with variance 1/fan_in, like jax's lecun_normal
+    std = math.sqrt(1.0 / fan_in) / 0.87962566103423978
+    with torch.no_grad():
+        t.normal_(0, 1, generator=gen)
+        t.clamp_(-2, 2).mul_(std)
+    return t
+
+
+class Dense(nn.Module):
+    def __init__(self, d_in: int, d_out: int, bias: bool = True):
+        super().__init__()
+        self.d_in, self.d_out = d_in, d_out
+        self.kernel = nn.Parameter(lecun_normal_(torch.empty(d_in, d_out), d_in))
+        self.bias = nn.Parameter(torch.zeros(d_out)) if bias else None
+
+    def forward(self, x, dtype=None):
+        w = self.kernel if dtype is None else self.kernel.to(dtype)
+        y = x.to(w.dtype) @ w
+        if self.bias is not None:
+            y = y + self.bias.to(y.dtype)
+        return y
+
+
+class LayerNorm(nn.Module):
+    def __init__(self, d: int, eps: float = 1e-6):
+        super().__init__()
+        self.eps = eps
+        self.scale = nn.Parameter(torch.ones(d))
+        self.bias = nn.Parameter(torch.zeros(d))
+
+    def forward(self, x):
+        return F.layer_norm(x.float(), (x.shape[-1],), self.scale, self.bias, self.eps)
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, d: int, eps: float = 1e-6):
+        super().__init__()
+        self.eps = eps
+        self.scale = nn.Parameter(torch.ones(d))
+
+    def forward(self, x):
+        xf = x.float()
+        return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self.scale
+
+
+class Embed(nn.Module):
+    def __init__(self, n: int, d: int):
+        super().__init__()
+        # flax Embed default: variance_scaling(1, fan_in, normal, out_axis=0) -> std 1/sqrt(d)
+        self.embedding = nn.Parameter(torch.randn(n, d) / math.sqrt(d))
+
+    def forward(self, idx):
+        return self.embedding[idx]
+
+
+def gelu_tanh(x):
+    return F.gelu(x, approximate="tanh")

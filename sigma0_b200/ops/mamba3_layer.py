@@ -1,0 +1,166 @@
+"""CUDA execution of Mamba3 layers.
+
+Two autograd functions:
+
+* :func:`mamba3_sequence_layer` -- the whole pre-norm ``half_glu1`` residual
+  block (LayerNorm -> in_proj -> Mamba3 SSD -> out_norm -> out_proj -> GELU ->
+  out2 gate -> residual) as ONE autograd node.  It owns its saved tensors
+  (the fp32 layer input, the bf16 projection, the pre-norm SSD output and the
+  two GLU pre-activations) and recomputes the cheap ones in backward (the
+  LayerNorm output, out_norm output and GELU).
+* :func:`mamba3_mixer` -- the mixer alone (in_proj ... out_proj), used where the
+  residual wrapper is not fused (e.g. the book pre-layer at width 503).
+
+GEMMs are cuBLAS bf16 (``torch.matmul``; weight gradients with fp32 output);
+the SSD, its pre/post-processing and all row/elementwise work are the sm_100a
+kernels of ``csrc/``.  The projection buffer's row stride is padded to a
+multiple of 8 elements so every kernel can use 16-byte accesses.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._ext import ext
+from . import weights as W
+
+EPS = 1e-6
+
+
+def _pad8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+def _mm_f32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a @ b with bf16 operands and an fp32 result (weight gradients)."""
+    return torch.mm(a, b, out_dtype=torch.float32)
+
+
+def _check_dims(m) -> None:
+    d = m.dims
+    if (d.d_state, d.headdim, d.chunk_size, d.R) != (128, 64, 64, 32):
+        raise NotImplementedError(
+            f"the CUDA Mamba3 kernels are built for d_state=128, headdim=64, chunk=64, 32 rope angles; "
+            f"got {d}; use impl='torch' for other geometries")
+
+
+class _Mamba3Core:
+    """Forward/backward of in_proj -> SSD -> out_norm -> out_proj on flat rows."""
+
+    @staticmethod
+    def forward(xn, B, L, m):
+        C = ext()
+        d = m.dims
+        ldp = _pad8(d.d_in_proj)
+        w_in = W.bf16_padded(m.in_proj.kernel, ldp)
+        proj = xn @ w_in                                              # [T, ldp]
+        pre = C.m3_prep_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.A_floor, EPS)
+        y = C.m3_ssd_fwd(proj, pre, m.B_bias, m.C_bias, m.D, B, L, d.n_heads, True, False)[0]
+        y2 = y.view(-1, d.d_inner)
+        yn, yr = C.rms_fwd(y2, m.out_norm.scale, EPS)
+        o = yn @ W.bf16(m.out_proj.kernel)                            # [T, H]
+        return o, proj, y2, yr
+
+    @staticmethod
+    def backward(do, xn, proj, y2, yr, B, L, m):
+        """Returns (dxn bf16, grads dict keyed by parameter)."""
+        C = ext()
+        d = m.dims
+        ldp = proj.shape[1]
+        yn, _ = C.rms_fwd(y2, m.out_norm.scale, EPS)
+        g_out_proj = _mm_f32(yn.t(), do)
+        dyn = do @ W.bf16(m.out_proj.kernel).t()
+        dy, g_out_norm = C.rms_bwd(dyn.contiguous(), y2, m.out_norm.scale, yr)
+        dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_ssd_bwd(
+            proj, dy, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D, B, L,
+            d.n_heads, m.A_floor, EPS)
+        g_in = _mm_f32(xn.t(), dproj)[:, :d.d_in_proj]
+        dxn = dproj @ W.bf16_padded(m.in_proj.kernel, ldp).t()
+        grads = {m.out_proj.kernel: g_out_proj, m.out_norm.scale: g_out_norm, m.in_proj.kernel: g_in,
+                 m.B_norm.scale: dwB, m.C_norm.scale: dwC, m.dt_bias: ddtb, m.D: dD,
+                 m.C_bias: dCb, m.B_bias: dBb}
+        return dxn, grads
+
+
+def _mixer_params(m):
+    return [m.in_proj.kernel, m.dt_bias, m.B_bias, m.C_bias, m.B_norm.scale, m.C_norm.scale, m.D,
+            m.out_norm.scale, m.out_proj.kernel]
+
+
+class _MixerFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, u, module, *params):
+        B, L, H = u.shape
+        xn = u.reshape(-1, H).to(torch.bfloat16).contiguous()
+        o, proj, y2, yr = _Mamba3Core.forward(xn, B, L, module)
+        ctx.module, ctx.shape, ctx.in_dtype = module, (B, L, H), u.dtype
+        ctx.save_for_backward(xn, proj, y2, yr)
+        return o.view(B, L, H)
+
+    @staticmethod
+    def backward(ctx, do):
+        xn, proj, y2, yr = ctx.saved_tensors
+        B, L, H = ctx.shape
+        m = ctx.module
+        do = do.reshape(-1, H).to(torch.bfloat16).contiguous()
+        dxn, grads = _Mamba3Core.backward(do, xn, proj, y2, yr, B, L, m)
+        du = dxn.view(B, L, H).to(ctx.in_dtype)
+        return (du, None) + tuple(grads[p] for p in _mixer_params(m))
+
+
+def mamba3_mixer(u: torch.Tensor, module) -> torch.Tensor:
+    _check_dims(module)
+    return _MixerFn.apply(u, module, *_mixer_params(module))
+
+
+class _LayerFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, layer, *params):
+        C = ext()
+        m = layer.seq
+        B, L, H = x.shape
+        xf = x.reshape(-1, H)
+        if xf.dtype != torch.float32 or not xf.is_contiguous():
+            xf = xf.float().contiguous()
+        xn, mu, rs = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, EPS)
+        o, proj, y2, yr = _Mamba3Core.forward(xn, B, L, m)
+        g = C.gelu_fwd(o)
+        h = g @ W.bf16(layer.out2.kernel)
+        out = C.glu_res_fwd(xf, g, h, layer.out2.bias)
+        ctx.layer, ctx.shape = layer, (B, L, H)
+        ctx.save_for_backward(xf, mu, rs, proj, y2, yr, o, h)
+        return out.view(B, L, H)
+
+    @staticmethod
+    def backward(ctx, dout):
+        C = ext()
+        xf, mu, rs, proj, y2, yr, o, h = ctx.saved_tensors
+        layer = ctx.layer
+        m = layer.seq
+        B, L, H = ctx.shape
+        dout = dout.reshape(-1, H)
+        if dout.dtype != torch.float32 or not dout.is_contiguous():
+            dout = dout.float().contiguous()
+        g = C.gelu_fwd(o)
+        dh, dgp, db2 = C.glu_res_bwd(dout, g, h, layer.out2.bias)
+        g_out2 = _mm_f32(g.t(), dh)
+        dgm = dh @ W.bf16(layer.out2.kernel).t()
+        do = C.gelu_bwd(o, dgp, dgm.contiguous())
+        xn, _, _ = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, EPS)
+        dxn, grads = _Mamba3Core.backward(do, xn, proj, y2, yr, B, L, m)
+        dx, dlw, dlb = C.ln_bwd(dxn.contiguous(), xf, mu, rs, layer.norm.scale, dout)
+        grads[layer.norm.scale] = dlw
+        grads[layer.norm.bias] = dlb
+        grads[layer.out2.kernel] = g_out2
+        grads[layer.out2.bias] = db2
+        return (dx.view(B, L, H), None) + tuple(grads[p] for p in _layer_params(layer))
+
+
+def _layer_params(layer):
+    return [layer.norm.scale, layer.norm.bias] + _mixer_params(layer.seq) + [layer.out2.kernel, layer.out2.bias]
+
+
+def mamba3_sequence_layer(x: torch.Tensor, layer) -> torch.Tensor:
+    _check_dims(layer.seq)
+    if x.shape[-1] % 8:
+        raise NotImplementedError("the fused layer path needs d_model % 8 == 0")
+    return _LayerFn.apply(x, layer, *_layer_params(layer))

@@ -1,0 +1,149 @@
+"""GPU numerics of the Mamba3 kernels against the plain-torch fp32 oracle."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+def _layer(H=512, seed=0):
+    from sigma0_b200.models.mamba3 import Mamba3
+    torch.manual_seed(seed)
+    m = Mamba3(H, impl="cuda").cuda()
+    with torch.no_grad():
+        m.B_bias.normal_(0, 0.5)
+        m.C_bias.normal_(0, 0.5)
+        m.D.normal_(1, 0.2)
+        m.B_norm.scale.normal_(1, 0.1)
+        m.C_norm.scale.normal_(1, 0.1)
+        m.in_proj.kernel.mul_(2.0)
+    return m
+
+
+def _oracle_y(m, proj, B, L):
+    from sigma0_b200.ops.reference import mamba3_ref as ref
+    z, x, Bn, Cn, ADT, DT, trap, ang = m._prep(proj.float().view(B, L, -1))
+    nh = m.dims.n_heads
+    Bh = Bn[:, :, None, :].expand(-1, -1, nh, -1)
+    Ch = Cn[:, :, None, :].expand(-1, -1, nh, -1)
+    y = ref.mamba3_ssd_chunked(Ch, Bh, x, ADT.transpose(1, 2), DT.transpose(1, 2), trap.transpose(1, 2),
+                               ang, m.C_bias, m.B_bias, m.D, z, chunk_size=64)
+    return y.reshape(B, L, -1)
+
+
+@pytest.mark.parametrize("L", [64, 200])
+def test_ssd_forward_matches_oracle(L):
+    from sigma0_b200.ops._ext import ext
+    C = ext()
+    m = _layer()
+    B = 2
+    d = m.dims
+    ldp = (d.d_in_proj + 7) // 8 * 8
+    proj = (torch.randn(B * L, ldp, device="cuda") * 0.5).to(torch.bfloat16)
+    pre = C.m3_prep_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.A_floor, 1e-6)
+    y = C.m3_ssd_fwd(proj, pre, m.B_bias, m.C_bias, m.D, B, L, d.n_heads, True, False)[0]
+    yr = _oracle_y(m, proj[:, :d.d_in_proj].contiguous(), B, L)
+    assert torch.isfinite(y.float()).all()
+    assert rel(y, yr) < 2e-2, rel(y, yr)
+
+
+@pytest.mark.parametrize("L", [128, 150])
+def test_ssd_backward_matches_oracle(L):
+    from sigma0_b200.ops._ext import ext
+    C = ext()
+    m = _layer(seed=1)
+    B = 2
+    d = m.dims
+    ldp = (d.d_in_proj + 7) // 8 * 8
+    proj = (torch.randn(B * L, ldp, device="cuda") * 0.5).to(torch.bfloat16)
+    proj[:, d.d_in_proj:] = 0
+    dy = torch.randn(B, L, d.d_inner, device="cuda").to(torch.bfloat16)
+    dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_ssd_bwd(
+        proj, dy, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D, B, L, d.n_heads,
+        m.A_floor, 1e-6)
+    p32 = proj[:, :d.d_in_proj].float().clone().requires_grad_(True)
+    params = [m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.D, m.C_bias, m.B_bias]
+    for p in params:
+        p.grad = None
+    y = _oracle_y(m, p32, B, L)
+    (y * dy.float()).sum().backward()
+    assert rel(dproj[:, :d.d_in_proj], p32.grad) < 3e-2, rel(dproj[:, :d.d_in_proj], p32.grad)
+    # column groups separately: z, x, B, C, dd_dt, dd_A, trap, angles
+    sizes = [d.d_inner, d.d_inner, d.d_state, d.d_state, d.n_heads, d.n_heads, d.n_heads, d.R]
+    off = 0
+    for name, s in zip(["z", "x", "B", "C", "dd_dt", "dd_A", "trap", "ang"], sizes):
+        e = rel(dproj[:, off:off + s], p32.grad[:, off:off + s])
+        assert e < 5e-2, (name, e)
+        off += s
+    assert (dproj[:, d.d_in_proj:] == 0).all()
+    for got, p, name in [(dwB, m.B_norm.scale, "B_norm"), (dwC, m.C_norm.scale, "C_norm"),
+                         (ddtb, m.dt_bias, "dt_bias"), (dD, m.D, "D"), (dCb, m.C_bias, "C_bias"),
+                         (dBb, m.B_bias, "B_bias")]:
+        assert rel(got, p.grad) < 5e-2, (name, rel(got, p.grad))
+
+
+def test_fused_layer_matches_torch_path():
+    """Whole pre-norm half_glu1 layer: fused CUDA autograd vs the torch composition."""
+    from sigma0_b200.models.mamba3 import Mamba3
+    from sigma0_b200.models.layers import SequenceLayer
+    torch.manual_seed(3)
+    H, B, L = 256, 2, 130
+    layer = SequenceLayer(Mamba3(H, impl="cuda", dtype=torch.bfloat16), H).cuda()
+    ref_layer = SequenceLayer(Mamba3(H, impl="torch", dtype=torch.float32), H).cuda()
+    ref_layer.load_state_dict(layer.state_dict())
+    x = torch.randn(B, L, H, device="cuda")
+    x1 = x.clone().requires_grad_(True)
+    x2 = x.clone().requires_grad_(True)
+    y1 = layer(x1)
+    y2 = ref_layer(x2)
+    assert rel(y1 - x, y2 - x) < 3e-2
+    g = torch.randn_like(y1)
+    (y1 * g).sum().backward()
+    (y2 * g).sum().backward()
+    assert rel(x1.grad, x2.grad) < 3e-2
+    for (n, p1), (_, p2) in zip(layer.named_parameters(), ref_layer.named_parameters()):
+        assert rel(p1.grad, p2.grad) < 6e-2, (n, rel(p1.grad, p2.grad))
+
+
+def test_linear_ce_matches_torch():
+    from sigma0_b200.ops.cross_entropy import linear_cross_entropy_mean
+    torch.manual_seed(0)
+    T, d, V = 1000, 128, 2112
+    h = torch.randn(2, T // 2, d, device="cuda", requires_grad=True)
+    Wk = (torch.randn(d, V, device="cuda") * 0.05).requires_grad_(True)
+    b = (torch.randn(V, device="cuda") * 0.1).requires_grad_(True)
+    lab = torch.randint(0, V, (2, T // 2), device="cuda")
+    w = torch.full((2, T // 2), 1.0 / T, device="cuda")
+    loss, ce = linear_cross_entropy_mean(h, Wk, b, lab, w)
+    loss.backward()
+    h2, W2, b2 = h.detach().clone().requires_grad_(True), Wk.detach().clone().requires_grad_(True), \
+        b.detach().clone().requires_grad_(True)
+    logits = h2.reshape(-1, d) @ W2 + b2
+    l2 = torch.nn.functional.cross_entropy(logits, lab.reshape(-1))
+    l2.backward()
+    assert abs(loss.item() - l2.item()) < 2e-2 * abs(l2.item())
+    assert rel(h.grad, h2.grad) < 3e-2
+    assert rel(Wk.grad, W2.grad) < 3e-2
+    assert rel(b.grad, b2.grad) < 3e-2
+
+
+def test_flat_adam_cuda_matches_cpu():
+    from sigma0_b200.train.optim import FlatAdam
+    torch.manual_seed(0)
+    net = torch.nn.Sequential(torch.nn.Linear(16, 32), torch.nn.Linear(32, 4))
+    net_c = torch.nn.Sequential(torch.nn.Linear(16, 32), torch.nn.Linear(32, 4))
+    net_c.load_state_dict(net.state_dict())
+    net = net.cuda()
+    o1 = FlatAdam(net, lr=1e-2, ssm_lr=1e-3, max_grad_norm=0.5)
+    o2 = FlatAdam(net_c, lr=1e-2, ssm_lr=1e-3, max_grad_norm=0.5)
+    for _ in range(3):
+        x = torch.randn(8, 16)
+        o1.zero_grad(); o2.zero_grad()
+        net(x.cuda()).pow(2).sum().backward()
+        net_c(x).pow(2).sum().backward()
+        o1.step(); o2.step()
+    assert (o1.flat.cpu() - o2.flat).abs().max().item() < 1e-5
