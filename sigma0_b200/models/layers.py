@@ -45,7 +45,8 @@ class SequenceLayer(nn.Module):
     def _fused_ok(self, x) -> bool:
         from .mamba3 import Mamba3
         return (x.is_cuda and isinstance(self.seq, Mamba3) and self.seq.impl == "cuda"
-                and self.prenorm and self.activation == "half_glu1" and self.dropout == 0.0)
+                and self.prenorm and self.activation == "half_glu1" and self.dropout == 0.0
+                and self.d_model % 8 == 0)
 
     def _act(self, x):
         cd = getattr(self.seq, "compute_dtype", torch.float32)
