@@ -34,93 +34,114 @@ M3Geo m3_geo(const at::Tensor& proj, int64_t B, int64_t L, int64_t nh) {
   return g;
 }
 
-M3Scan m3_scan(const at::Tensor& proj, const std::vector<at::Tensor>& pre, const at::Tensor& Bb,
-               const at::Tensor& Cb, const at::Tensor& D) {
+struct M3Pre {
+  at::Tensor bc, dt, adt, sig, rate, aend, angtot, theta0;
+};
+
+M3Scan m3_scan(const at::Tensor& proj, const M3Pre& pre, const at::Tensor& Bb, const at::Tensor& Cb,
+               const at::Tensor& D) {
   M3Scan s;
   s.proj = proj.data_ptr();
-  s.bc = pre[0].data_ptr();
-  s.dt = pre[1].data_ptr<float>();
-  s.adt = pre[2].data_ptr<float>();
-  s.sig = pre[3].data_ptr<float>();
-  s.rate = pre[4].data_ptr<float>();
+  s.bc = pre.bc.data_ptr();
+  s.dt = pre.dt.data_ptr<float>();
+  s.adt = pre.adt.data_ptr<float>();
+  s.sig = pre.sig.data_ptr<float>();
+  s.rate = pre.rate.data_ptr<float>();
   s.Bb = Bb.data_ptr<float>();
   s.Cb = Cb.data_ptr<float>();
   s.D = D.data_ptr<float>();
+  s.theta0 = pre.theta0.defined() ? pre.theta0.data_ptr<float>() : nullptr;
+  s.aend = pre.aend.defined() ? pre.aend.data_ptr<float>() : nullptr;
   return s;
 }
 
-std::vector<at::Tensor> m3_prep_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh, at::Tensor wB,
-                                    at::Tensor wC, at::Tensor dt_bias, double A_floor, double eps) {
-  c10::cuda::CUDAGuard guard(proj.device());
+// per-token prep + chunk totals + angle carry
+M3Pre m3_prepare(const at::Tensor& proj, int64_t B, int64_t L, int64_t nh, const at::Tensor& wB,
+                 const at::Tensor& wC, const at::Tensor& dt_bias, double A_floor, double eps) {
   M3Geo g = m3_geo(proj, B, L, nh);
+  TORCH_CHECK(nh <= 64, "at most 64 heads");
   auto f32 = proj.options().dtype(at::kFloat);
-  auto bc = at::empty({B * L, 2 * M3_N}, proj.options());
-  auto dt = at::empty({B, nh, L}, f32), adt = at::empty({B, nh, L}, f32), sig = at::empty({B, nh, L}, f32);
-  auto rate = at::empty({B * L, M3_R}, f32);
+  int nc = m3_nchunks((int)L);
+  M3Pre pre;
+  pre.bc = at::empty({B * L, 2 * M3_N}, proj.options());
+  pre.dt = at::empty({B, nh, L}, f32);
+  pre.adt = at::empty({B, nh, L}, f32);
+  pre.sig = at::empty({B, nh, L}, f32);
+  pre.rate = at::empty({B * L, M3_R}, f32);
   m3_prep_fwd_launch(g, proj.data_ptr(), wB.data_ptr<float>(), wC.data_ptr<float>(), dt_bias.data_ptr<float>(),
-                     (float)A_floor, (float)eps, bc.data_ptr(), dt.data_ptr<float>(), adt.data_ptr<float>(),
-                     sig.data_ptr<float>(), rate.data_ptr<float>(), stream());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {bc, dt, adt, sig, rate};
+                     (float)A_floor, (float)eps, pre.bc.data_ptr(), pre.dt.data_ptr<float>(), pre.adt.data_ptr<float>(),
+                     pre.sig.data_ptr<float>(), pre.rate.data_ptr<float>(), stream());
+  pre.aend = at::empty({B, nh, nc}, f32);
+  pre.angtot = at::empty({B, nh, nc, M3_R}, f32);
+  pre.theta0 = at::empty({B, nh, nc, M3_R}, f32);
+  M3Scan s0 = m3_scan(proj, pre, dt_bias, dt_bias, dt_bias);
+  m3_chunk_totals_launch(g, s0, pre.aend.data_ptr<float>(), pre.angtot.data_ptr<float>(),
+                         pre.theta0.data_ptr<float>(), stream());
+  return pre;
 }
 
-std::vector<at::Tensor> m3_ssd_fwd(at::Tensor proj, std::vector<at::Tensor> pre, at::Tensor Bb, at::Tensor Cb,
-                                   at::Tensor D, int64_t B, int64_t L, int64_t nh, bool write_y, bool store) {
+// y = ssd(proj); returns (y, states) -- states is the S_in of every chunk (bf16)
+std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh, at::Tensor wB, at::Tensor wC,
+                               at::Tensor dt_bias, at::Tensor Bb, at::Tensor Cb, at::Tensor D, double A_floor,
+                               double eps) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
-  TORCH_CHECK(write_y || store, "nothing to compute");
+  M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
   int nc = m3_nchunks((int)L);
-  at::Tensor y, states, theta0;
-  if (write_y) y = at::empty({B, L, nh * M3_P}, proj.options());
-  if (store) {
-    states = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
-    theta0 = at::empty({B, nh, nc, M3_R}, proj.options().dtype(at::kFloat));
-  }
-  m3_ssd_fwd_launch(g, m3_scan(proj, pre, Bb, Cb, D), write_y ? y.data_ptr() : nullptr,
-                    store ? states.data_ptr() : nullptr, store ? theta0.data_ptr<float>() : nullptr, stream());
+  auto states = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
+  M3Scan s = m3_scan(proj, pre, Bb, Cb, D);
+  m3_states_launch(g, s, states.data_ptr(), stream());
+  auto y = at::empty({B, L, nh * M3_P}, proj.options());
+  m3_scan_launch(g, s, states.data_ptr(), y.data_ptr(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {y, states, theta0};
+  return {y, states};
 }
 
-std::vector<at::Tensor> m3_ssd_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC,
-                                   at::Tensor dt_bias, at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B,
-                                   int64_t L, int64_t nh, double A_floor, double eps) {
+std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias,
+                               at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B, int64_t L, int64_t nh,
+                               double A_floor, double eps) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
   req(dy, at::kBFloat16, "dy");
-  auto pre = m3_prep_fwd(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
-  auto st = m3_ssd_fwd(proj, pre, Bb, Cb, D, B, L, nh, false, true);
+  M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
+  int nc = m3_nchunks((int)L);
+  M3Scan s = m3_scan(proj, pre, Bb, Cb, D);
+  auto states = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
+  m3_states_launch(g, s, states.data_ptr(), stream());
+  auto U = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
+  m3_dstates_launch(g, s, dy.data_ptr(), U.data_ptr(), stream());
   auto f32 = proj.options().dtype(at::kFloat);
   auto dproj = at::empty_like(proj);
   auto gQ = at::empty({B * L, nh, M3_N}, proj.options());
   auto gK = at::empty({B * L, nh, M3_N}, proj.options());
-  auto gAng = at::empty({B * L, nh, M3_R}, f32);
-  auto dgam = at::empty({B, nh, L}, f32), dscl = at::empty({B, nh, L}, f32), ddt = at::empty({B, nh, L}, f32),
-       dadt = at::empty({B, nh, L}, f32);
-  auto dD = at::empty({B, nh}, f32), dCb = at::empty({B, nh, M3_N}, f32), dBb = at::empty({B, nh, M3_N}, f32);
+  auto dthl = at::empty({B * L, nh, M3_R}, f32);
+  auto dthtot = at::empty({B, nh, nc, M3_R}, f32);
+  auto dgam = at::empty({B, nh, L}, f32), dscl = at::empty({B, nh, L}, f32), dadt = at::empty({B, nh, L}, f32);
+  auto dD = at::empty({B, nh, nc}, f32), dCb = at::empty({B, nh, nc, M3_N}, f32),
+       dBb = at::empty({B, nh, nc, M3_N}, f32);
   M3BwdOut o;
   o.dproj = dproj.data_ptr();
   o.gQ = gQ.data_ptr();
   o.gK = gK.data_ptr();
-  o.gAng = gAng.data_ptr<float>();
+  o.dthl = dthl.data_ptr<float>();
+  o.dthtot = dthtot.data_ptr<float>();
   o.dgam = dgam.data_ptr<float>();
   o.dscl = dscl.data_ptr<float>();
-  o.ddt = ddt.data_ptr<float>();
   o.dadt = dadt.data_ptr<float>();
   o.dD = dD.data_ptr<float>();
   o.dCb = dCb.data_ptr<float>();
   o.dBb = dBb.data_ptr<float>();
-  m3_ssd_bwd_launch(g, m3_scan(proj, pre, Bb, Cb, D), dy.data_ptr(), st[1].data_ptr(), st[2].data_ptr<float>(), o,
-                    stream());
+  m3_chunk_bwd_launch(g, s, dy.data_ptr(), states.data_ptr(), U.data_ptr(), o, stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   auto dwB = at::zeros({M3_N}, f32), dwC = at::zeros({M3_N}, f32), ddtb = at::zeros({nh}, f32);
   m3_prep_bwd_launch(g, proj.data_ptr(), wB.data_ptr<float>(), wC.data_ptr<float>(), dt_bias.data_ptr<float>(),
-                     (float)A_floor, (float)eps, gQ.data_ptr(), gK.data_ptr(), gAng.data_ptr<float>(),
-                     dgam.data_ptr<float>(), dscl.data_ptr<float>(), ddt.data_ptr<float>(), dadt.data_ptr<float>(),
-                     dproj.data_ptr(), dwB.data_ptr<float>(), dwC.data_ptr<float>(), ddtb.data_ptr<float>(),
-                     stream());
+                     (float)A_floor, (float)eps, gQ.data_ptr(), gK.data_ptr(), dthl.data_ptr<float>(),
+                     dthtot.data_ptr<float>(), dgam.data_ptr<float>(), dscl.data_ptr<float>(),
+                     dadt.data_ptr<float>(), dproj.data_ptr(), dwB.data_ptr<float>(), dwC.data_ptr<float>(),
+                     ddtb.data_ptr<float>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {dproj, dwB, dwC, ddtb, dD.sum(0), dCb.sum(0), dBb.sum(0)};
+  return {dproj, dwB, dwC, ddtb, dD.sum(at::IntArrayRef{0, 2}), dCb.sum(at::IntArrayRef{0, 2}),
+          dBb.sum(at::IntArrayRef{0, 2})};
 }
 
 // ---- row / elementwise ------------------------------------------------------------------
@@ -273,9 +294,8 @@ void adam(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sigma0_b200 sm_100a kernels";
-  m.def("m3_prep_fwd", &m3_prep_fwd);
-  m.def("m3_ssd_fwd", &m3_ssd_fwd);
-  m.def("m3_ssd_bwd", &m3_ssd_bwd);
+  m.def("m3_fwd", &m3_fwd, "Mamba3 SSD forward (prep, chunk states, passing, chunk scan) -> (y, states)");
+  m.def("m3_bwd", &m3_bwd, "Mamba3 SSD backward -> (dproj, dB_norm, dC_norm, ddt_bias, dD, dC_bias, dB_bias)");
   m.def("ln_fwd", &ln_fwd);
   m.def("ln_bwd", &ln_bwd);
   m.def("rms_fwd", &rms_fwd);

@@ -38,6 +38,25 @@ S0_DEV float gelu_t_grad(float x) {
 // Max 64 columns per lane (D <= 2048).
 constexpr int MAXV = 64;
 
+// Reduce per-warp column partials across the warps of a block through shared memory,
+// then one atomicAdd per column per block.  `vals[i]` is this lane's partial for
+// column lane + 32*i (VPL entries); `smem` holds blockDim/32 * 32 * VPL floats.
+template <int VPL>
+S0_DEV void block_col_atomic(float* vals, float* smem, float* out, int D) {
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) smem[(w * VPL + i) * 32 + lane] = vals[i];
+  __syncthreads();
+  for (int c = threadIdx.x; c < VPL * 32; c += blockDim.x) {
+    int i = c >> 5, l = c & 31;
+    float s = 0.f;
+    for (int k = 0; k < nw; ++k) s += smem[(k * VPL + i) * 32 + l];
+    int col = l + 32 * i;
+    if (col < D) atomicAdd(&out[col], s);
+  }
+  __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // LayerNorm forward: x fp32 [T, D] -> y bf16, mean/rstd fp32 [T]
 // ---------------------------------------------------------------------------
@@ -119,14 +138,9 @@ __global__ void ln_bwd_k(const bf16* __restrict__ dy, const float* __restrict__ 
       if (c < D) dxr[c] = (rr ? rr[c] : 0.f) + r * (gw_[i] - s1 - xh[i] * s2);
     }
   }
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    int c = lane + 32 * i;
-    if (c < D) {
-      atomicAdd(&dw[c], aw[i]);
-      atomicAdd(&db[c], ab[i]);
-    }
-  }
+  extern __shared__ float red_smem[];
+  block_col_atomic<VPL>(aw, red_smem, dw, D);
+  block_col_atomic<VPL>(ab, red_smem, db, D);
 }
 
 // ---------------------------------------------------------------------------
@@ -218,12 +232,23 @@ __global__ void rms_bwd_k(const bf16* __restrict__ dy, const bf16* __restrict__ 
       }
     }
   }
+  // block reduction: smem[w][col] then one atomic per column per block
+  extern __shared__ float red_smem[];
+  int wid = threadIdx.x >> 5, nwb = blockDim.x >> 5;
+  for (int i = threadIdx.x; i < nwb * D; i += blockDim.x) red_smem[i] = 0.f;
+  __syncthreads();
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     int c = lane + 32 * j;
     if (c < nv)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) atomicAdd(&dw[c * 8 + k], aw[j * 8 + k]);
+      for (int k = 0; k < 8; ++k) red_smem[wid * D + c * 8 + k] = aw[j * 8 + k];
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < D; col += blockDim.x) {
+    float t = 0.f;
+    for (int k = 0; k < nwb; ++k) t += red_smem[k * D + col];
+    atomicAdd(&dw[col], t);
   }
 }
 
@@ -292,11 +317,8 @@ __global__ void glu_res_bwd_k(const float* __restrict__ dout, const bf16* __rest
       }
     }
   }
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    int c = lane + 32 * i;
-    if (c < D) atomicAdd(&db[c], ab[i]);
-  }
+  extern __shared__ float red_smem[];
+  block_col_atomic<VPL>(ab, red_smem, db, D);
 }
 
 // do = (dgp + dgm) * gelu'(o)  -> bf16
@@ -435,6 +457,17 @@ static int row_grid(long T, int sms) {
   long cap = (long)sms * 8;
   return (int)(blocks < cap ? blocks : cap);
 }
+template <typename K>
+static void allow_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// grid for kernels that reduce columns: few blocks (2 per SM), each looping over rows
+static int red_grid(long T, int sms) {
+  long blocks = (T * 32 + 255) / 256;
+  long cap = (long)sms * 2;
+  return (int)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
 static int ew_grid(long n, int sms) {
   long blocks = (n + 255) / 256;
   long cap = (long)sms * 16;
@@ -452,12 +485,15 @@ void ln_fwd_launch(const float* x, const float* w, const float* b, void* y, floa
 }
 void ln_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,
                    const float* dres, float* dx, float* dw, float* db, long T, int D, int sms, cudaStream_t st) {
-  int gr = row_grid(T, sms);
+  int gr = red_grid(T, sms);
   const bf16* g = reinterpret_cast<const bf16*>(dy);
-  if (D <= 256) ln_bwd_k<8><<<gr, 256, 0, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
-  else if (D <= 512) ln_bwd_k<16><<<gr, 256, 0, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
-  else if (D <= 1024) ln_bwd_k<32><<<gr, 256, 0, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
-  else ln_bwd_k<64><<<gr, 256, 0, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  if (D <= 256) ln_bwd_k<8><<<gr, 256, 8 * 8 * 32 * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  else if (D <= 512) ln_bwd_k<16><<<gr, 256, 8 * 16 * 32 * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  else if (D <= 1024) ln_bwd_k<32><<<gr, 256, 8 * 32 * 32 * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  else {
+    allow_smem(ln_bwd_k<64>, 8 * 64 * 32 * 4);
+    ln_bwd_k<64><<<gr, 256, 8 * 64 * 32 * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  }
 }
 void rms_fwd_launch(const void* x, const float* w, void* y, float* rstd, long T, int D, float eps, int sms,
                     cudaStream_t st) {
@@ -466,15 +502,18 @@ void rms_fwd_launch(const void* x, const float* w, void* y, float* rstd, long T,
 }
 void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw, long T,
                     int D, int sms, cudaStream_t st) {
-  int gr = row_grid(T, sms);
+  int gr = red_grid(T, sms);
   const bf16* g = reinterpret_cast<const bf16*>(dy);
   const bf16* xp = reinterpret_cast<const bf16*>(x);
   bf16* o = reinterpret_cast<bf16*>(dx);
   int nv = D / 8;
-  if (nv <= 32) rms_bwd_k<1><<<gr, 256, 0, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
-  else if (nv <= 64) rms_bwd_k<2><<<gr, 256, 0, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
-  else if (nv <= 128) rms_bwd_k<4><<<gr, 256, 0, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
-  else rms_bwd_k<8><<<gr, 256, 0, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+  if (nv <= 32) rms_bwd_k<1><<<gr, 256, 8 * D * 4, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+  else if (nv <= 64) rms_bwd_k<2><<<gr, 256, 8 * D * 4, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+  else if (nv <= 128) rms_bwd_k<4><<<gr, 256, 8 * D * 4, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+  else {
+    allow_smem(rms_bwd_k<8>, 8 * (size_t)D * 4);
+    rms_bwd_k<8><<<gr, 256, 8 * D * 4, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+  }
 }
 void gelu_fwd_launch(const void* o, void* g, long n, int sms, cudaStream_t st) {
   gelu_fwd_k<<<ew_grid(n / 8, sms), 256, 0, st>>>(reinterpret_cast<const bf16*>(o), reinterpret_cast<bf16*>(g),
@@ -487,14 +526,17 @@ void glu_res_fwd_launch(const float* x, const void* g, const void* h, const floa
 }
 void glu_res_bwd_launch(const float* dout, const void* g, const void* h, const float* b, void* dh, float* dgp,
                         float* db, long T, int D, int sms, cudaStream_t st) {
-  int gr = row_grid(T, sms);
+  int gr = red_grid(T, sms);
   const bf16* gp = reinterpret_cast<const bf16*>(g);
   const bf16* hp = reinterpret_cast<const bf16*>(h);
   bf16* dhp = reinterpret_cast<bf16*>(dh);
-  if (D <= 256) glu_res_bwd_k<8><<<gr, 256, 0, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
-  else if (D <= 512) glu_res_bwd_k<16><<<gr, 256, 0, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
-  else if (D <= 1024) glu_res_bwd_k<32><<<gr, 256, 0, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
-  else glu_res_bwd_k<64><<<gr, 256, 0, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  if (D <= 256) glu_res_bwd_k<8><<<gr, 256, 8 * 8 * 32 * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  else if (D <= 512) glu_res_bwd_k<16><<<gr, 256, 8 * 16 * 32 * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  else if (D <= 1024) glu_res_bwd_k<32><<<gr, 256, 8 * 32 * 32 * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  else {
+    allow_smem(glu_res_bwd_k<64>, 8 * 64 * 32 * 4);
+    glu_res_bwd_k<64><<<gr, 256, 8 * 64 * 32 * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  }
 }
 void gelu_bwd_launch(const void* o, const float* dgp, const void* dgm, void* dout, long n, int sms,
                      cudaStream_t st) {

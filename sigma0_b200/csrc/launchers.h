@@ -5,7 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-// ---- Mamba3 SSD ----------------------------------------------------------------
+// ---- Mamba3 SSD (mamba3_ssd.cu) -------------------------------------------------------
 struct M3Geo {
   int B, L, nh;
   int ldp;   // row stride (elements) of proj / dproj
@@ -15,25 +15,30 @@ struct M3Scan {
   const void* bc;
   const float *dt, *adt, *sig, *rate;
   const float *Bb, *Cb, *D;
+  const float* theta0;   // [B, nh, nc, R]
+  const float* aend;     // [B, nh, nc]
 };
 struct M3BwdOut {
   void* dproj;
   void *gQ, *gK;
-  float* gAng;
-  float *dgam, *dscl, *ddt, *dadt;
+  float *dthl, *dthtot;
+  float *dgam, *dscl, *dadt;
   float *dD, *dCb, *dBb;
 };
 int m3_nchunks(int L);
 void m3_prep_fwd_launch(const M3Geo& g, const void* proj, const float* wB, const float* wC,
                         const float* dt_bias, float A_floor, float eps, void* bc, float* dt, float* adt,
                         float* sig, float* rate, cudaStream_t st);
-void m3_ssd_fwd_launch(const M3Geo& g, const M3Scan& s, void* y, void* states, float* theta0,
-                       cudaStream_t st);
-void m3_ssd_bwd_launch(const M3Geo& g, const M3Scan& s, const void* dy, const void* states,
-                       const float* theta0, const M3BwdOut& o, cudaStream_t st);
+void m3_chunk_totals_launch(const M3Geo& g, const M3Scan& s, float* aend, float* angtot, float* theta0,
+                            cudaStream_t st);
+void m3_states_launch(const M3Geo& g, const M3Scan& s, void* states, cudaStream_t st);
+void m3_scan_launch(const M3Geo& g, const M3Scan& s, const void* states, void* y, cudaStream_t st);
+void m3_dstates_launch(const M3Geo& g, const M3Scan& s, const void* dy, void* U, cudaStream_t st);
+void m3_chunk_bwd_launch(const M3Geo& g, const M3Scan& s, const void* dy, const void* states, const void* dsout,
+                         const M3BwdOut& o, cudaStream_t st);
 void m3_prep_bwd_launch(const M3Geo& g, const void* proj, const float* wB, const float* wC,
                         const float* dt_bias, float A_floor, float eps, const void* gQ, const void* gK,
-                        const float* gAng, const float* dgam, const float* dscl, const float* ddt,
+                        const float* dthl, const float* dthc, const float* dgam, const float* dscl,
                         const float* dadt, void* dproj, float* dwB, float* dwC, float* ddt_bias,
                         cudaStream_t st);
 

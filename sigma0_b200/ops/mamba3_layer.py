@@ -31,8 +31,9 @@ def _pad8(n: int) -> int:
 
 
 def _mm_f32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """a @ b with bf16 operands and an fp32 result (weight gradients)."""
-    return torch.mm(a, b, out_dtype=torch.float32)
+    """Weight gradient a @ b: bf16 operands, fp32 accumulation in the GEMM, bf16 result
+    (autograd widens it into the float32 gradient buffer)."""
+    return a @ b
 
 
 def _check_dims(m) -> None:
@@ -53,8 +54,8 @@ class _Mamba3Core:
         ldp = _pad8(d.d_in_proj)
         w_in = W.bf16_padded(m.in_proj.kernel, ldp)
         proj = xn @ w_in                                              # [T, ldp]
-        pre = C.m3_prep_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.A_floor, EPS)
-        y = C.m3_ssd_fwd(proj, pre, m.B_bias, m.C_bias, m.D, B, L, d.n_heads, True, False)[0]
+        y = C.m3_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias,
+                     m.D, m.A_floor, EPS)[0]
         y2 = y.view(-1, d.d_inner)
         yn, yr = C.rms_fwd(y2, m.out_norm.scale, EPS)
         o = yn @ W.bf16(m.out_proj.kernel)                            # [T, H]
@@ -70,7 +71,7 @@ class _Mamba3Core:
         g_out_proj = _mm_f32(yn.t(), do)
         dyn = do @ W.bf16(m.out_proj.kernel).t()
         dy, g_out_norm = C.rms_bwd(dyn.contiguous(), y2, m.out_norm.scale, yr)
-        dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_ssd_bwd(
+        dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_bwd(
             proj, dy, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D, B, L,
             d.n_heads, m.A_floor, EPS)
         g_in = _mm_f32(xn.t(), dproj)[:, :d.d_in_proj]

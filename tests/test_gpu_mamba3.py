@@ -35,7 +35,7 @@ def _oracle_y(m, proj, B, L):
     return y.reshape(B, L, -1)
 
 
-@pytest.mark.parametrize("L", [64, 200])
+@pytest.mark.parametrize("L", [64, 200, 1000])
 def test_ssd_forward_matches_oracle(L):
     from sigma0_b200.ops._ext import ext
     C = ext()
@@ -44,14 +44,14 @@ def test_ssd_forward_matches_oracle(L):
     d = m.dims
     ldp = (d.d_in_proj + 7) // 8 * 8
     proj = (torch.randn(B * L, ldp, device="cuda") * 0.5).to(torch.bfloat16)
-    pre = C.m3_prep_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.A_floor, 1e-6)
-    y = C.m3_ssd_fwd(proj, pre, m.B_bias, m.C_bias, m.D, B, L, d.n_heads, True, False)[0]
+    y = C.m3_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D,
+                 m.A_floor, 1e-6)[0]
     yr = _oracle_y(m, proj[:, :d.d_in_proj].contiguous(), B, L)
     assert torch.isfinite(y.float()).all()
     assert rel(y, yr) < 2e-2, rel(y, yr)
 
 
-@pytest.mark.parametrize("L", [128, 150])
+@pytest.mark.parametrize("L", [128, 150, 700])
 def test_ssd_backward_matches_oracle(L):
     from sigma0_b200.ops._ext import ext
     C = ext()
@@ -62,7 +62,7 @@ def test_ssd_backward_matches_oracle(L):
     proj = (torch.randn(B * L, ldp, device="cuda") * 0.5).to(torch.bfloat16)
     proj[:, d.d_in_proj:] = 0
     dy = torch.randn(B, L, d.d_inner, device="cuda").to(torch.bfloat16)
-    dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_ssd_bwd(
+    dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_bwd(
         proj, dy, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D, B, L, d.n_heads,
         m.A_floor, 1e-6)
     p32 = proj[:, :d.d_in_proj].float().clone().requires_grad_(True)
