@@ -58,11 +58,15 @@ class FlatAdam:
             groups[leaf_group(n, opt_config, attention_model)].append((n, p))
         order = groups["ssm"] + groups["regular"]
         dev = order[0][1].device
-        total = sum(p.numel() for _, p in order)
-        self.n_ssm = sum(p.numel() for _, p in groups["ssm"])
+        # every slice starts on a 128-element boundary so bf16/fp32 views are 256-byte
+        # aligned (cuBLAS picks its vectorised kernels only for aligned operands)
+        A = 128
+        rnd = lambda n: (n + A - 1) // A * A
+        total = sum(rnd(p.numel()) for _, p in order)
+        self.n_ssm = sum(rnd(p.numel()) for _, p in groups["ssm"])
         self.numel = total
         self.device = dev
-        self.flat = torch.empty(total, dtype=torch.float32, device=dev)
+        self.flat = torch.zeros(total, dtype=torch.float32, device=dev)
         self.grad = torch.zeros(total, dtype=torch.float32, device=dev)
         self.m = torch.zeros(total, dtype=torch.float32, device=dev)
         self.v = torch.zeros(total, dtype=torch.float32, device=dev)
@@ -79,7 +83,7 @@ class FlatAdam:
                 W.register(p, self.shadow[off:off + k].view(p.shape))
             self.names.append(n)
             self.slices[n] = (off, off + k)
-            off += k
+            off += rnd(k)
         if self.shadow is not None:
             self.shadow.copy_(self.flat)
         self.step_count = 0
