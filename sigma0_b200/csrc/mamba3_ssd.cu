@@ -205,27 +205,31 @@ __device__ __forceinline__ void row_scalars(const float* sDT, const float* sSig,
   __syncthreads();
 }
 
-// theta[row][r] = theta0[r] + sum_{i<=row} rate[i][r] * DT[i]  (mod 2pi), into sTh.
+// theta[row][r] = theta0[r] + sum_{i<=row} rate[i][r] * DT[i]  (mod 2pi); writes cos/sin
+// tables sCos/sSin [64][RP] (sCos doubles as the scratch for the local prefix).
 template <int NTH>
 __device__ __forceinline__ void chunk_angles(const float* sRate, const float* sDT, const float* th0,
-                                             float* sTh, float* sSeg, int tid) {
+                                             float* sCos, float* sSin, float* sSeg, int tid) {
   constexpr int NSEG = NTH / 32, RPS = CS / NSEG;
   int r = tid & 31, seg = tid >> 5;
   float acc = 0.f;
-#pragma unroll 4
+#pragma unroll
   for (int i = 0; i < RPS; ++i) {
     int row = seg * RPS + i;
     acc += sRate[row * RP + r] * sDT[row];
-    sTh[row * RP + r] = acc;
+    sCos[row * RP + r] = acc;
   }
   sSeg[seg * 32 + r] = acc;
   __syncthreads();
   float base = th0[r];
   for (int s = 0; s < seg; ++s) base += sSeg[s * 32 + r];
-#pragma unroll 4
+#pragma unroll
   for (int i = 0; i < RPS; ++i) {
     int row = seg * RPS + i;
-    sTh[row * RP + r] = wrap2pi(base + sTh[row * RP + r]);
+    float sn, cs;
+    sincosf(wrap2pi(base + sCos[row * RP + r]), &sn, &cs);
+    sCos[row * RP + r] = cs;
+    sSin[row * RP + r] = sn;
   }
   __syncthreads();
 }
@@ -233,9 +237,9 @@ __device__ __forceinline__ void chunk_angles(const float* sRate, const float* sD
 // Q = rope(Cn + cb) into sQ (may alias sCn), K = rope(Bn + bb) * scale into sK (may alias sBn);
 // qkr[row] = (Cn+cb).(Bn+bb).  Either output may be skipped (nullptr).
 template <int NTH>
-__device__ __forceinline__ void build_qk(const bf16* sCn, const bf16* sBn, bf16* sQ, bf16* sK, const float* sTh,
-                                         const float* sScl, const float* sCbv, const float* sBbv, float* sQKr,
-                                         int tid) {
+__device__ __forceinline__ void build_qk(const bf16* sCn, const bf16* sBn, bf16* sQ, bf16* sK, const float* sCos,
+                                         const float* sSin, const float* sScl, const float* sCbv, const float* sBbv,
+                                         float* sQKr, int tid) {
   constexpr int TPR = NTH / CS;   // threads per row for the dot product (2 or 4)
   if (sQKr) {
     int row = tid / TPR, part = tid % TPR;
@@ -256,8 +260,7 @@ __device__ __forceinline__ void build_qk(const bf16* sCn, const bf16* sBn, bf16*
     int r = tid & 31, seg = tid >> 5;
     for (int i = 0; i < RPS; ++i) {
       int row = seg * RPS + i;
-      float sn, cs;
-      sincosf(sTh[row * RP + r], &sn, &cs);
+      const float sn = sSin[row * RP + r], cs = sCos[row * RP + r];
       if (sQ) {
         float2 c = unpack_bf16(*reinterpret_cast<const uint32_t*>(sCn + row * LDN + 2 * r));
         float c0 = c.x + sCbv[2 * r], c1 = c.y + sCbv[2 * r + 1];
@@ -291,79 +294,6 @@ __device__ __forceinline__ void build_qk(const bf16* sCn, const bf16* sBn, bf16*
 
 __device__ __forceinline__ size_t state_off(const Geo& g, int b, int h, int c) {
   return ((((size_t)b * g.nh + h) * g.nc) + c) * (size_t)P * N;
-}
-
-// ---------------------------------------------------------------------------
-// F2: per-chunk state contribution S_c[p][n] = sum_s w_s V[s][p] K[s][n]   (128 threads)
-// ---------------------------------------------------------------------------
-constexpr size_t STATE_SMEM = sizeof(bf16) * (CS * LDN + 2 * CS * LDP) +
-                              sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 5 * CS + N + 4 * 32 + 32);
-
-__global__ void __launch_bounds__(128) m3_chunk_state(ScanIn in, Geo g, bf16* __restrict__ states) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  bf16* sB = reinterpret_cast<bf16*>(smem);
-  bf16* sX = sB + CS * LDN;
-  bf16* sVd = sX + CS * LDP;
-  float* sRate = reinterpret_cast<float*>(sVd + CS * LDP);
-  float* sTh = sRate + CS * RP;
-  float* sDT = sTh + CS * RP;
-  float* sSig = sDT + CS + 1;
-  float* sADT = sSig + CS + 1;
-  float* sCum = sADT + CS;
-  float* sGam = sCum + CS;
-  float* sScl = sGam + CS;
-  float* sW = sScl + CS;
-  float* sBbv = sW + CS;
-  float* sSeg = sBbv + N;
-  float* sTh0 = sSeg + 4 * 32;
-
-  const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
-  const int t0 = c * CS, m0 = warp * 16;
-  const size_t bh = (size_t)b * g.nh + h;
-  load_rows<128>(in.bc + (size_t)b * g.L * 2 * N, 2 * N, 0, N, sB, LDN, t0, g.L, tid);
-  load_rows<128>(in.proj + (size_t)b * g.L * g.ldp, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
-  cp_async_commit();
-  load_scalars<128>(in, g, b, h, t0, sDT, sADT, sSig, sRate, tid);
-  for (int i = tid; i < N; i += 128) sBbv[i] = in.Bb[h * N + i];
-  if (tid < 32) sTh0[tid] = in.theta0[(bh * g.nc + c) * R + tid];
-  cp_async_wait_all();
-  __syncthreads();
-  row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
-  chunk_angles<128>(sRate, sDT, sTh0, sTh, sSeg, tid);
-  build_qk<128>(nullptr, sB, nullptr, sB, sTh, sScl, nullptr, sBbv, nullptr, tid);
-  const float cend = sCum[CS - 1];
-  if (tid < CS) sW[tid] = __expf(cend - sCum[tid]);
-  __syncthreads();
-  for (int i = tid; i < CS * P / 2; i += 128) {
-    int r = i / (P / 2), p = 2 * (i % (P / 2));
-    float2 v = unpack_bf16(*reinterpret_cast<const uint32_t*>(sX + r * LDP + p));
-    float w = sW[r];
-    *reinterpret_cast<uint32_t*>(sVd + r * LDP + p) = pack_bf16(v.x * w, v.y * w);
-  }
-  __syncthreads();
-  float st[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) st[i][0] = st[i][1] = st[i][2] = st[i][3] = 0.f;
-#pragma unroll
-  for (int kk = 0; kk < CS / 16; ++kk) {
-    uint32_t a[4];
-    load_a_t(a, sVd, LDP, m0, kk * 16, lane);
-#pragma unroll
-    for (int np = 0; np < 8; ++np) {
-      uint32_t bb[4];
-      load_b_kn(bb, sB, LDN, np * 16, kk * 16, lane);
-      mma_bf16(st[2 * np], a, bb[0], bb[1]);
-      mma_bf16(st[2 * np + 1], a, bb[2], bb[3]);
-    }
-  }
-  bf16* dst = states + state_off(g, b, h, c);
-#pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
-    int n = nt * 8 + 2 * tq;
-    *reinterpret_cast<uint32_t*>(dst + (m0 + gq) * N + n) = pack_bf16(st[nt][0], st[nt][1]);
-    *reinterpret_cast<uint32_t*>(dst + (m0 + gq + 8) * N + n) = pack_bf16(st[nt][2], st[nt][3]);
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -403,12 +333,90 @@ __global__ void __launch_bounds__(256) m3_pass(bf16* __restrict__ buf, const flo
 }
 
 // ---------------------------------------------------------------------------
-// F4: chunk scan -> gated y (128 threads, 2 blocks per SM)
+// Column-group conventions for the chunk kernels.  A block of NW warps has four
+// 16-row blocks (rb = warp & 3) and CG = NW/4 column groups (cg = warp >> 2);
+// 64-wide outputs give each warp 64/CG columns, 128-wide outputs 128/CG.
 // ---------------------------------------------------------------------------
-constexpr size_t SCAN_SMEM = sizeof(bf16) * (3 * CS * LDN + 2 * CS * LDP) +
-                             sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 5 * CS + 2 * N + 4 * 32 + 32);
 
-__global__ void __launch_bounds__(128, 2)
+// F2: per-chunk state contribution S_c[p][n] = sum_s w_s V[s][p] K[s][n]   (256 threads)
+constexpr size_t STATE_SMEM = sizeof(bf16) * (CS * LDN + 2 * CS * LDP) +
+                              sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 5 * CS + N + 8 * 32 + 32);
+
+__global__ void __launch_bounds__(256) m3_chunk_state(ScanIn in, Geo g, bf16* __restrict__ states) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* sB = reinterpret_cast<bf16*>(smem);
+  bf16* sX = sB + CS * LDN;
+  bf16* sVd = sX + CS * LDP;
+  float* sSin = reinterpret_cast<float*>(sVd + CS * LDP);   // rates, then sin table
+  float* sCos = sSin + CS * RP;
+  float* sDT = sCos + CS * RP;
+  float* sSig = sDT + CS + 1;
+  float* sADT = sSig + CS + 1;
+  float* sCum = sADT + CS;
+  float* sGam = sCum + CS;
+  float* sScl = sGam + CS;
+  float* sW = sScl + CS;
+  float* sBbv = sW + CS;
+  float* sSeg = sBbv + N;
+  float* sTh0 = sSeg + 8 * 32;
+
+  const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
+  const int rb = warp & 3, cg = warp >> 2;
+  const int t0 = c * CS, m0 = rb * 16;
+  const size_t bh = (size_t)b * g.nh + h;
+  load_rows<256>(in.bc + (size_t)b * g.L * 2 * N, 2 * N, 0, N, sB, LDN, t0, g.L, tid);
+  load_rows<256>(in.proj + (size_t)b * g.L * g.ldp, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
+  cp_async_commit();
+  load_scalars<256>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
+  for (int i = tid; i < N; i += 256) sBbv[i] = in.Bb[h * N + i];
+  if (tid < 32) sTh0[tid] = in.theta0[(bh * g.nc + c) * R + tid];
+  cp_async_wait_all();
+  __syncthreads();
+  row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
+  chunk_angles<256>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
+  build_qk<256>(nullptr, sB, nullptr, sB, sCos, sSin, sScl, nullptr, sBbv, nullptr, tid);
+  const float cend = sCum[CS - 1];
+  if (tid < CS) sW[tid] = __expf(cend - sCum[tid]);
+  __syncthreads();
+  for (int i = tid; i < CS * P / 2; i += 256) {
+    int r = i / (P / 2), p = 2 * (i % (P / 2));
+    float2 v = unpack_bf16(*reinterpret_cast<const uint32_t*>(sX + r * LDP + p));
+    float w = sW[r];
+    *reinterpret_cast<uint32_t*>(sVd + r * LDP + p) = pack_bf16(v.x * w, v.y * w);
+  }
+  __syncthreads();
+  float st[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) st[i][0] = st[i][1] = st[i][2] = st[i][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < CS / 16; ++kk) {
+    uint32_t a[4];
+    load_a_t(a, sVd, LDP, m0, kk * 16, lane);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t bb[4];
+      load_b_kn(bb, sB, LDN, cg * 64 + np * 16, kk * 16, lane);
+      mma_bf16(st[2 * np], a, bb[0], bb[1]);
+      mma_bf16(st[2 * np + 1], a, bb[2], bb[3]);
+    }
+  }
+  bf16* dst = states + state_off(g, b, h, c);
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    int n = cg * 64 + nt * 8 + 2 * tq;
+    *reinterpret_cast<uint32_t*>(dst + (m0 + gq) * N + n) = pack_bf16(st[nt][0], st[nt][1]);
+    *reinterpret_cast<uint32_t*>(dst + (m0 + gq + 8) * N + n) = pack_bf16(st[nt][2], st[nt][3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// F4: chunk scan -> gated y  (256 threads: rows rb, 32-column halves cg)
+// ---------------------------------------------------------------------------
+constexpr size_t SCAN_SMEM = sizeof(bf16) * (3 * CS * LDN + 3 * CS * LDP) +
+                             sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 5 * CS + 2 * N + 8 * 32 + 32);
+
+__global__ void __launch_bounds__(256)
     m3_chunk_scan(ScanIn in, Geo g, const bf16* __restrict__ states, bf16* __restrict__ y) {
   extern __shared__ __align__(16) unsigned char smem[];
   bf16* sC = reinterpret_cast<bf16*>(smem);   // Cn -> Q
@@ -416,9 +424,10 @@ __global__ void __launch_bounds__(128, 2)
   bf16* sSt = sB + CS * LDN;                  // S_in [p][n]
   bf16* sX = sSt + CS * LDN;
   bf16* sZ = sX + CS * LDP;                   // z -> y staging
-  float* sRate = reinterpret_cast<float*>(sZ + CS * LDP);
-  float* sTh = sRate + CS * RP;
-  float* sDT = sTh + CS * RP;
+  bf16* sP = sZ + CS * LDP;
+  float* sSin = reinterpret_cast<float*>(sP + CS * LDP);
+  float* sCos = sSin + CS * RP;
+  float* sDT = sCos + CS * RP;
   float* sSig = sDT + CS + 1;
   float* sADT = sSig + CS + 1;
   float* sCum = sADT + CS;
@@ -428,28 +437,29 @@ __global__ void __launch_bounds__(128, 2)
   float* sCbv = sQKr + CS;
   float* sBbv = sCbv + N;
   float* sSeg = sBbv + N;
-  float* sTh0 = sSeg + 4 * 32;
+  float* sTh0 = sSeg + 8 * 32;
 
   const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
-  const int t0 = c * CS, m0 = warp * 16;
+  const int rb = warp & 3, cg = warp >> 2, c32 = cg * 32;
+  const int t0 = c * CS, m0 = rb * 16;
   const size_t bh = (size_t)b * g.nh + h;
   const bf16* bcb = in.bc + (size_t)b * g.L * 2 * N;
   const bf16* pb = in.proj + (size_t)b * g.L * g.ldp;
-  load_rows<128>(bcb, 2 * N, 0, N, sB, LDN, t0, g.L, tid);
-  load_rows<128>(bcb, 2 * N, N, N, sC, LDN, t0, g.L, tid);
-  load_rows<128>(pb, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
-  load_rows<128>(pb, g.ldp, h * P, P, sZ, LDP, t0, g.L, tid);
+  load_rows<256>(bcb, 2 * N, 0, N, sB, LDN, t0, g.L, tid);
+  load_rows<256>(bcb, 2 * N, N, N, sC, LDN, t0, g.L, tid);
+  load_rows<256>(pb, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
+  load_rows<256>(pb, g.ldp, h * P, P, sZ, LDP, t0, g.L, tid);
   {
     const bf16* src = states + state_off(g, b, h, c);
-    for (int i = tid; i < P * N / 8; i += 128) {
+    for (int i = tid; i < P * N / 8; i += 256) {
       int r = i / (N / 8), ch = i % (N / 8);
       cp_async16(sSt + r * LDN + ch * 8, src + r * N + ch * 8);
     }
   }
   cp_async_commit();
-  load_scalars<128>(in, g, b, h, t0, sDT, sADT, sSig, sRate, tid);
-  for (int i = tid; i < N; i += 128) {
+  load_scalars<256>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
+  for (int i = tid; i < N; i += 256) {
     sCbv[i] = in.Cb[h * N + i];
     sBbv[i] = in.Bb[h * N + i];
   }
@@ -457,14 +467,14 @@ __global__ void __launch_bounds__(128, 2)
   cp_async_wait_all();
   __syncthreads();
   row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
-  chunk_angles<128>(sRate, sDT, sTh0, sTh, sSeg, tid);
-  build_qk<128>(sC, sB, sC, sB, sTh, sScl, sCbv, sBbv, sQKr, tid);
+  chunk_angles<256>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
+  build_qk<256>(sC, sB, sC, sB, sCos, sSin, sScl, sCbv, sBbv, sQKr, tid);
 
   const int r0 = m0 + gq, r1 = r0 + 8;
   const float cum0 = sCum[r0], cum1 = sCum[r1];
-  float sacc[8][4], yacc[8][4];
+  float sacc[4][4], yacc[4][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int e = 0; e < 4; ++e) sacc[i][e] = yacc[i][e] = 0.f;
 #pragma unroll
@@ -472,35 +482,38 @@ __global__ void __launch_bounds__(128, 2)
     uint32_t a[4];
     load_a(a, sC, LDN, m0, kk * 16, lane);
 #pragma unroll
-    for (int np = 0; np < 4; ++np) {
+    for (int np = 0; np < 2; ++np) {
       uint32_t bb[4];
-      load_b_nk(bb, sB, LDN, np * 16, kk * 16, lane);
+      load_b_nk(bb, sB, LDN, c32 + np * 16, kk * 16, lane);
       mma_bf16(sacc[2 * np], a, bb[0], bb[1]);
       mma_bf16(sacc[2 * np + 1], a, bb[2], bb[3]);
-      load_b_nk(bb, sSt, LDN, np * 16, kk * 16, lane);
+      load_b_nk(bb, sSt, LDN, c32 + np * 16, kk * 16, lane);
       mma_bf16(yacc[2 * np], a, bb[0], bb[1]);
       mma_bf16(yacc[2 * np + 1], a, bb[2], bb[3]);
     }
   }
   const float e0 = __expf(cum0), e1 = __expf(cum1);
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    int s0c = nt * 8 + 2 * tq;
+  for (int nt = 0; nt < 4; ++nt) {
+    int s0c = c32 + nt * 8 + 2 * tq;
     float cs0 = sCum[s0c], cs1 = sCum[s0c + 1];
-    sacc[nt][0] = (s0c < r0) ? sacc[nt][0] * __expf(cum0 - cs0) : 0.f;
-    sacc[nt][1] = (s0c + 1 < r0) ? sacc[nt][1] * __expf(cum0 - cs1) : 0.f;
-    sacc[nt][2] = (s0c < r1) ? sacc[nt][2] * __expf(cum1 - cs0) : 0.f;
-    sacc[nt][3] = (s0c + 1 < r1) ? sacc[nt][3] * __expf(cum1 - cs1) : 0.f;
+    float p0 = (s0c < r0) ? sacc[nt][0] * __expf(cum0 - cs0) : 0.f;
+    float p1 = (s0c + 1 < r0) ? sacc[nt][1] * __expf(cum0 - cs1) : 0.f;
+    float p2 = (s0c < r1) ? sacc[nt][2] * __expf(cum1 - cs0) : 0.f;
+    float p3 = (s0c + 1 < r1) ? sacc[nt][3] * __expf(cum1 - cs1) : 0.f;
+    *reinterpret_cast<uint32_t*>(sP + r0 * LDP + s0c) = pack_bf16(p0, p1);
+    *reinterpret_cast<uint32_t*>(sP + r1 * LDP + s0c) = pack_bf16(p2, p3);
     yacc[nt][0] *= e0; yacc[nt][1] *= e0; yacc[nt][2] *= e1; yacc[nt][3] *= e1;
   }
+  __syncthreads();
 #pragma unroll
   for (int kk = 0; kk < CS / 16; ++kk) {
     uint32_t a[4];
-    acc_to_a(a, sacc[2 * kk], sacc[2 * kk + 1]);
+    load_a(a, sP, LDP, m0, kk * 16, lane);
 #pragma unroll
-    for (int np = 0; np < 4; ++np) {
+    for (int np = 0; np < 2; ++np) {
       uint32_t bb[4];
-      load_b_kn(bb, sX, LDP, np * 16, kk * 16, lane);
+      load_b_kn(bb, sX, LDP, c32 + np * 16, kk * 16, lane);
       mma_bf16(yacc[2 * np], a, bb[0], bb[1]);
       mma_bf16(yacc[2 * np + 1], a, bb[2], bb[3]);
     }
@@ -508,8 +521,8 @@ __global__ void __launch_bounds__(128, 2)
   const float Dh = in.D[h];
   const float q0 = Dh + sQKr[r0] * sGam[r0], q1 = Dh + sQKr[r1] * sGam[r1];
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    int p = nt * 8 + 2 * tq;
+  for (int nt = 0; nt < 4; ++nt) {
+    int p = c32 + nt * 8 + 2 * tq;
     float2 v0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sX + r0 * LDP + p));
     float2 v1 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sX + r1 * LDP + p));
     float2 z0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sZ + r0 * LDP + p));
@@ -521,32 +534,32 @@ __global__ void __launch_bounds__(128, 2)
     *reinterpret_cast<uint32_t*>(sZ + r0 * LDP + p) = pack_bf16(a0, a1);
     *reinterpret_cast<uint32_t*>(sZ + r1 * LDP + p) = pack_bf16(a2, a3);
   }
-  __syncwarp();
-  for (int i = lane; i < 16 * 8; i += 32) {
+  __syncthreads();
+  for (int i = tid; i < CS * 8; i += 256) {
     int r = i >> 3, ch = i & 7;
-    int tt = t0 + m0 + r;
+    int tt = t0 + r;
     if (tt < g.L)
       *reinterpret_cast<uint4*>(y + ((size_t)b * g.L + tt) * g.d_inner + h * P + ch * 8) =
-          *reinterpret_cast<const uint4*>(sZ + (m0 + r) * LDP + ch * 8);
+          *reinterpret_cast<const uint4*>(sZ + r * LDP + ch * 8);
   }
 }
 
 // ---------------------------------------------------------------------------
-// B1: per-chunk dstate contribution U_c[p][n] = sum_l exp(cum_l) dY0[l][p] Q[l][n]
-// with dY0 = dy * silu(z)  (128 threads)
+// B1: per-chunk dstate contribution U_c[p][n] = sum_l exp(cum_l) dY0[l][p] Q[l][n],
+// dY0 = dy * silu(z)  (256 threads: p rows rb, n halves cg)
 // ---------------------------------------------------------------------------
 constexpr size_t DST_SMEM = sizeof(bf16) * (CS * LDN + 2 * CS * LDP) +
-                            sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 4 * CS + N + 4 * 32 + 32);
+                            sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 4 * CS + N + 8 * 32 + 32);
 
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
     m3_chunk_dstate(ScanIn in, Geo g, const bf16* __restrict__ dy, bf16* __restrict__ U) {
   extern __shared__ __align__(16) unsigned char smem[];
   bf16* sC = reinterpret_cast<bf16*>(smem);
   bf16* sZ = sC + CS * LDN;
   bf16* sdY = sZ + CS * LDP;
-  float* sRate = reinterpret_cast<float*>(sdY + CS * LDP);
-  float* sTh = sRate + CS * RP;
-  float* sDT = sTh + CS * RP;
+  float* sSin = reinterpret_cast<float*>(sdY + CS * LDP);
+  float* sCos = sSin + CS * RP;
+  float* sDT = sCos + CS * RP;
   float* sSig = sDT + CS + 1;
   float* sADT = sSig + CS + 1;
   float* sCum = sADT + CS;
@@ -554,25 +567,26 @@ __global__ void __launch_bounds__(128)
   float* sScl = sGam + CS;
   float* sCbv = sScl + CS;
   float* sSeg = sCbv + N;
-  float* sTh0 = sSeg + 4 * 32;
+  float* sTh0 = sSeg + 8 * 32;
 
   const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
-  const int t0 = c * CS, m0 = warp * 16;
+  const int rb = warp & 3, cg = warp >> 2;
+  const int t0 = c * CS, m0 = rb * 16;
   const size_t bh = (size_t)b * g.nh + h;
-  load_rows<128>(in.bc + (size_t)b * g.L * 2 * N, 2 * N, N, N, sC, LDN, t0, g.L, tid);
-  load_rows<128>(in.proj + (size_t)b * g.L * g.ldp, g.ldp, h * P, P, sZ, LDP, t0, g.L, tid);
-  load_rows<128>(dy + (size_t)b * g.L * g.d_inner, g.d_inner, h * P, P, sdY, LDP, t0, g.L, tid);
+  load_rows<256>(in.bc + (size_t)b * g.L * 2 * N, 2 * N, N, N, sC, LDN, t0, g.L, tid);
+  load_rows<256>(in.proj + (size_t)b * g.L * g.ldp, g.ldp, h * P, P, sZ, LDP, t0, g.L, tid);
+  load_rows<256>(dy + (size_t)b * g.L * g.d_inner, g.d_inner, h * P, P, sdY, LDP, t0, g.L, tid);
   cp_async_commit();
-  load_scalars<128>(in, g, b, h, t0, sDT, sADT, sSig, sRate, tid);
-  for (int i = tid; i < N; i += 128) sCbv[i] = in.Cb[h * N + i];
+  load_scalars<256>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
+  for (int i = tid; i < N; i += 256) sCbv[i] = in.Cb[h * N + i];
   if (tid < 32) sTh0[tid] = in.theta0[(bh * g.nc + c) * R + tid];
   cp_async_wait_all();
   __syncthreads();
   row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
-  chunk_angles<128>(sRate, sDT, sTh0, sTh, sSeg, tid);
-  build_qk<128>(sC, nullptr, sC, nullptr, sTh, sScl, sCbv, nullptr, nullptr, tid);
-  for (int i = tid; i < CS * P / 2; i += 128) {
+  chunk_angles<256>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
+  build_qk<256>(sC, nullptr, sC, nullptr, sCos, sSin, sScl, sCbv, nullptr, nullptr, tid);
+  for (int i = tid; i < CS * P / 2; i += 256) {
     int r = i / (P / 2), p = 2 * (i % (P / 2));
     float2 z = unpack_bf16(*reinterpret_cast<const uint32_t*>(sZ + r * LDP + p));
     float2 d = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdY + r * LDP + p));
@@ -581,32 +595,32 @@ __global__ void __launch_bounds__(128)
         pack_bf16(d.x * z.x * sigmoidf_(z.x) * e, d.y * z.y * sigmoidf_(z.y) * e);
   }
   __syncthreads();
-  float acc[16][4];
+  float acc[8][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 #pragma unroll
   for (int kk = 0; kk < CS / 16; ++kk) {
     uint32_t a[4];
     load_a_t(a, sdY, LDP, m0, kk * 16, lane);
 #pragma unroll
-    for (int np = 0; np < 8; ++np) {
+    for (int np = 0; np < 4; ++np) {
       uint32_t bb[4];
-      load_b_kn(bb, sC, LDN, np * 16, kk * 16, lane);
+      load_b_kn(bb, sC, LDN, cg * 64 + np * 16, kk * 16, lane);
       mma_bf16(acc[2 * np], a, bb[0], bb[1]);
       mma_bf16(acc[2 * np + 1], a, bb[2], bb[3]);
     }
   }
   bf16* dst = U + state_off(g, b, h, c);
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
-    int n = nt * 8 + 2 * tq;
+  for (int nt = 0; nt < 8; ++nt) {
+    int n = cg * 64 + nt * 8 + 2 * tq;
     *reinterpret_cast<uint32_t*>(dst + (m0 + gq) * N + n) = pack_bf16(acc[nt][0], acc[nt][1]);
     *reinterpret_cast<uint32_t*>(dst + (m0 + gq + 8) * N + n) = pack_bf16(acc[nt][2], acc[nt][3]);
   }
 }
 
 // ---------------------------------------------------------------------------
-// B3: chunk backward (256 threads: warp w owns rows (w&3)*16 and column half w>>2)
+// B3: chunk backward (512 threads: rows rb = warp&3, column quarters cq = warp>>2)
 // ---------------------------------------------------------------------------
 struct BwdOut {
   bf16* dproj;          // dz / dx columns are written here
@@ -618,10 +632,12 @@ struct BwdOut {
   float *dD, *dCb, *dBb;             // [B, nh, nc], [B, nh, nc, N] x2
 };
 
+constexpr int BWD_NT = 512;
 constexpr size_t BWD_SMEM = sizeof(bf16) * (5 * CS * LDN + 5 * CS * LDP) +
-                            sizeof(float) * (3 * CS * RP + 2 * (CS + 1) + 9 * CS + 4 * N + 8 * 32 + 32 + 8);
+                            sizeof(float) * (3 * CS * RP + 2 * (CS + 1) + 9 * CS + 4 * N + 16 * 32 + 32 + 16 +
+                                             16);
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(BWD_NT, 1)
     m3_chunk_bwd(ScanIn in, Geo g, const bf16* __restrict__ dy, const bf16* __restrict__ states,
                  const bf16* __restrict__ dsout, BwdOut out) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -635,9 +651,9 @@ __global__ void __launch_bounds__(256, 1)
   bf16* sdY = sZ + CS * LDP;                  // dy -> dY0
   bf16* sP = sdY + CS * LDP;
   bf16* sdS = sP + CS * LDP;
-  float* sRate = reinterpret_cast<float*>(sdS + CS * LDP);
-  float* sTh = sRate + CS * RP;
-  float* sDth = sTh + CS * RP;
+  float* sSin = reinterpret_cast<float*>(sdS + CS * LDP);
+  float* sCos = sSin + CS * RP;
+  float* sDth = sCos + CS * RP;
   float* sDT = sDth + CS * RP;
   float* sSig = sDT + CS + 1;
   float* sADT = sSig + CS + 1;
@@ -653,34 +669,36 @@ __global__ void __launch_bounds__(256, 1)
   float* sBbv = sCbv + N;
   float* sDcb = sBbv + N;
   float* sDbb = sDcb + N;
-  float* sSeg = sDbb + N;       // [8][32]
-  float* sTh0 = sSeg + 8 * 32;  // [32]
-  float* sMisc = sTh0 + 32;     // [8]
+  float* sSeg = sDbb + N;        // [16][32]
+  float* sTh0 = sSeg + 16 * 32;  // [32]
+  float* sMisc = sTh0 + 32;      // [16]
+  float* sDD = sMisc + 16;       // [16]
 
   const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
-  const int rw = warp & 3, hf = warp >> 2;
-  const int t0 = c * CS, m0 = rw * 16;
+  const int rb = warp & 3, cq = warp >> 2;
+  const int c16 = cq * 16, c32 = cq * 32;
+  const int t0 = c * CS, m0 = rb * 16;
   const size_t bh = (size_t)b * g.nh + h;
   const bf16* bcb = in.bc + (size_t)b * g.L * 2 * N;
   const bf16* pb = in.proj + (size_t)b * g.L * g.ldp;
-  load_rows<256>(bcb, 2 * N, 0, N, sBn, LDN, t0, g.L, tid);
-  load_rows<256>(bcb, 2 * N, N, N, sQ, LDN, t0, g.L, tid);
-  load_rows<256>(pb, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
-  load_rows<256>(pb, g.ldp, h * P, P, sZ, LDP, t0, g.L, tid);
-  load_rows<256>(dy + (size_t)b * g.L * g.d_inner, g.d_inner, h * P, P, sdY, LDP, t0, g.L, tid);
+  load_rows<BWD_NT>(bcb, 2 * N, 0, N, sBn, LDN, t0, g.L, tid);
+  load_rows<BWD_NT>(bcb, 2 * N, N, N, sQ, LDN, t0, g.L, tid);
+  load_rows<BWD_NT>(pb, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
+  load_rows<BWD_NT>(pb, g.ldp, h * P, P, sZ, LDP, t0, g.L, tid);
+  load_rows<BWD_NT>(dy + (size_t)b * g.L * g.d_inner, g.d_inner, h * P, P, sdY, LDP, t0, g.L, tid);
   {
     const bf16* s1 = states + state_off(g, b, h, c);
     const bf16* s2 = dsout + state_off(g, b, h, c);
-    for (int i = tid; i < P * N / 8; i += 256) {
+    for (int i = tid; i < P * N / 8; i += BWD_NT) {
       int r = i / (N / 8), ch = i % (N / 8);
       cp_async16(sSt + r * LDN + ch * 8, s1 + r * N + ch * 8);
       cp_async16(sdSt + r * LDN + ch * 8, s2 + r * N + ch * 8);
     }
   }
   cp_async_commit();
-  load_scalars<256>(in, g, b, h, t0, sDT, sADT, sSig, sRate, tid);
-  for (int i = tid; i < N; i += 256) {
+  load_scalars<BWD_NT>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
+  for (int i = tid; i < N; i += BWD_NT) {
     sCbv[i] = in.Cb[h * N + i];
     sBbv[i] = in.Bb[h * N + i];
     sDcb[i] = 0.f;
@@ -691,20 +709,24 @@ __global__ void __launch_bounds__(256, 1)
   cp_async_wait_all();
   __syncthreads();
   row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
-  chunk_angles<256>(sRate, sDT, sTh0, sTh, sSeg, tid);
-  build_qk<256>(sQ, sBn, sQ, sK, sTh, sScl, sCbv, sBbv, sQKr, tid);
+  chunk_angles<BWD_NT>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
+  build_qk<BWD_NT>(sQ, sBn, sQ, sK, sCos, sSin, sScl, sCbv, sBbv, sQKr, tid);
   const float cend = sCum[CS - 1];
   if (tid < CS) sW[tid] = __expf(cend - sCum[tid]);
-  // dcum_end: sum(dS_out * S_out), S_out = S_in of the next chunk (zero gradient after the last)
-  {
+  {   // d cum_end: sum(dS_out * S_out), S_out = S_in of the next chunk (no gradient past the last)
     float dot = 0.f;
     if (c + 1 < g.nc) {
       const bf16* so = states + state_off(g, b, h, c + 1);
-      for (int i = tid; i < P * N / 2; i += 256) {
-        int r = (2 * i) / N, n = (2 * i) % N;
-        float2 a = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdSt + r * LDN + n));
-        float2 s = unpack_bf16(*reinterpret_cast<const uint32_t*>(so + r * N + n));
-        dot += a.x * s.x + a.y * s.y;
+      for (int i = tid; i < P * N / 8; i += BWD_NT) {
+        int r = i / (N / 8), ch = i % (N / 8);
+        uint4 sv = *reinterpret_cast<const uint4*>(so + r * N + ch * 8);
+        uint4 dv = *reinterpret_cast<const uint4*>(sdSt + r * LDN + ch * 8);
+        uint32_t a[4] = {sv.x, sv.y, sv.z, sv.w}, d[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float2 x = unpack_bf16(a[k]), y2 = unpack_bf16(d[k]);
+          dot += x.x * y2.x + x.y * y2.y;
+        }
       }
     }
     dot = warp_sum(dot);
@@ -717,34 +739,28 @@ __global__ void __launch_bounds__(256, 1)
   const float e0 = __expf(cum0), e1 = __expf(cum1);
   const float Dh = in.D[h];
   const float q0 = Dh + sQKr[r0] * sGam[r0], q1 = Dh + sQKr[r1] * sGam[r1];
-  const int c32 = hf * 32;   // this warp's 32-column slice of 64-wide outputs
-  const int c64 = hf * 64;   // this warp's 64-column slice of 128-wide outputs
   float dD_acc = 0.f;
 
-  // ---- A: P (cols c32..), Y_off, then P V; dY0, dz -------------------------------------
-  float pacc[4][4], yacc[4][4];
+  // ---- A: P (cols c16..), Y_off, then P V; dY0, dz --------------------------------------
+  float pacc[2][4], yacc[2][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < 2; ++i)
 #pragma unroll
     for (int e = 0; e < 4; ++e) pacc[i][e] = yacc[i][e] = 0.f;
 #pragma unroll
   for (int kk = 0; kk < N / 16; ++kk) {
-    uint32_t a[4];
+    uint32_t a[4], bb[4];
     load_a(a, sQ, LDN, m0, kk * 16, lane);
-#pragma unroll
-    for (int np = 0; np < 2; ++np) {
-      uint32_t bb[4];
-      load_b_nk(bb, sK, LDN, c32 + np * 16, kk * 16, lane);
-      mma_bf16(pacc[2 * np], a, bb[0], bb[1]);
-      mma_bf16(pacc[2 * np + 1], a, bb[2], bb[3]);
-      load_b_nk(bb, sSt, LDN, c32 + np * 16, kk * 16, lane);
-      mma_bf16(yacc[2 * np], a, bb[0], bb[1]);
-      mma_bf16(yacc[2 * np + 1], a, bb[2], bb[3]);
-    }
+    load_b_nk(bb, sK, LDN, c16, kk * 16, lane);
+    mma_bf16(pacc[0], a, bb[0], bb[1]);
+    mma_bf16(pacc[1], a, bb[2], bb[3]);
+    load_b_nk(bb, sSt, LDN, c16, kk * 16, lane);
+    mma_bf16(yacc[0], a, bb[0], bb[1]);
+    mma_bf16(yacc[1], a, bb[2], bb[3]);
   }
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
-    int s0c = c32 + nt * 8 + 2 * tq;
+  for (int nt = 0; nt < 2; ++nt) {
+    int s0c = c16 + nt * 8 + 2 * tq;
     float cs0 = sCum[s0c], cs1 = sCum[s0c + 1];
     pacc[nt][0] = (s0c < r0) ? pacc[nt][0] * __expf(cum0 - cs0) : 0.f;
     pacc[nt][1] = (s0c + 1 < r0) ? pacc[nt][1] * __expf(cum0 - cs1) : 0.f;
@@ -756,25 +772,21 @@ __global__ void __launch_bounds__(256, 1)
   }
   __syncthreads();
   {
-    float vacc[4][4];
+    float vacc[2][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) vacc[i][0] = vacc[i][1] = vacc[i][2] = vacc[i][3] = 0.f;
+    for (int i = 0; i < 2; ++i) vacc[i][0] = vacc[i][1] = vacc[i][2] = vacc[i][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < CS / 16; ++kk) {
-      uint32_t a[4];
+      uint32_t a[4], bb[4];
       load_a(a, sP, LDP, m0, kk * 16, lane);
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t bb[4];
-        load_b_kn(bb, sX, LDP, c32 + np * 16, kk * 16, lane);
-        mma_bf16(vacc[2 * np], a, bb[0], bb[1]);
-        mma_bf16(vacc[2 * np + 1], a, bb[2], bb[3]);
-      }
+      load_b_kn(bb, sX, LDP, c16, kk * 16, lane);
+      mma_bf16(vacc[0], a, bb[0], bb[1]);
+      mma_bf16(vacc[1], a, bb[2], bb[3]);
     }
     float dq0 = 0.f, dq1 = 0.f, dc0 = 0.f, dc1 = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      int p = c32 + nt * 8 + 2 * tq;
+    for (int nt = 0; nt < 2; ++nt) {
+      int p = c16 + nt * 8 + 2 * tq;
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr) {
         int row = hr ? r1 : r0;
@@ -812,27 +824,23 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
   __syncthreads();   // sdY (dY0) complete
-  // ---- B: dP = dY0 V^T (cols c32..) -> dS, G = dP * P ------------------------------------
-  float dsacc[4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) dsacc[i][0] = dsacc[i][1] = dsacc[i][2] = dsacc[i][3] = 0.f;
-#pragma unroll
-  for (int kk = 0; kk < P / 16; ++kk) {
-    uint32_t a[4];
-    load_a(a, sdY, LDP, m0, kk * 16, lane);
-#pragma unroll
-    for (int np = 0; np < 2; ++np) {
-      uint32_t bb[4];
-      load_b_nk(bb, sX, LDP, c32 + np * 16, kk * 16, lane);
-      mma_bf16(dsacc[2 * np], a, bb[0], bb[1]);
-      mma_bf16(dsacc[2 * np + 1], a, bb[2], bb[3]);
-    }
-  }
+  // ---- B: dP = dY0 V^T (cols c16..) -> dS, G = dP * P ------------------------------------
   {
+    float dsacc[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) dsacc[i][0] = dsacc[i][1] = dsacc[i][2] = dsacc[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < P / 16; ++kk) {
+      uint32_t a[4], bb[4];
+      load_a(a, sdY, LDP, m0, kk * 16, lane);
+      load_b_nk(bb, sX, LDP, c16, kk * 16, lane);
+      mma_bf16(dsacc[0], a, bb[0], bb[1]);
+      mma_bf16(dsacc[1], a, bb[2], bb[3]);
+    }
     float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      int s0c = c32 + nt * 8 + 2 * tq;
+    for (int nt = 0; nt < 2; ++nt) {
+      int s0c = c16 + nt * 8 + 2 * tq;
       float cs0 = sCum[s0c], cs1 = sCum[s0c + 1];
       float f00 = (s0c < r0) ? __expf(cum0 - cs0) : 0.f;
       float f01 = (s0c + 1 < r0) ? __expf(cum0 - cs1) : 0.f;
@@ -852,9 +860,8 @@ __global__ void __launch_bounds__(256, 1)
         atomicAdd(&sDcum[s0c], -ca);
         atomicAdd(&sDcum[s0c + 1], -cb);
       }
-      dsacc[nt][0] *= f00; dsacc[nt][1] *= f01; dsacc[nt][2] *= f10; dsacc[nt][3] *= f11;
-      *reinterpret_cast<uint32_t*>(sdS + r0 * LDP + s0c) = pack_bf16(dsacc[nt][0], dsacc[nt][1]);
-      *reinterpret_cast<uint32_t*>(sdS + r1 * LDP + s0c) = pack_bf16(dsacc[nt][2], dsacc[nt][3]);
+      *reinterpret_cast<uint32_t*>(sdS + r0 * LDP + s0c) = pack_bf16(dsacc[nt][0] * f00, dsacc[nt][1] * f01);
+      *reinterpret_cast<uint32_t*>(sdS + r1 * LDP + s0c) = pack_bf16(dsacc[nt][2] * f10, dsacc[nt][3] * f11);
     }
     rs0 += __shfl_xor_sync(0xffffffffu, rs0, 1); rs0 += __shfl_xor_sync(0xffffffffu, rs0, 2);
     rs1 += __shfl_xor_sync(0xffffffffu, rs1, 1); rs1 += __shfl_xor_sync(0xffffffffu, rs1, 2);
@@ -864,25 +871,25 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
   __syncthreads();   // sdS complete
-  // ---- C: dQ = exp(cum_l) dY0 S_in + dS K  (cols c64..) -> gQ, dtheta, dC_bias ---------
+  // ---- C: dQ = exp(cum_l) dY0 S_in + dS K  (cols c32..) -> gQ, dtheta, dC_bias ---------
   {
-    float qacc[8][4];
+    float qacc[4][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) qacc[i][0] = qacc[i][1] = qacc[i][2] = qacc[i][3] = 0.f;
+    for (int i = 0; i < 4; ++i) qacc[i][0] = qacc[i][1] = qacc[i][2] = qacc[i][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < P / 16; ++kk) {
       uint32_t a[4];
       load_a(a, sdY, LDP, m0, kk * 16, lane);
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {
+      for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
-        load_b_kn(bb, sSt, LDN, c64 + np * 16, kk * 16, lane);
+        load_b_kn(bb, sSt, LDN, c32 + np * 16, kk * 16, lane);
         mma_bf16(qacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(qacc[2 * np + 1], a, bb[2], bb[3]);
       }
     }
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < 4; ++nt) {
       qacc[nt][0] *= e0; qacc[nt][1] *= e0; qacc[nt][2] *= e1; qacc[nt][3] *= e1;
     }
 #pragma unroll
@@ -890,9 +897,9 @@ __global__ void __launch_bounds__(256, 1)
       uint32_t a[4];
       load_a(a, sdS, LDP, m0, kk * 16, lane);
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {
+      for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
-        load_b_kn(bb, sK, LDN, c64 + np * 16, kk * 16, lane);
+        load_b_kn(bb, sK, LDN, c32 + np * 16, kk * 16, lane);
         mma_bf16(qacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(qacc[2 * np + 1], a, bb[2], bb[3]);
       }
@@ -904,14 +911,13 @@ __global__ void __launch_bounds__(256, 1)
       float gm = sGam[row] * sDqk[row];
       bf16* dst = out.gQ + (((size_t)b * g.L + (tt < g.L ? tt : 0)) * g.nh + h) * N;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        int n = c64 + nt * 8 + 2 * tq;
+      for (int nt = 0; nt < 4; ++nt) {
+        int n = c32 + nt * 8 + 2 * tq;
         float g0 = qacc[nt][hr * 2], g1 = qacc[nt][hr * 2 + 1];
         float d0, d1;
         if (n < 2 * R) {
           int r = n >> 1;
-          float sn, cs;
-          sincosf(sTh[row * RP + r], &sn, &cs);
+          float sn = sSin[row * RP + r], cs = sCos[row * RP + r];
           float2 q = unpack_bf16(*reinterpret_cast<const uint32_t*>(sQ + row * LDN + n));
           sDth[row * RP + r] = -g0 * q.y + g1 * q.x;
           d0 = g0 * cs + g1 * sn;
@@ -930,7 +936,7 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < 4; ++nt) {
       float a0 = qacc[nt][0] + qacc[nt][2], a1 = qacc[nt][1] + qacc[nt][3];
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) {
@@ -938,31 +944,31 @@ __global__ void __launch_bounds__(256, 1)
         a1 += __shfl_xor_sync(0xffffffffu, a1, o);
       }
       if (gq == 0) {
-        atomicAdd(&sDcb[c64 + nt * 8 + 2 * tq], a0);
-        atomicAdd(&sDcb[c64 + nt * 8 + 2 * tq + 1], a1);
+        atomicAdd(&sDcb[c32 + nt * 8 + 2 * tq], a0);
+        atomicAdd(&sDcb[c32 + nt * 8 + 2 * tq + 1], a1);
       }
     }
   }
-  // ---- D: dK = w_s (V dS_out) + dS^T Q  (cols c64..) -> gK, dscale, dtheta, dB_bias ------
+  // ---- D: dK = w_s (V dS_out) + dS^T Q  (cols c32..) -> gK, dscale, dtheta, dB_bias ------
   {
-    float kacc[8][4];
+    float kacc[4][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) kacc[i][0] = kacc[i][1] = kacc[i][2] = kacc[i][3] = 0.f;
+    for (int i = 0; i < 4; ++i) kacc[i][0] = kacc[i][1] = kacc[i][2] = kacc[i][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < P / 16; ++kk) {
       uint32_t a[4];
       load_a(a, sX, LDP, m0, kk * 16, lane);
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {
+      for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
-        load_b_kn(bb, sdSt, LDN, c64 + np * 16, kk * 16, lane);
+        load_b_kn(bb, sdSt, LDN, c32 + np * 16, kk * 16, lane);
         mma_bf16(kacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(kacc[2 * np + 1], a, bb[2], bb[3]);
       }
     }
     const float w0 = sW[r0], w1 = sW[r1];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < 4; ++nt) {
       kacc[nt][0] *= w0; kacc[nt][1] *= w0; kacc[nt][2] *= w1; kacc[nt][3] *= w1;
     }
 #pragma unroll
@@ -970,9 +976,9 @@ __global__ void __launch_bounds__(256, 1)
       uint32_t a[4];
       load_a_t(a, sdS, LDP, m0, kk * 16, lane);
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {
+      for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
-        load_b_kn(bb, sQ, LDN, c64 + np * 16, kk * 16, lane);
+        load_b_kn(bb, sQ, LDN, c32 + np * 16, kk * 16, lane);
         mma_bf16(kacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(kacc[2 * np + 1], a, bb[2], bb[3]);
       }
@@ -987,8 +993,8 @@ __global__ void __launch_bounds__(256, 1)
       bf16* dst = out.gK + (((size_t)b * g.L + (tt < g.L ? tt : 0)) * g.nh + h) * N;
       float dsc = 0.f;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        int n = c64 + nt * 8 + 2 * tq;
+      for (int nt = 0; nt < 4; ++nt) {
+        int n = c32 + nt * 8 + 2 * tq;
         float g0 = kacc[nt][hr * 2], g1 = kacc[nt][hr * 2 + 1];
         float2 bn = unpack_bf16(*reinterpret_cast<const uint32_t*>(sBn + row * LDN + n));
         float b0 = bn.x + sBbv[n], b1 = bn.y + sBbv[n + 1];
@@ -996,8 +1002,7 @@ __global__ void __launch_bounds__(256, 1)
         float d0, d1, cb0, cb1;
         if (n < 2 * R) {
           int r = n >> 1;
-          float sn, cs;
-          sincosf(sTh[row * RP + r], &sn, &cs);
+          float sn = sSin[row * RP + r], cs = sCos[row * RP + r];
           float k0 = b0 * cs - b1 * sn, k1 = b0 * sn + b1 * cs;
           dsc += g0 * k0 + g1 * k1;
           float h0 = g0 * sc, h1 = g1 * sc;
@@ -1029,7 +1034,7 @@ __global__ void __launch_bounds__(256, 1)
       atomicAdd(&sDscl[r1], dsc1);
     }
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < 4; ++nt) {
       float a0 = kacc[nt][0] + kacc[nt][2], a1 = kacc[nt][1] + kacc[nt][3];
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) {
@@ -1037,34 +1042,30 @@ __global__ void __launch_bounds__(256, 1)
         a1 += __shfl_xor_sync(0xffffffffu, a1, o);
       }
       if (gq == 0) {
-        atomicAdd(&sDbb[c64 + nt * 8 + 2 * tq], a0);
-        atomicAdd(&sDbb[c64 + nt * 8 + 2 * tq + 1], a1);
+        atomicAdd(&sDbb[c32 + nt * 8 + 2 * tq], a0);
+        atomicAdd(&sDbb[c32 + nt * 8 + 2 * tq + 1], a1);
       }
     }
   }
   __syncthreads();   // every warp done reading sX (V) as an MMA operand
-  // ---- E: dV = w_s (K dS_out^T) + P^T dY0 + (D+qk) dY0  (cols c32..) ------------------
+  // ---- E: dV = w_s (K dS_out^T) + P^T dY0 + (D+qk) dY0  (cols c16..) ------------------
   {
-    float vacc2[4][4];
+    float vacc2[2][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) vacc2[i][0] = vacc2[i][1] = vacc2[i][2] = vacc2[i][3] = 0.f;
+    for (int i = 0; i < 2; ++i) vacc2[i][0] = vacc2[i][1] = vacc2[i][2] = vacc2[i][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < N / 16; ++kk) {
-      uint32_t a[4];
+      uint32_t a[4], bb[4];
       load_a(a, sK, LDN, m0, kk * 16, lane);
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t bb[4];
-        load_b_nk(bb, sdSt, LDN, c32 + np * 16, kk * 16, lane);
-        mma_bf16(vacc2[2 * np], a, bb[0], bb[1]);
-        mma_bf16(vacc2[2 * np + 1], a, bb[2], bb[3]);
-      }
+      load_b_nk(bb, sdSt, LDN, c16, kk * 16, lane);
+      mma_bf16(vacc2[0], a, bb[0], bb[1]);
+      mma_bf16(vacc2[1], a, bb[2], bb[3]);
     }
     const float w0 = sW[r0], w1 = sW[r1];
     float dcs0 = 0.f, dcs1 = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      int p = c32 + nt * 8 + 2 * tq;
+    for (int nt = 0; nt < 2; ++nt) {
+      int p = c16 + nt * 8 + 2 * tq;
       float2 v0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sX + r0 * LDP + p));
       float2 v1 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sX + r1 * LDP + p));
       vacc2[nt][0] *= w0; vacc2[nt][1] *= w0; vacc2[nt][2] *= w1; vacc2[nt][3] *= w1;
@@ -1079,19 +1080,15 @@ __global__ void __launch_bounds__(256, 1)
     }
 #pragma unroll
     for (int kk = 0; kk < CS / 16; ++kk) {
-      uint32_t a[4];
+      uint32_t a[4], bb[4];
       load_a_t(a, sP, LDP, m0, kk * 16, lane);
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t bb[4];
-        load_b_kn(bb, sdY, LDP, c32 + np * 16, kk * 16, lane);
-        mma_bf16(vacc2[2 * np], a, bb[0], bb[1]);
-        mma_bf16(vacc2[2 * np + 1], a, bb[2], bb[3]);
-      }
+      load_b_kn(bb, sdY, LDP, c16, kk * 16, lane);
+      mma_bf16(vacc2[0], a, bb[0], bb[1]);
+      mma_bf16(vacc2[1], a, bb[2], bb[3]);
     }
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      int p = c32 + nt * 8 + 2 * tq;
+    for (int nt = 0; nt < 2; ++nt) {
+      int p = c16 + nt * 8 + 2 * tq;
       float2 d0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdY + r0 * LDP + p));
       float2 d1 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdY + r1 * LDP + p));
       *reinterpret_cast<uint32_t*>(sX + r0 * LDP + p) =
@@ -1101,19 +1098,18 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
   // ---- F: reductions and stores ------------------------------------------------------------
-  __shared__ float sDD[8];
   {
     float dd = warp_sum(dD_acc);
     if (lane == 0) sDD[warp] = dd;
   }
-  __syncthreads();   // all atomics on sDcum/sDscl/sDqk/sDth done; sX holds dV, sZ holds dz
+  __syncthreads();   // all shared atomics done; sX holds dV, sZ holds dz
   if (tid == 0) {
     float dot = 0.f, s = 0.f;
-    for (int k = 0; k < 8; ++k) { dot += sMisc[k]; s += sDD[k]; }
+    for (int k = 0; k < BWD_NT / 32; ++k) { dot += sMisc[k]; s += sDD[k]; }
     sDcum[CS - 1] += dot;
     out.dD[bh * g.nc + c] = s;
   }
-  for (int i = tid; i < CS * 8; i += 256) {
+  for (int i = tid; i < CS * 8; i += BWD_NT) {
     int r = i >> 3, ch = i & 7;
     int tt = t0 + r;
     if (tt < g.L) {
@@ -1124,11 +1120,13 @@ __global__ void __launch_bounds__(256, 1)
           *reinterpret_cast<const uint4*>(sZ + r * LDP + ch * 8);
     }
   }
-  {   // dtheta: within-segment suffix sums (thread r, 8 segments of 8 rows)
+  constexpr int NSEG = BWD_NT / 32, RPS = CS / NSEG;
+  {   // dtheta: within-segment suffix sums (thread r, NSEG segments of RPS rows)
     int r = tid & 31, seg = tid >> 5;
     float acc = 0.f;
-    for (int i = 7; i >= 0; --i) {
-      int row = seg * 8 + i;
+#pragma unroll
+    for (int i = RPS - 1; i >= 0; --i) {
+      int row = seg * RPS + i;
       acc += sDth[row * RP + r];
       sDth[row * RP + r] = acc;
     }
@@ -1148,9 +1146,10 @@ __global__ void __launch_bounds__(256, 1)
   {
     int r = tid & 31, seg = tid >> 5;
     float base = 0.f;
-    for (int s = seg + 1; s < 8; ++s) base += sSeg[s * 32 + r];
-    for (int i = 0; i < 8; ++i) {
-      int row = seg * 8 + i;
+    for (int s = seg + 1; s < NSEG; ++s) base += sSeg[s * 32 + r];
+#pragma unroll
+    for (int i = 0; i < RPS; ++i) {
+      int row = seg * RPS + i;
       int tt = t0 + row;
       float G = base + sDth[row * RP + r];
       if (tt < g.L) out.dthl[(((size_t)b * g.L + tt) * g.nh + h) * R + r] = G;
@@ -1169,7 +1168,7 @@ __global__ void __launch_bounds__(256, 1)
       out.dadt[k] = sADT[tid];
     }
   }
-  for (int i = tid; i < N; i += 256) {
+  for (int i = tid; i < N; i += BWD_NT) {
     out.dCb[(bh * g.nc + c) * N + i] = sDcb[i];
     out.dBb[(bh * g.nc + c) * N + i] = sDbb[i];
   }
@@ -1177,17 +1176,19 @@ __global__ void __launch_bounds__(256, 1)
 
 // ---------------------------------------------------------------------------
 // prep backward: warps stride over tokens; head reductions, the dtheta carry,
-// BCNorm backward and the decay / trapezoid parameter chain.
+// BCNorm backward and the decay / trapezoid parameter chain.  The per-head angle
+// term sum_r G[h][r] * rate[r] is reduced through a per-warp shared tile.
 // ---------------------------------------------------------------------------
-__global__ void m3_prep_bwd(const bf16* __restrict__ proj, Geo g, const float* __restrict__ wB,
-                            const float* __restrict__ wC, const float* __restrict__ dt_bias,
-                            float A_floor, float eps, const bf16* __restrict__ gQ,
-                            const bf16* __restrict__ gK, const float* __restrict__ dthl,
-                            const float* __restrict__ dthc, const float* __restrict__ dgam,
-                            const float* __restrict__ dscl, const float* __restrict__ dadt,
-                            bf16* __restrict__ dproj, float* __restrict__ dwB,
-                            float* __restrict__ dwC, float* __restrict__ ddt_bias) {
-  const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(256)
+    m3_prep_bwd(const bf16* __restrict__ proj, Geo g, const float* __restrict__ wB,
+                const float* __restrict__ wC, const float* __restrict__ dt_bias, float A_floor, float eps,
+                const bf16* __restrict__ gQ, const bf16* __restrict__ gK, const float* __restrict__ dthl,
+                const float* __restrict__ dthc, const float* __restrict__ dgam,
+                const float* __restrict__ dscl, const float* __restrict__ dadt, bf16* __restrict__ dproj,
+                float* __restrict__ dwB, float* __restrict__ dwC, float* __restrict__ ddt_bias) {
+  __shared__ float tile[8][32][33];
+  __shared__ float dts[8][64];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nw = (gridDim.x * blockDim.x) >> 5;
   const int T = g.B * g.L;
@@ -1196,30 +1197,38 @@ __global__ void m3_prep_bwd(const bf16* __restrict__ proj, Geo g, const float* _
     const int b = tok / g.L, t = tok % g.L, c = t / CS;
     const bf16* row = proj + (size_t)tok * g.ldp;
     bf16* drow = dproj + (size_t)tok * g.ldp;
-    const float araw = __bfloat162float(row[g.off_ang + lane]);
-    const float th = tanhf(araw);
+    for (int h = lane; h < g.nh; h += 32)
+      dts[wib][h] = softplusf_(__bfloat162float(row[g.off_dt + h]) + dt_bias[h]);
+    const float th = tanhf(__bfloat162float(row[g.off_ang + lane]));
     const float rt = th * PI_F;                       // angle rate (lane = r)
     const float drt = PI_F * (1.f - th * th);         // d rate / d angle
-    float sb[4] = {0, 0, 0, 0}, sc[4] = {0, 0, 0, 0}, sa = 0.f;
-    float dang0 = 0.f, dang1 = 0.f;                   // lane h&31 keeps head h's angle term
+    __syncwarp();
+    float sb[4] = {0, 0, 0, 0}, sc[4] = {0, 0, 0, 0}, sa = 0.f, dang[2] = {0.f, 0.f};
+    for (int h0 = 0, j = 0; h0 < g.nh; h0 += 32, ++j) {
+      const int hn = min(32, g.nh - h0);
 #pragma unroll 4
-    for (int h = 0; h < g.nh; ++h) {
-      size_t base = ((size_t)tok * g.nh + h) * N + lane * 4;
-      uint2 kb = *reinterpret_cast<const uint2*>(gK + base);
-      uint2 qb = *reinterpret_cast<const uint2*>(gQ + base);
-      float2 k01 = unpack_bf16(kb.x), k23 = unpack_bf16(kb.y);
-      float2 q01 = unpack_bf16(qb.x), q23 = unpack_bf16(qb.y);
-      sb[0] += k01.x; sb[1] += k01.y; sb[2] += k23.x; sb[3] += k23.y;
-      sc[0] += q01.x; sc[1] += q01.y; sc[2] += q23.x; sc[3] += q23.y;
-      size_t bh = (size_t)b * g.nh + h;
-      float G = dthl[((size_t)tok * g.nh + h) * R + lane] + dthc[(bh * g.nc + c) * R + lane];
-      float DT = softplusf_(__bfloat162float(row[g.off_dt + h]) + dt_bias[h]);
-      sa += G * DT * drt;
-      float part = warp_sum(G * rt);
-      if (lane == (h & 31)) {
-        if (h < 32) dang0 = part;
-        else dang1 = part;
+      for (int hh = 0; hh < hn; ++hh) {
+        const int h = h0 + hh;
+        size_t base = ((size_t)tok * g.nh + h) * N + lane * 4;
+        uint2 kb = *reinterpret_cast<const uint2*>(gK + base);
+        uint2 qb = *reinterpret_cast<const uint2*>(gQ + base);
+        float2 k01 = unpack_bf16(kb.x), k23 = unpack_bf16(kb.y);
+        float2 q01 = unpack_bf16(qb.x), q23 = unpack_bf16(qb.y);
+        sb[0] += k01.x; sb[1] += k01.y; sb[2] += k23.x; sb[3] += k23.y;
+        sc[0] += q01.x; sc[1] += q01.y; sc[2] += q23.x; sc[3] += q23.y;
+        float G = dthl[((size_t)tok * g.nh + h) * R + lane] +
+                  dthc[(((size_t)b * g.nh + h) * g.nc + c) * R + lane];
+        sa += G * dts[wib][h] * drt;
+        tile[wib][hh][lane] = G * rt;
       }
+      __syncwarp();
+      float acc = 0.f;
+      if (lane < hn) {
+#pragma unroll 8
+        for (int r = 0; r < R; ++r) acc += tile[wib][lane][r];
+      }
+      dang[j] = acc;
+      __syncwarp();
     }
     float xb[4], xc[4], ssb = 0.f, ssc = 0.f;
 #pragma unroll
@@ -1255,14 +1264,13 @@ __global__ void m3_prep_bwd(const bf16* __restrict__ proj, Geo g, const float* _
       float dAr = __bfloat162float(row[g.off_A + h]);
       float tr = __bfloat162float(row[g.off_trap + h]);
       float xdt = ddtr + dt_bias[h];
-      float DT = softplusf_(xdt);
+      float DT = dts[wib][h];
       float spA = softplusf_(dAr);
       float A = fminf(-spA, -A_floor);
       float sg = sigmoidf_(tr);
       size_t k = ((size_t)b * g.nh + h) * g.L + t;
       float dsp = (t > 0) ? dscl[k - 1] : 0.f;
-      float dang = j ? dang1 : dang0;
-      float dDT = dang + dgam[k] * sg + dsp * (1.f - sg) + dadt[k] * A;
+      float dDT = dang[j] + dgam[k] * sg + dsp * (1.f - sg) + dadt[k] * A;
       float dsg = dgam[k] * DT - dsp * DT;
       float dA = dadt[k] * DT;
       float d_ddt = dDT * sigmoidf_(xdt);
@@ -1270,10 +1278,11 @@ __global__ void m3_prep_bwd(const bf16* __restrict__ proj, Geo g, const float* _
       drow[g.off_dt + h] = __float2bfloat16(d_ddt);
       drow[g.off_A + h] = __float2bfloat16(d_dA);
       drow[g.off_trap + h] = __float2bfloat16(dsg * sg * (1.f - sg));
-      if (j < 2) adt[j] += d_ddt;
+      adt[j] += d_ddt;
     }
     int used = g.off_ang + R;
     for (int cc = used + lane; cc < g.ldp; cc += 32) drow[cc] = __float2bfloat16(0.f);
+    __syncwarp();
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -1339,7 +1348,7 @@ void m3_states_launch(const M3Geo& G, const M3Scan& S, void* states, cudaStream_
   Geo g = make_geo(G);
   ScanIn in = make_in(S);
   set_smem(m3_chunk_state, STATE_SMEM);
-  m3_chunk_state<<<dim3(g.nh, g.nc, g.B), 128, STATE_SMEM, st>>>(in, g, reinterpret_cast<bf16*>(states));
+  m3_chunk_state<<<dim3(g.nh, g.nc, g.B), 256, STATE_SMEM, st>>>(in, g, reinterpret_cast<bf16*>(states));
   m3_pass<false><<<dim3(g.B * g.nh, P * N / 256), 256, 0, st>>>(reinterpret_cast<bf16*>(states), S.aend, g);
 }
 
@@ -1347,7 +1356,7 @@ void m3_scan_launch(const M3Geo& G, const M3Scan& S, const void* states, void* y
   Geo g = make_geo(G);
   ScanIn in = make_in(S);
   set_smem(m3_chunk_scan, SCAN_SMEM);
-  m3_chunk_scan<<<dim3(g.nh, g.nc, g.B), 128, SCAN_SMEM, st>>>(in, g, reinterpret_cast<const bf16*>(states),
+  m3_chunk_scan<<<dim3(g.nh, g.nc, g.B), 256, SCAN_SMEM, st>>>(in, g, reinterpret_cast<const bf16*>(states),
                                                                reinterpret_cast<bf16*>(y));
 }
 
@@ -1355,7 +1364,7 @@ void m3_dstates_launch(const M3Geo& G, const M3Scan& S, const void* dy, void* U,
   Geo g = make_geo(G);
   ScanIn in = make_in(S);
   set_smem(m3_chunk_dstate, DST_SMEM);
-  m3_chunk_dstate<<<dim3(g.nh, g.nc, g.B), 128, DST_SMEM, st>>>(in, g, reinterpret_cast<const bf16*>(dy),
+  m3_chunk_dstate<<<dim3(g.nh, g.nc, g.B), 256, DST_SMEM, st>>>(in, g, reinterpret_cast<const bf16*>(dy),
                                                                 reinterpret_cast<bf16*>(U));
   m3_pass<true><<<dim3(g.B * g.nh, P * N / 256), 256, 0, st>>>(reinterpret_cast<bf16*>(U), S.aend, g);
 }
@@ -1372,7 +1381,7 @@ void m3_chunk_bwd_launch(const M3Geo& G, const M3Scan& S, const void* dy, const 
   out.dgam = O.dgam; out.dscl = O.dscl; out.dadt = O.dadt;
   out.dD = O.dD; out.dCb = O.dCb; out.dBb = O.dBb;
   set_smem(m3_chunk_bwd, BWD_SMEM);
-  m3_chunk_bwd<<<dim3(g.nh, g.nc, g.B), 256, BWD_SMEM, st>>>(
+  m3_chunk_bwd<<<dim3(g.nh, g.nc, g.B), BWD_NT, BWD_SMEM, st>>>(
       in, g, reinterpret_cast<const bf16*>(dy), reinterpret_cast<const bf16*>(states),
       reinterpret_cast<const bf16*>(dsout), out);
   m3_rev_carry<<<g.B * g.nh, 32, 0, st>>>(O.dthtot, g);
