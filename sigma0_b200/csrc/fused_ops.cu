@@ -98,19 +98,21 @@ __global__ void ln_fwd_k(const float* __restrict__ x, const float* __restrict__ 
   }
 }
 
-// LayerNorm backward fused with the residual: dx = dres + LN'(dy); dw, db accumulated.
+// LayerNorm backward fused with the residual: dx = dres + LN'(dy); dw, db accumulated
+// in shared memory per block (one global atomic per column per block).
 template <int VPL>
-__global__ void ln_bwd_k(const bf16* __restrict__ dy, const float* __restrict__ x,
-                         const float* __restrict__ mean, const float* __restrict__ rstd,
-                         const float* __restrict__ w, const float* __restrict__ dres,
-                         float* __restrict__ dx, float* __restrict__ dw, float* __restrict__ db, int T,
-                         int D) {
+__global__ void __launch_bounds__(256)
+    ln_bwd_k(const bf16* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
+             const float* __restrict__ rstd, const float* __restrict__ w, const float* __restrict__ dres,
+             float* __restrict__ dx, float* __restrict__ dw, float* __restrict__ db, int T, int D) {
+  extern __shared__ float red_smem[];   // [2][D]
+  float* sw = red_smem;
+  float* sb = red_smem + D;
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) red_smem[i] = 0.f;
+  __syncthreads();
   int lane = threadIdx.x & 31;
   int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int nw = (gridDim.x * blockDim.x) >> 5;
-  float aw[VPL], ab[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) { aw[i] = 0.f; ab[i] = 0.f; }
   for (int row = gw; row < T; row += nw) {
     const float* xr = x + (size_t)row * D;
     const bf16* gr = dy + (size_t)row * D;
@@ -125,8 +127,10 @@ __global__ void ln_bwd_k(const bf16* __restrict__ dy, const float* __restrict__ 
       gw_[i] = c < D ? g * w[c] : 0.f;
       s1 += gw_[i];
       s2 += gw_[i] * xh[i];
-      aw[i] += g * xh[i];
-      ab[i] += g;
+      if (c < D) {
+        atomicAdd(&sw[c], g * xh[i]);
+        atomicAdd(&sb[c], g);
+      }
     }
     s1 = warp_sum(s1) / D;
     s2 = warp_sum(s2) / D;
@@ -138,9 +142,11 @@ __global__ void ln_bwd_k(const bf16* __restrict__ dy, const float* __restrict__ 
       if (c < D) dxr[c] = (rr ? rr[c] : 0.f) + r * (gw_[i] - s1 - xh[i] * s2);
     }
   }
-  extern __shared__ float red_smem[];
-  block_col_atomic<VPL>(aw, red_smem, dw, D);
-  block_col_atomic<VPL>(ab, red_smem, db, D);
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    atomicAdd(&dw[c], sw[c]);
+    atomicAdd(&db[c], sb[c]);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -289,18 +295,18 @@ __global__ void glu_res_fwd_k(const float* __restrict__ x, const bf16* __restric
   }
 }
 
-// dh = dout * g * s(1-s) (bf16), dgp = dout * s (fp32), db accumulated; rows of D columns.
+// dh = dout * g * s(1-s) (bf16), dgp = dout * s (fp32), db accumulated in shared memory.
 template <int VPL>
-__global__ void glu_res_bwd_k(const float* __restrict__ dout, const bf16* __restrict__ g,
-                              const bf16* __restrict__ h, const float* __restrict__ b,
-                              bf16* __restrict__ dh, float* __restrict__ dgp, float* __restrict__ db,
-                              int T, int D) {
+__global__ void __launch_bounds__(256)
+    glu_res_bwd_k(const float* __restrict__ dout, const bf16* __restrict__ g, const bf16* __restrict__ h,
+                  const float* __restrict__ b, bf16* __restrict__ dh, float* __restrict__ dgp,
+                  float* __restrict__ db, int T, int D) {
+  extern __shared__ float red_smem[];   // [D]
+  for (int i = threadIdx.x; i < D; i += blockDim.x) red_smem[i] = 0.f;
+  __syncthreads();
   int lane = threadIdx.x & 31;
   int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int nw = (gridDim.x * blockDim.x) >> 5;
-  float ab[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) ab[i] = 0.f;
   for (int row = gw; row < T; row += nw) {
     size_t o = (size_t)row * D;
 #pragma unroll
@@ -313,12 +319,12 @@ __global__ void glu_res_bwd_k(const float* __restrict__ dout, const bf16* __rest
         float v = d * gg * s * (1.f - s);
         dh[o + c] = __float2bfloat16(v);
         dgp[o + c] = d * s;
-        ab[i] += v;
+        atomicAdd(&red_smem[c], v);
       }
     }
   }
-  extern __shared__ float red_smem[];
-  block_col_atomic<VPL>(ab, red_smem, db, D);
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&db[c], red_smem[c]);
 }
 
 // do = (dgp + dgm) * gelu'(o)  -> bf16
@@ -465,7 +471,7 @@ static void allow_smem(K kernel, size_t bytes) {
 // grid for kernels that reduce columns: few blocks (2 per SM), each looping over rows
 static int red_grid(long T, int sms) {
   long blocks = (T * 32 + 255) / 256;
-  long cap = (long)sms * 2;
+  long cap = (long)sms * 6;
   return (int)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
 }
 static int ew_grid(long n, int sms) {
@@ -487,12 +493,11 @@ void ln_bwd_launch(const void* dy, const float* x, const float* mean, const floa
                    const float* dres, float* dx, float* dw, float* db, long T, int D, int sms, cudaStream_t st) {
   int gr = red_grid(T, sms);
   const bf16* g = reinterpret_cast<const bf16*>(dy);
-  if (D <= 256) ln_bwd_k<8><<<gr, 256, 8 * 8 * 32 * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
-  else if (D <= 512) ln_bwd_k<16><<<gr, 256, 8 * 16 * 32 * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
-  else if (D <= 1024) ln_bwd_k<32><<<gr, 256, 8 * 32 * 32 * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  if (D <= 256) ln_bwd_k<8><<<gr, 256, 2 * D * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  else if (D <= 512) ln_bwd_k<16><<<gr, 256, 2 * D * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+  else if (D <= 1024) ln_bwd_k<32><<<gr, 256, 2 * D * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
   else {
-    allow_smem(ln_bwd_k<64>, 8 * 64 * 32 * 4);
-    ln_bwd_k<64><<<gr, 256, 8 * 64 * 32 * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
+    ln_bwd_k<64><<<gr, 256, 2 * D * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
   }
 }
 void rms_fwd_launch(const void* x, const float* w, void* y, float* rstd, long T, int D, float eps, int sms,
@@ -530,12 +535,11 @@ void glu_res_bwd_launch(const float* dout, const void* g, const void* h, const f
   const bf16* gp = reinterpret_cast<const bf16*>(g);
   const bf16* hp = reinterpret_cast<const bf16*>(h);
   bf16* dhp = reinterpret_cast<bf16*>(dh);
-  if (D <= 256) glu_res_bwd_k<8><<<gr, 256, 8 * 8 * 32 * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
-  else if (D <= 512) glu_res_bwd_k<16><<<gr, 256, 8 * 16 * 32 * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
-  else if (D <= 1024) glu_res_bwd_k<32><<<gr, 256, 8 * 32 * 32 * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  if (D <= 256) glu_res_bwd_k<8><<<gr, 256, D * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  else if (D <= 512) glu_res_bwd_k<16><<<gr, 256, D * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+  else if (D <= 1024) glu_res_bwd_k<32><<<gr, 256, D * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
   else {
-    allow_smem(glu_res_bwd_k<64>, 8 * 64 * 32 * 4);
-    glu_res_bwd_k<64><<<gr, 256, 8 * 64 * 32 * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
+    glu_res_bwd_k<64><<<gr, 256, D * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
   }
 }
 void gelu_bwd_launch(const void* o, const float* dgp, const void* dgm, void* dout, long n, int sms,

@@ -100,26 +100,42 @@ __global__ void m3_prep_fwd(const bf16* __restrict__ proj, Geo g, const float* _
 }
 
 // ---------------------------------------------------------------------------
-// chunk totals (one warp per (h, c, b)): aend = sum ADT, angtot[r] = sum rate*DT
+// chunk totals, one block per (chunk, batch) over all heads:
+//   aend[h] = sum_t ADT[h][t],  angtot[h][r] = sum_t rate[t][r] * DT[h][t]
 // ---------------------------------------------------------------------------
-__global__ void m3_chunk_totals(ScanIn in, Geo g, float* __restrict__ aend, float* __restrict__ angtot) {
-  const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z, lane = threadIdx.x;
-  const size_t bh = (size_t)b * g.nh + h;
+__global__ void __launch_bounds__(256) m3_chunk_totals(ScanIn in, Geo g, float* __restrict__ aend,
+                                                       float* __restrict__ angtot) {
+  __shared__ float srate[CS][R + 1];
+  __shared__ float sdt[64][CS + 1];
+  const int c = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
   const int t0 = c * CS;
-  float a = 0.f, ang = 0.f;
-  for (int i = 0; i < CS; ++i) {
-    int tt = t0 + i;
-    if (tt >= g.L) break;
-    float dtv = in.dt[bh * g.L + tt];
-    ang += in.rate[((size_t)b * g.L + tt) * R + lane] * dtv;
+  for (int i = tid; i < CS * R; i += 256) {
+    int r = i / R, k = i % R;
+    int tt = t0 + r;
+    srate[r][k] = tt < g.L ? in.rate[((size_t)b * g.L + tt) * R + k] : 0.f;
   }
-  for (int i = lane; i < CS; i += 32) {
-    int tt = t0 + i;
-    if (tt < g.L) a += in.adt[bh * g.L + tt];
+  for (int i = tid; i < g.nh * CS; i += 256) {
+    int h = i / CS, r = i % CS;
+    int tt = t0 + r;
+    sdt[h][r] = tt < g.L ? in.dt[((size_t)b * g.nh + h) * g.L + tt] : 0.f;
   }
-  a = warp_sum(a);
-  angtot[(bh * g.nc + c) * R + lane] = ang;
-  if (lane == 0) aend[bh * g.nc + c] = a;
+  __syncthreads();
+  for (int o = tid; o < g.nh * R; o += 256) {
+    int h = o / R, k = o % R;
+    float acc = 0.f;
+#pragma unroll 8
+    for (int r = 0; r < CS; ++r) acc += srate[r][k] * sdt[h][r];
+    angtot[((((size_t)b * g.nh + h) * g.nc) + c) * R + k] = acc;
+  }
+  for (int h = tid; h < g.nh; h += 256) {
+    float a = 0.f;
+    size_t base = ((size_t)b * g.nh + h) * g.L;
+    for (int r = 0; r < CS; ++r) {
+      int tt = t0 + r;
+      if (tt < g.L) a += in.adt[base + tt];
+    }
+    aend[((size_t)b * g.nh + h) * g.nc + c] = a;
+  }
 }
 
 // exclusive scan over chunks (forward, mod 2pi): theta0[c] = sum_{c'<c} angtot[c']
@@ -127,11 +143,18 @@ __global__ void m3_theta_scan(const float* __restrict__ angtot, float* __restric
   const size_t bh = blockIdx.x;
   const int lane = threadIdx.x;
   float run = 0.f;
-  for (int c = 0; c < g.nc; ++c) {
-    size_t k = (bh * g.nc + c) * R + lane;
-    float v = angtot[k];
-    theta0[k] = run;
-    run = wrap2pi(run + v);
+  constexpr int U = 8;
+  for (int c0 = 0; c0 < g.nc; c0 += U) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) v[u] = (c0 + u < g.nc) ? angtot[(bh * g.nc + c0 + u) * R + lane] : 0.f;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (c0 + u < g.nc) {
+        theta0[(bh * g.nc + c0 + u) * R + lane] = run;
+        run = wrap2pi(run + v[u]);
+      }
+    }
   }
 }
 
@@ -140,11 +163,22 @@ __global__ void m3_rev_carry(float* __restrict__ x, Geo g) {
   const size_t bh = blockIdx.x;
   const int lane = threadIdx.x;
   float run = 0.f;
-  for (int c = g.nc - 1; c >= 0; --c) {
-    size_t k = (bh * g.nc + c) * R + lane;
-    float v = x[k];
-    x[k] = run;
-    run += v;
+  constexpr int U = 8;
+  for (int k0 = 0; k0 < g.nc; k0 += U) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      int c = g.nc - 1 - (k0 + u);
+      v[u] = (c >= 0) ? x[(bh * g.nc + c) * R + lane] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      int c = g.nc - 1 - (k0 + u);
+      if (c >= 0) {
+        x[(bh * g.nc + c) * R + lane] = run;
+        run += v[u];
+      }
+    }
   }
 }
 
@@ -302,22 +336,25 @@ __device__ __forceinline__ size_t state_off(const Geo& g, int b, int h, int c) {
 //   backward (REV=true):  buf[c] <- dS_out[c]; run = exp(aend[c]) * run + U[c]
 // ---------------------------------------------------------------------------
 template <bool REV>
-__global__ void __launch_bounds__(256) m3_pass(bf16* __restrict__ buf, const float* __restrict__ aend, Geo g) {
+__global__ void __launch_bounds__(128) m3_pass(bf16* __restrict__ buf, const float* __restrict__ aend, Geo g) {
   const size_t bh = blockIdx.x;
-  const int e = blockIdx.y * 256 + threadIdx.x;
-  const size_t stride = (size_t)P * N;
-  bf16* base = buf + bh * g.nc * stride + e;
+  const int e8 = blockIdx.y * 128 + threadIdx.x;        // 8 consecutive elements per thread
+  const size_t stride = (size_t)P * N / 8;              // in uint4 units
+  uint4* base = reinterpret_cast<uint4*>(buf) + bh * g.nc * stride + e8;
   const float* ae = aend + bh * g.nc;
-  float run = 0.f;
-  constexpr int U = 8;
+  float run[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) run[k] = 0.f;
+  constexpr int U = 4;
   for (int k0 = 0; k0 < g.nc; k0 += U) {
-    float v[U], d[U];
+    uint4 v[U];
+    float d[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       int k = k0 + u;
       int c = REV ? g.nc - 1 - k : k;
       bool ok = k < g.nc;
-      v[u] = ok ? __bfloat162float(base[(size_t)c * stride]) : 0.f;
+      v[u] = ok ? base[(size_t)c * stride] : make_uint4(0, 0, 0, 0);
       d[u] = ok ? __expf(ae[c]) : 1.f;
     }
 #pragma unroll
@@ -325,8 +362,15 @@ __global__ void __launch_bounds__(256) m3_pass(bf16* __restrict__ buf, const flo
       int k = k0 + u;
       if (k < g.nc) {
         int c = REV ? g.nc - 1 - k : k;
-        base[(size_t)c * stride] = __float2bfloat16(run);
-        run = d[u] * run + v[u];
+        uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w}, o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float2 f = unpack_bf16(w[q]);
+          o[q] = pack_bf16(run[2 * q], run[2 * q + 1]);
+          run[2 * q] = d[u] * run[2 * q] + f.x;
+          run[2 * q + 1] = d[u] * run[2 * q + 1] + f.y;
+        }
+        base[(size_t)c * stride] = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
   }
@@ -1340,7 +1384,7 @@ void m3_chunk_totals_launch(const M3Geo& G, const M3Scan& S, float* aend, float*
                             cudaStream_t st) {
   Geo g = make_geo(G);
   ScanIn in = make_in(S);
-  m3_chunk_totals<<<dim3(g.nh, g.nc, g.B), 32, 0, st>>>(in, g, aend, angtot);
+  m3_chunk_totals<<<dim3(g.nc, g.B), 256, 0, st>>>(in, g, aend, angtot);
   m3_theta_scan<<<g.B * g.nh, 32, 0, st>>>(angtot, theta0, g);
 }
 
@@ -1349,7 +1393,7 @@ void m3_states_launch(const M3Geo& G, const M3Scan& S, void* states, cudaStream_
   ScanIn in = make_in(S);
   set_smem(m3_chunk_state, STATE_SMEM);
   m3_chunk_state<<<dim3(g.nh, g.nc, g.B), 256, STATE_SMEM, st>>>(in, g, reinterpret_cast<bf16*>(states));
-  m3_pass<false><<<dim3(g.B * g.nh, P * N / 256), 256, 0, st>>>(reinterpret_cast<bf16*>(states), S.aend, g);
+  m3_pass<false><<<dim3(g.B * g.nh, P * N / 8 / 128), 128, 0, st>>>(reinterpret_cast<bf16*>(states), S.aend, g);
 }
 
 void m3_scan_launch(const M3Geo& G, const M3Scan& S, const void* states, void* y, cudaStream_t st) {
@@ -1366,7 +1410,7 @@ void m3_dstates_launch(const M3Geo& G, const M3Scan& S, const void* dy, void* U,
   set_smem(m3_chunk_dstate, DST_SMEM);
   m3_chunk_dstate<<<dim3(g.nh, g.nc, g.B), 256, DST_SMEM, st>>>(in, g, reinterpret_cast<const bf16*>(dy),
                                                                 reinterpret_cast<bf16*>(U));
-  m3_pass<true><<<dim3(g.B * g.nh, P * N / 256), 256, 0, st>>>(reinterpret_cast<bf16*>(U), S.aend, g);
+  m3_pass<true><<<dim3(g.B * g.nh, P * N / 8 / 128), 128, 0, st>>>(reinterpret_cast<bf16*>(U), S.aend, g);
 }
 
 void m3_chunk_bwd_launch(const M3Geo& G, const M3Scan& S, const void* dy, const void* states, const void* dsout,
