@@ -1,0 +1,192 @@
+"""Gated DeltaNet (GDN) and Kimi Delta Attention (KDA) mixers.
+
+Parameters and computation follow the reference ``GDNSSM``
+(``src/base_model/models/gdn.py:40-630``): q/k/v projections, optional causal
+depthwise Conv1d(k=4) with SiLU, L2-normalised q and k (epsilon under the
+square root), ``q *= head_dim**-0.5``, write gate ``beta = sigmoid(b_proj)``,
+decay ``log alpha = log_sigmoid(gk_proj)`` (per head for GDN, per key dim for
+KDA), output gate ``silu(g_proj)``, per-head RMSNorm, ``o_proj`` and the
+``D * x`` feed-through.
+
+The recurrence per head (state S: (hvd, hd)):
+``S <- S * alpha;  S <- S + beta (v - S k) k^T;  o = S q``.
+Training uses the exact chunkwise form: within a chunk the delta-rule
+interactions are resolved with a unit-lower-triangular solve (the WY form of
+Yang et al., "Gated Delta Networks"), across chunks the state is carried.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .common import Dense, RMSNorm, lecun_normal_
+
+
+def l2_normalize(x, eps=1e-6):
+    xf = x.float()
+    return (xf * torch.rsqrt((xf * xf).sum(-1, keepdim=True) + eps)).to(x.dtype)
+
+
+class CausalDepthwiseConv1d(nn.Module):
+    def __init__(self, channels, kernel_size=4):
+        super().__init__()
+        self.k = kernel_size
+        self.kernel = nn.Parameter(lecun_normal_(torch.empty(kernel_size, channels), kernel_size))
+        self.bias = nn.Parameter(torch.zeros(channels))
+
+    def _conv(self, xc):
+        # xc (B, k-1+L, C) -> (B, L, C)
+        L = xc.shape[1] - (self.k - 1)
+        out = self.bias.to(xc.dtype).expand(xc.shape[0], L, -1).clone()
+        for j in range(self.k):
+            out = out + xc[:, j:j + L] * self.kernel[j].to(xc.dtype)
+        return out
+
+    def forward(self, x):
+        return self._conv(F.pad(x, (0, 0, self.k - 1, 0)))
+
+    def step(self, buf, x):
+        xc = torch.cat([buf, x], dim=1)
+        return xc[:, -(self.k - 1):], self._conv(xc)
+
+
+def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None):
+    """q,k (B,L,nh,hd); v (B,L,nh,hvd); beta (B,L,nh); alog (B,L,nh,hd or 1).
+
+    Returns o (B,L,nh,hvd) and the final state (B,nh,hvd,hd).
+    """
+    B, L, nh, hd = q.shape
+    hvd = v.shape[-1]
+    pad = (chunk - L % chunk) % chunk
+    if pad:
+        q, k, v = (F.pad(t, (0, 0, 0, 0, 0, pad)) for t in (q, k, v))
+        beta = F.pad(beta, (0, 0, 0, pad))
+        alog = F.pad(alog, (0, 0, 0, 0, 0, pad))
+    nc = (L + pad) // chunk
+    C = chunk
+    f = lambda t: t.float().reshape(B, nc, C, *t.shape[2:]).transpose(2, 3)   # (B,nc,nh,C,...)
+    q, k, v, alog = f(q), f(k), f(v), f(alog)
+    beta = beta.float().reshape(B, nc, C, nh).transpose(2, 3)                   # (B,nc,nh,C)
+    G = alog.cumsum(3)                                                          # (B,nc,nh,C,d|1)
+    tri = torch.tril(torch.ones(C, C, dtype=torch.bool, device=q.device))
+    stri = torch.tril(torch.ones(C, C, dtype=torch.bool, device=q.device), -1)
+    kb = k * beta[..., None]
+    vb = v * beta[..., None]
+    if G.shape[-1] == 1:
+        dG = (G[..., :, None, 0] - G[..., None, :, 0]).masked_fill(~tri, 0.0)
+        W = torch.exp(dG) * tri
+        intra = (q @ k.transpose(-1, -2)) * W
+        Lm = -(kb @ k.transpose(-1, -2)) * W * stri
+    else:
+        dG = (G[..., :, None, :] - G[..., None, :, :]).masked_fill(~tri[..., None], 0.0)
+        W = torch.exp(dG) * tri[..., None]
+        intra = torch.einsum("...id,...jd,...ijd->...ij", q, k, W)
+        Lm = -torch.einsum("...id,...jd,...ijd->...ij", kb, k, W) * stri
+    I = torch.eye(C, device=q.device)
+    A = I - Lm
+    vc = torch.linalg.solve_triangular(A, vb, upper=False)                     # (B,nc,nh,C,hvd)
+    kcd = torch.linalg.solve_triangular(A, kb * torch.exp(G), upper=False)    # (B,nc,nh,C,hd)
+    dec_end = torch.exp(G[..., -1:, :] - G)                                     # (B,nc,nh,C,d|1)
+    kdec = k * dec_end
+    S = torch.zeros(B, nh, hvd, hd, device=q.device) if S0 is None else S0.float()
+    outs = []
+    for c in range(nc):
+        qc = q[:, c] * torch.exp(G[:, c])
+        vnew = vc[:, c] - kcd[:, c] @ S.transpose(-1, -2)                       # (B,nh,C,hvd)
+        o = qc @ S.transpose(-1, -2) + intra[:, c] @ vnew
+        outs.append(o)
+        tot = torch.exp(G[:, c, :, -1, :])                                      # (B,nh,d|1)
+        S = S * tot[:, :, None, :] + vnew.transpose(-1, -2) @ kdec[:, c]
+    o = torch.stack(outs, 1).transpose(2, 3).reshape(B, nc * C, nh, hvd)[:, :L]
+    return o, S
+
+
+def gated_delta_recurrent(q, k, v, beta, alog, S=None):
+    B, L, nh, hd = q.shape
+    hvd = v.shape[-1]
+    S = torch.zeros(B, nh, hvd, hd, device=q.device) if S is None else S.float()
+    outs = []
+    for t in range(L):
+        a = torch.exp(alog[:, t].float())                                       # (B,nh,d|1)
+        S = S * a[:, :, None, :]
+        kt = k[:, t].float()
+        Sk = torch.einsum("bnvk,bnk->bnv", S, kt)
+        delta = v[:, t].float() - Sk
+        S = S + torch.einsum("bnv,bnk->bnvk", beta[:, t].float()[..., None] * delta, kt)
+        outs.append(torch.einsum("bnvk,bnk->bnv", S, q[:, t].float()))
+    return torch.stack(outs, 1), S
+
+
+class GDN(nn.Module):
+    is_transformer = False
+
+    def __init__(self, H, num_heads, head_dim=128, expand_v=2, chunk_size=64, use_conv=True, use_kda=False,
+                 impl="torch"):
+        super().__init__()
+        self.H = H
+        self.nh = min(num_heads, max(1, H // head_dim))
+        self.hd = min(head_dim, H)
+        self.hvd = self.hd * expand_v
+        self.chunk = chunk_size
+        self.use_conv, self.use_kda, self.impl = use_conv, use_kda, impl
+        nh, hd, hvd = self.nh, self.hd, self.hvd
+        self.q_proj = Dense(H, nh * hd, bias=False)
+        self.k_proj = Dense(H, nh * hd, bias=False)
+        self.v_proj = Dense(H, nh * hvd, bias=False)
+        self.b_proj = Dense(H, nh, bias=True)
+        self.gk_proj = Dense(H, nh * hd if use_kda else nh, bias=True)
+        self.g_proj = Dense(H, nh * hvd, bias=False)
+        self.o_proj = Dense(nh * hvd, H, bias=False)
+        if use_conv:
+            self.q_conv = CausalDepthwiseConv1d(nh * hd)
+            self.k_conv = CausalDepthwiseConv1d(nh * hd)
+            self.v_conv = CausalDepthwiseConv1d(nh * hvd)
+        self.out_norm = RMSNorm(hvd)
+        self.D = nn.Parameter(torch.randn(H))
+
+    def _inputs(self, x, bufs=None):
+        B, L, _ = x.shape
+        nh, hd, hvd = self.nh, self.hd, self.hvd
+        q, k, v = self.q_proj(x), self.k_proj(x), self.v_proj(x)
+        new_bufs = None
+        if self.use_conv:
+            if bufs is None:
+                q, k, v = F.silu(self.q_conv(q)), F.silu(self.k_conv(k)), F.silu(self.v_conv(v))
+            else:
+                qb, q = self.q_conv.step(bufs[0], q)
+                kb, k = self.k_conv.step(bufs[1], k)
+                vb, v = self.v_conv.step(bufs[2], v)
+                q, k, v = F.silu(q), F.silu(k), F.silu(v)
+                new_bufs = (qb, kb, vb)
+        q = l2_normalize(q.reshape(B, L, nh, hd)) * hd ** -0.5
+        k = l2_normalize(k.reshape(B, L, nh, hd))
+        v = v.reshape(B, L, nh, hvd)
+        beta = torch.sigmoid(self.b_proj(x))
+        alog = F.logsigmoid(self.gk_proj(x)).reshape(B, L, nh, hd if self.use_kda else 1)
+        g = F.silu(self.g_proj(x)).reshape(B, L, nh, hvd)
+        return q, k, v, beta, alog, g, new_bufs
+
+    def _out(self, x, o, g):
+        B, L = o.shape[:2]
+        o = self.out_norm(o) * g
+        return self.o_proj(o.reshape(B, L, self.nh * self.hvd)) + x * self.D
+
+    def forward(self, x):
+        q, k, v, beta, alog, g, _ = self._inputs(x)
+        o, _ = gated_delta_chunked(q, k, v, beta, alog, self.chunk)
+        return self._out(x, o, g)
+
+    def initial_state(self, batch, device=None):
+        S = torch.zeros(batch, self.nh, self.hvd, self.hd, device=device)
+        if not self.use_conv:
+            return S
+        z = lambda c: torch.zeros(batch, 3, c, device=device)
+        return (S, (z(self.nh * self.hd), z(self.nh * self.hd), z(self.nh * self.hvd)))
+
+    def step(self, state, x):
+        S, bufs = (state if self.use_conv else (state, None))
+        q, k, v, beta, alog, g, nb = self._inputs(x, bufs)
+        o, S = gated_delta_recurrent(q, k, v, beta, alog, S)
+        out = self._out(x, o, g)
+        return ((S, nb) if self.use_conv else S), out
