@@ -83,18 +83,25 @@ M3Pre m3_prepare(const at::Tensor& proj, int64_t B, int64_t L, int64_t nh, const
 // y = ssd(proj); returns (y, states) -- states is the S_in of every chunk (bf16)
 std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh, at::Tensor wB, at::Tensor wC,
                                at::Tensor dt_bias, at::Tensor Bb, at::Tensor Cb, at::Tensor D, double A_floor,
-                               double eps) {
+                               double eps, bool want_final = false) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
   M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
   int nc = m3_nchunks((int)L);
   auto states = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
   M3Scan s = m3_scan(proj, pre, Bb, Cb, D);
-  m3_states_launch(g, s, states.data_ptr(), stream());
+  at::Tensor fin, thf;
+  if (want_final) fin = at::empty({B, nh, M3_P, M3_N}, proj.options().dtype(at::kFloat));
+  m3_states_launch(g, s, states.data_ptr(), stream(), want_final ? fin.data_ptr<float>() : nullptr);
   auto y = at::empty({B, L, nh * M3_P}, proj.options());
   m3_scan_launch(g, s, states.data_ptr(), y.data_ptr(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {y, states};
+  if (want_final) {
+    // angle after the last token: theta0 of the last chunk + that chunk's total, mod 2pi
+    auto last = pre.theta0.select(2, nc - 1) + pre.angtot.select(2, nc - 1);
+    thf = last - 2 * M_PI * at::floor(last / (2 * M_PI));
+  }
+  return {y, states, fin, thf};
 }
 
 std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias,
@@ -290,11 +297,124 @@ void adam(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ---- decode / engine ----------------------------------------------------------------------
+void m3_decode_step(at::Tensor proj, int64_t nh, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias, at::Tensor Bb,
+                    at::Tensor Cb, at::Tensor D, double A_floor, double eps, at::Tensor ang, at::Tensor ssm,
+                    at::Tensor kprev, at::Tensor vprev, at::Tensor y) {
+  req(proj, at::kBFloat16, "proj");
+  req(ssm, at::kFloat, "ssm");
+  req(y, at::kBFloat16, "y");
+  c10::cuda::CUDAGuard guard(proj.device());
+  int64_t B = proj.size(0);
+  TORCH_CHECK(ssm.numel() == B * nh * M3_P * M3_N, "state shape");
+  m3_decode_step_launch(proj.data_ptr(), (int)B, (int)proj.size(1), (int)nh, wB.data_ptr<float>(),
+                        wC.data_ptr<float>(), dt_bias.data_ptr<float>(), Bb.data_ptr<float>(), Cb.data_ptr<float>(),
+                        D.data_ptr<float>(), (float)A_floor, (float)eps, ang.data_ptr<float>(), ssm.data_ptr<float>(),
+                        kprev.data_ptr<float>(), vprev.data_ptr<float>(), y.data_ptr(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void eng_process(at::Tensor asks, at::Tensor bids, at::Tensor trades, at::Tensor msgs, int64_t init_id,
+                 int64_t book_depth, int64_t cancel_mode, int64_t type4, bool check_fill) {
+  req(asks, at::kInt, "asks");
+  req(bids, at::kInt, "bids");
+  req(trades, at::kInt, "trades");
+  req(msgs, at::kInt, "msgs");
+  TORCH_CHECK(asks.size(1) <= 128 && trades.size(1) <= 128, "at most 128 rows per side / trades");
+  TORCH_CHECK(cancel_mode <= 1, "cancel modes 2/3 (random fallback) run on the CPU engine");
+  c10::cuda::CUDAGuard guard(asks.device());
+  int64_t nb = asks.size(0);
+  eng_process_launch(asks.data_ptr<int>(), bids.data_ptr<int>(), trades.data_ptr<int>(), msgs.data_ptr<int>(),
+                     (int)msgs.size(1), (int)nb, (int)asks.size(1), (int)trades.size(1), (int)init_id,
+                     (int)book_depth, (int)cancel_mode, (int)type4, check_fill ? 1 : 0, stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+at::Tensor eng_l2(at::Tensor asks, at::Tensor bids, int64_t levels) {
+  req(asks, at::kInt, "asks");
+  c10::cuda::CUDAGuard guard(asks.device());
+  auto out = at::empty({asks.size(0), 4 * levels}, asks.options());
+  eng_l2_launch(asks.data_ptr<int>(), bids.data_ptr<int>(), out.data_ptr<int>(), (int)levels, (int)asks.size(0),
+                (int)asks.size(1), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+void gen_apply(at::Tensor asks, at::Tensor bids, at::Tensor trades, at::Tensor toks, std::vector<int64_t> lay,
+               int64_t init_id, int64_t book_depth, int64_t cancel_mode, int64_t type4, bool check_fill,
+               at::Tensor new_oid, at::Tensor p_mid, at::Tensor time_in, at::Tensor raw_out, at::Tensor msg_out,
+               at::Tensor prov_out, at::Tensor l2_out, at::Tensor img_out, bool apply) {
+  req(asks, at::kInt, "asks");
+  req(bids, at::kInt, "bids");
+  req(trades, at::kInt, "trades");
+  req(toks, at::kLong, "toks");
+  req(p_mid, at::kInt, "p_mid");
+  req(time_in, at::kInt, "time_in");
+  req(raw_out, at::kInt, "raw_out");
+  req(msg_out, at::kInt, "msg_out");
+  req(prov_out, at::kInt, "prov_out");
+  req(l2_out, at::kInt, "l2_out");
+  req(new_oid, at::kInt, "new_oid");
+  TORCH_CHECK(img_out.is_cuda() && img_out.scalar_type() == at::kFloat && img_out.stride(1) == 1, "img_out");
+  TORCH_CHECK(lay.size() == 22, "layout has 22 entries");
+  TORCH_CHECK(asks.size(1) <= 128 && trades.size(1) <= 128, "at most 128 rows per side / trades");
+  TORCH_CHECK(cancel_mode <= 1, "cancel modes 2/3 run on the CPU engine");
+  GenLayout L;
+  int* f = &L.msg_len;
+  for (int i = 0; i < 22; ++i) f[i] = (int)lay[i];
+  TORCH_CHECK(L.msg_len <= 32 && L.l2_levels <= 64 && L.price_digits <= 4, "layout out of range");
+  TORCH_CHECK(toks.size(1) == L.msg_len, "toks width");
+  TORCH_CHECK(img_out.size(1) >= 3 + L.img_levels, "img_out width");
+  TORCH_CHECK(l2_out.size(1) == 4 * L.l2_levels, "l2_out width");
+  c10::cuda::CUDAGuard guard(asks.device());
+  gen_apply_launch(asks.data_ptr<int>(), bids.data_ptr<int>(), trades.data_ptr<int>(), toks.data_ptr<int64_t>(), L,
+                   (int)asks.size(1), (int)trades.size(1), (int)init_id, (int)book_depth, (int)cancel_mode,
+                   (int)type4, check_fill ? 1 : 0, new_oid.data_ptr<int>(), p_mid.data_ptr<int>(),
+                   time_in.data_ptr<int>(), raw_out.data_ptr<int>(), msg_out.data_ptr<int>(),
+                   prov_out.data_ptr<int>(), l2_out.data_ptr<int>(), img_out.data_ptr<float>(),
+                   (int)img_out.stride(0), (int)asks.size(0), apply ? 1 : 0, stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gen_sample(at::Tensor logits, c10::optional<at::Tensor> bias, at::Tensor allow, int64_t seed, at::Tensor ctr,
+                int64_t salt, int64_t top_n, at::Tensor out, int64_t out_offset, int64_t out_stride) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "logits");
+  req(allow, at::kByte, "allow");
+  req(ctr, at::kLong, "ctr");
+  req(out, at::kLong, "out");
+  TORCH_CHECK(top_n == 1 || top_n == -1, "device sampler supports top_n 1 (argmax) and -1 (full)");
+  int64_t V = logits.size(1);
+  TORCH_CHECK(allow.numel() == V, "mask width");
+  TORCH_CHECK(out_offset + (logits.size(0) - 1) * out_stride < out.numel(), "out too small");
+  const float* bp = nullptr;
+  if (bias.has_value()) {
+    req(*bias, at::kFloat, "bias");
+    TORCH_CHECK(bias->numel() == V, "bias width");
+    bp = bias->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard guard(logits.device());
+  gen_sample_launch(logits.data_ptr<float>(), (int)logits.stride(0), bp, allow.data_ptr<unsigned char>(), (int)V,
+                    (int)logits.size(0), (unsigned long long)seed, reinterpret_cast<const long long*>(ctr.data_ptr<int64_t>()), (int)salt, (int)top_n,
+                    out.data_ptr<int64_t>() + out_offset, (int)out_stride, stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gen_time_tokens(at::Tensor msg, int64_t dt_pos, int64_t time_off, at::Tensor time) {
+  req(msg, at::kLong, "msg");
+  req(time, at::kInt, "time");
+  c10::cuda::CUDAGuard guard(msg.device());
+  gen_time_tokens_launch(msg.data_ptr<int64_t>(), (int)msg.size(1), (int)dt_pos, (int)time_off,
+                         time.data_ptr<int>(), (int)msg.size(0), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sigma0_b200 sm_100a kernels";
-  m.def("m3_fwd", &m3_fwd, "Mamba3 SSD forward (prep, chunk states, passing, chunk scan) -> (y, states)");
+  m.def("m3_fwd", &m3_fwd, py::arg("proj"), py::arg("B"), py::arg("L"), py::arg("nh"), py::arg("wB"), py::arg("wC"),
+        py::arg("dt_bias"), py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("A_floor"), py::arg("eps"),
+        py::arg("want_final") = false, "Mamba3 SSD forward (prep, chunk states, passing, chunk scan) -> (y, states)");
   m.def("m3_bwd", &m3_bwd, "Mamba3 SSD backward -> (dproj, dB_norm, dC_norm, ddt_bias, dD, dC_bias, dB_bias)");
   m.def("ln_fwd", &ln_fwd);
   m.def("ln_bwd", &ln_bwd);
@@ -307,4 +427,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("sumsq", &sumsq);
   m.def("adam", &adam);
+  m.def("m3_decode_step", &m3_decode_step, "Mamba3 one-token recurrent step (states updated in place)");
+  m.def("eng_process", &eng_process, "batched matching engine: apply [B, M, 8] messages, one warp per book");
+  m.def("eng_l2", &eng_l2, "batched L2 extraction");
+  m.def("gen_apply", &gen_apply, "generation: decode message tokens, match, L2 and next book image");
+  m.def("gen_sample", &gen_sample, "syntax-masked argmax / Gumbel-max sampling from fp32 logits");
+  m.def("gen_time_tokens", &gen_time_tokens, "generation: absolute-time tokens from delta-t tokens");
 }

@@ -31,7 +31,8 @@ void m3_prep_fwd_launch(const M3Geo& g, const void* proj, const float* wB, const
                         float* sig, float* rate, cudaStream_t st);
 void m3_chunk_totals_launch(const M3Geo& g, const M3Scan& s, float* aend, float* angtot, float* theta0,
                             cudaStream_t st);
-void m3_states_launch(const M3Geo& g, const M3Scan& s, void* states, cudaStream_t st);
+void m3_states_launch(const M3Geo& g, const M3Scan& s, void* states, cudaStream_t st,
+                      float* final_state = nullptr);
 void m3_scan_launch(const M3Geo& g, const M3Scan& s, const void* states, void* y, cudaStream_t st);
 void m3_dstates_launch(const M3Geo& g, const M3Scan& s, const void* dy, void* U, cudaStream_t st);
 void m3_chunk_bwd_launch(const M3Geo& g, const M3Scan& s, const void* dy, const void* states, const void* dsout,
@@ -64,3 +65,37 @@ void sumsq_launch(const float* g, long n, float* out, int sms, cudaStream_t st);
 void adam_launch(float* p, const float* g, float* m, float* v, void* pb, long n, const float* sumsq,
                  float max_norm, const float* lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
                  int sms, cudaStream_t st);
+
+// ---- Mamba3 decode step (decode.cu) ---------------------------------------------------
+void m3_decode_step_launch(const void* proj, int B, int ldp, int nh, const float* wB, const float* wC,
+                           const float* dt_bias, const float* Bb, const float* Cb, const float* D, float A_floor,
+                           float eps, float* ang, float* ssm, float* kprev, float* vprev, void* y,
+                           cudaStream_t st);
+
+// ---- batched matching engine (engine.cu) ------------------------------------------------
+void eng_process_launch(int* asks, int* bids, int* trades, const int* msgs, int n_msgs, int n_books, int n_orders,
+                        int n_trades, int init_id, int book_depth, int cancel_mode, int type4, int check_fill,
+                        cudaStream_t st);
+void eng_l2_launch(const int* asks, const int* bids, int* out, int levels, int n_books, int n_orders,
+                   cudaStream_t st);
+
+// Token layout of one message for the generation step (positions and field
+// token offsets of the active tokenizer mode).
+struct GenLayout {
+  int msg_len, fused_ed, ev_pos, ev_off, dir_pos, dir_off;
+  int sign_off, price_off, price_digits, p_pos, pref_pos;
+  int size_digits, size_off, size_n, s_pos, sref_pos;
+  int time_off, dt_pos, tref_pos;
+  int tick, img_levels, l2_levels;
+};
+void gen_apply_launch(int* asks, int* bids, int* trades, const int64_t* toks, const GenLayout& L, int n_orders,
+                      int n_trades, int init_id, int book_depth, int cancel_mode, int type4, int check_fill,
+                      const int* new_oid, int* p_mid, const int* time_in, int* raw_out, int* msg_out, int* prov_out,
+                      int* l2_out, float* img_out, int img_stride, int n_books, int apply, cudaStream_t st);
+
+// generation (generate.cu)
+void gen_sample_launch(const float* logits, int ldl, const float* bias, const unsigned char* allow, int V, int B,
+                       unsigned long long seed, const long long* ctr, int salt, int top_n, int64_t* out,
+                       int out_stride, cudaStream_t st);
+void gen_time_tokens_launch(int64_t* msg, int msg_len, int dt_pos, int time_off, int* time, int n,
+                            cudaStream_t st);

@@ -336,7 +336,8 @@ __device__ __forceinline__ size_t state_off(const Geo& g, int b, int h, int c) {
 //   backward (REV=true):  buf[c] <- dS_out[c]; run = exp(aend[c]) * run + U[c]
 // ---------------------------------------------------------------------------
 template <bool REV>
-__global__ void __launch_bounds__(128) m3_pass(bf16* __restrict__ buf, const float* __restrict__ aend, Geo g) {
+__global__ void __launch_bounds__(128) m3_pass(bf16* __restrict__ buf, const float* __restrict__ aend, Geo g,
+                                              float* __restrict__ final_state) {
   const size_t bh = blockIdx.x;
   const int e8 = blockIdx.y * 128 + threadIdx.x;        // 8 consecutive elements per thread
   const size_t stride = (size_t)P * N / 8;              // in uint4 units
@@ -373,6 +374,11 @@ __global__ void __launch_bounds__(128) m3_pass(bf16* __restrict__ buf, const flo
         base[(size_t)c * stride] = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
+  }
+  if (final_state) {   // state after the last chunk (decode prefill)
+    float4* fs = reinterpret_cast<float4*>(final_state + (bh * P * N) + (size_t)e8 * 8);
+    fs[0] = make_float4(run[0], run[1], run[2], run[3]);
+    fs[1] = make_float4(run[4], run[5], run[6], run[7]);
   }
 }
 
@@ -1388,12 +1394,13 @@ void m3_chunk_totals_launch(const M3Geo& G, const M3Scan& S, float* aend, float*
   m3_theta_scan<<<g.B * g.nh, 32, 0, st>>>(angtot, theta0, g);
 }
 
-void m3_states_launch(const M3Geo& G, const M3Scan& S, void* states, cudaStream_t st) {
+void m3_states_launch(const M3Geo& G, const M3Scan& S, void* states, cudaStream_t st, float* final_state) {
   Geo g = make_geo(G);
   ScanIn in = make_in(S);
   set_smem(m3_chunk_state, STATE_SMEM);
   m3_chunk_state<<<dim3(g.nh, g.nc, g.B), 256, STATE_SMEM, st>>>(in, g, reinterpret_cast<bf16*>(states));
-  m3_pass<false><<<dim3(g.B * g.nh, P * N / 8 / 128), 128, 0, st>>>(reinterpret_cast<bf16*>(states), S.aend, g);
+  m3_pass<false><<<dim3(g.B * g.nh, P * N / 8 / 128), 128, 0, st>>>(reinterpret_cast<bf16*>(states), S.aend, g,
+                                                                          final_state);
 }
 
 void m3_scan_launch(const M3Geo& G, const M3Scan& S, const void* states, void* y, cudaStream_t st) {
@@ -1410,7 +1417,7 @@ void m3_dstates_launch(const M3Geo& G, const M3Scan& S, const void* dy, void* U,
   set_smem(m3_chunk_dstate, DST_SMEM);
   m3_chunk_dstate<<<dim3(g.nh, g.nc, g.B), 256, DST_SMEM, st>>>(in, g, reinterpret_cast<const bf16*>(dy),
                                                                 reinterpret_cast<bf16*>(U));
-  m3_pass<true><<<dim3(g.B * g.nh, P * N / 8 / 128), 128, 0, st>>>(reinterpret_cast<bf16*>(U), S.aend, g);
+  m3_pass<true><<<dim3(g.B * g.nh, P * N / 8 / 128), 128, 0, st>>>(reinterpret_cast<bf16*>(U), S.aend, g, nullptr);
 }
 
 void m3_chunk_bwd_launch(const M3Geo& G, const M3Scan& S, const void* dy, const void* states, const void* dsout,

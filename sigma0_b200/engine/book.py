@@ -117,7 +117,7 @@ class OrderBook:
     def _match_one(self, side, top, qtm, agr_oid, sec, ns, agr_tid, s):
         newq = max(0, side[top, 1] - qtm)
         qtm = int(qtm - side[top, 1])
-        tr = np.nonzero(self.trades[:, 2] == EMPTY)[0]
+        tr = np.nonzero(self.trades[:, 4] == EMPTY)[0]   # the reference tests column 4
         ti = tr[0] if len(tr) else -1
         self.trades[ti] = [side[top, 0], -s * (side[top, 1] - newq), side[top, 2],
                            agr_oid, sec, ns, side[top, 3], agr_tid]

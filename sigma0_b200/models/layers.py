@@ -93,10 +93,21 @@ class SequenceLayer(nn.Module):
             x = self.norm(x)
         return state, x
 
-    def prefill(self, x, max_cache_len):
-        if self.is_transformer and hasattr(self.seq, "prefill"):
+    @torch.no_grad()
+    def prefill(self, x, max_cache_len=None):
+        """Training-identical forward that also returns the decode state."""
+        if self.is_transformer:
             return self.seq.prefill(x, max_cache_len)
-        return None, self(x)
+        skip = x
+        h = self.norm(x) if self.prenorm else x
+        if hasattr(self.seq, "prefill"):
+            state, h = self.seq.prefill(h)
+        else:
+            state, h = self.seq.step(self.seq.initial_state(x.shape[0], x.device), h)
+        x = skip + self._act(h)
+        if not self.prenorm:
+            x = self.norm(x)
+        return state, x
 
 
 class StackedEncoder(nn.Module):
@@ -129,6 +140,15 @@ class StackedEncoder(nn.Module):
 
     def initial_state(self, batch, device=None):
         return [l.initial_state(batch, device) for l in self.layers]
+
+    @torch.no_grad()
+    def prefill(self, x, max_cache_len=None):
+        x = self.encoder(x)
+        states = []
+        for layer in self.layers:
+            st, x = layer.prefill(x, max_cache_len)
+            states.append(st)
+        return states, x
 
     def step(self, states, x):
         x = self.encoder(x)

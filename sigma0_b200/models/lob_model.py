@@ -58,6 +58,18 @@ class LobBookEncoder(nn.Module):
         return ([l.initial_state(batch, device) for l in self.pre_layers],
                 [l.initial_state(batch, device) for l in self.post_layers])
 
+    @torch.no_grad()
+    def prefill(self, x, max_cache_len=None):
+        pre, post = [], []
+        for l in self.pre_layers:
+            st, x = l.prefill(x, max_cache_len)
+            pre.append(st)
+        x = self.projection(x)
+        for l in self.post_layers:
+            st, x = l.prefill(x, max_cache_len)
+            post.append(st)
+        return (pre, post), x
+
     def step(self, states, x):
         pre, post = states
         npre, npost = [], []
@@ -145,8 +157,26 @@ class LobModel(nn.Module):
                 self.book_encoder.initial_state(batch, device) if self.use_book_data else None,
                 self.fused_s5.initial_state(batch, device))
 
+    @torch.no_grad()
+    def prefill(self, tokens, book=None, max_cache_len=None):
+        """Forward over a context that returns (decode state, log-probs of the last token)."""
+        sm, xm = self.message_encoder.prefill(tokens, max_cache_len)
+        sb = None
+        if self.use_book_data:
+            sb, xb = self.book_encoder.prefill(self.repeat_book(book, tokens.shape[1]), max_cache_len)
+            x = torch.cat([xm, xb.to(xm.dtype)], dim=-1)
+        else:
+            x = xm
+        sf, h = self.fused_s5.prefill(x, max_cache_len)
+        return (sm, sb, sf), F.log_softmax(self.decoder(h[:, -1:]).float(), dim=-1)
+
     def step(self, state, tokens, book=None):
         """Recurrent step over ``tokens`` (B, l) with book rows (B, l, d_book) -> (state, logp)."""
+        state, h = self.step_hidden(state, tokens, book)
+        return state, F.log_softmax(self.decoder(h).float(), dim=-1)
+
+    def step_hidden(self, state, tokens, book=None):
+        """``step`` without the decoder: (state, last hidden (B, l, d_model))."""
         sm, sb, sf = state
         sm, xm = self.message_encoder.step(sm, tokens)
         if self.use_book_data:
@@ -155,4 +185,4 @@ class LobModel(nn.Module):
         else:
             x = xm
         sf, h = self.fused_s5.step(sf, x)
-        return (sm, sb, sf), F.log_softmax(self.decoder(h).float(), dim=-1)
+        return (sm, sb, sf), h

@@ -128,8 +128,14 @@ class Mamba3(nn.Module):
         return (z(batch, d.n_heads, d.R), z(batch, d.n_heads, d.headdim, d.d_state),
                 z(batch, d.n_heads, d.d_state), z(batch, d.n_heads, d.headdim))
 
+    def _cuda_ok(self, u) -> bool:
+        d = self.dims
+        return (self.impl == "cuda" and u.is_cuda and (d.d_state, d.headdim, d.chunk_size, d.R) == (128, 64, 64, 32))
+
     def step(self, state, u: torch.Tensor):
         """Run ``u`` (B, L, H) through the recurrence from ``state``; returns (state, out)."""
+        if self._cuda_ok(u) and u.shape[1] == 1:
+            return self._step_cuda(state, u)
         proj = self.in_proj(u, dtype=self.compute_dtype)
         z, x, B, C, ADT, DT, trap, ang = self._prep(proj)
         nh = self.dims.n_heads
@@ -139,3 +145,55 @@ class Mamba3(nn.Module):
                                         trap.transpose(1, 2), ang, self.C_bias, self.B_bias,
                                         self.D, z, state)
         return state, self._post(y)
+
+    # -- CUDA decode and prefill -------------------------------------------------------------
+    def _proj_cuda(self, u2):
+        from ..ops import weights as W
+        d = self.dims
+        ldp = (d.d_in_proj + 7) // 8 * 8
+        return u2.to(torch.bfloat16).contiguous() @ W.bf16_padded(self.in_proj.kernel, ldp)
+
+    def _post_cuda(self, y2):
+        from ..ops._ext import ext
+        from ..ops import weights as W
+        yn, _ = ext().rms_fwd(y2, self.out_norm.scale, 1e-6)
+        return yn @ W.bf16(self.out_proj.kernel)
+
+    def _step_cuda(self, state, u):
+        from ..ops._ext import ext
+        d = self.dims
+        B = u.shape[0]
+        proj = self._proj_cuda(u[:, 0])
+        ang, ssm, kp, vp = state
+        y = torch.empty(B, d.d_inner, dtype=torch.bfloat16, device=u.device)
+        ext().m3_decode_step(proj, d.n_heads, self.B_norm.scale, self.C_norm.scale, self.dt_bias, self.B_bias,
+                             self.C_bias, self.D, self.A_floor, 1e-6, ang, ssm, kp, vp, y)
+        return state, self._post_cuda(y)[:, None]
+
+    @torch.no_grad()
+    def prefill(self, u: torch.Tensor):
+        """Chunked forward over ``u`` (B, L, H) that also returns the recurrent state
+        after the last token (the decode carry), instead of stepping token by token."""
+        d = self.dims
+        B, L, H = u.shape
+        if not self._cuda_ok(u):
+            proj = self.in_proj(u, dtype=self.compute_dtype)
+            z, x, Bn, Cn, ADT, DT, trap, ang = self._prep(proj)
+            st0 = self.initial_state(B, u.device)
+            nh = d.n_heads
+            y, st = ref.mamba3_recurrent(Cn[:, :, None].expand(-1, -1, nh, -1), Bn[:, :, None].expand(-1, -1, nh, -1),
+                                         x, ADT.transpose(1, 2), DT.transpose(1, 2), trap.transpose(1, 2), ang,
+                                         self.C_bias, self.B_bias, self.D, z, st0)
+            return st, self._post(y)
+        from ..ops._ext import ext
+        proj = self._proj_cuda(u.reshape(-1, H))
+        y, _, fin, thf = ext().m3_fwd(proj, B, L, d.n_heads, self.B_norm.scale, self.C_norm.scale, self.dt_bias,
+                                      self.B_bias, self.C_bias, self.D, self.A_floor, 1e-6, want_final=True)
+        # k_prev / v_prev: the last token's rotated key and value
+        last = proj.view(B, L, -1)[:, -1, :d.d_in_proj].float()
+        z, x, Bn, Cn, ADT, DT, trap, angr = self._prep(last[:, None])
+        cos, sin = torch.cos(thf), torch.sin(thf)
+        Kb = Bn[:, 0][:, None, :] + self.B_bias[None]
+        kp = ref.apply_rope(Kb, cos, sin)
+        st = (thf.contiguous(), fin, kp.contiguous(), x[:, 0].contiguous())
+        return st, self._post_cuda(y.view(-1, d.d_inner)).view(B, L, H)

@@ -13,6 +13,7 @@ import torch
 import torch.nn.functional as F
 
 _SHADOW: Dict[int, torch.Tensor] = {}
+_PADDED: Dict[tuple, torch.Tensor] = {}
 
 
 def register(param: torch.Tensor, shadow: torch.Tensor) -> None:
@@ -21,6 +22,16 @@ def register(param: torch.Tensor, shadow: torch.Tensor) -> None:
 
 def clear() -> None:
     _SHADOW.clear()
+    _PADDED.clear()
+
+
+def freeze(module: torch.nn.Module) -> None:
+    """Inference: cache a bf16 copy of every parameter once (and, lazily, the
+    padded GEMM operands), so decode steps stop re-casting float32 weights."""
+    for p in module.parameters():
+        if id(p) not in _SHADOW:
+            _SHADOW[id(p)] = p.detach().to(torch.bfloat16)
+            _PADDED[("frozen", id(p))] = _SHADOW[id(p)]
 
 
 def bf16(param: torch.Tensor) -> torch.Tensor:
@@ -35,4 +46,11 @@ def bf16_padded(param: torch.Tensor, cols: int) -> torch.Tensor:
     w = bf16(param)
     if w.shape[1] == cols:
         return w
-    return F.pad(w, (0, cols - w.shape[1]))
+    frozen = ("frozen", id(param)) in _PADDED
+    key = (id(param), cols)
+    if frozen and key in _PADDED:
+        return _PADDED[key]
+    out = F.pad(w, (0, cols - w.shape[1]))
+    if frozen:
+        _PADDED[key] = out
+    return out
