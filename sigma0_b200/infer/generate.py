@@ -321,7 +321,9 @@ class Generator:
         self.book[:, 0] = torch.from_numpy(np.stack(imgs)).to(self.book.dtype)
 
     @torch.no_grad()
-    def generate(self, n_msgs: int) -> GenOutput:
+    def generate(self, n_msgs: int, events=None) -> GenOutput:
+        """Generate ``n_msgs`` messages for every book.  ``events``: optional list of
+        ``n_msgs + 1`` CUDA events recorded before each message and at the end."""
         B, L, dev = self.B, self.tok.MSG_LEN, self.dev
         self.o_raw = torch.zeros(B, 14, dtype=torch.int32, device=dev)
         self.o_msg = torch.zeros(B, 8, dtype=torch.int32, device=dev)
@@ -336,6 +338,8 @@ class Generator:
         self.graph = None
         graph = self.on_gpu and self.use_graphs and n_msgs > 1
         for k in range(n_msgs):
+            if events is not None:
+                events[k].record()
             if self.on_gpu:
                 if graph and self.graph is None and k == 1:
                     self._capture()
@@ -351,6 +355,8 @@ class Generator:
             out_l2[:, k] = self.o_l2
             out_prov[:, k] = self.o_prov
             out_mid[:, k] = self.p_mid
+        if events is not None:
+            events[n_msgs].record()
         return GenOutput(out_tok, out_raw, out_l2, out_prov, out_mid)
 
     def _capture(self):
