@@ -45,7 +45,7 @@ class FlatAdam:
     def __init__(self, model: nn.Module, lr: float, ssm_lr: float, weight_decay: float = 0.05,
                  max_grad_norm: float = 1.0, betas=(0.9, 0.999), eps: float = 1e-8,
                  opt_config: str = "standard", attention_model: bool = False,
-                 bf16_shadow: bool = True):
+                 bf16_shadow: bool = True, pad_multiple: int = 128):
         self.model = model
         self.b1, self.b2 = betas
         self.eps = eps
@@ -63,6 +63,7 @@ class FlatAdam:
         A = 128
         rnd = lambda n: (n + A - 1) // A * A
         total = sum(rnd(p.numel()) for _, p in order)
+        total = -(-total // pad_multiple) * pad_multiple   # equal shards when sharded
         self.n_ssm = sum(rnd(p.numel()) for _, p in groups["ssm"])
         self.numel = total
         self.device = dev
@@ -91,6 +92,41 @@ class FlatAdam:
         self._lr = torch.zeros(2, dtype=torch.float32, device=dev)
         self.last_grad_norm: Optional[torch.Tensor] = None
 
+    # -- sharding (ZeRO-1/2: each rank owns a contiguous slice of the flat buffer) -------------
+    def shard(self, world: int, rank: int) -> None:
+        """Keep Adam moments only for this rank's shard ``[lo, hi)`` of the flat buffer
+        (``numel / world`` elements; the buffer is padded so the shards are equal)."""
+        if self.numel % (128 * world):
+            raise ValueError("build FlatAdam with pad_multiple=128*world to shard it")
+        per = self.numel // world
+        self.world, self.rank = world, rank
+        self.shard_per = per
+        self.lo, self.hi = min(rank * per, self.numel), min((rank + 1) * per, self.numel)
+        n = self.hi - self.lo
+        self.m = torch.zeros(n, dtype=torch.float32, device=self.device)
+        self.v = torch.zeros(n, dtype=torch.float32, device=self.device)
+        self.sharded = True
+
+    def shard_bounds(self):
+        if not getattr(self, "sharded", False):
+            return None
+        return [[min(k * self.shard_per, self.numel), min((k + 1) * self.shard_per, self.numel)]
+                for k in range(self.world)]
+
+    def local_moments(self):
+        return self.m, self.v
+
+    def load_full_moments(self, m: torch.Tensor, v: torch.Tensor, step: int) -> None:
+        """Moments of the whole flat buffer (any sharding at save time) -> this rank's layout."""
+        self.step_count = int(step)
+        lo, hi = (self.lo, self.hi) if getattr(self, "sharded", False) else (0, self.numel)
+        self.m.copy_(m[lo:hi])
+        self.v.copy_(v[lo:hi])
+
+    def params_in_order(self):
+        named = dict(self.model.named_parameters())
+        return [named[n] for n in self.names]
+
     def refresh_shadow(self):
         if self.shadow is not None:
             self.shadow.copy_(self.flat)
@@ -105,6 +141,38 @@ class FlatAdam:
         self.step_count = int(sd["step"])
         self.m.copy_(sd["m"])
         self.v.copy_(sd["v"])
+
+    def step_shard(self, gshard: torch.Tensor, grad_sumsq: torch.Tensor, lr_scale: float = 1.0) -> None:
+        """Adam on this rank's shard only: ``gshard`` is the reduced gradient of ``[lo, hi)``
+        and ``grad_sumsq`` the global sum of squares (for clipping)."""
+        self.step_count += 1
+        t = self.step_count
+        bc1, bc2 = 1 - self.b1 ** t, 1 - self.b2 ** t
+        lr_s, lr_r = self.base_lr["ssm"] * lr_scale, self.base_lr["regular"] * lr_scale
+        self.last_grad_norm = grad_sumsq
+        lo, hi, ns = self.lo, self.hi, self.n_ssm
+        pieces = []
+        if lo < min(hi, ns):
+            pieces.append((lo, min(hi, ns), lr_s, 0.0, 0))
+        if max(lo, ns) < hi:
+            pieces.append((max(lo, ns), hi, lr_r, self.wd, 1))
+        if self.device.type == "cuda":
+            from ..ops._ext import ext
+            C = ext()
+            self._lr.copy_(torch.tensor([lr_s, lr_r]), non_blocking=True)
+            for a, b, _, wd, gi in pieces:
+                sh = self.shadow[a:b] if self.shadow is not None else None
+                C.adam(self.flat[a:b], gshard[a - lo:b - lo], self.m[a - lo:b - lo], self.v[a - lo:b - lo], sh,
+                       grad_sumsq, self.max_grad_norm, self._lr[gi:gi + 1], self.b1, self.b2, self.eps, wd, bc1, bc2)
+            return
+        nrm = math.sqrt(float(grad_sumsq))
+        scale = 1.0 if (self.max_grad_norm <= 0 or nrm < self.max_grad_norm) else self.max_grad_norm / nrm
+        for a, b, lr, wd, _ in pieces:
+            g = gshard[a - lo:b - lo] * scale
+            m, v, p = self.m[a - lo:b - lo], self.v[a - lo:b - lo], self.flat[a:b]
+            m.mul_(self.b1).add_(g, alpha=1 - self.b1)
+            v.mul_(self.b2).addcmul_(g, g, value=1 - self.b2)
+            p.sub_(lr * ((m / bc1) / ((v / bc2).sqrt() + self.eps) + wd * p))
 
     def step(self, lr_scale: float = 1.0, grad_sumsq: Optional[torch.Tensor] = None):
         """One update.  ``grad_sumsq`` overrides the local sum of squares (sharded optimizers)."""

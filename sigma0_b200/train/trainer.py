@@ -30,7 +30,8 @@ from .optim import FlatAdam, cosine_schedule
 
 class Trainer:
     def __init__(self, args, device: Optional[torch.device] = None, world: int = 1, rank: int = 0,
-                 group=None, total_steps: int = 1000, seed: int = 0, sharded: bool = False):
+                 group=None, total_steps: int = 1000, seed: int = 0, sharded: bool = False,
+                 accum_steps: int = 1, grad_wire_dtype: str = "float32"):
         self.args = args
         self.device = device or torch.device("cuda" if torch.cuda.is_available() else "cpu")
         self.world, self.rank, self.group = world, rank, group
@@ -50,37 +51,91 @@ class Trainer:
                             weight_decay=float(getattr(args, "weight_decay", 0.05)),
                             max_grad_norm=float(getattr(args, "max_grad_norm", 1.0)),
                             opt_config=str(getattr(args, "opt_config", "standard")),
-                            attention_model=attn_only)
+                            attention_model=attn_only,
+                            pad_multiple=128 * (world if (sharded and world > 1) else 1))
         self.total_steps = total_steps
         self.warmup_steps = int(round(float(getattr(args, "warmup_end", 0.01)) * total_steps))
         lr_min = float(getattr(args, "lr_min", 0.0) or 0.0)
         self.lr_min_frac = (lr_min / lr) if lr_min > 0 else 0.05
         self.ignore_times = bool(getattr(args, "ignore_times", False))
         self.sharded = sharded and world > 1
+        if self.sharded:
+            self.opt.shard(world, rank)
+            self._gshard = torch.empty(self.opt.hi - self.opt.lo, dtype=torch.float32, device=self.device)
+        if grad_wire_dtype not in ("float32", "bfloat16"):
+            raise ValueError(f"grad_wire_dtype must be float32 or bfloat16, not {grad_wire_dtype!r}")
+        self.wire_bf16 = grad_wire_dtype == "bfloat16"
+        self.accum_steps = max(1, int(accum_steps))
+        self.global_batch = int(getattr(args, "micro_bsz", 1)) * world
         self.step_idx = 0
         self._sumsq_all = torch.zeros(1, device=self.device)
 
     # -- one step -------------------------------------------------------------------------
-    def _reduce_grads(self):
+    def _update(self, lr_scale: float):
+        """Gradient reduction over ranks + optimizer update.
+
+        * one rank: plain update;
+        * replicated DP: all-reduce of the flat gradient (the reference's pmean,
+          ``training/train_helpers.py:2123-2196``), optionally on a bf16 wire
+          (``GRAD_ALLREDUCE_DTYPE=bfloat16``, ``:2045-2066``);
+        * sharded DP (ZeRO-1/2): reduce-scatter so each rank gets the summed
+          gradient of its shard, global-norm from the shards' sums of squares,
+          Adam on the shard, then all-gather of the updated parameters."""
+        opt = self.opt
         if self.world == 1:
-            return None
-        g = self.opt.grad
+            opt.step(lr_scale=lr_scale)
+            return
+        g = opt.grad
         if not self.sharded:
-            g.div_(self.world)
-            dist.all_reduce(g, group=self.group)
-            return None
-        raise NotImplementedError
+            if self.wire_bf16:
+                gb = g.to(torch.bfloat16)
+                dist.all_reduce(gb, group=self.group)
+                g.copy_(gb)
+                g.div_(self.world)
+            else:
+                g.div_(self.world)
+                dist.all_reduce(g, group=self.group)
+            opt.step(lr_scale=lr_scale)
+            return
+        gs = self._gshard
+        if self.wire_bf16:
+            out = torch.empty(gs.numel(), dtype=torch.bfloat16, device=self.device)
+            dist.reduce_scatter_tensor(out, g.to(torch.bfloat16), group=self.group)
+            gs.copy_(out)
+        else:
+            dist.reduce_scatter_tensor(gs, g, group=self.group)
+        gs.div_(self.world)
+        ss = self._sumsq_all
+        if gs.is_cuda:
+            from ..ops._ext import ext
+            ss.zero_()
+            ext().sumsq(gs, ss)
+        else:
+            ss.copy_((gs * gs).sum().reshape(1))
+        dist.all_reduce(ss, group=self.group)
+        opt.step_shard(gs, ss, lr_scale=lr_scale)
+        dist.all_gather_into_tensor(opt.flat, opt.flat[opt.lo:opt.hi].clone(), group=self.group)
+        opt.refresh_shadow()
 
     def step_device(self, tokens, labels, book=None):
+        """One optimizer step on device tensors; with ``accum_steps > 1`` the batch is
+        split into micro-batches whose gradients accumulate before the update."""
         self.opt.zero_grad()
-        loss, ce_pos = self.model.loss(tokens, book, labels, ignore_times=self.ignore_times,
-                                       tokenizer=self.tok)
-        loss.backward()
-        self._reduce_grads()
+        k = self.accum_steps
+        if k == 1:
+            loss, _ = self.model.loss(tokens, book, labels, ignore_times=self.ignore_times, tokenizer=self.tok)
+            loss.backward()
+            total = loss.detach()
+        else:
+            total = torch.zeros((), device=tokens.device)
+            for tc, lc, bc in zip(tokens.chunk(k), labels.chunk(k), book.chunk(k) if book is not None else [None] * k):
+                loss, _ = self.model.loss(tc, bc, lc, ignore_times=self.ignore_times, tokenizer=self.tok)
+                (loss / k).backward()
+                total = total + loss.detach() / k
         scale = cosine_schedule(self.step_idx + 1, self.warmup_steps, self.total_steps, self.lr_min_frac)
-        self.opt.step(lr_scale=scale)
+        self._update(scale)
         self.step_idx += 1
-        return loss.detach()
+        return total
 
     def to_device(self, batch):
         return tuple(t.to(self.device, non_blocking=True) if t is not None else None for t in batch)

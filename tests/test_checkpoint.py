@@ -1,0 +1,83 @@
+"""Checkpoint round trip, retention, corruption fallback and params-only restore."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from sigma0_b200.ckpt import CheckpointManager, CheckpointError, remap_step
+
+
+def _args(**kw):
+    from sigma0_b200.models import preset_args
+    return preset_args("smoke", d_model=64, mamba3_d_state=16, mamba3_headdim=16, n_messages=4, micro_bsz=2,
+                       warmup_end=0.0, **kw)
+
+
+def _data():
+    from sigma0_b200.data import make_sequences, LobWindowDataset, collate
+    ds = LobWindowDataset.from_days(make_sequences(2, 5, seed=4), 4, token_mode="22tok")
+    return collate([ds[i] for i in range(2)])
+
+
+def _trainer(seed=0, **kw):
+    from sigma0_b200.train.trainer import Trainer
+    return Trainer(_args(**kw), device=torch.device("cpu"), total_steps=20, seed=seed)
+
+
+def test_resume_continues_bit_exactly(tmp_path):
+    batch = _data()
+    a = _trainer()
+    for _ in range(2):
+        a.step_device(*batch)
+    mgr = CheckpointManager(str(tmp_path))
+    mgr.save(2, a, metrics={"loss": 1.0})
+    mgr.wait()
+    a.step_device(*batch)
+    b = _trainer(seed=7)
+    meta = mgr.restore(b)
+    assert meta["step"] == 2 and b.step_idx == 2 and b.opt.step_count == 2
+    b.step_device(*batch)
+    assert torch.equal(a.opt.flat, b.opt.flat)
+    assert torch.equal(a.opt.m, b.opt.m) and torch.equal(a.opt.v, b.opt.v)
+
+
+def test_retention_and_corruption_fallback(tmp_path):
+    a = _trainer()
+    mgr = CheckpointManager(str(tmp_path), max_to_keep=2, keep_period=5)
+    for s in (1, 2, 3, 4, 5, 6, 7):
+        mgr.save(s, a, blocking=True)
+    assert mgr.steps() == [5, 6, 7]   # newest two, plus multiples of keep_period
+    with open(os.path.join(str(tmp_path), "7", "state", "params.f32"), "r+b") as f:
+        f.seek(16)
+        f.write(b"\x00\x01\x02\x03")
+    assert not mgr.verify(7) and mgr.verify(6)
+    meta = mgr.restore(_trainer(seed=3))
+    assert meta["restored_step"] == 6
+    with pytest.raises(CheckpointError):
+        mgr.restore(_trainer(), step=7)
+
+
+def test_params_only_restore_into_other_layout(tmp_path):
+    a = _trainer()
+    a.step_device(*_data())
+    mgr = CheckpointManager(str(tmp_path))
+    mgr.save(1, a, blocking=True)
+    b = _trainer(seed=5, opt_config="noBCdecay")   # different optimizer grouping -> different flat layout
+    mgr.restore(b, params_only=True)
+    pa = dict(a.model.named_parameters())
+    for n, p in b.model.named_parameters():
+        assert torch.equal(p, pa[n]), n
+
+
+def test_export_npz_uses_flax_paths(tmp_path):
+    a = _trainer()
+    p = os.path.join(str(tmp_path), "params.npz")
+    CheckpointManager(str(tmp_path)).export_params_npz(a, p)
+    z = np.load(p)
+    assert "params/decoder/kernel" in z.files
+    assert any(k.startswith("params/message_encoder/encoder/embedding") for k in z.files)
+
+
+def test_remap_step():
+    assert remap_step(100, 64, 32) == 200 and remap_step(100, 64, 64) == 100 and remap_step(7, 4, 8) == 3
