@@ -408,6 +408,47 @@ void gen_time_tokens(at::Tensor msg, int64_t dt_pos, int64_t time_off, at::Tenso
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void dp_fused_adam(std::vector<int64_t> G, std::vector<int64_t> P, std::vector<int64_t> S,
+                   std::vector<int64_t> flags, std::vector<int64_t> sums, at::Tensor m, at::Tensor v,
+                   at::Tensor scratch, at::Tensor status, int64_t lo, int64_t hi, int64_t n_ssm, int64_t rank,
+                   int64_t seq, int64_t spin_limit, double lr_s, double lr_r, double wd, double b1, double b2,
+                   double eps, double bc1, double bc2, double max_norm) {
+  const int world = (int)G.size();
+  TORCH_CHECK(world >= 1 && world <= DPF_MAXW, "world size must be in [1, ", DPF_MAXW, "]");
+  TORCH_CHECK((int)P.size() == world && (int)S.size() == world && (int)flags.size() == world &&
+                  (int)sums.size() == world, "one pointer per rank for every buffer");
+  req(m, at::kFloat, "m");
+  req(v, at::kFloat, "v");
+  req(scratch, at::kInt, "scratch");
+  req(status, at::kInt, "status");
+  TORCH_CHECK(lo % 128 == 0 && hi % 4 == 0 && hi >= lo && m.numel() == hi - lo && v.numel() == hi - lo,
+              "shard bounds / moment sizes");
+  TORCH_CHECK(scratch.numel() >= 2, "scratch holds [sumsq, abort]");
+  c10::cuda::CUDAGuard guard(m.device());
+  DpfArgs a{};
+  for (int k = 0; k < world; ++k) {
+    a.G[k] = reinterpret_cast<float*>(G[k]);
+    a.P[k] = reinterpret_cast<float*>(P[k]);
+    a.S[k] = reinterpret_cast<__nv_bfloat16*>(S[k]);
+    a.flags[k] = reinterpret_cast<int*>(flags[k]);
+    a.sums[k] = reinterpret_cast<float*>(sums[k]);
+    TORCH_CHECK(G[k] % 16 == 0 && P[k] % 16 == 0 && S[k] % 8 == 0, "buffers must be 16-byte aligned");
+  }
+  a.m = m.data_ptr<float>();
+  a.v = v.data_ptr<float>();
+  a.sumsq_local = reinterpret_cast<float*>(scratch.data_ptr<int>());
+  a.abort = scratch.data_ptr<int>() + 1;
+  a.status = status.data_ptr<int>();
+  a.lo = lo; a.hi = hi; a.n_ssm = n_ssm;
+  a.world = world; a.rank = (int)rank; a.seq = (int)seq; a.spin_limit = spin_limit;
+  a.lr_s = (float)lr_s; a.lr_r = (float)lr_r; a.wd = (float)wd; a.b1 = (float)b1; a.b2 = (float)b2;
+  a.eps = (float)eps; a.bc1 = (float)bc1; a.bc2 = (float)bc2; a.max_norm = (float)max_norm;
+  a.inv_world = 1.f / world;
+  C10_CUDA_CHECK(cudaMemsetAsync(scratch.data_ptr<int>(), 0, 2 * sizeof(int), stream()));
+  int rc = dp_fused_adam_launch(a, num_sms(m), stream());
+  TORCH_CHECK(rc == 0, "dp_fused_adam launch failed: ", rc > 0 ? cudaGetErrorString((cudaError_t)rc) : "occupancy");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -430,6 +471,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("m3_decode_step", &m3_decode_step, "Mamba3 one-token recurrent step (states updated in place)");
   m.def("eng_process", &eng_process, "batched matching engine: apply [B, M, 8] messages, one warp per book");
   m.def("eng_l2", &eng_l2, "batched L2 extraction");
+  m.def("dp_fused_adam", &dp_fused_adam, "fused reduce-scatter + AdamW + all-gather over peer memory");
   m.def("gen_apply", &gen_apply, "generation: decode message tokens, match, L2 and next book image");
   m.def("gen_sample", &gen_sample, "syntax-masked argmax / Gumbel-max sampling from fp32 logits");
   m.def("gen_time_tokens", &gen_time_tokens, "generation: absolute-time tokens from delta-t tokens");

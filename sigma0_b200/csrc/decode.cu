@@ -32,90 +32,146 @@ struct DecArgs {
   bf16* y;                 // [B, d_inner]
 };
 
+constexpr int HG = 8;   // heads per block: the per-token prologue is shared, state loads overlap
+
+// One block per (group of HG heads, book).  The first head's state loads are
+// issued before the prologue so their latency overlaps it.  Prologue: BCNorm of the token's B/C
+// row (shared by all heads), per-head dt / decay / trapezoid gate, angle update
+// and RoPE of K = Bn + B_bias[h], Q = Cn + C_bias[h], all into shared memory
+// behind a single barrier.  Main loop: each thread owns 32 consecutive state
+// entries of one row p (4 threads per row, 8 float4); the next head's state is
+// loaded into registers before the current head's is stored, so every thread
+// keeps 16 float4 loads in flight.
 __global__ void __launch_bounds__(NT) m3_decode_step(DecArgs a) {
-  __shared__ float sK[N], sQ[N], sKp[N], sX[P], sVp[P], sZ[P], sRed[2][8];
-  __shared__ float sSc[4];
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float sBn[N], sCn[N];
+  __shared__ float sK[HG][N], sQ[HG][N], sKp[HG][N];
+  __shared__ float sX[HG][P], sVp[HG][P], sZ[HG][P];
+  __shared__ float sDt[HG], sDec[HG], sSg[HG], sRed[2][4], sTh[HG][R];
+  const int b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int h0 = blockIdx.x * HG;
+  const int nhg = min(HG, a.nh - h0);
   const bf16* row = a.proj + (size_t)b * a.ldp;
   const int off_B = 2 * a.d_inner, off_C = off_B + N, off_dt = off_C + N;
   const int off_A = off_dt + a.nh, off_tr = off_A + a.nh, off_ang = off_tr + a.nh;
-  const size_t bh = (size_t)b * a.nh + h;
-  // BCNorm sums (warps 0-3: B, 4-7: C)
+  // the first head's state is independent of the prologue: start streaming it now
+  const int p = tid >> 2, part = tid & 3;
+  float4 cur[8], nxt[8];
+  auto state_row = [&](int hh) {
+    return a.ssm + (((size_t)b * a.nh + h0 + hh) * P + p) * N + part * 32;
+  };
   {
-    float v = 0.f;
-    if (tid < N) {
-      float x = __bfloat162float(row[off_B + tid]);
-      v = x * x;
-    } else {
-      float x = __bfloat162float(row[off_C + tid - N]);
-      v = x * x;
-    }
-    v = warp_sum(v);
+    const float4* src = reinterpret_cast<const float4*>(state_row(0));
+#pragma unroll
+    for (int q = 0; q < 8; ++q) cur[q] = src[q];
+  }
+  // BCNorm sums (warps 0-3: B, 4-7: C)
+  float bc = __bfloat162float(row[(tid < N) ? off_B + tid : off_C + tid - N]);
+  {
+    float v = warp_sum(bc * bc);
     if (lane == 0) sRed[warp >> 2][warp & 3] = v;
   }
-  if (tid == 0) {
+  if (tid < HG && tid < nhg) {
+    const int h = h0 + tid;
     float dt = softplusf_(__bfloat162float(row[off_dt + h]) + a.dt_bias[h]);
     float A = fminf(-softplusf_(__bfloat162float(row[off_A + h])), -a.A_floor);
-    sSc[0] = dt;
-    sSc[1] = __expf(A * dt);
-    sSc[2] = sigmoidf_(__bfloat162float(row[off_tr + h]));
+    sDt[tid] = dt;
+    sDec[tid] = __expf(A * dt);
+    sSg[tid] = sigmoidf_(__bfloat162float(row[off_tr + h]));
+  }
+  for (int i = tid; i < HG * P; i += NT) {
+    const int hh = i / P, p = i % P;
+    if (hh < nhg) {
+      const int h = h0 + hh;
+      const size_t bh = (size_t)b * a.nh + h;
+      sX[hh][p] = __bfloat162float(row[a.d_inner + h * P + p]);
+      sZ[hh][p] = __bfloat162float(row[h * P + p]);
+      sVp[hh][p] = a.vprev[bh * P + p];
+    }
   }
   __syncthreads();
-  const float dt = sSc[0], dec = sSc[1], sg = sSc[2];
   if (tid < N) {
-    float ssb = sRed[0][0] + sRed[0][1] + sRed[0][2] + sRed[0][3];
-    float ssc = sRed[1][0] + sRed[1][1] + sRed[1][2] + sRed[1][3];
-    float rb = rsqrtf(ssb / N + a.eps), rc = rsqrtf(ssc / N + a.eps);
-    sK[tid] = __bfloat162float(row[off_B + tid]) * rb * a.wB[tid] + a.Bb[h * N + tid];
-    sQ[tid] = __bfloat162float(row[off_C + tid]) * rc * a.wC[tid] + a.Cb[h * N + tid];
-    sKp[tid] = a.kprev[bh * N + tid];
-  }
-  if (tid < P) {
-    sX[tid] = __bfloat162float(row[a.d_inner + h * P + tid]);
-    sZ[tid] = __bfloat162float(row[h * P + tid]);
-    sVp[tid] = a.vprev[bh * P + tid];
+    const float rb = rsqrtf((sRed[0][0] + sRed[0][1] + sRed[0][2] + sRed[0][3]) / N + a.eps);
+    sBn[tid] = bc * rb * a.wB[tid];
+  } else {
+    const float rc = rsqrtf((sRed[1][0] + sRed[1][1] + sRed[1][2] + sRed[1][3]) / N + a.eps);
+    sCn[tid - N] = bc * rc * a.wC[tid - N];
   }
   __syncthreads();
-  if (tid < R) {   // angle state and rotation of the first 2R dims
-    float th = a.ang[bh * R + tid] + tanhf(__bfloat162float(row[off_ang + tid])) * PI_F * dt;
-    th = th - TWO_PI_F * floorf(th / TWO_PI_F);
-    a.ang[bh * R + tid] = th;
-    float sn, cs;
-    sincosf(th, &sn, &cs);
-    float k0 = sK[2 * tid], k1 = sK[2 * tid + 1], q0 = sQ[2 * tid], q1 = sQ[2 * tid + 1];
-    sK[2 * tid] = k0 * cs - k1 * sn;
-    sK[2 * tid + 1] = k0 * sn + k1 * cs;
-    sQ[2 * tid] = q0 * cs - q1 * sn;
-    sQ[2 * tid + 1] = q0 * sn + q1 * cs;
+  // per head: biased K/Q, previous K, angle update + rotation of the first 2R dims
+  for (int i = tid; i < HG * N; i += NT) {
+    const int hh = i / N, n = i % N;
+    if (hh < nhg) {
+      const int h = h0 + hh;
+      const size_t bh = (size_t)b * a.nh + h;
+      sKp[hh][n] = a.kprev[bh * N + n];
+      float k = sBn[n] + a.Bb[h * N + n], q = sCn[n] + a.Cb[h * N + n];
+      if (n < 2 * R) {
+        const int r = n >> 1;
+        float th = a.ang[bh * R + r] + tanhf(__bfloat162float(row[off_ang + r])) * PI_F * sDt[hh];
+        th = th - TWO_PI_F * floorf(th / TWO_PI_F);
+        if ((n & 1) == 0) sTh[hh][r] = th;   // written back after the barrier below
+        float sn, cs;
+        sincosf(th, &sn, &cs);
+        // partner element of the rotated pair
+        const int m = n ^ 1;
+        const float k2 = sBn[m] + a.Bb[h * N + m], q2 = sCn[m] + a.Cb[h * N + m];
+        if ((n & 1) == 0) { k = k * cs - k2 * sn; q = q * cs - q2 * sn; }
+        else { k = k2 * sn + k * cs; q = q2 * sn + q * cs; }
+      }
+      sK[hh][n] = k;
+      sQ[hh][n] = q;
+    }
   }
   __syncthreads();
-  // state rows: 4 threads per row p, 32 consecutive n each (float4 x 8)
-  const int p = tid >> 2, part = tid & 3;
-  float* hrow = a.ssm + (bh * P + p) * N + part * 32;
-  const float cprev = (1.f - sg) * dt * dec * sVp[p];
-  const float ccur = sg * dt * sX[p];
-  float acc = 0.f;
+  for (int hh = 0; hh < nhg; ++hh) {
+    if (hh + 1 < nhg) {
+      const float4* src = reinterpret_cast<const float4*>(state_row(hh + 1));
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    float4 hv = reinterpret_cast<float4*>(hrow)[q];
-    int n = part * 32 + q * 4;
-    hv.x = dec * hv.x + cprev * sKp[n] + ccur * sK[n];
-    hv.y = dec * hv.y + cprev * sKp[n + 1] + ccur * sK[n + 1];
-    hv.z = dec * hv.z + cprev * sKp[n + 2] + ccur * sK[n + 2];
-    hv.w = dec * hv.w + cprev * sKp[n + 3] + ccur * sK[n + 3];
-    reinterpret_cast<float4*>(hrow)[q] = hv;
-    acc += sQ[n] * hv.x + sQ[n + 1] * hv.y + sQ[n + 2] * hv.z + sQ[n + 3] * hv.w;
+      for (int q = 0; q < 8; ++q) nxt[q] = src[q];
+    }
+    const float dt = sDt[hh], dec = sDec[hh], sg = sSg[hh];
+    const float cprev = (1.f - sg) * dt * dec * sVp[hh][p];
+    const float ccur = sg * dt * sX[hh][p];
+    const float* K = sK[hh];
+    const float* Kp = sKp[hh];
+    const float* Q = sQ[hh];
+    float4* dst = reinterpret_cast<float4*>(state_row(hh));
+    float acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 hv = cur[q];
+      const int n = part * 32 + q * 4;
+      hv.x = dec * hv.x + cprev * Kp[n] + ccur * K[n];
+      hv.y = dec * hv.y + cprev * Kp[n + 1] + ccur * K[n + 1];
+      hv.z = dec * hv.z + cprev * Kp[n + 2] + ccur * K[n + 2];
+      hv.w = dec * hv.w + cprev * Kp[n + 3] + ccur * K[n + 3];
+      dst[q] = hv;
+      acc += Q[n] * hv.x + Q[n + 1] * hv.y + Q[n + 2] * hv.z + Q[n + 3] * hv.w;
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (part == 0) {
+      const int h = h0 + hh;
+      const float z = sZ[hh][p];
+      const float yv = (acc + a.D[h] * sX[hh][p]) * z * sigmoidf_(z);
+      a.y[(size_t)b * a.d_inner + h * P + p] = __float2bfloat16(yv);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) cur[q] = nxt[q];
   }
-  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-  if (part == 0) {
-    float z = sZ[p];
-    float yv = (acc + a.D[h] * sX[p]) * z * sigmoidf_(z);
-    a.y[(size_t)b * a.d_inner + h * P + p] = __float2bfloat16(yv);
+  // the carries for the next token
+  for (int i = tid; i < HG * R; i += NT) {
+    const int hh = i / R, r = i % R;
+    if (hh < nhg) a.ang[((size_t)b * a.nh + h0 + hh) * R + r] = sTh[hh][r];
   }
-  __syncthreads();
-  if (tid < N) a.kprev[bh * N + tid] = sK[tid];
-  if (tid < P) a.vprev[bh * P + tid] = sX[tid];
+  for (int i = tid; i < HG * N; i += NT) {
+    const int hh = i / N, n = i % N;
+    if (hh < nhg) a.kprev[((size_t)b * a.nh + h0 + hh) * N + n] = sK[hh][n];
+  }
+  for (int i = tid; i < HG * P; i += NT) {
+    const int hh = i / P, pp = i % P;
+    if (hh < nhg) a.vprev[((size_t)b * a.nh + h0 + hh) * P + pp] = sX[hh][pp];
+  }
 }
 
 }  // namespace dec
@@ -134,5 +190,5 @@ void m3_decode_step_launch(const void* proj, int B, int ldp, int nh, const float
   a.A_floor = A_floor; a.eps = eps;
   a.ang = ang; a.ssm = ssm; a.kprev = kprev; a.vprev = vprev;
   a.y = reinterpret_cast<__nv_bfloat16*>(y);
-  s0::dec::m3_decode_step<<<dim3(nh, B), s0::dec::NT, 0, st>>>(a);
+  s0::dec::m3_decode_step<<<dim3((nh + s0::dec::HG - 1) / s0::dec::HG, B), s0::dec::NT, 0, st>>>(a);
 }

@@ -2,6 +2,7 @@
 // include no torch headers (fast, parallel compiles); tensor handling lives in
 // bindings.cpp.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -99,3 +100,23 @@ void gen_sample_launch(const float* logits, int ldl, const float* bias, const un
                        int out_stride, cudaStream_t st);
 void gen_time_tokens_launch(int64_t* msg, int msg_len, int dt_pos, int time_off, int* time, int n,
                             cudaStream_t st);
+
+// fused data-parallel gradient sync + AdamW over peer memory (dp_fused.cu)
+#define DPF_MAXW 8
+struct DpfArgs {
+  float* G[DPF_MAXW];          // every rank's flat gradient (peer-mapped)
+  float* P[DPF_MAXW];          // every rank's flat fp32 parameters
+  __nv_bfloat16* S[DPF_MAXW];  // every rank's bf16 shadow (or null)
+  int* flags[DPF_MAXW];        // every rank's flag words [3][DPF_MAXW]
+  float* sums[DPF_MAXW];       // every rank's sum-of-squares slots [DPF_MAXW]
+  float* m;                    // this rank's Adam moments for [lo, hi)
+  float* v;
+  float* sumsq_local;          // zeroed before the launch
+  int* abort;                  // zeroed before the launch
+  int* status;                 // 0 = ok, 100 + phase = a peer did not arrive
+  long lo, hi, n_ssm;
+  int world, rank, seq;
+  long long spin_limit;
+  float lr_s, lr_r, wd, b1, b2, eps, bc1, bc2, max_norm, inv_world;
+};
+int dp_fused_adam_launch(const DpfArgs& a, int sms, cudaStream_t st);

@@ -45,7 +45,7 @@ class FlatAdam:
     def __init__(self, model: nn.Module, lr: float, ssm_lr: float, weight_decay: float = 0.05,
                  max_grad_norm: float = 1.0, betas=(0.9, 0.999), eps: float = 1e-8,
                  opt_config: str = "standard", attention_model: bool = False,
-                 bf16_shadow: bool = True, pad_multiple: int = 128):
+                 bf16_shadow: bool = True, pad_multiple: int = 128, alloc=None):
         self.model = model
         self.b1, self.b2 = betas
         self.eps = eps
@@ -67,11 +67,12 @@ class FlatAdam:
         self.n_ssm = sum(rnd(p.numel()) for _, p in groups["ssm"])
         self.numel = total
         self.device = dev
-        self.flat = torch.zeros(total, dtype=torch.float32, device=dev)
-        self.grad = torch.zeros(total, dtype=torch.float32, device=dev)
+        mk = alloc or (lambda n, dt, d: torch.zeros(n, dtype=dt, device=d))
+        self.flat = mk(total, torch.float32, dev)
+        self.grad = mk(total, torch.float32, dev)
         self.m = torch.zeros(total, dtype=torch.float32, device=dev)
         self.v = torch.zeros(total, dtype=torch.float32, device=dev)
-        self.shadow = torch.empty(total, dtype=torch.bfloat16, device=dev) if (bf16_shadow and dev.type == "cuda") else None
+        self.shadow = mk(total, torch.bfloat16, dev) if (bf16_shadow and dev.type == "cuda") else None
         self.names: List[str] = []
         self.slices: Dict[str, Tuple[int, int]] = {}
         off = 0

@@ -31,7 +31,7 @@ from .optim import FlatAdam, cosine_schedule
 class Trainer:
     def __init__(self, args, device: Optional[torch.device] = None, world: int = 1, rank: int = 0,
                  group=None, total_steps: int = 1000, seed: int = 0, sharded: bool = False,
-                 accum_steps: int = 1, grad_wire_dtype: str = "float32"):
+                 accum_steps: int = 1, grad_wire_dtype: str = "float32", dp_impl: str = "nccl"):
         self.args = args
         self.device = device or torch.device("cuda" if torch.cuda.is_available() else "cpu")
         self.world, self.rank, self.group = world, rank, group
@@ -52,23 +52,36 @@ class Trainer:
                             max_grad_norm=float(getattr(args, "max_grad_norm", 1.0)),
                             opt_config=str(getattr(args, "opt_config", "standard")),
                             attention_model=attn_only,
-                            pad_multiple=128 * (world if (sharded and world > 1) else 1))
+                            pad_multiple=128 * (world if ((sharded or dp_impl == "fused") and world > 1) else 1),
+                            alloc=self._alloc(dp_impl, world))
         self.total_steps = total_steps
         self.warmup_steps = int(round(float(getattr(args, "warmup_end", 0.01)) * total_steps))
         lr_min = float(getattr(args, "lr_min", 0.0) or 0.0)
         self.lr_min_frac = (lr_min / lr) if lr_min > 0 else 0.05
         self.ignore_times = bool(getattr(args, "ignore_times", False))
-        self.sharded = sharded and world > 1
+        if dp_impl not in ("nccl", "fused"):
+            raise ValueError(f"dp_impl must be 'nccl' or 'fused', not {dp_impl!r}")
+        self.fused = None
+        self.sharded = (sharded or dp_impl == "fused") and world > 1
         if self.sharded:
             self.opt.shard(world, rank)
             self._gshard = torch.empty(self.opt.hi - self.opt.lo, dtype=torch.float32, device=self.device)
         if grad_wire_dtype not in ("float32", "bfloat16"):
             raise ValueError(f"grad_wire_dtype must be float32 or bfloat16, not {grad_wire_dtype!r}")
         self.wire_bf16 = grad_wire_dtype == "bfloat16"
+        if dp_impl == "fused" and world > 1:
+            from ..parallel.fused_dp import FusedDPSync
+            self.fused = FusedDPSync(self.opt, group)
         self.accum_steps = max(1, int(accum_steps))
         self.global_batch = int(getattr(args, "micro_bsz", 1)) * world
         self.step_idx = 0
         self._sumsq_all = torch.zeros(1, device=self.device)
+
+    def _alloc(self, dp_impl, world):
+        if dp_impl == "fused" and world > 1 and self.device.type == "cuda":
+            from ..parallel.fused_dp import symmetric_alloc
+            return symmetric_alloc()
+        return None
 
     # -- one step -------------------------------------------------------------------------
     def _update(self, lr_scale: float):
@@ -96,6 +109,9 @@ class Trainer:
                 g.div_(self.world)
                 dist.all_reduce(g, group=self.group)
             opt.step(lr_scale=lr_scale)
+            return
+        if self.fused is not None:
+            self.fused.step(lr_scale)
             return
         gs = self._gshard
         if self.wire_bf16:

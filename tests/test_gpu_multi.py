@@ -1,0 +1,108 @@
+"""Multi-GPU data parallelism (needs >= 2 GPUs): the fused peer-memory
+reduce-scatter + AdamW + all-gather kernel against the NCCL sharded path, and
+its bounded cross-rank wait when a peer never arrives."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+need2 = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _args():
+    from sigma0_b200.models import preset_args
+    return preset_args("350m", n_layers=2, n_messages=8, micro_bsz=1, impl="cuda", warmup_end=0.0)
+
+
+def _batch(rank):
+    from sigma0_b200.data import make_sequences, LobWindowDataset, collate
+    ds = LobWindowDataset.from_days(make_sequences(1, 9, seed=10 + rank), 8, token_mode="22tok")
+    return tuple(t.cuda() for t in collate([ds[0]]))
+
+
+def _worker(rank, world, port, out, mode):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from sigma0_b200.train.trainer import Trainer
+        batch = _batch(rank)
+        if mode == "compare":
+            # identical gradients through both paths: the update is then deterministic
+            res = {}
+            for impl in ("nccl", "fused"):
+                tr = Trainer(_args(), device=torch.device("cuda", rank), world=world, rank=rank, total_steps=10,
+                             seed=0, sharded=True, dp_impl=impl)
+                g = torch.Generator(device="cuda").manual_seed(100 + rank)
+                for _ in range(3):
+                    tr.opt.grad.copy_(torch.randn(tr.opt.numel, device="cuda", generator=g) * 1e-2)
+                    tr._update(1.0)
+                torch.cuda.synchronize()
+                res[impl] = tr.opt.flat.detach().cpu().clone()
+                if impl == "fused":
+                    tr.fused.check()
+                    res["shadow_matches"] = bool(torch.equal(tr.opt.shadow, tr.opt.flat.to(torch.bfloat16)))
+                    tr.step_device(*batch)          # and a real training step through the fused path
+                    torch.cuda.synchronize()
+                    tr.fused.check()
+                    res["trained_finite"] = bool(torch.isfinite(tr.opt.flat).all())
+                    # every rank holds identical parameters after the fused all-gather
+                    chk = tr.opt.flat.double().sum().reshape(1)
+                    allc = [torch.zeros_like(chk) for _ in range(world)]
+                    dist.all_gather(allc, chk)
+                    res["ranks_agree"] = all(torch.equal(allc[0], c) for c in allc)
+                del tr
+                torch.cuda.empty_cache()
+            if rank == 0:
+                torch.save(res, out)
+        else:   # "timeout": rank 1 never joins the fused step; rank 0 must come back with an error status
+            from sigma0_b200.parallel.fused_dp import FusedDPSync
+            tr = Trainer(_args(), device=torch.device("cuda", rank), world=world, rank=rank, total_steps=10,
+                         seed=0, dp_impl="fused")
+            tr.fused.SPIN_LIMIT = 2_000_000
+            if rank == 0:
+                tr.opt.zero_grad()
+                tr._update(1.0)
+                torch.cuda.synchronize()
+                try:
+                    tr.fused.check()
+                    torch.save({"raised": False}, out)
+                except RuntimeError as e:
+                    torch.save({"raised": True, "msg": str(e)}, out)
+            dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@need2
+def test_fused_dp_matches_nccl_sharded(tmp_path):
+    out = str(tmp_path / "res.pt")
+    mp.spawn(_worker, args=(2, _port(), out, "compare"), nprocs=2, join=True)
+    res = torch.load(out)
+    a, b = res["nccl"], res["fused"]
+    assert torch.isfinite(b).all()
+    assert (a - b).abs().max().item() < 1e-6, (a - b).abs().max().item()
+    assert res["shadow_matches"] and res["trained_finite"] and res["ranks_agree"]
+
+
+@need2
+def test_fused_dp_bounded_wait_reports_missing_peer(tmp_path):
+    out = str(tmp_path / "res.pt")
+    mp.spawn(_worker, args=(2, _port(), out, "timeout"), nprocs=2, join=True)
+    res = torch.load(out)
+    assert res["raised"] and "phase 0" in res["msg"]
