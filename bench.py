@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--books", type=int, default=512, help="gen: books per GPU")
     p.add_argument("--ctx_msgs", type=int, default=500, help="gen: conditioning messages per book")
     p.add_argument("--no_graphs", action="store_true")
+    p.add_argument("--dp_impl", choices=["fused", "nccl", "nccl_sharded"], default="fused",
+                   help="N>1 gradient sync: fused peer-memory RS+AdamW+AG kernel, or NCCL all-reduce / RS+AG")
     return p.parse_args()
 
 
@@ -271,7 +273,8 @@ def main():
     if a.n_messages:
         args.n_messages = a.n_messages
     Bm, nm = args.micro_bsz, args.n_messages
-    trainer = Trainer(args, device=dev, world=world, rank=rank, total_steps=10_000, seed=0)
+    trainer = Trainer(args, device=dev, world=world, rank=rank, total_steps=10_000, seed=0,
+                      sharded=a.dp_impl == "nccl_sharded", dp_impl="fused" if a.dp_impl == "fused" else "nccl")
 
     # synthetic data: Bm sequences per rank, replayed through the engine
     days = make_sequences(Bm, nm + 1, seed=1000 + rank)
@@ -336,6 +339,7 @@ def main():
             "config": {"model": f"mamba3-lob-{a.preset} ({n_params/1e6:.1f}M params, d_model {args.d_model}, "
                                 f"{args.n_message_layers}+{args.n_book_pre_layers}+{args.n_book_post_layers}+{args.n_layers} layers)",
                        "global_batch": Bm * world, "seq_len": L, "parallelism": f"dp{world}",
+                       "grad_sync": (a.dp_impl if world > 1 else "none"),
                        "l2": "working set (weights + ~90 GB activations per step) far above L2; no flush needed",
                        "vocab": args.vocab_size, "token_mode": args.token_mode},
             "loss": float(loss), "gpu_launches": launches, "clocks": clk, "e2e": e2e,

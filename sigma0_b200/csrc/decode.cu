@@ -38,11 +38,11 @@ constexpr int HG = 8;   // heads per block: the per-token prologue is shared, st
 // issued before the prologue so their latency overlaps it.  Prologue: BCNorm of the token's B/C
 // row (shared by all heads), per-head dt / decay / trapezoid gate, angle update
 // and RoPE of K = Bn + B_bias[h], Q = Cn + C_bias[h], all into shared memory
-// behind a single barrier.  Main loop: each thread owns 32 consecutive state
-// entries of one row p (4 threads per row, 8 float4); the next head's state is
-// loaded into registers before the current head's is stored, so every thread
-// keeps 16 float4 loads in flight.
-__global__ void __launch_bounds__(NT) m3_decode_step(DecArgs a) {
+// behind two barriers.  Main loop: each warp streams 8 rows of a head's state,
+// one coalesced 512-byte row per instruction; the next head's state is loaded
+// into registers before the current head's is stored, so every thread keeps
+// 16 float4 loads in flight.
+__global__ void __launch_bounds__(NT, 2) m3_decode_step(DecArgs a) {
   __shared__ float sBn[N], sCn[N];
   __shared__ float sK[HG][N], sQ[HG][N], sKp[HG][N];
   __shared__ float sX[HG][P], sVp[HG][P], sZ[HG][P];
@@ -53,16 +53,17 @@ __global__ void __launch_bounds__(NT) m3_decode_step(DecArgs a) {
   const bf16* row = a.proj + (size_t)b * a.ldp;
   const int off_B = 2 * a.d_inner, off_C = off_B + N, off_dt = off_C + N;
   const int off_A = off_dt + a.nh, off_tr = off_A + a.nh, off_ang = off_tr + a.nh;
-  // the first head's state is independent of the prologue: start streaming it now
-  const int p = tid >> 2, part = tid & 3;
+  // the first head's state is independent of the prologue: start streaming it now.
+  // Warp w owns rows 8w..8w+7 of the P x N state; lane l owns columns 4l..4l+3,
+  // so each load/store instruction of a warp covers one contiguous 512-byte row.
   float4 cur[8], nxt[8];
-  auto state_row = [&](int hh) {
-    return a.ssm + (((size_t)b * a.nh + h0 + hh) * P + p) * N + part * 32;
+  auto head_state = [&](int hh) {
+    return reinterpret_cast<float4*>(a.ssm + (((size_t)b * a.nh + h0 + hh) * P + warp * 8) * N) + lane;
   };
   {
-    const float4* src = reinterpret_cast<const float4*>(state_row(0));
+    const float4* src = head_state(0);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) cur[q] = src[q];
+    for (int r = 0; r < 8; ++r) cur[r] = src[r * (N / 4)];
   }
   // BCNorm sums (warps 0-3: B, 4-7: C)
   float bc = __bfloat162float(row[(tid < N) ? off_B + tid : off_C + tid - N]);
@@ -125,39 +126,59 @@ __global__ void __launch_bounds__(NT) m3_decode_step(DecArgs a) {
   __syncthreads();
   for (int hh = 0; hh < nhg; ++hh) {
     if (hh + 1 < nhg) {
-      const float4* src = reinterpret_cast<const float4*>(state_row(hh + 1));
+      const float4* src = head_state(hh + 1);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) nxt[q] = src[q];
+      for (int r = 0; r < 8; ++r) nxt[r] = src[r * (N / 4)];
     }
     const float dt = sDt[hh], dec = sDec[hh], sg = sSg[hh];
-    const float cprev = (1.f - sg) * dt * dec * sVp[hh][p];
-    const float ccur = sg * dt * sX[hh][p];
-    const float* K = sK[hh];
-    const float* Kp = sKp[hh];
-    const float* Q = sQ[hh];
-    float4* dst = reinterpret_cast<float4*>(state_row(hh));
-    float acc = 0.f;
+    const float4 K = reinterpret_cast<const float4*>(sK[hh])[lane];
+    const float4 Kp = reinterpret_cast<const float4*>(sKp[hh])[lane];
+    const float4 Q = reinterpret_cast<const float4*>(sQ[hh])[lane];
+    float4* dst = head_state(hh);
+    float part[8];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      float4 hv = cur[q];
-      const int n = part * 32 + q * 4;
-      hv.x = dec * hv.x + cprev * Kp[n] + ccur * K[n];
-      hv.y = dec * hv.y + cprev * Kp[n + 1] + ccur * K[n + 1];
-      hv.z = dec * hv.z + cprev * Kp[n + 2] + ccur * K[n + 2];
-      hv.w = dec * hv.w + cprev * Kp[n + 3] + ccur * K[n + 3];
-      dst[q] = hv;
-      acc += Q[n] * hv.x + Q[n + 1] * hv.y + Q[n + 2] * hv.z + Q[n + 3] * hv.w;
+    for (int r = 0; r < 8; ++r) {
+      const int p = warp * 8 + r;
+      const float cprev = (1.f - sg) * dt * dec * sVp[hh][p];
+      const float ccur = sg * dt * sX[hh][p];
+      float4 hv = cur[r];
+      hv.x = dec * hv.x + cprev * Kp.x + ccur * K.x;
+      hv.y = dec * hv.y + cprev * Kp.y + ccur * K.y;
+      hv.z = dec * hv.z + cprev * Kp.z + ccur * K.z;
+      hv.w = dec * hv.w + cprev * Kp.w + ccur * K.w;
+      dst[r * (N / 4)] = hv;
+      part[r] = Q.x * hv.x + Q.y * hv.y + Q.z * hv.z + Q.w * hv.w;
     }
-    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    // transposed butterfly: 8 row sums over 32 lanes in 9 shuffles; lane l ends
+    // with the full sum of row 4*b4 + 2*b3 + b2 (b_i = bit i of l)
+    float q4[4], q2[2];
+    const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = u16 ? part[i] : part[i + 4], keep = u16 ? part[i + 4] : part[i];
+      q4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = u8 ? q4[i] : q4[i + 2], keep = u8 ? q4[i + 2] : q4[i];
+      q2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float acc;
+    {
+      const float send = u4 ? q2[0] : q2[1], keep = u4 ? q2[1] : q2[0];
+      acc = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-    if (part == 0) {
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    if ((lane & 3) == 0) {
+      const int p = warp * 8 + (u16 ? 4 : 0) + (u8 ? 2 : 0) + (u4 ? 1 : 0);
       const int h = h0 + hh;
       const float z = sZ[hh][p];
       const float yv = (acc + a.D[h] * sX[hh][p]) * z * sigmoidf_(z);
       a.y[(size_t)b * a.d_inner + h * P + p] = __float2bfloat16(yv);
     }
 #pragma unroll
-    for (int q = 0; q < 8; ++q) cur[q] = nxt[q];
+    for (int r = 0; r < 8; ++r) cur[r] = nxt[r];
   }
   // the carries for the next token
   for (int i = tid; i < HG * R; i += NT) {
