@@ -43,8 +43,9 @@ def parse():
     p.add_argument("--micro_bsz", type=int, default=None)
     p.add_argument("--n_messages", type=int, default=None)
     p.add_argument("--no_e2e", action="store_true")
-    p.add_argument("--mode", choices=["train", "gen"], default="train",
-                   help="train: the headline training step; gen: engine-in-the-loop generation")
+    p.add_argument("--mode", choices=["train", "gen", "decode"], default="train",
+                   help="train: the headline training step; gen: engine-in-the-loop generation; "
+                        "decode: the Mamba3 recurrent decode kernel alone")
     p.add_argument("--books", type=int, default=512, help="gen: books per GPU")
     p.add_argument("--ctx_msgs", type=int, default=500, help="gen: conditioning messages per book")
     p.add_argument("--no_graphs", action="store_true")
@@ -243,12 +244,49 @@ def gen_main(a):
     return 0
 
 
+def decode_main(a):
+    """Kernel microbenchmark: one Mamba3 layer's recurrent decode step (d_model 1024,
+    32 heads x 64 x 128 fp32 state) for ``--books`` books; bandwidth-bound by design."""
+    import torch
+    from sigma0_b200.models.mamba3 import Mamba3
+    from sigma0_b200.ops._ext import ext
+    torch.manual_seed(0)
+    B = a.books
+    m = Mamba3(1024, impl="cuda").cuda()
+    st = m.initial_state(B, "cuda")
+    d = m.dims
+    proj = m._proj_cuda(torch.randn(B, 1024, device="cuda"))
+    y = torch.empty(B, d.d_inner, dtype=torch.bfloat16, device="cuda")
+
+    def call():
+        ext().m3_decode_step(proj, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D,
+                             m.A_floor, 1e-6, *st, y)
+    for _ in range(a.warmup):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / a.steps * 1000
+    nbytes = st[1].numel() * 4 * 2
+    print(json.dumps({"metric": "Mamba3 decode step (one layer)", "value": us, "unit": "us", "books": B,
+                      "state_bytes_rw": nbytes, "achieved_GBps": nbytes / us / 1e3, "steps": a.steps,
+                      "warmup": a.warmup, "higher_is_better": False,
+                      "l2": "state larger than L2 for books >= 128; no flush needed"}))
+    return 0
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         return reference_arm(a)
     if a.mode == "gen":
         return gen_main(a)
+    if a.mode == "decode":
+        return decode_main(a)
     import torch
     import torch.distributed as dist
     from sigma0_b200.models import preset_args
