@@ -171,16 +171,18 @@ std::vector<at::Tensor> ln_bwd(at::Tensor dy, at::Tensor x, at::Tensor mean, at:
   req(x, at::kFloat, "x");
   c10::cuda::CUDAGuard guard(x.device());
   int64_t D = x.size(-1), T = x.numel() / D;
+  TORCH_CHECK(D % 4 == 0 && D <= 2048, "LayerNorm width must be a multiple of 4, at most 2048");
   auto dx = at::empty_like(x);
-  auto dw = at::zeros({D}, x.options()), db = at::zeros({D}, x.options());
+  auto dw = at::empty({D}, x.options()), db = at::empty({D}, x.options());
+  auto part = at::empty({(int64_t)col_blocks(T, num_sms(x)), 2, D}, x.options());
   const float* r = nullptr;
   if (dres.has_value() && dres->defined()) {
     req(*dres, at::kFloat, "dres");
     r = dres->data_ptr<float>();
   }
   ln_bwd_launch(dy.data_ptr(), x.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
-                w.data_ptr<float>(), r, dx.data_ptr<float>(), dw.data_ptr<float>(), db.data_ptr<float>(), T, (int)D,
-                num_sms(x), stream());
+                w.data_ptr<float>(), r, dx.data_ptr<float>(), dw.data_ptr<float>(), db.data_ptr<float>(),
+                part.data_ptr<float>(), T, (int)D, num_sms(x), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {dx, dw, db};
 }
@@ -203,10 +205,12 @@ std::vector<at::Tensor> rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::T
   req(x, at::kBFloat16, "x");
   c10::cuda::CUDAGuard guard(x.device());
   int64_t D = x.size(-1), T = x.numel() / D;
+  TORCH_CHECK(D % 8 == 0 && D <= 2048, "RMSNorm width must be a multiple of 8, at most 2048");
   auto dx = at::empty_like(x);
-  auto dw = at::zeros({D}, x.options().dtype(at::kFloat));
+  auto dw = at::empty({D}, x.options().dtype(at::kFloat));
+  auto part = at::empty({(int64_t)col_blocks(T, num_sms(x)), D}, x.options().dtype(at::kFloat));
   rms_bwd_launch(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
-                 dw.data_ptr<float>(), T, (int)D, num_sms(x), stream());
+                 dw.data_ptr<float>(), part.data_ptr<float>(), T, (int)D, num_sms(x), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {dx, dw};
 }
@@ -240,10 +244,13 @@ std::vector<at::Tensor> glu_res_bwd(at::Tensor dout, at::Tensor g, at::Tensor h,
   int64_t D = dout.size(-1), T = dout.numel() / D;
   c10::cuda::CUDAGuard guard(dout.device());
   auto dh = at::empty(dout.sizes(), dout.options().dtype(at::kBFloat16));
+  TORCH_CHECK(D % 4 == 0 && D <= 2048, "GLU width must be a multiple of 4, at most 2048");
   auto dgp = at::empty_like(dout);
-  auto db = at::zeros({D}, dout.options());
+  auto db = at::empty({D}, dout.options());
+  auto part = at::empty({(int64_t)col_blocks(T, num_sms(dout)), D}, dout.options());
   glu_res_bwd_launch(dout.data_ptr<float>(), g.data_ptr(), h.data_ptr(), b.data_ptr<float>(), dh.data_ptr(),
-                     dgp.data_ptr<float>(), db.data_ptr<float>(), T, (int)D, num_sms(dout), stream());
+                     dgp.data_ptr<float>(), db.data_ptr<float>(), part.data_ptr<float>(), T, (int)D, num_sms(dout),
+                     stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {dh, dgp, db};
 }

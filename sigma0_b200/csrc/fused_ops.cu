@@ -98,55 +98,94 @@ __global__ void ln_fwd_k(const float* __restrict__ x, const float* __restrict__ 
   }
 }
 
-// LayerNorm backward fused with the residual: dx = dres + LN'(dy); dw, db accumulated
-// in shared memory per block (one global atomic per column per block).
-template <int VPL>
-__global__ void __launch_bounds__(256)
+// Column reductions (dgamma, dbeta, dbias) without atomics: every warp
+// accumulates its rows' contributions in its own shared-memory row (no
+// conflicts: a column belongs to one lane), the block sums its warps into one
+// partial row of `part`, and col_sum_k adds the blocks' partial rows in a fixed
+// order (deterministic).  Row data moves as float4 / 4 x bf16.
+constexpr int CB_NT = 256;
+
+__device__ __forceinline__ float4 ld_bf16x4(const bf16* p) {
+  uint2 u = *reinterpret_cast<const uint2*>(p);
+  float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void st_bf16x4(bf16* p, float4 v) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+}
+__device__ __forceinline__ void add4(float* p, float4 v) {
+  float4 o = *reinterpret_cast<float4*>(p);
+  o.x += v.x; o.y += v.y; o.z += v.z; o.w += v.w;
+  *reinterpret_cast<float4*>(p) = o;
+}
+
+// LayerNorm backward fused with the residual: dx = dres + LN'(dy); per-block
+// partial rows of dw and db go to part[block][2][D].  J float4 chunks per lane.
+template <int J>
+__global__ void __launch_bounds__(CB_NT)
     ln_bwd_k(const bf16* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
              const float* __restrict__ rstd, const float* __restrict__ w, const float* __restrict__ dres,
-             float* __restrict__ dx, float* __restrict__ dw, float* __restrict__ db, int T, int D) {
-  extern __shared__ float red_smem[];   // [2][D]
-  float* sw = red_smem;
-  float* sb = red_smem + D;
-  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) red_smem[i] = 0.f;
-  __syncthreads();
-  int lane = threadIdx.x & 31;
-  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int nw = (gridDim.x * blockDim.x) >> 5;
+             float* __restrict__ dx, float* __restrict__ part, int T, int D) {
+  extern __shared__ __align__(16) float red_smem[];   // [8][2][D]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float* sw = red_smem + (size_t)wid * 2 * D;
+  float* sb = sw + D;
+  for (int c = lane * 4; c < 2 * D; c += 128) *reinterpret_cast<float4*>(sw + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncwarp();
+  const int gw = blockIdx.x * (CB_NT / 32) + wid, nw = gridDim.x * (CB_NT / 32);
   for (int row = gw; row < T; row += nw) {
-    const float* xr = x + (size_t)row * D;
-    const bf16* gr = dy + (size_t)row * D;
-    float mu = mean[row], r = rstd[row];
-    float xh[VPL], gw_[VPL];
+    const size_t o = (size_t)row * D;
+    const float mu = mean[row], r = rstd[row];
+    float4 xh[J], gw_[J];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      int c = lane + 32 * i;
-      float g = c < D ? __bfloat162float(gr[c]) : 0.f;
-      xh[i] = c < D ? (xr[c] - mu) * r : 0.f;
-      gw_[i] = c < D ? g * w[c] : 0.f;
-      s1 += gw_[i];
-      s2 += gw_[i] * xh[i];
+    for (int j = 0; j < J; ++j) {
+      const int c = 4 * (lane + 32 * j);
       if (c < D) {
-        atomicAdd(&sw[c], g * xh[i]);
-        atomicAdd(&sb[c], g);
+        const float4 xv = *reinterpret_cast<const float4*>(x + o + c);
+        const float4 g = ld_bf16x4(dy + o + c);
+        const float4 wv = *reinterpret_cast<const float4*>(w + c);
+        xh[j] = make_float4((xv.x - mu) * r, (xv.y - mu) * r, (xv.z - mu) * r, (xv.w - mu) * r);
+        gw_[j] = make_float4(g.x * wv.x, g.y * wv.y, g.z * wv.z, g.w * wv.w);
+        s1 += gw_[j].x + gw_[j].y + gw_[j].z + gw_[j].w;
+        s2 += gw_[j].x * xh[j].x + gw_[j].y * xh[j].y + gw_[j].z * xh[j].z + gw_[j].w * xh[j].w;
+        add4(sw + c, make_float4(g.x * xh[j].x, g.y * xh[j].y, g.z * xh[j].z, g.w * xh[j].w));
+        add4(sb + c, g);
       }
     }
     s1 = warp_sum(s1) / D;
     s2 = warp_sum(s2) / D;
-    float* dxr = dx + (size_t)row * D;
-    const float* rr = dres ? dres + (size_t)row * D : nullptr;
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      int c = lane + 32 * i;
-      if (c < D) dxr[c] = (rr ? rr[c] : 0.f) + r * (gw_[i] - s1 - xh[i] * s2);
+    for (int j = 0; j < J; ++j) {
+      const int c = 4 * (lane + 32 * j);
+      if (c < D) {
+        float4 rv = dres ? *reinterpret_cast<const float4*>(dres + o + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        rv.x += r * (gw_[j].x - s1 - xh[j].x * s2);
+        rv.y += r * (gw_[j].y - s1 - xh[j].y * s2);
+        rv.z += r * (gw_[j].z - s1 - xh[j].z * s2);
+        rv.w += r * (gw_[j].w - s1 - xh[j].w * s2);
+        *reinterpret_cast<float4*>(dx + o + c) = rv;
+      }
     }
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < D; c += blockDim.x) {
-    atomicAdd(&dw[c], sw[c]);
-    atomicAdd(&db[c], sb[c]);
+  float* dst = part + (size_t)blockIdx.x * 2 * D;
+  for (int c = threadIdx.x; c < 2 * D; c += CB_NT) {
+    float t = 0.f;
+    for (int k = 0; k < CB_NT / 32; ++k) t += red_smem[(size_t)k * 2 * D + c];
+    dst[c] = t;
   }
+}
+
+// out_s[c] = sum over blocks of part[block][s][c], s < sets (fixed order)
+__global__ void col_sum_k(const float* __restrict__ part, int nblk, int sets, int D, float* __restrict__ out0,
+                          float* __restrict__ out1) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= sets * D) return;
+  const int s = i / D, c = i % D;
+  float t = 0.f;
+  for (int b = 0; b < nblk; ++b) t += part[((size_t)b * sets + s) * D + c];
+  (s == 0 ? out0 : out1)[c] = t;
 }
 
 // ---------------------------------------------------------------------------
@@ -254,7 +293,7 @@ __global__ void rms_bwd_k(const bf16* __restrict__ dy, const bf16* __restrict__ 
   for (int col = threadIdx.x; col < D; col += blockDim.x) {
     float t = 0.f;
     for (int k = 0; k < nwb; ++k) t += red_smem[k * D + col];
-    atomicAdd(&dw[col], t);
+    dw[(size_t)blockIdx.x * D + col] = t;   // this block's partial row (dw is the partial buffer)
   }
 }
 
@@ -295,36 +334,44 @@ __global__ void glu_res_fwd_k(const float* __restrict__ x, const bf16* __restric
   }
 }
 
-// dh = dout * g * s(1-s) (bf16), dgp = dout * s (fp32), db accumulated in shared memory.
-template <int VPL>
-__global__ void __launch_bounds__(256)
+// dh = dout * g * s(1-s) (bf16), dgp = dout * s (fp32); per-block partial rows of db.
+template <int J>
+__global__ void __launch_bounds__(CB_NT)
     glu_res_bwd_k(const float* __restrict__ dout, const bf16* __restrict__ g, const bf16* __restrict__ h,
                   const float* __restrict__ b, bf16* __restrict__ dh, float* __restrict__ dgp,
-                  float* __restrict__ db, int T, int D) {
-  extern __shared__ float red_smem[];   // [D]
-  for (int i = threadIdx.x; i < D; i += blockDim.x) red_smem[i] = 0.f;
-  __syncthreads();
-  int lane = threadIdx.x & 31;
-  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int nw = (gridDim.x * blockDim.x) >> 5;
+                  float* __restrict__ part, int T, int D) {
+  extern __shared__ __align__(16) float red_smem[];   // [8][D]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float* sb = red_smem + (size_t)wid * D;
+  for (int c = lane * 4; c < D; c += 128) *reinterpret_cast<float4*>(sb + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncwarp();
+  const int gw = blockIdx.x * (CB_NT / 32) + wid, nw = gridDim.x * (CB_NT / 32);
   for (int row = gw; row < T; row += nw) {
-    size_t o = (size_t)row * D;
+    const size_t o = (size_t)row * D;
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      int c = lane + 32 * i;
+    for (int j = 0; j < J; ++j) {
+      const int c = 4 * (lane + 32 * j);
       if (c < D) {
-        float gg = __bfloat162float(g[o + c]);
-        float s = sigmoidf_(__bfloat162float(h[o + c]) + b[c]);
-        float d = dout[o + c];
-        float v = d * gg * s * (1.f - s);
-        dh[o + c] = __float2bfloat16(v);
-        dgp[o + c] = d * s;
-        atomicAdd(&red_smem[c], v);
+        const float4 gg = ld_bf16x4(g + o + c), hh = ld_bf16x4(h + o + c);
+        const float4 bb = *reinterpret_cast<const float4*>(b + c);
+        const float4 d = *reinterpret_cast<const float4*>(dout + o + c);
+        const float sx = sigmoidf_(hh.x + bb.x), sy = sigmoidf_(hh.y + bb.y);
+        const float sz = sigmoidf_(hh.z + bb.z), sw = sigmoidf_(hh.w + bb.w);
+        const float4 v = make_float4(d.x * gg.x * sx * (1.f - sx), d.y * gg.y * sy * (1.f - sy),
+                                     d.z * gg.z * sz * (1.f - sz), d.w * gg.w * sw * (1.f - sw));
+        st_bf16x4(dh + o + c, v);
+        *reinterpret_cast<float4*>(dgp + o + c) = make_float4(d.x * sx, d.y * sy, d.z * sz, d.w * sw);
+        add4(sb + c, v);
       }
     }
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&db[c], red_smem[c]);
+  float* dst = part + (size_t)blockIdx.x * D;
+  for (int c = threadIdx.x; c < D; c += CB_NT) {
+    float t = 0.f;
+    for (int k = 0; k < CB_NT / 32; ++k) t += red_smem[(size_t)k * D + c];
+    dst[c] = t;
+  }
 }
 
 // do = (dgp + dgm) * gelu'(o)  -> bf16
@@ -489,36 +536,48 @@ void ln_fwd_launch(const float* x, const float* w, const float* b, void* y, floa
   else if (D <= 1024) ln_fwd_k<32><<<gr, 256, 0, st>>>(x, w, b, yp, mean, rstd, (int)T, D, eps);
   else ln_fwd_k<64><<<gr, 256, 0, st>>>(x, w, b, yp, mean, rstd, (int)T, D, eps);
 }
+int col_blocks(long T, int sms) {
+  long b = (T + 15) / 16;
+  long cap = 2L * sms;
+  return (int)(b < cap ? (b > 0 ? b : 1) : cap);
+}
+static void col_sum(const float* part, int nblk, int sets, int D, float* o0, float* o1, cudaStream_t st) {
+  int n = sets * D;
+  col_sum_k<<<(n + 255) / 256, 256, 0, st>>>(part, nblk, sets, D, o0, o1);
+}
 void ln_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,
-                   const float* dres, float* dx, float* dw, float* db, long T, int D, int sms, cudaStream_t st) {
-  int gr = red_grid(T, sms);
+                   const float* dres, float* dx, float* dw, float* db, float* part, long T, int D, int sms,
+                   cudaStream_t st) {
+  const int gr = col_blocks(T, sms);
   const bf16* g = reinterpret_cast<const bf16*>(dy);
-  if (D <= 256) ln_bwd_k<8><<<gr, 256, 2 * D * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
-  else if (D <= 512) ln_bwd_k<16><<<gr, 256, 2 * D * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
-  else if (D <= 1024) ln_bwd_k<32><<<gr, 256, 2 * D * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
-  else {
-    ln_bwd_k<64><<<gr, 256, 2 * D * 4, st>>>(g, x, mean, rstd, w, dres, dx, dw, db, (int)T, D);
-  }
+  const size_t sm = (size_t)(CB_NT / 32) * 2 * D * 4;
+  if (D <= 256) { allow_smem(ln_bwd_k<2>, sm); ln_bwd_k<2><<<gr, CB_NT, sm, st>>>(g, x, mean, rstd, w, dres, dx, part, (int)T, D); }
+  else if (D <= 512) { allow_smem(ln_bwd_k<4>, sm); ln_bwd_k<4><<<gr, CB_NT, sm, st>>>(g, x, mean, rstd, w, dres, dx, part, (int)T, D); }
+  else if (D <= 1024) { allow_smem(ln_bwd_k<8>, sm); ln_bwd_k<8><<<gr, CB_NT, sm, st>>>(g, x, mean, rstd, w, dres, dx, part, (int)T, D); }
+  else { allow_smem(ln_bwd_k<16>, sm); ln_bwd_k<16><<<gr, CB_NT, sm, st>>>(g, x, mean, rstd, w, dres, dx, part, (int)T, D); }
+  col_sum(part, gr, 2, D, dw, db, st);
 }
 void rms_fwd_launch(const void* x, const float* w, void* y, float* rstd, long T, int D, float eps, int sms,
                     cudaStream_t st) {
   rms_fwd_k<<<row_grid(T, sms), 256, 0, st>>>(reinterpret_cast<const bf16*>(x), w, reinterpret_cast<bf16*>(y),
                                              rstd, (int)T, D, eps);
 }
-void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw, long T,
-                    int D, int sms, cudaStream_t st) {
-  int gr = red_grid(T, sms);
+void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw,
+                    float* part, long T, int D, int sms, cudaStream_t st) {
+  const int gr = col_blocks(T, sms);
   const bf16* g = reinterpret_cast<const bf16*>(dy);
   const bf16* xp = reinterpret_cast<const bf16*>(x);
   bf16* o = reinterpret_cast<bf16*>(dx);
-  int nv = D / 8;
-  if (nv <= 32) rms_bwd_k<1><<<gr, 256, 8 * D * 4, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
-  else if (nv <= 64) rms_bwd_k<2><<<gr, 256, 8 * D * 4, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
-  else if (nv <= 128) rms_bwd_k<4><<<gr, 256, 8 * D * 4, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+  const int nv = D / 8;
+  const size_t sm = 8 * (size_t)D * 4;
+  if (nv <= 32) rms_bwd_k<1><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
+  else if (nv <= 64) rms_bwd_k<2><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
+  else if (nv <= 128) rms_bwd_k<4><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
   else {
-    allow_smem(rms_bwd_k<8>, 8 * (size_t)D * 4);
-    rms_bwd_k<8><<<gr, 256, 8 * D * 4, st>>>(g, xp, w, rstd, o, dw, (int)T, D);
+    allow_smem(rms_bwd_k<8>, sm);
+    rms_bwd_k<8><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
   }
+  col_sum(part, gr, 1, D, dw, nullptr, st);
 }
 void gelu_fwd_launch(const void* o, void* g, long n, int sms, cudaStream_t st) {
   gelu_fwd_k<<<ew_grid(n / 8, sms), 256, 0, st>>>(reinterpret_cast<const bf16*>(o), reinterpret_cast<bf16*>(g),
@@ -530,17 +589,17 @@ void glu_res_fwd_launch(const float* x, const void* g, const void* h, const floa
                                                     reinterpret_cast<const bf16*>(h), b, out, n / 8, D);
 }
 void glu_res_bwd_launch(const float* dout, const void* g, const void* h, const float* b, void* dh, float* dgp,
-                        float* db, long T, int D, int sms, cudaStream_t st) {
-  int gr = red_grid(T, sms);
+                        float* db, float* part, long T, int D, int sms, cudaStream_t st) {
+  const int gr = col_blocks(T, sms);
   const bf16* gp = reinterpret_cast<const bf16*>(g);
   const bf16* hp = reinterpret_cast<const bf16*>(h);
   bf16* dhp = reinterpret_cast<bf16*>(dh);
-  if (D <= 256) glu_res_bwd_k<8><<<gr, 256, D * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
-  else if (D <= 512) glu_res_bwd_k<16><<<gr, 256, D * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
-  else if (D <= 1024) glu_res_bwd_k<32><<<gr, 256, D * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
-  else {
-    glu_res_bwd_k<64><<<gr, 256, D * 4, st>>>(dout, gp, hp, b, dhp, dgp, db, (int)T, D);
-  }
+  const size_t sm = (size_t)(CB_NT / 32) * D * 4;
+  if (D <= 256) { allow_smem(glu_res_bwd_k<2>, sm); glu_res_bwd_k<2><<<gr, CB_NT, sm, st>>>(dout, gp, hp, b, dhp, dgp, part, (int)T, D); }
+  else if (D <= 512) { allow_smem(glu_res_bwd_k<4>, sm); glu_res_bwd_k<4><<<gr, CB_NT, sm, st>>>(dout, gp, hp, b, dhp, dgp, part, (int)T, D); }
+  else if (D <= 1024) { allow_smem(glu_res_bwd_k<8>, sm); glu_res_bwd_k<8><<<gr, CB_NT, sm, st>>>(dout, gp, hp, b, dhp, dgp, part, (int)T, D); }
+  else { allow_smem(glu_res_bwd_k<16>, sm); glu_res_bwd_k<16><<<gr, CB_NT, sm, st>>>(dout, gp, hp, b, dhp, dgp, part, (int)T, D); }
+  col_sum(part, gr, 1, D, db, nullptr, st);
 }
 void gelu_bwd_launch(const void* o, const float* dgp, const void* dgm, void* dout, long n, int sms,
                      cudaStream_t st) {

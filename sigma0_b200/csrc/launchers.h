@@ -47,17 +47,19 @@ void m3_prep_bwd_launch(const M3Geo& g, const void* proj, const float* wB, const
 // ---- fused row/elementwise ops, loss and optimizer (fused_ops.cu) -------------------
 void ln_fwd_launch(const float* x, const float* w, const float* b, void* y, float* mean, float* rstd, long T,
                    int D, float eps, int sms, cudaStream_t st);
+int col_blocks(long T, int sms);   // blocks (= partial rows) of the column-reduction kernels
 void ln_bwd_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,
-                   const float* dres, float* dx, float* dw, float* db, long T, int D, int sms, cudaStream_t st);
+                   const float* dres, float* dx, float* dw, float* db, float* part, long T, int D, int sms,
+                   cudaStream_t st);
 void rms_fwd_launch(const void* x, const float* w, void* y, float* rstd, long T, int D, float eps, int sms,
                     cudaStream_t st);
-void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw, long T,
-                    int D, int sms, cudaStream_t st);
+void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw,
+                    float* part, long T, int D, int sms, cudaStream_t st);
 void gelu_fwd_launch(const void* o, void* g, long n, int sms, cudaStream_t st);
 void glu_res_fwd_launch(const float* x, const void* g, const void* h, const float* b, float* out, long n, int D,
                         int sms, cudaStream_t st);
 void glu_res_bwd_launch(const float* dout, const void* g, const void* h, const float* b, void* dh, float* dgp,
-                        float* db, long T, int D, int sms, cudaStream_t st);
+                        float* db, float* part, long T, int D, int sms, cudaStream_t st);
 void gelu_bwd_launch(const void* o, const float* dgp, const void* dgm, void* dout, long n, int sms,
                      cudaStream_t st);
 void ce_launch(void* logits, const float* bias, const int64_t* labels, const float* wrow, float* loss, long T,

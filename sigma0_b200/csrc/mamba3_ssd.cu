@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(128) m3_pass(bf16* __restrict__ buf, const flo
   float run[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) run[k] = 0.f;
-  constexpr int U = 4;
+  constexpr int U = 16;   // chunks in flight per thread (256 bytes): the chain is latency-bound otherwise
   for (int k0 = 0; k0 < g.nc; k0 += U) {
     uint4 v[U];
     float d[U];
