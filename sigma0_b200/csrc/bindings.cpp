@@ -350,7 +350,8 @@ at::Tensor eng_l2(at::Tensor asks, at::Tensor bids, int64_t levels) {
 void gen_apply(at::Tensor asks, at::Tensor bids, at::Tensor trades, at::Tensor toks, std::vector<int64_t> lay,
                int64_t init_id, int64_t book_depth, int64_t cancel_mode, int64_t type4, bool check_fill,
                at::Tensor new_oid, at::Tensor p_mid, at::Tensor time_in, at::Tensor raw_out, at::Tensor msg_out,
-               at::Tensor prov_out, at::Tensor l2_out, at::Tensor img_out, bool apply) {
+               at::Tensor prov_out, at::Tensor l2_out, at::Tensor img_out, bool apply,
+               c10::optional<at::Tensor> inject) {
   req(asks, at::kInt, "asks");
   req(bids, at::kInt, "bids");
   req(trades, at::kInt, "trades");
@@ -373,13 +374,19 @@ void gen_apply(at::Tensor asks, at::Tensor bids, at::Tensor trades, at::Tensor t
   TORCH_CHECK(toks.size(1) == L.msg_len, "toks width");
   TORCH_CHECK(img_out.size(1) >= 3 + L.img_levels, "img_out width");
   TORCH_CHECK(l2_out.size(1) == 4 * L.l2_levels, "l2_out width");
+  const int* injp = nullptr;
+  if (inject.has_value() && inject->defined()) {
+    req(*inject, at::kInt, "inject");
+    TORCH_CHECK(inject->numel() == 5, "inject = [flag, event_type, side, qty, offset_ticks]");
+    injp = inject->data_ptr<int>();
+  }
   c10::cuda::CUDAGuard guard(asks.device());
   gen_apply_launch(asks.data_ptr<int>(), bids.data_ptr<int>(), trades.data_ptr<int>(), toks.data_ptr<int64_t>(), L,
                    (int)asks.size(1), (int)trades.size(1), (int)init_id, (int)book_depth, (int)cancel_mode,
                    (int)type4, check_fill ? 1 : 0, new_oid.data_ptr<int>(), p_mid.data_ptr<int>(),
                    time_in.data_ptr<int>(), raw_out.data_ptr<int>(), msg_out.data_ptr<int>(),
                    prov_out.data_ptr<int>(), l2_out.data_ptr<int>(), img_out.data_ptr<float>(),
-                   (int)img_out.stride(0), (int)asks.size(0), apply ? 1 : 0, stream());
+                   (int)img_out.stride(0), (int)asks.size(0), apply ? 1 : 0, injp, stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(32 * WPB)
               const int64_t* __restrict__ toks, GenLayout L, Cfg cfg, const int* __restrict__ new_oid,
               int* __restrict__ p_mid, const int* __restrict__ time_in, int* __restrict__ raw_out,
               int* __restrict__ msg_out, int* __restrict__ prov_out, int* __restrict__ l2_out,
-              float* __restrict__ img_out, int img_stride, int n_books, int apply) {
+              float* __restrict__ img_out, int img_stride, int n_books, int apply, const int* __restrict__ inj) {
   __shared__ int sA[WPB][MAXO * 6], sB[WPB][MAXO * 6], sT[WPB][MAXT * 8], sTmp[WPB][32];
   __shared__ int sL2[WPB][4 * 64];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -408,6 +408,15 @@ __global__ void __launch_bounds__(32 * WPB)
     int oid_ref = oid_l1 != NEG_RET ? oid_l1 : oid_l2;
     int oid = is_cd ? oid_ref : new_oid[0];
     int m[8] = {et, dir * 2 - 1, size, p_abs, oid, -88, ts, tns};
+    // do(Q): replace the generated order by [type, side, qty, mid + offset ticks]
+    const bool injected = inj != nullptr && inj[0] != 0;
+    if (injected) {
+      m[0] = inj[1];
+      m[1] = inj[2] * 2 - 1;
+      m[2] = inj[3];
+      m[3] = pm_old + inj[4] * L.tick;
+      m[4] = new_oid[0];
+    }
     if (lane == 0) {
       int* ro = raw_out + (size_t)book * 14;
       ro[0] = oid; ro[1] = et; ro[2] = dir; ro[3] = p_abs; ro[4] = price; ro[5] = size;
@@ -415,7 +424,7 @@ __global__ void __launch_bounds__(32 * WPB)
       for (int c = 0; c < 8; ++c) msg_out[(size_t)book * 8 + c] = m[c];
       int res = !is_cd ? 0 : (oid_l1 != NEG_RET ? 1 : (oid_l2 != NEG_RET ? 2 : 3));
       bool disagree = is_cd && pref != NA_V && price != NA_V && price != pref;
-      prov_out[book] = res + (disagree ? 8 : 0);
+      prov_out[book] = res + (disagree ? 8 : 0) + (injected ? 16 : 0);
     }
     __syncwarp();
     WarpBook wb{sA[w], sB[w], sT[w]};
@@ -491,10 +500,11 @@ void eng_l2_launch(const int* asks, const int* bids, int* out, int levels, int n
 void gen_apply_launch(int* asks, int* bids, int* trades, const int64_t* toks, const GenLayout& L, int n_orders,
                       int n_trades, int init_id, int book_depth, int cancel_mode, int type4, int check_fill,
                       const int* new_oid, int* p_mid, const int* time_in, int* raw_out, int* msg_out, int* prov_out,
-                      int* l2_out, float* img_out, int img_stride, int n_books, int apply, cudaStream_t st) {
+                      int* l2_out, float* img_out, int img_stride, int n_books, int apply, const int* inj,
+                      cudaStream_t st) {
   s0::eng::Cfg c{n_orders, n_trades, init_id, book_depth, cancel_mode, type4, check_fill};
   int blocks = (n_books + s0::eng::WPB - 1) / s0::eng::WPB;
   s0::eng::gen_apply<<<blocks, 32 * s0::eng::WPB, 0, st>>>(asks, bids, trades, toks, L, c, new_oid, p_mid, time_in,
                                                             raw_out, msg_out, prov_out, l2_out, img_out, img_stride,
-                                                            n_books, apply);
+                                                            n_books, apply, inj);
 }

@@ -94,7 +94,8 @@ struct GenLayout {
 void gen_apply_launch(int* asks, int* bids, int* trades, const int64_t* toks, const GenLayout& L, int n_orders,
                       int n_trades, int init_id, int book_depth, int cancel_mode, int type4, int check_fill,
                       const int* new_oid, int* p_mid, const int* time_in, int* raw_out, int* msg_out, int* prov_out,
-                      int* l2_out, float* img_out, int img_stride, int n_books, int apply, cudaStream_t st);
+                      int* l2_out, float* img_out, int img_stride, int n_books, int apply, const int* inj,
+                      cudaStream_t st);
 
 // generation (generate.cu)
 void gen_sample_launch(const float* logits, int ldl, const float* bias, const unsigned char* allow, int V, int B,

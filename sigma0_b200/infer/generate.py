@@ -83,7 +83,7 @@ def _best_quotes(ob: OrderBook):
 # ---------------------------------------------------------------------------
 
 def apply_message_cpu(ob: OrderBook, toks: np.ndarray, tok: MessageTokenizer, p_mid: int, new_oid: int,
-                      tick: int = 100, img_levels: int = 500, l2_levels: int = 10):
+                      tick: int = 100, img_levels: int = 500, l2_levels: int = 10, inject=None):
     """Decode one message's tokens, resolve the order id, apply it to ``ob``.
 
     Returns (raw row (14,), engine msg (8,), provenance, l2 (4*l2_levels,),
@@ -109,6 +109,12 @@ def apply_message_cpu(ob: OrderBook, toks: np.ndarray, tok: MessageTokenizer, p_
     raw[0], raw[3] = oid, p_abs
     res = 0 if not is_cd else (1 if oid_l1 != NEG_RET else (2 if oid_l2 != NEG_RET else 3))
     prov = res + (8 if is_cd and pref != NA_VAL and price != NA_VAL and price != pref else 0)
+    if inject is not None and inject[0]:
+        # do(Q): the engine gets our order instead of the generated one (the decoded
+        # generated message is still reported in ``raw``)
+        msg = np.array([inject[1], inject[2] * 2 - 1, inject[3], p_mid + inject[4] * tick, new_oid, -88, ts, tns],
+                       dtype=np.int64)
+        prov += 16
     ob.process(msg)
     ba, bb = _best_quotes(ob)
     pm_new = p_mid if (ba <= 0 or bb <= 0) else ((ba + bb) // 2 // tick) * tick
@@ -166,6 +172,7 @@ class GenOutput:
     l2: torch.Tensor          # (B, n, 4*levels) int32 book after each message
     provenance: torch.Tensor  # (B, n) int32 order-id resolution bits
     mid: torch.Tensor         # (B, n) int32 mid price after each message
+    engine_msgs: Optional[torch.Tensor] = None   # (B, n, 8) int32 messages the engine processed
 
 
 class Generator:
@@ -300,17 +307,19 @@ class Generator:
             c = self.cfg
             ext().gen_apply(self.asks, self.bids, self.trades, self.msg, self.layout, c.init_id, c.book_depth,
                             c.cancel_mode, c.type_4_interpretation, c.check_book_fill, self.new_oid, self.p_mid,
-                            self.time, self.o_raw, self.o_msg, self.o_prov, self.o_l2, self.book[:, 0], True)
+                            self.time, self.o_raw, self.o_msg, self.o_prov, self.o_l2, self.book[:, 0], True,
+                            self.inj_buf)
             self.ctr.add_(1)
             self.new_oid.sub_(1)
 
     def _engine_cpu(self, oid: int):
         msg = self.msg.cpu().numpy()
         pm = self.p_mid.cpu().numpy()
+        inj = self.inj_buf.cpu().numpy()
         imgs = []
         for b, ob in enumerate(self.books_cpu):
             raw, em, prov, l2, img, pm_new = apply_message_cpu(ob, msg[b], self.tok, int(pm[b]), oid, self.tick,
-                                                               self.img_levels, self.l2_levels)
+                                                               self.img_levels, self.l2_levels, inject=inj)
             self.o_raw[b] = torch.from_numpy(raw.astype(np.int32))
             self.o_msg[b] = torch.from_numpy(em.astype(np.int32))
             self.o_l2[b] = torch.from_numpy(l2.astype(np.int32))
@@ -321,10 +330,23 @@ class Generator:
         self.book[:, 0] = torch.from_numpy(np.stack(imgs)).to(self.book.dtype)
 
     @torch.no_grad()
-    def generate(self, n_msgs: int, events=None) -> GenOutput:
-        """Generate ``n_msgs`` messages for every book.  ``events``: optional list of
-        ``n_msgs + 1`` CUDA events recorded before each message and at the end."""
+    def generate(self, n_msgs: int, events=None, inject: Optional[dict] = None) -> GenOutput:
+        """Generate ``n_msgs`` messages for every book.
+
+        ``events``: optional list of ``n_msgs + 1`` CUDA events recorded before each
+        message and at the end.  ``inject``: do(Q) -- ``{"step": k, "event_type": 1|4,
+        "side": 0|1, "qty": Q, "offset_ticks": o}`` replaces the generated order at
+        step ``k`` (every book) by that order at ``mid + o`` ticks (the reference's
+        ``sample_new`` inject_* arguments, ``docs/inference.md``)."""
         B, L, dev = self.B, self.tok.MSG_LEN, self.dev
+        plan = torch.zeros(n_msgs, 5, dtype=torch.int32)
+        if inject is not None:
+            k = int(inject["step"])
+            if not 0 <= k < n_msgs:
+                raise ValueError(f"inject step {k} outside the {n_msgs}-message horizon")
+            plan[k] = torch.tensor([1, int(inject["event_type"]), int(inject["side"]), int(inject["qty"]),
+                                    int(inject.get("offset_ticks", 0))], dtype=torch.int32)
+        self.inj_buf = torch.zeros(5, dtype=torch.int32, device=dev)
         self.o_raw = torch.zeros(B, 14, dtype=torch.int32, device=dev)
         self.o_msg = torch.zeros(B, 8, dtype=torch.int32, device=dev)
         self.o_prov = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -334,10 +356,13 @@ class Generator:
         out_l2 = torch.zeros(B, n_msgs, 4 * self.l2_levels, dtype=torch.int32, device=dev)
         out_prov = torch.zeros(B, n_msgs, dtype=torch.int32, device=dev)
         out_mid = torch.zeros(B, n_msgs, dtype=torch.int32, device=dev)
+        out_em = torch.zeros(B, n_msgs, 8, dtype=torch.int32, device=dev)
         self.new_oid.fill_(n_msgs)
         self.graph = None
         graph = self.on_gpu and self.use_graphs and n_msgs > 1
         for k in range(n_msgs):
+            if inject is not None:
+                self.inj_buf.copy_(plan[k])
             if events is not None:
                 events[k].record()
             if self.on_gpu:
@@ -355,9 +380,10 @@ class Generator:
             out_l2[:, k] = self.o_l2
             out_prov[:, k] = self.o_prov
             out_mid[:, k] = self.p_mid
+            out_em[:, k] = self.o_msg
         if events is not None:
             events[n_msgs].record()
-        return GenOutput(out_tok, out_raw, out_l2, out_prov, out_mid)
+        return GenOutput(out_tok, out_raw, out_l2, out_prov, out_mid, out_em)
 
     def _capture(self):
         """Capture one message as a CUDA graph (the state buffers are updated in place)."""

@@ -73,3 +73,25 @@ def test_argmax_generation_is_deterministic():
         g.condition(*ctx)
         outs.append(g.generate(2).tokens)
     assert torch.equal(outs[0], outs[1])
+
+
+def test_do_q_injection_replaces_the_order():
+    torch.manual_seed(0)
+    a = preset_args("smoke", n_messages=6)
+    m = build_model(a).eval()
+    tok = get_tokenizer("22tok")
+    days = make_sequences(2, 8, seed=3)
+    ctx = _context(days, 6, tok)
+    g = Generator(m, "22tok", top_n=1, seed=1)
+    g.condition(*ctx)
+    base = g.generate(3)
+    g.condition(*ctx)
+    out = g.generate(3, inject={"step": 1, "event_type": 1, "side": 1, "qty": 777, "offset_ticks": -1})
+    em = out.engine_msgs.numpy()
+    mid_before = out.mid[:, 0].numpy()
+    for b in range(2):
+        assert list(em[b, 1, :4]) == [1, 1, 777, int(mid_before[b]) - 100]
+        assert em[b, 1, 4] == 2            # the running new-order id at step 1 of 3
+        assert out.provenance[b, 1] & 16 and not out.provenance[b, 0] & 16
+    # the step before the injection is untouched
+    assert torch.equal(base.tokens[:, 0], out.tokens[:, 0])

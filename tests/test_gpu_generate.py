@@ -105,11 +105,12 @@ def test_gen_apply_matches_cpu_oracle():
     for k in range(n):
         oid.fill_(n - k)
         t = torch.from_numpy(toks_all[:, k].astype(np.int64)).cuda()
+        inj = [1, 1 + (k % 2) * 3, k % 2, 55, -1 - k % 3] if k % 17 == 5 else None   # do(Q) at a few steps
         ext().gen_apply(asks, bids, trades, t, lay, cfg.init_id, cfg.book_depth, cfg.cancel_mode,
                         cfg.type_4_interpretation, cfg.check_book_fill, oid, p_mid, tin, o_raw, o_msg, o_prov, o_l2,
-                        img, True)
+                        img, True, torch.tensor(inj, dtype=torch.int32, device="cuda") if inj else None)
         for b in range(nb):
-            raw, msg, prov, l2, im, pmn = apply_message_cpu(obs[b], toks_all[b, k], tok, pm[b], n - k)
+            raw, msg, prov, l2, im, pmn = apply_message_cpu(obs[b], toks_all[b, k], tok, pm[b], n - k, inject=inj)
             pm[b] = pmn
             provs.add(prov)
             assert np.array_equal(o_raw[b].cpu().numpy(), raw), (k, b, o_raw[b], raw)
