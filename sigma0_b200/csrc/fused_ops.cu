@@ -236,65 +236,76 @@ __global__ void rms_fwd_k(const bf16* __restrict__ x, const float* __restrict__ 
   }
 }
 
-// RMSNorm backward: dx = r*g*w - x*r^3*mean(g*w*x); per-block partial rows of
-// dw = sum g*x*r in part[block][D].  Two passes over a row (the second re-reads
-// it from L1) keep registers low; column partials in per-warp shared rows.
-template <int J>   // 8-element chunks per lane: D <= 256 * J
-__global__ void __launch_bounds__(CB_NT)
-    rms_bwd_k(const bf16* __restrict__ dy, const bf16* __restrict__ x, const float* __restrict__ w,
-              const float* __restrict__ rstd, bf16* __restrict__ dx, float* __restrict__ part, int T, int D) {
-  extern __shared__ __align__(16) float red_smem[];   // [8][D]
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  float* sw = red_smem + (size_t)wid * D;
-  for (int c = lane * 4; c < D; c += 128) *reinterpret_cast<float4*>(sw + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-  __syncwarp();
-  const int gw = blockIdx.x * (CB_NT / 32) + wid, nw = gridDim.x * (CB_NT / 32);
+// RMSNorm backward: register column accumulators, one partial row of dw per block.
+template <int PER>
+__global__ void rms_bwd_k(const bf16* __restrict__ dy, const bf16* __restrict__ x, const float* __restrict__ w,
+                          const float* __restrict__ rstd, bf16* __restrict__ dx, float* __restrict__ dw, int T,
+                          int D) {
+  int lane = threadIdx.x & 31;
+  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  int nv = D / 8;   // uint4 chunks per row; lane handles chunks lane + 32*j
+  float aw[PER * 8];
+#pragma unroll
+  for (int i = 0; i < PER * 8; ++i) aw[i] = 0.f;
   for (int row = gw; row < T; row += nw) {
-    const size_t o = (size_t)row * D;
-    const float r = rstd[row];
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
+    const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * D);
+    float r = rstd[row];
     float m = 0.f;
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int c = 8 * (lane + 32 * j);
-      if (c < D) {
-        const uint4 ux = *reinterpret_cast<const uint4*>(x + o + c), ug = *reinterpret_cast<const uint4*>(dy + o + c);
-        const uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w};
-        float acc[8];
+    for (int j = 0; j < PER; ++j) {
+      int c = lane + 32 * j;
+      if (c < nv) {
+        uint4 ux = xr[c], ug = gr[c];
+        uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
-          m += fg.x * w[c + 2 * k] * fx.x + fg.y * w[c + 2 * k + 1] * fx.y;
-          acc[2 * k] = fg.x * fx.x * r;
-          acc[2 * k + 1] = fg.y * fx.y * r;
+          float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          int col = c * 8 + 2 * k;
+          m += fg.x * w[col] * fx.x + fg.y * w[col + 1] * fx.y;
+          aw[j * 8 + 2 * k] += fg.x * fx.x * r;
+          aw[j * 8 + 2 * k + 1] += fg.y * fx.y * r;
         }
-        add4(sw + c, make_float4(acc[0], acc[1], acc[2], acc[3]));
-        add4(sw + c + 4, make_float4(acc[4], acc[5], acc[6], acc[7]));
       }
     }
     m = warp_sum(m) / D;
+    uint4* dr = reinterpret_cast<uint4*>(dx + (size_t)row * D);
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int c = 8 * (lane + 32 * j);
-      if (c < D) {
-        const uint4 ux = *reinterpret_cast<const uint4*>(x + o + c), ug = *reinterpret_cast<const uint4*>(dy + o + c);
-        const uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w};
-        uint32_t ov[4];
+    for (int j = 0; j < PER; ++j) {
+      int c = lane + 32 * j;
+      if (c < nv) {
+        uint4 ux = xr[c], ug = gr[c];
+        uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w}, o[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
-          ov[k] = pack_bf16(r * fg.x * w[c + 2 * k] - fx.x * r * r * r * m,
-                            r * fg.y * w[c + 2 * k + 1] - fx.y * r * r * r * m);
+          float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          int col = c * 8 + 2 * k;
+          float d0 = r * fg.x * w[col] - fx.x * r * r * r * m;
+          float d1 = r * fg.y * w[col + 1] - fx.y * r * r * r * m;
+          o[k] = pack_bf16(d0, d1);
         }
-        *reinterpret_cast<uint4*>(dx + o + c) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+        dr[c] = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
   }
+  // block reduction: smem[w][col] then one atomic per column per block
+  extern __shared__ float red_smem[];
+  int wid = threadIdx.x >> 5, nwb = blockDim.x >> 5;
+  for (int i = threadIdx.x; i < nwb * D; i += blockDim.x) red_smem[i] = 0.f;
   __syncthreads();
-  float* dst = part + (size_t)blockIdx.x * D;
-  for (int c = threadIdx.x; c < D; c += CB_NT) {
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    int c = lane + 32 * j;
+    if (c < nv)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) red_smem[wid * D + c * 8 + k] = aw[j * 8 + k];
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < D; col += blockDim.x) {
     float t = 0.f;
-    for (int k = 0; k < CB_NT / 32; ++k) t += red_smem[(size_t)k * D + c];
-    dst[c] = t;
+    for (int k = 0; k < nwb; ++k) t += red_smem[k * D + col];
+    dw[(size_t)blockIdx.x * D + col] = t;   // this block's partial row (dw is the partial buffer)
   }
 }
 
@@ -569,11 +580,15 @@ void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* 
   const bf16* g = reinterpret_cast<const bf16*>(dy);
   const bf16* xp = reinterpret_cast<const bf16*>(x);
   bf16* o = reinterpret_cast<bf16*>(dx);
-  const size_t sm = (size_t)(CB_NT / 32) * D * 4;
-  if (D <= 256) { allow_smem(rms_bwd_k<1>, sm); rms_bwd_k<1><<<gr, CB_NT, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
-  else if (D <= 512) { allow_smem(rms_bwd_k<2>, sm); rms_bwd_k<2><<<gr, CB_NT, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
-  else if (D <= 1024) { allow_smem(rms_bwd_k<4>, sm); rms_bwd_k<4><<<gr, CB_NT, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
-  else { allow_smem(rms_bwd_k<8>, sm); rms_bwd_k<8><<<gr, CB_NT, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
+  const int nv = D / 8;
+  const size_t sm = 8 * (size_t)D * 4;
+  if (nv <= 32) rms_bwd_k<1><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
+  else if (nv <= 64) rms_bwd_k<2><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
+  else if (nv <= 128) rms_bwd_k<4><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
+  else {
+    allow_smem(rms_bwd_k<8>, sm);
+    rms_bwd_k<8><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
+  }
   col_sum(part, gr, 1, D, dw, nullptr, st);
 }
 void gelu_fwd_launch(const void* o, void* g, long n, int sms, cudaStream_t st) {
