@@ -1,0 +1,89 @@
+"""CLIs (train/infer/plan) and evaluation metrics on CPU."""
+import glob
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+
+def test_train_cli_runs_and_resumes(tmp_path, capsys):
+    from sigma0_b200.cli.train import main
+    base = ["--preset", "smoke", "--impl", "torch", "--synthetic", "2", "--n_messages", "4", "--micro_bsz", "2",
+            "--log_every", "1", "--watchdog_timeout", "0", "--ckpt_dir", str(tmp_path / "ck")]
+    assert main(base + ["--steps", "2", "--save_every", "1"]) == 0
+    assert main(base + ["--steps", "3"]) == 0
+    lines = [json.loads(l) for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+    assert any(l.get("event") == "resumed" and l["trainer_step"] == 2 for l in lines)
+    assert lines[-1]["event"] == "finished" and lines[-1]["steps"] == 3
+
+
+def test_train_cli_config_file(tmp_path):
+    from sigma0_b200.cli.train import parse
+    (tmp_path / "c.yaml").write_text("steps: 7\nlog_every: 3\nenv_S0_TEST_KNOB: 1\n")
+    a = parse(["--config", str(tmp_path / "c.yaml"), "--log_every", "5"])
+    assert a.steps == 7 and a.log_every == 5 and os.environ.get("S0_TEST_KNOB") == "1"
+
+
+def test_infer_cli_writes_lobster_csvs(tmp_path):
+    import pandas as pd
+    from sigma0_b200.cli.infer import main
+    out = tmp_path / "gen"
+    assert main(["--preset", "smoke", "--impl", "torch", "--synthetic", "2", "--n_sequences", "2", "--batch_size",
+                 "2", "--n_cond_msgs", "4", "--n_gen_msgs", "3", "--sample_top_n", "1", "--save_dir", str(out)]) == 0
+    gen = sorted(glob.glob(str(out / "data_gen" / "*_message_real_id_*_gen_id_0.csv")))
+    assert len(gen) == 2
+    df = pd.read_csv(gen[0])
+    assert list(df.columns) == ["time", "event_type", "order_id", "size", "price", "direction"] and len(df) == 3
+    assert set(df.direction) <= {-1, 1}
+    cond = pd.read_csv(glob.glob(str(out / "data_cond" / "*_orderbook_real_id_0.csv"))[0])
+    assert len(cond) == 5                                   # N + 1 book rows
+    assert os.path.exists(out / "sample_indices_rank0.json")
+
+
+def test_plan_commands(tmp_path):
+    from sigma0_b200.cli.plan import build_plan
+    (tmp_path / "p.yaml").write_text("name: smoke\nsbatch_nodes: 1\nenv_MODEL_PRESET: 75m\n")
+    p = build_plan(str(tmp_path / "p.yaml"))
+    s = p.shell()
+    assert "--nproc-per-node=8" in s and "MODEL_PRESET=75m" in s and "sigma0_b200.cli.train" in s
+    (tmp_path / "m.yaml").write_text("include: p.yaml\nsbatch_nodes: 4\nsbatch_time: 02:00:00\n")
+    s = build_plan(str(tmp_path / "m.yaml")).shell()
+    assert s.startswith("env") and "sbatch" in s and "--nodes=4" in s and "srun" in s
+
+
+def test_message_perplexity_decomposes():
+    from sigma0_b200.data import make_sequences, LobWindowDataset, collate
+    from sigma0_b200.encoding import get_tokenizer
+    from sigma0_b200.eval.perplexity import message_perplexity
+    from sigma0_b200.models import preset_args, build_model
+    torch.manual_seed(0)
+    m = build_model(preset_args("smoke")).eval()
+    ds = LobWindowDataset.from_days(make_sequences(2, 5, seed=1), 4, token_mode="22tok")
+    mp = message_perplexity(m, [collate([ds[0], ds[1]])], get_tokenizer("22tok"))
+    d = mp.as_dict()
+    assert mp.n_messages == 8
+    assert abs(mp.full_nats - (mp.roles["main"] + mp.roles["absolute_time"] + mp.roles["reference"])) < 1e-9
+    assert 0 < d["main"]["nats_per_message"] < d["full"]["nats_per_message"]
+
+
+def test_lob_metrics_on_engine_replay():
+    from sigma0_b200.data.synthetic import generate_day
+    from sigma0_b200.eval.lob_metrics import validity_report, marginals, score, event_returns
+    d1, d2 = generate_day(400, seed=1), generate_day(400, seed=2)
+
+    def view(d):
+        m = d.msgs
+        msgs = np.stack([m[:, 8], m[:, 9], m[:, 1], m[:, 0], m[:, 5], m[:, 3], m[:, 2] * 2 - 1], 1)
+        return msgs, d.books[:, 3:]
+    m1, b1 = view(d1)
+    rep = validity_report(m1)
+    assert rep["non_monotone_time"] == 0 and rep["bad_event_type"] == 0
+    s = score(marginals(*view(d1)), marginals(*view(d2)), n_boot=10)
+    names = {x.metric for x in s}
+    assert "spread_ticks/wasserstein" in names and all(x.ci_low <= x.ci_high for x in s)
+    same = {x.metric: x.value for x in score(marginals(m1, b1), marginals(m1, b1), n_boot=2)}
+    assert same["order_size/ks"] == 0.0
+    r = event_returns(m1, b1, horizons_ms=(1, 10))
+    assert r["anchors"][0] > 0 and set(r["event"]) == {1, 10}
