@@ -41,10 +41,13 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return torch.stack([o0, o1], dim=-1).reshape(x.shape)
 
 
-def angle_cumsum(angles: torch.Tensor, DT: torch.Tensor) -> torch.Tensor:
-    """angles (Bt, L, R), DT (Bt, H, L) -> cumulative angles (Bt, L, H, R) mod 2*pi."""
+def angle_cumsum(angles: torch.Tensor, DT: torch.Tensor, offset=None) -> torch.Tensor:
+    """angles (Bt, L, R), DT (Bt, H, L) -> cumulative angles (Bt, L, H, R) mod 2*pi,
+    starting from ``offset`` (Bt, H, R) when given (a sequence continued from a carry)."""
     rate = torch.tanh(angles)[:, :, None, :] * math.pi * DT.transpose(1, 2)[..., None]
     cs = torch.cumsum(rate, dim=1)
+    if offset is not None:
+        cs = cs + offset[:, None]
     return cs - TWO_PI * torch.floor(cs / TWO_PI)
 
 
@@ -65,12 +68,16 @@ def segsum(x: torch.Tensor) -> torch.Tensor:
 
 
 def mamba3_ssd_chunked(Q, K, V, ADT, DT, Trap, angles, Q_bias, K_bias, D, Z, chunk_size=64,
-                       return_final_state=False, initial_state=None):
-    """Chunked SSD forward; returns y (Bt, L, H, P) (and the final state (Bt, H, P, N))."""
+                       return_final_state=False, initial_state=None, angle_offset=None):
+    """Chunked SSD forward; returns y (Bt, L, H, P) (and the final state (Bt, H, P, N)).
+
+    ``initial_state`` (Bt, H, P, N) and ``angle_offset`` (Bt, H, R) continue a sequence
+    from a carry (context parallelism); the last token's trapezoid term that the next
+    segment's first token would add is left out, as at the end of a sequence."""
     Bt, L, H, N = Q.shape
     P = V.shape[-1]
     CS = chunk_size
-    ang = angle_cumsum(angles, DT)                          # (Bt, L, H, R)
+    ang = angle_cumsum(angles, DT, angle_offset)            # (Bt, L, H, R)
     cos, sin = torch.cos(ang), torch.sin(ang)
     gamma, scale = trapezoid_gamma_scale(DT, Trap)          # (Bt, H, L)
     Qb = Q + Q_bias
@@ -119,9 +126,16 @@ def mamba3_ssd_chunked(Q, K, V, ADT, DT, Trap, angles, Q_bias, K_bias, D, Z, chu
     Y = Y + (D[None, None, None, :, None] + qkc[..., None]) * Vc
     Y = Y * F.silu(Zc)
     Y = Y.reshape(Bt, Lp, H, P)[:, :L]
+    if return_final_state == "all":
+        return Y, st, ang, Kr_unscaled_last(Kb, cos, sin), cum
     if return_final_state:
         return Y, st
     return Y
+
+
+def Kr_unscaled_last(Kb, cos, sin):
+    """The last token's rotated (unscaled) key: the decode state's k_prev."""
+    return apply_rope(Kb[:, -1:], cos[:, -1:], sin[:, -1:])[:, 0]
 
 
 def mamba3_recurrent(Q, K, V, ADT, DT, Trap, angles, Q_bias, K_bias, D, Z, state=None):

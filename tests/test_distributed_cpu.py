@@ -34,7 +34,7 @@ def _free_port():
 
 def _worker(rank, world, port, mode, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=120))
     try:
         from sigma0_b200.train.trainer import Trainer
         torch.set_num_threads(1)
@@ -112,3 +112,43 @@ def test_sharded_checkpoint_restores_at_world_one(tmp_path):
         lo = d["lo"]
         k = min(d["m"].numel(), tr.opt.numel - lo)
         assert torch.equal(tr.opt.m[lo:lo + k], d["m"][:k])
+
+
+def _diloco_worker(rank, world, port, mode, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=120))
+    try:
+        from sigma0_b200.train.trainer import Trainer
+        from sigma0_b200.train.diloco import DiLoCo
+        torch.set_num_threads(1)
+        tr = Trainer(_args(), device=torch.device("cpu"), world=1, rank=0, total_steps=10, seed=0)
+        dl = DiLoCo(tr, inner_steps=2, mode=mode)
+        tok, lab, book = _batch()
+        per = tok.shape[0] // world
+        sl = slice(rank * per, (rank + 1) * per)
+        for _ in range(4):
+            dl.step(tok[sl], lab[sl], book[sl])
+        torch.save({"flat": tr.opt.flat.clone(), "outer": dl.outer_steps}, os.path.join(out_dir, f"d{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["diloco", "fedavg"])
+def test_diloco_ranks_agree_after_outer_steps(tmp_path, mode):
+    mp.spawn(_diloco_worker, args=(2, _free_port(), mode, str(tmp_path)), nprocs=2, join=True)
+    a, b = (torch.load(os.path.join(tmp_path, f"d{r}.pt")) for r in range(2))
+    assert a["outer"] == 2 and torch.equal(a["flat"], b["flat"])
+    assert torch.isfinite(a["flat"]).all()
+
+
+def test_fedavg_one_inner_step_is_parameter_average(tmp_path):
+    """FedAvg with H=1 on a single process equals the local step (average of one)."""
+    from sigma0_b200.train.trainer import Trainer
+    from sigma0_b200.train.diloco import DiLoCo
+    tr = Trainer(_args(), device=torch.device("cpu"), total_steps=10, seed=0)
+    ref = Trainer(_args(), device=torch.device("cpu"), total_steps=10, seed=0)
+    dl = DiLoCo(tr, inner_steps=1, mode="fedavg")
+    tok, lab, book = _batch()
+    dl.step(tok, lab, book)
+    ref.step_device(tok, lab, book)
+    assert torch.allclose(tr.opt.flat, ref.opt.flat, atol=1e-7)
