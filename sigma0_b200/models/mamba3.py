@@ -156,7 +156,7 @@ class Mamba3(nn.Module):
     def _post_cuda(self, y2):
         from ..ops._ext import ext
         from ..ops import weights as W
-        yn, _ = ext().rms_fwd(y2, self.out_norm.scale, 1e-6)
+        yn, _ = ext().rms_fwd(y2, self.out_norm.scale, self.out_norm.eps)
         return yn @ W.bf16(self.out_proj.kernel)
 
     def _step_cuda(self, state, u):
@@ -167,7 +167,7 @@ class Mamba3(nn.Module):
         ang, ssm, kp, vp = state
         y = torch.empty(B, d.d_inner, dtype=torch.bfloat16, device=u.device)
         ext().m3_decode_step(proj, d.n_heads, self.B_norm.scale, self.C_norm.scale, self.dt_bias, self.B_bias,
-                             self.C_bias, self.D, self.A_floor, 1e-6, ang, ssm, kp, vp, y)
+                             self.C_bias, self.D, self.A_floor, self.B_norm.eps, ang, ssm, kp, vp, y)
         return state, self._post_cuda(y)[:, None]
 
     @torch.no_grad()
@@ -188,7 +188,7 @@ class Mamba3(nn.Module):
         from ..ops._ext import ext
         proj = self._proj_cuda(u.reshape(-1, H))
         y, _, fin, thf = ext().m3_fwd(proj, B, L, d.n_heads, self.B_norm.scale, self.C_norm.scale, self.dt_bias,
-                                      self.B_bias, self.C_bias, self.D, self.A_floor, 1e-6, want_final=True)
+                                      self.B_bias, self.C_bias, self.D, self.A_floor, self.B_norm.eps, want_final=True)
         # k_prev / v_prev: the last token's rotated key and value
         last = proj.view(B, L, -1)[:, -1, :d.d_in_proj].float()
         z, x, Bn, Cn, ADT, DT, trap, angr = self._prep(last[:, None])

@@ -311,8 +311,9 @@ def build_backbone(args: Any, *, print_shapes: bool = False) -> BackboneBuild:
 def build_model(args: Any):
     """Build the outer LOB model for ``args`` (an argparse namespace or similar)."""
     from .lob_model import LobModel
+    from .legacy_norm import apply_legacy_norm, legacy_norm_enabled
     bb = build_backbone(args)
-    return LobModel(bb.factory_at, vocab_size=int(args.vocab_size), d_model=int(args.d_model),
+    model = LobModel(bb.factory_at, vocab_size=int(args.vocab_size), d_model=int(args.d_model),
                     d_book=int(_g(args, "d_book", 503)),
                     n_message_layers=int(_g(args, "n_message_layers", 2)),
                     n_fused_layers=int(_g(args, "n_layers", 6)),
@@ -324,3 +325,6 @@ def build_model(args: Any):
                     msg_len=int(_g(args, "msg_len", 22)),
                     use_book_data=bool(_g(args, "use_book_data", True)),
                     attn_factory_at=bb.attn_factory_at, attn_layers=bb.attn_layers)
+    if bool(_g(args, "legacy_norm", False)) or legacy_norm_enabled():
+        apply_legacy_norm(model)
+    return model

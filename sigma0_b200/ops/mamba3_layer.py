@@ -55,9 +55,9 @@ class _Mamba3Core:
         w_in = W.bf16_padded(m.in_proj.kernel, ldp)
         proj = xn @ w_in                                              # [T, ldp]
         y = C.m3_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias,
-                     m.D, m.A_floor, EPS)[0]
+                     m.D, m.A_floor, m.B_norm.eps)[0]
         y2 = y.view(-1, d.d_inner)
-        yn, yr = C.rms_fwd(y2, m.out_norm.scale, EPS)
+        yn, yr = C.rms_fwd(y2, m.out_norm.scale, m.out_norm.eps)
         o = yn @ W.bf16(m.out_proj.kernel)                            # [T, H]
         return o, proj, y2, yr
 
@@ -67,13 +67,13 @@ class _Mamba3Core:
         C = ext()
         d = m.dims
         ldp = proj.shape[1]
-        yn, _ = C.rms_fwd(y2, m.out_norm.scale, EPS)
+        yn, _ = C.rms_fwd(y2, m.out_norm.scale, m.out_norm.eps)
         g_out_proj = _mm_f32(yn.t(), do)
         dyn = do @ W.bf16(m.out_proj.kernel).t()
         dy, g_out_norm = C.rms_bwd(dyn.contiguous(), y2, m.out_norm.scale, yr)
         dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_bwd(
             proj, dy, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D, B, L,
-            d.n_heads, m.A_floor, EPS)
+            d.n_heads, m.A_floor, m.B_norm.eps)
         g_in = _mm_f32(xn.t(), dproj)[:, :d.d_in_proj]
         dxn = dproj @ W.bf16_padded(m.in_proj.kernel, ldp).t()
         grads = {m.out_proj.kernel: g_out_proj, m.out_norm.scale: g_out_norm, m.in_proj.kernel: g_in,
@@ -122,7 +122,7 @@ class _LayerFn(torch.autograd.Function):
         xf = x.reshape(-1, H)
         if xf.dtype != torch.float32 or not xf.is_contiguous():
             xf = xf.float().contiguous()
-        xn, mu, rs = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, EPS)
+        xn, mu, rs = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)
         o, proj, y2, yr = _Mamba3Core.forward(xn, B, L, m)
         g = C.gelu_fwd(o)
         h = g @ W.bf16(layer.out2.kernel)
@@ -146,7 +146,7 @@ class _LayerFn(torch.autograd.Function):
         g_out2 = _mm_f32(g.t(), dh)
         dgm = dh @ W.bf16(layer.out2.kernel).t()
         do = C.gelu_bwd(o, dgp, dgm.contiguous())
-        xn, _, _ = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, EPS)
+        xn, _, _ = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)
         dxn, grads = _Mamba3Core.backward(do, xn, proj, y2, yr, B, L, m)
         dx, dlw, dlb = C.ln_bwd(dxn.contiguous(), xf, mu, rs, layer.norm.scale, dout)
         grads[layer.norm.scale] = dlw

@@ -47,7 +47,13 @@ class Trainer:
                 dist.broadcast(p.data, 0, group=group)
         lr_base = float(getattr(args, "ssm_lr_base", 1e-3))
         lr = lr_base * float(getattr(args, "lr_factor", 1.0))
-        self.opt = FlatAdam(self.model, lr=lr, ssm_lr=lr_base,
+        opt_cls = FlatAdam
+        extra_opt = {}
+        if str(getattr(args, "opt_config", "standard")) == "muon":
+            from .muon import FlatMuon
+            opt_cls = FlatMuon
+            extra_opt = dict(muon_lr=float(getattr(args, "muon_lr", 0.02)))
+        self.opt = opt_cls(self.model, lr=lr, ssm_lr=lr_base, **extra_opt,
                             weight_decay=float(getattr(args, "weight_decay", 0.05)),
                             max_grad_norm=float(getattr(args, "max_grad_norm", 1.0)),
                             opt_config=str(getattr(args, "opt_config", "standard")),
