@@ -255,9 +255,44 @@ class Generator:
         self.ctr = torch.zeros(1, dtype=torch.int64, device=dev)
         self.new_oid = torch.zeros(1, dtype=torch.int32, device=dev)
         self.graph = None
+        self._oid_offset = 0
         self._gen = torch.Generator(device=dev).manual_seed(self.seed)
 
     # -- one message ---------------------------------------------------------------------------
+    # -- outside orders ---------------------------------------------------------------------------
+    @torch.no_grad()
+    def apply_engine_messages(self, msgs) -> torch.Tensor:
+        """Process outside orders (B, m, 8) on the generator's books between generated
+        messages (a trading agent in the loop); the trades rows are cleared first, so
+        the returned (B, n_trades, 8) trades belong to these messages and any generated
+        message processed before the next call."""
+        msgs = torch.as_tensor(msgs)
+        if self.on_gpu:
+            from ..ops._ext import ext
+            c = self.cfg
+            self.trades.fill_(-1)
+            ext().eng_process(self.asks, self.bids, self.trades, msgs.to(self.dev, torch.int32).contiguous(),
+                              c.init_id, c.book_depth, c.cancel_mode, c.type_4_interpretation, c.check_book_fill)
+            return self.trades
+        out = []
+        for b, ob in enumerate(self.books_cpu):
+            ob.trades[:] = -1
+            for row in msgs[b].numpy():
+                ob.process(row)
+            out.append(torch.from_numpy(ob.trades.copy()))
+        return torch.stack(out)
+
+    def trade_rows(self) -> torch.Tensor:
+        if self.on_gpu:
+            return self.trades.cpu().long()
+        return torch.from_numpy(np.stack([ob.trades for ob in self.books_cpu]))
+
+    def sides(self):
+        if self.on_gpu:
+            return self.asks.cpu().long(), self.bids.cpu().long()
+        return (torch.from_numpy(np.stack([ob.asks for ob in self.books_cpu])),
+                torch.from_numpy(np.stack([ob.bids for ob in self.books_cpu])))
+
     def _logits(self, h):
         from ..ops import weights as W
         h2 = h[:, -1].to(torch.bfloat16)
@@ -357,7 +392,9 @@ class Generator:
         out_prov = torch.zeros(B, n_msgs, dtype=torch.int32, device=dev)
         out_mid = torch.zeros(B, n_msgs, dtype=torch.int32, device=dev)
         out_em = torch.zeros(B, n_msgs, 8, dtype=torch.int32, device=dev)
-        self.new_oid.fill_(n_msgs)
+        # order ids of generated new orders count down within a call (the reference's
+        # n_msg_todo) and never repeat across calls
+        self.new_oid.fill_(n_msgs + self._oid_offset)
         self.graph = None
         graph = self.on_gpu and self.use_graphs and n_msgs > 1
         for k in range(n_msgs):
@@ -374,7 +411,7 @@ class Generator:
                     self._message_device()
             else:
                 self._message_device()
-                self._engine_cpu(n_msgs - k)
+                self._engine_cpu(n_msgs - k + self._oid_offset)
             out_tok[:, k] = self.msg
             out_raw[:, k] = self.o_raw
             out_l2[:, k] = self.o_l2
@@ -383,6 +420,7 @@ class Generator:
             out_em[:, k] = self.o_msg
         if events is not None:
             events[n_msgs].record()
+        self._oid_offset += n_msgs
         return GenOutput(out_tok, out_raw, out_l2, out_prov, out_mid, out_em)
 
     def _capture(self):
