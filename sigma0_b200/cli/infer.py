@@ -121,6 +121,7 @@ def main(argv=None):
         raw = out.raw.cpu().numpy()
         l2 = out.l2.cpu().numpy()
         prov = out.provenance.cpu().numpy()
+        mids = out.mid.cpu().numpy()
         for j, i in enumerate(batch):
             di, s = windows[i]
             d = days[di]
@@ -138,7 +139,7 @@ def main(argv=None):
                 os.path.join(a.save_dir, "data_gen", f"{pre}_message_real_id_{i}_gen_id_0.csv"), index=False)
             pd.DataFrame(l2[j]).to_csv(
                 os.path.join(a.save_dir, "data_gen", f"{pre}_orderbook_real_id_{i}_gen_id_0.csv"), index=False)
-            pd.DataFrame({"provenance": prov[j]}).to_csv(
+            pd.DataFrame({"provenance": prov[j], "mid_after": mids[j]}).to_csv(
                 os.path.join(a.save_dir, "data_gen", f"{pre}_provenance_real_id_{i}_gen_id_0.csv"), index=False)
     return 0
 

@@ -209,3 +209,16 @@ def ticker_balanced_order(tickers: Sequence[str], seed: int = 0) -> np.ndarray:
             if l:
                 out.append(l.pop())
     return np.array(out, dtype=np.int64)
+
+
+def make_snapshots(books: np.ndarray, times_ns: Sequence[int]) -> np.ndarray:
+    """L2 snapshots at the given wall-clock times (ns since midnight): the book of the
+    last event at or before each time (the wide-book snapshot builder of the
+    reference's ``tools/data_build/make_snapshots.py``).  ``books`` rows are
+    ``[dmid, time_s, time_ns, L2...]`` describing the book before each message, so the
+    state *at* a message time is taken from the next row."""
+    b = np.asarray(books)
+    t = b[:, 1].astype(np.int64) * 1_000_000_000 + b[:, 2].astype(np.int64)
+    idx = np.searchsorted(t, np.asarray(times_ns, dtype=np.int64), side="right")
+    idx = np.clip(idx, 0, len(b) - 1)
+    return b[idx, 3:]

@@ -1,0 +1,99 @@
+"""Pipeline: scoring a generation run, J4 injection gate, model store, packaging, evidence."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+
+@pytest.fixture(scope="module")
+def run_dir(tmp_path_factory):
+    from sigma0_b200.cli.infer import main
+    out = tmp_path_factory.mktemp("run")
+    assert main(["--preset", "smoke", "--impl", "torch", "--synthetic", "3", "--n_sequences", "3", "--batch_size", "3",
+                 "--n_cond_msgs", "4", "--n_gen_msgs", "6", "--sample_top_n", "1", "--save_dir", str(out)]) == 0
+    return str(out)
+
+
+def test_lobbench_modes_and_merge(run_dir):
+    from sigma0_b200.pipeline.lobbench import score_run, merge, load_run, shard
+    assert len(load_run(run_dir)) == 3
+    for mode in ("uncond", "cond", "context", "time_lagged"):
+        r = score_run(run_dir, mode, n_boot=5)
+        assert r["n_windows"] >= 2 and "order_size/wasserstein" in r["scores"]
+    d = score_run(run_dir, "divergence", buckets=2)
+    assert len(d["buckets"]) == 2
+    parts = [score_run(run_dir, "cond", windows=shard([0, 1, 2], 2, k)) for k in range(2)]
+    m = merge(parts)
+    assert m["n_windows"] == 3
+
+
+def test_injection_j4(tmp_path):
+    from sigma0_b200.cli.infer import main
+    from sigma0_b200.pipeline.injection import verify_injection
+    out = tmp_path / "inj"
+    assert main(["--preset", "smoke", "--impl", "torch", "--synthetic", "2", "--n_sequences", "2", "--batch_size", "2",
+                 "--n_cond_msgs", "4", "--n_gen_msgs", "4", "--sample_top_n", "1", "--save_dir", str(out),
+                 "--inject_step", "2", "--inject_event_type", "1", "--inject_side", "1", "--inject_qty", "37",
+                 "--inject_price_offset_ticks", "-1"]) == 0
+    r = verify_injection(str(out), step=2, side=1, qty=37, offset_ticks=-1)
+    assert r["J4"], r
+    bad = verify_injection(str(out), step=2, side=1, qty=38, offset_ticks=-1)
+    assert not bad["J4"]
+
+
+def test_model_store_and_packaging(tmp_path):
+    from sigma0_b200.ckpt import CheckpointManager
+    from sigma0_b200.models import preset_args
+    from sigma0_b200.pipeline.model_store import pin, resolve, ModelStoreError
+    from sigma0_b200.pipeline.package import pack, verify, unpack
+    from sigma0_b200.pipeline.integrity import tree_sha256, record_evidence, check_evidence
+    from sigma0_b200.train.trainer import Trainer
+    tr = Trainer(preset_args("smoke"), device=torch.device("cpu"))
+    ck = tmp_path / "ck"
+    CheckpointManager(str(ck)).save(5, tr, blocking=True)
+    store = str(tmp_path / "pins.json")
+    pin(store, "smoke-5", str(ck), 5, architecture="mamba3")
+    assert resolve(store, "smoke-5")["step"] == 5
+    with open(ck / "5" / "metadata" / "metadata", "a") as f:
+        f.write(" ")
+    with pytest.raises(ModelStoreError):
+        resolve(store, "smoke-5")
+    arc = str(tmp_path / "run.tar")
+    man = pack(str(ck), arc)
+    assert man and verify(arc) == {"mismatch": [], "missing": [], "extra": []}
+    unpack(arc, str(tmp_path / "restored"))
+    os.remove(tmp_path / "restored" / "MANIFEST.sha256.json")
+    assert tree_sha256(str(tmp_path / "restored")) == tree_sha256(str(ck))
+    src = str(tmp_path / "src.txt")
+    open(src, "w").write("x")
+    ev = str(tmp_path / "ev.json")
+    record_evidence(ev, [src], {"two": lambda: 1 + 1 == 2})
+    assert check_evidence(ev) == {"changed": [], "missing": [], "failed": []}
+    open(src, "w").write("y")
+    assert check_evidence(ev)["changed"] == [src]
+
+
+def test_guards_and_tools(tmp_path):
+    from sigma0_b200.pipeline.guards import non_english_lines, forbidden_imports, perplexity_decomposition_ok
+    import sigma0_b200
+    root = os.path.dirname(sigma0_b200.__file__)
+    assert non_english_lines([root]) == []
+    assert forbidden_imports([root], ["triton", "jax", "flax"]) == []
+    f = tmp_path / "x.py"
+    f.write_text("import triton.language as tl\n# café\n")
+    assert forbidden_imports([str(f)], ["triton"]) and non_english_lines([str(f)])
+    rep = {"roles": {"main": 1.0, "absolute_time": 0.5, "reference": 0.25}, "full": {"nats_per_message": 1.75}}
+    assert perplexity_decomposition_ok(rep)
+
+
+def test_snapshots_and_ce_by_position():
+    from sigma0_b200.data.synthetic import generate_day
+    from sigma0_b200.data.lobster import make_snapshots
+    from sigma0_b200.eval.ce_by_position import main
+    d = generate_day(50, seed=2)
+    t = d.books[:, 1].astype(np.int64) * 10**9 + d.books[:, 2].astype(np.int64)
+    snap = make_snapshots(d.books, [t[5], t[5] + 1])
+    assert np.array_equal(snap[0], d.books[6, 3:]) and np.array_equal(snap[1], d.books[6, 3:])
+    assert main(["--preset", "smoke", "--impl", "torch", "--n_messages", "4", "--max_batches", "1"]) == 0
