@@ -106,15 +106,22 @@ std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh
 
 std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias,
                                at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B, int64_t L, int64_t nh,
-                               double A_floor, double eps) {
+                               double A_floor, double eps, c10::optional<at::Tensor> saved_states) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
   req(dy, at::kBFloat16, "dy");
   M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
   int nc = m3_nchunks((int)L);
   M3Scan s = m3_scan(proj, pre, Bb, Cb, D);
-  auto states = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
-  m3_states_launch(g, s, states.data_ptr(), stream());
+  at::Tensor states;
+  if (saved_states.has_value() && saved_states->defined()) {   // the forward's passed states: no recompute
+    states = *saved_states;
+    req(states, at::kBFloat16, "saved_states");
+    TORCH_CHECK(states.numel() == B * nh * nc * M3_P * M3_N, "saved_states shape");
+  } else {
+    states = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
+    m3_states_launch(g, s, states.data_ptr(), stream());
+  }
   auto U = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
   m3_dstates_launch(g, s, dy.data_ptr(), U.data_ptr(), stream());
   auto f32 = proj.options().dtype(at::kFloat);
@@ -470,7 +477,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("m3_fwd", &m3_fwd, py::arg("proj"), py::arg("B"), py::arg("L"), py::arg("nh"), py::arg("wB"), py::arg("wC"),
         py::arg("dt_bias"), py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("A_floor"), py::arg("eps"),
         py::arg("want_final") = false, "Mamba3 SSD forward (prep, chunk states, passing, chunk scan) -> (y, states)");
-  m.def("m3_bwd", &m3_bwd, "Mamba3 SSD backward -> (dproj, dB_norm, dC_norm, ddt_bias, dD, dC_bias, dB_bias)");
+  m.def("m3_bwd", &m3_bwd, py::arg("proj"), py::arg("dy"), py::arg("wB"), py::arg("wC"), py::arg("dt_bias"),
+        py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("B"), py::arg("L"), py::arg("nh"), py::arg("A_floor"),
+        py::arg("eps"), py::arg("saved_states") = py::none(),
+        "Mamba3 SSD backward -> (dproj, dB_norm, dC_norm, ddt_bias, dD, dC_bias, dB_bias)");
   m.def("ln_fwd", &ln_fwd);
   m.def("ln_bwd", &ln_bwd);
   m.def("rms_fwd", &rms_fwd);

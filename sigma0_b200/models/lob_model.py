@@ -35,6 +35,7 @@ class LobBookEncoder(nn.Module):
         for i in range(n_pre):
             self.add_module(f"pre_layers_{i}", SequenceLayer(factory_at(d_book), d_book, activation, prenorm, dropout))
         self.projection = Dense(d_book, d_model)
+        self.compute_dtype = torch.float32
         for i in range(n_post):
             self.add_module(f"post_layers_{i}", SequenceLayer(factory_at(d_model), d_model, activation, prenorm, dropout))
 
@@ -49,10 +50,17 @@ class LobBookEncoder(nn.Module):
     def forward(self, x):
         for l in self.pre_layers:
             x = l(x)
-        x = self.projection(x)
+        x = self._project(x)
         for l in self.post_layers:
             x = l(x)
         return x
+
+    def _project(self, x):
+        """The d_book -> d_model projection: bf16 (K padded to 8) on CUDA, else fp32."""
+        if x.is_cuda and self.compute_dtype == torch.bfloat16:
+            from ..ops.linear import linear_bf16
+            return linear_bf16(x, self.projection.kernel, self.projection.bias)
+        return self.projection(x)
 
     def initial_state(self, batch, device=None):
         return ([l.initial_state(batch, device) for l in self.pre_layers],
@@ -64,7 +72,7 @@ class LobBookEncoder(nn.Module):
         for l in self.pre_layers:
             st, x = l.prefill(x, max_cache_len)
             pre.append(st)
-        x = self.projection(x)
+        x = self._project(x)
         for l in self.post_layers:
             st, x = l.prefill(x, max_cache_len)
             post.append(st)

@@ -18,12 +18,18 @@ multiple of 8 elements so every kernel can use 16-byte accesses.
 """
 from __future__ import annotations
 
+import os
+
 import torch
+import torch.nn.functional as F
 
 from ._ext import ext
 from . import weights as W
 
 EPS = 1e-6
+# keep the forward's passed SSD chunk states for the backward instead of recomputing
+# them (S0_RECOMPUTE_SSD_STATES=1 trades ~1 ms per layer-step for ~0.7 GB per layer)
+SAVE_STATES = os.environ.get("S0_RECOMPUTE_SSD_STATES", "0") in ("0", "", "false")
 
 
 def _pad8(n: int) -> int:
@@ -52,30 +58,47 @@ class _Mamba3Core:
         C = ext()
         d = m.dims
         ldp = _pad8(d.d_in_proj)
+        H = xn.shape[1]
+        Hp = _pad8(H)
         w_in = W.bf16_padded(m.in_proj.kernel, ldp)
+        if Hp != H:   # odd widths (the 503-wide book layers): pad K so the GEMM rows are 16-byte aligned
+            xn = F.pad(xn, (0, Hp - H))
+            w_in = F.pad(w_in, (0, 0, 0, Hp - H))
         proj = xn @ w_in                                              # [T, ldp]
-        y = C.m3_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias,
-                     m.D, m.A_floor, m.B_norm.eps)[0]
+        y, states = C.m3_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias,
+                             m.C_bias, m.D, m.A_floor, m.B_norm.eps)[:2]
         y2 = y.view(-1, d.d_inner)
         yn, yr = C.rms_fwd(y2, m.out_norm.scale, m.out_norm.eps)
-        o = yn @ W.bf16(m.out_proj.kernel)                            # [T, H]
-        return o, proj, y2, yr
+        o = yn @ W.bf16_padded(m.out_proj.kernel, Hp)                 # [T, Hp]
+        if Hp != H:
+            o = o[:, :H]
+        # the passed chunk states are kept for the backward (bf16, B*nh*nc*P*N) unless the
+        # model is set to recompute them (memory for time)
+        return o, proj, y2, yr, (states if SAVE_STATES else None)
 
     @staticmethod
-    def backward(do, xn, proj, y2, yr, B, L, m):
+    def backward(do, xn, proj, y2, yr, B, L, m, states=None):
         """Returns (dxn bf16, grads dict keyed by parameter)."""
         C = ext()
         d = m.dims
         ldp = proj.shape[1]
+        H = xn.shape[1]
+        Hp = _pad8(H)
+        w_out = W.bf16_padded(m.out_proj.kernel, Hp)
+        w_in = W.bf16_padded(m.in_proj.kernel, ldp)
+        if Hp != H:
+            do = F.pad(do, (0, Hp - H))
+            xn = F.pad(xn, (0, Hp - H))
+            w_in = F.pad(w_in, (0, 0, 0, Hp - H))
         yn, _ = C.rms_fwd(y2, m.out_norm.scale, m.out_norm.eps)
-        g_out_proj = _mm_f32(yn.t(), do)
-        dyn = do @ W.bf16(m.out_proj.kernel).t()
+        g_out_proj = _mm_f32(yn.t(), do)[:, :H]
+        dyn = do @ w_out.t()
         dy, g_out_norm = C.rms_bwd(dyn.contiguous(), y2, m.out_norm.scale, yr)
         dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_bwd(
             proj, dy, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D, B, L,
-            d.n_heads, m.A_floor, m.B_norm.eps)
-        g_in = _mm_f32(xn.t(), dproj)[:, :d.d_in_proj]
-        dxn = dproj @ W.bf16_padded(m.in_proj.kernel, ldp).t()
+            d.n_heads, m.A_floor, m.B_norm.eps, saved_states=states)
+        g_in = _mm_f32(xn.t(), dproj)[:H, :d.d_in_proj]
+        dxn = (dproj @ w_in.t())[:, :H]
         grads = {m.out_proj.kernel: g_out_proj, m.out_norm.scale: g_out_norm, m.in_proj.kernel: g_in,
                  m.B_norm.scale: dwB, m.C_norm.scale: dwC, m.dt_bias: ddtb, m.D: dD,
                  m.C_bias: dCb, m.B_bias: dBb}
@@ -92,18 +115,18 @@ class _MixerFn(torch.autograd.Function):
     def forward(ctx, u, module, *params):
         B, L, H = u.shape
         xn = u.reshape(-1, H).to(torch.bfloat16).contiguous()
-        o, proj, y2, yr = _Mamba3Core.forward(xn, B, L, module)
+        o, proj, y2, yr, st = _Mamba3Core.forward(xn, B, L, module)
         ctx.module, ctx.shape, ctx.in_dtype = module, (B, L, H), u.dtype
-        ctx.save_for_backward(xn, proj, y2, yr)
+        ctx.save_for_backward(xn, proj, y2, yr, st)
         return o.view(B, L, H)
 
     @staticmethod
     def backward(ctx, do):
-        xn, proj, y2, yr = ctx.saved_tensors
+        xn, proj, y2, yr, st = ctx.saved_tensors
         B, L, H = ctx.shape
         m = ctx.module
         do = do.reshape(-1, H).to(torch.bfloat16).contiguous()
-        dxn, grads = _Mamba3Core.backward(do, xn, proj, y2, yr, B, L, m)
+        dxn, grads = _Mamba3Core.backward(do, xn, proj, y2, yr, B, L, m, st)
         du = dxn.view(B, L, H).to(ctx.in_dtype)
         return (du, None) + tuple(grads[p] for p in _mixer_params(m))
 
@@ -123,18 +146,18 @@ class _LayerFn(torch.autograd.Function):
         if xf.dtype != torch.float32 or not xf.is_contiguous():
             xf = xf.float().contiguous()
         xn, mu, rs = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)
-        o, proj, y2, yr = _Mamba3Core.forward(xn, B, L, m)
+        o, proj, y2, yr, st = _Mamba3Core.forward(xn, B, L, m)
         g = C.gelu_fwd(o)
         h = g @ W.bf16(layer.out2.kernel)
         out = C.glu_res_fwd(xf, g, h, layer.out2.bias)
         ctx.layer, ctx.shape = layer, (B, L, H)
-        ctx.save_for_backward(xf, mu, rs, proj, y2, yr, o, h)
+        ctx.save_for_backward(xf, mu, rs, proj, y2, yr, o, h, st)
         return out.view(B, L, H)
 
     @staticmethod
     def backward(ctx, dout):
         C = ext()
-        xf, mu, rs, proj, y2, yr, o, h = ctx.saved_tensors
+        xf, mu, rs, proj, y2, yr, o, h, st = ctx.saved_tensors
         layer = ctx.layer
         m = layer.seq
         B, L, H = ctx.shape
@@ -147,7 +170,7 @@ class _LayerFn(torch.autograd.Function):
         dgm = dh @ W.bf16(layer.out2.kernel).t()
         do = C.gelu_bwd(o, dgp, dgm.contiguous())
         xn, _, _ = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)
-        dxn, grads = _Mamba3Core.backward(do, xn, proj, y2, yr, B, L, m)
+        dxn, grads = _Mamba3Core.backward(do, xn, proj, y2, yr, B, L, m, st)
         dx, dlw, dlb = C.ln_bwd(dxn.contiguous(), xf, mu, rs, layer.norm.scale, dout)
         grads[layer.norm.scale] = dlw
         grads[layer.norm.bias] = dlb

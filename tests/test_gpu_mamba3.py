@@ -147,3 +147,25 @@ def test_flat_adam_cuda_matches_cpu():
         net_c(x).pow(2).sum().backward()
         o1.step(); o2.step()
     assert (o1.flat.cpu() - o2.flat).abs().max().item() < 1e-5
+
+
+def test_odd_width_book_layer_paths_match_fp32():
+    """The padded bf16 paths for 503-wide book layers (mixer GEMMs and dense layers)."""
+    from sigma0_b200.ops.linear import linear_bf16
+    torch.manual_seed(0)
+    x = torch.randn(300, 503, device="cuda", requires_grad=True)
+    w = torch.randn(503, 1024, device="cuda", requires_grad=True)
+    b = torch.randn(1024, device="cuda", requires_grad=True)
+    y = linear_bf16(x, w, b)
+    yr = x @ w + b
+    assert rel(y, yr) < 1e-2
+    g = torch.randn_like(y)
+    gx, gw, gb = torch.autograd.grad(y, (x, w, b), g)
+    rx, rw, rb = torch.autograd.grad(yr, (x, w, b), g)
+    assert rel(gx, rx) < 1e-2 and rel(gw, rw) < 1e-2 and rel(gb, rb) < 1e-5
+    m = _layer(H=503, seed=3)
+    u = torch.randn(2, 130, 503, device="cuda") * 0.5
+    y = m(u)
+    m.impl = "torch"
+    y2 = m(u)
+    assert rel(y, y2) < 3e-2, rel(y, y2)
