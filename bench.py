@@ -381,6 +381,7 @@ def main():
                        "l2": "working set (weights + ~90 GB activations per step) far above L2; no flush needed",
                        "vocab": args.vocab_size, "token_mode": args.token_mode},
             "loss": float(loss), "gpu_launches": launches, "clocks": clk, "e2e": e2e,
+            "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9,
             "baseline_note": "vs_baseline divides by the reference's published 75m recipe rate, 178.5k tok/s per GH200",
         }
         print(json.dumps(out))
