@@ -470,6 +470,21 @@ void dp_fused_adam(std::vector<int64_t> G, std::vector<int64_t> P, std::vector<i
   TORCH_CHECK(rc == 0, "dp_fused_adam launch failed: ", rc > 0 ? cudaGetErrorString((cudaError_t)rc) : "occupancy");
 }
 
+std::vector<at::Tensor> tc_gemm_test(at::Tensor A, at::Tensor B, int64_t M) {
+  req(A, at::kBFloat16, "A");
+  req(B, at::kBFloat16, "B");
+  int64_t K = A.size(1), N = B.size(0);
+  TORCH_CHECK(A.size(0) == M && B.size(1) == K, "A (M, K), B (N, K)");
+  c10::cuda::CUDAGuard guard(A.device());
+  auto D = at::zeros({128, N}, A.options().dtype(at::kFloat));
+  auto err = at::zeros({1}, A.options().dtype(at::kInt));
+  int rc = tc_gemm_test_launch(A.data_ptr(), B.data_ptr(), D.data_ptr<float>(), (int)M, (int)N, (int)K,
+                               err.data_ptr<int>(), stream());
+  TORCH_CHECK(rc == 0, "unsupported shape");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {D, err};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -495,6 +510,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("m3_decode_step", &m3_decode_step, "Mamba3 one-token recurrent step (states updated in place)");
   m.def("eng_process", &eng_process, "batched matching engine: apply [B, M, 8] messages, one warp per book");
   m.def("eng_l2", &eng_l2, "batched L2 extraction");
+  m.def("tc_gemm_test", &tc_gemm_test, "tcgen05 self-test: D = A B^T in tensor memory (returns all 128 lanes)");
   m.def("dp_fused_adam", &dp_fused_adam, "fused reduce-scatter + AdamW + all-gather over peer memory");
   m.def("gen_apply", &gen_apply, "generation: decode message tokens, match, L2 and next book image");
   m.def("gen_sample", &gen_sample, "syntax-masked argmax / Gumbel-max sampling from fp32 logits");

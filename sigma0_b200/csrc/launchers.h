@@ -123,3 +123,6 @@ struct DpfArgs {
   float lr_s, lr_r, wd, b1, b2, eps, bc1, bc2, max_norm, inv_world;
 };
 int dp_fused_adam_launch(const DpfArgs& a, int sms, cudaStream_t st);
+
+// tcgen05 building-block self-test (tc_test.cu)
+int tc_gemm_test_launch(const void* A, const void* B, float* D, int M, int N, int K, int* err, cudaStream_t st);

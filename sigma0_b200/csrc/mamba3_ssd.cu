@@ -1256,7 +1256,7 @@ __global__ void __launch_bounds__(256)
     float sb[4] = {0, 0, 0, 0}, sc[4] = {0, 0, 0, 0}, sa = 0.f, dang[2] = {0.f, 0.f};
     for (int h0 = 0, j = 0; h0 < g.nh; h0 += 32, ++j) {
       const int hn = min(32, g.nh - h0);
-#pragma unroll 4
+#pragma unroll 16   // 16 heads' loads in flight per warp: the head loop is latency-bound
       for (int hh = 0; hh < hn; ++hh) {
         const int h = h0 + hh;
         size_t base = ((size_t)tok * g.nh + h) * N + lane * 4;
