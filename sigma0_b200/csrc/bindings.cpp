@@ -510,6 +510,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("m3_decode_step", &m3_decode_step, "Mamba3 one-token recurrent step (states updated in place)");
   m.def("eng_process", &eng_process, "batched matching engine: apply [B, M, 8] messages, one warp per book");
   m.def("eng_l2", &eng_l2, "batched L2 extraction");
+  m.def("m3_use_tc_scan", [](bool on) { m3_use_tc_scan(on ? 1 : 0); }, "select the tcgen05 chunk-scan kernel");
+  m.def("m3_tc_error", []() { return m3_tc_error(); }, "nonzero if a tcgen05 bounded wait timed out");
   m.def("tc_gemm_test", &tc_gemm_test, "tcgen05 self-test: D = A B^T in tensor memory (returns all 128 lanes)");
   m.def("dp_fused_adam", &dp_fused_adam, "fused reduce-scatter + AdamW + all-gather over peer memory");
   m.def("gen_apply", &gen_apply, "generation: decode message tokens, match, L2 and next book image");

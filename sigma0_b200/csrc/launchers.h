@@ -126,3 +126,5 @@ int dp_fused_adam_launch(const DpfArgs& a, int sms, cudaStream_t st);
 
 // tcgen05 building-block self-test (tc_test.cu)
 int tc_gemm_test_launch(const void* A, const void* B, float* D, int M, int N, int K, int* err, cudaStream_t st);
+void m3_use_tc_scan(int on);   // select the tcgen05 chunk scan
+int m3_tc_error();             // nonzero once a bounded tcgen05 wait gave up
