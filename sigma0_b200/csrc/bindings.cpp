@@ -314,13 +314,24 @@ void adam(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<
 // ---- decode / engine ----------------------------------------------------------------------
 void m3_decode_step(at::Tensor proj, int64_t nh, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias, at::Tensor Bb,
                     at::Tensor Cb, at::Tensor D, double A_floor, double eps, at::Tensor ang, at::Tensor ssm,
-                    at::Tensor kprev, at::Tensor vprev, at::Tensor y) {
+                    at::Tensor kprev, at::Tensor vprev, at::Tensor y, int64_t T) {
   req(proj, at::kBFloat16, "proj");
   req(ssm, at::kFloat, "ssm");
   req(y, at::kBFloat16, "y");
   c10::cuda::CUDAGuard guard(proj.device());
   int64_t B = proj.size(0);
-  TORCH_CHECK(ssm.numel() == B * nh * M3_P * M3_N, "state shape");
+  TORCH_CHECK(ssm.numel() * T == B * nh * M3_P * M3_N, "state shape");
+  B /= T;
+  if (T > 1) {
+    TORCH_CHECK(T <= 8, "at most 8 tokens per multi-token decode step");
+    m3_decode_multi_launch(proj.data_ptr(), (int)B, (int)T, (int)proj.size(1), (int)nh, wB.data_ptr<float>(),
+                           wC.data_ptr<float>(), dt_bias.data_ptr<float>(), Bb.data_ptr<float>(),
+                           Cb.data_ptr<float>(), D.data_ptr<float>(), (float)A_floor, (float)eps,
+                           ang.data_ptr<float>(), ssm.data_ptr<float>(), kprev.data_ptr<float>(),
+                           vprev.data_ptr<float>(), y.data_ptr(), stream());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   m3_decode_step_launch(proj.data_ptr(), (int)B, (int)proj.size(1), (int)nh, wB.data_ptr<float>(),
                         wC.data_ptr<float>(), dt_bias.data_ptr<float>(), Bb.data_ptr<float>(), Cb.data_ptr<float>(),
                         D.data_ptr<float>(), (float)A_floor, (float)eps, ang.data_ptr<float>(), ssm.data_ptr<float>(),
@@ -507,7 +518,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("sumsq", &sumsq);
   m.def("adam", &adam);
-  m.def("m3_decode_step", &m3_decode_step, "Mamba3 one-token recurrent step (states updated in place)");
+  m.def("m3_decode_step", &m3_decode_step, py::arg("proj"), py::arg("nh"), py::arg("wB"), py::arg("wC"),
+        py::arg("dt_bias"), py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("A_floor"), py::arg("eps"),
+        py::arg("ang"), py::arg("ssm"), py::arg("kprev"), py::arg("vprev"), py::arg("y"), py::arg("T") = 1,
+        "Mamba3 recurrent step over T tokens (proj rows [B*T, ldp]; states updated in place)");
   m.def("eng_process", &eng_process, "batched matching engine: apply [B, M, 8] messages, one warp per book");
   m.def("eng_l2", &eng_l2, "batched L2 extraction");
   m.def("m3_use_tc_scan", [](bool on) { m3_use_tc_scan(on ? 1 : 0); }, "select the tcgen05 chunk-scan kernel");

@@ -315,8 +315,10 @@ class Generator:
             t = torch.multinomial(torch.softmax(logits, -1), 1, generator=self._gen)[:, 0]
         self.msg[:, pos] = t
 
-    def _model_step(self, col):
-        st, h = self.model.step_hidden(self.state, self.msg[:, col:col + 1], self.book)
+    def _model_step(self, col, n=1):
+        """Advance the model over message columns col .. col+n-1 (all of them known)."""
+        book = self.book if (self.book is None or n == 1) else self.book.expand(-1, n, -1).contiguous()
+        st, h = self.model.step_hidden(self.state, self.msg[:, col:col + n], book)
         _assign_state(self.state, st)
         return h
 
@@ -332,8 +334,9 @@ class Generator:
                                   self.time)
         else:
             time_tokens_cpu(self.msg, self.tok, self.time)
-        for col in range(ts - 1, ts + 4):
-            self._model_step(col)
+        # the previous field's last token and the four computed time tokens go through
+        # the model as one 5-token step (no logits are needed for them)
+        self._model_step(ts - 1, 5)
         for pos in range(ts + 5, L):
             h = self._model_step(pos - 1)
             self._sample_into(h, pos)

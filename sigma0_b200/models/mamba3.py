@@ -134,7 +134,7 @@ class Mamba3(nn.Module):
 
     def step(self, state, u: torch.Tensor):
         """Run ``u`` (B, L, H) through the recurrence from ``state``; returns (state, out)."""
-        if self._cuda_ok(u) and u.shape[1] == 1:
+        if self._cuda_ok(u) and u.shape[1] <= 8:
             return self._step_cuda(state, u)
         proj = self.in_proj(u, dtype=self.compute_dtype)
         z, x, B, C, ADT, DT, trap, ang = self._prep(proj)
@@ -160,15 +160,17 @@ class Mamba3(nn.Module):
         return yn @ W.bf16(self.out_proj.kernel)
 
     def _step_cuda(self, state, u):
+        """1..8 tokens through the recurrence in one kernel (each head's state is read and
+        written once for all the tokens); the state tensors are updated in place."""
         from ..ops._ext import ext
         d = self.dims
-        B = u.shape[0]
-        proj = self._proj_cuda(u[:, 0])
+        B, L, H = u.shape
+        proj = self._proj_cuda(u.reshape(B * L, H))
         ang, ssm, kp, vp = state
-        y = torch.empty(B, d.d_inner, dtype=torch.bfloat16, device=u.device)
+        y = torch.empty(B * L, d.d_inner, dtype=torch.bfloat16, device=u.device)
         ext().m3_decode_step(proj, d.n_heads, self.B_norm.scale, self.C_norm.scale, self.dt_bias, self.B_bias,
-                             self.C_bias, self.D, self.A_floor, self.B_norm.eps, ang, ssm, kp, vp, y)
-        return state, self._post_cuda(y)[:, None]
+                             self.C_bias, self.D, self.A_floor, self.B_norm.eps, ang, ssm, kp, vp, y, L)
+        return state, self._post_cuda(y).view(B, L, -1)
 
     @torch.no_grad()
     def prefill(self, u: torch.Tensor):

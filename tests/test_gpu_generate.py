@@ -42,6 +42,29 @@ def test_decode_step_and_prefill_match_oracle():
     assert rel(got[:, L:], want[:, L:]) < 3e-2
 
 
+@pytest.mark.parametrize("T", [2, 5, 8])
+def test_multi_token_decode_matches_single_steps(T):
+    """One T-token recurrent step (state read/written once) == T one-token steps,
+    including the carried angle, key and value; odd head counts cover a partial
+    head group."""
+    for H in (512, 448):
+        m = _layer(H, seed=T)
+        B, L = 4, 70
+        u = torch.randn(B, L + T, H, device="cuda") * 0.5
+        with torch.no_grad():
+            st1, _ = m.prefill(u[:, :L])
+            st2 = tuple(s.clone() for s in st1)
+            ys = []
+            for t in range(T):
+                st1, y = m.step(st1, u[:, L + t:L + t + 1])
+                ys.append(y)
+            st2, y2 = m.step(st2, u[:, L:L + T])
+        y1 = torch.cat(ys, 1)
+        assert rel(y2, y1) < 1e-2, rel(y2, y1)
+        for a, b in zip(st2, st1):
+            assert rel(a, b) < 1e-4, rel(a, b)
+
+
 def _rand_engine_stream(n_books, n_msgs, seed):
     from sigma0_b200.data.synthetic import generate_day
     days = [generate_day(n_msgs, seed=seed + i) for i in range(n_books)]
