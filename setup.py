@@ -18,6 +18,8 @@ nvcc_flags = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr
                      "-Xptxas=-v" if os.environ.get("S0_PTXAS_VERBOSE") else "-Xptxas=-O3"]
 if os.environ.get("S0_CHECK"):
     nvcc_flags.append("-DS0_CHECK=1")
+if os.environ.get("S0_PHASE_PROBE"):      # per-phase clock counters in the chunk backward
+    nvcc_flags.append("-DS0_PHASE_PROBE=1")
 
 setup(
     name="sigma0_b200",

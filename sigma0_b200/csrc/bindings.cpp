@@ -311,6 +311,15 @@ void adam(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ---- profiling ---------------------------------------------------------------------------
+at::Tensor m3_phase_probe() {
+  unsigned long long v[16];
+  if (!m3_phase_probe_read(v)) return at::empty({0}, at::kLong);
+  auto t = at::empty({16}, at::kLong);
+  for (int i = 0; i < 16; ++i) t[i] = (int64_t)v[i];
+  return t;
+}
+
 // ---- decode / engine ----------------------------------------------------------------------
 void m3_decode_step(at::Tensor proj, int64_t nh, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias, at::Tensor Bb,
                     at::Tensor Cb, at::Tensor D, double A_floor, double eps, at::Tensor ang, at::Tensor ssm,
@@ -518,6 +527,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("sumsq", &sumsq);
   m.def("adam", &adam);
+  m.def("m3_phase_probe", &m3_phase_probe,
+        "chunk-backward per-phase clock sums since the last call (empty unless built with S0_PHASE_PROBE)");
   m.def("m3_decode_step", &m3_decode_step, py::arg("proj"), py::arg("nh"), py::arg("wB"), py::arg("wC"),
         py::arg("dt_bias"), py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("A_floor"), py::arg("eps"),
         py::arg("ang"), py::arg("ssm"), py::arg("kprev"), py::arg("vprev"), py::arg("y"), py::arg("T") = 1,

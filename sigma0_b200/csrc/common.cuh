@@ -24,8 +24,14 @@ S0_DEV void cp_async16(void* smem, const void* gmem, int src_bytes = 16) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem),
                "r"(src_bytes));
 }
+S0_DEV void cp_async4(void* smem, const void* gmem, int src_bytes = 4) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes));
+}
 S0_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 S0_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
+// wait until at most N of the most recently committed groups are still in flight
+template <int N>
+S0_DEV void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
 S0_DEV void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"

@@ -132,3 +132,4 @@ void m3_decode_multi_launch(const void* proj, int B, int T, int ldp, int nh, con
                             const float* dt_bias, const float* Bb, const float* Cb, const float* D, float A_floor,
                             float eps, float* ang, float* ssm, float* kprev, float* vprev, void* y,
                             cudaStream_t st);
+bool m3_phase_probe_read(unsigned long long* out);

@@ -31,7 +31,7 @@ namespace m3 {
 constexpr int CS = 64, N = 128, P = 64, R = 32;
 constexpr int LDN = N + 8;   // bf16 row stride for N-wide tiles (conflict-free ldmatrix)
 constexpr int LDP = P + 8;   // bf16 row stride for 64-wide tiles
-constexpr int RP = R + 1;    // f32 row stride for per-row angle arrays
+constexpr int RP = R + 4;    // f32 row stride for per-row angle arrays (16-byte rows; 4*row + r spreads banks)
 constexpr float PI_F = 3.14159265358979323846f;
 constexpr float TWO_PI_F = 6.28318530717958647692f;
 
@@ -53,6 +53,24 @@ struct ScanIn {
   const float* theta0; // [B, nh, nc, R] angle at each chunk start
   const float* aend;   // [B, nh, nc]    sum of ADT over each chunk
 };
+
+// Optional per-phase cycle counters of the chunk backward (built with -DS0_PHASE_PROBE):
+// thread 0 of every block adds the clock64() delta of each phase to g_bwd_phase[k].
+#ifdef S0_PHASE_PROBE
+__device__ unsigned long long g_bwd_phase[16];
+#define BWD_PHASE_START long long _tp = clock64()
+#define BWD_PHASE(k)                                                              \
+  do {                                                                            \
+    if (threadIdx.x == 0) {                                                       \
+      const long long _t = clock64();                                             \
+      atomicAdd(&g_bwd_phase[k], (unsigned long long)(_t - _tp));                 \
+      _tp = _t;                                                                   \
+    }                                                                             \
+  } while (0)
+#else
+#define BWD_PHASE_START
+#define BWD_PHASE(k)
+#endif
 
 __device__ __forceinline__ float wrap2pi(float x) { return x - TWO_PI_F * floorf(x / TWO_PI_F); }
 
@@ -220,6 +238,28 @@ __device__ __forceinline__ void load_scalars(const ScanIn& in, const Geo& g, int
   }
 }
 
+// load_scalars through cp.async (zero-filled past the sequence end), so the scalar loads
+// share one wait with the operand tiles instead of adding their own round trips.
+template <int NTH>
+__device__ __forceinline__ void load_scalars_async(const ScanIn& in, const Geo& g, int b, int h, int t0, float* sDT,
+                                                   float* sADT, float* sSig, float* sRate, int tid) {
+  const size_t base = ((size_t)b * g.nh + h) * g.L;
+  for (int i = tid; i < 3 * (CS + 1); i += NTH) {
+    const int which = i / (CS + 1), k = i % (CS + 1);
+    const int tt = t0 + k;
+    const bool ok = tt < g.L && (which < 2 || k < CS);
+    const float* src = which == 0 ? in.dt : which == 1 ? in.sig : in.adt;
+    float* dst = which == 0 ? sDT : which == 1 ? sSig : sADT;
+    if (which < 2 || k < CS) cp_async4(dst + k, src + base + (ok ? tt : 0), ok ? 4 : 0);
+  }
+  for (int i = tid; i < CS * R; i += NTH) {
+    const int r = i / R, k = i % R;
+    const int tt = t0 + r;
+    const bool ok = tt < g.L;
+    cp_async4(sRate + r * RP + k, in.rate + ((size_t)b * g.L + (ok ? tt : 0)) * R + k, ok ? 4 : 0);
+  }
+}
+
 // gamma, scale and the within-chunk inclusive cumsum of ADT (needs two warps).
 __device__ __forceinline__ void row_scalars(const float* sDT, const float* sSig, const float* sADT,
                                             float* sGam, float* sScl, float* sCum, int tid) {
@@ -263,8 +303,11 @@ __device__ __forceinline__ void chunk_angles(const float* sRate, const float* sD
 #pragma unroll
   for (int i = 0; i < RPS; ++i) {
     int row = seg * RPS + i;
+    // fast hardware sine/cosine on the angle reduced to [-pi, pi), where its absolute
+    // error is ~2^-21 (far below the bf16 rounding of the rotated operands)
+    const float th = base + sCos[row * RP + r];
     float sn, cs;
-    sincosf(wrap2pi(base + sCos[row * RP + r]), &sn, &cs);
+    __sincosf(th - TWO_PI_F * floorf(th * (1.f / TWO_PI_F) + 0.5f), &sn, &cs);
     sCos[row * RP + r] = cs;
     sSin[row * RP + r] = sn;
   }
@@ -272,58 +315,71 @@ __device__ __forceinline__ void chunk_angles(const float* sRate, const float* sD
 }
 
 // Q = rope(Cn + cb) into sQ (may alias sCn), K = rope(Bn + bb) * scale into sK (may alias sBn);
-// qkr[row] = (Cn+cb).(Bn+bb).  Either output may be skipped (nullptr).
+// qkr[row] = (Cn+cb).(Bn+bb).  Either output may be skipped (nullptr; its input and bias
+// pointers are then not read; qkr needs both).  Each thread owns
+// 8 consecutive columns of a row (16-byte loads and stores; 16 consecutive threads share
+// a row and reduce the qk dot product with shuffles); it reads its slice before writing,
+// so the in-place aliasing is safe without a barrier.
 template <int NTH>
 __device__ __forceinline__ void build_qk(const bf16* sCn, const bf16* sBn, bf16* sQ, bf16* sK, const float* sCos,
                                          const float* sSin, const float* sScl, const float* sCbv, const float* sBbv,
                                          float* sQKr, int tid) {
-  constexpr int TPR = NTH / CS;   // threads per row for the dot product (2 or 4)
-  if (sQKr) {
-    int row = tid / TPR, part = tid % TPR;
-    constexpr int W = N / TPR;
-    float s = 0.f;
-    for (int n = part * W; n < part * W + W; n += 2) {
-      float2 c = unpack_bf16(*reinterpret_cast<const uint32_t*>(sCn + row * LDN + n));
-      float2 bb = unpack_bf16(*reinterpret_cast<const uint32_t*>(sBn + row * LDN + n));
-      s += (c.x + sCbv[n]) * (bb.x + sBbv[n]) + (c.y + sCbv[n + 1]) * (bb.y + sBbv[n + 1]);
-    }
+  static_assert((CS * N / 8) % NTH == 0, "whole warps per iteration");
+  for (int i = tid; i < CS * N / 8; i += NTH) {
+    const int row = i >> 4, n0 = (i & 15) * 8;
+    const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+    const float4 zf = make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool hq = sQ != nullptr, hk = sK != nullptr;
+    const uint4 cv = hq ? *reinterpret_cast<const uint4*>(sCn + row * LDN + n0) : z4;
+    const uint4 bv = hk ? *reinterpret_cast<const uint4*>(sBn + row * LDN + n0) : z4;
+    const float4 cb0 = hq ? *reinterpret_cast<const float4*>(sCbv + n0) : zf;
+    const float4 cb1 = hq ? *reinterpret_cast<const float4*>(sCbv + n0 + 4) : zf;
+    const float4 bb0 = hk ? *reinterpret_cast<const float4*>(sBbv + n0) : zf;
+    const float4 bb1 = hk ? *reinterpret_cast<const float4*>(sBbv + n0 + 4) : zf;
+    const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+    const float cbs[8] = {cb0.x, cb0.y, cb0.z, cb0.w, cb1.x, cb1.y, cb1.z, cb1.w};
+    const float bbs[8] = {bb0.x, bb0.y, bb0.z, bb0.w, bb1.x, bb1.y, bb1.z, bb1.w};
+    float cq[8], bk[8];
+    float qk = 0.f;
 #pragma unroll
-    for (int o = 1; o < TPR; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (part == 0) sQKr[row] = s;
-    __syncthreads();
-  }
-  {
-    constexpr int NSEG = NTH / 32, RPS = CS / NSEG;
-    int r = tid & 31, seg = tid >> 5;
-    for (int i = 0; i < RPS; ++i) {
-      int row = seg * RPS + i;
-      const float sn = sSin[row * RP + r], cs = sCos[row * RP + r];
-      if (sQ) {
-        float2 c = unpack_bf16(*reinterpret_cast<const uint32_t*>(sCn + row * LDN + 2 * r));
-        float c0 = c.x + sCbv[2 * r], c1 = c.y + sCbv[2 * r + 1];
-        *reinterpret_cast<uint32_t*>(sQ + row * LDN + 2 * r) = pack_bf16(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
-      }
-      if (sK) {
-        float2 bb = unpack_bf16(*reinterpret_cast<const uint32_t*>(sBn + row * LDN + 2 * r));
-        float b0 = bb.x + sBbv[2 * r], b1 = bb.y + sBbv[2 * r + 1];
-        float sc = sScl[row];
-        *reinterpret_cast<uint32_t*>(sK + row * LDN + 2 * r) =
-            pack_bf16((b0 * cs - b1 * sn) * sc, (b0 * sn + b1 * cs) * sc);
+    for (int k = 0; k < 4; ++k) {
+      const float2 c2 = unpack_bf16(cw[k]), b2 = unpack_bf16(bw[k]);
+      cq[2 * k] = c2.x + cbs[2 * k];
+      cq[2 * k + 1] = c2.y + cbs[2 * k + 1];
+      bk[2 * k] = b2.x + bbs[2 * k];
+      bk[2 * k + 1] = b2.y + bbs[2 * k + 1];
+      qk += cq[2 * k] * bk[2 * k] + cq[2 * k + 1] * bk[2 * k + 1];
+    }
+    if (sQKr) {
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) qk += __shfl_xor_sync(0xffffffffu, qk, o);
+      if ((i & 15) == 0) sQKr[row] = qk;
+    }
+    if (n0 < 2 * R) {
+      const float4 cs4 = *reinterpret_cast<const float4*>(sCos + row * RP + n0 / 2);
+      const float4 sn4 = *reinterpret_cast<const float4*>(sSin + row * RP + n0 / 2);
+      const float css[4] = {cs4.x, cs4.y, cs4.z, cs4.w}, sns[4] = {sn4.x, sn4.y, sn4.z, sn4.w};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float c0 = cq[2 * m], c1 = cq[2 * m + 1], b0 = bk[2 * m], b1 = bk[2 * m + 1];
+        cq[2 * m] = c0 * css[m] - c1 * sns[m];
+        cq[2 * m + 1] = c0 * sns[m] + c1 * css[m];
+        bk[2 * m] = b0 * css[m] - b1 * sns[m];
+        bk[2 * m + 1] = b0 * sns[m] + b1 * css[m];
       }
     }
-  }
-  for (int i = tid; i < CS * (N - 2 * R) / 2; i += NTH) {
-    int row = i / ((N - 2 * R) / 2);
-    int n = 2 * R + 2 * (i % ((N - 2 * R) / 2));
     if (sQ) {
-      float2 c = unpack_bf16(*reinterpret_cast<const uint32_t*>(sCn + row * LDN + n));
-      *reinterpret_cast<uint32_t*>(sQ + row * LDN + n) = pack_bf16(c.x + sCbv[n], c.y + sCbv[n + 1]);
+      uint4 o;
+      o.x = pack_bf16(cq[0], cq[1]); o.y = pack_bf16(cq[2], cq[3]);
+      o.z = pack_bf16(cq[4], cq[5]); o.w = pack_bf16(cq[6], cq[7]);
+      *reinterpret_cast<uint4*>(sQ + row * LDN + n0) = o;
     }
     if (sK) {
-      float2 bb = unpack_bf16(*reinterpret_cast<const uint32_t*>(sBn + row * LDN + n));
-      float sc = sScl[row];
-      *reinterpret_cast<uint32_t*>(sK + row * LDN + n) =
-          pack_bf16((bb.x + sBbv[n]) * sc, (bb.y + sBbv[n + 1]) * sc);
+      const float sc = sScl[row];
+      uint4 o;
+      o.x = pack_bf16(bk[0] * sc, bk[1] * sc); o.y = pack_bf16(bk[2] * sc, bk[3] * sc);
+      o.z = pack_bf16(bk[4] * sc, bk[5] * sc); o.w = pack_bf16(bk[6] * sc, bk[7] * sc);
+      *reinterpret_cast<uint4*>(sK + row * LDN + n0) = o;
     }
   }
   __syncthreads();
@@ -393,7 +449,7 @@ __global__ void __launch_bounds__(128) m3_pass(bf16* __restrict__ buf, const flo
 
 // F2: per-chunk state contribution S_c[p][n] = sum_s w_s V[s][p] K[s][n]   (256 threads)
 constexpr size_t STATE_SMEM = sizeof(bf16) * (CS * LDN + 2 * CS * LDP) +
-                              sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 5 * CS + N + 8 * 32 + 32);
+                              sizeof(float) * (2 * CS * RP + 2 * (CS + 4) + 5 * CS + N + 8 * 32 + 32);
 
 __global__ void __launch_bounds__(256) m3_chunk_state(ScanIn in, Geo g, bf16* __restrict__ states) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -403,8 +459,8 @@ __global__ void __launch_bounds__(256) m3_chunk_state(ScanIn in, Geo g, bf16* __
   float* sSin = reinterpret_cast<float*>(sVd + CS * LDP);   // rates, then sin table
   float* sCos = sSin + CS * RP;
   float* sDT = sCos + CS * RP;
-  float* sSig = sDT + CS + 1;
-  float* sADT = sSig + CS + 1;
+  float* sSig = sDT + CS + 4;   // CS + 1 used; padded to keep later arrays 16-byte aligned
+  float* sADT = sSig + CS + 4;
   float* sCum = sADT + CS;
   float* sGam = sCum + CS;
   float* sScl = sGam + CS;
@@ -467,7 +523,7 @@ __global__ void __launch_bounds__(256) m3_chunk_state(ScanIn in, Geo g, bf16* __
 // F4: chunk scan -> gated y  (256 threads: rows rb, 32-column halves cg)
 // ---------------------------------------------------------------------------
 constexpr size_t SCAN_SMEM = sizeof(bf16) * (3 * CS * LDN + 3 * CS * LDP) +
-                             sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 5 * CS + 2 * N + 8 * 32 + 32);
+                             sizeof(float) * (2 * CS * RP + 2 * (CS + 4) + 5 * CS + 2 * N + 8 * 32 + 32);
 
 __global__ void __launch_bounds__(256)
     m3_chunk_scan(ScanIn in, Geo g, const bf16* __restrict__ states, bf16* __restrict__ y) {
@@ -481,8 +537,8 @@ __global__ void __launch_bounds__(256)
   float* sSin = reinterpret_cast<float*>(sP + CS * LDP);
   float* sCos = sSin + CS * RP;
   float* sDT = sCos + CS * RP;
-  float* sSig = sDT + CS + 1;
-  float* sADT = sSig + CS + 1;
+  float* sSig = sDT + CS + 4;   // CS + 1 used; padded to keep later arrays 16-byte aligned
+  float* sADT = sSig + CS + 4;
   float* sCum = sADT + CS;
   float* sGam = sCum + CS;
   float* sScl = sGam + CS;
@@ -677,7 +733,7 @@ __device__ __forceinline__ void build_qk_swz(unsigned char* tQ, unsigned char* t
 
 constexpr size_t TSCAN_TILES = 3 * 16384 + 2 * 8192;     // Q, K, S_in (N-wide) + V^T, P
 constexpr size_t TSCAN_SMEM = 1024 + TSCAN_TILES + sizeof(bf16) * (2 * CS * LDP) +
-                              sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 5 * CS + 2 * N + 8 * 32 + 32);
+                              sizeof(float) * (2 * CS * RP + 2 * (CS + 4) + 5 * CS + 2 * N + 8 * 32 + 32);
 
 __global__ void __launch_bounds__(256, 2)
     m3_chunk_scan_tc(ScanIn in, Geo g, const bf16* __restrict__ states, bf16* __restrict__ y) {
@@ -696,8 +752,8 @@ __global__ void __launch_bounds__(256, 2)
   float* sSin = reinterpret_cast<float*>(sZ + CS * LDP);
   float* sCos = sSin + CS * RP;
   float* sDT = sCos + CS * RP;
-  float* sSig = sDT + CS + 1;
-  float* sADT = sSig + CS + 1;
+  float* sSig = sDT + CS + 4;   // CS + 1 used; padded to keep later arrays 16-byte aligned
+  float* sADT = sSig + CS + 4;
   float* sCum = sADT + CS;
   float* sGam = sCum + CS;
   float* sScl = sGam + CS;
@@ -830,7 +886,7 @@ __global__ void __launch_bounds__(256, 2)
 // dY0 = dy * silu(z)  (256 threads: p rows rb, n halves cg)
 // ---------------------------------------------------------------------------
 constexpr size_t DST_SMEM = sizeof(bf16) * (CS * LDN + 2 * CS * LDP) +
-                            sizeof(float) * (2 * CS * RP + 2 * (CS + 1) + 4 * CS + N + 8 * 32 + 32);
+                            sizeof(float) * (2 * CS * RP + 2 * (CS + 4) + 4 * CS + N + 8 * 32 + 32);
 
 __global__ void __launch_bounds__(256)
     m3_chunk_dstate(ScanIn in, Geo g, const bf16* __restrict__ dy, bf16* __restrict__ U) {
@@ -841,8 +897,8 @@ __global__ void __launch_bounds__(256)
   float* sSin = reinterpret_cast<float*>(sdY + CS * LDP);
   float* sCos = sSin + CS * RP;
   float* sDT = sCos + CS * RP;
-  float* sSig = sDT + CS + 1;
-  float* sADT = sSig + CS + 1;
+  float* sSig = sDT + CS + 4;   // CS + 1 used; padded to keep later arrays 16-byte aligned
+  float* sADT = sSig + CS + 4;
   float* sCum = sADT + CS;
   float* sGam = sCum + CS;
   float* sScl = sGam + CS;
@@ -915,7 +971,7 @@ struct BwdOut {
 
 constexpr int BWD_NT = 512;
 constexpr size_t BWD_SMEM = sizeof(bf16) * (5 * CS * LDN + 5 * CS * LDP) +
-                            sizeof(float) * (3 * CS * RP + 2 * (CS + 1) + 9 * CS + 4 * N + 16 * 32 + 32 + 16 +
+                            sizeof(float) * (3 * CS * RP + 2 * (CS + 4) + 9 * CS + 4 * N + 16 * 32 + 32 + 16 +
                                              16);
 
 __global__ void __launch_bounds__(BWD_NT, 1)
@@ -936,8 +992,8 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   float* sCos = sSin + CS * RP;
   float* sDth = sCos + CS * RP;
   float* sDT = sDth + CS * RP;
-  float* sSig = sDT + CS + 1;
-  float* sADT = sSig + CS + 1;
+  float* sSig = sDT + CS + 4;   // CS + 1 used; padded to keep later arrays 16-byte aligned
+  float* sADT = sSig + CS + 4;
   float* sCum = sADT + CS;
   float* sGam = sCum + CS;
   float* sScl = sGam + CS;
@@ -955,6 +1011,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   float* sMisc = sTh0 + 32;      // [16]
   float* sDD = sMisc + 16;       // [16]
 
+  BWD_PHASE_START;
   const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
   const int rb = warp & 3, cq = warp >> 2;
@@ -963,6 +1020,16 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   const size_t bh = (size_t)b * g.nh + h;
   const bf16* bcb = in.bc + (size_t)b * g.L * 2 * N;
   const bf16* pb = in.proj + (size_t)b * g.L * g.ldp;
+  // group 1: the per-row scalars, rates, biases and the chunk's start angle (small);
+  // group 2: the operand tiles.  The angle and decay prologue runs on group 1 while
+  // group 2 is still in flight.
+  load_scalars_async<BWD_NT>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
+  for (int i = tid; i < 2 * N + R; i += BWD_NT) {   // 4-byte copies: these arrays are only 4-byte aligned
+    if (i < N) cp_async4(sCbv + i, in.Cb + h * N + i);
+    else if (i < 2 * N) cp_async4(sBbv + i - N, in.Bb + h * N + i - N);
+    else cp_async4(sTh0 + i - 2 * N, in.theta0 + (bh * g.nc + c) * R + i - 2 * N);
+  }
+  cp_async_commit();
   load_rows<BWD_NT>(bcb, 2 * N, 0, N, sBn, LDN, t0, g.L, tid);
   load_rows<BWD_NT>(bcb, 2 * N, N, N, sQ, LDN, t0, g.L, tid);
   load_rows<BWD_NT>(pb, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
@@ -978,42 +1045,26 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     }
   }
   cp_async_commit();
-  load_scalars<BWD_NT>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
   for (int i = tid; i < N; i += BWD_NT) {
-    sCbv[i] = in.Cb[h * N + i];
-    sBbv[i] = in.Bb[h * N + i];
     sDcb[i] = 0.f;
     sDbb[i] = 0.f;
   }
   if (tid < CS) { sDqk[tid] = 0.f; sDcum[tid] = 0.f; sDscl[tid] = 0.f; }
-  if (tid < 32) sTh0[tid] = in.theta0[(bh * g.nc + c) * R + tid];
+  cp_async_wait_group<1>();
+  __syncthreads();
+  BWD_PHASE(0);
+  row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
+  BWD_PHASE(8);
+  chunk_angles<BWD_NT>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
   cp_async_wait_all();
   __syncthreads();
-  row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
-  chunk_angles<BWD_NT>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
+  BWD_PHASE(9);
   build_qk<BWD_NT>(sQ, sBn, sQ, sK, sCos, sSin, sScl, sCbv, sBbv, sQKr, tid);
+  BWD_PHASE(10);
   const float cend = sCum[CS - 1];
   if (tid < CS) sW[tid] = __expf(cend - sCum[tid]);
-  {   // d cum_end: sum(dS_out * S_out), S_out = S_in of the next chunk (no gradient past the last)
-    float dot = 0.f;
-    if (c + 1 < g.nc) {
-      const bf16* so = states + state_off(g, b, h, c + 1);
-      for (int i = tid; i < P * N / 8; i += BWD_NT) {
-        int r = i / (N / 8), ch = i % (N / 8);
-        uint4 sv = *reinterpret_cast<const uint4*>(so + r * N + ch * 8);
-        uint4 dv = *reinterpret_cast<const uint4*>(sdSt + r * LDN + ch * 8);
-        uint32_t a[4] = {sv.x, sv.y, sv.z, sv.w}, d[4] = {dv.x, dv.y, dv.z, dv.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          float2 x = unpack_bf16(a[k]), y2 = unpack_bf16(d[k]);
-          dot += x.x * y2.x + x.y * y2.y;
-        }
-      }
-    }
-    dot = warp_sum(dot);
-    if (lane == 0) sMisc[warp] = dot;
-  }
   __syncthreads();
+  BWD_PHASE(1);
 
   const int r0 = m0 + gq, r1 = r0 + 8;
   const float cum0 = sCum[r0], cum1 = sCum[r1];
@@ -1105,6 +1156,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     }
   }
   __syncthreads();   // sdY (dY0) complete
+  BWD_PHASE(2);
   // ---- B: dP = dY0 V^T (cols c16..) -> dS, G = dP * P ------------------------------------
   {
     float dsacc[2][4];
@@ -1152,6 +1204,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     }
   }
   __syncthreads();   // sdS complete
+  BWD_PHASE(3);
   // ---- C: dQ = exp(cum_l) dY0 S_in + dS K  (cols c32..) -> gQ, dtheta, dC_bias ---------
   {
     float qacc[4][4];
@@ -1230,6 +1283,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
       }
     }
   }
+  BWD_PHASE(7);
   // ---- D: dK = w_s (V dS_out) + dS^T Q  (cols c32..) -> gK, dscale, dtheta, dB_bias ------
   {
     float kacc[4][4];
@@ -1329,6 +1383,17 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     }
   }
   __syncthreads();   // every warp done reading sX (V) as an MMA operand
+  BWD_PHASE(4);
+  // the next chunk's input state (S_out of this chunk), for d cum_end after E
+  uint4 nsv[P * N / 8 / BWD_NT];
+  if (c + 1 < g.nc) {
+    const bf16* so = states + state_off(g, b, h, c + 1);
+#pragma unroll
+    for (int k = 0; k < P * N / 8 / BWD_NT; ++k) {
+      const int i = tid + k * BWD_NT;
+      nsv[k] = *reinterpret_cast<const uint4*>(so + (i / (N / 8)) * N + (i % (N / 8)) * 8);
+    }
+  }
   // ---- E: dV = w_s (K dS_out^T) + P^T dY0 + (D+qk) dY0  (cols c16..) ------------------
   {
     float vacc2[2][4];
@@ -1378,12 +1443,33 @@ __global__ void __launch_bounds__(BWD_NT, 1)
           pack_bf16(vacc2[nt][2] + q1 * d1.x, vacc2[nt][3] + q1 * d1.y);
     }
   }
+  {   // d cum_end: sum(dS_out * S_out), S_out = S_in of the next chunk (no gradient past the last)
+    float dot = 0.f;
+    if (c + 1 < g.nc) {
+#pragma unroll
+      for (int kq = 0; kq < P * N / 8 / BWD_NT; ++kq) {
+        const int i = tid + kq * BWD_NT;
+        const int r = i / (N / 8), ch = i % (N / 8);
+        const uint4 sv = nsv[kq];
+        const uint4 dv = *reinterpret_cast<const uint4*>(sdSt + r * LDN + ch * 8);
+        const uint32_t a[4] = {sv.x, sv.y, sv.z, sv.w}, d[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 x = unpack_bf16(a[k]), y2 = unpack_bf16(d[k]);
+          dot += x.x * y2.x + x.y * y2.y;
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) sMisc[warp] = dot;
+  }
   // ---- F: reductions and stores ------------------------------------------------------------
   {
     float dd = warp_sum(dD_acc);
     if (lane == 0) sDD[warp] = dd;
   }
   __syncthreads();   // all shared atomics done; sX holds dV, sZ holds dz
+  BWD_PHASE(5);
   if (tid == 0) {
     float dot = 0.f, s = 0.f;
     for (int k = 0; k < BWD_NT / 32; ++k) { dot += sMisc[k]; s += sDD[k]; }
@@ -1453,6 +1539,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     out.dCb[(bh * g.nc + c) * N + i] = sDcb[i];
     out.dBb[(bh * g.nc + c) * N + i] = sDbb[i];
   }
+  BWD_PHASE(6);
 }
 
 // ---------------------------------------------------------------------------
@@ -1703,4 +1790,18 @@ void m3_prep_bwd_launch(const M3Geo& G, const void* proj, const float* wB, const
                                       reinterpret_cast<const bf16*>(gQ), reinterpret_cast<const bf16*>(gK),
                                       dthl, dthc, dgam, dscl, dadt, reinterpret_cast<bf16*>(dproj), dwB, dwC,
                                       ddt_bias);
+}
+
+// copies the chunk-backward phase counters to out[16] and clears them; false when the
+// library was built without -DS0_PHASE_PROBE
+bool m3_phase_probe_read(unsigned long long* out) {
+#ifdef S0_PHASE_PROBE
+  cudaMemcpyFromSymbol(out, s0::m3::g_bwd_phase, sizeof(unsigned long long) * 16);
+  static const unsigned long long zeros[16] = {};
+  cudaMemcpyToSymbol(s0::m3::g_bwd_phase, zeros, sizeof(zeros));
+  return true;
+#else
+  (void)out;
+  return false;
+#endif
 }
