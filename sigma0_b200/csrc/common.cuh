@@ -102,7 +102,10 @@ S0_DEV void acc_to_a(uint32_t* a, const float* c0, const float* c1) {
   a[3] = pack_bf16(c1[2], c1[3]);
 }
 
-S0_DEV float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
+// fast division (__fdividef): the IEEE-exact division is a multi-instruction sequence and
+// the logistic's operand is >= 1, where the fast form is within 2 ulp (and gives 0 for
+// an infinite exponential)
+S0_DEV float sigmoidf_(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 S0_DEV float softplusf_(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 S0_DEV float warp_sum(float v) {

@@ -970,7 +970,7 @@ struct BwdOut {
 };
 
 constexpr int BWD_NT = 512;
-constexpr size_t BWD_SMEM = sizeof(bf16) * (5 * CS * LDN + 5 * CS * LDP) +
+constexpr size_t BWD_SMEM = sizeof(bf16) * (5 * CS * LDN + 6 * CS * LDP) +
                             sizeof(float) * (3 * CS * RP + 2 * (CS + 4) + 9 * CS + 4 * N + 16 * 32 + 32 + 16 +
                                              16);
 
@@ -988,7 +988,8 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   bf16* sdY = sZ + CS * LDP;                  // dy -> dY0
   bf16* sP = sdY + CS * LDP;
   bf16* sdS = sP + CS * LDP;
-  float* sSin = reinterpret_cast<float*>(sdS + CS * LDP);
+  bf16* sdY0 = sdS + CS * LDP;                // dY0 = dy * silu(z)
+  float* sSin = reinterpret_cast<float*>(sdY0 + CS * LDP);
   float* sCos = sSin + CS * RP;
   float* sDth = sCos + CS * RP;
   float* sDT = sDth + CS * RP;
@@ -1015,7 +1016,10 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
   const int rb = warp & 3, cq = warp >> 2;
-  const int c16 = cq * 16, c32 = cq * 32;
+  // 64-wide outputs: columns c16..c16+15; 128-wide outputs (dQ, dK): the 16-column
+  // blocks cq and cq + 4, so every warp has one block inside the rotated half (n < 2R)
+  // and one outside it and the rotation work is spread evenly
+  const int c16 = cq * 16;
   const int t0 = c * CS, m0 = rb * 16;
   const size_t bh = (size_t)b * g.nh + h;
   const bf16* bcb = in.bc + (size_t)b * g.L * 2 * N;
@@ -1049,7 +1053,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     sDcb[i] = 0.f;
     sDbb[i] = 0.f;
   }
-  if (tid < CS) { sDqk[tid] = 0.f; sDcum[tid] = 0.f; sDscl[tid] = 0.f; }
+  if (tid < CS) { sDcum[tid] = 0.f; sDscl[tid] = 0.f; }
   cp_async_wait_group<1>();
   __syncthreads();
   BWD_PHASE(0);
@@ -1059,6 +1063,30 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   cp_async_wait_all();
   __syncthreads();
   BWD_PHASE(9);
+  // dY0 = dy * silu(z) and the qk-diagonal row sums dqk[row] = sum_p dY0 * V (they need
+  // no GEMM): one 8-column slice per thread, 8 threads per row
+  for (int i = tid; i < CS * P / 8; i += BWD_NT) {
+    const int row = i >> 3, p0 = (i & 7) * 8;
+    const uint4 dv = *reinterpret_cast<const uint4*>(sdY + row * LDP + p0);
+    const uint4 zv = *reinterpret_cast<const uint4*>(sZ + row * LDP + p0);
+    const uint4 xv = *reinterpret_cast<const uint4*>(sX + row * LDP + p0);
+    const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t ow[4];
+    float dq = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 d2 = unpack_bf16(dw[k]), z2 = unpack_bf16(zw[k]), x2 = unpack_bf16(xw[k]);
+      const float a0 = d2.x * z2.x * sigmoidf_(z2.x), a1 = d2.y * z2.y * sigmoidf_(z2.y);
+      dq += a0 * x2.x + a1 * x2.y;
+      ow[k] = pack_bf16(a0, a1);
+    }
+    *reinterpret_cast<uint4*>(sdY0 + row * LDP + p0) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    dq += __shfl_xor_sync(0xffffffffu, dq, 1);
+    dq += __shfl_xor_sync(0xffffffffu, dq, 2);
+    dq += __shfl_xor_sync(0xffffffffu, dq, 4);
+    if ((i & 7) == 0) sDqk[row] = dq;
+  }
   build_qk<BWD_NT>(sQ, sBn, sQ, sK, sCos, sSin, sScl, sCbv, sBbv, sQKr, tid);
   BWD_PHASE(10);
   const float cend = sCum[CS - 1];
@@ -1071,101 +1099,31 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   const float e0 = __expf(cum0), e1 = __expf(cum1);
   const float Dh = in.D[h];
   const float q0 = Dh + sQKr[r0] * sGam[r0], q1 = Dh + sQKr[r1] * sGam[r1];
-  float dD_acc = 0.f;
 
-  // ---- A: P (cols c16..), Y_off, then P V; dY0, dz --------------------------------------
-  float pacc[2][4], yacc[2][4];
-#pragma unroll
-  for (int i = 0; i < 2; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) pacc[i][e] = yacc[i][e] = 0.f;
-#pragma unroll
-  for (int kk = 0; kk < N / 16; ++kk) {
-    uint32_t a[4], bb[4];
-    load_a(a, sQ, LDN, m0, kk * 16, lane);
-    load_b_nk(bb, sK, LDN, c16, kk * 16, lane);
-    mma_bf16(pacc[0], a, bb[0], bb[1]);
-    mma_bf16(pacc[1], a, bb[2], bb[3]);
-    load_b_nk(bb, sSt, LDN, c16, kk * 16, lane);
-    mma_bf16(yacc[0], a, bb[0], bb[1]);
-    mma_bf16(yacc[1], a, bb[2], bb[3]);
-  }
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    int s0c = c16 + nt * 8 + 2 * tq;
-    float cs0 = sCum[s0c], cs1 = sCum[s0c + 1];
-    pacc[nt][0] = (s0c < r0) ? pacc[nt][0] * __expf(cum0 - cs0) : 0.f;
-    pacc[nt][1] = (s0c + 1 < r0) ? pacc[nt][1] * __expf(cum0 - cs1) : 0.f;
-    pacc[nt][2] = (s0c < r1) ? pacc[nt][2] * __expf(cum1 - cs0) : 0.f;
-    pacc[nt][3] = (s0c + 1 < r1) ? pacc[nt][3] * __expf(cum1 - cs1) : 0.f;
-    yacc[nt][0] *= e0; yacc[nt][1] *= e0; yacc[nt][2] *= e1; yacc[nt][3] *= e1;
-    *reinterpret_cast<uint32_t*>(sP + r0 * LDP + s0c) = pack_bf16(pacc[nt][0], pacc[nt][1]);
-    *reinterpret_cast<uint32_t*>(sP + r1 * LDP + s0c) = pack_bf16(pacc[nt][2], pacc[nt][3]);
-  }
-  __syncthreads();
+  // ---- A: P = masked QK^T, Y_off = Q S_in^T and dP = dY0 V^T on one (rows, cols c16..)
+  // tile per warp; P and dS = dP * decay go to shared memory, G = dP * P feeds d cum --------
+  float yacc[2][4];
   {
-    float vacc[2][4];
+    float pacc[2][4], dsacc[2][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) vacc[i][0] = vacc[i][1] = vacc[i][2] = vacc[i][3] = 0.f;
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-    for (int kk = 0; kk < CS / 16; ++kk) {
+      for (int e = 0; e < 4; ++e) pacc[i][e] = yacc[i][e] = dsacc[i][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < N / 16; ++kk) {
       uint32_t a[4], bb[4];
-      load_a(a, sP, LDP, m0, kk * 16, lane);
-      load_b_kn(bb, sX, LDP, c16, kk * 16, lane);
-      mma_bf16(vacc[0], a, bb[0], bb[1]);
-      mma_bf16(vacc[1], a, bb[2], bb[3]);
+      load_a(a, sQ, LDN, m0, kk * 16, lane);
+      load_b_nk(bb, sK, LDN, c16, kk * 16, lane);
+      mma_bf16(pacc[0], a, bb[0], bb[1]);
+      mma_bf16(pacc[1], a, bb[2], bb[3]);
+      load_b_nk(bb, sSt, LDN, c16, kk * 16, lane);
+      mma_bf16(yacc[0], a, bb[0], bb[1]);
+      mma_bf16(yacc[1], a, bb[2], bb[3]);
     }
-    float dq0 = 0.f, dq1 = 0.f, dc0 = 0.f, dc1 = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      int p = c16 + nt * 8 + 2 * tq;
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        int row = hr ? r1 : r0;
-        float qd = hr ? q1 : q0;
-        float2 v = unpack_bf16(*reinterpret_cast<const uint32_t*>(sX + row * LDP + p));
-        float2 z = unpack_bf16(*reinterpret_cast<const uint32_t*>(sZ + row * LDP + p));
-        float2 d = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdY + row * LDP + p));
-        float vv[2] = {v.x, v.y}, zz[2] = {z.x, z.y}, dd[2] = {d.x, d.y}, o[2], dz[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          int k = hr * 2 + e;
-          float yo = yacc[nt][k];
-          float y0 = vacc[nt][k] + yo + qd * vv[e];
-          float sg = sigmoidf_(zz[e]);
-          float dy0 = dd[e] * zz[e] * sg;
-          dz[e] = dd[e] * y0 * sg * (1.f + zz[e] * (1.f - sg));
-          o[e] = dy0;
-          if (hr) { dq1 += dy0 * vv[e]; dc1 += dy0 * yo; }
-          else { dq0 += dy0 * vv[e]; dc0 += dy0 * yo; }
-        }
-        *reinterpret_cast<uint32_t*>(sdY + row * LDP + p) = pack_bf16(o[0], o[1]);
-        *reinterpret_cast<uint32_t*>(sZ + row * LDP + p) = pack_bf16(dz[0], dz[1]);
-      }
-    }
-    dq0 += __shfl_xor_sync(0xffffffffu, dq0, 1); dq0 += __shfl_xor_sync(0xffffffffu, dq0, 2);
-    dq1 += __shfl_xor_sync(0xffffffffu, dq1, 1); dq1 += __shfl_xor_sync(0xffffffffu, dq1, 2);
-    dc0 += __shfl_xor_sync(0xffffffffu, dc0, 1); dc0 += __shfl_xor_sync(0xffffffffu, dc0, 2);
-    dc1 += __shfl_xor_sync(0xffffffffu, dc1, 1); dc1 += __shfl_xor_sync(0xffffffffu, dc1, 2);
-    if (tq == 0) {
-      atomicAdd(&sDqk[r0], dq0);
-      atomicAdd(&sDqk[r1], dq1);
-      atomicAdd(&sDcum[r0], dc0);
-      atomicAdd(&sDcum[r1], dc1);
-      dD_acc += dq0 + dq1;
-    }
-  }
-  __syncthreads();   // sdY (dY0) complete
-  BWD_PHASE(2);
-  // ---- B: dP = dY0 V^T (cols c16..) -> dS, G = dP * P ------------------------------------
-  {
-    float dsacc[2][4];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) dsacc[i][0] = dsacc[i][1] = dsacc[i][2] = dsacc[i][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < P / 16; ++kk) {
       uint32_t a[4], bb[4];
-      load_a(a, sdY, LDP, m0, kk * 16, lane);
+      load_a(a, sdY0, LDP, m0, kk * 16, lane);
       load_b_nk(bb, sX, LDP, c16, kk * 16, lane);
       mma_bf16(dsacc[0], a, bb[0], bb[1]);
       mma_bf16(dsacc[1], a, bb[2], bb[3]);
@@ -1173,14 +1131,19 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      int s0c = c16 + nt * 8 + 2 * tq;
-      float cs0 = sCum[s0c], cs1 = sCum[s0c + 1];
-      float f00 = (s0c < r0) ? __expf(cum0 - cs0) : 0.f;
-      float f01 = (s0c + 1 < r0) ? __expf(cum0 - cs1) : 0.f;
-      float f10 = (s0c < r1) ? __expf(cum1 - cs0) : 0.f;
-      float f11 = (s0c + 1 < r1) ? __expf(cum1 - cs1) : 0.f;
-      float g00 = dsacc[nt][0] * pacc[nt][0], g01 = dsacc[nt][1] * pacc[nt][1];
-      float g10 = dsacc[nt][2] * pacc[nt][2], g11 = dsacc[nt][3] * pacc[nt][3];
+      const int s0c = c16 + nt * 8 + 2 * tq;
+      const float cs0 = sCum[s0c], cs1 = sCum[s0c + 1];
+      const float f00 = (s0c < r0) ? __expf(cum0 - cs0) : 0.f;
+      const float f01 = (s0c + 1 < r0) ? __expf(cum0 - cs1) : 0.f;
+      const float f10 = (s0c < r1) ? __expf(cum1 - cs0) : 0.f;
+      const float f11 = (s0c + 1 < r1) ? __expf(cum1 - cs1) : 0.f;
+      const float p00 = pacc[nt][0] * f00, p01 = pacc[nt][1] * f01;
+      const float p10 = pacc[nt][2] * f10, p11 = pacc[nt][3] * f11;
+      yacc[nt][0] *= e0; yacc[nt][1] *= e0; yacc[nt][2] *= e1; yacc[nt][3] *= e1;
+      *reinterpret_cast<uint32_t*>(sP + r0 * LDP + s0c) = pack_bf16(p00, p01);
+      *reinterpret_cast<uint32_t*>(sP + r1 * LDP + s0c) = pack_bf16(p10, p11);
+      const float g00 = dsacc[nt][0] * p00, g01 = dsacc[nt][1] * p01;
+      const float g10 = dsacc[nt][2] * p10, g11 = dsacc[nt][3] * p11;
       rs0 += g00 + g01;
       rs1 += g10 + g11;
       float ca = g00 + g10, cb = g01 + g11;
@@ -1203,9 +1166,56 @@ __global__ void __launch_bounds__(BWD_NT, 1)
       atomicAdd(&sDcum[r1], rs1);
     }
   }
-  __syncthreads();   // sdS complete
+  __syncthreads();   // sP, sdS complete
+  BWD_PHASE(2);
+  // ---- B: y0 = P V + Y_off + (D + qk) V -> dz (into sZ); d cum from dY0 . Y_off ---------
+  {
+    float vacc[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) vacc[i][0] = vacc[i][1] = vacc[i][2] = vacc[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < CS / 16; ++kk) {
+      uint32_t a[4], bb[4];
+      load_a(a, sP, LDP, m0, kk * 16, lane);
+      load_b_kn(bb, sX, LDP, c16, kk * 16, lane);
+      mma_bf16(vacc[0], a, bb[0], bb[1]);
+      mma_bf16(vacc[1], a, bb[2], bb[3]);
+    }
+    float dc0 = 0.f, dc1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int p = c16 + nt * 8 + 2 * tq;
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int row = hr ? r1 : r0;
+        const float qd = hr ? q1 : q0;
+        const float2 v = unpack_bf16(*reinterpret_cast<const uint32_t*>(sX + row * LDP + p));
+        const float2 z = unpack_bf16(*reinterpret_cast<const uint32_t*>(sZ + row * LDP + p));
+        const float2 d = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdY + row * LDP + p));
+        const float vv[2] = {v.x, v.y}, zz[2] = {z.x, z.y}, dd[2] = {d.x, d.y};
+        float dz[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int k = hr * 2 + e;
+          const float yo = yacc[nt][k];
+          const float y0 = vacc[nt][k] + yo + qd * vv[e];
+          const float sg = sigmoidf_(zz[e]);
+          dz[e] = dd[e] * y0 * sg * (1.f + zz[e] * (1.f - sg));
+          const float dy0 = dd[e] * zz[e] * sg;
+          if (hr) dc1 += dy0 * yo; else dc0 += dy0 * yo;
+        }
+        *reinterpret_cast<uint32_t*>(sZ + row * LDP + p) = pack_bf16(dz[0], dz[1]);
+      }
+    }
+    dc0 += __shfl_xor_sync(0xffffffffu, dc0, 1); dc0 += __shfl_xor_sync(0xffffffffu, dc0, 2);
+    dc1 += __shfl_xor_sync(0xffffffffu, dc1, 1); dc1 += __shfl_xor_sync(0xffffffffu, dc1, 2);
+    if (tq == 0) {
+      atomicAdd(&sDcum[r0], dc0);
+      atomicAdd(&sDcum[r1], dc1);
+    }
+  }
   BWD_PHASE(3);
-  // ---- C: dQ = exp(cum_l) dY0 S_in + dS K  (cols c32..) -> gQ, dtheta, dC_bias ---------
+  // ---- C: dQ = exp(cum_l) dY0 S_in + dS K  (cols cq*16.. and cq*16+64..) -> gQ, dtheta, dC_bias ---------
   {
     float qacc[4][4];
 #pragma unroll
@@ -1213,11 +1223,11 @@ __global__ void __launch_bounds__(BWD_NT, 1)
 #pragma unroll
     for (int kk = 0; kk < P / 16; ++kk) {
       uint32_t a[4];
-      load_a(a, sdY, LDP, m0, kk * 16, lane);
+      load_a(a, sdY0, LDP, m0, kk * 16, lane);
 #pragma unroll
       for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
-        load_b_kn(bb, sSt, LDN, c32 + np * 16, kk * 16, lane);
+        load_b_kn(bb, sSt, LDN, cq * 16 + np * 64, kk * 16, lane);
         mma_bf16(qacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(qacc[2 * np + 1], a, bb[2], bb[3]);
       }
@@ -1233,7 +1243,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
 #pragma unroll
       for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
-        load_b_kn(bb, sK, LDN, c32 + np * 16, kk * 16, lane);
+        load_b_kn(bb, sK, LDN, cq * 16 + np * 64, kk * 16, lane);
         mma_bf16(qacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(qacc[2 * np + 1], a, bb[2], bb[3]);
       }
@@ -1246,7 +1256,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
       bf16* dst = out.gQ + (((size_t)b * g.L + (tt < g.L ? tt : 0)) * g.nh + h) * N;
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        int n = c32 + nt * 8 + 2 * tq;
+        int n = cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq;
         float g0 = qacc[nt][hr * 2], g1 = qacc[nt][hr * 2 + 1];
         float d0, d1;
         if (n < 2 * R) {
@@ -1278,13 +1288,13 @@ __global__ void __launch_bounds__(BWD_NT, 1)
         a1 += __shfl_xor_sync(0xffffffffu, a1, o);
       }
       if (gq == 0) {
-        atomicAdd(&sDcb[c32 + nt * 8 + 2 * tq], a0);
-        atomicAdd(&sDcb[c32 + nt * 8 + 2 * tq + 1], a1);
+        atomicAdd(&sDcb[cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq], a0);
+        atomicAdd(&sDcb[cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq + 1], a1);
       }
     }
   }
   BWD_PHASE(7);
-  // ---- D: dK = w_s (V dS_out) + dS^T Q  (cols c32..) -> gK, dscale, dtheta, dB_bias ------
+  // ---- D: dK = w_s (V dS_out) + dS^T Q  (cols cq*16.. and cq*16+64..) -> gK, dscale, dtheta, dB_bias ------
   {
     float kacc[4][4];
 #pragma unroll
@@ -1296,7 +1306,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
 #pragma unroll
       for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
-        load_b_kn(bb, sdSt, LDN, c32 + np * 16, kk * 16, lane);
+        load_b_kn(bb, sdSt, LDN, cq * 16 + np * 64, kk * 16, lane);
         mma_bf16(kacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(kacc[2 * np + 1], a, bb[2], bb[3]);
       }
@@ -1313,7 +1323,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
 #pragma unroll
       for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
-        load_b_kn(bb, sQ, LDN, c32 + np * 16, kk * 16, lane);
+        load_b_kn(bb, sQ, LDN, cq * 16 + np * 64, kk * 16, lane);
         mma_bf16(kacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(kacc[2 * np + 1], a, bb[2], bb[3]);
       }
@@ -1329,7 +1339,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
       float dsc = 0.f;
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        int n = c32 + nt * 8 + 2 * tq;
+        int n = cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq;
         float g0 = kacc[nt][hr * 2], g1 = kacc[nt][hr * 2 + 1];
         float2 bn = unpack_bf16(*reinterpret_cast<const uint32_t*>(sBn + row * LDN + n));
         float b0 = bn.x + sBbv[n], b1 = bn.y + sBbv[n + 1];
@@ -1377,8 +1387,8 @@ __global__ void __launch_bounds__(BWD_NT, 1)
         a1 += __shfl_xor_sync(0xffffffffu, a1, o);
       }
       if (gq == 0) {
-        atomicAdd(&sDbb[c32 + nt * 8 + 2 * tq], a0);
-        atomicAdd(&sDbb[c32 + nt * 8 + 2 * tq + 1], a1);
+        atomicAdd(&sDbb[cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq], a0);
+        atomicAdd(&sDbb[cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq + 1], a1);
       }
     }
   }
@@ -1428,15 +1438,15 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     for (int kk = 0; kk < CS / 16; ++kk) {
       uint32_t a[4], bb[4];
       load_a_t(a, sP, LDP, m0, kk * 16, lane);
-      load_b_kn(bb, sdY, LDP, c16, kk * 16, lane);
+      load_b_kn(bb, sdY0, LDP, c16, kk * 16, lane);
       mma_bf16(vacc2[0], a, bb[0], bb[1]);
       mma_bf16(vacc2[1], a, bb[2], bb[3]);
     }
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       int p = c16 + nt * 8 + 2 * tq;
-      float2 d0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdY + r0 * LDP + p));
-      float2 d1 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdY + r1 * LDP + p));
+      float2 d0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdY0 + r0 * LDP + p));
+      float2 d1 = unpack_bf16(*reinterpret_cast<const uint32_t*>(sdY0 + r1 * LDP + p));
       *reinterpret_cast<uint32_t*>(sX + r0 * LDP + p) =
           pack_bf16(vacc2[nt][0] + q0 * d0.x, vacc2[nt][1] + q0 * d0.y);
       *reinterpret_cast<uint32_t*>(sX + r1 * LDP + p) =
@@ -1464,15 +1474,16 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     if (lane == 0) sMisc[warp] = dot;
   }
   // ---- F: reductions and stores ------------------------------------------------------------
-  {
-    float dd = warp_sum(dD_acc);
-    if (lane == 0) sDD[warp] = dd;
+  if (warp == 0) {   // dD = sum over rows of dqk (= sum_p dY0 * V)
+    const float dd = warp_sum(sDqk[lane] + sDqk[lane + 32]);
+    if (lane == 0) sDD[0] = dd;
   }
   __syncthreads();   // all shared atomics done; sX holds dV, sZ holds dz
   BWD_PHASE(5);
   if (tid == 0) {
     float dot = 0.f, s = 0.f;
-    for (int k = 0; k < BWD_NT / 32; ++k) { dot += sMisc[k]; s += sDD[k]; }
+    for (int k = 0; k < BWD_NT / 32; ++k) dot += sMisc[k];
+    s = sDD[0];
     sDcum[CS - 1] += dot;
     out.dD[bh * g.nc + c] = s;
   }
