@@ -970,6 +970,8 @@ struct BwdOut {
 };
 
 constexpr int BWD_NT = 512;
+constexpr int BPLD = 2 * N + 8;   // row stride of the bias-gradient partial-sum table (floats)
+static_assert(32 * BPLD * 4 <= 2 * 64 * (N + 8) * 2, "partial table fits in the B and Q tiles");
 constexpr size_t BWD_SMEM = sizeof(bf16) * (5 * CS * LDN + 6 * CS * LDP) +
                             sizeof(float) * (3 * CS * RP + 2 * (CS + 4) + 9 * CS + 4 * N + 16 * 32 + 32 + 16 +
                                              16);
@@ -1005,9 +1007,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   float* sDscl = sDcum + CS;
   float* sCbv = sDscl + CS;
   float* sBbv = sCbv + N;
-  float* sDcb = sBbv + N;
-  float* sDbb = sDcb + N;
-  float* sSeg = sDbb + N;        // [16][32]
+  float* sSeg = sBbv + 3 * N;    // [16][32] (2N floats of spare room before it)
   float* sTh0 = sSeg + 16 * 32;  // [32]
   float* sMisc = sTh0 + 32;      // [16]
   float* sDD = sMisc + 16;       // [16]
@@ -1049,10 +1049,6 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     }
   }
   cp_async_commit();
-  for (int i = tid; i < N; i += BWD_NT) {
-    sDcb[i] = 0.f;
-    sDbb[i] = 0.f;
-  }
   if (tid < CS) { sDcum[tid] = 0.f; sDscl[tid] = 0.f; }
   cp_async_wait_group<1>();
   __syncthreads();
@@ -1215,185 +1211,144 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     }
   }
   BWD_PHASE(3);
-  // ---- C: dQ = exp(cum_l) dY0 S_in + dS K  (cols cq*16.. and cq*16+64..) -> gQ, dtheta, dC_bias ---------
+  float colp[4][4];   // per-thread column partial sums of dQ / dK (bias gradients)
+  // ---- C: dQ = exp(cum_l) dY0 S_in + dS K and dK = w_s (V dS_out) + dS^T Q on the same
+  // columns (cq*16.. and cq*16+64..), then one epilogue for both: gQ, gK, dtheta, dscale,
+  // dC_bias, dB_bias (the shared B, Q, sin/cos and bias reads happen once) ---------------
   {
-    float qacc[4][4];
+    float qacc[4][4], kacc[4][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) qacc[i][0] = qacc[i][1] = qacc[i][2] = qacc[i][3] = 0.f;
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) qacc[i][e] = kacc[i][e] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < P / 16; ++kk) {
-      uint32_t a[4];
+      uint32_t a[4], ax[4];
       load_a(a, sdY0, LDP, m0, kk * 16, lane);
+      load_a(ax, sX, LDP, m0, kk * 16, lane);
 #pragma unroll
       for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
         load_b_kn(bb, sSt, LDN, cq * 16 + np * 64, kk * 16, lane);
         mma_bf16(qacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(qacc[2 * np + 1], a, bb[2], bb[3]);
+        load_b_kn(bb, sdSt, LDN, cq * 16 + np * 64, kk * 16, lane);
+        mma_bf16(kacc[2 * np], ax, bb[0], bb[1]);
+        mma_bf16(kacc[2 * np + 1], ax, bb[2], bb[3]);
       }
     }
+    const float w0 = sW[r0], w1 = sW[r1];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
       qacc[nt][0] *= e0; qacc[nt][1] *= e0; qacc[nt][2] *= e1; qacc[nt][3] *= e1;
+      kacc[nt][0] *= w0; kacc[nt][1] *= w0; kacc[nt][2] *= w1; kacc[nt][3] *= w1;
     }
 #pragma unroll
     for (int kk = 0; kk < CS / 16; ++kk) {
-      uint32_t a[4];
+      uint32_t a[4], at[4];
       load_a(a, sdS, LDP, m0, kk * 16, lane);
+      load_a_t(at, sdS, LDP, m0, kk * 16, lane);
 #pragma unroll
       for (int np = 0; np < 2; ++np) {
         uint32_t bb[4];
         load_b_kn(bb, sK, LDN, cq * 16 + np * 64, kk * 16, lane);
         mma_bf16(qacc[2 * np], a, bb[0], bb[1]);
         mma_bf16(qacc[2 * np + 1], a, bb[2], bb[3]);
-      }
-    }
-#pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-      int row = hr ? r1 : r0;
-      int tt = t0 + row;
-      float gm = sGam[row] * sDqk[row];
-      bf16* dst = out.gQ + (((size_t)b * g.L + (tt < g.L ? tt : 0)) * g.nh + h) * N;
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        int n = cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq;
-        float g0 = qacc[nt][hr * 2], g1 = qacc[nt][hr * 2 + 1];
-        float d0, d1;
-        if (n < 2 * R) {
-          int r = n >> 1;
-          float sn = sSin[row * RP + r], cs = sCos[row * RP + r];
-          float2 q = unpack_bf16(*reinterpret_cast<const uint32_t*>(sQ + row * LDN + n));
-          sDth[row * RP + r] = -g0 * q.y + g1 * q.x;
-          d0 = g0 * cs + g1 * sn;
-          d1 = -g0 * sn + g1 * cs;
-        } else {
-          d0 = g0;
-          d1 = g1;
-        }
-        float2 bn = unpack_bf16(*reinterpret_cast<const uint32_t*>(sBn + row * LDN + n));
-        d0 += gm * (bn.x + sBbv[n]);
-        d1 += gm * (bn.y + sBbv[n + 1]);
-        if (tt < g.L) *reinterpret_cast<uint32_t*>(dst + n) = pack_bf16(d0, d1);
-        else { d0 = 0.f; d1 = 0.f; }
-        qacc[nt][hr * 2] = d0;
-        qacc[nt][hr * 2 + 1] = d1;
-      }
-    }
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      float a0 = qacc[nt][0] + qacc[nt][2], a1 = qacc[nt][1] + qacc[nt][3];
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        a0 += __shfl_xor_sync(0xffffffffu, a0, o);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, o);
-      }
-      if (gq == 0) {
-        atomicAdd(&sDcb[cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq], a0);
-        atomicAdd(&sDcb[cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq + 1], a1);
-      }
-    }
-  }
-  BWD_PHASE(7);
-  // ---- D: dK = w_s (V dS_out) + dS^T Q  (cols cq*16.. and cq*16+64..) -> gK, dscale, dtheta, dB_bias ------
-  {
-    float kacc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) kacc[i][0] = kacc[i][1] = kacc[i][2] = kacc[i][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < P / 16; ++kk) {
-      uint32_t a[4];
-      load_a(a, sX, LDP, m0, kk * 16, lane);
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t bb[4];
-        load_b_kn(bb, sdSt, LDN, cq * 16 + np * 64, kk * 16, lane);
-        mma_bf16(kacc[2 * np], a, bb[0], bb[1]);
-        mma_bf16(kacc[2 * np + 1], a, bb[2], bb[3]);
-      }
-    }
-    const float w0 = sW[r0], w1 = sW[r1];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      kacc[nt][0] *= w0; kacc[nt][1] *= w0; kacc[nt][2] *= w1; kacc[nt][3] *= w1;
-    }
-#pragma unroll
-    for (int kk = 0; kk < CS / 16; ++kk) {
-      uint32_t a[4];
-      load_a_t(a, sdS, LDP, m0, kk * 16, lane);
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t bb[4];
         load_b_kn(bb, sQ, LDN, cq * 16 + np * 64, kk * 16, lane);
-        mma_bf16(kacc[2 * np], a, bb[0], bb[1]);
-        mma_bf16(kacc[2 * np + 1], a, bb[2], bb[3]);
+        mma_bf16(kacc[2 * np], at, bb[0], bb[1]);
+        mma_bf16(kacc[2 * np + 1], at, bb[2], bb[3]);
       }
     }
+    BWD_PHASE(11);
     float dsc0 = 0.f, dsc1 = 0.f;
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
-      int row = hr ? r1 : r0;
-      int tt = t0 + row;
-      float sc = sScl[row];
-      float gm = sGam[row] * sDqk[row];
-      bf16* dst = out.gK + (((size_t)b * g.L + (tt < g.L ? tt : 0)) * g.nh + h) * N;
+      const int row = hr ? r1 : r0;
+      const int tt = t0 + row;
+      const bool live = tt < g.L;
+      const float sc = sScl[row];
+      const float gm = sGam[row] * sDqk[row];
+      const size_t orow = (((size_t)b * g.L + (live ? tt : 0)) * g.nh + h) * N;
       float dsc = 0.f;
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        int n = cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq;
-        float g0 = kacc[nt][hr * 2], g1 = kacc[nt][hr * 2 + 1];
-        float2 bn = unpack_bf16(*reinterpret_cast<const uint32_t*>(sBn + row * LDN + n));
-        float b0 = bn.x + sBbv[n], b1 = bn.y + sBbv[n + 1];
-        float2 qv = unpack_bf16(*reinterpret_cast<const uint32_t*>(sQ + row * LDN + n));
-        float d0, d1, cb0, cb1;
-        if (n < 2 * R) {
-          int r = n >> 1;
-          float sn = sSin[row * RP + r], cs = sCos[row * RP + r];
-          float k0 = b0 * cs - b1 * sn, k1 = b0 * sn + b1 * cs;
-          dsc += g0 * k0 + g1 * k1;
-          float h0 = g0 * sc, h1 = g1 * sc;
-          sDth[row * RP + r] += -h0 * k1 + h1 * k0;
-          d0 = h0 * cs + h1 * sn;
-          d1 = -h0 * sn + h1 * cs;
+        const int n = cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq;
+        const float g0 = qacc[nt][hr * 2], g1 = qacc[nt][hr * 2 + 1];
+        const float k0g = kacc[nt][hr * 2], k1g = kacc[nt][hr * 2 + 1];
+        const float2 bn = unpack_bf16(*reinterpret_cast<const uint32_t*>(sBn + row * LDN + n));
+        const float2 bbv = *reinterpret_cast<const float2*>(sBbv + n);
+        const float b0 = bn.x + bbv.x, b1 = bn.y + bbv.y;
+        const float2 qv = unpack_bf16(*reinterpret_cast<const uint32_t*>(sQ + row * LDN + n));
+        float dq0, dq1, dk0, dk1, cb0, cb1;
+        if (nt < 2) {   // columns n < 2R: rotated
+          const int r = n >> 1;
+          const float sn = sSin[row * RP + r], cs = sCos[row * RP + r];
+          dq0 = g0 * cs + g1 * sn;
+          dq1 = -g0 * sn + g1 * cs;
+          const float kr0 = b0 * cs - b1 * sn, kr1 = b0 * sn + b1 * cs;
+          dsc += k0g * kr0 + k1g * kr1;
+          const float h0 = k0g * sc, h1 = k1g * sc;
+          sDth[row * RP + r] = (-g0 * qv.y + g1 * qv.x) + (-h0 * kr1 + h1 * kr0);
+          dk0 = h0 * cs + h1 * sn;
+          dk1 = -h0 * sn + h1 * cs;
           cb0 = qv.x * cs + qv.y * sn;      // C + C_bias recovered from Q (inverse rotation)
           cb1 = -qv.x * sn + qv.y * cs;
         } else {
-          dsc += g0 * b0 + g1 * b1;
-          d0 = g0 * sc;
-          d1 = g1 * sc;
+          dq0 = g0;
+          dq1 = g1;
+          dsc += k0g * b0 + k1g * b1;
+          dk0 = k0g * sc;
+          dk1 = k1g * sc;
           cb0 = qv.x;
           cb1 = qv.y;
         }
-        d0 += gm * cb0;
-        d1 += gm * cb1;
-        if (tt < g.L) *reinterpret_cast<uint32_t*>(dst + n) = pack_bf16(d0, d1);
-        else { d0 = 0.f; d1 = 0.f; }
-        kacc[nt][hr * 2] = d0;
-        kacc[nt][hr * 2 + 1] = d1;
+        dq0 += gm * b0;
+        dq1 += gm * b1;
+        dk0 += gm * cb0;
+        dk1 += gm * cb1;
+        if (live) {
+          *reinterpret_cast<uint32_t*>(out.gQ + orow + n) = pack_bf16(dq0, dq1);
+          *reinterpret_cast<uint32_t*>(out.gK + orow + n) = pack_bf16(dk0, dk1);
+        } else {
+          dq0 = dq1 = dk0 = dk1 = 0.f;
+        }
+        qacc[nt][hr * 2] = dq0;
+        qacc[nt][hr * 2 + 1] = dq1;
+        kacc[nt][hr * 2] = dk0;
+        kacc[nt][hr * 2 + 1] = dk1;
       }
       if (hr) dsc1 = dsc; else dsc0 = dsc;
     }
+    BWD_PHASE(12);
     dsc0 += __shfl_xor_sync(0xffffffffu, dsc0, 1); dsc0 += __shfl_xor_sync(0xffffffffu, dsc0, 2);
     dsc1 += __shfl_xor_sync(0xffffffffu, dsc1, 1); dsc1 += __shfl_xor_sync(0xffffffffu, dsc1, 2);
     if (tq == 0) {
       atomicAdd(&sDscl[r0], dsc0);
       atomicAdd(&sDscl[r1], dsc1);
     }
+    // bias gradients: column sums over this thread's two rows; the 32 partial rows per
+    // column (4 row blocks x 8 row groups) go to a table after the barrier below
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
-      float a0 = kacc[nt][0] + kacc[nt][2], a1 = kacc[nt][1] + kacc[nt][3];
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        a0 += __shfl_xor_sync(0xffffffffu, a0, o);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, o);
-      }
-      if (gq == 0) {
-        atomicAdd(&sDbb[cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq], a0);
-        atomicAdd(&sDbb[cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq + 1], a1);
-      }
+      colp[nt][0] = qacc[nt][0] + qacc[nt][2];
+      colp[nt][1] = qacc[nt][1] + qacc[nt][3];
+      colp[nt][2] = kacc[nt][0] + kacc[nt][2];
+      colp[nt][3] = kacc[nt][1] + kacc[nt][3];
     }
   }
-  __syncthreads();   // every warp done reading sX (V) as an MMA operand
+  BWD_PHASE(7);
+  __syncthreads();   // every warp done reading sX (V) as an MMA operand; sBn and sQ are dead
   BWD_PHASE(4);
+  {   // partial column sums -> part[32][BPLD] over the dead B and Q tiles
+    float* part = reinterpret_cast<float*>(sBn);
+    const int prow = rb * 8 + gq;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int n = cq * 16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq;
+      *reinterpret_cast<float2*>(part + prow * BPLD + n) = make_float2(colp[nt][0], colp[nt][1]);
+      *reinterpret_cast<float2*>(part + prow * BPLD + N + n) = make_float2(colp[nt][2], colp[nt][3]);
+    }
+  }
   // the next chunk's input state (S_out of this chunk), for d cum_end after E
   uint4 nsv[P * N / 8 / BWD_NT];
   if (c + 1 < g.nc) {
@@ -1546,9 +1501,15 @@ __global__ void __launch_bounds__(BWD_NT, 1)
       out.dadt[k] = sADT[tid];
     }
   }
-  for (int i = tid; i < N; i += BWD_NT) {
-    out.dCb[(bh * g.nc + c) * N + i] = sDcb[i];
-    out.dBb[(bh * g.nc + c) * N + i] = sDbb[i];
+  {
+    const float* part = reinterpret_cast<const float*>(sBn);
+    for (int i = tid; i < 2 * N; i += BWD_NT) {
+      float sum = 0.f;
+#pragma unroll 8
+      for (int r = 0; r < 32; ++r) sum += part[r * BPLD + i];
+      if (i < N) out.dCb[(bh * g.nc + c) * N + i] = sum;
+      else out.dBb[(bh * g.nc + c) * N + i - N] = sum;
+    }
   }
   BWD_PHASE(6);
 }
