@@ -1519,7 +1519,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
 // BCNorm backward and the decay / trapezoid parameter chain.  The per-head angle
 // term sum_r G[h][r] * rate[r] is reduced through a per-warp shared tile.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
     m3_prep_bwd(const bf16* __restrict__ proj, Geo g, const float* __restrict__ wB,
                 const float* __restrict__ wC, const float* __restrict__ dt_bias, float A_floor, float eps,
                 const bf16* __restrict__ gQ, const bf16* __restrict__ gK, const float* __restrict__ dthl,
@@ -1542,6 +1542,30 @@ __global__ void __launch_bounds__(256)
     const float th = tanhf(__bfloat162float(row[g.off_ang + lane]));
     const float rt = th * PI_F;                       // angle rate (lane = r)
     const float drt = PI_F * (1.f - th * th);         // d rate / d angle
+    // loads that do not depend on the head loop, issued before it so their latency
+    // overlaps the head loads: the B/C row and the per-head scalars of this token
+    float xb[4], xc[4];
+    {
+      const uint2 bv = *reinterpret_cast<const uint2*>(row + g.off_B + lane * 4);
+      const uint2 cv = *reinterpret_cast<const uint2*>(row + g.off_C + lane * 4);
+      const float2 b01 = unpack_bf16(bv.x), b23 = unpack_bf16(bv.y);
+      const float2 c01 = unpack_bf16(cv.x), c23 = unpack_bf16(cv.y);
+      xb[0] = b01.x; xb[1] = b01.y; xb[2] = b23.x; xb[3] = b23.y;
+      xc[0] = c01.x; xc[1] = c01.y; xc[2] = c23.x; xc[3] = c23.y;
+    }
+    float hs_dgam[2], hs_dsp[2], hs_dadt[2], hs_ddtr[2], hs_dAr[2], hs_tr[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int h = lane + 32 * j;
+      const bool ok = h < g.nh;
+      const size_t k = ((size_t)b * g.nh + (ok ? h : 0)) * g.L + t;
+      hs_dgam[j] = ok ? dgam[k] : 0.f;
+      hs_dsp[j] = (ok && t > 0) ? dscl[k - 1] : 0.f;
+      hs_dadt[j] = ok ? dadt[k] : 0.f;
+      hs_ddtr[j] = ok ? __bfloat162float(row[g.off_dt + h]) : 0.f;
+      hs_dAr[j] = ok ? __bfloat162float(row[g.off_A + h]) : 0.f;
+      hs_tr[j] = ok ? __bfloat162float(row[g.off_trap + h]) : 0.f;
+    }
     __syncwarp();
     float sb[4] = {0, 0, 0, 0}, sc[4] = {0, 0, 0, 0}, sa = 0.f, dang[2] = {0.f, 0.f};
     for (int h0 = 0, j = 0; h0 < g.nh; h0 += 32, ++j) {
@@ -1570,11 +1594,9 @@ __global__ void __launch_bounds__(256)
       dang[j] = acc;
       __syncwarp();
     }
-    float xb[4], xc[4], ssb = 0.f, ssc = 0.f;
+    float ssb = 0.f, ssc = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      xb[i] = __bfloat162float(row[g.off_B + lane * 4 + i]);
-      xc[i] = __bfloat162float(row[g.off_C + lane * 4 + i]);
       ssb += xb[i] * xb[i];
       ssc += xc[i] * xc[i];
     }
@@ -1599,20 +1621,22 @@ __global__ void __launch_bounds__(256)
       awC[i] += sc[i] * xc[i] * rc;
     }
     drow[g.off_ang + lane] = __float2bfloat16(sa);
-    for (int h = lane, j = 0; h < g.nh; h += 32, ++j) {
-      float ddtr = __bfloat162float(row[g.off_dt + h]);
-      float dAr = __bfloat162float(row[g.off_A + h]);
-      float tr = __bfloat162float(row[g.off_trap + h]);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int h = lane + 32 * j;
+      if (h >= g.nh) break;
+      float ddtr = hs_ddtr[j];
+      float dAr = hs_dAr[j];
+      float tr = hs_tr[j];
       float xdt = ddtr + dt_bias[h];
       float DT = dts[wib][h];
       float spA = softplusf_(dAr);
       float A = fminf(-spA, -A_floor);
       float sg = sigmoidf_(tr);
-      size_t k = ((size_t)b * g.nh + h) * g.L + t;
-      float dsp = (t > 0) ? dscl[k - 1] : 0.f;
-      float dDT = dang[j] + dgam[k] * sg + dsp * (1.f - sg) + dadt[k] * A;
-      float dsg = dgam[k] * DT - dsp * DT;
-      float dA = dadt[k] * DT;
+      float dsp = hs_dsp[j];
+      float dDT = dang[j] + hs_dgam[j] * sg + dsp * (1.f - sg) + hs_dadt[j] * A;
+      float dsg = hs_dgam[j] * DT - dsp * DT;
+      float dA = hs_dadt[j] * DT;
       float d_ddt = dDT * sigmoidf_(xdt);
       float d_dA = (-spA < -A_floor) ? -dA * sigmoidf_(dAr) : 0.f;
       drow[g.off_dt + h] = __float2bfloat16(d_ddt);
@@ -1624,12 +1648,27 @@ __global__ void __launch_bounds__(256)
     for (int cc = used + lane; cc < g.ldp; cc += 32) drow[cc] = __float2bfloat16(0.f);
     __syncwarp();
   }
+  // parameter gradients: sum the 8 warps in shared memory first, then one atomic per
+  // column per block (per-warp atomics all land on the same few L2 lines and serialise)
+  __syncthreads();
+  float* red = &tile[0][0][0];                     // [8][2N + 64]
+  constexpr int RW = 2 * N + 64;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    atomicAdd(&dwB[lane * 4 + i], awB[i]);
-    atomicAdd(&dwC[lane * 4 + i], awC[i]);
+    red[wib * RW + lane * 4 + i] = awB[i];
+    red[wib * RW + N + lane * 4 + i] = awC[i];
   }
-  for (int h = lane, j = 0; h < g.nh && j < 2; h += 32, ++j) atomicAdd(&ddt_bias[h], adt[j]);
+  red[wib * RW + 2 * N + lane] = adt[0];
+  red[wib * RW + 2 * N + 32 + lane] = adt[1];
+  __syncthreads();
+  for (int k = threadIdx.x; k < RW; k += blockDim.x) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) v += red[w * RW + k];
+    if (k < N) atomicAdd(&dwB[k], v);
+    else if (k < 2 * N) atomicAdd(&dwC[k - N], v);
+    else if (k - 2 * N < g.nh) atomicAdd(&ddt_bias[k - 2 * N], v);
+  }
 }
 
 }  // namespace m3
@@ -1757,7 +1796,7 @@ void m3_prep_bwd_launch(const M3Geo& G, const void* proj, const float* wB, const
   Geo g = make_geo(G);
   long T = (long)g.B * g.L;
   int blocks = (int)((T * 32 + 255) / 256);
-  if (blocks > 148 * 4) blocks = 148 * 4;
+  if (blocks > 148 * 2) blocks = 148 * 2;   // one wave at two 256-thread blocks per SM
   m3_prep_bwd<<<blocks, 256, 0, st>>>(reinterpret_cast<const bf16*>(proj), g, wB, wC, dt_bias, A_floor, eps,
                                       reinterpret_cast<const bf16*>(gQ), reinterpret_cast<const bf16*>(gK),
                                       dthl, dthc, dgam, dscl, dadt, reinterpret_cast<bf16*>(dproj), dwB, dwC,
