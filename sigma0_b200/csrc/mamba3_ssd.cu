@@ -260,6 +260,23 @@ __device__ __forceinline__ void load_scalars_async(const ScanIn& in, const Geo& 
   }
 }
 
+// Group 1 of a chunk kernel's loads: scalars, rates, the head's biases (either may be
+// null) and the chunk's start angle, committed as one cp.async group so the angle and
+// decay prologue can start while the operand tiles (group 2) are still in flight.
+template <int NTH>
+__device__ __forceinline__ void load_prologue_async(const ScanIn& in, const Geo& g, int b, int h, int c, int t0,
+                                                    float* sDT, float* sADT, float* sSig, float* sRate,
+                                                    float* sCbv, float* sBbv, float* sTh0, int tid) {
+  load_scalars_async<NTH>(in, g, b, h, t0, sDT, sADT, sSig, sRate, tid);
+  const size_t bh = (size_t)b * g.nh + h;
+  for (int i = tid; i < 2 * N + R; i += NTH) {   // 4-byte copies: these arrays are only 4-byte aligned
+    if (i < N) { if (sCbv) cp_async4(sCbv + i, in.Cb + h * N + i); }
+    else if (i < 2 * N) { if (sBbv) cp_async4(sBbv + i - N, in.Bb + h * N + i - N); }
+    else cp_async4(sTh0 + i - 2 * N, in.theta0 + (bh * g.nc + c) * R + i - 2 * N);
+  }
+  cp_async_commit();
+}
+
 // gamma, scale and the within-chunk inclusive cumsum of ADT (needs two warps).
 __device__ __forceinline__ void row_scalars(const float* sDT, const float* sSig, const float* sADT,
                                             float* sGam, float* sScl, float* sCum, int tid) {
@@ -473,17 +490,16 @@ __global__ void __launch_bounds__(256) m3_chunk_state(ScanIn in, Geo g, bf16* __
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
   const int rb = warp & 3, cg = warp >> 2;
   const int t0 = c * CS, m0 = rb * 16;
-  const size_t bh = (size_t)b * g.nh + h;
+  load_prologue_async<256>(in, g, b, h, c, t0, sDT, sADT, sSig, sSin, nullptr, sBbv, sTh0, tid);
   load_rows<256>(in.bc + (size_t)b * g.L * 2 * N, 2 * N, 0, N, sB, LDN, t0, g.L, tid);
   load_rows<256>(in.proj + (size_t)b * g.L * g.ldp, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
   cp_async_commit();
-  load_scalars<256>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
-  for (int i = tid; i < N; i += 256) sBbv[i] = in.Bb[h * N + i];
-  if (tid < 32) sTh0[tid] = in.theta0[(bh * g.nc + c) * R + tid];
-  cp_async_wait_all();
+  cp_async_wait_group<1>();
   __syncthreads();
   row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
   chunk_angles<256>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
+  cp_async_wait_all();
+  __syncthreads();
   build_qk<256>(nullptr, sB, nullptr, sB, sCos, sSin, sScl, nullptr, sBbv, nullptr, tid);
   const float cend = sCum[CS - 1];
   if (tid < CS) sW[tid] = __expf(cend - sCum[tid]);
@@ -552,9 +568,9 @@ __global__ void __launch_bounds__(256)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
   const int rb = warp & 3, cg = warp >> 2, c32 = cg * 32;
   const int t0 = c * CS, m0 = rb * 16;
-  const size_t bh = (size_t)b * g.nh + h;
   const bf16* bcb = in.bc + (size_t)b * g.L * 2 * N;
   const bf16* pb = in.proj + (size_t)b * g.L * g.ldp;
+  load_prologue_async<256>(in, g, b, h, c, t0, sDT, sADT, sSig, sSin, sCbv, sBbv, sTh0, tid);
   load_rows<256>(bcb, 2 * N, 0, N, sB, LDN, t0, g.L, tid);
   load_rows<256>(bcb, 2 * N, N, N, sC, LDN, t0, g.L, tid);
   load_rows<256>(pb, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
@@ -567,16 +583,12 @@ __global__ void __launch_bounds__(256)
     }
   }
   cp_async_commit();
-  load_scalars<256>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
-  for (int i = tid; i < N; i += 256) {
-    sCbv[i] = in.Cb[h * N + i];
-    sBbv[i] = in.Bb[h * N + i];
-  }
-  if (tid < 32) sTh0[tid] = in.theta0[(bh * g.nc + c) * R + tid];
-  cp_async_wait_all();
+  cp_async_wait_group<1>();
   __syncthreads();
   row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
   chunk_angles<256>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
+  cp_async_wait_all();
+  __syncthreads();
   build_qk<256>(sC, sB, sC, sB, sCos, sSin, sScl, sCbv, sBbv, sQKr, tid);
 
   const int r0 = m0 + gq, r1 = r0 + 8;
@@ -910,18 +922,17 @@ __global__ void __launch_bounds__(256)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
   const int rb = warp & 3, cg = warp >> 2;
   const int t0 = c * CS, m0 = rb * 16;
-  const size_t bh = (size_t)b * g.nh + h;
+  load_prologue_async<256>(in, g, b, h, c, t0, sDT, sADT, sSig, sSin, sCbv, nullptr, sTh0, tid);
   load_rows<256>(in.bc + (size_t)b * g.L * 2 * N, 2 * N, N, N, sC, LDN, t0, g.L, tid);
   load_rows<256>(in.proj + (size_t)b * g.L * g.ldp, g.ldp, h * P, P, sZ, LDP, t0, g.L, tid);
   load_rows<256>(dy + (size_t)b * g.L * g.d_inner, g.d_inner, h * P, P, sdY, LDP, t0, g.L, tid);
   cp_async_commit();
-  load_scalars<256>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
-  for (int i = tid; i < N; i += 256) sCbv[i] = in.Cb[h * N + i];
-  if (tid < 32) sTh0[tid] = in.theta0[(bh * g.nc + c) * R + tid];
-  cp_async_wait_all();
+  cp_async_wait_group<1>();
   __syncthreads();
   row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
   chunk_angles<256>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
+  cp_async_wait_all();
+  __syncthreads();
   build_qk<256>(sC, nullptr, sC, nullptr, sCos, sSin, sScl, sCbv, nullptr, nullptr, tid);
   for (int i = tid; i < CS * P / 2; i += 256) {
     int r = i / (P / 2), p = 2 * (i % (P / 2));

@@ -120,6 +120,9 @@ class StackedEncoder(nn.Module):
                  attn_layers: Sequence[int] = ()):
         super().__init__()
         self.encoder = Embed(vocab_size, d_model) if use_embed_layer else Dense(d_input, d_model)
+        # dtype of the input Dense's GEMM on CUDA (bf16 tensor cores when the model computes
+        # in bf16; fp32 would run a SIMT GEMM); the embedding lookup ignores it
+        self.compute_dtype = torch.float32
         attn_at = frozenset(attn_layers) if attn_factory is not None else frozenset()
         if attn_at and max(attn_at) >= n_layers:
             raise ValueError(f"attn_layers={tuple(sorted(attn_at))} out of range for n_layers={n_layers}")
@@ -132,8 +135,13 @@ class StackedEncoder(nn.Module):
     def layers(self):
         return [getattr(self, f"layers_{i}") for i in range(self.n_layers)]
 
+    def _encode(self, x):
+        if isinstance(self.encoder, Dense) and x.is_cuda and self.compute_dtype != torch.float32:
+            return self.encoder(x, dtype=self.compute_dtype)
+        return self.encoder(x)
+
     def forward(self, x):
-        x = self.encoder(x)
+        x = self._encode(x)
         for layer in self.layers:
             x = layer(x)
         return x
@@ -143,7 +151,7 @@ class StackedEncoder(nn.Module):
 
     @torch.no_grad()
     def prefill(self, x, max_cache_len=None):
-        x = self.encoder(x)
+        x = self._encode(x)
         states = []
         for layer in self.layers:
             st, x = layer.prefill(x, max_cache_len)
@@ -151,7 +159,7 @@ class StackedEncoder(nn.Module):
         return states, x
 
     def step(self, states, x):
-        x = self.encoder(x)
+        x = self._encode(x)
         new = []
         for s, layer in zip(states, self.layers):
             s, x = layer.step(s, x)

@@ -327,6 +327,9 @@ def build_model(args: Any):
                     attn_factory_at=bb.attn_factory_at, attn_layers=bb.attn_layers)
     if bool(_g(args, "legacy_norm", False)) or legacy_norm_enabled():
         apply_legacy_norm(model)
-    if getattr(model, "book_encoder", None) is not None and str(_g(args, "impl", "torch")) == "cuda":
-        model.book_encoder.compute_dtype = _compute_dtype(args)
+    if str(_g(args, "impl", "torch")) == "cuda":
+        for enc in (getattr(model, "book_encoder", None), getattr(model, "message_encoder", None),
+                    getattr(model, "fused_s5", None)):
+            if enc is not None and hasattr(enc, "compute_dtype"):
+                enc.compute_dtype = _compute_dtype(args)
     return model
