@@ -181,13 +181,17 @@ std::vector<at::Tensor> ln_bwd(at::Tensor dy, at::Tensor x, at::Tensor mean, at:
   TORCH_CHECK(D % 4 == 0 && D <= 2048, "LayerNorm width must be a multiple of 4, at most 2048");
   auto dx = at::empty_like(x);
   auto dw = at::empty({D}, x.options()), db = at::empty({D}, x.options());
-  auto part = at::empty({(int64_t)col_blocks(T, num_sms(x)), 2, D}, x.options());
+  auto part = at::empty({std::max<int64_t>(col_blocks(T, num_sms(x)), num_sms(x)), 2, D}, x.options());
   const float* r = nullptr;
   if (dres.has_value() && dres->defined()) {
     req(*dres, at::kFloat, "dres");
     r = dres->data_ptr<float>();
   }
-  ln_bwd_launch(dy.data_ptr(), x.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+  if (D > 512 && D <= 1024 && T >= num_sms(x))
+    ln_bwd_pipe_launch(dy.data_ptr(), x.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+                       w.data_ptr<float>(), r, dx.data_ptr<float>(), dw.data_ptr<float>(), db.data_ptr<float>(),
+                       part.data_ptr<float>(), T, (int)D, num_sms(x), stream());
+  else ln_bwd_launch(dy.data_ptr(), x.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
                 w.data_ptr<float>(), r, dx.data_ptr<float>(), dw.data_ptr<float>(), db.data_ptr<float>(),
                 part.data_ptr<float>(), T, (int)D, num_sms(x), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -199,6 +203,7 @@ std::vector<at::Tensor> rms_fwd(at::Tensor x, at::Tensor w, double eps) {
   c10::cuda::CUDAGuard guard(x.device());
   int64_t D = x.size(-1), T = x.numel() / D;
   TORCH_CHECK(D % 8 == 0 && D <= 2048, "RMSNorm width must be a multiple of 8, at most 2048");
+  if (reinterpret_cast<uintptr_t>(w.data_ptr()) % 16) w = w.clone();   // the kernel reads w as float4
   auto y = at::empty_like(x);
   auto rstd = at::empty({T}, x.options().dtype(at::kFloat));
   rms_fwd_launch(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), rstd.data_ptr<float>(), T, (int)D, (float)eps,
@@ -213,11 +218,16 @@ std::vector<at::Tensor> rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::T
   c10::cuda::CUDAGuard guard(x.device());
   int64_t D = x.size(-1), T = x.numel() / D;
   TORCH_CHECK(D % 8 == 0 && D <= 2048, "RMSNorm width must be a multiple of 8, at most 2048");
+  if (reinterpret_cast<uintptr_t>(w.data_ptr()) % 16) w = w.clone();   // the kernel reads w as float4
   auto dx = at::empty_like(x);
   auto dw = at::empty({D}, x.options().dtype(at::kFloat));
-  auto part = at::empty({(int64_t)col_blocks(T, num_sms(x)), D}, x.options().dtype(at::kFloat));
-  rms_bwd_launch(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
-                 dw.data_ptr<float>(), part.data_ptr<float>(), T, (int)D, num_sms(x), stream());
+  auto part = at::empty({std::max<int64_t>(col_blocks(T, num_sms(x)), num_sms(x)), D}, x.options().dtype(at::kFloat));
+  if (D > 1024 && D <= 2048 && T >= num_sms(x))
+    rms_bwd_pipe_launch(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
+                        dw.data_ptr<float>(), part.data_ptr<float>(), T, (int)D, num_sms(x), stream());
+  else
+    rms_bwd_launch(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
+                   dw.data_ptr<float>(), part.data_ptr<float>(), T, (int)D, num_sms(x), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {dx, dw};
 }

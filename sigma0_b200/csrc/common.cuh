@@ -24,6 +24,9 @@ S0_DEV void cp_async16(void* smem, const void* gmem, int src_bytes = 16) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem),
                "r"(src_bytes));
 }
+S0_DEV void cp_async8(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
 S0_DEV void cp_async4(void* smem, const void* gmem, int src_bytes = 4) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes));
 }

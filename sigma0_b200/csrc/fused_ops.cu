@@ -177,6 +177,113 @@ __global__ void __launch_bounds__(CB_NT)
   }
 }
 
+// LayerNorm backward, pipelined (same math as ln_bwd_k): each warp stages its next
+// row (x fp32, dy bf16, dres fp32) in shared memory with cp.async while computing the
+// current one.  LB_NW warps per block, one block per SM; dw / db partials in registers
+// (a lane owns its columns), summed over the warps through shared memory at the end.
+// D <= 1024, D % 4 == 0.
+constexpr int LB_NW = 10;
+__global__ void __launch_bounds__(LB_NW * 32, 1)
+    ln_bwd_pipe_k(const bf16* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
+                  const float* __restrict__ rstd, const float* __restrict__ w, const float* __restrict__ dres,
+                  float* __restrict__ dx, float* __restrict__ part, int T, int D) {
+  constexpr int J = 8;                                             // float4 chunks per lane (D <= 1024)
+  extern __shared__ __align__(16) unsigned char lb_smem[];
+  float* sw = reinterpret_cast<float*>(lb_smem);                   // [D]
+  float* stage = sw + 3 * D;                                       // [LB_NW][2][x D | dres D | dy D/2]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int SZ = 2 * D + D / 2;                                    // floats per staged row
+  for (int c = threadIdx.x; c < D; c += blockDim.x) sw[c] = w[c];
+  float4 aw[J], ab[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) aw[j] = ab[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float* my = stage + (size_t)wid * 2 * SZ;
+  const int gw = blockIdx.x * LB_NW + wid, nw = gridDim.x * LB_NW;
+  auto issue = [&](int row, int buf) {
+    float* bx = my + (size_t)buf * SZ;
+    float* br = bx + D;
+    bf16* bg = reinterpret_cast<bf16*>(br + D);
+    const size_t o = (size_t)row * D;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = 4 * (lane + 32 * j);
+      if (c < D) {
+        cp_async16(bx + c, x + o + c);
+        if (dres) cp_async16(br + c, dres + o + c);
+        cp_async8(bg + c, dy + o + c);
+      }
+    }
+  };
+  __syncthreads();
+  int buf = 0;
+  float mu_n = 0.f, r_n = 0.f;
+  if (gw < T) { issue(gw, 0); mu_n = mean[gw]; r_n = rstd[gw]; }
+  cp_async_commit();
+  for (int row = gw; row < T; row += nw) {
+    const float mu = mu_n, r = r_n;
+    const int nxt = row + nw;
+    if (nxt < T) { issue(nxt, buf ^ 1); mu_n = mean[nxt]; r_n = rstd[nxt]; }
+    cp_async_commit();
+    cp_async_wait_group<1>();
+    const float* bx = my + (size_t)buf * SZ;
+    const float* br = bx + D;
+    const bf16* bg = reinterpret_cast<const bf16*>(br + D);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = 4 * (lane + 32 * j);
+      if (c < D) {
+        const float4 xv = *reinterpret_cast<const float4*>(bx + c);
+        const float4 g = ld_bf16x4(bg + c);
+        const float4 wv = *reinterpret_cast<const float4*>(sw + c);
+        const float h0 = (xv.x - mu) * r, h1 = (xv.y - mu) * r, h2 = (xv.z - mu) * r, h3 = (xv.w - mu) * r;
+        const float a0 = g.x * wv.x, a1 = g.y * wv.y, a2 = g.z * wv.z, a3 = g.w * wv.w;
+        s1 += a0 + a1 + a2 + a3;
+        s2 += a0 * h0 + a1 * h1 + a2 * h2 + a3 * h3;
+        aw[j].x += g.x * h0; aw[j].y += g.y * h1; aw[j].z += g.z * h2; aw[j].w += g.w * h3;
+        ab[j].x += g.x; ab[j].y += g.y; ab[j].z += g.z; ab[j].w += g.w;
+      }
+    }
+    s1 = warp_sum(s1) / D;
+    s2 = warp_sum(s2) / D;
+    const size_t o = (size_t)row * D;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = 4 * (lane + 32 * j);
+      if (c < D) {
+        const float4 xv = *reinterpret_cast<const float4*>(bx + c);
+        const float4 g = ld_bf16x4(bg + c);
+        const float4 wv = *reinterpret_cast<const float4*>(sw + c);
+        float4 rv = dres ? *reinterpret_cast<const float4*>(br + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        rv.x += r * (g.x * wv.x - s1 - (xv.x - mu) * r * s2);
+        rv.y += r * (g.y * wv.y - s1 - (xv.y - mu) * r * s2);
+        rv.z += r * (g.z * wv.z - s1 - (xv.z - mu) * r * s2);
+        rv.w += r * (g.w * wv.w - s1 - (xv.w - mu) * r * s2);
+        *reinterpret_cast<float4*>(dx + o + c) = rv;
+      }
+    }
+    buf ^= 1;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  float* red = stage;                                              // [LB_NW][2][D]
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = 4 * (lane + 32 * j);
+    if (c < D) {
+      *reinterpret_cast<float4*>(red + (size_t)wid * 2 * D + c) = aw[j];
+      *reinterpret_cast<float4*>(red + (size_t)wid * 2 * D + D + c) = ab[j];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < 2 * D; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < LB_NW; ++k) t += red[(size_t)k * 2 * D + c];
+    part[(size_t)blockIdx.x * 2 * D + c] = t;
+  }
+}
+
 // out_s[c] = sum over blocks of part[block][s][c], s < sets.  Block = 32 columns x
 // 8 row slices (coalesced along columns); fixed summation order (deterministic).
 __global__ void __launch_bounds__(256) col_sum_k(const float* __restrict__ part, int nblk, int sets, int D,
@@ -202,110 +309,244 @@ __global__ void __launch_bounds__(256) col_sum_k(const float* __restrict__ part,
 // ---------------------------------------------------------------------------
 // RMSNorm over bf16 rows (out_norm): y = x * rsqrt(mean(x^2)+eps) * w
 // ---------------------------------------------------------------------------
-__global__ void rms_fwd_k(const bf16* __restrict__ x, const float* __restrict__ w, bf16* __restrict__ y,
-                          float* __restrict__ rstd, int T, int D, float eps) {
-  int lane = threadIdx.x & 31;
-  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int nw = (gridDim.x * blockDim.x) >> 5;
+// One warp per row; PER 16-byte chunks per lane hold the whole row in registers, so
+// all of a row's loads are in flight at once (D <= 256 * PER).  w must be 16-byte aligned.
+template <int PER>
+__global__ void __launch_bounds__(256, 2) rms_fwd_k(const bf16* __restrict__ x, const float* __restrict__ w,
+                                                 bf16* __restrict__ y, float* __restrict__ rstd, int T, int D,
+                                                 float eps) {
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int nv = D / 8;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
   for (int row = gw; row < T; row += nw) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
-    uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * D);
-    int nv = D / 8;
+    uint4 u[PER];
     float s = 0.f;
-    for (int c = lane; c < nv; c += 32) {
-      uint4 u = xr[c];
-      uint32_t a[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int k = 0; k < 4; ++k) { float2 f = unpack_bf16(a[k]); s += f.x * f.x + f.y * f.y; }
+    for (int j = 0; j < PER; ++j) {
+      const int c = lane + 32 * j;
+      u[j] = c < nv ? xr[c] : make_uint4(0u, 0u, 0u, 0u);
     }
-    s = warp_sum(s);
-    float r = rsqrtf(s / D + eps);
-    for (int c = lane; c < nv; c += 32) {
-      uint4 u = xr[c];
-      uint32_t a[4] = {u.x, u.y, u.z, u.w};
-      uint32_t o[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float2 f = unpack_bf16(a[k]);
-        int col = c * 8 + 2 * k;
-        o[k] = pack_bf16(f.x * r * w[col], f.y * r * w[col + 1]);
+    for (int j = 0; j < PER; ++j) {
+      const uint32_t a[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) { const float2 f = unpack_bf16(a[k]); s += f.x * f.x + f.y * f.y; }
+    }
+    const float r = rsqrtf(warp_sum(s) / D + eps);
+    uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * D);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nv) {
+        const float4 wa = w4[2 * c], wb = w4[2 * c + 1];
+        const float ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t a[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = unpack_bf16(a[k]);
+          o[k] = pack_bf16(f.x * r * ws[2 * k], f.y * r * ws[2 * k + 1]);
+        }
+        yr[c] = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      yr[c] = make_uint4(o[0], o[1], o[2], o[3]);
     }
     if (lane == 0) rstd[row] = r;
   }
 }
 
-// RMSNorm backward: register column accumulators, one partial row of dw per block.
+// RMSNorm backward: one warp per row with the row of x and dy in registers (all loads
+// in flight together); dw column partials accumulate in the warp's own shared-memory
+// row (a column belongs to one lane, no conflicts) and each block writes one partial
+// row, summed by col_sum_k.  w must be 16-byte aligned.
 template <int PER>
-__global__ void rms_bwd_k(const bf16* __restrict__ dy, const bf16* __restrict__ x, const float* __restrict__ w,
-                          const float* __restrict__ rstd, bf16* __restrict__ dx, float* __restrict__ dw, int T,
-                          int D) {
-  int lane = threadIdx.x & 31;
-  int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int nw = (gridDim.x * blockDim.x) >> 5;
-  int nv = D / 8;   // uint4 chunks per row; lane handles chunks lane + 32*j
-  float aw[PER * 8];
-#pragma unroll
-  for (int i = 0; i < PER * 8; ++i) aw[i] = 0.f;
+__global__ void __launch_bounds__(256, 2) rms_bwd_k(const bf16* __restrict__ dy, const bf16* __restrict__ x,
+                                                 const float* __restrict__ w, const float* __restrict__ rstd,
+                                                 bf16* __restrict__ dx, float* __restrict__ dw, int T, int D) {
+  extern __shared__ __align__(16) float red_smem[];   // [8][D]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int nv = D / 8;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float* sw = red_smem + (size_t)wid * D;
+  for (int c = lane * 4; c < D; c += 128) *reinterpret_cast<float4*>(sw + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncwarp();
   for (int row = gw; row < T; row += nw) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
     const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * D);
-    float r = rstd[row];
+    const float r = rstd[row];
+    uint4 ux[PER], ug[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = lane + 32 * j;
+      const bool ok = c < nv;
+      ux[j] = ok ? xr[c] : make_uint4(0u, 0u, 0u, 0u);
+      ug[j] = ok ? gr[c] : make_uint4(0u, 0u, 0u, 0u);
+    }
     float m = 0.f;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-      int c = lane + 32 * j;
+      const int c = lane + 32 * j;
       if (c < nv) {
-        uint4 ux = xr[c], ug = gr[c];
-        uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w};
+        const float4 wa = w4[2 * c], wb = w4[2 * c + 1];
+        const float ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t ax[4] = {ux[j].x, ux[j].y, ux[j].z, ux[j].w}, ag[4] = {ug[j].x, ug[j].y, ug[j].z, ug[j].w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
-          int col = c * 8 + 2 * k;
-          m += fg.x * w[col] * fx.x + fg.y * w[col + 1] * fx.y;
-          aw[j * 8 + 2 * k] += fg.x * fx.x * r;
-          aw[j * 8 + 2 * k + 1] += fg.y * fx.y * r;
+          const float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          m += fg.x * ws[2 * k] * fx.x + fg.y * ws[2 * k + 1] * fx.y;
         }
       }
     }
     m = warp_sum(m) / D;
+    const float r3m = r * r * r * m;
     uint4* dr = reinterpret_cast<uint4*>(dx + (size_t)row * D);
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-      int c = lane + 32 * j;
+      const int c = lane + 32 * j;
       if (c < nv) {
-        uint4 ux = xr[c], ug = gr[c];
-        uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w}, o[4];
+        const float4 wa = w4[2 * c], wb = w4[2 * c + 1];
+        const float ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t ax[4] = {ux[j].x, ux[j].y, ux[j].z, ux[j].w}, ag[4] = {ug[j].x, ug[j].y, ug[j].z, ug[j].w};
+        uint32_t o[4];
+        float cw[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
-          int col = c * 8 + 2 * k;
-          float d0 = r * fg.x * w[col] - fx.x * r * r * r * m;
-          float d1 = r * fg.y * w[col + 1] - fx.y * r * r * r * m;
-          o[k] = pack_bf16(d0, d1);
+          const float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          o[k] = pack_bf16(r * fg.x * ws[2 * k] - fx.x * r3m, r * fg.y * ws[2 * k + 1] - fx.y * r3m);
+          cw[2 * k] = fg.x * fx.x * r;
+          cw[2 * k + 1] = fg.y * fx.y * r;
+        }
+        dr[c] = make_uint4(o[0], o[1], o[2], o[3]);
+        add4(sw + c * 8, make_float4(cw[0], cw[1], cw[2], cw[3]));
+        add4(sw + c * 8 + 4, make_float4(cw[4], cw[5], cw[6], cw[7]));
+      }
+    }
+  }
+  __syncthreads();
+  const int nwb = blockDim.x >> 5;
+  for (int col = threadIdx.x; col < D; col += blockDim.x) {
+    float t = 0.f;
+    for (int k = 0; k < nwb; ++k) t += red_smem[(size_t)k * D + col];
+    dw[(size_t)blockIdx.x * D + col] = t;   // this block's partial row (dw is the partial buffer)
+  }
+}
+
+// RMSNorm backward, pipelined: each warp stages its NEXT row of x and dy in shared
+// memory with cp.async while it computes the current one, so every warp always has a
+// row in flight (the register version issues one row's loads, waits, computes, and
+// only then loads the next).  12 warps per block, one block per SM:
+//   stage [12 warps][2 buffers][x | dy][D] bf16 + w [D] + dw accumulators [D] fp32.
+// dw partials accumulate in registers (a lane owns its columns for every row), then the
+// block's warps are summed through shared memory into one partial row for col_sum_k.
+constexpr int RB_NW = 12;
+template <int PER>
+__global__ void __launch_bounds__(RB_NW * 32, 1)
+    rms_bwd_pipe_k(const bf16* __restrict__ dy, const bf16* __restrict__ x, const float* __restrict__ w,
+                   const float* __restrict__ rstd, bf16* __restrict__ dx, float* __restrict__ part, int T, int D) {
+  extern __shared__ __align__(16) unsigned char rb_smem[];
+  float* sw = reinterpret_cast<float*>(rb_smem);                 // [D]
+  float* sred = sw + D;                                          // [D] (unused until the end)
+  bf16* stage = reinterpret_cast<bf16*>(sred + D);               // [RB_NW][2][2][D]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nv = D / 8;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) sw[c] = w[c];
+  float aw[PER * 8];
+#pragma unroll
+  for (int i = 0; i < PER * 8; ++i) aw[i] = 0.f;
+  bf16* my = stage + (size_t)wid * 4 * D;
+  const int gw = blockIdx.x * RB_NW + wid, nw = gridDim.x * RB_NW;
+  auto issue = [&](int row, int buf) {
+    bf16* bx = my + (size_t)buf * 2 * D;
+    bf16* bg = bx + D;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nv) {
+        cp_async16(bx + c * 8, x + (size_t)row * D + c * 8);
+        cp_async16(bg + c * 8, dy + (size_t)row * D + c * 8);
+      }
+    }
+  };
+  __syncthreads();
+  int buf = 0;
+  float r_next = 0.f;
+  if (gw < T) { issue(gw, 0); r_next = rstd[gw]; }
+  cp_async_commit();
+  for (int row = gw; row < T; row += nw) {
+    const float r = r_next;
+    const int nxt = row + nw;
+    if (nxt < T) { issue(nxt, buf ^ 1); r_next = rstd[nxt]; }
+    cp_async_commit();
+    cp_async_wait_group<1>();        // this row's copies (this lane's own chunks) are in
+    const bf16* bx = my + (size_t)buf * 2 * D;
+    const bf16* bg = bx + D;
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nv) {
+        const uint4 ux = *reinterpret_cast<const uint4*>(bx + c * 8);
+        const uint4 ug = *reinterpret_cast<const uint4*>(bg + c * 8);
+        const float4 wa = *reinterpret_cast<const float4*>(sw + c * 8);
+        const float4 wb = *reinterpret_cast<const float4*>(sw + c * 8 + 4);
+        const float ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          m += fg.x * ws[2 * k] * fx.x + fg.y * ws[2 * k + 1] * fx.y;
+        }
+      }
+    }
+    m = warp_sum(m) / D;
+    const float r3m = r * r * r * m;
+    uint4* dr = reinterpret_cast<uint4*>(dx + (size_t)row * D);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nv) {
+        const uint4 ux = *reinterpret_cast<const uint4*>(bx + c * 8);
+        const uint4 ug = *reinterpret_cast<const uint4*>(bg + c * 8);
+        const float4 wa = *reinterpret_cast<const float4*>(sw + c * 8);
+        const float4 wb = *reinterpret_cast<const float4*>(sw + c * 8 + 4);
+        const float ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t ax[4] = {ux.x, ux.y, ux.z, ux.w}, ag[4] = {ug.x, ug.y, ug.z, ug.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          o[k] = pack_bf16(r * fg.x * ws[2 * k] - fx.x * r3m, r * fg.y * ws[2 * k + 1] - fx.y * r3m);
+          aw[j * 8 + 2 * k] += fg.x * fx.x * r;
+          aw[j * 8 + 2 * k + 1] += fg.y * fx.y * r;
         }
         dr[c] = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
+    buf ^= 1;
   }
-  // block reduction: smem[w][col] then one atomic per column per block
-  extern __shared__ float red_smem[];
-  int wid = threadIdx.x >> 5, nwb = blockDim.x >> 5;
-  for (int i = threadIdx.x; i < nwb * D; i += blockDim.x) red_smem[i] = 0.f;
+  cp_async_wait_all();
   __syncthreads();
+  // block sum of the warps' column partials: the staging area becomes [RB_NW][D] floats
+  float* red = reinterpret_cast<float*>(stage);
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
-    int c = lane + 32 * j;
-    if (c < nv)
-#pragma unroll
-      for (int k = 0; k < 8; ++k) red_smem[wid * D + c * 8 + k] = aw[j * 8 + k];
+    const int c = lane + 32 * j;
+    if (c < nv) {
+      *reinterpret_cast<float4*>(red + (size_t)wid * D + c * 8) = make_float4(aw[j * 8], aw[j * 8 + 1], aw[j * 8 + 2], aw[j * 8 + 3]);
+      *reinterpret_cast<float4*>(red + (size_t)wid * D + c * 8 + 4) =
+          make_float4(aw[j * 8 + 4], aw[j * 8 + 5], aw[j * 8 + 6], aw[j * 8 + 7]);
+    }
   }
   __syncthreads();
-  for (int col = threadIdx.x; col < D; col += blockDim.x) {
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
     float t = 0.f;
-    for (int k = 0; k < nwb; ++k) t += red_smem[k * D + col];
-    dw[(size_t)blockIdx.x * D + col] = t;   // this block's partial row (dw is the partial buffer)
+#pragma unroll
+    for (int k = 0; k < RB_NW; ++k) t += red[(size_t)k * D + c];
+    part[(size_t)blockIdx.x * D + c] = t;
   }
 }
 
@@ -569,10 +810,26 @@ void ln_bwd_launch(const void* dy, const float* x, const float* mean, const floa
   else { allow_smem(ln_bwd_k<16>, sm); ln_bwd_k<16><<<gr, CB_NT, sm, st>>>(g, x, mean, rstd, w, dres, dx, part, (int)T, D); }
   col_sum(part, gr, 2, D, dw, db, st);
 }
+// pipelined variant (512 < D <= 1024): one block per SM; `part` holds >= sms rows of 2D
+void ln_bwd_pipe_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,
+                        const float* dres, float* dx, float* dw, float* db, float* part, long T, int D, int sms,
+                        cudaStream_t st) {
+  const int gr = (int)(T < sms ? T : sms);
+  const size_t sm = sizeof(float) * ((size_t)3 * D + (size_t)LB_NW * 2 * (2 * D + D / 2));   // w, spare, stage
+  allow_smem(ln_bwd_pipe_k, sm);
+  ln_bwd_pipe_k<<<gr, LB_NW * 32, sm, st>>>(reinterpret_cast<const bf16*>(dy), x, mean, rstd, w, dres, dx, part,
+                                            (int)T, D);
+  col_sum(part, gr, 2, D, dw, db, st);
+}
 void rms_fwd_launch(const void* x, const float* w, void* y, float* rstd, long T, int D, float eps, int sms,
                     cudaStream_t st) {
-  rms_fwd_k<<<row_grid(T, sms), 256, 0, st>>>(reinterpret_cast<const bf16*>(x), w, reinterpret_cast<bf16*>(y),
-                                             rstd, (int)T, D, eps);
+  const int nv = D / 8, gr = row_grid(T, sms);
+  const bf16* xp = reinterpret_cast<const bf16*>(x);
+  bf16* yp = reinterpret_cast<bf16*>(y);
+  if (nv <= 32) rms_fwd_k<1><<<gr, 256, 0, st>>>(xp, w, yp, rstd, (int)T, D, eps);
+  else if (nv <= 64) rms_fwd_k<2><<<gr, 256, 0, st>>>(xp, w, yp, rstd, (int)T, D, eps);
+  else if (nv <= 128) rms_fwd_k<4><<<gr, 256, 0, st>>>(xp, w, yp, rstd, (int)T, D, eps);
+  else rms_fwd_k<8><<<gr, 256, 0, st>>>(xp, w, yp, rstd, (int)T, D, eps);
 }
 void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw,
                     float* part, long T, int D, int sms, cudaStream_t st) {
@@ -582,13 +839,20 @@ void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* 
   bf16* o = reinterpret_cast<bf16*>(dx);
   const int nv = D / 8;
   const size_t sm = 8 * (size_t)D * 4;
-  if (nv <= 32) rms_bwd_k<1><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
-  else if (nv <= 64) rms_bwd_k<2><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
-  else if (nv <= 128) rms_bwd_k<4><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
-  else {
-    allow_smem(rms_bwd_k<8>, sm);
-    rms_bwd_k<8><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D);
-  }
+  if (nv <= 32) { allow_smem(rms_bwd_k<1>, sm); rms_bwd_k<1><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
+  else if (nv <= 64) { allow_smem(rms_bwd_k<2>, sm); rms_bwd_k<2><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
+  else if (nv <= 128) { allow_smem(rms_bwd_k<4>, sm); rms_bwd_k<4><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
+  else { allow_smem(rms_bwd_k<8>, sm); rms_bwd_k<8><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
+  col_sum(part, gr, 1, D, dw, nullptr, st);
+}
+// pipelined variant for wide rows (D > 1024): one block per SM; `part` holds >= sms rows
+void rms_bwd_pipe_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw,
+                         float* part, long T, int D, int sms, cudaStream_t st) {
+  const int gr = (int)(T < sms ? T : sms);
+  const size_t sm = (size_t)2 * D * 4 + (size_t)RB_NW * 4 * D * 2;
+  allow_smem(rms_bwd_pipe_k<8>, sm);
+  rms_bwd_pipe_k<8><<<gr, RB_NW * 32, sm, st>>>(reinterpret_cast<const bf16*>(dy), reinterpret_cast<const bf16*>(x),
+                                                 w, rstd, reinterpret_cast<bf16*>(dx), part, (int)T, D);
   col_sum(part, gr, 1, D, dw, nullptr, st);
 }
 void gelu_fwd_launch(const void* o, void* g, long n, int sms, cudaStream_t st) {

@@ -133,3 +133,8 @@ void m3_decode_multi_launch(const void* proj, int B, int T, int ldp, int nh, con
                             float eps, float* ang, float* ssm, float* kprev, float* vprev, void* y,
                             cudaStream_t st);
 bool m3_phase_probe_read(unsigned long long* out);
+void rms_bwd_pipe_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw,
+                         float* part, long T, int D, int sms, cudaStream_t st);
+void ln_bwd_pipe_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,
+                        const float* dres, float* dx, float* dw, float* db, float* part, long T, int D, int sms,
+                        cudaStream_t st);

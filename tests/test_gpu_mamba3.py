@@ -169,3 +169,45 @@ def test_odd_width_book_layer_paths_match_fp32():
     m.impl = "torch"
     y2 = m(u)
     assert rel(y, y2) < 3e-2, rel(y, y2)
+
+
+@pytest.mark.parametrize("T,D", [(300, 2048), (5000, 2048), (257, 1024), (100, 2048), (40, 64)])
+def test_rmsnorm_kernels_match_fp32(T, D):
+    """rms_fwd / rms_bwd (register and pipelined variants) against fp32 autograd."""
+    from sigma0_b200.ops._ext import ext
+    C = ext()
+    torch.manual_seed(D + T)
+    x = (torch.randn(T, D, device="cuda") * 2).to(torch.bfloat16)
+    w = torch.randn(D, device="cuda") * 0.5 + 1
+    g = torch.randn(T, D, device="cuda").to(torch.bfloat16)
+    y, r = C.rms_fwd(x, w, 1e-6)
+    xf = x.float().requires_grad_(True)
+    wf = w.clone().requires_grad_(True)
+    yr = xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + 1e-6) * wf
+    (yr * g.float()).sum().backward()
+    assert rel(y, yr.detach()) < 1e-2
+    dx, dw = C.rms_bwd(g, x, w, r)
+    assert rel(dx, xf.grad) < 1e-2, rel(dx, xf.grad)
+    assert rel(dw, wf.grad) < 1e-3, rel(dw, wf.grad)
+
+
+@pytest.mark.parametrize("T,D,res", [(3000, 1024, True), (200, 1024, False), (150, 768, True), (90, 1024, True),
+                                     (500, 512, True)])
+def test_layernorm_backward_matches_fp32(T, D, res):
+    """ln_bwd (register and pipelined variants) with the residual gradient against fp32 autograd."""
+    from sigma0_b200.ops._ext import ext
+    C = ext()
+    torch.manual_seed(T + D)
+    x = torch.randn(T, D, device="cuda") * 2 + 0.5
+    w = torch.randn(D, device="cuda") * 0.5 + 1
+    b = torch.randn(D, device="cuda") * 0.1
+    xn, mu, rs = C.ln_fwd(x, w, b, 1e-6)
+    g = torch.randn(T, D, device="cuda").to(torch.bfloat16)
+    dres = torch.randn(T, D, device="cuda") if res else None
+    xf, wf, bf = (t.clone().requires_grad_(True) for t in (x, w, b))
+    yr = torch.nn.functional.layer_norm(xf, (D,), wf, bf, 1e-6)
+    (yr * g.float()).sum().backward()
+    dx, dw, db = C.ln_bwd(g, x, mu, rs, w, dres)
+    want = xf.grad + (dres if res else 0)
+    assert rel(dx, want) < 1e-3, rel(dx, want)
+    assert rel(dw, wf.grad) < 1e-3 and rel(db, bf.grad) < 1e-3
