@@ -262,6 +262,7 @@ std::vector<at::Tensor> glu_res_bwd(at::Tensor dout, at::Tensor g, at::Tensor h,
   c10::cuda::CUDAGuard guard(dout.device());
   auto dh = at::empty(dout.sizes(), dout.options().dtype(at::kBFloat16));
   TORCH_CHECK(D % 4 == 0 && D <= 2048, "GLU width must be a multiple of 4, at most 2048");
+  if (reinterpret_cast<uintptr_t>(b.data_ptr()) % 16) b = b.clone();   // read as float4
   auto dgp = at::empty_like(dout);
   auto db = at::empty({D}, dout.options());
   auto part = at::empty({(int64_t)col_blocks(T, num_sms(dout)), D}, dout.options());

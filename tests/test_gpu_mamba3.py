@@ -211,3 +211,21 @@ def test_layernorm_backward_matches_fp32(T, D, res):
     want = xf.grad + (dres if res else 0)
     assert rel(dx, want) < 1e-3, rel(dx, want)
     assert rel(dw, wf.grad) < 1e-3 and rel(db, bf.grad) < 1e-3
+
+
+@pytest.mark.parametrize("T,D", [(3000, 1024), (100, 512), (77, 1024), (50, 200)])
+def test_glu_residual_backward_matches_fp32(T, D):
+    """glu_res_bwd (column-owner and row variants) against fp32 autograd of x + g * sigmoid(h + b)."""
+    from sigma0_b200.ops._ext import ext
+    C = ext()
+    torch.manual_seed(T * 7 + D)
+    g = torch.randn(T, D, device="cuda").to(torch.bfloat16)
+    h = torch.randn(T, D, device="cuda").to(torch.bfloat16)
+    b = torch.randn(D, device="cuda") * 0.3
+    dout = torch.randn(T, D, device="cuda")
+    gf, hf, bf = g.float().requires_grad_(True), h.float().requires_grad_(True), b.clone().requires_grad_(True)
+    (((gf * torch.sigmoid(hf + bf)) * dout).sum()).backward()
+    dh, dgp, db = C.glu_res_bwd(dout, g, h, b)
+    assert rel(dh, hf.grad) < 1e-2, rel(dh, hf.grad)
+    assert rel(dgp, gf.grad) < 1e-5, rel(dgp, gf.grad)
+    assert rel(db, bf.grad) < 1e-4, rel(db, bf.grad)
