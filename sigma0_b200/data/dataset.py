@@ -8,9 +8,14 @@ The book input is one row per message (the state before that message) after
 the volume-image transform; the model repeats it to token resolution on the
 device (the reference's ``repeat_book``, ``training/train_helpers.py:1383``).
 
+Other objectives (``mask=``): ``"inference"``, ``"random"``, ``"causal"`` or any
+``fn(seq (n_messages, MSG_LEN), rng) -> (masked seq, label)`` from ``data/masks.py``;
+these return the flattened masked window and a scalar label.  ``book_ablation`` replaces
+the book input by zeros, noise or a shuffled copy (seeded per window).
+
 Sources are either in-memory :class:`~sigma0_b200.data.synthetic.SyntheticDay`
-objects or ``.npy`` message/book file pairs (the reference's on-disk layout,
-optionally zstd-compressed ``.npy.zst`` is not supported without zstandard).
+objects or ``.npy`` message/book file pairs (the reference's on-disk layout;
+``.npy.zst`` files load when the ``zstandard`` module is available).
 """
 from __future__ import annotations
 
@@ -21,14 +26,17 @@ import numpy as np
 import torch
 
 from ..encoding import get_tokenizer, START_TOK
+from . import masks as M
 from .book_transform import transform_books_numpy
 
 
 class LobWindowDataset(torch.utils.data.Dataset):
     def __init__(self, msgs: Sequence[np.ndarray], books: Sequence[np.ndarray], n_messages: int,
                  token_mode: str = "22tok", book_depth: int = 500, use_book_data: bool = True,
-                 stride: Optional[int] = None, return_raw_msgs: bool = False):
+                 stride: Optional[int] = None, return_raw_msgs: bool = False, mask="no_mask",
+                 book_ablation: str = "real", seed: int = 0):
         self.tok = get_tokenizer(token_mode)
+        self.mask, self.book_ablation, self.seed = mask, book_ablation, seed
         self.n = n_messages
         self.book_depth = book_depth
         self.use_book = use_book_data
@@ -47,10 +55,12 @@ class LobWindowDataset(torch.utils.data.Dataset):
 
     @classmethod
     def from_dir(cls, directory: str, n_messages: int, **kw):
-        mf = sorted(f for f in os.listdir(directory) if f.endswith("message.npy"))
-        bf = sorted(f for f in os.listdir(directory) if f.endswith("book.npy"))
-        msgs = [np.load(os.path.join(directory, f), mmap_mode="r") for f in mf]
-        books = [np.load(os.path.join(directory, f), mmap_mode="r") for f in bf]
+        def names(tag):
+            fs = {f[:-4] if f.endswith(".zst") else f for f in os.listdir(directory)
+                  if f.endswith(tag + ".npy") or f.endswith(tag + ".npy.zst")}
+            return sorted(fs)
+        msgs = [M.load_npy(os.path.join(directory, f)) for f in names("message")]
+        books = [M.load_npy(os.path.join(directory, f)) for f in names("book")]
         return cls(msgs, books, n_messages, **kw)
 
     def __len__(self):
@@ -59,13 +69,27 @@ class LobWindowDataset(torch.utils.data.Dataset):
     def __getitem__(self, i):
         f, s = self.index[i]
         raw = np.asarray(self.msgs[f][s:s + self.n])
-        x = self.tok.encode_msgs(raw).reshape(-1)
-        y = x.copy()
-        x = np.concatenate([[START_TOK], x[:-1]]).astype(np.int64)
-        out = [torch.from_numpy(x), torch.from_numpy(y.astype(np.int64))]
+        enc = self.tok.encode_msgs(raw)
+        if self.mask == "no_mask":
+            x = enc.reshape(-1)
+            y = x.copy()
+            x = np.concatenate([[START_TOK], x[:-1]])
+        elif self.mask == "inference":
+            (x, _), y = M.inference_mask(enc)
+        else:
+            rng = np.random.default_rng([self.seed, f, s])
+            if self.mask == "random":
+                m, y = M.random_mask(self.tok, enc, rng)
+            elif self.mask == "causal":
+                m, y = M.causal_mask(self.tok, enc, rng)
+            else:
+                m, y = self.mask(enc, rng)
+            x = np.asarray(m).reshape(-1)
+        out = [torch.from_numpy(np.asarray(x, dtype=np.int64)), torch.from_numpy(np.asarray(y, dtype=np.int64))]
         if self.use_book:
             b = transform_books_numpy(np.asarray(self.books[f][s:s + self.n]), self.book_depth)
-            out.append(torch.from_numpy(b))
+            b = M.ablate_books(b, self.book_ablation, (f, s))
+            out.append(torch.from_numpy(np.ascontiguousarray(b)))
         if self.return_raw:
             out.append(torch.from_numpy(raw))
         return tuple(out)
