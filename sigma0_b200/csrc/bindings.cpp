@@ -83,7 +83,7 @@ M3Pre m3_prepare(const at::Tensor& proj, int64_t B, int64_t L, int64_t nh, const
 // y = ssd(proj); returns (y, states) -- states is the S_in of every chunk (bf16)
 std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh, at::Tensor wB, at::Tensor wC,
                                at::Tensor dt_bias, at::Tensor Bb, at::Tensor Cb, at::Tensor D, double A_floor,
-                               double eps, bool want_final = false) {
+                               double eps, bool want_final = false, bool return_prep = false) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
   M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
@@ -101,16 +101,29 @@ std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh
     auto last = pre.theta0.select(2, nc - 1) + pre.angtot.select(2, nc - 1);
     thf = last - 2 * M_PI * at::floor(last / (2 * M_PI));
   }
+  if (return_prep)   // the per-token prep and chunk carries, so the backward need not recompute them
+    return {y, states, fin, thf, pre.bc, pre.dt, pre.adt, pre.sig, pre.rate, pre.aend, pre.theta0};
   return {y, states, fin, thf};
 }
 
 std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias,
                                at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B, int64_t L, int64_t nh,
-                               double A_floor, double eps, c10::optional<at::Tensor> saved_states) {
+                               double A_floor, double eps, c10::optional<at::Tensor> saved_states,
+                               c10::optional<std::vector<at::Tensor>> saved_prep) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
   req(dy, at::kBFloat16, "dy");
-  M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
+  M3Pre pre;
+  if (saved_prep.has_value() && saved_prep->size() == 7) {   // (bc, dt, adt, sig, rate, aend, theta0) of m3_fwd
+    const auto& v = *saved_prep;
+    pre.bc = v[0]; pre.dt = v[1]; pre.adt = v[2]; pre.sig = v[3]; pre.rate = v[4]; pre.aend = v[5]; pre.theta0 = v[6];
+    req(pre.bc, at::kBFloat16, "saved_prep bc");
+    TORCH_CHECK(pre.bc.numel() == B * L * 2 * M3_N && pre.dt.numel() == B * nh * L &&
+                    pre.theta0.numel() == B * nh * m3_nchunks((int)L) * M3_R,
+                "saved_prep shapes do not match this call");
+  } else {
+    pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
+  }
   int nc = m3_nchunks((int)L);
   M3Scan s = m3_scan(proj, pre, Bb, Cb, D);
   at::Tensor states;
@@ -522,10 +535,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sigma0_b200 sm_100a kernels";
   m.def("m3_fwd", &m3_fwd, py::arg("proj"), py::arg("B"), py::arg("L"), py::arg("nh"), py::arg("wB"), py::arg("wC"),
         py::arg("dt_bias"), py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("A_floor"), py::arg("eps"),
-        py::arg("want_final") = false, "Mamba3 SSD forward (prep, chunk states, passing, chunk scan) -> (y, states)");
+        py::arg("want_final") = false, py::arg("return_prep") = false,
+        "Mamba3 SSD forward (prep, chunk states, passing, chunk scan) -> (y, states, final state, final angle"
+        "[, bc, dt, adt, sig, rate, aend, theta0])");
   m.def("m3_bwd", &m3_bwd, py::arg("proj"), py::arg("dy"), py::arg("wB"), py::arg("wC"), py::arg("dt_bias"),
         py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("B"), py::arg("L"), py::arg("nh"), py::arg("A_floor"),
-        py::arg("eps"), py::arg("saved_states") = py::none(),
+        py::arg("eps"), py::arg("saved_states") = py::none(), py::arg("saved_prep") = py::none(),
         "Mamba3 SSD backward -> (dproj, dB_norm, dC_norm, ddt_bias, dD, dC_bias, dB_bias)");
   m.def("ln_fwd", &ln_fwd);
   m.def("ln_bwd", &ln_bwd);

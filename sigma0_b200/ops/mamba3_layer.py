@@ -30,6 +30,9 @@ EPS = 1e-6
 # keep the forward's passed SSD chunk states for the backward instead of recomputing
 # them (S0_RECOMPUTE_SSD_STATES=1 trades ~1 ms per layer-step for ~0.7 GB per layer)
 SAVE_STATES = os.environ.get("S0_RECOMPUTE_SSD_STATES", "0") in ("0", "", "false")
+# keep the fused layer's LayerNorm output and GELU output (bf16, 2 x T x d_model) for the
+# backward instead of recomputing them (S0_SAVE_LAYER_ACTS=0 recomputes: memory for time)
+SAVE_ACTS = os.environ.get("S0_SAVE_LAYER_ACTS", "1") not in ("0", "", "false")
 
 
 def _pad8(n: int) -> int:
@@ -65,19 +68,23 @@ class _Mamba3Core:
             xn = F.pad(xn, (0, Hp - H))
             w_in = F.pad(w_in, (0, 0, 0, Hp - H))
         proj = xn @ w_in                                              # [T, ldp]
-        y, states = C.m3_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias,
-                             m.C_bias, m.D, m.A_floor, m.B_norm.eps)[:2]
+        out = C.m3_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias,
+                       m.C_bias, m.D, m.A_floor, m.B_norm.eps, return_prep=SAVE_STATES)
+        y, states = out[0], out[1]
+        prep = tuple(out[4:]) if SAVE_STATES else ()
         y2 = y.view(-1, d.d_inner)
         yn, yr = C.rms_fwd(y2, m.out_norm.scale, m.out_norm.eps)
         o = yn @ W.bf16_padded(m.out_proj.kernel, Hp)                 # [T, Hp]
         if Hp != H:
             o = o[:, :H]
-        # the passed chunk states are kept for the backward (bf16, B*nh*nc*P*N) unless the
-        # model is set to recompute them (memory for time)
-        return o, proj, y2, yr, (states if SAVE_STATES else None)
+        # the passed chunk states (bf16, B*nh*nc*P*N) and the per-token prep (BCNorm'd B/C,
+        # dt, decay, gate, angle rates, chunk carries: ~1/8 of the states' size) are kept for
+        # the backward unless the model is set to recompute them (memory for time)
+        return o, proj, y2, yr, ((states,) + prep if SAVE_STATES else None)
 
     @staticmethod
     def backward(do, xn, proj, y2, yr, B, L, m, states=None):
+        """``states``: None, or the forward's saved (states, *prep) tuple."""
         """Returns (dxn bf16, grads dict keyed by parameter)."""
         C = ext()
         d = m.dims
@@ -94,9 +101,11 @@ class _Mamba3Core:
         g_out_proj = _mm_f32(yn.t(), do)[:, :H]
         dyn = do @ w_out.t()
         dy, g_out_norm = C.rms_bwd(dyn.contiguous(), y2, m.out_norm.scale, yr)
+        saved_states = states[0] if states else None
+        saved_prep = list(states[1:]) if states and len(states) == 8 else None
         dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_bwd(
             proj, dy, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D, B, L,
-            d.n_heads, m.A_floor, m.B_norm.eps, saved_states=states)
+            d.n_heads, m.A_floor, m.B_norm.eps, saved_states=saved_states, saved_prep=saved_prep)
         g_in = _mm_f32(xn.t(), dproj)[:H, :d.d_in_proj]
         dxn = (dproj @ w_in.t())[:, :H]
         grads = {m.out_proj.kernel: g_out_proj, m.out_norm.scale: g_out_norm, m.in_proj.kernel: g_in,
@@ -117,12 +126,14 @@ class _MixerFn(torch.autograd.Function):
         xn = u.reshape(-1, H).to(torch.bfloat16).contiguous()
         o, proj, y2, yr, st = _Mamba3Core.forward(xn, B, L, module)
         ctx.module, ctx.shape, ctx.in_dtype = module, (B, L, H), u.dtype
-        ctx.save_for_backward(xn, proj, y2, yr, st)
+        ctx.n_st = 0 if st is None else len(st)
+        ctx.save_for_backward(xn, proj, y2, yr, *(st or ()))
         return o.view(B, L, H)
 
     @staticmethod
     def backward(ctx, do):
-        xn, proj, y2, yr, st = ctx.saved_tensors
+        xn, proj, y2, yr, *st = ctx.saved_tensors
+        st = tuple(st) if ctx.n_st else None
         B, L, H = ctx.shape
         m = ctx.module
         do = do.reshape(-1, H).to(torch.bfloat16).contiguous()
@@ -151,25 +162,31 @@ class _LayerFn(torch.autograd.Function):
         h = g @ W.bf16(layer.out2.kernel)
         out = C.glu_res_fwd(xf, g, h, layer.out2.bias)
         ctx.layer, ctx.shape = layer, (B, L, H)
-        ctx.save_for_backward(xf, mu, rs, proj, y2, yr, o, h, st)
+        ctx.n_st = 0 if st is None else len(st)
+        ctx.saved_acts = SAVE_ACTS
+        acts = (xn, g) if SAVE_ACTS else ()
+        ctx.save_for_backward(xf, mu, rs, proj, y2, yr, o, h, *acts, *(st or ()))
         return out.view(B, L, H)
 
     @staticmethod
     def backward(ctx, dout):
         C = ext()
-        xf, mu, rs, proj, y2, yr, o, h, st = ctx.saved_tensors
+        xf, mu, rs, proj, y2, yr, o, h, *rest = ctx.saved_tensors
+        if ctx.saved_acts:
+            xn_s, g_s, *rest = rest
+        st = tuple(rest) if ctx.n_st else None
         layer = ctx.layer
         m = layer.seq
         B, L, H = ctx.shape
         dout = dout.reshape(-1, H)
         if dout.dtype != torch.float32 or not dout.is_contiguous():
             dout = dout.float().contiguous()
-        g = C.gelu_fwd(o)
+        g = g_s if ctx.saved_acts else C.gelu_fwd(o)
         dh, dgp, db2 = C.glu_res_bwd(dout, g, h, layer.out2.bias)
         g_out2 = _mm_f32(g.t(), dh)
         dgm = dh @ W.bf16(layer.out2.kernel).t()
         do = C.gelu_bwd(o, dgp, dgm.contiguous())
-        xn, _, _ = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)
+        xn = xn_s if ctx.saved_acts else C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)[0]
         dxn, grads = _Mamba3Core.backward(do, xn, proj, y2, yr, B, L, m, st)
         dx, dlw, dlb = C.ln_bwd(dxn.contiguous(), xf, mu, rs, layer.norm.scale, dout)
         grads[layer.norm.scale] = dlw
