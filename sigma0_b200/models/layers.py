@@ -84,6 +84,9 @@ class SequenceLayer(nn.Module):
     def step(self, state, x):
         if self.is_transformer:
             return self.seq.step(state, x)
+        if self._fused_ok(x) and x.shape[1] <= 8:
+            from ..ops.mamba3_layer import mamba3_layer_step
+            return mamba3_layer_step(state, x, self)
         skip = x
         if self.prenorm:
             x = self.norm(x)
@@ -98,6 +101,9 @@ class SequenceLayer(nn.Module):
         """Training-identical forward that also returns the decode state."""
         if self.is_transformer:
             return self.seq.prefill(x, max_cache_len)
+        if self._fused_ok(x):
+            from ..ops.mamba3_layer import mamba3_layer_prefill
+            return mamba3_layer_prefill(x, self)
         skip = x
         h = self.norm(x) if self.prenorm else x
         if hasattr(self.seq, "prefill"):

@@ -196,6 +196,42 @@ class _LayerFn(torch.autograd.Function):
         return (dx.view(B, L, H), None) + tuple(grads[p] for p in _layer_params(layer))
 
 
+@torch.no_grad()
+def mamba3_layer_prefill(x: torch.Tensor, layer):
+    """(decode state, output) of the fused half_glu1 Mamba3 layer over a context: the same
+    kernels as the training forward (LayerNorm, chunked SSD with its final state, RMSNorm,
+    GELU, gate + residual), so generation conditions on exactly the training function."""
+    C = ext()
+    B, L, H = x.shape
+    xf = x.reshape(-1, H)
+    if xf.dtype != torch.float32 or not xf.is_contiguous():
+        xf = xf.float().contiguous()
+    xn, _, _ = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)
+    st, o = layer.seq.prefill(xn.view(B, L, H))
+    g = C.gelu_fwd(o.reshape(-1, H).to(torch.bfloat16).contiguous())
+    h = g @ W.bf16(layer.out2.kernel)
+    out = C.glu_res_fwd(xf, g, h, layer.out2.bias)
+    return st, out.view(B, L, H)
+
+
+@torch.no_grad()
+def mamba3_layer_step(state, x: torch.Tensor, layer):
+    """Recurrent step (1..8 known tokens) of the fused half_glu1 Mamba3 layer with the
+    training forward's row kernels (4 launches + 3 GEMMs + the decode kernel per layer
+    instead of a chain of elementwise ops)."""
+    C = ext()
+    B, L, H = x.shape
+    xf = x.reshape(-1, H)
+    if xf.dtype != torch.float32 or not xf.is_contiguous():
+        xf = xf.float().contiguous()
+    xn, _, _ = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)
+    state, o = layer.seq.step(state, xn.view(B, L, H))
+    g = C.gelu_fwd(o.reshape(-1, H).to(torch.bfloat16).contiguous())
+    h = g @ W.bf16(layer.out2.kernel)
+    out = C.glu_res_fwd(xf, g, h, layer.out2.bias)
+    return state, out.view(B, L, H)
+
+
 def _layer_params(layer):
     return [layer.norm.scale, layer.norm.bias] + _mixer_params(layer.seq) + [layer.out2.kernel, layer.out2.bias]
 

@@ -230,3 +230,25 @@ def test_generator_graph_equals_eager():
             r = raw[b, k]
             ob.process(np.array([r[1], r[2] * 2 - 1, r[5], r[3], r[0], -88, r[8], r[9]]))
             assert np.array_equal(ob.l2(10), outs[1].l2[b, k].cpu().numpy())
+
+
+def test_fused_layer_prefill_matches_forward_and_steps():
+    """SequenceLayer.prefill on the fused CUDA path: output == the training forward, and the
+    returned state continues like stepping the unfused layer token by token."""
+    from sigma0_b200.models.layers import SequenceLayer
+    from sigma0_b200.models.mamba3 import Mamba3
+    torch.manual_seed(3)
+    H = 256
+    layer = SequenceLayer(Mamba3(H, impl="cuda"), H, "half_glu1", True, 0.0).cuda()
+    with torch.no_grad():
+        layer.seq.B_bias.normal_(0, 0.5)
+        layer.seq.C_bias.normal_(0, 0.5)
+        layer.out2.kernel.mul_(2.0)
+    x = torch.randn(2, 130, H, device="cuda")
+    with torch.no_grad():
+        want = layer(x)
+        st, got = layer.prefill(x[:, :128])
+        assert rel(got, want[:, :128]) < 1e-2, rel(got, want[:, :128])
+        for t in (128, 129):
+            st, y = layer.step(st, x[:, t:t + 1])
+            assert rel(y, want[:, t:t + 1]) < 3e-2, (t, rel(y, want[:, t:t + 1]))
