@@ -335,6 +335,41 @@ void adam(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ---- tensor-parallel fused GEMM + all-reduce ------------------------------------------------
+int64_t tp_gemm_allreduce(at::Tensor A, at::Tensor Bt, std::vector<int64_t> recv, int64_t rows_own,
+                          std::vector<int64_t> out, std::vector<int64_t> flags, int64_t rank, int64_t seq,
+                          int64_t spin_limit, at::Tensor status, at::Tensor abort,
+                          c10::optional<at::Tensor> stamps) {
+  req(A, at::kBFloat16, "A");
+  req(Bt, at::kBFloat16, "Bt");
+  TORCH_CHECK(A.dim() == 2 && Bt.dim() == 2 && A.size(1) == Bt.size(1), "A [M, K] and Bt [N, K]");
+  const int world = (int)recv.size();
+  TORCH_CHECK(world >= 1 && world <= TPF_MAXW && (int)out.size() == world && (int)flags.size() == world,
+              "one receive, output and flag pointer per rank (at most ", TPF_MAXW, ")");
+  c10::cuda::CUDAGuard guard(A.device());
+  TpfArgs a;
+  a.A = reinterpret_cast<const __nv_bfloat16*>(A.data_ptr());
+  a.Bt = reinterpret_cast<const __nv_bfloat16*>(Bt.data_ptr());
+  a.M = (int)A.size(0); a.N = (int)Bt.size(0); a.K = (int)A.size(1);
+  for (int k = 0; k < TPF_MAXW; ++k) {
+    a.recv[k] = k < world ? reinterpret_cast<__nv_bfloat16*>(recv[k]) : nullptr;
+    a.out[k] = k < world ? reinterpret_cast<__nv_bfloat16*>(out[k]) : nullptr;
+    a.flags[k] = k < world ? reinterpret_cast<int*>(flags[k]) : nullptr;
+  }
+  a.world = world; a.rank = (int)rank; a.seq = (int)seq; a.spin_limit = spin_limit;
+  a.rows_own = rows_own;
+  TORCH_CHECK(rows_own * world >= (A.size(0) + 127) / 128 * 128 && rows_own % 128 == 0, "receive slots too small");
+  a.status = status.data_ptr<int>();
+  a.abort = abort.data_ptr<int>();
+  a.stamps = nullptr;
+  if (stamps && stamps->defined()) {
+    TORCH_CHECK(stamps->scalar_type() == at::kLong && stamps->is_cuda() && stamps->numel() >= 4 + num_sms(A),
+                "stamps: int64 CUDA tensor of at least 4 + SM-count entries");
+    a.stamps = reinterpret_cast<unsigned long long*>(stamps->data_ptr<int64_t>());
+  }
+  return tp_gemm_allreduce_launch(a, num_sms(A), stream());
+}
+
 // ---- profiling ---------------------------------------------------------------------------
 at::Tensor m3_phase_probe() {
   unsigned long long v[16];
@@ -553,6 +588,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("sumsq", &sumsq);
   m.def("adam", &adam);
+  m.def("tp_gemm_allreduce", &tp_gemm_allreduce, py::arg("A"), py::arg("Bt"), py::arg("recv"), py::arg("rows_own"),
+        py::arg("out"), py::arg("flags"), py::arg("rank"), py::arg("seq"), py::arg("spin_limit"), py::arg("status"),
+        py::arg("abort"), py::arg("stamps") = py::none(),
+        "out = sum over ranks of A_r Bt_r^T: tcgen05 tiles reduced into the owners' peer buffers, then all-gathered "
+        "(cooperative launch; returns 0 or a launch error)");
   m.def("m3_phase_probe", &m3_phase_probe,
         "chunk-backward per-phase clock sums since the last call (empty unless built with S0_PHASE_PROBE)");
   m.def("m3_decode_step", &m3_decode_step, py::arg("proj"), py::arg("nh"), py::arg("wB"), py::arg("wC"),

@@ -138,3 +138,25 @@ void rms_bwd_pipe_launch(const void* dy, const void* x, const float* w, const fl
 void ln_bwd_pipe_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,
                         const float* dres, float* dx, float* dw, float* db, float* part, long T, int D, int sms,
                         cudaStream_t st);
+
+// tensor-parallel row-parallel GEMM fused with its all-reduce over peer memory (tp_fused.cu)
+#define TPF_MAXW 8
+struct TpfArgs {
+  const __nv_bfloat16* A;      // this rank's [M, K] activations (row-major)
+  const __nv_bfloat16* Bt;     // this rank's projection rows, transposed: [N, K]
+  int M, N, K;                 // M % 128 == 0, N % 128 == 0, K % 64 == 0
+  __nv_bfloat16* recv[TPF_MAXW];// every rank's receive buffer [world][rows_own, N] bf16 (peer-mapped):
+                               // slot r holds rank r's partial of the owner's row tiles
+  long rows_own;               // rows per slot: ceil(M / 128 / world) * 128
+  __nv_bfloat16* out[TPF_MAXW];// every rank's bf16 output [M, N] (peer-mapped)
+  int* flags[TPF_MAXW];        // every rank's flag words [2][TPF_MAXW]
+  int world, rank, seq;
+  long long spin_limit;
+  int* status;                 // 0 ok; 1 a GEMM-pipeline wait timed out; 2 a phase-3 copy wait timed out;
+                               // 100 + phase a peer did not arrive
+  int* abort;                  // zeroed before the launch
+  unsigned long long* stamps;  // optional [4 + gridDim] %globaltimer stamps (ns): block 0 at launch, after
+                               // the phase-1 grid barrier, after phase 3, at exit; then each CTA's end of
+                               // phase-1 work (nullptr: none recorded)
+};
+int tp_gemm_allreduce_launch(const TpfArgs& a, int sms, cudaStream_t st);

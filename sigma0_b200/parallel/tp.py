@@ -121,6 +121,7 @@ class Mamba3TP(nn.Module):
         self.out_proj_kernel = nn.Parameter(full.out_proj.kernel.detach()[hp].clone())
         self.A_floor = full.A_floor
         self.eps = 1e-6
+        self.fused_out = None
 
     def _rms(self, x, scale):
         return x * torch.rsqrt((x * x).mean(-1, keepdim=True) + self.eps) * scale
@@ -151,7 +152,18 @@ class Mamba3TP(nn.Module):
         y = y.reshape(*lead, nhl * P)
         ss = all_reduce_both((y * y).sum(-1, keepdim=True), self.group)      # full-width RMS statistic
         yn = y * torch.rsqrt(ss / d.d_inner + self.eps) * self.out_norm_scale
+        if self.fused_out is not None and yn.is_cuda:
+            from .tp_fused import fused_row_parallel
+            out = fused_row_parallel(yn.reshape(-1, yn.shape[-1]), self.out_proj_kernel, self.fused_out)
+            return out.reshape(*lead, -1).to(u.dtype)
         return reduce_from_tp(yn @ self.out_proj_kernel, self.group).to(u.dtype)
+
+    def use_fused_out_proj(self, max_rows: int) -> None:
+        """Route out_proj + its all-reduce through the fused peer-memory kernel
+        (``parallel/tp_fused.py``) for inputs of up to ``max_rows`` tokens."""
+        from .tp_fused import FusedRowParallel
+        self.fused_out = FusedRowParallel(max_rows, self.out_proj_kernel.shape[1], self.group,
+                                          self.out_proj_kernel.device)
 
     def full_in_proj_grad(self):
         """This rank's in_proj gradient scattered into the full (H, d_in_proj) layout."""

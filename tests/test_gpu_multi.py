@@ -1,6 +1,7 @@
-"""Multi-GPU data parallelism (needs >= 2 GPUs): the fused peer-memory
-reduce-scatter + AdamW + all-gather kernel against the NCCL sharded path, and
-its bounded cross-rank wait when a peer never arrives."""
+"""Multi-GPU fused paths (need >= 2 GPUs): the fused peer-memory reduce-scatter +
+AdamW + all-gather kernel against the NCCL sharded path and its bounded cross-rank
+wait when a peer never arrives; the fused tensor-parallel GEMM + all-reduce against
+GEMM + NCCL all-reduce."""
 import os
 import socket
 
@@ -106,3 +107,37 @@ def test_fused_dp_bounded_wait_reports_missing_peer(tmp_path):
     mp.spawn(_worker, args=(2, _port(), out, "timeout"), nprocs=2, join=True)
     res = torch.load(out)
     assert res["raised"] and "phase 0" in res["msg"]
+
+
+def _tp_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from sigma0_b200.parallel.tp_fused import FusedRowParallel
+        h = FusedRowParallel(max_rows=2048, n_out=512)
+        errs = []
+        for it in range(3):
+            g = torch.Generator(device="cuda").manual_seed(1000 * it + rank)
+            y = torch.randn(1500, 256, device="cuda", generator=g).to(torch.bfloat16)
+            w = (torch.randn(256, 512, device="cuda", generator=g) / 16).to(torch.bfloat16)
+            got = h(y, w.t().contiguous())
+            ref = y.float() @ w.float()
+            dist.all_reduce(ref)
+            torch.cuda.synchronize()
+            h.check()
+            errs.append(((got.float() - ref).norm() / ref.norm()).item())
+        if rank == 0:
+            torch.save({"errs": errs}, out)
+    finally:
+        dist.destroy_process_group()
+
+
+@need2
+def test_fused_tp_gemm_allreduce_matches_nccl(tmp_path):
+    out = str(tmp_path / "tp.pt")
+    mp.spawn(_tp_worker, args=(2, _port(), out), nprocs=2, join=True)
+    errs = torch.load(out)["errs"]
+    assert max(errs) < 1e-2, errs
