@@ -370,6 +370,78 @@ int64_t tp_gemm_allreduce(at::Tensor A, at::Tensor Bt, std::vector<int64_t> recv
   return tp_gemm_allreduce_launch(a, num_sms(A), stream());
 }
 
+// ---- attention ----------------------------------------------------------------------------
+static void attn_check(const at::Tensor& t, const char* name, int64_t hd) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, " must be a bf16 CUDA tensor");
+  TORCH_CHECK(t.dim() == 4 && t.size(3) == hd && t.stride(3) == 1, name, ": [B, L, nh, ", hd, "] with a contiguous head dim");
+  TORCH_CHECK(t.stride(0) % 8 == 0 && t.stride(1) % 8 == 0 && t.stride(2) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              name, ": strides must be multiples of 8 elements and the base 16-byte aligned");
+}
+
+static AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                          const at::Tensor& lse, double scale, int64_t window, int64_t q_offset) {
+  const int64_t hd = q.size(3);
+  TORCH_CHECK(hd == 64 || hd == 128, "attention head dim must be 64 or 128, got ", hd);
+  attn_check(q, "q", hd);
+  attn_check(k, "k", hd);
+  attn_check(v, "v", hd);
+  attn_check(o, "o", hd);
+  TORCH_CHECK(k.sizes() == v.sizes() && q.size(0) == k.size(0) && q.size(2) == k.size(2) && o.sizes() == q.sizes(),
+              "q/o [B, Lq, nh, hd] and k/v [B, Lk, nh, hd]");
+  req(lse, at::kFloat, "lse");
+  TORCH_CHECK(lse.is_contiguous() && lse.numel() == q.size(0) * q.size(2) * q.size(1), "lse [B, nh, Lq]");
+  AttnArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.sq_b = q.stride(0); a.sq_l = q.stride(1); a.sq_h = q.stride(2);
+  a.sk_b = k.stride(0); a.sk_l = k.stride(1); a.sk_h = k.stride(2);
+  a.sv_b = v.stride(0); a.sv_l = v.stride(1); a.sv_h = v.stride(2);
+  a.so_b = o.stride(0); a.so_l = o.stride(1); a.so_h = o.stride(2);
+  a.B = (int)q.size(0); a.nh = (int)q.size(2); a.Lq = (int)q.size(1); a.Lk = (int)k.size(1);
+  a.q_offset = (int)q_offset; a.window = (int)window;
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  return a;
+}
+
+void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, double scale, int64_t window,
+              int64_t q_offset) {
+  c10::cuda::CUDAGuard guard(q.device());
+  const AttnArgs a = attn_args(q, k, v, o, lse, scale, window, q_offset);
+  const int rc = attn_fwd_launch(a, (int)q.size(3), stream());
+  TORCH_CHECK(rc == 0, "attn_fwd launch failed (", rc, ")");
+}
+
+void attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dout, at::Tensor D,
+              at::Tensor dq_acc, at::Tensor dk, at::Tensor dv, double scale, int64_t window, int64_t q_offset) {
+  c10::cuda::CUDAGuard guard(q.device());
+  AttnBwdArgs a;
+  a.f = attn_args(q, k, v, o, lse, scale, window, q_offset);
+  const int64_t hd = q.size(3);
+  attn_check(dout, "dout", hd);
+  attn_check(dk, "dk", hd);
+  attn_check(dv, "dv", hd);
+  TORCH_CHECK(dout.sizes() == q.sizes() && dk.sizes() == k.sizes() && dv.sizes() == v.sizes(), "gradient shapes");
+  req(D, at::kFloat, "D");
+  req(dq_acc, at::kFloat, "dq_acc");
+  TORCH_CHECK(D.is_contiguous() && D.numel() == lse.numel(), "D [B, nh, Lq]");
+  TORCH_CHECK(dq_acc.is_contiguous() && dq_acc.sizes() == q.sizes(), "dq_acc [B, Lq, nh, hd] fp32, contiguous");
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.sd_b = dout.stride(0); a.sd_l = dout.stride(1); a.sd_h = dout.stride(2);
+  a.D = D.data_ptr<float>();
+  a.dq_acc = dq_acc.data_ptr<float>();
+  a.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  a.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  a.sdk_b = dk.stride(0); a.sdk_l = dk.stride(1); a.sdk_h = dk.stride(2);
+  a.sdv_b = dv.stride(0); a.sdv_l = dv.stride(1); a.sdv_h = dv.stride(2);
+  a.scale = (float)scale;
+  const int rc = attn_bwd_launch(a, (int)hd, stream());
+  TORCH_CHECK(rc == 0, "attn_bwd launch failed (", rc, ")");
+}
+
 // ---- profiling ---------------------------------------------------------------------------
 at::Tensor m3_phase_probe() {
   unsigned long long v[16];
@@ -593,6 +665,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("abort"), py::arg("stamps") = py::none(),
         "out = sum over ranks of A_r Bt_r^T: tcgen05 tiles reduced into the owners' peer buffers, then all-gathered "
         "(cooperative launch; returns 0 or a launch error)");
+  m.def("attn_fwd", &attn_fwd,
+        "causal / sliding-window flash attention forward: o and the base-2 row log-sum-exp (window <= 0: none)");
+  m.def("attn_bwd", &attn_bwd,
+        "flash attention backward: dk, dv written, dq accumulated into the zeroed fp32 dq_acc (scaled)");
   m.def("m3_phase_probe", &m3_phase_probe,
         "chunk-backward per-phase clock sums since the last call (empty unless built with S0_PHASE_PROBE)");
   m.def("m3_decode_step", &m3_decode_step, py::arg("proj"), py::arg("nh"), py::arg("wB"), py::arg("wC"),

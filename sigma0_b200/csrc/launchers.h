@@ -160,3 +160,25 @@ struct TpfArgs {
                                // phase-1 work (nullptr: none recorded)
 };
 int tp_gemm_allreduce_launch(const TpfArgs& a, int sms, cudaStream_t st);
+
+// causal / sliding-window flash attention (attention.cu); strides in elements
+struct AttnArgs {
+  const __nv_bfloat16 *q, *k, *v;  // q [B, Lq, nh, HD], k/v [B, Lk, nh, HD] (strided)
+  __nv_bfloat16* o;                // [B, Lq, nh, HD] (strided)
+  float* lse;                      // [B, nh, Lq] base-2 log-sum-exp of the scaled scores
+  long sq_b, sq_l, sq_h, sk_b, sk_l, sk_h, sv_b, sv_l, sv_h, so_b, so_l, so_h;
+  int B, nh, Lq, Lk, q_offset, window;  // window <= 0: unbounded
+  float scale_log2;                // softmax scale * log2(e)
+};
+struct AttnBwdArgs {
+  AttnArgs f;                      // the forward's tensors (o, lse as written by it)
+  const __nv_bfloat16* dout;       // [B, Lq, nh, HD] (strided)
+  long sd_b, sd_l, sd_h;
+  float* D;                        // [B, nh, Lq] scratch: rowsum(dO * O)
+  float* dq_acc;                   // [B, Lq, nh, HD] fp32, zeroed by the caller
+  __nv_bfloat16 *dk, *dv;          // [B, Lk, nh, HD] (strided)
+  long sdk_b, sdk_l, sdk_h, sdv_b, sdv_l, sdv_h;
+  float scale;                     // softmax scale
+};
+int attn_fwd_launch(const AttnArgs& a, int hd, cudaStream_t st);
+int attn_bwd_launch(const AttnBwdArgs& a, int hd, cudaStream_t st);
