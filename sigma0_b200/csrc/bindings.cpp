@@ -442,6 +442,87 @@ void attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor
   TORCH_CHECK(rc == 0, "attn_bwd launch failed (", rc, ")");
 }
 
+// ---- gated delta rule chunk scan -----------------------------------------------------------
+static void gdn_req(const at::Tensor& t, at::ScalarType dt, const char* name, std::initializer_list<int64_t> shape) {
+  req(t, dt, name);
+  TORCH_CHECK(t.is_contiguous() && t.sizes() == at::IntArrayRef(shape), name, " must be contiguous with shape ",
+              at::IntArrayRef(shape), ", got ", t.sizes());
+}
+
+static GdnArgs gdn_args(const at::Tensor& qe, const at::Tensor& kc, const at::Tensor& kd, const at::Tensor& intra,
+                        const at::Tensor& tot, int64_t HVD) {
+  TORCH_CHECK(qe.dim() == 5 && qe.size(3) == 64, "qe [B, nh, nc, 64, HD]");
+  const int64_t B = qe.size(0), nh = qe.size(1), nc = qe.size(2), HD = qe.size(4);
+  TORCH_CHECK(HD == 64 || HD == 128, "key head dim must be 64 or 128");
+  TORCH_CHECK(HVD % 64 == 0, "value head dim must be a multiple of 64");
+  gdn_req(qe, at::kBFloat16, "qe", {B, nh, nc, 64, HD});
+  gdn_req(kc, at::kBFloat16, "kc", {B, nh, nc, 64, HD});
+  gdn_req(kd, at::kBFloat16, "kd", {B, nh, nc, 64, HD});
+  gdn_req(intra, at::kBFloat16, "intra", {B, nh, nc, 64, 64});
+  gdn_req(tot, at::kFloat, "tot", {B, nh, nc, HD});
+  GdnArgs a{};
+  a.qe = reinterpret_cast<const __nv_bfloat16*>(qe.data_ptr());
+  a.kc = reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr());
+  a.kd = reinterpret_cast<const __nv_bfloat16*>(kd.data_ptr());
+  a.intra = reinterpret_cast<const __nv_bfloat16*>(intra.data_ptr());
+  a.tot = tot.data_ptr<float>();
+  a.B = (int)B; a.nh = (int)nh; a.nc = (int)nc; a.HVD = (int)HVD;
+  return a;
+}
+
+void gdn_scan_fwd(at::Tensor qe, at::Tensor kc, at::Tensor kd, at::Tensor intra, at::Tensor vc, at::Tensor tot,
+                  c10::optional<at::Tensor> S0, at::Tensor o, at::Tensor S_all, at::Tensor vnew, at::Tensor S_fin) {
+  c10::cuda::CUDAGuard guard(qe.device());
+  const int64_t HVD = vc.size(-1);
+  GdnArgs a = gdn_args(qe, kc, kd, intra, tot, HVD);
+  const int64_t B = a.B, nh = a.nh, nc = a.nc, HD = qe.size(4);
+  gdn_req(vc, at::kFloat, "vc", {B, nh, nc, 64, HVD});
+  gdn_req(o, at::kFloat, "o", {B, nh, nc, 64, HVD});
+  gdn_req(vnew, at::kFloat, "vnew", {B, nh, nc, 64, HVD});
+  gdn_req(S_all, at::kFloat, "S_all", {B, nh, nc, HVD, HD});
+  gdn_req(S_fin, at::kFloat, "S_fin", {B, nh, HVD, HD});
+  a.vc = vc.data_ptr<float>();
+  a.S0 = nullptr;
+  if (S0 && S0->defined()) {
+    gdn_req(*S0, at::kFloat, "S0", {B, nh, HVD, HD});
+    a.S0 = S0->data_ptr<float>();
+  }
+  a.o = o.data_ptr<float>(); a.S_all = S_all.data_ptr<float>(); a.vnew = vnew.data_ptr<float>();
+  a.S_fin = S_fin.data_ptr<float>();
+  const int rc = gdn_scan_launch(a, (int)HD, false, stream());
+  TORCH_CHECK(rc == 0, "gdn_scan_fwd launch failed (", rc, ")");
+}
+
+void gdn_scan_bwd(at::Tensor qe, at::Tensor kc, at::Tensor kd, at::Tensor intra, at::Tensor tot, at::Tensor S_all,
+                  at::Tensor vnew, at::Tensor dout, c10::optional<at::Tensor> dS_fin, at::Tensor dqe_p, at::Tensor dkc_p,
+                  at::Tensor dkd_p, at::Tensor din_p, at::Tensor dtot_p, at::Tensor dvc, at::Tensor dS0) {
+  c10::cuda::CUDAGuard guard(qe.device());
+  const int64_t HVD = vnew.size(-1);
+  GdnArgs a = gdn_args(qe, kc, kd, intra, tot, HVD);
+  const int64_t B = a.B, nh = a.nh, nc = a.nc, HD = qe.size(4), nvb = HVD / 64;
+  gdn_req(S_all, at::kFloat, "S_all", {B, nh, nc, HVD, HD});
+  gdn_req(vnew, at::kFloat, "vnew", {B, nh, nc, 64, HVD});
+  gdn_req(dout, at::kFloat, "dout", {B, nh, nc, 64, HVD});
+  gdn_req(dqe_p, at::kFloat, "dqe_p", {nvb, B, nh, nc, 64, HD});
+  gdn_req(dkc_p, at::kFloat, "dkc_p", {nvb, B, nh, nc, 64, HD});
+  gdn_req(dkd_p, at::kFloat, "dkd_p", {nvb, B, nh, nc, 64, HD});
+  gdn_req(din_p, at::kFloat, "din_p", {nvb, B, nh, nc, 64, 64});
+  gdn_req(dtot_p, at::kFloat, "dtot_p", {nvb, B, nh, nc, HD});
+  gdn_req(dvc, at::kFloat, "dvc", {B, nh, nc, 64, HVD});
+  gdn_req(dS0, at::kFloat, "dS0", {B, nh, HVD, HD});
+  a.S_all = S_all.data_ptr<float>(); a.vnew = vnew.data_ptr<float>(); a.dout = dout.data_ptr<float>();
+  a.dS_fin = nullptr;
+  if (dS_fin && dS_fin->defined()) {
+    gdn_req(*dS_fin, at::kFloat, "dS_fin", {B, nh, HVD, HD});
+    a.dS_fin = dS_fin->data_ptr<float>();
+  }
+  a.dqe_p = dqe_p.data_ptr<float>(); a.dkc_p = dkc_p.data_ptr<float>(); a.dkd_p = dkd_p.data_ptr<float>();
+  a.din_p = din_p.data_ptr<float>(); a.dtot_p = dtot_p.data_ptr<float>(); a.dvc = dvc.data_ptr<float>();
+  a.dS0 = dS0.data_ptr<float>();
+  const int rc = gdn_scan_launch(a, (int)HD, true, stream());
+  TORCH_CHECK(rc == 0, "gdn_scan_bwd launch failed (", rc, ")");
+}
+
 // ---- profiling ---------------------------------------------------------------------------
 at::Tensor m3_phase_probe() {
   unsigned long long v[16];
@@ -669,6 +750,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "causal / sliding-window flash attention forward: o and the base-2 row log-sum-exp (window <= 0: none)");
   m.def("attn_bwd", &attn_bwd,
         "flash attention backward: dk, dv written, dq accumulated into the zeroed fp32 dq_acc (scaled)");
+  m.def("gdn_scan_fwd", &gdn_scan_fwd,
+        "gated delta rule cross-chunk scan: o, the chunk-start states, vnew and the final state");
+  m.def("gdn_scan_bwd", &gdn_scan_bwd,
+        "reverse scan: per value-block partial gradients of qe / kc / kd / intra / tot, dvc and dS0");
   m.def("m3_phase_probe", &m3_phase_probe,
         "chunk-backward per-phase clock sums since the last call (empty unless built with S0_PHASE_PROBE)");
   m.def("m3_decode_step", &m3_decode_step, py::arg("proj"), py::arg("nh"), py::arg("wB"), py::arg("wC"),

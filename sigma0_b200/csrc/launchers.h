@@ -182,3 +182,26 @@ struct AttnBwdArgs {
 };
 int attn_fwd_launch(const AttnArgs& a, int hd, cudaStream_t st);
 int attn_bwd_launch(const AttnBwdArgs& a, int hd, cudaStream_t st);
+
+// cross-chunk state scan of the chunked gated delta rule (gdn_scan.cu); chunk length 64,
+// value rows split in blocks of 64; every tensor contiguous
+struct GdnArgs {
+  const __nv_bfloat16 *qe, *kc, *kd;  // [B, nh, nc, 64, HD]
+  const __nv_bfloat16* intra;         // [B, nh, nc, 64, 64] (lower triangle incl. diagonal)
+  const float* vc;                    // [B, nh, nc, 64, HVD]
+  const float* tot;                   // [B, nh, nc, HD] per-key-column decay over the chunk
+  const float* S0;                    // [B, nh, HVD, HD] initial state (nullptr: zeros)
+  float* o;                           // [B, nh, nc, 64, HVD]
+  float* S_all;                       // [B, nh, nc, HVD, HD] state at each chunk start
+  float* vnew;                        // [B, nh, nc, 64, HVD]
+  float* S_fin;                       // [B, nh, HVD, HD]
+  const float* dout;                  // backward: dL/do [B, nh, nc, 64, HVD]
+  const float* dS_fin;                // backward: dL/dS_fin (nullptr: zeros)
+  float *dqe_p, *dkc_p, *dkd_p;       // [HVD / 64, B, nh, nc, 64, HD] per value-block partials
+  float* din_p;                       // [HVD / 64, B, nh, nc, 64, 64]
+  float* dtot_p;                      // [HVD / 64, B, nh, nc, HD]
+  float* dvc;                         // [B, nh, nc, 64, HVD]
+  float* dS0;                         // [B, nh, HVD, HD]
+  int B, nh, nc, HVD;
+};
+int gdn_scan_launch(const GdnArgs& a, int hd, bool bwd, cudaStream_t st);

@@ -51,10 +51,64 @@ class CausalDepthwiseConv1d(nn.Module):
         return xc[:, -(self.k - 1):], self._conv(xc)
 
 
-def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None):
+class _GDNScan(torch.autograd.Function):
+    """The cross-chunk state scan on the sm_100a kernels of ``csrc/gdn_scan.cu``.
+
+    Inputs in (B, nh, nc, C, ...) layout: qe = q exp(G), kc = (I - L)^-1 (beta k exp(G)),
+    kd = k exp(G_end - G), intra (lower-triangular scores), vc = (I - L)^-1 (beta v),
+    tot = exp(G_end) per key column, S0 (or None).  Returns o (B, nh, nc, C, hvd) and the
+    final state.  The kernel multiplies in bf16 with fp32 accumulation and keeps the
+    state in fp32."""
+
+    @staticmethod
+    def forward(ctx, qe, kc, kd, intra, vc, tot, S0):
+        from ..ops._ext import ext
+        bf = lambda t: t.detach().to(torch.bfloat16).contiguous()
+        qe_b, kc_b, kd_b, in_b = bf(qe), bf(kc), bf(kd), bf(intra)
+        vc_c, tot_c = vc.detach().float().contiguous(), tot.detach().float().contiguous()
+        B, nh, nc, C, hd = qe.shape
+        hvd = vc.shape[-1]
+        o = torch.empty(B, nh, nc, C, hvd, device=qe.device)
+        vnew = torch.empty_like(o)
+        S_all = torch.empty(B, nh, nc, hvd, hd, device=qe.device)
+        S_fin = torch.empty(B, nh, hvd, hd, device=qe.device)
+        s0 = S0.detach().float().contiguous() if S0 is not None else None
+        ext().gdn_scan_fwd(qe_b, kc_b, kd_b, in_b, vc_c, tot_c, s0, o, S_all, vnew, S_fin)
+        ctx.save_for_backward(qe_b, kc_b, kd_b, in_b, tot_c, S_all, vnew)
+        ctx.has_s0 = S0 is not None
+        return o, S_fin
+
+    @staticmethod
+    def backward(ctx, do, dS_fin):
+        from ..ops._ext import ext
+        qe_b, kc_b, kd_b, in_b, tot_c, S_all, vnew = ctx.saved_tensors
+        B, nh, nc, C, hd = qe_b.shape
+        hvd = vnew.shape[-1]
+        nvb = hvd // 64
+        do = torch.zeros_like(vnew) if do is None else do.float().contiguous()
+        dS_fin = None if dS_fin is None else dS_fin.float().contiguous()
+        dev = vnew.device
+        dqe = torch.empty(nvb, B, nh, nc, C, hd, device=dev)
+        dkc, dkd = torch.empty_like(dqe), torch.empty_like(dqe)
+        din = torch.empty(nvb, B, nh, nc, C, C, device=dev)
+        dtot = torch.empty(nvb, B, nh, nc, hd, device=dev)
+        dvc = torch.empty_like(vnew)
+        dS0 = torch.empty(B, nh, hvd, hd, device=dev)
+        ext().gdn_scan_bwd(qe_b, kc_b, kd_b, in_b, tot_c, S_all, vnew, do, dS_fin, dqe, dkc, dkd, din, dtot, dvc, dS0)
+        return (dqe.sum(0), dkc.sum(0), dkd.sum(0), din.sum(0), dvc, dtot.sum(0),
+                dS0 if ctx.has_s0 else None)
+
+
+def _scan_kernel_ok(q, v, chunk) -> bool:
+    return q.is_cuda and chunk == 64 and q.shape[-1] in (64, 128) and v.shape[-1] % 64 == 0
+
+
+def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None, use_kernel=None):
     """q,k (B,L,nh,hd); v (B,L,nh,hvd); beta (B,L,nh); alog (B,L,nh,hd or 1).
 
-    Returns o (B,L,nh,hvd) and the final state (B,nh,hvd,hd).
+    Returns o (B,L,nh,hvd) and the final state (B,nh,hvd,hd).  On CUDA (chunk 64, key
+    head dim 64 / 128, value head dim a multiple of 64) the cross-chunk scan runs the
+    ``gdn_scan`` kernels; ``use_kernel=False`` keeps the host loop (the oracle).
     """
     B, L, nh, hd = q.shape
     hvd = v.shape[-1]
@@ -89,6 +143,15 @@ def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None):
     kcd = torch.linalg.solve_triangular(A, kb * torch.exp(G), upper=False)    # (B,nc,nh,C,hd)
     dec_end = torch.exp(G[..., -1:, :] - G)                                     # (B,nc,nh,C,d|1)
     kdec = k * dec_end
+    if use_kernel is None:
+        use_kernel = _scan_kernel_ok(q, v, chunk)
+    if use_kernel:
+        P = lambda t: t.transpose(1, 2)                                         # -> (B,nh,nc,...)
+        tot = P(torch.exp(G[..., -1, :])).expand(B, nh, nc, hd)
+        o, S = _GDNScan.apply(P(q * torch.exp(G)), P(kcd), P(kdec), P(intra), P(vc), tot,
+                              None if S0 is None else S0.float())
+        o = P(o).transpose(2, 3).reshape(B, nc * C, nh, hvd)[:, :L]
+        return o, S
     S = torch.zeros(B, nh, hvd, hd, device=q.device) if S0 is None else S0.float()
     outs = []
     for c in range(nc):
