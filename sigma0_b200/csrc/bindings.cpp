@@ -523,6 +523,44 @@ void gdn_scan_bwd(at::Tensor qe, at::Tensor kc, at::Tensor kd, at::Tensor intra,
   TORCH_CHECK(rc == 0, "gdn_scan_bwd launch failed (", rc, ")");
 }
 
+// ---- per-key-dim-decay intra-chunk matrices -------------------------------------------------
+static KdaArgs kda_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& kb, const at::Tensor& G) {
+  TORCH_CHECK(q.dim() == 3 && q.size(1) == 64 && q.size(2) % 32 == 0, "q [N, 64, HD] with HD a multiple of 32");
+  const int64_t N = q.size(0), HD = q.size(2);
+  gdn_req(q, at::kFloat, "q", {N, 64, HD});
+  gdn_req(k, at::kFloat, "k", {N, 64, HD});
+  gdn_req(kb, at::kFloat, "kb", {N, 64, HD});
+  gdn_req(G, at::kFloat, "G", {N, 64, HD});
+  KdaArgs a{};
+  a.q = q.data_ptr<float>(); a.k = k.data_ptr<float>(); a.kb = kb.data_ptr<float>(); a.G = G.data_ptr<float>();
+  a.N = N; a.HD = (int)HD;
+  return a;
+}
+
+void kda_intra_fwd(at::Tensor q, at::Tensor k, at::Tensor kb, at::Tensor G, at::Tensor intra, at::Tensor Lm) {
+  c10::cuda::CUDAGuard guard(q.device());
+  KdaArgs a = kda_args(q, k, kb, G);
+  gdn_req(intra, at::kFloat, "intra", {a.N, 64, 64});
+  gdn_req(Lm, at::kFloat, "Lm", {a.N, 64, 64});
+  a.intra = intra.data_ptr<float>(); a.Lm = Lm.data_ptr<float>();
+  const int rc = kda_intra_launch(a, false, stream());
+  TORCH_CHECK(rc == 0, "kda_intra_fwd launch failed (", rc, ")");
+}
+
+void kda_intra_bwd(at::Tensor q, at::Tensor k, at::Tensor kb, at::Tensor G, at::Tensor gI, at::Tensor gL,
+                   at::Tensor dq, at::Tensor dk, at::Tensor dkb, at::Tensor dG) {
+  c10::cuda::CUDAGuard guard(q.device());
+  KdaArgs a = kda_args(q, k, kb, G);
+  const int64_t N = a.N, HD = a.HD;
+  gdn_req(gI, at::kFloat, "gI", {N, 64, 64});
+  gdn_req(gL, at::kFloat, "gL", {N, 64, 64});
+  for (auto* t : {&dq, &dk, &dkb, &dG}) gdn_req(*t, at::kFloat, "gradient", {N, 64, HD});
+  a.gI = gI.data_ptr<float>(); a.gL = gL.data_ptr<float>();
+  a.dq = dq.data_ptr<float>(); a.dk = dk.data_ptr<float>(); a.dkb = dkb.data_ptr<float>(); a.dG = dG.data_ptr<float>();
+  const int rc = kda_intra_launch(a, true, stream());
+  TORCH_CHECK(rc == 0, "kda_intra_bwd launch failed (", rc, ")");
+}
+
 // ---- profiling ---------------------------------------------------------------------------
 at::Tensor m3_phase_probe() {
   unsigned long long v[16];
@@ -754,6 +792,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "gated delta rule cross-chunk scan: o, the chunk-start states, vnew and the final state");
   m.def("gdn_scan_bwd", &gdn_scan_bwd,
         "reverse scan: per value-block partial gradients of qe / kc / kd / intra / tot, dvc and dS0");
+  m.def("kda_intra_fwd", &kda_intra_fwd, "per-key-dim-decay intra-chunk score and WY matrices of 64-step chunks");
+  m.def("kda_intra_bwd", &kda_intra_bwd, "gradients of q, k, kb and the cumulative log decay G");
   m.def("m3_phase_probe", &m3_phase_probe,
         "chunk-backward per-phase clock sums since the last call (empty unless built with S0_PHASE_PROBE)");
   m.def("m3_decode_step", &m3_decode_step, py::arg("proj"), py::arg("nh"), py::arg("wB"), py::arg("wC"),

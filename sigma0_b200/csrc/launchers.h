@@ -205,3 +205,15 @@ struct GdnArgs {
   int B, nh, nc, HVD;
 };
 int gdn_scan_launch(const GdnArgs& a, int hd, bool bwd, cudaStream_t st);
+
+// intra-chunk score / WY matrices of the per-key-dim-decay delta rule (kda_intra.cu);
+// N chunks of 64 steps, every tensor contiguous fp32
+struct KdaArgs {
+  const float *q, *k, *kb, *G;        // [N, 64, HD]; G = within-chunk cumulative log decay
+  float *intra, *Lm;                  // forward outputs [N, 64, 64]
+  const float *gI, *gL;               // backward inputs [N, 64, 64]
+  float *dq, *dk, *dkb, *dG;          // backward outputs [N, 64, HD]
+  long N;
+  int HD;                             // a multiple of 32
+};
+int kda_intra_launch(const KdaArgs& a, bool bwd, cudaStream_t st);

@@ -99,6 +99,35 @@ class _GDNScan(torch.autograd.Function):
                 dS0 if ctx.has_s0 else None)
 
 
+class _KDAIntra(torch.autograd.Function):
+    """intra = sum_d q k exp(G_i - G_j) (i >= j) and Lm = -sum_d kb k exp(G_i - G_j) (i > j)
+    per 64-step chunk on the kernels of ``csrc/kda_intra.cu`` (no [C, C, hd] tensor)."""
+
+    @staticmethod
+    def forward(ctx, q, k, kb, G):
+        from ..ops._ext import ext
+        shp = q.shape
+        f = lambda t: t.detach().float().reshape(-1, shp[-2], shp[-1]).contiguous()
+        qf, kf, kbf, Gf = f(q), f(k), f(kb), f(G)
+        N = qf.shape[0]
+        intra = torch.empty(N, 64, 64, device=q.device)
+        Lm = torch.empty_like(intra)
+        ext().kda_intra_fwd(qf, kf, kbf, Gf, intra, Lm)
+        ctx.save_for_backward(qf, kf, kbf, Gf)
+        ctx.shp = shp
+        return intra.reshape(*shp[:-1], 64), Lm.reshape(*shp[:-1], 64)
+
+    @staticmethod
+    def backward(ctx, gI, gL):
+        from ..ops._ext import ext
+        qf, kf, kbf, Gf = ctx.saved_tensors
+        N = qf.shape[0]
+        g = lambda t: torch.zeros(N, 64, 64, device=qf.device) if t is None else t.float().reshape(N, 64, 64).contiguous()
+        dq, dk, dkb, dG = (torch.empty_like(qf) for _ in range(4))
+        ext().kda_intra_bwd(qf, kf, kbf, Gf, g(gI), g(gL), dq, dk, dkb, dG)
+        return tuple(t.reshape(ctx.shp) for t in (dq, dk, dkb, dG))
+
+
 def _scan_kernel_ok(q, v, chunk) -> bool:
     return q.is_cuda and chunk == 64 and q.shape[-1] in (64, 128) and v.shape[-1] % 64 == 0
 
@@ -127,7 +156,11 @@ def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None, use_kernel=None)
     stri = torch.tril(torch.ones(C, C, dtype=torch.bool, device=q.device), -1)
     kb = k * beta[..., None]
     vb = v * beta[..., None]
-    if G.shape[-1] == 1:
+    if use_kernel is None:
+        use_kernel = _scan_kernel_ok(q, v, chunk)
+    if G.shape[-1] != 1 and use_kernel:
+        intra, Lm = _KDAIntra.apply(q, k, kb, G)
+    elif G.shape[-1] == 1:
         dG = (G[..., :, None, 0] - G[..., None, :, 0]).masked_fill(~tri, 0.0)
         W = torch.exp(dG) * tri
         intra = (q @ k.transpose(-1, -2)) * W
@@ -143,8 +176,6 @@ def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None, use_kernel=None)
     kcd = torch.linalg.solve_triangular(A, kb * torch.exp(G), upper=False)    # (B,nc,nh,C,hd)
     dec_end = torch.exp(G[..., -1:, :] - G)                                     # (B,nc,nh,C,d|1)
     kdec = k * dec_end
-    if use_kernel is None:
-        use_kernel = _scan_kernel_ok(q, v, chunk)
     if use_kernel:
         P = lambda t: t.transpose(1, 2)                                         # -> (B,nh,nc,...)
         tot = P(torch.exp(G[..., -1, :])).expand(B, nh, nc, hd)

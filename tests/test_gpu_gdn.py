@@ -49,3 +49,26 @@ def test_gdn_layer_uses_the_scan_kernel():
     _ext.reset_launch_count()
     m(torch.randn(1, 130, 256, device="cuda")).sum().backward()
     assert _ext.launch_count() >= 2
+
+
+def test_kda_intra_kernel_matches_einsum():
+    """Per-key-dim decay score / WY matrices and their gradients against the tensor
+    expression (strong decays included: the weights stay in [0, 1])."""
+    from sigma0_b200.models.gdn import _KDAIntra
+    g = torch.Generator(device="cuda").manual_seed(3)
+    N, C, hd = 6, 64, 128
+    q, k, kb = (torch.randn(N, C, hd, device="cuda", generator=g).requires_grad_(True) for _ in range(3))
+    alog = torch.nn.functional.logsigmoid(torch.randn(N, C, hd, device="cuda", generator=g) * 3)
+    G = alog.cumsum(1).requires_grad_(True)
+    I1, L1 = _KDAIntra.apply(q, k, kb, G)
+    xs = [t.detach().clone().requires_grad_(True) for t in (q, k, kb, G)]
+    tri = torch.tril(torch.ones(C, C, dtype=torch.bool, device="cuda"))
+    W = torch.exp((xs[3][:, :, None, :] - xs[3][:, None, :, :]).masked_fill(~tri[..., None], 0.0)) * tri[..., None]
+    I2 = torch.einsum("nid,njd,nijd->nij", xs[0], xs[1], W)
+    L2 = -torch.einsum("nid,njd,nijd->nij", xs[2], xs[1], W) * torch.tril(tri, -1)
+    assert _rel(I1, I2) < 1e-4 and _rel(L1, L2) < 1e-4
+    wI, wL = torch.randn_like(I2), torch.randn_like(L2)
+    ((I1 * wI).sum() + (L1 * wL).sum()).backward()
+    ((I2 * wI).sum() + (L2 * wL).sum()).backward()
+    for name, a, b in zip(("q", "k", "kb", "G"), (q, k, kb, G), xs):
+        assert _rel(a.grad, b.grad) < 1e-4, (name, _rel(a.grad, b.grad))
