@@ -4,7 +4,9 @@
 // reference calls cuDNN's flash attention, src/base_model/models/nsa.py:27-59, and a
 // Pallas MHA, src/base_model/models/transformer.py:19-85).  Query i (absolute position
 // q_offset + i) attends to keys j <= q_offset + i, and with a window W only to
-// j > q_offset + i - W; keys beyond Lk do not exist.  Layouts are the models' own:
+// j > q_offset + i - W; keys beyond Lk do not exist.  Optional tables give every key its
+// own absolute position (compressed or gathered key blocks: NSA) and every batch entry
+// its own query offset (query groups flattened into the batch).  Layouts are the models' own:
 // q/o [B, Lq, nh, HD], k/v [B, Lk, nh, HD] with arbitrary batch / row / head strides
 // (elements; multiples of 8) and contiguous head dimension HD in {64, 128}.
 //
@@ -32,8 +34,12 @@ namespace attn {
 using bf16 = __nv_bfloat16;
 constexpr int NT = 256;
 
-__device__ __forceinline__ bool visible(int key, int qpos, int Lk, int window) {
-  return key <= qpos && key < Lk && (window <= 0 || key > qpos - window);
+// key index `key` sits at absolute position `kp` (= key unless a position table is given)
+__device__ __forceinline__ bool visible(int key, int kp, int qpos, int Lk, int window) {
+  return key < Lk && kp <= qpos && (window <= 0 || kp > qpos - window);
+}
+__device__ __forceinline__ int key_pos(const int* kp, int key, int Lk) {
+  return kp ? (key < Lk ? __ldg(kp + key) : 0x7fffffff) : key;
 }
 
 // rows x HD tile of a strided [.., rows, .., HD] tensor -> shared [rows][HD + 8], zero-filled
@@ -63,10 +69,16 @@ __global__ void __launch_bounds__(NT, HD == 64 ? 2 : 1) attn_fwd_k(AttnArgs a) {
   const bf16* qg = a.q + b * a.sq_b + (long)q0 * a.sq_l + h * a.sq_h;
   const bf16* kg = a.k + b * a.sk_b + h * a.sk_h;
   const bf16* vg = a.v + b * a.sv_b + h * a.sv_h;
-  const int qlo = a.q_offset + q0;                                   // smallest query position here
-  const int hi = min(a.Lk, qlo + BQ);                                // keys [lo, hi) can be visible
-  const int lo = a.window > 0 ? max(0, qlo - a.window + 1) : 0;
-  const int kb0 = lo / BKV, kb1 = (hi + BKV - 1) / BKV;
+  const int qoff = a.qoff ? a.qoff[b] : a.q_offset;
+  const int* kp = a.kpos ? a.kpos + (long)b * a.Lk : nullptr;     // per-key positions (else the index)
+  const int qlo = qoff + q0;                                         // smallest query position here
+  int kb0 = 0, kb1 = (a.Lk + BKV - 1) / BKV;
+  if (!kp) {
+    const int hi = min(a.Lk, qlo + BQ);                              // keys [lo, hi) can be visible
+    const int lo = a.window > 0 ? max(0, qlo - a.window + 1) : 0;
+    kb0 = lo / BKV;
+    kb1 = (hi + BKV - 1) / BKV;
+  }
 
   load_tile<HD>(sQ, qg, a.sq_l, BQ, a.Lq - q0, tid);
   if (kb0 < kb1) {
@@ -81,7 +93,7 @@ __global__ void __launch_bounds__(NT, HD == 64 ? 2 : 1) attn_fwd_k(AttnArgs a) {
   float m[2] = {-CUDART_INF_F, -CUDART_INF_F}, l[2] = {0.f, 0.f};
   uint32_t qf[KS][4];
   const int row0 = q0 + warp * 16 + g;                               // this thread's rows: row0, row0 + 8
-  const int qp0 = a.q_offset + row0, qp1 = qp0 + 8;
+  const int qp0 = qoff + row0, qp1 = qp0 + 8;
 
   for (int kb = kb0; kb < kb1; ++kb) {
     const int st = (kb - kb0) & 1;
@@ -113,7 +125,7 @@ __global__ void __launch_bounds__(NT, HD == 64 ? 2 : 1) attn_fwd_k(AttnArgs a) {
       }
     // scale into the base-2 domain; per-element mask only where the block needs it
     const int key0 = kb * BKV;
-    const bool full = key0 + BKV - 1 <= qlo && key0 + BKV <= a.Lk &&
+    const bool full = !kp && key0 + BKV - 1 <= qlo && key0 + BKV <= a.Lk &&
                       (a.window <= 0 || key0 > qlo + BQ - 1 - a.window);
 #pragma unroll
     for (int nt = 0; nt < BKV / 8; ++nt)
@@ -122,7 +134,7 @@ __global__ void __launch_bounds__(NT, HD == 64 ? 2 : 1) attn_fwd_k(AttnArgs a) {
         float x = s[nt][e] * a.scale_log2;
         if (!full) {
           const int key = key0 + nt * 8 + 2 * t + (e & 1);
-          if (!visible(key, e < 2 ? qp0 : qp1, a.Lk, a.window)) x = -CUDART_INF_F;
+          if (!visible(key, key_pos(kp, key, a.Lk), e < 2 ? qp0 : qp1, a.Lk, a.window)) x = -CUDART_INF_F;
         }
         s[nt][e] = x;
       }
@@ -207,6 +219,93 @@ __global__ void __launch_bounds__(NT, HD == 64 ? 2 : 1) attn_fwd_k(AttnArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------
+// head-summed probabilities (NSA block importance; no gradient)
+// ------------------------------------------------------------------------------------------
+// imp[b, i, j] = sum_h exp2(s_bhij * c - lse_bhi) over visible keys: grid (query blocks of
+// 128, key blocks of 64, batch); the heads stream through a two-stage ring of Q / K tiles
+// and the sum stays in registers.  Tiles whose keys all lie after the last query are zero.
+template <int HD>
+__global__ void __launch_bounds__(NT) attn_probsum_k(AttnArgs a, float* imp) {
+  constexpr int BQ = 128, BKV = 64, LDS = HD + 8, KS = HD / 16;
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* sQ = reinterpret_cast<bf16*>(smem);     // [2][BQ][LDS]
+  bf16* sK = sQ + 2 * BQ * LDS;                 // [2][BKV][LDS]
+  __shared__ int s_minpos;
+  const int q0 = blockIdx.x * BQ, key0 = blockIdx.y * BKV, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int qoff = a.qoff ? a.qoff[b] : a.q_offset;
+  const int* kp = a.kpos ? a.kpos + (long)b * a.Lk : nullptr;
+  const int row0 = q0 + warp * 16 + g, qp0 = qoff + row0, qp1 = qp0 + 8;
+  if (warp == 0) {
+    int m = min(key_pos(kp, key0 + lane, a.Lk), key_pos(kp, key0 + 32 + lane, a.Lk));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_minpos = m;
+  }
+  __syncthreads();
+  const bool any = s_minpos <= qoff + q0 + BQ - 1;
+  float acc[BKV / 8][4];
+#pragma unroll
+  for (int i = 0; i < BKV / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  if (any) {
+    auto load = [&](int h, int st) {
+      load_tile<HD>(sQ + st * BQ * LDS, a.q + b * a.sq_b + (long)q0 * a.sq_l + h * a.sq_h, a.sq_l, BQ, a.Lq - q0, tid);
+      load_tile<HD>(sK + st * BKV * LDS, a.k + b * a.sk_b + (long)key0 * a.sk_l + h * a.sk_h, a.sk_l, BKV,
+                    a.Lk - key0, tid);
+    };
+    load(0, 0);
+    cp_async_commit();
+    for (int h = 0; h < a.nh; ++h) {
+      const int st = h & 1;
+      if (h + 1 < a.nh) load(h + 1, st ^ 1);
+      cp_async_commit();
+      cp_async_wait_group<1>();
+      __syncthreads();
+      const bf16* cQ = sQ + st * BQ * LDS;
+      const bf16* cK = sK + st * BKV * LDS;
+      float s[BKV / 8][4];
+#pragma unroll
+      for (int i = 0; i < BKV / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        uint32_t qa[4];
+        load_a(qa, cQ, LDS, warp * 16, kk * 16, lane);
+#pragma unroll
+        for (int np = 0; np < BKV / 16; ++np) {
+          uint32_t bb[4];
+          load_b_nk(bb, cK, LDS, np * 16, kk * 16, lane);
+          mma_bf16(s[2 * np], qa, bb[0], bb[1]);
+          mma_bf16(s[2 * np + 1], qa, bb[2], bb[3]);
+        }
+      }
+      const float* lse = a.lse + ((long)b * a.nh + h) * a.Lq;
+      const float l0 = row0 < a.Lq ? lse[row0] : CUDART_INF_F, l1 = row0 + 8 < a.Lq ? lse[row0 + 8] : CUDART_INF_F;
+#pragma unroll
+      for (int nt = 0; nt < BKV / 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = key0 + nt * 8 + 2 * t + (e & 1);
+          const bool ok = visible(key, key_pos(kp, key, a.Lk), e < 2 ? qp0 : qp1, a.Lk, a.window);
+          acc[nt][e] += ok ? exp2f(s[nt][e] * a.scale_log2 - (e < 2 ? l0 : l1)) : 0.f;
+        }
+      __syncthreads();                                               // stage st free
+    }
+    cp_async_wait_group<0>();
+  }
+  float* out = imp + (long)b * a.Lq * a.Lk;
+#pragma unroll
+  for (int nt = 0; nt < BKV / 8; ++nt)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int row = row0 + 8 * hf, key = key0 + nt * 8 + 2 * t;
+      if (row < a.Lq) {
+        if (key < a.Lk) out[(long)row * a.Lk + key] = acc[nt][2 * hf];
+        if (key + 1 < a.Lk) out[(long)row * a.Lk + key + 1] = acc[nt][2 * hf + 1];
+      }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // backward
 // ------------------------------------------------------------------------------------------
 // D[b, h, i] = sum_d dO[b, i, h, d] * O[b, i, h, d] (one warp per row)
@@ -247,9 +346,15 @@ __global__ void __launch_bounds__(NT, 1) attn_bwd_k(AttnBwdArgs a) {
   const float* lg = f.lse + ((long)b * f.nh + h) * f.Lq;
   const float* Dg = a.D + ((long)b * f.nh + h) * f.Lq;
   // query rows that can see keys [k0, k0 + BC)
-  const int ilo = max(0, k0 - f.q_offset);
-  const int ihi = f.window > 0 ? min(f.Lq, k0 + BC - 1 + f.window - f.q_offset) : f.Lq;
-  const int qb0 = ilo / BR, qb1 = ihi > ilo ? (ihi + BR - 1) / BR : qb0;
+  const int qoff = f.qoff ? f.qoff[b] : f.q_offset;
+  const int* kp = f.kpos ? f.kpos + (long)b * f.Lk : nullptr;
+  int qb0 = 0, qb1 = (f.Lq + BR - 1) / BR;
+  if (!kp) {
+    const int ilo = max(0, k0 - qoff);
+    const int ihi = f.window > 0 ? min(f.Lq, k0 + BC - 1 + f.window - qoff) : f.Lq;
+    qb0 = ilo / BR;
+    qb1 = ihi > ilo ? (ihi + BR - 1) / BR : qb0;
+  }
 
   load_tile<HD>(sK, f.k + b * f.sk_b + (long)k0 * f.sk_l + h * f.sk_h, f.sk_l, BC, f.Lk - k0, tid);
   load_tile<HD>(sV, f.v + b * f.sv_b + (long)k0 * f.sv_l + h * f.sv_h, f.sv_l, BC, f.Lk - k0, tid);
@@ -272,6 +377,7 @@ __global__ void __launch_bounds__(NT, 1) attn_bwd_k(AttnBwdArgs a) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) dk[i][e] = dv[i][e] = 0.f;
   const int key_a = k0 + warp * 16 + g, key_b = key_a + 8;           // this thread's key rows
+  const int kpa = key_pos(kp, key_a, f.Lk), kpb = key_pos(kp, key_b, f.Lk);
   const int kmax = k0 + BC - 1;
 
   for (int qb = qb0; qb < qb1; ++qb) {
@@ -308,8 +414,8 @@ __global__ void __launch_bounds__(NT, 1) attn_bwd_k(AttnBwdArgs a) {
       }
     }
     // P^T and dS^T (rows: keys key_a / key_b; columns: queries)
-    const int qlo = f.q_offset + r0, qhi = qlo + BR - 1;
-    const bool full = kmax <= qlo && kmax < f.Lk && r0 + BR <= f.Lq && (f.window <= 0 || k0 > qhi - f.window);
+    const int qlo = qoff + r0, qhi = qlo + BR - 1;
+    const bool full = !kp && kmax <= qlo && kmax < f.Lk && r0 + BR <= f.Lq && (f.window <= 0 || k0 > qhi - f.window);
 #pragma unroll
     for (int nt = 0; nt < BR / 8; ++nt)
 #pragma unroll
@@ -318,7 +424,9 @@ __global__ void __launch_bounds__(NT, 1) attn_bwd_k(AttnBwdArgs a) {
         float p = exp2f(s[nt][e] * f.scale_log2 - cL[ci]);
         if (!full) {
           const int qi = r0 + ci;
-          if (qi >= f.Lq || !visible(e < 2 ? key_a : key_b, f.q_offset + qi, f.Lk, f.window)) p = 0.f;
+          if (qi >= f.Lq || !(e < 2 ? visible(key_a, kpa, qoff + qi, f.Lk, f.window)
+                                    : visible(key_b, kpb, qoff + qi, f.Lk, f.window)))
+            p = 0.f;
         }
         s[nt][e] = p;
         dp[nt][e] = p * (dp[nt][e] - cDD[ci]);
@@ -425,8 +533,24 @@ int bwd_launch(const AttnBwdArgs& a, cudaStream_t st) {
   return (int)cudaGetLastError();
 }
 
+template <int HD>
+int probsum_launch(const AttnArgs& a, float* imp, cudaStream_t st) {
+  const size_t sm = (size_t)2 * (128 + 64) * (HD + 8) * 2;
+  cudaFuncSetAttribute(attn_probsum_k<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  dim3 grid((a.Lq + 127) / 128, (a.Lk + 63) / 64, a.B);
+  attn_probsum_k<HD><<<grid, NT, sm, st>>>(a, imp);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace attn
 }  // namespace s0
+
+int attn_probsum_launch(const AttnArgs& a, float* imp, int hd, cudaStream_t st) {
+  if (a.Lq <= 0 || a.Lk <= 0) return 0;
+  if (hd == 64) return s0::attn::probsum_launch<64>(a, imp, st);
+  if (hd == 128) return s0::attn::probsum_launch<128>(a, imp, st);
+  return -1;
+}
 
 int attn_fwd_launch(const AttnArgs& a, int hd, cudaStream_t st) {
   if (a.Lq <= 0 || a.Lk <= 0) return 0;

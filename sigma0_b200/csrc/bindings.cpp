@@ -380,7 +380,8 @@ static void attn_check(const at::Tensor& t, const char* name, int64_t hd) {
 }
 
 static AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
-                          const at::Tensor& lse, double scale, int64_t window, int64_t q_offset) {
+                          const at::Tensor& lse, double scale, int64_t window, int64_t q_offset,
+                          const c10::optional<at::Tensor>& kpos, const c10::optional<at::Tensor>& qoff) {
   const int64_t hd = q.size(3);
   TORCH_CHECK(hd == 64 || hd == 128, "attention head dim must be 64 or 128, got ", hd);
   attn_check(q, "q", hd);
@@ -404,22 +405,36 @@ static AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Te
   a.B = (int)q.size(0); a.nh = (int)q.size(2); a.Lq = (int)q.size(1); a.Lk = (int)k.size(1);
   a.q_offset = (int)q_offset; a.window = (int)window;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.kpos = nullptr;
+  a.qoff = nullptr;
+  if (kpos && kpos->defined()) {
+    req(*kpos, at::kInt, "kpos");
+    TORCH_CHECK(kpos->is_contiguous() && kpos->dim() == 2 && kpos->size(0) == k.size(0) && kpos->size(1) == k.size(1),
+                "kpos [B, Lk] int32");
+    a.kpos = kpos->data_ptr<int>();
+  }
+  if (qoff && qoff->defined()) {
+    req(*qoff, at::kInt, "qoff");
+    TORCH_CHECK(qoff->is_contiguous() && qoff->numel() == q.size(0), "qoff [B] int32");
+    a.qoff = qoff->data_ptr<int>();
+  }
   return a;
 }
 
 void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, double scale, int64_t window,
-              int64_t q_offset) {
+              int64_t q_offset, c10::optional<at::Tensor> kpos, c10::optional<at::Tensor> qoff) {
   c10::cuda::CUDAGuard guard(q.device());
-  const AttnArgs a = attn_args(q, k, v, o, lse, scale, window, q_offset);
+  const AttnArgs a = attn_args(q, k, v, o, lse, scale, window, q_offset, kpos, qoff);
   const int rc = attn_fwd_launch(a, (int)q.size(3), stream());
   TORCH_CHECK(rc == 0, "attn_fwd launch failed (", rc, ")");
 }
 
 void attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dout, at::Tensor D,
-              at::Tensor dq_acc, at::Tensor dk, at::Tensor dv, double scale, int64_t window, int64_t q_offset) {
+              at::Tensor dq_acc, at::Tensor dk, at::Tensor dv, double scale, int64_t window, int64_t q_offset,
+              c10::optional<at::Tensor> kpos, c10::optional<at::Tensor> qoff) {
   c10::cuda::CUDAGuard guard(q.device());
   AttnBwdArgs a;
-  a.f = attn_args(q, k, v, o, lse, scale, window, q_offset);
+  a.f = attn_args(q, k, v, o, lse, scale, window, q_offset, kpos, qoff);
   const int64_t hd = q.size(3);
   attn_check(dout, "dout", hd);
   attn_check(dk, "dk", hd);
@@ -440,6 +455,18 @@ void attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor
   a.scale = (float)scale;
   const int rc = attn_bwd_launch(a, (int)hd, stream());
   TORCH_CHECK(rc == 0, "attn_bwd launch failed (", rc, ")");
+}
+
+void attn_probsum(at::Tensor q, at::Tensor k, at::Tensor lse, at::Tensor imp, double scale, int64_t window,
+                  int64_t q_offset, c10::optional<at::Tensor> kpos, c10::optional<at::Tensor> qoff) {
+  c10::cuda::CUDAGuard guard(q.device());
+  const AttnArgs a = attn_args(q, k, k, q, lse, scale, window, q_offset, kpos, qoff);
+  req(imp, at::kFloat, "imp");
+  TORCH_CHECK(imp.is_contiguous() && imp.dim() == 3 && imp.size(0) == q.size(0) && imp.size(1) == q.size(1) &&
+                  imp.size(2) == k.size(1),
+              "imp [B, Lq, Lk] fp32");
+  const int rc = attn_probsum_launch(a, imp.data_ptr<float>(), (int)q.size(3), stream());
+  TORCH_CHECK(rc == 0, "attn_probsum launch failed (", rc, ")");
 }
 
 // ---- gated delta rule chunk scan -----------------------------------------------------------
@@ -784,10 +811,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("abort"), py::arg("stamps") = py::none(),
         "out = sum over ranks of A_r Bt_r^T: tcgen05 tiles reduced into the owners' peer buffers, then all-gathered "
         "(cooperative launch; returns 0 or a launch error)");
-  m.def("attn_fwd", &attn_fwd,
-        "causal / sliding-window flash attention forward: o and the base-2 row log-sum-exp (window <= 0: none)");
-  m.def("attn_bwd", &attn_bwd,
+  m.def("attn_fwd", &attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("scale"), py::arg("window"), py::arg("q_offset"), py::arg("kpos") = py::none(),
+        py::arg("qoff") = py::none(),
+        "causal / sliding-window flash attention forward: o and the base-2 row log-sum-exp (window <= 0: none; "
+        "optional per-key positions and per-entry query offsets)");
+  m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("dout"), py::arg("D"), py::arg("dq_acc"), py::arg("dk"), py::arg("dv"), py::arg("scale"),
+        py::arg("window"), py::arg("q_offset"), py::arg("kpos") = py::none(), py::arg("qoff") = py::none(),
         "flash attention backward: dk, dv written, dq accumulated into the zeroed fp32 dq_acc (scaled)");
+  m.def("attn_probsum", &attn_probsum, py::arg("q"), py::arg("k"), py::arg("lse"), py::arg("imp"), py::arg("scale"),
+        py::arg("window"), py::arg("q_offset"), py::arg("kpos") = py::none(), py::arg("qoff") = py::none(),
+        "head-summed softmax probabilities [B, Lq, Lk] of a finished forward (no gradient)");
   m.def("gdn_scan_fwd", &gdn_scan_fwd,
         "gated delta rule cross-chunk scan: o, the chunk-start states, vnew and the final state");
   m.def("gdn_scan_bwd", &gdn_scan_bwd,

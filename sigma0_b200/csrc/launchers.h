@@ -169,6 +169,8 @@ struct AttnArgs {
   long sq_b, sq_l, sq_h, sk_b, sk_l, sk_h, sv_b, sv_l, sv_h, so_b, so_l, so_h;
   int B, nh, Lq, Lk, q_offset, window;  // window <= 0: unbounded
   float scale_log2;                // softmax scale * log2(e)
+  const int* kpos;                 // optional [B, Lk] absolute key positions (nullptr: the key index)
+  const int* qoff;                 // optional [B] per-entry query offsets (nullptr: q_offset)
 };
 struct AttnBwdArgs {
   AttnArgs f;                      // the forward's tensors (o, lse as written by it)
@@ -182,6 +184,8 @@ struct AttnBwdArgs {
 };
 int attn_fwd_launch(const AttnArgs& a, int hd, cudaStream_t st);
 int attn_bwd_launch(const AttnBwdArgs& a, int hd, cudaStream_t st);
+// imp [B, Lq, Lk] = head-summed softmax probabilities of a finished forward (lse)
+int attn_probsum_launch(const AttnArgs& a, float* imp, int hd, cudaStream_t st);
 
 // cross-chunk state scan of the chunked gated delta rule (gdn_scan.cu); chunk length 64,
 // value rows split in blocks of 64; every tensor contiguous

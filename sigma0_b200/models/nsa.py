@@ -30,6 +30,7 @@ import torch.nn as nn
 
 from .common import Dense, LayerNorm
 from .rope import apply_rope, rotary_embedding, rope_at, sinusoidal
+from ..ops.attention import attention_probsum, flash_attention, flash_attention_lse, kernel_supported
 from .transformer import FFN, causal_attention, effective_heads
 
 
@@ -71,8 +72,19 @@ class NSABlock(nn.Module):
         nb = k.shape[1] // BS
         kc = k[:, :nb * BS].reshape(B, nb, BS, nh, hd).float().mean(2)
         vc = v[:, :nb * BS].reshape(B, nb, BS, nh, hd).float().mean(2)
-        sc = torch.einsum("blhd,bnhd->blhn", q.float() * scale, kc)
         t = torch.arange(q_offset, q_offset + Lq, device=q.device)
+        if nb > 0 and kernel_supported(q, k, v):
+            # flash kernels: compressed block n sits at its last token, (n + 1) * BS - 1
+            kcb, vcb = kc.to(q.dtype), vc.to(q.dtype)
+            kpos = ((torch.arange(nb, device=q.device) + 1) * BS - 1).to(torch.int32).expand(B, nb)
+            o, lse = flash_attention_lse(q, kcb, vcb, scale, q_offset=q_offset, kpos=kpos)
+            imp = attention_probsum(q, kcb, lse, scale, q_offset=q_offset, kpos=kpos)
+            visible = torch.clamp((t - BS + 1) // BS + 1, min=0)
+            cmask = torch.arange(nb, device=q.device)[None, :] < visible[:, None]
+            cur = (t // BS)[:, None] == torch.arange(nb, device=q.device)[None, :]
+            imp = torch.where(cur[None], torch.ones_like(imp), imp).masked_fill(~cmask[None], -1e9)
+            return o, imp
+        sc = torch.einsum("blhd,bnhd->blhn", q.float() * scale, kc)
         visible = torch.clamp((t - BS + 1) // BS + 1, min=0)
         cmask = torch.arange(nb, device=q.device)[None, :] < visible[:, None]      # (Lq, nb)
         sc = sc.masked_fill(~cmask[None, :, None, :], float("-inf"))
@@ -105,10 +117,17 @@ class NSABlock(nn.Module):
         ksel = kb[bidx, top].reshape(B, ng, S * SB, nh, hd)
         vsel = vb[bidx, top].reshape(B, ng, S * SB, nh, hd)
         qg = torch.nn.functional.pad(q, (0, 0, 0, 0, 0, pad)).reshape(B, ng, SB, nh, hd)
-        sc = torch.einsum("bgqhd,bgkhd->bgqhk", qg.float() * scale, ksel.float())
-        qpos = q_offset + torch.arange(ng * SB, device=q.device).reshape(ng, SB)
         off = torch.arange(S * SB, device=q.device)
         kpos = top[..., off // SB] * SB + (off % SB)                                  # (B, ng, S*SB)
+        if kernel_supported(q, k, v):
+            # flash kernels over the gathered blocks: every (batch, group) is one batch entry
+            qoff = (q_offset + torch.arange(ng, device=q.device) * SB).repeat(B)
+            o = flash_attention(qg.reshape(B * ng, SB, nh, hd), ksel.reshape(B * ng, S * SB, nh, hd),
+                                vsel.reshape(B * ng, S * SB, nh, hd), scale=scale,
+                                kpos=kpos.reshape(B * ng, S * SB), qoff=qoff)
+            return o.reshape(B, ng * SB, nh, hd)[:, :Lq]
+        sc = torch.einsum("bgqhd,bgkhd->bgqhk", qg.float() * scale, ksel.float())
+        qpos = q_offset + torch.arange(ng * SB, device=q.device).reshape(ng, SB)
         causal = kpos[:, :, None, :] <= qpos[None, :, :, None]                       # (B, ng, SB, S*SB)
         sc = sc.masked_fill(~causal[:, :, :, None, :], float("-inf"))
         attn = torch.softmax(sc, dim=-1).nan_to_num(0.0)

@@ -46,46 +46,95 @@ def _kernel_ready(t: torch.Tensor) -> torch.Tensor:
 
 class _FlashAttn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, scale, window, q_offset):
+    def forward(ctx, q, k, v, scale, window, q_offset, kpos, qoff):
         from ._ext import ext
         q, k, v = _kernel_ready(q), _kernel_ready(k), _kernel_ready(v)
         B, Lq, nh, hd = q.shape
         o = torch.empty_like(q, memory_format=torch.contiguous_format)
         lse = torch.empty(B, nh, Lq, dtype=torch.float32, device=q.device)
-        ext().attn_fwd(q, k, v, o, lse, scale, window, q_offset)
-        ctx.save_for_backward(q, k, v, o, lse)
+        ext().attn_fwd(q, k, v, o, lse, scale, window, q_offset, kpos, qoff)
+        ctx.save_for_backward(q, k, v, o, lse, kpos, qoff)
         ctx.args = (scale, window, q_offset)
-        return o
+        ctx.mark_non_differentiable(lse)
+        return o, lse
 
     @staticmethod
-    def backward(ctx, do):
+    def backward(ctx, do, _dlse):
         from ._ext import ext
-        q, k, v, o, lse = ctx.saved_tensors
+        q, k, v, o, lse, kpos, qoff = ctx.saved_tensors
         scale, window, q_offset = ctx.args
         do = _kernel_ready(do.to(torch.bfloat16))
         D = torch.empty_like(lse)
         dq = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
         dk = torch.empty(k.shape, dtype=torch.bfloat16, device=k.device)
         dv = torch.empty(v.shape, dtype=torch.bfloat16, device=v.device)
-        ext().attn_bwd(q, k, v, o, lse, do, D, dq, dk, dv, scale, window, q_offset)
-        return dq.to(torch.bfloat16), dk, dv, None, None, None
+        ext().attn_bwd(q, k, v, o, lse, do, D, dq, dk, dv, scale, window, q_offset, kpos, qoff)
+        return dq.to(torch.bfloat16), dk, dv, None, None, None, None, None
 
 
-def flash_attention(q, k, v, scale=None, causal=True, window=None, q_offset=0, force_kernel=False):
+_ENABLED = [True]
+
+
+class use_kernels:
+    """``with use_kernels(False):`` runs the tensor-expression paths instead of the
+    kernels (benchmarks and parity checks against the same module)."""
+
+    def __init__(self, on: bool):
+        self.on, self.prev = on, None
+
+    def __enter__(self):
+        self.prev, _ENABLED[0] = _ENABLED[0], self.on
+
+    def __exit__(self, *exc):
+        _ENABLED[0] = self.prev
+
+
+def kernel_supported(q, k, v) -> bool:
+    return (_ENABLED[0] and q.is_cuda and q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
+            and q.shape[-1] in (64, 128))
+
+
+def flash_attention_lse(q, k, v, scale, window=None, q_offset=0, kpos=None, qoff=None):
+    """The kernels' forward with its base-2 row log-sum-exp: (o, lse [B, nh, Lq]).
+
+    ``kpos`` (int32 [B, Lk]) gives every key an absolute position (compressed or gathered
+    key blocks); ``qoff`` (int32 [B]) gives every batch entry its own query offset."""
+    kp = None if kpos is None else kpos.to(device=q.device, dtype=torch.int32).contiguous()
+    qo = None if qoff is None else qoff.to(device=q.device, dtype=torch.int32).contiguous()
+    return _FlashAttn.apply(q, k, v, float(scale), int(window or 0), int(q_offset), kp, qo)
+
+
+def attention_probsum(q, k, lse, scale, window=None, q_offset=0, kpos=None, qoff=None):
+    """Head-summed softmax probabilities [B, Lq, Lk] (fp32) of a forward whose ``lse``
+    is given -- the NSA block importance.  No gradient."""
+    from ._ext import ext
+    q, k = _kernel_ready(q.detach()), _kernel_ready(k.detach())
+    imp = torch.empty(q.shape[0], q.shape[1], k.shape[1], dtype=torch.float32, device=q.device)
+    kp = None if kpos is None else kpos.to(device=q.device, dtype=torch.int32).contiguous()
+    qo = None if qoff is None else qoff.to(device=q.device, dtype=torch.int32).contiguous()
+    ext().attn_probsum(q, k, lse, imp, float(scale), int(window or 0), int(q_offset), kp, qo)
+    return imp
+
+
+def flash_attention(q, k, v, scale=None, causal=True, window=None, q_offset=0, force_kernel=False,
+                    kpos=None, qoff=None):
     """q (B, Lq, nh, hd), k/v (B, Lk, nh, hd) -> (B, Lq, nh, hd).
 
-    Query i sits at absolute position ``q_offset + i`` and sees keys j <= that
-    position (within ``window`` tokens when given)."""
+    Query i sits at absolute position ``q_offset + i`` (``qoff[b] + i`` when given) and
+    sees keys at positions <= its own (within ``window`` tokens when given); key j sits
+    at position j, or ``kpos[b, j]``."""
     hd = q.shape[-1]
     scale = scale if scale is not None else hd ** -0.5
-    full = window is None and q_offset == 0 and q.shape[1] == k.shape[1]
+    tables = kpos is not None or qoff is not None
+    full = window is None and q_offset == 0 and q.shape[1] == k.shape[1] and not tables
     # Full causal attention stays on torch's fused attention, which dispatches to a
-    # Blackwell-native library kernel (0.9-1.4 PFLOP/s forward on B200 against 0.15-0.18
-    # for these mma.sync kernels); windows and decode offsets, which it can only take as a
-    # dense mask, run the kernels here (11x the masked path at window 512).
-    if ((not full or force_kernel) and causal and q.is_cuda and q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16
-            and v.dtype == torch.bfloat16 and hd in (64, 128)):
-        return _FlashAttn.apply(q, k, v, float(scale), int(window or 0), int(q_offset))
+    # Blackwell-native library kernel (0.9-1.4 PFLOP/s forward on B200 against 0.15-0.2
+    # for these mma.sync kernels); windows, decode offsets and position tables, which it
+    # can only take as a dense mask, run the kernels here (7-16x the masked path).
+    if (not full or force_kernel) and causal and kernel_supported(q, k, v):
+        return flash_attention_lse(q, k, v, scale, window, q_offset, kpos, qoff)[0]
+    if tables:
+        raise ValueError("key-position / query-offset tables need bf16 CUDA inputs with head dim 64 or 128")
     if full:
         o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                            is_causal=causal, scale=scale)
