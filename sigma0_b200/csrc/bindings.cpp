@@ -588,6 +588,59 @@ void kda_intra_bwd(at::Tensor q, at::Tensor k, at::Tensor kb, at::Tensor G, at::
   TORCH_CHECK(rc == 0, "kda_intra_bwd launch failed (", rc, ")");
 }
 
+// ---- S5 complex diagonal scan ----------------------------------------------------------------
+static const float2* c2(const at::Tensor& t) { return reinterpret_cast<const float2*>(t.data_ptr()); }
+static float2* c2m(at::Tensor& t) { return reinterpret_cast<float2*>(t.data_ptr()); }
+
+static S5Args s5_args(const at::Tensor& lam, int64_t B, int64_t L, int64_t P) {
+  gdn_req(lam, at::kComplexFloat, "lam", {P});
+  S5Args a{};
+  a.lam = c2(lam);
+  a.B = B; a.L = (int)L; a.P = (int)P; a.nchunk = (int)((L + 63) / 64);
+  return a;
+}
+
+void s5_scan_fwd(at::Tensor lam, at::Tensor bu, c10::optional<at::Tensor> x0, at::Tensor xs, at::Tensor xlast,
+                 at::Tensor part) {
+  c10::cuda::CUDAGuard guard(bu.device());
+  TORCH_CHECK(bu.dim() == 3, "bu [B, L, P]");
+  const int64_t B = bu.size(0), L = bu.size(1), P = bu.size(2);
+  S5Args a = s5_args(lam, B, L, P);
+  gdn_req(bu, at::kComplexFloat, "bu", {B, L, P});
+  gdn_req(xs, at::kComplexFloat, "xs", {B, L, P});
+  gdn_req(xlast, at::kComplexFloat, "xlast", {B, P});
+  gdn_req(part, at::kComplexFloat, "part", {B, a.nchunk, P});
+  a.bu = c2(bu); a.xs = c2m(xs); a.xlast = c2m(xlast); a.part = c2m(part);
+  a.x0 = nullptr;
+  if (x0 && x0->defined()) {
+    gdn_req(*x0, at::kComplexFloat, "x0", {B, P});
+    a.x0 = c2(*x0);
+  }
+  const int rc = s5_scan_launch(a, false, stream());
+  TORCH_CHECK(rc == 0, "s5_scan_fwd launch failed (", rc, ")");
+}
+
+void s5_scan_bwd(at::Tensor lam, at::Tensor xs, c10::optional<at::Tensor> x0, at::Tensor dxs,
+                 c10::optional<at::Tensor> dxlast, at::Tensor dbu, at::Tensor dlam, c10::optional<at::Tensor> dx0,
+                 at::Tensor part) {
+  c10::cuda::CUDAGuard guard(xs.device());
+  TORCH_CHECK(xs.dim() == 3, "xs [B, L, P]");
+  const int64_t B = xs.size(0), L = xs.size(1), P = xs.size(2);
+  S5Args a = s5_args(lam, B, L, P);
+  gdn_req(xs, at::kComplexFloat, "xs", {B, L, P});
+  gdn_req(dxs, at::kComplexFloat, "dxs", {B, L, P});
+  gdn_req(dbu, at::kComplexFloat, "dbu", {B, L, P});
+  gdn_req(dlam, at::kComplexFloat, "dlam", {P});
+  gdn_req(part, at::kComplexFloat, "part", {B, a.nchunk, P});
+  a.xs = c2m(xs); a.dxs = c2(dxs); a.dbu = c2m(dbu); a.dlam = c2m(dlam); a.part = c2m(part);
+  a.x0 = nullptr; a.dxlast = nullptr; a.dx0 = nullptr;
+  if (x0 && x0->defined()) { gdn_req(*x0, at::kComplexFloat, "x0", {B, P}); a.x0 = c2(*x0); }
+  if (dxlast && dxlast->defined()) { gdn_req(*dxlast, at::kComplexFloat, "dxlast", {B, P}); a.dxlast = c2(*dxlast); }
+  if (dx0 && dx0->defined()) { gdn_req(*dx0, at::kComplexFloat, "dx0", {B, P}); a.dx0 = c2m(*dx0); }
+  const int rc = s5_scan_launch(a, true, stream());
+  TORCH_CHECK(rc == 0, "s5_scan_bwd launch failed (", rc, ")");
+}
+
 // ---- profiling ---------------------------------------------------------------------------
 at::Tensor m3_phase_probe() {
   unsigned long long v[16];
@@ -829,6 +882,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "reverse scan: per value-block partial gradients of qe / kc / kd / intra / tot, dvc and dS0");
   m.def("kda_intra_fwd", &kda_intra_fwd, "per-key-dim-decay intra-chunk score and WY matrices of 64-step chunks");
   m.def("kda_intra_bwd", &kda_intra_bwd, "gradients of q, k, kb and the cumulative log decay G");
+  m.def("s5_scan_fwd", &s5_scan_fwd, "S5 complex diagonal recurrence: all states and the final one");
+  m.def("s5_scan_bwd", &s5_scan_bwd, "reverse recurrence: dBu, dlam (accumulated into the zeroed dlam), dx0");
   m.def("m3_phase_probe", &m3_phase_probe,
         "chunk-backward per-phase clock sums since the last call (empty unless built with S0_PHASE_PROBE)");
   m.def("m3_decode_step", &m3_decode_step, py::arg("proj"), py::arg("nh"), py::arg("wB"), py::arg("wC"),

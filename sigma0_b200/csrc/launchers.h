@@ -221,3 +221,20 @@ struct KdaArgs {
   int HD;                             // a multiple of 32
 };
 int kda_intra_launch(const KdaArgs& a, bool bwd, cudaStream_t st);
+
+// S5 complex diagonal recurrence x_t = lam * x_{t-1} + Bu_t (s5_scan.cu); complex64 as float2,
+// every tensor contiguous, chunks of 64 steps
+struct S5Args {
+  const float2* lam;                  // [P]
+  const float2* bu;                   // [B, L, P]
+  const float2* x0;                   // [B, P] initial state (nullptr: zeros)
+  float2* xs;                         // [B, L, P] (forward output; backward input)
+  float2* xlast;                      // [B, P]
+  float2* part;                       // [B, nchunk, P] scratch
+  const float2* dxs;                  // backward: [B, L, P]
+  const float2* dxlast;               // backward: [B, P] (nullptr: zeros)
+  float2 *dbu, *dlam, *dx0;           // backward outputs ([B, L, P], [P] zeroed, [B, P] or nullptr)
+  long B;
+  int L, P, nchunk;
+};
+int s5_scan_launch(const S5Args& a, bool bwd, cudaStream_t st);

@@ -33,6 +33,40 @@ def make_dplr_hippo(N: int):
     return lam_re + 1j * lam_im, V
 
 
+class _S5Scan(torch.autograd.Function):
+    """x_t = lam * x_{t-1} + Bu_t on the kernels of ``csrc/s5_scan.cu`` (complex64):
+    returns every state and the final one; gradients for lam, Bu and x0."""
+
+    @staticmethod
+    def forward(ctx, lam, bu, x0):
+        from ..ops._ext import ext
+        c64 = lambda t: t.detach().to(torch.complex64).contiguous()
+        lam_c, bu_c = c64(lam), c64(bu)
+        x0_c = None if x0 is None else c64(x0)
+        B, L, P = bu_c.shape
+        xs = torch.empty_like(bu_c)
+        xl = torch.empty(B, P, dtype=torch.complex64, device=bu.device)
+        part = torch.empty(B, (L + 63) // 64, P, dtype=torch.complex64, device=bu.device)
+        ext().s5_scan_fwd(lam_c, bu_c, x0_c, xs, xl, part)
+        ctx.save_for_backward(lam_c, xs, x0_c)
+        ctx.has_x0 = x0 is not None
+        return xs, xl
+
+    @staticmethod
+    def backward(ctx, dxs, dxl):
+        from ..ops._ext import ext
+        lam_c, xs, x0_c = ctx.saved_tensors
+        B, L, P = xs.shape
+        dxs = torch.zeros_like(xs) if dxs is None else dxs.to(torch.complex64).contiguous()
+        dxl = None if dxl is None else dxl.to(torch.complex64).contiguous()
+        dbu = torch.empty_like(xs)
+        dlam = torch.zeros(P, dtype=torch.complex64, device=xs.device)
+        dx0 = torch.empty(B, P, dtype=torch.complex64, device=xs.device) if ctx.has_x0 else None
+        part = torch.empty(B, (L + 63) // 64, P, dtype=torch.complex64, device=xs.device)
+        ext().s5_scan_bwd(lam_c, xs, x0_c, dxs, dxl, dbu, dlam, dx0, part)
+        return dlam, dbu, dx0
+
+
 class S5(nn.Module):
     is_transformer = False
 
@@ -86,11 +120,15 @@ class S5(nn.Module):
                               torch.complex(self.C2[..., 0], self.C2[..., 1])], -1)
         return torch.complex(self.C[..., 0], self.C[..., 1])
 
+    use_kernel = True        # CUDA tensors take the s5_scan kernels (False: the chunked einsum)
+
     def _scan(self, lb, Bu, x0=None, reverse=False):
         """x_t = lb * x_{t-1} + Bu_t over (B, L, P) complex."""
         if reverse:
             xs, _ = self._scan(lb, Bu.flip(1))
             return xs.flip(1), None
+        if Bu.is_cuda and self.use_kernel and Bu.shape[1] > 0:
+            return _S5Scan.apply(lb, Bu, x0)
         B_, L, P = Bu.shape
         C = self.chunk
         t = torch.arange(C, device=Bu.device)

@@ -13,7 +13,7 @@ from __future__ import annotations
 _C = None
 _COUNT = [0]
 # kernels launched per call, where it is not one
-_LAUNCHES = {"m3_fwd": 6, "m3_bwd": 10, "ln_bwd": 2, "rms_bwd": 2, "glu_res_bwd": 2, "attn_bwd": 2}
+_LAUNCHES = {"m3_fwd": 6, "m3_bwd": 10, "ln_bwd": 2, "rms_bwd": 2, "glu_res_bwd": 2, "attn_bwd": 2, "s5_scan_fwd": 3, "s5_scan_bwd": 3}
 
 
 class _Counted:
