@@ -516,7 +516,7 @@ void gdn_scan_fwd(at::Tensor qe, at::Tensor kc, at::Tensor kd, at::Tensor intra,
   }
   a.o = o.data_ptr<float>(); a.S_all = S_all.data_ptr<float>(); a.vnew = vnew.data_ptr<float>();
   a.S_fin = S_fin.data_ptr<float>();
-  const int rc = gdn_scan_launch(a, (int)HD, false, stream());
+  const int rc = gdn_scan_launch(a, (int)HD, false, num_sms(qe), stream());
   TORCH_CHECK(rc == 0, "gdn_scan_fwd launch failed (", rc, ")");
 }
 
@@ -526,7 +526,7 @@ void gdn_scan_bwd(at::Tensor qe, at::Tensor kc, at::Tensor kd, at::Tensor intra,
   c10::cuda::CUDAGuard guard(qe.device());
   const int64_t HVD = vnew.size(-1);
   GdnArgs a = gdn_args(qe, kc, kd, intra, tot, HVD);
-  const int64_t B = a.B, nh = a.nh, nc = a.nc, HD = qe.size(4), nvb = HVD / 64;
+  const int64_t B = a.B, nh = a.nh, nc = a.nc, HD = qe.size(4), nvb = HVD / gdn_scan_bwd_value_block();
   gdn_req(S_all, at::kFloat, "S_all", {B, nh, nc, HVD, HD});
   gdn_req(vnew, at::kFloat, "vnew", {B, nh, nc, 64, HVD});
   gdn_req(dout, at::kFloat, "dout", {B, nh, nc, 64, HVD});
@@ -546,7 +546,7 @@ void gdn_scan_bwd(at::Tensor qe, at::Tensor kc, at::Tensor kd, at::Tensor intra,
   a.dqe_p = dqe_p.data_ptr<float>(); a.dkc_p = dkc_p.data_ptr<float>(); a.dkd_p = dkd_p.data_ptr<float>();
   a.din_p = din_p.data_ptr<float>(); a.dtot_p = dtot_p.data_ptr<float>(); a.dvc = dvc.data_ptr<float>();
   a.dS0 = dS0.data_ptr<float>();
-  const int rc = gdn_scan_launch(a, (int)HD, true, stream());
+  const int rc = gdn_scan_launch(a, (int)HD, true, num_sms(qe), stream());
   TORCH_CHECK(rc == 0, "gdn_scan_bwd launch failed (", rc, ")");
 }
 
@@ -878,6 +878,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "head-summed softmax probabilities [B, Lq, Lk] of a finished forward (no gradient)");
   m.def("gdn_scan_fwd", &gdn_scan_fwd,
         "gated delta rule cross-chunk scan: o, the chunk-start states, vnew and the final state");
+  m.def("gdn_scan_bwd_value_block", &gdn_scan_bwd_value_block,
+        "value rows per CTA of the reverse scan (the leading dimension of its partials is HVD / this)");
   m.def("gdn_scan_bwd", &gdn_scan_bwd,
         "reverse scan: per value-block partial gradients of qe / kc / kd / intra / tot, dvc and dS0");
   m.def("kda_intra_fwd", &kda_intra_fwd, "per-key-dim-decay intra-chunk score and WY matrices of 64-step chunks");

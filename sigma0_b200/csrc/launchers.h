@@ -201,14 +201,15 @@ struct GdnArgs {
   float* S_fin;                       // [B, nh, HVD, HD]
   const float* dout;                  // backward: dL/do [B, nh, nc, 64, HVD]
   const float* dS_fin;                // backward: dL/dS_fin (nullptr: zeros)
-  float *dqe_p, *dkc_p, *dkd_p;       // [HVD / 64, B, nh, nc, 64, HD] per value-block partials
-  float* din_p;                       // [HVD / 64, B, nh, nc, 64, 64]
-  float* dtot_p;                      // [HVD / 64, B, nh, nc, HD]
+  float *dqe_p, *dkc_p, *dkd_p;       // [HVD / VBb, B, nh, nc, 64, HD] per value-block partials
+  float* din_p;                       // [HVD / VBb, B, nh, nc, 64, 64]
+  float* dtot_p;                      // [HVD / VBb, B, nh, nc, HD]  (VBb = gdn_scan_bwd_value_block())
   float* dvc;                         // [B, nh, nc, 64, HVD]
   float* dS0;                         // [B, nh, HVD, HD]
   int B, nh, nc, HVD;
 };
-int gdn_scan_launch(const GdnArgs& a, int hd, bool bwd, cudaStream_t st);
+int gdn_scan_launch(const GdnArgs& a, int hd, bool bwd, int sms, cudaStream_t st);
+int gdn_scan_bwd_value_block();
 
 // intra-chunk score / WY matrices of the per-key-dim-decay delta rule (kda_intra.cu);
 // N chunks of 64 steps, every tensor contiguous fp32

@@ -84,7 +84,7 @@ class _GDNScan(torch.autograd.Function):
         qe_b, kc_b, kd_b, in_b, tot_c, S_all, vnew = ctx.saved_tensors
         B, nh, nc, C, hd = qe_b.shape
         hvd = vnew.shape[-1]
-        nvb = hvd // 64
+        nvb = hvd // ext().gdn_scan_bwd_value_block()
         do = torch.zeros_like(vnew) if do is None else do.float().contiguous()
         dS_fin = None if dS_fin is None else dS_fin.float().contiguous()
         dev = vnew.device
