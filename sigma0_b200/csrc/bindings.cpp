@@ -407,6 +407,7 @@ static AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Te
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.kpos = nullptr;
   a.qoff = nullptr;
+  a.status = nullptr;
   if (kpos && kpos->defined()) {
     req(*kpos, at::kInt, "kpos");
     TORCH_CHECK(kpos->is_contiguous() && kpos->dim() == 2 && kpos->size(0) == k.size(0) && kpos->size(1) == k.size(1),
@@ -427,6 +428,17 @@ void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor
   const AttnArgs a = attn_args(q, k, v, o, lse, scale, window, q_offset, kpos, qoff);
   const int rc = attn_fwd_launch(a, (int)q.size(3), stream());
   TORCH_CHECK(rc == 0, "attn_fwd launch failed (", rc, ")");
+}
+
+void attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, double scale,
+                 int64_t window, int64_t q_offset, c10::optional<at::Tensor> kpos, c10::optional<at::Tensor> qoff,
+                 at::Tensor status) {
+  c10::cuda::CUDAGuard guard(q.device());
+  AttnArgs a = attn_args(q, k, v, o, lse, scale, window, q_offset, kpos, qoff);
+  req(status, at::kInt, "status");
+  a.status = status.data_ptr<int>();
+  const int rc = attn_fwd_tc_launch(a, (int)q.size(3), stream());
+  TORCH_CHECK(rc == 0, "attn_fwd_tc launch failed (", rc, ")");
 }
 
 void attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dout, at::Tensor D,
@@ -869,6 +881,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("qoff") = py::none(),
         "causal / sliding-window flash attention forward: o and the base-2 row log-sum-exp (window <= 0: none; "
         "optional per-key positions and per-entry query offsets)");
+  m.def("attn_fwd_tc", &attn_fwd_tc, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("scale"), py::arg("window"), py::arg("q_offset"), py::arg("kpos"), py::arg("qoff"), py::arg("status"),
+        "flash attention forward on tcgen05 / TMEM / TMA (same outputs as attn_fwd; status set on a wait timeout)");
   m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dout"), py::arg("D"), py::arg("dq_acc"), py::arg("dk"), py::arg("dv"), py::arg("scale"),
         py::arg("window"), py::arg("q_offset"), py::arg("kpos") = py::none(), py::arg("qoff") = py::none(),

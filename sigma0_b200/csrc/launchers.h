@@ -171,6 +171,7 @@ struct AttnArgs {
   float scale_log2;                // softmax scale * log2(e)
   const int* kpos;                 // optional [B, Lk] absolute key positions (nullptr: the key index)
   const int* qoff;                 // optional [B] per-entry query offsets (nullptr: q_offset)
+  int* status;                     // optional: set to 1 when a bounded wait of the tcgen05 forward timed out
 };
 struct AttnBwdArgs {
   AttnArgs f;                      // the forward's tensors (o, lse as written by it)
@@ -184,6 +185,8 @@ struct AttnBwdArgs {
 };
 int attn_fwd_launch(const AttnArgs& a, int hd, cudaStream_t st);
 int attn_bwd_launch(const AttnBwdArgs& a, int hd, cudaStream_t st);
+// the same forward on tcgen05 / TMEM / TMA (attention_tc.cu); -3: unaligned base, -4: tensor map
+int attn_fwd_tc_launch(const AttnArgs& a, int hd, cudaStream_t st);
 // imp [B, Lq, Lk] = head-summed softmax probabilities of a finished forward (lse)
 int attn_probsum_launch(const AttnArgs& a, float* imp, int hd, cudaStream_t st);
 

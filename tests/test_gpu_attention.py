@@ -66,3 +66,4 @@ def test_flash_attention_runs_the_kernel():
     torch.cuda.synchronize()
     if before is not None:
         assert _ext.launch_count() > before
+
