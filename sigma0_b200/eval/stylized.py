@@ -16,7 +16,9 @@ The analyse-only diagnostics of the reference's ``tools/diagnostics/lob_evals.py
   fitted on generated windows and on real windows and both are scored by AUC on held-out
   real windows; the ratio (synthetic / real AUC excess over 0.5) is the headline;
 * ``build_origin`` / ``stamp`` / ``write_provenance`` -- every number carries where it
-  came from (run directory, checkpoint, experiment, ticker, depth).
+  came from (run directory, checkpoint, experiment, ticker, depth);
+* the tail-, regime- and position-conditioned breakdowns (``eval/conditioned.py``),
+  selected with ``--evals``.
 
     python -m sigma0_b200.eval.stylized --run <save_dir> --out <dir> [--experiment NAME]
 """
@@ -208,6 +210,10 @@ def main(argv=None):
     ap.add_argument("--experiment", default="")
     ap.add_argument("--ticker", default="")
     ap.add_argument("--checkpoint", default="")
+    ap.add_argument("--evals", nargs="+", default=["stylized", "tstr", "tail", "regime", "position"],
+                    choices=["stylized", "tstr", "tail", "regime", "position"])
+    ap.add_argument("--bin_width", type=int, default=25, help="position-in-window bin width (messages)")
+    ap.add_argument("--cond_msgs", type=int, default=None, help="conditioning length c of the run (position eval)")
     a = ap.parse_args(argv)
     from ..pipeline.lobbench import load_run
     run = load_run(a.run)
@@ -220,12 +226,23 @@ def main(argv=None):
     origin = build_origin(a.run, a.experiment, a.ticker, depth, a.checkpoint)
     write_provenance(a.out, origin, {"windows": len(ids)})
     results = {"sanity": assert_generation_sane(br, bg, origin)}
-    results["stylized_facts"] = stylized_facts(br, bg)
-    results["tstr"] = tstr(mr, br, mg, bg)
+    if "stylized" in a.evals:
+        results["stylized_facts"] = stylized_facts(br, bg)
+    if "tstr" in a.evals:
+        results["tstr"] = tstr(mr, br, mg, bg)
+    cond = [e for e in ("tail", "regime", "position") if e in a.evals]
+    if cond:
+        from .conditioned import run_all
+        res = run_all(mr, br, mg, bg, bin_width=a.bin_width, c=a.cond_msgs)
+        for e in cond:
+            results[e] = res[e]
     for k, v in results.items():
         with open(os.path.join(a.out, f"{k}.json"), "w") as f:
             json.dump(stamp(v, origin), f, indent=1, default=float)
-    print(json.dumps({k: (v if k != "stylized_facts" else v["diff"]) for k, v in results.items()}, default=float))
+    summary = {k: (v["diff"] if k == "stylized_facts" else v) for k, v in results.items()
+               if k not in ("tail", "regime", "position")}
+    summary.update({k: "written" for k in ("tail", "regime", "position") if k in results})
+    print(json.dumps(summary, default=float))
 
 
 if __name__ == "__main__":
