@@ -17,8 +17,9 @@ The analyse-only diagnostics of the reference's ``tools/diagnostics/lob_evals.py
   real windows; the ratio (synthetic / real AUC excess over 0.5) is the headline;
 * ``build_origin`` / ``stamp`` / ``write_provenance`` -- every number carries where it
   came from (run directory, checkpoint, experiment, ticker, depth);
-* the tail-, regime- and position-conditioned breakdowns (``eval/conditioned.py``),
-  selected with ``--evals``.
+* the tail-, regime- and position-conditioned breakdowns (``eval/conditioned.py``) and the
+  joint volatility-volume, limit-order response, resampler-baseline and reproducibility
+  comparisons (``eval/observational.py``), selected with ``--evals``.
 
     python -m sigma0_b200.eval.stylized --run <save_dir> --out <dir> [--experiment NAME]
 """
@@ -139,9 +140,12 @@ def stylized_facts(books_real: Sequence[np.ndarray], books_gen: Sequence[np.ndar
 
 
 def _ofi_features(msgs: np.ndarray, book: np.ndarray, H: int, W: int):
-    """(features, labels): signed order flow over the last W events, spread, and the sign
-    of the mid move over the next H events, at every event with a valid book."""
+    """(features, labels): signed order flow over the last W events, spread and touch
+    imbalance, and the sign of the mid move over the next H events, at every event with a
+    valid book."""
     ask, bid, ok = _touch(book)
+    b = np.asarray(book, dtype=np.float64)
+    av, bv = b[:, 1], b[:, 3]
     mid = 0.5 * (ask + bid)
     side = np.where(np.asarray(msgs)[:, 6] > 0, 1.0, -1.0)
     size = np.asarray(msgs)[:, 4].astype(np.float64)
@@ -151,9 +155,10 @@ def _ofi_features(msgs: np.ndarray, book: np.ndarray, H: int, W: int):
     X, y = [], []
     for t in range(W, len(mid) - H):
         if ok[t] and ok[t + H] and mid[t + H] != mid[t]:
-            X.append([cs[t + 1] - cs[t + 1 - W], ask[t] - bid[t]])
+            imb = (bv[t] - av[t]) / max(av[t] + bv[t], 1e-12)
+            X.append([cs[t + 1] - cs[t + 1 - W], ask[t] - bid[t], imb])
             y.append(1.0 if mid[t + H] > mid[t] else 0.0)
-    return np.array(X).reshape(-1, 2), np.array(y)
+    return np.array(X).reshape(-1, 3), np.array(y)
 
 
 def _logistic(X, y, l2=1e-3, iters=200):
@@ -179,27 +184,62 @@ def auc(scores: np.ndarray, y: np.ndarray) -> float:
     return float((r[pos].sum() - n1 * (n1 + 1) / 2) / (n1 * n0))
 
 
-def tstr(msgs_real, books_real, msgs_gen, books_gen, H: int = 10, W: int = 20, seed: int = 0) -> Dict:
+def tstr(msgs_real, books_real, msgs_gen, books_gen, H: int = 10, W: int = 20, seed: int = 0,
+         n_boot: int = 200) -> Dict:
+    """Train on synthetic, test on real: a mid-direction predictor on [windowed OFI, spread,
+    touch imbalance] fitted on generated windows (s -> r) and on real training windows
+    (r -> r), both scored by AUC on the same held-out real windows.  Reports the AUC ratio
+    s->r / r->r with a bootstrap interval over test windows, the excess-over-chance ratio,
+    and a gradient-boosting row when scikit-learn is installed."""
     rng = np.random.default_rng(seed)
     n = len(books_real)
     perm = rng.permutation(n)
     test, train = perm[: max(n // 3, 1)], perm[max(n // 3, 1):]
+
     def feats(ms, bs, idx):
-        parts = [_ofi_features(ms[i], bs[i], H, W) for i in idx]
-        X = np.concatenate([p[0] for p in parts]) if parts else np.zeros((0, 2))
-        y = np.concatenate([p[1] for p in parts]) if parts else np.zeros(0)
-        return X, y
-    Xte, yte = feats(msgs_real, books_real, test)
-    Xr, yr = feats(msgs_real, books_real, train)
-    Xg, yg = feats(msgs_gen, books_gen, range(len(books_gen)))
-    res = {"n_test": int(len(yte)), "n_train_real": int(len(yr)), "n_train_gen": int(len(yg))}
-    if min(len(yte), len(yr), len(yg)) < 10 or len(set(yr)) < 2 or len(set(yg)) < 2:
+        parts = [(_ofi_features(ms[i], bs[i], H, W), i) for i in idx]
+        X = np.concatenate([p[0][0] for p in parts]) if parts else np.zeros((0, 3))
+        y = np.concatenate([p[0][1] for p in parts]) if parts else np.zeros(0)
+        wid = np.concatenate([np.full(len(p[0][1]), p[1]) for p in parts]) if parts else np.zeros(0)
+        return X, y, wid
+    Xte, yte, wte = feats(msgs_real, books_real, test)
+    Xr, yr, _ = feats(msgs_real, books_real, train)
+    Xg, yg, _ = feats(msgs_gen, books_gen, range(len(books_gen)))
+    res = {"n_test": int(len(yte)), "n_train_real": int(len(yr)), "n_train_gen": int(len(yg)),
+           "n_test_windows": int(len(np.unique(wte)))}
+    if min(len(yte), len(yr), len(yg)) < 10 or len(set(yr)) < 2 or len(set(yg)) < 2 or len(set(yte)) < 2:
         res["skipped"] = "too few labelled events"
         return res
-    res["auc_trained_on_real"] = auc(_logistic(Xr, yr)(Xte), yte)
-    res["auc_trained_on_gen"] = auc(_logistic(Xg, yg)(Xte), yte)
+    pr, pg = _logistic(Xr, yr)(Xte), _logistic(Xg, yg)(Xte)
+    res["auc_trained_on_real"] = auc(pr, yte)
+    res["auc_trained_on_gen"] = auc(pg, yte)
     ex_r = res["auc_trained_on_real"] - 0.5
     res["tstr_ratio"] = (res["auc_trained_on_gen"] - 0.5) / ex_r if abs(ex_r) > 1e-9 else float("nan")
+    a_rr = res["auc_trained_on_real"]
+    res["auc_ratio"] = res["auc_trained_on_gen"] / a_rr if a_rr > 0 else float("nan")
+    rows = {w: np.where(wte == w)[0] for w in np.unique(wte)}
+    ws = list(rows)
+    ratios = []
+    for _ in range(n_boot):
+        sel = np.concatenate([rows[ws[i]] for i in rng.integers(0, len(ws), len(ws))])
+        if len(set(yte[sel])) < 2:
+            continue
+        rr_ = auc(pr[sel], yte[sel])
+        if rr_ > 0:
+            ratios.append(auc(pg[sel], yte[sel]) / rr_)
+    res["auc_ratio_ci"] = ([float(np.percentile(ratios, 2.5)), float(np.percentile(ratios, 97.5))]
+                          if ratios else [float("nan")] * 2)
+    try:
+        from sklearn.ensemble import HistGradientBoostingClassifier
+
+        def gbm(X, y):
+            m = HistGradientBoostingClassifier(max_depth=3, max_iter=120, learning_rate=0.08, random_state=0)
+            m.fit(X, y)
+            return auc(m.predict_proba(Xte)[:, 1], yte)
+        g_rr, g_sr = gbm(Xr, yr), gbm(Xg, yg)
+        res["gbm"] = {"auc_rr": g_rr, "auc_sr": g_sr, "ratio": g_sr / g_rr if g_rr > 0 else float("nan")}
+    except ImportError:
+        res["gbm"] = {"status": "skipped (scikit-learn not installed)"}
     return res
 
 
@@ -210,8 +250,10 @@ def main(argv=None):
     ap.add_argument("--experiment", default="")
     ap.add_argument("--ticker", default="")
     ap.add_argument("--checkpoint", default="")
-    ap.add_argument("--evals", nargs="+", default=["stylized", "tstr", "tail", "regime", "position"],
-                    choices=["stylized", "tstr", "tail", "regime", "position"])
+    ALL = ["stylized", "tstr", "tail", "regime", "position", "joint", "otm", "baselines", "repro"]
+    ap.add_argument("--evals", nargs="+", default=ALL, choices=ALL)
+    ap.add_argument("--baseline", default="", help="repro: a previous diagnostics output directory")
+    ap.add_argument("--otm_h", type=int, default=100, help="otm: horizon in messages")
     ap.add_argument("--bin_width", type=int, default=25, help="position-in-window bin width (messages)")
     ap.add_argument("--cond_msgs", type=int, default=None, help="conditioning length c of the run (position eval)")
     a = ap.parse_args(argv)
@@ -236,12 +278,36 @@ def main(argv=None):
         res = run_all(mr, br, mg, bg, bin_width=a.bin_width, c=a.cond_msgs)
         for e in cond:
             results[e] = res[e]
+    from . import observational as O
+    if "joint" in a.evals:
+        results["joint"] = O.joint_canonical(mr, br, mg, bg)
+    if "otm" in a.evals:
+        results["otm"] = O.otm_observational(mr, br, mg, bg, H=a.otm_h)
+    if "baselines" in a.evals or "repro" in a.evals:
+        from .conditioned import dense_features, w1
+        fr = [dense_features(m, b) for m, b in zip(mr, br)]
+        fg = [dense_features(m, b) for m, b in zip(mg, bg)]
+        pool = lambda fs, f: np.concatenate([w[f] for w in fs]) if fs else np.zeros(0)
+        real = {f: pool(fr, f) for f in (fr[0] if fr else {})}
+        gen = {f: pool(fg, f) for f in (fg[0] if fg else {})}
+        if "baselines" in a.evals:
+            results["baselines"] = O.resampler_baseline(real, gen)
+        if "repro" in a.evals:
+            this = {f: w1(real[f], gen[f]) for f in real if f in gen}
+            base = None
+            bp = os.path.join(a.baseline, "repro.json") if a.baseline else ""
+            if bp and os.path.exists(bp):
+                with open(bp) as fh:
+                    base = {f: v["this"] for f, v in json.load(fh).get("per_feature", {}).items()}
+            res = O.reproducibility(this, base)
+            res.setdefault("per_feature", {f: {"this": v} for f, v in this.items()})
+            results["repro"] = res
     for k, v in results.items():
         with open(os.path.join(a.out, f"{k}.json"), "w") as f:
             json.dump(stamp(v, origin), f, indent=1, default=float)
-    summary = {k: (v["diff"] if k == "stylized_facts" else v) for k, v in results.items()
-               if k not in ("tail", "regime", "position")}
-    summary.update({k: "written" for k in ("tail", "regime", "position") if k in results})
+    big = ("tail", "regime", "position", "joint", "otm", "baselines", "repro")
+    summary = {k: (v["diff"] if k == "stylized_facts" else v) for k, v in results.items() if k not in big}
+    summary.update({k: "written" for k in big if k in results})
     print(json.dumps(summary, default=float))
 
 

@@ -105,7 +105,8 @@ def test_diagnostics_cli_writes_every_breakdown(tmp_path):
         shutil.copy(p, str(run / "data_gen" / os.path.basename(p).replace(".csv", "_gen_id_0.csv")))
     out = tmp_path / "diag"
     diag(["--run", str(run), "--out", str(out), "--experiment", "smoke", "--bin_width", "2", "--cond_msgs", "4"])
-    for name in ("sanity", "stylized_facts", "tstr", "tail", "regime", "position", "_provenance"):
+    for name in ("sanity", "stylized_facts", "tstr", "tail", "regime", "position", "joint", "otm", "baselines",
+                 "repro", "_provenance"):
         assert (out / f"{name}.json").exists(), name
     pos = json.load(open(out / "position.json"))
     assert pos["origin"]["experiment"] == "smoke" and pos["c"] == 4

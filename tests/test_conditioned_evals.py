@@ -82,3 +82,21 @@ def test_dense_features_basic_values():
     np.testing.assert_allclose(f["limit_bid_order_depth"][0], 0.0)
     np.testing.assert_allclose(f["limit_ask_order_depth"][1], 2.0)
     assert np.isnan(f["log_inter_arrival_time"][0]) and f["log_inter_arrival_time"][1] == pytest.approx(np.log(0.5))
+
+
+def test_observational_comparisons_on_identical_runs():
+    from sigma0_b200.eval import observational as O
+    rng = np.random.default_rng(4)
+    wins = [_window(rng, 300, d) for d in rng.normal(0, 0.3, 40)]
+    msgs, books = [w[0] for w in wins], [w[1] for w in wins]
+    j = O.joint_canonical(msgs, books, msgs, books)
+    assert j["delta_rho"] == pytest.approx(0.0) and j["closure"] == pytest.approx(1.0)
+    assert j["sliced_w2"] == pytest.approx(0.0, abs=1e-9) and j["sliced_w2_floor_real_vs_real"] > 0
+    otm = O.otm_observational(msgs, books, msgs, books, H=20)
+    assert otm["R_real"] == otm["R_gen"] and sum(v[1] for v in otm["R_real"].values()) > 0
+    r = rng.standard_normal(20000)
+    base = O.resampler_baseline({"x": r}, {"x": r + 2.0})["resampler_gap_closure"]["x"]
+    assert base["ws_model"] == pytest.approx(2.0, rel=1e-3) and base["gap_closure"] < -10
+    rep = O.reproducibility({"x": 0.1, "y": 0.2}, {"x": 0.12})
+    assert rep["per_feature"] == {"x": {"this": 0.1, "baseline": 0.12}}
+    assert O.reproducibility({"x": 0.1}, None)["status"] == "no baseline available"
