@@ -26,7 +26,7 @@ W1 is the L1 distance between the two empirical quantile functions on a common g
 """
 from __future__ import annotations
 
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import Dict, Optional, Sequence
 
 import numpy as np
 

@@ -29,7 +29,7 @@ import torch
 import torch.nn as nn
 
 from .common import Dense, LayerNorm
-from .rope import apply_rope, rotary_embedding, rope_at, sinusoidal
+from .rope import apply_rope, rotary_embedding, sinusoidal
 from ..ops.attention import attention_probsum, flash_attention, flash_attention_lse, kernel_supported
 from .transformer import FFN, causal_attention, effective_heads
 

@@ -141,3 +141,44 @@ def test_fused_tp_gemm_allreduce_matches_nccl(tmp_path):
     mp.spawn(_tp_worker, args=(2, _port(), out), nprocs=2, join=True)
     errs = torch.load(out)["errs"]
     assert max(errs) < 1e-2, errs
+
+
+def _gdn_tp_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from sigma0_b200.models.gdn import GDN
+        from sigma0_b200.parallel.tp_heads import GDNTP
+        torch.manual_seed(0)
+        full = GDN(256, num_heads=4, head_dim=64, expand_v=2).cuda()
+        x = torch.randn(2, 300, 256, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
+        res = {}
+        for fused in (False, True):
+            m = GDNTP(full, None).cuda()
+            if fused:
+                m.use_fused_out_proj(2 * 300)
+            xi = x.clone().requires_grad_(True)
+            y = m(xi)
+            y.square().mean().backward()
+            torch.cuda.synchronize()
+            if fused:
+                m.fused.check()
+            res[fused] = (y.detach().float().cpu(), xi.grad.float().cpu(), m.o_w.grad.float().cpu())
+        if rank == 0:
+            torch.save(res, out)
+    finally:
+        dist.destroy_process_group()
+
+
+@need2
+def test_gdn_tensor_parallel_fused_out_proj_matches_nccl(tmp_path):
+    """Head-parallel GDN on 2 GPUs: the fused GEMM + all-reduce output projection against
+    the GEMM + NCCL path (outputs and gradients; bf16 partials in the fused kernel)."""
+    out = str(tmp_path / "gdn_tp.pt")
+    mp.spawn(_gdn_tp_worker, args=(2, _port(), out), nprocs=2, join=True)
+    res = torch.load(out)
+    for a, b in zip(res[True], res[False]):
+        assert ((a - b).norm() / b.norm()).item() < 2e-2
