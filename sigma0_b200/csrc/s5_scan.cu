@@ -19,6 +19,7 @@ namespace s0 {
 namespace s5 {
 
 constexpr int T = 64, NT = 256;
+constexpr int U = 8;   // steps whose loads are issued together (they do not depend on the recurrence)
 
 __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
   return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
@@ -56,7 +57,14 @@ __global__ void __launch_bounds__(NT) s5_fwd_local_k(S5Args a) {
   const int t0 = c * T, t1 = min(a.L, t0 + T);
   const float2* bu = a.bu + (b * a.L) * a.P + p;
   float2 x = make_float2(0.f, 0.f);
-  for (int t = t0; t < t1; ++t) x = cfma(lam, x, bu[(long)t * a.P]);
+  for (int t = t0; t < t1; t += U) {
+    float2 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) v[u] = t + u < t1 ? bu[(long)(t + u) * a.P] : make_float2(0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (t + u < t1) x = cfma(lam, x, v[u]);
+  }
   a.part[(b * a.nchunk + c) * a.P + p] = x;
 }
 
@@ -96,9 +104,16 @@ __global__ void __launch_bounds__(NT) s5_fwd_apply_k(S5Args a) {
   const int t0 = c * T, t1 = min(a.L, t0 + T);
   const long base = (b * a.L) * a.P + p;
   float2 x = a.part[(b * a.nchunk + c) * a.P + p];
-  for (int t = t0; t < t1; ++t) {
-    x = cfma(lam, x, a.bu[base + (long)t * a.P]);
-    a.xs[base + (long)t * a.P] = x;
+  for (int t = t0; t < t1; t += U) {
+    float2 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) v[u] = t + u < t1 ? a.bu[base + (long)(t + u) * a.P] : make_float2(0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (t + u < t1) {
+        x = cfma(lam, x, v[u]);
+        a.xs[base + (long)(t + u) * a.P] = x;
+      }
   }
   if (t1 == a.L) a.xlast[b * a.P + p] = x;
 }
@@ -111,14 +126,20 @@ __global__ void __launch_bounds__(NT) s5_bwd_local_k(S5Args a) {
   const int t0 = c * T, t1 = min(a.L, t0 + T);
   const long base = (b * a.L) * a.P + p;
   float2 g = make_float2(0.f, 0.f);
-  for (int t = t1 - 1; t >= t0; --t) {
-    float2 d = a.dxs[base + (long)t * a.P];
-    if (t == a.L - 1 && a.dxlast) {
-      const float2 e = a.dxlast[b * a.P + p];
-      d.x += e.x;
-      d.y += e.y;
-    }
-    g = cfma(lc, g, d);
+  const float2 e = (t1 == a.L && a.dxlast) ? a.dxlast[b * a.P + p] : make_float2(0.f, 0.f);
+  for (int t = t1 - 1; t >= t0; t -= U) {
+    float2 d[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) d[u] = t - u >= t0 ? a.dxs[base + (long)(t - u) * a.P] : make_float2(0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (t - u >= t0) {
+        if (t - u == a.L - 1) {
+          d[u].x += e.x;
+          d[u].y += e.y;
+        }
+        g = cfma(lc, g, d[u]);
+      }
   }
   a.part[(b * a.nchunk + c) * a.P + p] = g;
 }
@@ -132,17 +153,29 @@ __global__ void __launch_bounds__(NT) s5_bwd_apply_k(S5Args a) {
   const long base = (b * a.L) * a.P + p;
   float2 g = a.part[(b * a.nchunk + c) * a.P + p];
   float2 dl = make_float2(0.f, 0.f);
-  for (int t = t1 - 1; t >= t0; --t) {
-    float2 d = a.dxs[base + (long)t * a.P];
-    if (t == a.L - 1 && a.dxlast) {
-      const float2 e = a.dxlast[b * a.P + p];
-      d.x += e.x;
-      d.y += e.y;
+  const float2 e = (t1 == a.L && a.dxlast) ? a.dxlast[b * a.P + p] : make_float2(0.f, 0.f);
+  const float2 x0 = a.x0 ? a.x0[b * a.P + p] : make_float2(0.f, 0.f);
+  for (int t = t1 - 1; t >= t0; t -= U) {
+    float2 d[U], xp[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int tt = t - u;
+      d[u] = tt >= t0 ? a.dxs[base + (long)tt * a.P] : make_float2(0.f, 0.f);
+      xp[u] = tt >= t0 && tt > 0 ? a.xs[base + (long)(tt - 1) * a.P] : x0;
     }
-    g = cfma(lc, g, d);
-    a.dbu[base + (long)t * a.P] = g;
-    const float2 xp = t > 0 ? a.xs[base + (long)(t - 1) * a.P] : (a.x0 ? a.x0[b * a.P + p] : make_float2(0.f, 0.f));
-    dl = cfma(g, cconj(xp), dl);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int tt = t - u;
+      if (tt >= t0) {
+        if (tt == a.L - 1) {
+          d[u].x += e.x;
+          d[u].y += e.y;
+        }
+        g = cfma(lc, g, d[u]);
+        a.dbu[base + (long)tt * a.P] = g;
+        dl = cfma(g, cconj(xp[u]), dl);
+      }
+    }
   }
   atomicAdd(&a.dlam[p].x, dl.x);
   atomicAdd(&a.dlam[p].y, dl.y);
