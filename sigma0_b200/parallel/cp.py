@@ -102,12 +102,14 @@ class Mamba3CP(nn.Module):
 
 
 def shard_model_cp(model: nn.Module, group=None) -> nn.Module:
-    """Wrap every ``Mamba3`` mixer of ``model`` for context parallelism."""
+    """Wrap every ``Mamba3`` mixer and every transformer / NSA block of ``model`` for
+    context parallelism (the hybrid backbones mix both)."""
+    from .cp_attention import context_parallel_attention
     for _, mod in list(model.named_modules()):
         for cname, child in list(mod.named_children()):
             if isinstance(child, Mamba3):
                 setattr(mod, cname, Mamba3CP(child, group))
-    return model
+    return context_parallel_attention(model, group)
 
 
 def split_sequence(x: torch.Tensor, group=None, dim: int = 1) -> torch.Tensor:

@@ -78,3 +78,15 @@ def test_context_parallel_attention_matches_full(kind, tmp_path):
             # (a key bias shifts every score of a row equally and cancels in the softmax)
             err = (res[0]["grads"][n] - p.grad).norm().item()
             assert err <= 5e-5 * p.grad.norm().item() + 1e-5, (kind, n, err)
+
+
+def test_shard_model_cp_wraps_mamba3_and_attention_blocks():
+    from sigma0_b200.models.mamba3 import Mamba3
+    from sigma0_b200.models.nsa import NSABlock
+    from sigma0_b200.models.transformer import TransformerBlock
+    from sigma0_b200.parallel.cp import Mamba3CP, shard_model_cp
+    from sigma0_b200.parallel.cp_attention import NSABlockCP, TransformerBlockCP
+    m = torch.nn.Sequential(Mamba3(64, d_state=16, headdim=16, chunk_size=16), TransformerBlock(64, n_heads=4),
+                            NSABlock(64, n_heads=4, block_size=8, select_block=16))
+    shard_model_cp(m)
+    assert [type(c) for c in m] == [Mamba3CP, TransformerBlockCP, NSABlockCP]
