@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "launchers.h"
+#include "tma_host.h"
 #include "tc_common.cuh"
 
 namespace s0 {
@@ -302,7 +303,9 @@ static int encode(CUtensorMap* m, const void* ptr, int B, int L, int nh, int HD,
   const cuuint64_t strides[3] = {(cuuint64_t)sh * 2, (cuuint64_t)sl * 2, (cuuint64_t)sb * 2};
   const cuuint32_t box[4] = {64, 1, 128, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
-  return cuTensorMapEncodeTiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box,
+  const auto enc = s0::tensor_map_encoder();
+  if (!enc) return -4;
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box,
                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
              ? 0

@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "launchers.h"
+#include "tma_host.h"
 #include "tc_common.cuh"
 
 namespace cg = cooperative_groups;
@@ -340,7 +341,9 @@ int launch_bn(const TpfArgs& a, int sms, cudaStream_t st) {
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
     const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    return cuTensorMapEncodeTiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+    const auto enc = s0::tensor_map_encoder();
+    if (!enc) return CUDA_ERROR_NOT_FOUND;
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
                                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   };
