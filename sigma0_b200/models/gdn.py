@@ -132,12 +132,28 @@ def _scan_kernel_ok(q, v, chunk) -> bool:
     return q.is_cuda and chunk == 64 and q.shape[-1] in (64, 128) and v.shape[-1] % 64 == 0
 
 
-def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None, use_kernel=None):
+def chunk_transitions_product(M: torch.Tensor) -> torch.Tensor:
+    """M (B, nc, nh, d, d) -> M_0 M_1 ... M_{nc-1} (B, nh, d, d) by a log-depth pairwise
+    product (the order of the factors is kept)."""
+    while M.shape[1] > 1:
+        if M.shape[1] % 2:
+            eye = torch.eye(M.shape[-1], dtype=M.dtype, device=M.device).expand(M.shape[0], 1, *M.shape[2:])
+            M = torch.cat([M, eye], 1)
+        M = M[:, 0::2] @ M[:, 1::2]
+    return M[:, 0]
+
+
+def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None, use_kernel=None, return_transition=False):
     """q,k (B,L,nh,hd); v (B,L,nh,hvd); beta (B,L,nh); alog (B,L,nh,hd or 1).
 
     Returns o (B,L,nh,hvd) and the final state (B,nh,hvd,hd).  On CUDA (chunk 64, key
     head dim 64 / 128, value head dim a multiple of 64) the cross-chunk scan runs the
     ``gdn_scan`` kernels; ``use_kernel=False`` keeps the host loop (the oracle).
+
+    ``return_transition=True`` also returns the sequence's state transition T (B, nh, hd,
+    hd): the final state is S0 T plus the final state from a zero start, since every chunk
+    maps S -> S (diag(tot) - kc^T kd) + vc^T kd (context parallelism composes segments
+    with it).
     """
     B, L, nh, hd = q.shape
     hvd = v.shape[-1]
@@ -176,13 +192,18 @@ def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None, use_kernel=None)
     kcd = torch.linalg.solve_triangular(A, kb * torch.exp(G), upper=False)    # (B,nc,nh,C,hd)
     dec_end = torch.exp(G[..., -1:, :] - G)                                     # (B,nc,nh,C,d|1)
     kdec = k * dec_end
+    trans = None
+    if return_transition:
+        totd = torch.exp(G[..., -1, :]).expand(B, nc, nh, hd)
+        Mc = torch.diag_embed(totd) - kcd.transpose(-1, -2) @ kdec                  # (B,nc,nh,hd,hd)
+        trans = chunk_transitions_product(Mc)
     if use_kernel:
         P = lambda t: t.transpose(1, 2)                                         # -> (B,nh,nc,...)
         tot = P(torch.exp(G[..., -1, :])).expand(B, nh, nc, hd)
         o, S = _GDNScan.apply(P(q * torch.exp(G)), P(kcd), P(kdec), P(intra), P(vc), tot,
                               None if S0 is None else S0.float())
         o = P(o).transpose(2, 3).reshape(B, nc * C, nh, hvd)[:, :L]
-        return o, S
+        return (o, S, trans) if return_transition else (o, S)
     S = torch.zeros(B, nh, hvd, hd, device=q.device) if S0 is None else S0.float()
     outs = []
     for c in range(nc):
@@ -193,7 +214,7 @@ def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None, use_kernel=None)
         tot = torch.exp(G[:, c, :, -1, :])                                      # (B,nh,d|1)
         S = S * tot[:, :, None, :] + vnew.transpose(-1, -2) @ kdec[:, c]
     o = torch.stack(outs, 1).transpose(2, 3).reshape(B, nc * C, nh, hvd)[:, :L]
-    return o, S
+    return (o, S, trans) if return_transition else (o, S)
 
 
 def gated_delta_recurrent(q, k, v, beta, alog, S=None):

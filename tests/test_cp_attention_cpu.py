@@ -86,7 +86,9 @@ def test_shard_model_cp_wraps_mamba3_and_attention_blocks():
     from sigma0_b200.models.transformer import TransformerBlock
     from sigma0_b200.parallel.cp import Mamba3CP, shard_model_cp
     from sigma0_b200.parallel.cp_attention import NSABlockCP, TransformerBlockCP
+    from sigma0_b200.models.gdn import GDN
+    from sigma0_b200.parallel.cp_gdn import GDNCP
     m = torch.nn.Sequential(Mamba3(64, d_state=16, headdim=16, chunk_size=16), TransformerBlock(64, n_heads=4),
-                            NSABlock(64, n_heads=4, block_size=8, select_block=16))
+                            NSABlock(64, n_heads=4, block_size=8, select_block=16), GDN(64, num_heads=4, head_dim=16))
     shard_model_cp(m)
-    assert [type(c) for c in m] == [Mamba3CP, TransformerBlockCP, NSABlockCP]
+    assert [type(c) for c in m] == [Mamba3CP, TransformerBlockCP, NSABlockCP, GDNCP]
