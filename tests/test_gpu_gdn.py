@@ -72,3 +72,14 @@ def test_kda_intra_kernel_matches_einsum():
     ((I2 * wI).sum() + (L2 * wL).sum()).backward()
     for name, a, b in zip(("q", "k", "kb", "G"), (q, k, kb, G), xs):
         assert _rel(a.grad, b.grad) < 1e-4, (name, _rel(a.grad, b.grad))
+
+
+def test_segment_transition_with_the_scan_kernels():
+    """The final state from an initial state S0 equals S0 T + the final state from zero
+    (the identity context parallelism composes segments with), with the CUDA scans."""
+    from sigma0_b200.models.gdn import gated_delta_chunked
+    for kda in (False, True):
+        q, k, v, beta, alog, S0 = (t.detach() for t in _inputs(1, 200, 2, 128, 128, kda, 7))
+        _, S_zero, T = gated_delta_chunked(q, k, v, beta, alog, 64, use_kernel=True, return_transition=True)
+        _, S_full = gated_delta_chunked(q, k, v, beta, alog, 64, S0=S0, use_kernel=True)
+        assert _rel(S_full, S0 @ T + S_zero) < 2e-2
