@@ -1,5 +1,5 @@
-"""Tensor parallelism (heads split over a tensor-parallel group) for the GDN / KDA mixer and
-the transformer block.
+"""Tensor parallelism (heads split over a tensor-parallel group) for the GDN / KDA mixer, the
+transformer block and the NSA block.
 
 The reference shards these over its ``tp`` mesh axis: the projections that produce a head's
 inputs are column-parallel, the projection that consumes the heads' outputs is
@@ -14,8 +14,8 @@ row-parallel and followed by a psum (``src/base_model/models/gdn.py:87-243``,
 * a replicated parameter that only sees this rank's heads (GDN's per-head RMSNorm scale)
   enters through ``copy_to_tp`` too, so its gradient is summed over the group.
 
-``shard_heads(model, group)`` replaces every ``GDN`` mixer and every ``TransformerBlock``
-of a model in place with its slice.
+``shard_heads(model, group)`` replaces every ``GDN`` mixer, ``TransformerBlock`` and
+``NSABlock`` of a model in place with its slice.
 """
 from __future__ import annotations
 
@@ -27,7 +27,8 @@ import torch.nn.functional as F
 
 from ..models.common import gelu_tanh
 from ..models.gdn import GDN, gated_delta_chunked, gated_delta_recurrent, l2_normalize
-from ..models.rope import sinusoidal
+from ..models.nsa import NSABlock
+from ..models.rope import apply_rope, rotary_embedding, sinusoidal
 from ..models.transformer import TransformerBlock, causal_attention
 from .tp import copy_to_tp, reduce_from_tp
 
@@ -203,12 +204,80 @@ class TransformerBlockTP(nn.Module, _RowParallel):
         return x + (reduce_from_tp(f @ self.w2.to(cd), self.group) + self.b2.to(cd)).float()
 
 
+class NSABlockTP(nn.Module, _RowParallel):
+    """NSA heads and FFN width split over the group.  The three branches are per head,
+    except the block selection: it ranks blocks by importance summed over all heads, so each
+    rank's per-head sum is summed over the group before the top-k (the current block's
+    importance and the masked entries are then reset to their constants, as in the
+    single-device block), and every rank selects the same blocks."""
+    is_transformer = True
+
+    def __init__(self, full: NSABlock, group=None):
+        super().__init__()
+        # the full block lends its branch methods and configuration; it is not registered as
+        # a submodule, so its unsliced weights stay out of this module's parameters
+        self.__dict__["inner"] = full
+        self.group = group
+        T, r = dist.get_world_size(group), dist.get_rank(group)
+        self.nhl, self.h0 = _split(T, r, full.nh, "NSA heads")
+        self.fl, self.f0 = _split(T, r, full.ff.layers_0.kernel.shape[1], "FFN columns")
+        nhl, h0, hd = self.nhl, self.h0, full.hd
+        self.wq = _cols(full.q_proj.kernel, h0, nhl, hd)
+        self.wk = _cols(full.k_proj.kernel, h0, nhl, hd)
+        self.wv = _cols(full.v_proj.kernel, h0, nhl, hd)
+        self.wg = _cols(full.g_proj.kernel, h0, nhl, 3)
+        self.wo = _cols(full.o_proj.kernel, h0, nhl, hd, dim=0)                        # row-parallel
+        self.w1, self.b1 = _cols(full.ff.layers_0.kernel, self.f0, self.fl, 1), _cols(full.ff.layers_0.bias, self.f0,
+                                                                                     self.fl, 1)
+        self.w2 = _cols(full.ff.layers_2.kernel, self.f0, self.fl, 1, dim=0)
+        self.b2 = nn.Parameter(full.ff.layers_2.bias.detach().clone())
+        self.norm1, self.norm2 = full.norm1, full.norm2                                # replicated
+
+    def _out_weight(self):
+        return self.wo
+
+    def forward(self, x):
+        m, grp = self.inner, self.group
+        B, L, H = x.shape
+        cd = m.compute_dtype
+        if m.pe != "rope":
+            x = x + sinusoidal(L, H, x.device)
+        h = copy_to_tp(self.norm1(x), grp).to(cd)
+        q = (h @ self.wq.to(cd)).reshape(B, L, self.nhl, m.hd)
+        k = (h @ self.wk.to(cd)).reshape(B, L, self.nhl, m.hd)
+        v = (h @ self.wv.to(cd)).reshape(B, L, self.nhl, m.hd)
+        if m.pe == "rope":
+            cos, sin = rotary_embedding(m.hd, L, m.rope_base, x.device)
+            q, k = apply_rope(q, k, cos, sin)
+        g = torch.sigmoid((h @ self.wg.to(cd)).float()).reshape(B, L, self.nhl, 3)
+        scale = m.hd ** -0.5
+        o_cmp, imp = m._compressed(q, k, v, scale)
+        with torch.no_grad():                                  # selection only: no gradient
+            imp = imp.detach().clone()
+            dist.all_reduce(imp, group=grp)
+            BS, nb = m.block_size, imp.shape[-1]
+            t = torch.arange(L, device=x.device)
+            cmask = torch.arange(nb, device=x.device)[None, :] < torch.clamp((t - BS + 1) // BS + 1, min=0)[:, None]
+            cur = (t // BS)[:, None] == torch.arange(nb, device=x.device)[None, :]
+            imp = torch.where(cur[None], torch.ones_like(imp), imp).masked_fill(~cmask[None], -1e9)
+        o_slc = m._select(q, k, v, imp, scale)
+        o_win = causal_attention(q, k, v, scale=scale, window=m.window)
+        o = g[..., 0:1] * o_cmp.float() + g[..., 1:2] * o_slc.float() + g[..., 2:3] * o_win.float()
+        x = x + self._reduce(o.reshape(B, L, -1).to(cd), self.wo.to(cd), grp).float()
+        h2 = copy_to_tp(self.norm2(x), grp).to(cd)
+        f = gelu_tanh(h2 @ self.w1.to(cd) + self.b1.to(cd))
+        return x + (reduce_from_tp(f @ self.w2.to(cd), grp) + self.b2.to(cd)).float()
+
+
 def shard_heads(model: nn.Module, group=None) -> nn.Module:
-    """Replace every ``GDN`` mixer and ``TransformerBlock`` of a model by its slice."""
+    """Replace every ``GDN`` mixer, ``TransformerBlock`` and ``NSABlock`` of a model by its
+    slice."""
     for _, mod in list(model.named_modules()):
         for cname, child in list(mod.named_children()):
             if isinstance(child, GDN):
                 setattr(mod, cname, GDNTP(child, group))
+            elif isinstance(child, NSABlock):
+                setattr(mod, cname, NSABlockTP(child, group))
             elif isinstance(child, TransformerBlock):
                 setattr(mod, cname, TransformerBlockTP(child, group))
     return model
