@@ -37,7 +37,10 @@ import torch
 
 
 def flax_path(name: str) -> str:
-    return "params/" + name.replace(".", "/")
+    """Torch parameter name -> Flax parameter path.  The context-parallel wrappers hold the
+    block they wrap as ``inner``; that segment is dropped so a wrapped model saves and loads
+    under the same paths as the plain one."""
+    return "params/" + "/".join(p for p in name.split(".") if p != "inner")
 
 
 def _sha256(path: str) -> str:

@@ -81,3 +81,23 @@ def test_export_npz_uses_flax_paths(tmp_path):
 
 def test_remap_step():
     assert remap_step(100, 64, 32) == 200 and remap_step(100, 64, 64) == 100 and remap_step(7, 4, 8) == 3
+
+
+def test_context_parallel_wrappers_keep_parameter_paths():
+    """Wrapping blocks for context parallelism does not change the checkpoint paths."""
+    import torch
+    from sigma0_b200.ckpt.checkpoint import flax_path
+    from sigma0_b200.models.gdn import GDN
+    from sigma0_b200.models.mamba3 import Mamba3
+    from sigma0_b200.models.nsa import NSABlock
+    from sigma0_b200.models.transformer import TransformerBlock
+    from sigma0_b200.parallel.cp import shard_model_cp
+
+    def build():
+        torch.manual_seed(0)
+        return torch.nn.Sequential(Mamba3(64, d_state=16, headdim=16, chunk_size=16), TransformerBlock(64, n_heads=4),
+                                   NSABlock(64, n_heads=4, block_size=8, select_block=16),
+                                   GDN(64, num_heads=4, head_dim=16))
+    plain = [flax_path(n) for n, _ in build().named_parameters()]
+    wrapped = [flax_path(n) for n, _ in shard_model_cp(build()).named_parameters()]
+    assert plain == wrapped
