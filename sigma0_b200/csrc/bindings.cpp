@@ -562,6 +562,29 @@ void gdn_scan_bwd(at::Tensor qe, at::Tensor kc, at::Tensor kd, at::Tensor intra,
   TORCH_CHECK(rc == 0, "gdn_scan_bwd launch failed (", rc, ")");
 }
 
+// ---- gated delta rule decode step ------------------------------------------------------------
+void gdn_decode(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor beta, at::Tensor alog, at::Tensor S,
+                at::Tensor o) {
+  c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(q.dim() == 4 && v.dim() == 4, "q [B, T, nh, hd], v [B, T, nh, hvd]");
+  const int64_t B = q.size(0), T = q.size(1), nh = q.size(2), hd = q.size(3), hvd = v.size(3);
+  TORCH_CHECK(hd == 64 || hd == 128, "key head dim must be 64 or 128");
+  const int64_t ad = alog.size(-1);
+  TORCH_CHECK(ad == 1 || ad == hd, "alog: one decay per head or per key dim");
+  gdn_req(q, at::kFloat, "q", {B, T, nh, hd});
+  gdn_req(k, at::kFloat, "k", {B, T, nh, hd});
+  gdn_req(v, at::kFloat, "v", {B, T, nh, hvd});
+  gdn_req(beta, at::kFloat, "beta", {B, T, nh});
+  gdn_req(alog, at::kFloat, "alog", {B, T, nh, ad});
+  gdn_req(S, at::kFloat, "S", {B, nh, hvd, hd});
+  gdn_req(o, at::kFloat, "o", {B, T, nh, hvd});
+  GdnDecodeArgs a{q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(), beta.data_ptr<float>(),
+                  alog.data_ptr<float>(), S.data_ptr<float>(), o.data_ptr<float>(),
+                  (int)B, (int)T, (int)nh, (int)hvd, (int)ad};
+  const int rc = gdn_decode_launch(a, (int)hd, stream());
+  TORCH_CHECK(rc == 0, "gdn_decode launch failed (", rc, ")");
+}
+
 // ---- per-key-dim-decay intra-chunk matrices -------------------------------------------------
 static KdaArgs kda_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& kb, const at::Tensor& G) {
   TORCH_CHECK(q.dim() == 3 && q.size(1) == 64 && q.size(2) % 32 == 0, "q [N, 64, HD] with HD a multiple of 32");
@@ -897,6 +920,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "value rows per CTA of the reverse scan (the leading dimension of its partials is HVD / this)");
   m.def("gdn_scan_bwd", &gdn_scan_bwd,
         "reverse scan: per value-block partial gradients of qe / kc / kd / intra / tot, dvc and dS0");
+  m.def("gdn_decode", &gdn_decode, "gated delta rule recurrent step over T tokens (state updated in place)");
   m.def("kda_intra_fwd", &kda_intra_fwd, "per-key-dim-decay intra-chunk score and WY matrices of 64-step chunks");
   m.def("kda_intra_bwd", &kda_intra_bwd, "gradients of q, k, kb and the cumulative log decay G");
   m.def("s5_scan_fwd", &s5_scan_fwd, "S5 complex diagonal recurrence: all states and the final one");

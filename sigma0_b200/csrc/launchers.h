@@ -242,3 +242,15 @@ struct S5Args {
   int L, P, nchunk;
 };
 int s5_scan_launch(const S5Args& a, bool bwd, cudaStream_t st);
+
+// recurrent decode step of the gated delta rule (gdn_decode.cu); fp32, contiguous
+struct GdnDecodeArgs {
+  const float *q, *k;                 // [B, T, nh, HD]
+  const float* v;                     // [B, T, nh, hvd]
+  const float* beta;                  // [B, T, nh]
+  const float* alog;                  // [B, T, nh, alog_dim]  (alog_dim 1: per head, HD: per key dim)
+  float* S;                           // [B, nh, hvd, HD] updated in place
+  float* o;                           // [B, T, nh, hvd]
+  int B, T, nh, hvd, alog_dim;
+};
+int gdn_decode_launch(const GdnDecodeArgs& a, int hd, cudaStream_t st);

@@ -217,9 +217,24 @@ def gated_delta_chunked(q, k, v, beta, alog, chunk=64, S0=None, use_kernel=None,
     return (o, S, trans) if return_transition else (o, S)
 
 
-def gated_delta_recurrent(q, k, v, beta, alog, S=None):
+def gated_delta_recurrent(q, k, v, beta, alog, S=None, use_kernel=None):
+    """Token-by-token recurrence: o (B,L,nh,hvd) and the new state (B,nh,hvd,hd).  On CUDA,
+    head dim 64 / 128, when no gradient is needed (decode) it runs the ``gdn_decode`` kernel
+    (``csrc/gdn_decode.cu``: one warp per state row, the state read and written once);
+    ``use_kernel=False`` keeps the loop below (the oracle)."""
     B, L, nh, hd = q.shape
     hvd = v.shape[-1]
+    if use_kernel is None:
+        needs_grad = torch.is_grad_enabled() and any(t is not None and t.requires_grad
+                                                     for t in (q, k, v, beta, alog, S))
+        use_kernel = q.is_cuda and hd in (64, 128) and not needs_grad
+    if use_kernel:
+        from ..ops._ext import ext
+        c = lambda t: t.detach().float().contiguous()
+        St = torch.zeros(B, nh, hvd, hd, device=q.device) if S is None else S.detach().float().clone().contiguous()
+        o = torch.empty(B, L, nh, hvd, device=q.device)
+        ext().gdn_decode(c(q), c(k), c(v), c(beta), c(alog), St, o)
+        return o, St
     S = torch.zeros(B, nh, hvd, hd, device=q.device) if S is None else S.float()
     outs = []
     for t in range(L):

@@ -83,3 +83,33 @@ def test_segment_transition_with_the_scan_kernels():
         _, S_zero, T = gated_delta_chunked(q, k, v, beta, alog, 64, use_kernel=True, return_transition=True)
         _, S_full = gated_delta_chunked(q, k, v, beta, alog, 64, S0=S0, use_kernel=True)
         assert _rel(S_full, S0 @ T + S_zero) < 2e-2
+
+
+@pytest.mark.parametrize("kda,hd,T", [(False, 128, 1), (True, 64, 5), (False, 64, 3)])
+def test_decode_kernel_matches_recurrence(kda, hd, T):
+    """The gdn_decode kernel against the token loop: outputs and the updated state, from a
+    non-zero state, over several tokens per call."""
+    from sigma0_b200.models.gdn import gated_delta_recurrent
+    q, k, v, beta, alog, S0 = (t.detach() for t in _inputs(3, T, 4, hd, 2 * hd, kda, T + hd))
+    o1, S1 = gated_delta_recurrent(q, k, v, beta, alog, S0, use_kernel=True)
+    o2, S2 = gated_delta_recurrent(q, k, v, beta, alog, S0, use_kernel=False)
+    assert _rel(o1, o2) < 1e-4 and _rel(S1, S2) < 1e-4
+    assert not torch.equal(S0, S1)                 # the input state is left untouched, a new one returned
+
+
+@pytest.mark.parametrize("kda", [False, True])
+def test_gdn_module_step_matches_forward(kda):
+    """Stepping a GDN / KDA mixer token by token on CUDA (decode kernel, convolution buffers)
+    reproduces its full-sequence forward."""
+    from sigma0_b200.models.gdn import GDN
+    torch.manual_seed(0)
+    m = GDN(256, num_heads=4, head_dim=64, use_kda=kda).cuda()
+    x = torch.randn(2, 70, 256, device="cuda")
+    with torch.no_grad():
+        full = m(x)
+        st = m.initial_state(2, "cuda")
+        outs = []
+        for t in range(70):
+            st, y = m.step(st, x[:, t:t + 1])
+            outs.append(y)
+    assert _rel(torch.cat(outs, 1), full) < 2e-2
