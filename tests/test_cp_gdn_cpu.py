@@ -22,10 +22,10 @@ def _rel(a, b):
     return ((a - b).norm() / (b.norm() + 1e-12)).item()
 
 
-def _mixer(kda):
+def _mixer(kda, conv=True):
     from sigma0_b200.models.gdn import GDN
     torch.manual_seed(0)
-    m = GDN(64, num_heads=4, head_dim=16, expand_v=2, chunk_size=16, use_kda=kda)
+    m = GDN(64, num_heads=4, head_dim=16, expand_v=2, chunk_size=16, use_kda=kda, use_conv=conv)
     with torch.no_grad():
         m.out_norm.scale.normal_(1.0, 0.3)
         m.gk_proj.bias.fill_(2.0)
@@ -37,14 +37,14 @@ def _data(L):
     return torch.randn(2, L, 64, generator=g), torch.randn(2, L, 64, generator=g)
 
 
-def _worker(rank, world, port, kda, L, out):
+def _worker(rank, world, port, kda, L, out, conv=True):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=120))
     try:
         torch.set_num_threads(1)
         from sigma0_b200.parallel.cp import split_sequence
         from sigma0_b200.parallel.cp_gdn import GDNCP
-        full = _mixer(kda)
+        full = _mixer(kda, conv)
         m = GDNCP(full)
         x, gout = _data(L)
         xs = split_sequence(x).clone().requires_grad_(True)
@@ -73,15 +73,16 @@ def test_segment_transition_identity():
         assert _rel(S_full, S0 @ T + S_zero) < 1e-6
 
 
-@pytest.mark.parametrize("kda,world,L", [(False, 2, 80), (True, 2, 80), (False, 3, 90)])
-def test_context_parallel_gdn_matches_full(kda, world, L, tmp_path):
-    full = _mixer(kda)
+@pytest.mark.parametrize("kda,world,L,conv", [(False, 2, 80, True), (True, 2, 80, True), (False, 3, 90, True),
+                                             (True, 2, 64, False)])
+def test_context_parallel_gdn_matches_full(kda, world, L, conv, tmp_path):
+    full = _mixer(kda, conv)
     x, gout = _data(L)
     x.requires_grad_(True)
     y = full(x)
     (y * gout).sum().backward()
     out = str(tmp_path / "r")
-    mp.spawn(_worker, args=(world, _port(), kda, L, out), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _port(), kda, L, out, conv), nprocs=world, join=True)
     res = [torch.load(f"{out}.{r}") for r in range(world)]
     Ls = L // world
     for r, part in enumerate(res):
