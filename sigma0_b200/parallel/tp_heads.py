@@ -45,9 +45,30 @@ def _split(world: int, rank: int, heads: int, what: str):
 
 
 class _RowParallel:
-    """The row-parallel output: NCCL all-reduce, or the fused kernel once enabled."""
+    """The row-parallel output: NCCL all-reduce, or the fused kernel once enabled; and the
+    consolidated state of the single-device block (``full_state_dict``)."""
 
     fused = None
+    # (this module's parameter, the single-device block's parameter, split dim or None)
+    _FULL: tuple = ()
+
+    def full_state_dict(self) -> dict:
+        """The single-device block's parameters, by its names, from every rank's slices (an
+        all-gather along each split dimension; replicated parameters as they are).  Every
+        rank of the group must call it."""
+        own = dict(self.named_parameters())
+        out = {}
+        for local, full, dim in self._full_table():
+            t = own[local].detach()
+            if dim is not None:
+                parts = [torch.empty_like(t) for _ in range(dist.get_world_size(self.group))]
+                dist.all_gather(parts, t.contiguous(), group=self.group)
+                t = torch.cat(parts, dim)
+            out[full] = t
+        return out
+
+    def _full_table(self) -> tuple:
+        return self._FULL
 
     def _reduce(self, y: torch.Tensor, w: torch.Tensor, group) -> torch.Tensor:
         if self.fused is not None and y.is_cuda:
@@ -102,6 +123,16 @@ class GDNTP(nn.Module, _RowParallel):
         self.out_norm_eps = full.out_norm.eps
         self.o_w = _cols(full.o_proj.kernel, h0, nhl, hvd, dim=0)                  # row-parallel
         self.D = nn.Parameter(full.D.detach().clone())                              # replicated
+
+    _FULL = (("q_w", "q_proj.kernel", -1), ("k_w", "k_proj.kernel", -1), ("v_w", "v_proj.kernel", -1),
+             ("g_w", "g_proj.kernel", -1), ("b_w", "b_proj.kernel", -1), ("b_b", "b_proj.bias", 0),
+             ("gk_w", "gk_proj.kernel", -1), ("gk_b", "gk_proj.bias", 0), ("o_w", "o_proj.kernel", 0),
+             ("out_norm_scale", "out_norm.scale", None), ("D", "D", None))
+    _FULL_CONV = (("qc_w", "q_conv.kernel", -1), ("qc_b", "q_conv.bias", 0), ("kc_w", "k_conv.kernel", -1),
+                  ("kc_b", "k_conv.bias", 0), ("vc_w", "v_conv.kernel", -1), ("vc_b", "v_conv.bias", 0))
+
+    def _full_table(self) -> tuple:
+        return self._FULL + (self._FULL_CONV if self.use_conv else ())
 
     def _out_weight(self):
         return self.o_w
@@ -186,6 +217,18 @@ class TransformerBlockTP(nn.Module, _RowParallel):
         self.w2 = _cols(full.ff.layers_2.kernel, self.f0, self.fl, 1, dim=0)
         self.b2 = nn.Parameter(full.ff.layers_2.bias.detach().clone())
 
+    _FULL = (("wq", "attn.query.kernel", 1), ("bq", "attn.query.bias", 0), ("wk", "attn.key.kernel", 1),
+             ("bk", "attn.key.bias", 0), ("wv", "attn.value.kernel", 1), ("bv", "attn.value.bias", 0),
+             ("wo", "attn.out.kernel", 0), ("bo", "attn.out.bias", None), ("norm1.scale", "norm1.scale", None),
+             ("norm1.bias", "norm1.bias", None), ("norm2.scale", "norm2.scale", None), ("norm2.bias", "norm2.bias", None),
+             ("w1", "ff.layers_0.kernel", -1), ("b1", "ff.layers_0.bias", 0), ("w2", "ff.layers_2.kernel", 0),
+             ("b2", "ff.layers_2.bias", None))
+
+    def full_state_dict(self) -> dict:
+        out = super().full_state_dict()
+        out["attn.out.kernel"] = out["attn.out.kernel"].reshape(-1, self.hd, self.H)     # (nh, hd, H)
+        return out
+
     def _out_weight(self):
         return self.wo
 
@@ -232,6 +275,12 @@ class NSABlockTP(nn.Module, _RowParallel):
         self.w2 = _cols(full.ff.layers_2.kernel, self.f0, self.fl, 1, dim=0)
         self.b2 = nn.Parameter(full.ff.layers_2.bias.detach().clone())
         self.norm1, self.norm2 = full.norm1, full.norm2                                # replicated
+
+    _FULL = (("wq", "q_proj.kernel", -1), ("wk", "k_proj.kernel", -1), ("wv", "v_proj.kernel", -1),
+             ("wg", "g_proj.kernel", -1), ("wo", "o_proj.kernel", 0), ("norm1.scale", "norm1.scale", None),
+             ("norm1.bias", "norm1.bias", None), ("norm2.scale", "norm2.scale", None), ("norm2.bias", "norm2.bias", None),
+             ("w1", "ff.layers_0.kernel", -1), ("b1", "ff.layers_0.bias", 0), ("w2", "ff.layers_2.kernel", 0),
+             ("b2", "ff.layers_2.bias", None))
 
     def _out_weight(self):
         return self.wo

@@ -1,6 +1,7 @@
 """Head-parallel GDN / KDA mixer and transformer block on CPU ranks (gloo, world 2)
 against the single-process modules: outputs, input gradients, and the gradient of every
-parameter slice (replicated parameters receive the full gradient on every rank)."""
+parameter slice (replicated parameters receive the full gradient on every rank), and the
+consolidated state (``full_state_dict``) against the single-device block's parameters."""
 import os
 import socket
 
@@ -61,7 +62,7 @@ def _worker(rank, world, port, kind, out):
         u.requires_grad_(True)
         y = m(u)
         (y * gout).sum().backward()
-        torch.save({"y": y.detach(), "du": u.grad, "grads": {n: p.grad for n, p in m.named_parameters()},
+        torch.save({"y": y.detach(), "du": u.grad, "full_sd": m.full_state_dict(), "grads": {n: p.grad for n, p in m.named_parameters()},
                     "h0": m.h0, "nhl": m.nhl, "f0": getattr(m, "f0", 0), "fl": getattr(m, "fl", 0)},
                    f"{out}.{rank}")
     finally:
@@ -105,3 +106,8 @@ def test_head_parallel_matches_full(kind, tmp_path):
         for name, ref in checks:
             err = (g[name] - ref).norm().item()
             assert err <= 5e-5 * ref.norm().item() + 1e-6, (kind, name, err)
+        # consolidation: every rank rebuilds the single-device block's parameters exactly
+        sd = {n: p.detach() for n, p in full.named_parameters()}
+        assert set(r["full_sd"]) == set(sd), (kind, set(sd) ^ set(r["full_sd"]))
+        for name, ref in sd.items():
+            assert r["full_sd"][name].shape == ref.shape and torch.equal(r["full_sd"][name], ref), (kind, name)
