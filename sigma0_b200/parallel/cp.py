@@ -102,15 +102,16 @@ class Mamba3CP(nn.Module):
 
 
 def shard_model_cp(model: nn.Module, group=None) -> nn.Module:
-    """Wrap every ``Mamba3`` mixer, ``GDN`` mixer and transformer / NSA block of ``model``
-    for context parallelism (the hybrid backbones mix them)."""
+    """Wrap every ``Mamba3`` mixer, ``GDN`` mixer, ``S5`` layer and transformer / NSA block
+    of ``model`` for context parallelism (the hybrid backbones mix them)."""
     from .cp_attention import context_parallel_attention
     from .cp_gdn import shard_gdn_cp
+    from .cp_s5 import shard_s5_cp
     for _, mod in list(model.named_modules()):
         for cname, child in list(mod.named_children()):
             if isinstance(child, Mamba3):
                 setattr(mod, cname, Mamba3CP(child, group))
-    return context_parallel_attention(shard_gdn_cp(model, group), group)
+    return context_parallel_attention(shard_s5_cp(shard_gdn_cp(model, group), group), group)
 
 
 def split_sequence(x: torch.Tensor, group=None, dim: int = 1) -> torch.Tensor:

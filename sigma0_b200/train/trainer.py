@@ -13,6 +13,16 @@ Data parallelism: with ``world > 1`` the flat gradient is averaged over ranks
 ``data``/``gpus`` (``training/train_helpers.py:2123-2196``) -- or, with
 ``sharded=True``, reduce-scattered so each rank updates only its shard of the
 flat buffer and the updated parameters are all-gathered (ZeRO-1/2 style).
+
+Context parallelism (``context_parallel=True``, ``world > 1``): every rank receives the
+whole batch and keeps one contiguous segment of every sequence (tokens and labels along
+the sequence, book rows along the messages; segments start on a message boundary).  The
+mixers and attention blocks are wrapped by ``parallel.cp.shard_model_cp``, which carries
+the recurrent state (and the attention keys / values) across segment boundaries, so the
+segment losses' mean is the full-sequence loss and the data-parallel gradient average
+above is its exact gradient.  The returned loss is averaged over the ranks.  The
+reference has no training-time context parallelism (its only sequence-parallel code is
+the test-time Mamba3 phase split, ``src/base_model/models/mamba3_seqpar.py``).
 """
 from __future__ import annotations
 
@@ -31,7 +41,8 @@ from .optim import FlatAdam, cosine_schedule
 class Trainer:
     def __init__(self, args, device: Optional[torch.device] = None, world: int = 1, rank: int = 0,
                  group=None, total_steps: int = 1000, seed: int = 0, sharded: bool = False,
-                 accum_steps: int = 1, grad_wire_dtype: str = "float32", dp_impl: str = "nccl"):
+                 accum_steps: int = 1, grad_wire_dtype: str = "float32", dp_impl: str = "nccl",
+                 context_parallel: bool = False):
         self.args = args
         self.device = device or torch.device("cuda" if torch.cuda.is_available() else "cpu")
         self.world, self.rank, self.group = world, rank, group
@@ -78,8 +89,12 @@ class Trainer:
         if dp_impl == "fused" and world > 1:
             from ..parallel.fused_dp import FusedDPSync
             self.fused = FusedDPSync(self.opt, group)
+        self.cp = bool(context_parallel) and world > 1
+        if self.cp:
+            from ..parallel.cp import shard_model_cp
+            shard_model_cp(self.model, group)   # the wrappers share the re-homed parameters
         self.accum_steps = max(1, int(accum_steps))
-        self.global_batch = int(getattr(args, "micro_bsz", 1)) * world
+        self.global_batch = int(getattr(args, "micro_bsz", 1)) * (1 if self.cp else world)
         self.step_idx = 0
         self._sumsq_all = torch.zeros(1, device=self.device)
 
@@ -143,6 +158,8 @@ class Trainer:
         """One optimizer step on device tensors; with ``accum_steps > 1`` the batch is
         split into micro-batches whose gradients accumulate before the update."""
         self.opt.zero_grad()
+        if self.cp:
+            tokens, labels, book = self._segment(tokens, labels, book)
         k = self.accum_steps
         if k == 1:
             loss, _ = self.model.loss(tokens, book, labels, ignore_times=self.ignore_times, tokenizer=self.tok)
@@ -157,7 +174,19 @@ class Trainer:
         scale = cosine_schedule(self.step_idx + 1, self.warmup_steps, self.total_steps, self.lr_min_frac)
         self._update(scale)
         self.step_idx += 1
+        if self.cp:
+            dist.all_reduce(total, group=self.group)
+            total = total / self.world
         return total
+
+    def _segment(self, tokens, labels, book):
+        """This rank's segment of every sequence (context parallelism)."""
+        from ..parallel.cp import split_sequence
+        msg_len = self.model.msg_len
+        if tokens.shape[1] % (self.world * msg_len):
+            raise ValueError(f"{tokens.shape[1]} tokens do not split into whole messages over {self.world} ranks")
+        book = split_sequence(book, self.group) if book is not None else None
+        return split_sequence(tokens, self.group), split_sequence(labels, self.group), book
 
     def to_device(self, batch):
         return tuple(t.to(self.device, non_blocking=True) if t is not None else None for t in batch)

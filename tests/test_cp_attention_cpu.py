@@ -80,7 +80,7 @@ def test_context_parallel_attention_matches_full(kind, tmp_path):
             assert err <= 5e-5 * p.grad.norm().item() + 1e-5, (kind, n, err)
 
 
-def test_shard_model_cp_wraps_mamba3_and_attention_blocks():
+def test_shard_model_cp_wraps_every_sequence_mixer():
     from sigma0_b200.models.mamba3 import Mamba3
     from sigma0_b200.models.nsa import NSABlock
     from sigma0_b200.models.transformer import TransformerBlock
@@ -88,7 +88,10 @@ def test_shard_model_cp_wraps_mamba3_and_attention_blocks():
     from sigma0_b200.parallel.cp_attention import NSABlockCP, TransformerBlockCP
     from sigma0_b200.models.gdn import GDN
     from sigma0_b200.parallel.cp_gdn import GDNCP
+    from sigma0_b200.models.s5 import make_s5_factory
+    from sigma0_b200.parallel.cp_s5 import S5CP
     m = torch.nn.Sequential(Mamba3(64, d_state=16, headdim=16, chunk_size=16), TransformerBlock(64, n_heads=4),
-                            NSABlock(64, n_heads=4, block_size=8, select_block=16), GDN(64, num_heads=4, head_dim=16))
+                            NSABlock(64, n_heads=4, block_size=8, select_block=16), GDN(64, num_heads=4, head_dim=16),
+                            make_s5_factory(32, 2)(64))
     shard_model_cp(m)
-    assert [type(c) for c in m] == [Mamba3CP, TransformerBlockCP, NSABlockCP, GDNCP]
+    assert [type(c) for c in m] == [Mamba3CP, TransformerBlockCP, NSABlockCP, GDNCP, S5CP]

@@ -152,3 +152,34 @@ def test_fedavg_one_inner_step_is_parameter_average(tmp_path):
     dl.step(tok, lab, book)
     ref.step_device(tok, lab, book)
     assert torch.allclose(tr.opt.flat, ref.opt.flat, atol=1e-7)
+
+
+def _cp_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=120))
+    try:
+        from sigma0_b200.train.trainer import Trainer
+        torch.set_num_threads(1)
+        tr = Trainer(_args(), device=torch.device("cpu"), world=world, rank=rank, total_steps=10, seed=0,
+                     context_parallel=True)
+        tok, lab, book = _batch()
+        losses = [float(tr.step_device(tok, lab, book)) for _ in range(3)]
+        if rank == 0:
+            torch.save({"flat": tr.opt.flat.clone(), "losses": losses}, os.path.join(out_dir, "cp.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_context_parallel_trainer_matches_single_process(tmp_path):
+    """Two context-parallel ranks, each holding half of every sequence, take the same three
+    optimizer steps as one process on the whole sequences."""
+    from sigma0_b200.train.trainer import Trainer
+    torch.set_num_threads(2)
+    tr = Trainer(_args(), device=torch.device("cpu"), world=1, rank=0, total_steps=10, seed=0)
+    tok, lab, book = _batch()
+    ref_losses = [float(tr.step_device(tok, lab, book)) for _ in range(3)]
+    mp.spawn(_cp_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    res = torch.load(os.path.join(str(tmp_path), "cp.pt"))
+    np.testing.assert_allclose(res["losses"], ref_losses, rtol=2e-5)
+    d = (res["flat"] - tr.opt.flat).norm() / tr.opt.flat.norm()
+    assert d < 1e-5, float(d)
