@@ -9,7 +9,8 @@ argument defaults (the reference's launch configs work unchanged for the keys
 both sides know).  Mirrors ``run/base_model/runtime/train.py:47-330``: model
 and optimizer flags, data selection, checkpointing/resume, watchdog, and the
 distributed options (replicated / sharded / fused gradient sync, bf16 wire,
-gradient accumulation).
+gradient accumulation, and ``--context_parallel``, which splits every sequence over the
+ranks instead of the batch).
 """
 from __future__ import annotations
 
@@ -50,6 +51,8 @@ def parse(argv=None):
     p.add_argument("--sharded", action="store_true")
     p.add_argument("--grad_wire_dtype", default="float32", choices=["float32", "bfloat16"])
     p.add_argument("--accum_steps", type=int, default=1)
+    p.add_argument("--context_parallel", action="store_true",
+                   help="split every sequence over the ranks (message-aligned segments) instead of the batch")
     p.add_argument("--seed", type=int, default=0)
     a = p.parse_args(argv)
     if a.config:
@@ -88,14 +91,16 @@ def main(argv=None):
     args = model_args(a, **extra)
     trainer = Trainer(args, device=dev, world=world, rank=rank, total_steps=a.steps, seed=a.seed,
                       sharded=a.sharded, accum_steps=a.accum_steps, grad_wire_dtype=a.grad_wire_dtype,
-                      dp_impl=a.dp_impl)
+                      dp_impl=a.dp_impl, context_parallel=a.context_parallel)
+    # context parallelism: every rank draws the same batch and keeps its segment of it
+    drank, dworld = (0, 1) if a.context_parallel else (rank, world)
     tickers = a.tickers.split(",") if a.tickers else None
     dr = tuple(a.train_date_range.split(",")) if a.train_date_range else None
-    days = load_days(a.data_dir, a.synthetic, args.n_messages + 1, a.seed + 1000 * rank, tickers, dr)
+    days = load_days(a.data_dir, a.synthetic, args.n_messages + 1, a.seed + 1000 * drank, tickers, dr)
     ds = LobWindowDataset([d.msgs for d in days], [d.books for d in days], args.n_messages,
                           token_mode=args.token_mode)
-    sampler = WindowSampler(len(ds), args.micro_bsz, world=1 if not a.data_dir else world,
-                            rank=0 if not a.data_dir else rank, seed=a.seed)
+    sampler = WindowSampler(len(ds), args.micro_bsz, world=1 if not a.data_dir else dworld,
+                            rank=0 if not a.data_dir else drank, seed=a.seed)
 
     def batches():
         for idx in sampler:

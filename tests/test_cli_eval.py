@@ -19,6 +19,30 @@ def test_train_cli_runs_and_resumes(tmp_path, capsys):
     assert lines[-1]["event"] == "finished" and lines[-1]["steps"] == 3
 
 
+def test_train_cli_context_parallel_matches_single_process():
+    """``--context_parallel`` on two gloo ranks (torchrun) logs the single process's losses."""
+    import socket
+    import subprocess
+    import sys
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    args = ["-m", "sigma0_b200.cli.train", "--preset", "smoke", "--impl", "torch", "--synthetic", "2",
+            "--n_messages", "4", "--micro_bsz", "2", "--log_every", "1", "--watchdog_timeout", "0", "--steps", "2"]
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+
+    def losses(cmd):
+        out = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+        assert out.returncode == 0, out.stderr[-2000:]
+        return [json.loads(l)["loss"] for l in out.stdout.splitlines() if l.startswith('{"step"')]
+    one = losses([sys.executable] + args)
+    two = losses([sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2",
+                  "--master-addr", "127.0.0.1", "--master-port", str(port)] + args + ["--context_parallel"])
+    assert len(one) == len(two) == 2
+    np.testing.assert_allclose(two, one, rtol=1e-5)
+
+
 def test_train_cli_config_file(tmp_path):
     from sigma0_b200.cli.train import parse
     (tmp_path / "c.yaml").write_text("steps: 7\nlog_every: 3\nenv_S0_TEST_KNOB: 1\n")
