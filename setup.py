@@ -11,15 +11,15 @@ from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("sigma0_b200", "csrc")
-sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
+# attention_tc.cu (a tcgen05 flash-attention forward) is left out of the build: it failed
+# with an unspecified launch failure on multi-wave grids and its cause is not found
+PARKED = {"attention_tc.cu"}
+sources = [s for s in sorted(glob.glob(os.path.join(CSRC, "*.cu"))) if os.path.basename(s) not in PARKED]
+sources += sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 nvcc_flags = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
                      "-Xptxas=-v" if os.environ.get("S0_PTXAS_VERBOSE") else "-Xptxas=-O3"]
-if os.environ.get("S0_CHECK"):
-    nvcc_flags.append("-DS0_CHECK=1")
-if os.environ.get("S0_PHASE_PROBE"):      # per-phase clock counters in the chunk backward
-    nvcc_flags.append("-DS0_PHASE_PROBE=1")
 
 setup(
     name="sigma0_b200",

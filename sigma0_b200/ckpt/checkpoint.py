@@ -1,6 +1,9 @@
 """Checkpoint save / restore for the flat-buffer trainer.
 
-Layout (the reference's Orbax manager layout, ``run/base_model/runtime/train.py:538-578``):
+Directory layout and retention are modelled on the reference's Orbax manager
+(``run/base_model/runtime/train.py:538-578``); the array format is NOT Orbax: arrays
+are raw little-endian float32 files plus a JSON leaf table, so Orbax checkpoints are
+not read here.  ``export_params_npz`` exchanges weights by Flax path.  Files:
 
     <base>/<step>/state/params.f32          float32 flat parameter buffer
     <base>/<step>/state/adam_m.r<k>.f32     Adam first moment, rank k's shard

@@ -430,17 +430,6 @@ void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor
   TORCH_CHECK(rc == 0, "attn_fwd launch failed (", rc, ")");
 }
 
-void attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, double scale,
-                 int64_t window, int64_t q_offset, c10::optional<at::Tensor> kpos, c10::optional<at::Tensor> qoff,
-                 at::Tensor status) {
-  c10::cuda::CUDAGuard guard(q.device());
-  AttnArgs a = attn_args(q, k, v, o, lse, scale, window, q_offset, kpos, qoff);
-  req(status, at::kInt, "status");
-  a.status = status.data_ptr<int>();
-  const int rc = attn_fwd_tc_launch(a, (int)q.size(3), stream());
-  TORCH_CHECK(rc == 0, "attn_fwd_tc launch failed (", rc, ")");
-}
-
 void attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dout, at::Tensor D,
               at::Tensor dq_acc, at::Tensor dk, at::Tensor dv, double scale, int64_t window, int64_t q_offset,
               c10::optional<at::Tensor> kpos, c10::optional<at::Tensor> qoff) {
@@ -677,13 +666,6 @@ void s5_scan_bwd(at::Tensor lam, at::Tensor xs, c10::optional<at::Tensor> x0, at
 }
 
 // ---- profiling ---------------------------------------------------------------------------
-at::Tensor m3_phase_probe() {
-  unsigned long long v[16];
-  if (!m3_phase_probe_read(v)) return at::empty({0}, at::kLong);
-  auto t = at::empty({16}, at::kLong);
-  for (int i = 0; i < 16; ++i) t[i] = (int64_t)v[i];
-  return t;
-}
 
 // ---- decode / engine ----------------------------------------------------------------------
 void m3_decode_step(at::Tensor proj, int64_t nh, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias, at::Tensor Bb,
@@ -855,21 +837,6 @@ void dp_fused_adam(std::vector<int64_t> G, std::vector<int64_t> P, std::vector<i
   TORCH_CHECK(rc == 0, "dp_fused_adam launch failed: ", rc > 0 ? cudaGetErrorString((cudaError_t)rc) : "occupancy");
 }
 
-std::vector<at::Tensor> tc_gemm_test(at::Tensor A, at::Tensor B, int64_t M) {
-  req(A, at::kBFloat16, "A");
-  req(B, at::kBFloat16, "B");
-  int64_t K = A.size(1), N = B.size(0);
-  TORCH_CHECK(A.size(0) == M && B.size(1) == K, "A (M, K), B (N, K)");
-  c10::cuda::CUDAGuard guard(A.device());
-  auto D = at::zeros({128, N}, A.options().dtype(at::kFloat));
-  auto err = at::zeros({1}, A.options().dtype(at::kInt));
-  int rc = tc_gemm_test_launch(A.data_ptr(), B.data_ptr(), D.data_ptr<float>(), (int)M, (int)N, (int)K,
-                               err.data_ptr<int>(), stream());
-  TORCH_CHECK(rc == 0, "unsupported shape");
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {D, err};
-}
-
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -904,9 +871,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("qoff") = py::none(),
         "causal / sliding-window flash attention forward: o and the base-2 row log-sum-exp (window <= 0: none; "
         "optional per-key positions and per-entry query offsets)");
-  m.def("attn_fwd_tc", &attn_fwd_tc, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
-        py::arg("scale"), py::arg("window"), py::arg("q_offset"), py::arg("kpos"), py::arg("qoff"), py::arg("status"),
-        "flash attention forward on tcgen05 / TMEM / TMA (same outputs as attn_fwd; status set on a wait timeout)");
   m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dout"), py::arg("D"), py::arg("dq_acc"), py::arg("dk"), py::arg("dv"), py::arg("scale"),
         py::arg("window"), py::arg("q_offset"), py::arg("kpos") = py::none(), py::arg("qoff") = py::none(),
@@ -925,8 +889,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_intra_bwd", &kda_intra_bwd, "gradients of q, k, kb and the cumulative log decay G");
   m.def("s5_scan_fwd", &s5_scan_fwd, "S5 complex diagonal recurrence: all states and the final one");
   m.def("s5_scan_bwd", &s5_scan_bwd, "reverse recurrence: dBu, dlam (accumulated into the zeroed dlam), dx0");
-  m.def("m3_phase_probe", &m3_phase_probe,
-        "chunk-backward per-phase clock sums since the last call (empty unless built with S0_PHASE_PROBE)");
   m.def("m3_decode_step", &m3_decode_step, py::arg("proj"), py::arg("nh"), py::arg("wB"), py::arg("wC"),
         py::arg("dt_bias"), py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("A_floor"), py::arg("eps"),
         py::arg("ang"), py::arg("ssm"), py::arg("kprev"), py::arg("vprev"), py::arg("y"), py::arg("T") = 1,
@@ -935,7 +897,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("eng_l2", &eng_l2, "batched L2 extraction");
   m.def("m3_use_tc_scan", [](bool on) { m3_use_tc_scan(on ? 1 : 0); }, "select the tcgen05 chunk-scan kernel");
   m.def("m3_tc_error", []() { return m3_tc_error(); }, "nonzero if a tcgen05 bounded wait timed out");
-  m.def("tc_gemm_test", &tc_gemm_test, "tcgen05 self-test: D = A B^T in tensor memory (returns all 128 lanes)");
   m.def("dp_fused_adam", &dp_fused_adam, "fused reduce-scatter + AdamW + all-gather over peer memory");
   m.def("gen_apply", &gen_apply, "generation: decode message tokens, match, L2 and next book image");
   m.def("gen_sample", &gen_sample, "syntax-masked argmax / Gumbel-max sampling from fp32 logits");

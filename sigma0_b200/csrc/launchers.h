@@ -124,15 +124,12 @@ struct DpfArgs {
 };
 int dp_fused_adam_launch(const DpfArgs& a, int sms, cudaStream_t st);
 
-// tcgen05 building-block self-test (tc_test.cu)
-int tc_gemm_test_launch(const void* A, const void* B, float* D, int M, int N, int K, int* err, cudaStream_t st);
 void m3_use_tc_scan(int on);   // select the tcgen05 chunk scan
 int m3_tc_error();             // nonzero once a bounded tcgen05 wait gave up
 void m3_decode_multi_launch(const void* proj, int B, int T, int ldp, int nh, const float* wB, const float* wC,
                             const float* dt_bias, const float* Bb, const float* Cb, const float* D, float A_floor,
                             float eps, float* ang, float* ssm, float* kprev, float* vprev, void* y,
                             cudaStream_t st);
-bool m3_phase_probe_read(unsigned long long* out);
 void rms_bwd_pipe_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw,
                          float* part, long T, int D, int sms, cudaStream_t st);
 void ln_bwd_pipe_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,
@@ -185,8 +182,6 @@ struct AttnBwdArgs {
 };
 int attn_fwd_launch(const AttnArgs& a, int hd, cudaStream_t st);
 int attn_bwd_launch(const AttnBwdArgs& a, int hd, cudaStream_t st);
-// the same forward on tcgen05 / TMEM / TMA (attention_tc.cu); -3: unaligned base, -4: tensor map
-int attn_fwd_tc_launch(const AttnArgs& a, int hd, cudaStream_t st);
 // imp [B, Lq, Lk] = head-summed softmax probabilities of a finished forward (lse)
 int attn_probsum_launch(const AttnArgs& a, float* imp, int hd, cudaStream_t st);
 

@@ -54,23 +54,6 @@ struct ScanIn {
   const float* aend;   // [B, nh, nc]    sum of ADT over each chunk
 };
 
-// Optional per-phase cycle counters of the chunk backward (built with -DS0_PHASE_PROBE):
-// thread 0 of every block adds the clock64() delta of each phase to g_bwd_phase[k].
-#ifdef S0_PHASE_PROBE
-__device__ unsigned long long g_bwd_phase[16];
-#define BWD_PHASE_START long long _tp = clock64()
-#define BWD_PHASE(k)                                                              \
-  do {                                                                            \
-    if (threadIdx.x == 0) {                                                       \
-      const long long _t = clock64();                                             \
-      atomicAdd(&g_bwd_phase[k], (unsigned long long)(_t - _tp));                 \
-      _tp = _t;                                                                   \
-    }                                                                             \
-  } while (0)
-#else
-#define BWD_PHASE_START
-#define BWD_PHASE(k)
-#endif
 
 __device__ __forceinline__ float wrap2pi(float x) { return x - TWO_PI_F * floorf(x / TWO_PI_F); }
 
@@ -1023,7 +1006,6 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   float* sMisc = sTh0 + 32;      // [16]
   float* sDD = sMisc + 16;       // [16]
 
-  BWD_PHASE_START;
   const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
   const int rb = warp & 3, cq = warp >> 2;
@@ -1063,13 +1045,10 @@ __global__ void __launch_bounds__(BWD_NT, 1)
   if (tid < CS) { sDcum[tid] = 0.f; sDscl[tid] = 0.f; }
   cp_async_wait_group<1>();
   __syncthreads();
-  BWD_PHASE(0);
   row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
-  BWD_PHASE(8);
   chunk_angles<BWD_NT>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
   cp_async_wait_all();
   __syncthreads();
-  BWD_PHASE(9);
   // dY0 = dy * silu(z) and the qk-diagonal row sums dqk[row] = sum_p dY0 * V (they need
   // no GEMM): one 8-column slice per thread, 8 threads per row
   for (int i = tid; i < CS * P / 8; i += BWD_NT) {
@@ -1095,11 +1074,9 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     if ((i & 7) == 0) sDqk[row] = dq;
   }
   build_qk<BWD_NT>(sQ, sBn, sQ, sK, sCos, sSin, sScl, sCbv, sBbv, sQKr, tid);
-  BWD_PHASE(10);
   const float cend = sCum[CS - 1];
   if (tid < CS) sW[tid] = __expf(cend - sCum[tid]);
   __syncthreads();
-  BWD_PHASE(1);
 
   const int r0 = m0 + gq, r1 = r0 + 8;
   const float cum0 = sCum[r0], cum1 = sCum[r1];
@@ -1174,7 +1151,6 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     }
   }
   __syncthreads();   // sP, sdS complete
-  BWD_PHASE(2);
   // ---- B: y0 = P V + Y_off + (D + qk) V -> dz (into sZ); d cum from dY0 . Y_off ---------
   {
     float vacc[2][4];
@@ -1221,7 +1197,6 @@ __global__ void __launch_bounds__(BWD_NT, 1)
       atomicAdd(&sDcum[r1], dc1);
     }
   }
-  BWD_PHASE(3);
   float colp[4][4];   // per-thread column partial sums of dQ / dK (bias gradients)
   // ---- C: dQ = exp(cum_l) dY0 S_in + dS K and dK = w_s (V dS_out) + dS^T Q on the same
   // columns (cq*16.. and cq*16+64..), then one epilogue for both: gQ, gK, dtheta, dscale,
@@ -1270,7 +1245,6 @@ __global__ void __launch_bounds__(BWD_NT, 1)
         mma_bf16(kacc[2 * np + 1], at, bb[2], bb[3]);
       }
     }
-    BWD_PHASE(11);
     float dsc0 = 0.f, dsc1 = 0.f;
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
@@ -1330,7 +1304,6 @@ __global__ void __launch_bounds__(BWD_NT, 1)
       }
       if (hr) dsc1 = dsc; else dsc0 = dsc;
     }
-    BWD_PHASE(12);
     dsc0 += __shfl_xor_sync(0xffffffffu, dsc0, 1); dsc0 += __shfl_xor_sync(0xffffffffu, dsc0, 2);
     dsc1 += __shfl_xor_sync(0xffffffffu, dsc1, 1); dsc1 += __shfl_xor_sync(0xffffffffu, dsc1, 2);
     if (tq == 0) {
@@ -1347,9 +1320,7 @@ __global__ void __launch_bounds__(BWD_NT, 1)
       colp[nt][3] = kacc[nt][1] + kacc[nt][3];
     }
   }
-  BWD_PHASE(7);
   __syncthreads();   // every warp done reading sX (V) as an MMA operand; sBn and sQ are dead
-  BWD_PHASE(4);
   {   // partial column sums -> part[32][BPLD] over the dead B and Q tiles
     float* part = reinterpret_cast<float*>(sBn);
     const int prow = rb * 8 + gq;
@@ -1445,7 +1416,6 @@ __global__ void __launch_bounds__(BWD_NT, 1)
     if (lane == 0) sDD[0] = dd;
   }
   __syncthreads();   // all shared atomics done; sX holds dV, sZ holds dz
-  BWD_PHASE(5);
   if (tid == 0) {
     float dot = 0.f, s = 0.f;
     for (int k = 0; k < BWD_NT / 32; ++k) dot += sMisc[k];
@@ -1522,7 +1492,6 @@ __global__ void __launch_bounds__(BWD_NT, 1)
       else out.dBb[(bh * g.nc + c) * N + i - N] = sum;
     }
   }
-  BWD_PHASE(6);
 }
 
 // ---------------------------------------------------------------------------
@@ -1812,18 +1781,4 @@ void m3_prep_bwd_launch(const M3Geo& G, const void* proj, const float* wB, const
                                       reinterpret_cast<const bf16*>(gQ), reinterpret_cast<const bf16*>(gK),
                                       dthl, dthc, dgam, dscl, dadt, reinterpret_cast<bf16*>(dproj), dwB, dwC,
                                       ddt_bias);
-}
-
-// copies the chunk-backward phase counters to out[16] and clears them; false when the
-// library was built without -DS0_PHASE_PROBE
-bool m3_phase_probe_read(unsigned long long* out) {
-#ifdef S0_PHASE_PROBE
-  cudaMemcpyFromSymbol(out, s0::m3::g_bwd_phase, sizeof(unsigned long long) * 16);
-  static const unsigned long long zeros[16] = {};
-  cudaMemcpyToSymbol(s0::m3::g_bwd_phase, zeros, sizeof(zeros));
-  return true;
-#else
-  (void)out;
-  return false;
-#endif
 }

@@ -14,6 +14,7 @@
 #include "common.cuh"
 #include "noalloc.h"
 
+#include <cstdint>
 #include <cstdio>
 #include <mutex>
 
@@ -40,14 +41,15 @@ template <int PER>
 __global__ void __launch_bounds__(NT)
     rms_bwd_noalloc_k(const bf16* __restrict__ dy, const bf16* __restrict__ x, const float* __restrict__ w,
                       const float* __restrict__ rstd, bf16* __restrict__ dx, float* __restrict__ dw,
-                      Scratch* __restrict__ sc, int T, int D) {
+                      Scratch* __restrict__ sc, long long T, int D) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nwb = NT / 32;
-  const int gw = (blockIdx.x * NT + threadIdx.x) >> 5, nw = (gridDim.x * NT) >> 5;
+  const long long gw = (blockIdx.x * NT + threadIdx.x) >> 5, nw = (gridDim.x * NT) >> 5;
   const int nv = D / 8;
   float aw[PER * 8];
 #pragma unroll
   for (int i = 0; i < PER * 8; ++i) aw[i] = 0.f;
-  for (int row = gw; row < T; row += nw) {
+  // 64-bit row index: T may be close to 2^31 - 1, where row + nw would overflow an int
+  for (long long row = gw; row < T; row += nw) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
     const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * D);
     const float r = rstd[row];
@@ -171,6 +173,10 @@ extern "C" __attribute__((visibility("default"))) int s0_rms_bwd_noalloc(const v
     return -1;
   }
   if (!dy || !x || !w || !rstd || !dx || !dw) return fail(-1, "s0_rms_bwd_noalloc: null pointer argument");
+  // rows of dy, x and dx are read and written 16 bytes at a time: their base addresses must be
+  // 16-byte aligned (D % 8 == 0 keeps every row start aligned once the base is)
+  if ((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dx)) & 15u)
+    return fail(-1, "s0_rms_bwd_noalloc: dy, x and dx must be 16-byte aligned");
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail((int)e, "cudaGetDevice failed");
@@ -188,10 +194,10 @@ extern "C" __attribute__((visibility("default"))) int s0_rms_bwd_noalloc(const v
   const bf16* g = reinterpret_cast<const bf16*>(dy);
   const bf16* xp = reinterpret_cast<const bf16*>(x);
   bf16* o = reinterpret_cast<bf16*>(dx);
-  if (nv <= 32) rms_bwd_noalloc_k<1><<<blocks, NT, smem, st>>>(g, xp, w, rstd, o, dw, sc, (int)T, D);
-  else if (nv <= 64) rms_bwd_noalloc_k<2><<<blocks, NT, smem, st>>>(g, xp, w, rstd, o, dw, sc, (int)T, D);
-  else if (nv <= 128) rms_bwd_noalloc_k<4><<<blocks, NT, smem, st>>>(g, xp, w, rstd, o, dw, sc, (int)T, D);
-  else rms_bwd_noalloc_k<8><<<blocks, NT, smem, st>>>(g, xp, w, rstd, o, dw, sc, (int)T, D);
+  if (nv <= 32) rms_bwd_noalloc_k<1><<<blocks, NT, smem, st>>>(g, xp, w, rstd, o, dw, sc, T, D);
+  else if (nv <= 64) rms_bwd_noalloc_k<2><<<blocks, NT, smem, st>>>(g, xp, w, rstd, o, dw, sc, T, D);
+  else if (nv <= 128) rms_bwd_noalloc_k<4><<<blocks, NT, smem, st>>>(g, xp, w, rstd, o, dw, sc, T, D);
+  else rms_bwd_noalloc_k<8><<<blocks, NT, smem, st>>>(g, xp, w, rstd, o, dw, sc, T, D);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     std::snprintf(g_msg, sizeof(g_msg), "s0_rms_bwd_noalloc launch failed: %s", cudaGetErrorString(e));

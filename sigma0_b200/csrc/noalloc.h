@@ -17,7 +17,8 @@
 // (cudaGetSymbolAddress) and sets a kernel attribute; make that first call
 // before any stream capture on that device.
 // Limits: D (row width) a multiple of 8 and at most S0_NOALLOC_MAX_D;
-// 1 <= T (rows) <= 2^31 - 1.
+// 1 <= T (rows) <= 2^31 - 1; dy, x and dx start on a 16-byte boundary (rows are
+// moved 16 bytes at a time).
 #pragma once
 
 #ifdef __cplusplus

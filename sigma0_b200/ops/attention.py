@@ -44,22 +44,6 @@ def _kernel_ready(t: torch.Tensor) -> torch.Tensor:
     return t if ok else t.contiguous()
 
 
-# The tcgen05 forward (attention_tc.cu) is not dispatched: it matches the mma.sync forward
-# on single-wave grids but raised an unspecified launch failure once the grid needed a
-# second wave of CTAs, and the cause is not found yet.  The forward runs attn_fwd_k.
-_TC = [False]
-_STATUS = {}
-
-
-def tc_status(device) -> torch.Tensor:
-    """The status word of the tcgen05 forward on ``device`` (non-zero: a bounded wait
-    timed out in some call since it was zeroed)."""
-    d = torch.device(device)
-    if d not in _STATUS:
-        _STATUS[d] = torch.zeros(1, dtype=torch.int32, device=d)
-    return _STATUS[d]
-
-
 class _FlashAttn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, scale, window, q_offset, kpos, qoff):
@@ -68,10 +52,7 @@ class _FlashAttn(torch.autograd.Function):
         B, Lq, nh, hd = q.shape
         o = torch.empty_like(q, memory_format=torch.contiguous_format)
         lse = torch.empty(B, nh, Lq, dtype=torch.float32, device=q.device)
-        if _TC[0]:
-            ext().attn_fwd_tc(q, k, v, o, lse, scale, window, q_offset, kpos, qoff, tc_status(q.device))
-        else:
-            ext().attn_fwd(q, k, v, o, lse, scale, window, q_offset, kpos, qoff)
+        ext().attn_fwd(q, k, v, o, lse, scale, window, q_offset, kpos, qoff)
         ctx.save_for_backward(q, k, v, o, lse, kpos, qoff)
         ctx.args = (scale, window, q_offset)
         ctx.mark_non_differentiable(lse)

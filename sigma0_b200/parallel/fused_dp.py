@@ -55,11 +55,18 @@ class FusedDPSync:
         self._handles = hs
         self.scratch = torch.zeros(2, dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        # every step copies the status word to pinned host memory behind the kernel; the next
+        # step (or ``poll``) reads that copy, so a timed-out peer raises without a per-step
+        # device synchronisation
+        self._host_status = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self._status_ev = torch.cuda.Event()
+        self._pending = False
         self.seq = 0
         dist.barrier(group=self.group)
 
     def step(self, lr_scale: float) -> None:
         from ..ops._ext import ext
+        self._check_previous()
         o = self.opt
         o.step_count += 1
         t = o.step_count
@@ -68,10 +75,31 @@ class FusedDPSync:
                             o.lo, o.hi, o.n_ssm, self.rank, self.seq, self.SPIN_LIMIT,
                             o.base_lr["ssm"] * lr_scale, o.base_lr["regular"] * lr_scale, o.wd, o.b1, o.b2, o.eps,
                             1 - o.b1 ** t, 1 - o.b2 ** t, o.max_grad_norm)
+        self._host_status.copy_(self.status, non_blocking=True)
+        self._status_ev.record()
+        self._pending = True
 
-    def check(self) -> None:
-        """Raise if any in-kernel cross-rank wait timed out (reads one word; syncs the stream)."""
-        s = int(self.status.item())
+    def _raise_if(self, s: int) -> None:
         if s:
             raise RuntimeError(f"fused data-parallel step: a peer did not arrive (phase {s - 100}); "
                                f"a rank has failed or left")
+
+    def _check_previous(self) -> None:
+        """Raise if the previous step's kernel reported a timed-out wait (waits for that
+        step's status copy, which lags the host by at most one step)."""
+        if self._pending:
+            self._status_ev.synchronize()
+            self._pending = False
+            self._raise_if(int(self._host_status[0]))
+
+    def poll(self) -> None:
+        """Raise now if the last finished step reported a timed-out wait (non-blocking when
+        the step is still running; the next ``step`` checks it then)."""
+        if self._pending and self._status_ev.query():
+            self._pending = False
+            self._raise_if(int(self._host_status[0]))
+
+    def check(self) -> None:
+        """Raise if any in-kernel cross-rank wait timed out (reads one word; syncs the stream)."""
+        self._pending = False
+        self._raise_if(int(self.status.item()))

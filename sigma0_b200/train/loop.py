@@ -4,9 +4,11 @@ Mirrors the reference's ``train_epoch`` / ``train`` duties
 (``src/base_model/training/train_helpers.py:27-95,1033-1346``,
 ``run/base_model/runtime/train.py:296-325,538-790``):
 
-* ``StepWatchdog``: a daemon timer armed around every step; if a step does not
-  finish within ``timeout`` seconds (longer during warm-up) the process exits
-  with status 1, so a hung collective cannot hold the job forever;
+* ``StepWatchdog``: a daemon monitor armed for every step until the DEVICE has
+  finished it (a CUDA event recorded behind the step, polled without syncing the
+  host); if a step does not finish within ``timeout`` seconds (longer during
+  warm-up) the process exits with status 1, so a hung kernel or collective cannot
+  hold the job forever even on steps where the loop never reads the loss;
 * NaN/Inf loss -> stop without overwriting the newest (good) checkpoint;
 * a time limit (e.g. the scheduler's wall clock) -> save before it is reached;
 * periodic checkpoints and resume from the newest intact checkpoint, skipping
@@ -29,15 +31,26 @@ import torch
 
 
 class StepWatchdog:
-    """Arm before a step, disarm after; fires ``on_timeout`` (default: exit 1) if the step hangs."""
+    """Arm before a step; disarm after it, or hand it a completion token with ``watch``.
+
+    A step is covered until the host returns from it (``disarm``) or, on a GPU, until
+    the device has finished it: ``watch(step, done)`` keeps the step armed until
+    ``done()`` returns True (e.g. a CUDA event's ``query``), so a kernel or collective
+    that hangs on the device fires the watchdog even though the host enqueued the
+    step and moved on.  ``on_timeout`` (default: exit 1) fires once."""
 
     def __init__(self, timeout: float, warmup_timeout: Optional[float] = None, warmup_steps: int = 2,
-                 on_timeout: Optional[Callable[[str], None]] = None, clock=time.monotonic):
+                 on_timeout: Optional[Callable[[str], None]] = None, clock=time.monotonic,
+                 poll_s: Optional[float] = None):
         self.timeout, self.warmup_timeout = timeout, warmup_timeout or 4 * timeout
         self.warmup_steps = warmup_steps
         self.on_timeout = on_timeout or self._exit
         self.clock = clock
-        self._timer: Optional[threading.Timer] = None
+        self.poll_s = poll_s if poll_s is not None else max(0.005, min(0.5, self.timeout / 8))
+        self._lock = threading.Lock()
+        self._host: Optional[tuple] = None          # (step, deadline) of the step on the host
+        self._device: List[tuple] = []              # (step, deadline, done) enqueued, not finished
+        self._thread: Optional[threading.Thread] = None
         self.fired = False
 
     @staticmethod
@@ -45,21 +58,47 @@ class StepWatchdog:
         print(f"[watchdog] {msg}; exiting", flush=True)
         os._exit(1)
 
-    def arm(self, step: int) -> None:
-        self.disarm()
-        t = self.warmup_timeout if step < self.warmup_steps else self.timeout
+    def _limit(self, step: int) -> float:
+        return self.warmup_timeout if step < self.warmup_steps else self.timeout
 
-        def fire():
-            self.fired = True
-            self.on_timeout(f"step {step} exceeded {t:.0f} s")
-        self._timer = threading.Timer(t, fire)
-        self._timer.daemon = True
-        self._timer.start()
+    def _run(self) -> None:
+        while not self.fired:
+            time.sleep(self.poll_s)
+            now = self.clock()
+            with self._lock:
+                self._device = [r for r in self._device if not r[2]()]
+                late = [r for r in ([self._host] if self._host else []) + self._device if now > r[1]]
+            if late:
+                step = min(r[0] for r in late)
+                self.fired = True
+                self.on_timeout(f"step {step} exceeded {self._limit(step):.0f} s")
+                return
+
+    def _ensure_thread(self) -> None:
+        if self._thread is None or not self._thread.is_alive():
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def arm(self, step: int) -> None:
+        with self._lock:
+            self._host = (step, self.clock() + self._limit(step))
+        self._ensure_thread()
+
+    def watch(self, step: int, done: Callable[[], bool]) -> None:
+        """The host is done with ``step``; keep it armed until ``done()`` is True."""
+        with self._lock:
+            deadline = self._host[1] if self._host and self._host[0] == step else self.clock() + self._limit(step)
+            self._host = None
+            self._device.append((step, deadline, done))
 
     def disarm(self) -> None:
-        if self._timer is not None:
-            self._timer.cancel()
-            self._timer = None
+        with self._lock:
+            self._host = None
+
+    def pending(self) -> int:
+        """Steps the device has not finished yet."""
+        with self._lock:
+            return len(self._device)
 
 
 @dataclass
@@ -116,12 +155,14 @@ def fit(trainer, batches: Iterable, cfg: LoopConfig, log: Callable[[Dict], None]
         if batch[0].device.type == "cpu" and trainer.device.type == "cuda":
             batch = trainer.to_device(batch)
         loss = trainer.step_device(*batch)
+        if wd and trainer.device.type == "cuda":
+            ev = torch.cuda.Event()
+            ev.record()
+            wd.watch(step, ev.query)        # armed until the device has finished the step
         step += 1
         tok_count += batch[0].numel() * trainer.world
         if step % cfg.log_every == 0 or step == cfg.steps:
             last_loss = float(loss)             # the one host sync per log interval
-            if wd:
-                wd.disarm()
             dt = time.time() - t0
             gn = trainer.opt.last_grad_norm
             rec = {"step": step, "loss": last_loss, "tokens_per_s": tok_count / max(dt, 1e-9),

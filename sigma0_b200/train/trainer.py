@@ -195,7 +195,10 @@ class Trainer:
         """End-to-end step from host tensors ``(tokens, labels, book)``; returns the loss."""
         tokens, labels, book = self.to_device(batch)
         loss = self.step_device(tokens, labels, book)
-        return float(loss.item())
+        value = float(loss.item())
+        if self.fused is not None:      # the loss read synchronised: the status copy has landed
+            self.fused.poll()
+        return value
 
     @torch.no_grad()
     def eval_loss(self, tokens, labels, book=None) -> float:

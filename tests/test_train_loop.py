@@ -103,3 +103,24 @@ def test_flops_count_near_6n():
     f = lob_model_flops(a)
     # projections dominate: within 2x of 6*N per token, and SSD adds a positive share
     assert 0.5 < f.train / (6 * n) < 2.0 and f.ssd_fwd > 0
+
+
+def test_watchdog_covers_work_still_running_after_the_host_returns():
+    """A step the host enqueued and left stays armed until its completion token turns True:
+    a token that never does (a hung device) fires; one that does (a finished step) never fires."""
+    hits = []
+    wd = StepWatchdog(timeout=0.1, warmup_timeout=0.1, on_timeout=hits.append, poll_s=0.01)
+    wd.arm(0)
+    wd.watch(0, lambda: False)        # the device never finishes step 0
+    time.sleep(0.3)
+    assert wd.fired and "step 0 exceeded" in hits[0]
+    ok = []
+    wd2 = StepWatchdog(timeout=0.1, warmup_timeout=0.1, on_timeout=ok.append, poll_s=0.01)
+    done = {"v": False}
+    wd2.arm(0)
+    wd2.watch(0, lambda: done["v"])
+    time.sleep(0.03)
+    assert wd2.pending() == 1
+    done["v"] = True
+    time.sleep(0.2)
+    assert not ok and wd2.pending() == 0

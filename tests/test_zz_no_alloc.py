@@ -77,3 +77,19 @@ def test_noalloc_rejects_oversized_rows():
                                 dw.data_ptr(), 8, D, None)
     assert rc == -1
     assert b"at most 2048" in lib.s0_noalloc_last_error()
+
+
+def test_noalloc_rejects_misaligned_rows():
+    """A buffer that starts 8 bytes past a 16-byte boundary is refused with -1, not read."""
+    lib = _lib()
+    D = 512
+    buf = torch.zeros(8 * D + 8, device="cuda", dtype=torch.bfloat16)
+    x = buf[4:4 + 8 * D]                  # 8-byte offset from the allocation's base
+    assert x.data_ptr() % 16 == 8
+    w = torch.ones(D, device="cuda")
+    r = torch.ones(8, device="cuda")
+    dw = torch.zeros(D, device="cuda")
+    rc = lib.s0_rms_bwd_noalloc(x.data_ptr(), x.data_ptr(), w.data_ptr(), r.data_ptr(), x.data_ptr(),
+                                dw.data_ptr(), 8, D, None)
+    assert rc == -1
+    assert b"16-byte aligned" in lib.s0_noalloc_last_error()
