@@ -57,7 +57,7 @@ M3Scan m3_scan(const at::Tensor& proj, const M3Pre& pre, const at::Tensor& Bb, c
 
 // per-token prep + chunk totals + angle carry
 M3Pre m3_prepare(const at::Tensor& proj, int64_t B, int64_t L, int64_t nh, const at::Tensor& wB,
-                 const at::Tensor& wC, const at::Tensor& dt_bias, double A_floor, double eps) {
+                 const at::Tensor& wC, const at::Tensor& dt_bias, double A_floor, double eps, bool totals = true) {
   M3Geo g = m3_geo(proj, B, L, nh);
   TORCH_CHECK(nh <= 64, "at most 64 heads");
   auto f32 = proj.options().dtype(at::kFloat);
@@ -71,6 +71,7 @@ M3Pre m3_prepare(const at::Tensor& proj, int64_t B, int64_t L, int64_t nh, const
   m3_prep_fwd_launch(g, proj.data_ptr(), wB.data_ptr<float>(), wC.data_ptr<float>(), dt_bias.data_ptr<float>(),
                      (float)A_floor, (float)eps, pre.bc.data_ptr(), pre.dt.data_ptr<float>(), pre.adt.data_ptr<float>(),
                      pre.sig.data_ptr<float>(), pre.rate.data_ptr<float>(), stream());
+  if (!totals) return pre;
   pre.aend = at::empty({B, nh, nc}, f32);
   pre.angtot = at::empty({B, nh, nc, M3_R}, f32);
   pre.theta0 = at::empty({B, nh, nc, M3_R}, f32);
@@ -80,20 +81,54 @@ M3Pre m3_prepare(const at::Tensor& proj, int64_t B, int64_t L, int64_t nh, const
   return pre;
 }
 
-// y = ssd(proj); returns (y, states) -- states is the S_in of every chunk (bf16)
+// status word of the tcgen05 SSD kernels on each device (1 once a bounded wait gave up)
+at::Tensor m3_status(const at::Tensor& like) {
+  static std::vector<at::Tensor> per_dev(64);
+  const int d = like.device().index();
+  if (!per_dev[d].defined()) per_dev[d] = at::zeros({1}, like.options().dtype(at::kInt));
+  return per_dev[d];
+}
+bool g_m3_tc = true;   // the tcgen05 chunk walker (false: the chunk-parallel mma.sync kernels)
+
+// y = ssd(proj); returns (y, states, final state, final angle[, prep...]).  With the walker the
+// prep is (bc, dt, adt, sig, rate, theta0) and `states` holds the S_in images for the backward.
 std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh, at::Tensor wB, at::Tensor wC,
                                at::Tensor dt_bias, at::Tensor Bb, at::Tensor Cb, at::Tensor D, double A_floor,
                                double eps, bool want_final = false, bool return_prep = false) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
-  M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps);
+  M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps, !g_m3_tc);
   int nc = m3_nchunks((int)L);
-  auto states = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
-  M3Scan s = m3_scan(proj, pre, Bb, Cb, D);
   at::Tensor fin, thf;
   if (want_final) fin = at::empty({B, nh, M3_P, M3_N}, proj.options().dtype(at::kFloat));
-  m3_states_launch(g, s, states.data_ptr(), stream(), want_final ? fin.data_ptr<float>() : nullptr);
   auto y = at::empty({B, L, nh * M3_P}, proj.options());
+  if (g_m3_tc) {
+    if (want_final) thf = at::empty({B, nh, M3_R}, proj.options().dtype(at::kFloat));
+    M3TcFwd f{};
+    f.proj = proj.data_ptr(); f.bc = pre.bc.data_ptr();
+    f.dt = pre.dt.data_ptr<float>(); f.adt = pre.adt.data_ptr<float>(); f.sig = pre.sig.data_ptr<float>();
+    f.rate = pre.rate.data_ptr<float>();
+    f.Bb = Bb.data_ptr<float>(); f.Cb = Cb.data_ptr<float>(); f.D = D.data_ptr<float>();
+    f.y = y.data_ptr();
+    f.fin = want_final ? fin.data_ptr<float>() : nullptr;
+    f.thf = want_final ? thf.data_ptr<float>() : nullptr;
+    f.status = m3_status(proj).data_ptr<int>();
+    f.B = (int)B; f.L = (int)L; f.nh = (int)nh; f.ldp = g.ldp; f.lds = (int)L;
+    at::Tensor states, theta0;
+    if (return_prep) {   // the S_in images and chunk-start angles the backward walks back over
+      states = at::empty({B, nh, nc, M3_N * M3_P}, proj.options());
+      theta0 = at::empty({B, nh, nc, M3_R}, proj.options().dtype(at::kFloat));
+      f.states = states.data_ptr();
+      f.theta0 = theta0.data_ptr<float>();
+    }
+    const int rc = m3_fwd_tc_launch(f, stream());
+    TORCH_CHECK(rc == 0, "m3_fwd_tc launch failed (", rc, ")");
+    if (return_prep) return {y, states, fin, thf, pre.bc, pre.dt, pre.adt, pre.sig, pre.rate, theta0};
+    return {y, states, fin, thf};
+  }
+  auto states = at::empty({B, nh, nc, M3_P, M3_N}, proj.options());
+  M3Scan s = m3_scan(proj, pre, Bb, Cb, D);
+  m3_states_launch(g, s, states.data_ptr(), stream(), want_final ? fin.data_ptr<float>() : nullptr);
   m3_scan_launch(g, s, states.data_ptr(), y.data_ptr(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (want_final) {
@@ -106,6 +141,60 @@ std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh
   return {y, states, fin, thf};
 }
 
+// backward through the tcgen05 chunk walker; saved: the forward's (states, [bc, dt, adt, sig, rate, theta0])
+std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias,
+                                  at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B, int64_t L, int64_t nh,
+                                  double A_floor, double eps, c10::optional<at::Tensor> saved_states,
+                                  c10::optional<std::vector<at::Tensor>> saved_prep) {
+  M3Geo g = m3_geo(proj, B, L, nh);
+  const int nc = m3_nchunks((int)L);
+  at::Tensor bc, dt, adt, sig, rate, theta0, states;
+  if (saved_prep.has_value() && saved_prep->size() == 6 && saved_states.has_value() && saved_states->defined()) {
+    const auto& v = *saved_prep;
+    bc = v[0]; dt = v[1]; adt = v[2]; sig = v[3]; rate = v[4]; theta0 = v[5];
+    states = *saved_states;
+    req(bc, at::kBFloat16, "saved_prep bc");
+    req(states, at::kBFloat16, "saved_states");
+    TORCH_CHECK(bc.numel() == B * L * 2 * M3_N && dt.numel() == B * nh * L && theta0.numel() == B * nh * nc * M3_R &&
+                    states.numel() == B * nh * nc * M3_N * M3_P,
+                "saved forward tensors do not match this call");
+  } else {   // recompute: the forward walker writes the images (its y is discarded)
+    auto fw = m3_fwd(proj, B, L, nh, wB, wC, dt_bias, Bb, Cb, D, A_floor, eps, false, true);
+    states = fw[1]; bc = fw[4]; dt = fw[5]; adt = fw[6]; sig = fw[7]; rate = fw[8]; theta0 = fw[9];
+  }
+  auto f32 = proj.options().dtype(at::kFloat);
+  auto dproj = at::empty_like(proj);
+  auto gQ = at::empty({B * L, nh, M3_N}, proj.options());
+  auto gK = at::empty({B * L, nh, M3_N}, proj.options());
+  auto dthl = at::empty({B * L, nh, M3_R}, f32);
+  auto dthtot = at::empty({B, nh, nc, M3_R}, f32);
+  auto dgam = at::empty({B, nh, L}, f32), dscl = at::empty({B, nh, L}, f32), dadt = at::empty({B, nh, L}, f32);
+  auto dD = at::empty({B, nh}, f32), dCb = at::empty({B, nh, M3_N}, f32), dBb = at::empty({B, nh, M3_N}, f32);
+  M3TcBwd f{};
+  f.proj = proj.data_ptr(); f.bc = bc.data_ptr(); f.dy = dy.data_ptr();
+  f.dt = dt.data_ptr<float>(); f.adt = adt.data_ptr<float>(); f.sig = sig.data_ptr<float>();
+  f.rate = rate.data_ptr<float>();
+  f.Bb = Bb.data_ptr<float>(); f.Cb = Cb.data_ptr<float>(); f.D = D.data_ptr<float>();
+  f.states = states.data_ptr(); f.theta0 = theta0.data_ptr<float>();
+  f.dproj = dproj.data_ptr(); f.gQ = gQ.data_ptr(); f.gK = gK.data_ptr();
+  f.dthl = dthl.data_ptr<float>(); f.dthtot = dthtot.data_ptr<float>(); f.dgam = dgam.data_ptr<float>();
+  f.dscl = dscl.data_ptr<float>(); f.dadt = dadt.data_ptr<float>();
+  f.dD = dD.data_ptr<float>(); f.dCb = dCb.data_ptr<float>(); f.dBb = dBb.data_ptr<float>();
+  f.status = m3_status(proj).data_ptr<int>();
+  f.B = (int)B; f.L = (int)L; f.nh = (int)nh; f.ldp = g.ldp; f.lds = (int)L;
+  const int rc = m3_bwd_tc_launch(f, stream());
+  TORCH_CHECK(rc == 0, "m3_bwd_tc launch failed (", rc, ")");
+  m3_rev_carry_launch(g, dthtot.data_ptr<float>(), stream());
+  auto dwB = at::zeros({M3_N}, f32), dwC = at::zeros({M3_N}, f32), ddtb = at::zeros({nh}, f32);
+  m3_prep_bwd_launch(g, proj.data_ptr(), wB.data_ptr<float>(), wC.data_ptr<float>(), dt_bias.data_ptr<float>(),
+                     (float)A_floor, (float)eps, gQ.data_ptr(), gK.data_ptr(), dthl.data_ptr<float>(),
+                     dthtot.data_ptr<float>(), dgam.data_ptr<float>(), dscl.data_ptr<float>(),
+                     dadt.data_ptr<float>(), dproj.data_ptr(), dwB.data_ptr<float>(), dwC.data_ptr<float>(),
+                     ddtb.data_ptr<float>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dproj, dwB, dwC, ddtb, dD.sum(0), dCb.sum(0), dBb.sum(0)};
+}
+
 std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias,
                                at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B, int64_t L, int64_t nh,
                                double A_floor, double eps, c10::optional<at::Tensor> saved_states,
@@ -113,6 +202,7 @@ std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
   req(dy, at::kBFloat16, "dy");
+  if (g_m3_tc) return m3_bwd_tc(proj, dy, wB, wC, dt_bias, Bb, Cb, D, B, L, nh, A_floor, eps, saved_states, saved_prep);
   M3Pre pre;
   if (saved_prep.has_value() && saved_prep->size() == 7) {   // (bc, dt, adt, sig, rate, aend, theta0) of m3_fwd
     const auto& v = *saved_prep;
@@ -896,6 +986,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("eng_process", &eng_process, "batched matching engine: apply [B, M, 8] messages, one warp per book");
   m.def("eng_l2", &eng_l2, "batched L2 extraction");
   m.def("m3_use_tc_scan", [](bool on) { m3_use_tc_scan(on ? 1 : 0); }, "select the tcgen05 chunk-scan kernel");
+  m.def("m3_use_tc", [](bool on) { g_m3_tc = on; }, "select the tcgen05 chunk walker for the Mamba3 SSD");
+  m.def("m3_tc_status", [](at::Tensor like) { return m3_status(like); },
+        "status word of the tcgen05 SSD kernels on the tensor's device (nonzero: a bounded wait gave up)");
   m.def("m3_tc_error", []() { return m3_tc_error(); }, "nonzero if a tcgen05 bounded wait timed out");
   m.def("dp_fused_adam", &dp_fused_adam, "fused reduce-scatter + AdamW + all-gather over peer memory");
   m.def("gen_apply", &gen_apply, "generation: decode message tokens, match, L2 and next book image");

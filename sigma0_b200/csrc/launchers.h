@@ -27,6 +27,40 @@ struct M3BwdOut {
   float *dD, *dCb, *dBb;
 };
 int m3_nchunks(int L);
+
+// tcgen05 chunk walker (mamba3_tc.cu): the whole SSD forward / backward in one kernel each
+struct M3TcFwd {
+  const void* proj;                         // [B, L, ldp] bf16
+  const void* bc;                           // [B, L, 2N] bf16 (BCNorm'd B | C)
+  const float *dt, *adt, *sig;              // [B, nh, lds]
+  const float* rate;                        // [B, L, R]
+  const float *Bb, *Cb, *D;
+  void* y;                                  // [B, L, nh * P] bf16
+  void* states;                             // [B, nh, nc] swizzled bf16 S_in images (backward) or null
+  float* theta0;                            // [B, nh, nc, R] or null
+  const float* s0;                          // [B, nh, P, N] initial state or null
+  const float* th_in;                       // [B, nh, R] initial angle or null
+  float* fin;                               // [B, nh, P, N] final state or null
+  float* thf;                               // [B, nh, R] final angle or null
+  int* status;                              // set to 1 when a bounded wait gave up
+  int B, L, nh, ldp, lds;
+};
+int m3_fwd_tc_launch(const M3TcFwd& f, cudaStream_t st);   // 0, -3 (alignment), -4 (tensor map), CUDA error
+struct M3TcBwd {
+  const void *proj, *bc, *dy;               // dy: [B, L, nh * P] bf16
+  const float *dt, *adt, *sig, *rate, *Bb, *Cb, *D;
+  const void* states;                       // the forward's S_in images
+  const float* theta0;                      // the forward's chunk-start angles [B, nh, nc, R]
+  const float* ds_fin;                      // [B, nh, P, N] gradient of the final state or null
+  float* ds0;                               // [B, nh, P, N] gradient of the initial state or null
+  void* dproj;                              // [B, L, ldp] bf16: z and x columns written
+  void *gQ, *gK;                            // [B, L, nh * N] bf16
+  float *dthl, *dthtot, *dgam, *dscl, *dadt;
+  float *dD, *dCb, *dBb;                    // [B, nh], [B, nh, N], [B, nh, N]
+  int* status;
+  int B, L, nh, ldp, lds;
+};
+int m3_bwd_tc_launch(const M3TcBwd& f, cudaStream_t st);
 void m3_prep_fwd_launch(const M3Geo& g, const void* proj, const float* wB, const float* wC,
                         const float* dt_bias, float A_floor, float eps, void* bc, float* dt, float* adt,
                         float* sig, float* rate, cudaStream_t st);
@@ -38,6 +72,7 @@ void m3_scan_launch(const M3Geo& g, const M3Scan& s, const void* states, void* y
 void m3_dstates_launch(const M3Geo& g, const M3Scan& s, const void* dy, void* U, cudaStream_t st);
 void m3_chunk_bwd_launch(const M3Geo& g, const M3Scan& s, const void* dy, const void* states, const void* dsout,
                          const M3BwdOut& o, cudaStream_t st);
+void m3_rev_carry_launch(const M3Geo& g, float* dthtot, cudaStream_t st);   // exclusive reverse scan over chunks
 void m3_prep_bwd_launch(const M3Geo& g, const void* proj, const float* wB, const float* wC,
                         const float* dt_bias, float A_floor, float eps, const void* gQ, const void* gK,
                         const float* dthl, const float* dthc, const float* dgam, const float* dscl,

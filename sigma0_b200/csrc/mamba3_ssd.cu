@@ -1768,6 +1768,11 @@ void m3_chunk_bwd_launch(const M3Geo& G, const M3Scan& S, const void* dy, const 
   m3_rev_carry<<<g.B * g.nh, 32, 0, st>>>(O.dthtot, g);
 }
 
+void m3_rev_carry_launch(const M3Geo& G, float* dthtot, cudaStream_t st) {
+  Geo g = make_geo(G);
+  m3_rev_carry<<<g.B * g.nh, 32, 0, st>>>(dthtot, g);
+}
+
 void m3_prep_bwd_launch(const M3Geo& G, const void* proj, const float* wB, const float* wC,
                         const float* dt_bias, float A_floor, float eps, const void* gQ, const void* gK,
                         const float* dthl, const float* dthc, const float* dgam, const float* dscl,

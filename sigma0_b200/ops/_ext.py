@@ -13,7 +13,7 @@ from __future__ import annotations
 _C = None
 _COUNT = [0]
 # kernels launched per call, where it is not one
-_LAUNCHES = {"m3_fwd": 6, "m3_bwd": 10, "ln_bwd": 2, "rms_bwd": 2, "glu_res_bwd": 2, "attn_bwd": 2, "s5_scan_fwd": 3, "s5_scan_bwd": 3}
+_LAUNCHES = {"m3_fwd": 2, "m3_bwd": 5, "ln_bwd": 2, "rms_bwd": 2, "glu_res_bwd": 2, "attn_bwd": 2, "s5_scan_fwd": 3, "s5_scan_bwd": 3}
 
 
 class _Counted:
@@ -25,7 +25,7 @@ class _Counted:
         k = _LAUNCHES.get(name, 1)
 
         def call(*a, **kw):
-            # m3_bwd skips the state recompute (2 kernels) when given the forward's states
+            # m3_bwd skips the forward recompute (2 kernels) when given the forward's states
             _COUNT[0] += k - (2 if name == "m3_bwd" and kw.get("saved_states") is not None else 0)
             return fn(*a, **kw)
         return call

@@ -102,7 +102,7 @@ class _Mamba3Core:
         dyn = do @ w_out.t()
         dy, g_out_norm = C.rms_bwd(dyn.contiguous(), y2, m.out_norm.scale, yr)
         saved_states = states[0] if states else None
-        saved_prep = list(states[1:]) if states and len(states) == 8 else None
+        saved_prep = list(states[1:]) if states and len(states) in (7, 8) else None
         dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_bwd(
             proj, dy, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D, B, L,
             d.n_heads, m.A_floor, m.B_norm.eps, saved_states=saved_states, saved_prep=saved_prep)

@@ -51,6 +51,69 @@ def test_ssd_forward_matches_oracle(L):
     assert rel(y, yr) < 2e-2, rel(y, yr)
 
 
+def _walker_args(B, L, H, seed):
+    m = _layer(H=H, seed=seed)
+    d = m.dims
+    ldp = (d.d_in_proj + 7) // 8 * 8
+    proj = (torch.randn(B * L, ldp, device="cuda") * 0.5).to(torch.bfloat16)
+    proj[:, d.d_in_proj:] = 0
+    return m, d, proj
+
+
+@pytest.mark.parametrize("B,L,H", [(2, 64, 512), (3, 200, 512), (1, 1000, 256), (2, 4100, 512)])
+def test_ssd_forward_walker_matches_chunk_parallel_kernels(B, L, H):
+    """The tcgen05 chunk walker against the chunk-parallel kernels: y, final state and angle."""
+    from sigma0_b200.ops._ext import ext
+    C = ext()
+    m, d, proj = _walker_args(B, L, H, 2)
+    args = (proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D,
+            m.A_floor, 1e-6, True)
+    st = C.m3_tc_status(proj)
+    st.zero_()
+    try:
+        C.m3_use_tc(False)
+        y0, _, f0, th0 = C.m3_fwd(*args)[:4]
+        C.m3_use_tc(True)
+        y1, _, f1, th1 = C.m3_fwd(*args)[:4]
+    finally:
+        C.m3_use_tc(True)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert torch.isfinite(y1.float()).all()
+    assert rel(y1, y0) < 1e-2, rel(y1, y0)
+    assert rel(f1, f0) < 1e-2, rel(f1, f0)
+    dth = torch.remainder(th1 - th0 + 3.14159265, 2 * 3.14159265) - 3.14159265
+    assert dth.abs().max().item() < 1e-3
+
+
+@pytest.mark.parametrize("B,L,H", [(2, 64, 512), (3, 200, 512), (1, 1000, 256), (2, 2100, 512)])
+def test_ssd_backward_walker_matches_chunk_parallel_kernels(B, L, H):
+    """The reverse tcgen05 walker (given the forward walker's saved images) against the
+    chunk-parallel backward kernels: every output of m3_bwd."""
+    from sigma0_b200.ops._ext import ext
+    C = ext()
+    m, d, proj = _walker_args(B, L, H, 3)
+    dy = torch.randn(B, L, d.d_inner, device="cuda").to(torch.bfloat16)
+    common = (m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D)
+    st = C.m3_tc_status(proj)
+    st.zero_()
+    try:
+        C.m3_use_tc(False)
+        ref = C.m3_bwd(proj, dy, *common, B, L, d.n_heads, m.A_floor, 1e-6)
+        C.m3_use_tc(True)
+        out = C.m3_fwd(proj, B, L, d.n_heads, *common, m.A_floor, 1e-6, False, True)
+        got = C.m3_bwd(proj, dy, *common, B, L, d.n_heads, m.A_floor, 1e-6, saved_states=out[1],
+                       saved_prep=list(out[4:]))
+    finally:
+        C.m3_use_tc(True)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    names = ["dproj", "dwB", "dwC", "ddt_bias", "dD", "dC_bias", "dB_bias"]
+    for name, a, b in zip(names, got, ref):
+        assert torch.isfinite(a.float()).all(), name
+        assert rel(a, b) < 2e-2, (name, rel(a, b))
+
+
 @pytest.mark.parametrize("L", [128, 150, 700])
 def test_ssd_backward_matches_oracle(L):
     from sigma0_b200.ops._ext import ext
