@@ -306,7 +306,7 @@ def test_ssd_backward_with_saved_forward_tensors_matches_recompute():
     dy = torch.randn(B, L, d.d_inner, device="cuda").to(torch.bfloat16)
     args = (m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D)
     out = C.m3_fwd(proj, B, L, d.n_heads, *args, m.A_floor, 1e-6, return_prep=True)
-    assert len(out) == 11
+    assert len(out) == 10            # y, states, final state, final angle, 6 prep tensors
     full = C.m3_bwd(proj, dy, *args, B, L, d.n_heads, m.A_floor, 1e-6)
     saved = C.m3_bwd(proj, dy, *args, B, L, d.n_heads, m.A_floor, 1e-6, saved_states=out[1],
                      saved_prep=list(out[4:]))
