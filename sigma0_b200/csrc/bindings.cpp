@@ -5,6 +5,8 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <algorithm>
+#include <cstdlib>
 #include <vector>
 
 #include "launchers.h"
@@ -90,6 +92,26 @@ at::Tensor m3_status(const at::Tensor& like) {
 }
 bool g_m3_tc = true;   // the tcgen05 chunk walker (false: the chunk-parallel mma.sync kernels)
 
+// Segments per sequence for the walkers: one CTA walks one (sequence, head, segment).  With
+// fewer (sequence, head) pairs than CTA slots (two per SM forward, one backward) each sequence
+// is cut into segments that are walked in parallel from a zero state; a second pass re-walks
+// every segment but the first (forward) / last (backward) from its true carried state.
+int m3_segments(const at::Tensor& like, int64_t B, int64_t nh, int nc, int per_sm) {
+  const char* e = getenv("S0_M3_SEGMENTS");
+  int64_t want = e ? atoi(e) : (int64_t)per_sm * num_sms(like) / std::max<int64_t>(1, B * nh);
+  want = std::max<int64_t>(1, std::min<int64_t>(want, nc));
+  if (want <= 1) return 1;
+  const int cps = (int)((nc + want - 1) / want);
+  return (nc + cps - 1) / cps;
+}
+
+// per-segment totals of the decay ADT: [B, nh, nseg]
+at::Tensor m3_segment_decay(const at::Tensor& adt, int64_t B, int64_t nh, int64_t L, int nseg, int cps) {
+  const int64_t span = (int64_t)cps * 64;
+  auto a = at::constant_pad_nd(adt.view({B, nh, L}), {0, span * nseg - L});
+  return a.view({B, nh, nseg, span}).sum(-1);
+}
+
 // y = ssd(proj); returns (y, states, final state, final angle[, prep...]).  With the walker the
 // prep is (bc, dt, adt, sig, rate, theta0) and `states` holds the S_in images for the backward.
 std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh, at::Tensor wB, at::Tensor wC,
@@ -121,8 +143,44 @@ std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh
       f.states = states.data_ptr();
       f.theta0 = theta0.data_ptr<float>();
     }
-    const int rc = m3_fwd_tc_launch(f, stream());
-    TORCH_CHECK(rc == 0, "m3_fwd_tc launch failed (", rc, ")");
+    const int nseg = m3_segments(proj, B, nh, nc, 2);
+    if (nseg == 1) {
+      const int rc = m3_fwd_tc_launch(f, stream());
+      TORCH_CHECK(rc == 0, "m3_fwd_tc launch failed (", rc, ")");
+    } else {
+      const int cps = (nc + nseg - 1) / nseg;
+      auto f32 = proj.options().dtype(at::kFloat);
+      // segment start angles from the chunk angle carries; segment decay totals
+      M3Geo g2 = g;
+      auto aend = at::empty({B, nh, nc}, f32), angtot = at::empty({B, nh, nc, M3_R}, f32);
+      auto th0all = at::empty({B, nh, nc, M3_R}, f32);
+      M3Scan s0s = m3_scan(proj, pre, dt_bias, dt_bias, dt_bias);
+      m3_chunk_totals_launch(g2, s0s, aend.data_ptr<float>(), angtot.data_ptr<float>(), th0all.data_ptr<float>(),
+                             stream());
+      auto th_in = th0all.slice(2, 0, nc, cps).contiguous();                       // [B, nh, nseg, R]
+      auto adec = aend.view({B, nh, nc});
+      auto segA = at::constant_pad_nd(adec, {0, (int64_t)nseg * cps - nc}).view({B, nh, nseg, cps}).sum(-1);
+      auto fseg = at::empty({B, nh, nseg, M3_P, M3_N}, f32);
+      auto thseg = at::empty({B, nh, nseg, M3_R}, f32);
+      f.nseg = nseg;
+      f.th_in = th_in.data_ptr<float>();
+      f.fin = fseg.data_ptr<float>();
+      f.thf = thseg.data_ptr<float>();
+      int rc = m3_fwd_tc_launch(f, stream());                                      // pass 1: zero starts
+      TORCH_CHECK(rc == 0, "m3_fwd_tc launch failed (", rc, ")");
+      auto s_in = at::zeros_like(fseg);
+      for (int k = 1; k < nseg; ++k)
+        s_in.select(2, k).copy_(segA.select(2, k - 1).exp().unsqueeze(-1).unsqueeze(-1) * s_in.select(2, k - 1) +
+                                fseg.select(2, k - 1));
+      f.s0 = s_in.data_ptr<float>();
+      f.seg_lo = 1;
+      rc = m3_fwd_tc_launch(f, stream());                                           // pass 2: true starts
+      TORCH_CHECK(rc == 0, "m3_fwd_tc launch failed (", rc, ")");
+      if (want_final) {
+        fin.copy_(fseg.select(2, nseg - 1));
+        thf.copy_(thseg.select(2, nseg - 1));
+      }
+    }
     if (return_prep) return {y, states, fin, thf, pre.bc, pre.dt, pre.adt, pre.sig, pre.rate, theta0};
     return {y, states, fin, thf};
   }
@@ -169,7 +227,9 @@ std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB,
   auto dthl = at::empty({B * L, nh, M3_R}, f32);
   auto dthtot = at::empty({B, nh, nc, M3_R}, f32);
   auto dgam = at::empty({B, nh, L}, f32), dscl = at::empty({B, nh, L}, f32), dadt = at::empty({B, nh, L}, f32);
-  auto dD = at::empty({B, nh}, f32), dCb = at::empty({B, nh, M3_N}, f32), dBb = at::empty({B, nh, M3_N}, f32);
+  const int nseg = m3_segments(proj, B, nh, nc, 1);
+  auto dD = at::empty({B, nh, nseg}, f32), dCb = at::empty({B, nh, nseg, M3_N}, f32),
+       dBb = at::empty({B, nh, nseg, M3_N}, f32);
   M3TcBwd f{};
   f.proj = proj.data_ptr(); f.bc = bc.data_ptr(); f.dy = dy.data_ptr();
   f.dt = dt.data_ptr<float>(); f.adt = adt.data_ptr<float>(); f.sig = sig.data_ptr<float>();
@@ -182,8 +242,27 @@ std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB,
   f.dD = dD.data_ptr<float>(); f.dCb = dCb.data_ptr<float>(); f.dBb = dBb.data_ptr<float>();
   f.status = m3_status(proj).data_ptr<int>();
   f.B = (int)B; f.L = (int)L; f.nh = (int)nh; f.ldp = g.ldp; f.lds = (int)L;
-  const int rc = m3_bwd_tc_launch(f, stream());
-  TORCH_CHECK(rc == 0, "m3_bwd_tc launch failed (", rc, ")");
+  f.nseg = nseg;
+  if (nseg == 1) {
+    const int rc = m3_bwd_tc_launch(f, stream());
+    TORCH_CHECK(rc == 0, "m3_bwd_tc launch failed (", rc, ")");
+  } else {
+    const int cps = (nc + nseg - 1) / nseg;
+    auto segA = m3_segment_decay(adt, B, nh, L, nseg, cps);
+    auto ds0 = at::empty({B, nh, nseg, M3_P, M3_N}, f32);
+    f.ds0 = ds0.data_ptr<float>();
+    int rc = m3_bwd_tc_launch(f, stream());                                        // pass 1: zero ends
+    TORCH_CHECK(rc == 0, "m3_bwd_tc launch failed (", rc, ")");
+    auto dend = at::zeros_like(ds0);
+    for (int k = nseg - 2; k >= 0; --k)
+      dend.select(2, k).copy_(segA.select(2, k + 1).exp().unsqueeze(-1).unsqueeze(-1) * dend.select(2, k + 1) +
+                              ds0.select(2, k + 1));
+    f.ds_fin = dend.data_ptr<float>();
+    f.ds0 = nullptr;
+    f.seg_hi = nseg - 1;
+    rc = m3_bwd_tc_launch(f, stream());                                             // pass 2: true ends
+    TORCH_CHECK(rc == 0, "m3_bwd_tc launch failed (", rc, ")");
+  }
   m3_rev_carry_launch(g, dthtot.data_ptr<float>(), stream());
   auto dwB = at::zeros({M3_N}, f32), dwC = at::zeros({M3_N}, f32), ddtb = at::zeros({nh}, f32);
   m3_prep_bwd_launch(g, proj.data_ptr(), wB.data_ptr<float>(), wC.data_ptr<float>(), dt_bias.data_ptr<float>(),
@@ -192,7 +271,8 @@ std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB,
                      dadt.data_ptr<float>(), dproj.data_ptr(), dwB.data_ptr<float>(), dwC.data_ptr<float>(),
                      ddtb.data_ptr<float>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {dproj, dwB, dwC, ddtb, dD.sum(0), dCb.sum(0), dBb.sum(0)};
+  return {dproj, dwB, dwC, ddtb, dD.sum(at::IntArrayRef{0, 2}), dCb.sum(at::IntArrayRef{0, 2}),
+          dBb.sum(at::IntArrayRef{0, 2})};
 }
 
 std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias,

@@ -44,8 +44,9 @@ struct M3TcFwd {
   float* thf;                               // [B, nh, R] final angle or null
   int* status;                              // set to 1 when a bounded wait gave up
   int B, L, nh, ldp, lds;
+  int nseg = 1, seg_lo = 0, seg_hi = 0;     // segments per sequence; walk segments [lo, hi) (hi 0: all)
 };
-int m3_fwd_tc_launch(const M3TcFwd& f, cudaStream_t st);   // 0, -3 (alignment), -4 (tensor map), CUDA error
+int m3_fwd_tc_launch(const M3TcFwd& f, cudaStream_t st);   // 0, -3 (alignment), -4 (tensor map), -5 (segments), CUDA error
 struct M3TcBwd {
   const void *proj, *bc, *dy;               // dy: [B, L, nh * P] bf16
   const float *dt, *adt, *sig, *rate, *Bb, *Cb, *D;
@@ -59,6 +60,7 @@ struct M3TcBwd {
   float *dD, *dCb, *dBb;                    // [B, nh], [B, nh, N], [B, nh, N]
   int* status;
   int B, L, nh, ldp, lds;
+  int nseg = 1, seg_lo = 0, seg_hi = 0;
 };
 int m3_bwd_tc_launch(const M3TcBwd& f, cudaStream_t st);
 void m3_prep_fwd_launch(const M3Geo& g, const void* proj, const float* wB, const float* wC,

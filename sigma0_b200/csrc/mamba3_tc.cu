@@ -72,12 +72,13 @@ struct FwdArgs {
   const float *Bb, *Cb, *D;
   bf16* states;                            // [B, nh, nc] images of S_in (16 KB each) or null
   float* theta0;                           // [B, nh, nc, R] angle at each chunk start, or null
-  const float* s0;                         // [B, nh, P, N] initial state or null
-  const float* th_in;                      // [B, nh, R] initial angle or null
-  float* fin;                              // [B, nh, P, N] final state or null
-  float* thf;                              // [B, nh, R] final angle or null
+  const float* s0;                         // [B, nh, nseg, P, N] initial state of each segment or null
+  const float* th_in;                      // [B, nh, nseg, R] initial angle of each segment or null
+  float* fin;                              // [B, nh, nseg, P, N] final state of each segment or null
+  float* thf;                              // [B, nh, nseg, R] final angle of each segment or null
   int* status;
   int B, L, nh, ldp, lds, nc;
+  int cps, nseg, seg_lo, seg_hi;           // chunks per segment; this launch walks segments [lo, hi)
 };
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk16) {   // byte offset in an SW128 tile
@@ -89,11 +90,11 @@ __device__ __forceinline__ uint32_t frag_off(int row, int col) {   // bf16 (row,
 
 __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t ph) { return tc::mbar_wait(bar, ph, WAIT_LIMIT); }
 
-// loads of chunk c into stage c & 1 (V, rates, scalars); warp 0 calls it (all 32 lanes)
+// loads of chunk c (the i-th of this walk) into stage i & 1 (V, rates, scalars); warp 0 calls it
 __device__ __forceinline__ void load_stage(Smem& sm, const FwdArgs& a, const CUtensorMap* tm_proj, int b, int h,
-                                           int c, int lane) {
-  Stage& st = sm.stage[c & 1];
-  uint64_t* bar = &sm.vs_full[c & 1];
+                                           int c, int i, int lane) {
+  Stage& st = sm.stage[i & 1];
+  uint64_t* bar = &sm.vs_full[i & 1];
   const int t0 = c * CS;
   if (lane == 0) {
     tc::mbar_expect_tx(bar, BOX);
@@ -123,8 +124,10 @@ __global__ void __launch_bounds__(NT, 2)
   extern __shared__ unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024 - (tc::smem_u32(smem_raw) & 1023)) & 1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.x, b = bh / a.nh, h = bh % a.nh;
-  const int nc = a.nc;
+  const int nsl = a.seg_hi - a.seg_lo;
+  const int bh = blockIdx.x / nsl, seg = a.seg_lo + blockIdx.x % nsl, b = bh / a.nh, h = bh % a.nh;
+  const size_t slot = (size_t)bh * a.nseg + seg;          // this (sequence, head, segment)
+  const int nc = a.nc, cb = seg * a.cps, ce = min(nc, cb + a.cps);
 
   if (warp == 0) tc::tmem_alloc(&sm.tslot, TM_COLS);
   if (tid == 0) {
@@ -139,7 +142,7 @@ __global__ void __launch_bounds__(NT, 2)
     sm.cb[i] = a.Cb[h * N + i];
     sm.bb[i] = a.Bb[h * N + i];
   }
-  if (tid < R) sm.th[tid] = a.th_in ? a.th_in[(size_t)bh * R + tid] : 0.f;
+  if (tid < R) sm.th[tid] = a.th_in ? a.th_in[slot * R + tid] : 0.f;
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(NT, 2)
     float v[32];
     const int n = 32 * q + lane;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = a.s0[((size_t)bh * P + 32 * half + j) * N + n];
+    for (int j = 0; j < 32; ++j) v[j] = a.s0[(slot * P + 32 * half + j) * N + n];
     tc::tmem_st32(tmem + lane_base + TM_ST + 32 * half, v);
     tc::tmem_wait_st();
   }
@@ -170,21 +173,21 @@ __global__ void __launch_bounds__(NT, 2)
     if (lane == 0) {
       tc::mbar_expect_tx(&sm.bc_full, 4 * BOX);
       for (int k = 0; k < 4; ++k)
-        tc::tma_load_3d((k < 2 ? sm.bn : sm.cn) + (k & 1) * BOX, &tm_bc, 64 * k, 0, b, &sm.bc_full);
+        tc::tma_load_3d((k < 2 ? sm.bn : sm.cn) + (k & 1) * BOX, &tm_bc, 64 * k, cb * CS, b, &sm.bc_full);
     }
-    load_stage(sm, a, &tm_proj, b, h, 0, lane);
+    load_stage(sm, a, &tm_proj, b, h, cb, 0, lane);
   }
   const float Dh = a.D[h];
   bool ok = true;
   bool store_pending = false;                             // thread 0: bulk stores in flight
   int bc_loads = 1, vs_loads = 1;                         // loads issued so far (chunk count)
 
-  for (int c = 0; c < nc; ++c) {
-    const int t0 = c * CS;
-    Stage& st = sm.stage[c & 1];
-    ok = wait(&sm.vs_full[c & 1], (c >> 1) & 1) && ok;
-    if (warp == 0 && c + 1 < nc) load_stage(sm, a, &tm_proj, b, h, c + 1, lane);
-    if (c + 1 < nc) vs_loads = c + 2;
+  for (int c = cb; c < ce; ++c) {
+    const int t0 = c * CS, i = c - cb;                   // i: position in this walk
+    Stage& st = sm.stage[i & 1];
+    ok = wait(&sm.vs_full[i & 1], (i >> 1) & 1) && ok;
+    if (warp == 0 && c + 1 < ce) load_stage(sm, a, &tm_proj, b, h, c + 1, i + 1, lane);
+    if (c + 1 < ce) vs_loads = i + 2;
     // ---- B: row scalars and rotary angles ------------------------------------------------
     if (tid < CS) {
       const float d0 = st.dt[tid], s0_ = st.sig[tid], d1 = st.dt[tid + 1], s1 = st.sig[tid + 1];
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(NT, 2)
     if (a.theta0 && tid < R) a.theta0[((size_t)bh * nc + c) * R + tid] = sm.th[tid];
     __syncthreads();
     const float cend = sm.cum[CS - 1];
-    ok = wait(&sm.bc_full, c & 1) && ok;
+    ok = wait(&sm.bc_full, i & 1) && ok;
     // ---- C: Q, K in place; qk diagonal; w * V --------------------------------------------
     // warps 0-3 take the rotated columns (box 0), warps 4-7 the rest, so no warp diverges on
     // the rotation; each thread keeps one 8-column chunk (its biases live in registers)
@@ -291,7 +294,7 @@ __global__ void __launch_bounds__(NT, 2)
     {
       const int n = 32 * q + lane;
       float v[32];
-      if (c > 0 || a.s0) {
+      if (i > 0 || a.s0) {
         tc::fence_after_sync();
         tc::tmem_ld32(tmem + lane_base + TM_ST + 32 * half, v);
       } else {
@@ -303,7 +306,7 @@ __global__ void __launch_bounds__(NT, 2)
         *reinterpret_cast<uint4*>(sm.sin_ + swz(n, 4 * half + j)) =
             make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
                        pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
-      if (c > 0 || a.s0) {
+      if (i > 0 || a.s0) {
         const float e = __expf(cend);
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] *= e;
@@ -336,18 +339,18 @@ __global__ void __launch_bounds__(NT, 2)
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         tc::mma_bf16(tmem + TM_ST, tc::desc_mn_sw128(sm.bn + ks * 2048, BOX),
-                     tc::desc_mn_sw128(sm.wv + ks * 2048, BOX), id128, ks > 0 || c > 0 || a.s0 != nullptr);
+                     tc::desc_mn_sw128(sm.wv + ks * 2048, BOX), id128, ks > 0 || i > 0 || a.s0 != nullptr);
       tc::commit(&sm.mma1);
     }
     // ---- G: P = masked decayed scores ---------------------------------------------------------
-    ok = wait(&sm.mma1, c & 1) && ok;
+    ok = wait(&sm.mma1, i & 1) && ok;
     tc::fence_after_sync();
-    if (tid == 0 && c + 1 < nc) {   // Q / K tiles consumed: fetch the next chunk's Bn | Cn
+    if (tid == 0 && c + 1 < ce) {   // Q / K tiles consumed: fetch the next chunk's Bn | Cn
       tc::mbar_expect_tx(&sm.bc_full, 4 * BOX);
       for (int k = 0; k < 4; ++k)
         tc::tma_load_3d((k < 2 ? sm.bn : sm.cn) + (k & 1) * BOX, &tm_bc, 64 * k, t0 + CS, b, &sm.bc_full);
     }
-    if (c + 1 < nc) bc_loads = c + 2;
+    if (c + 1 < ce) bc_loads = i + 2;
     if (tid == 0 && store_pending) tc::bulk_wait_read();   // last chunk's y store has read p
     __syncthreads();
     {
@@ -389,7 +392,7 @@ __global__ void __launch_bounds__(NT, 2)
         zr[2 * j + 1] = (t0 + r1 < a.L) ? *reinterpret_cast<const uint32_t*>(zb + (size_t)r1 * a.ldp + p) : 0u;
       }
     }
-    ok = wait(&sm.mma2, c & 1) && ok;
+    ok = wait(&sm.mma2, i & 1) && ok;
     tc::fence_after_sync();
     // ---- I: gated output -> swizzled tile -> TMA store -----------------------------------------
     {
@@ -432,9 +435,9 @@ __global__ void __launch_bounds__(NT, 2)
     tc::tmem_ld32(tmem + lane_base + TM_ST + 32 * half, v);
     const int n = 32 * q + lane;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) a.fin[((size_t)bh * P + 32 * half + j) * N + n] = v[j];
+    for (int j = 0; j < 32; ++j) a.fin[(slot * P + 32 * half + j) * N + n] = v[j];
   }
-  if (ok && a.thf && tid < R) a.thf[(size_t)bh * R + tid] = sm.th[tid];
+  if (ok && a.thf && tid < R) a.thf[slot * R + tid] = sm.th[tid];
   if (!ok && tid == 0) {
     // a wait gave up: let the copies this CTA started land (bounded) before its shared memory
     // goes away, then report
@@ -498,7 +501,7 @@ struct __align__(1024) BSmem {
   float qkp[2][CS];
   float seg[16 * 32], misc[16];
   float cb[N], bb[N];
-  uint64_t full[2], mma1, mma2, mma3;
+  uint64_t full[2], mma1, mma2, mma3, edge;
   uint32_t tslot;
 };
 static_assert(sizeof(BSmem) + 1024 <= 232448, "backward shared memory exceeds 227 KB");
@@ -509,12 +512,13 @@ struct BwdArgs {
   const float *Bb, *Cb, *D;
   const bf16* states;            // the forward's S_in images
   const float* theta0;           // the forward's chunk-start angles
-  const float* ds_fin;           // [B, nh, P, N] gradient of the final state, or null
-  float* ds0;                    // [B, nh, P, N] gradient of the initial state, or null
+  const float* ds_fin;           // [B, nh, nseg, P, N] gradient of each segment's final state, or null
+  float* ds0;                    // [B, nh, nseg, P, N] gradient of each segment's initial state, or null
   float *dthl, *dthtot, *dgam, *dscl, *dadt;
-  float *dD, *dCb, *dBb;         // [B, nh], [B, nh, N] x2
+  float *dD, *dCb, *dBb;         // [B, nh, nseg], [B, nh, nseg, N] x2 (partial sums per segment)
   int* status;
   int B, L, nh, ldp, lds, nc;
+  int cps, nseg, seg_lo, seg_hi;
 };
 
 __device__ __forceinline__ int dth_idx(int row, int r) { return row * R + (r ^ ((row & 7) << 2)); }
@@ -560,8 +564,10 @@ __global__ void __launch_bounds__(BNT, 1)
   extern __shared__ unsigned char smem_raw[];
   BSmem& sm = *reinterpret_cast<BSmem*>(smem_raw + ((1024 - (tc::smem_u32(smem_raw) & 1023)) & 1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.x, b = bh / a.nh, h = bh % a.nh;
-  const int nc = a.nc;
+  const int nsl = a.seg_hi - a.seg_lo;
+  const int bh = blockIdx.x / nsl, seg = a.seg_lo + blockIdx.x % nsl, b = bh / a.nh, h = bh % a.nh;
+  const size_t slot = (size_t)bh * a.nseg + seg;
+  const int nc = a.nc, cb = seg * a.cps, ce = min(nc, cb + a.cps), nw = ce - cb;
   const int rb = warp & 3, cq = warp >> 2, g = lane >> 2, tq = lane & 3;
   const int r0 = 16 * rb + g, r1 = r0 + 8, c16 = cq * 16;
 
@@ -572,6 +578,7 @@ __global__ void __launch_bounds__(BNT, 1)
     tc::mbar_init(&sm.mma1, 1);
     tc::mbar_init(&sm.mma2, 1);
     tc::mbar_init(&sm.mma3, 1);
+    tc::mbar_init(&sm.edge, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   for (int i = tid; i < N; i += BNT) {
@@ -597,11 +604,18 @@ __global__ void __launch_bounds__(BNT, 1)
     float v[16];
     const int n = 32 * rb + lane;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = a.ds_fin[((size_t)bh * P + c16 + j) * N + n];
+    for (int j = 0; j < 16; ++j) v[j] = a.ds_fin[(slot * P + c16 + j) * N + n];
     tc::tmem_st16(tmem + lane_base + TB_CAR + c16, v);
     tc::tmem_wait_st();
   }
-  if (warp == 0) bwd_load_stage(sm, a, &tm_bc, &tm_proj, &tm_dy, b, h, nc - 1, 0, lane);
+  if (warp == 0) bwd_load_stage(sm, a, &tm_bc, &tm_proj, &tm_dy, b, h, ce - 1, 0, lane);
+  // a segment that ends before the sequence does: S_out of its last chunk is the next chunk's
+  // S_in image, read for that chunk's d cum_end (into the second stage, free until chunk 2)
+  const bool edge = ce < nc;
+  if (edge && tid == 0) {
+    tc::mbar_expect_tx(&sm.edge, 2 * BOX);
+    tc::bulk_load(sm.stage[1].sin_, a.states + ((size_t)bh * nc + ce) * (N * P), 2 * BOX, &sm.edge);
+  }
   const float Dh = a.D[h];
   float colq[4][2], colk[4][2], dDacc = 0.f;
 #pragma unroll
@@ -609,8 +623,8 @@ __global__ void __launch_bounds__(BNT, 1)
   bool ok = true, store_pending = false;
   int loads = 1;
 
-  for (int j = 0; j < nc; ++j) {
-    const int c = nc - 1 - j, t0 = c * CS;
+  for (int j = 0; j < nw; ++j) {
+    const int c = ce - 1 - j, t0 = c * CS;
     BStage& st = sm.stage[j & 1];
     if (tid == 0 && store_pending) tc::bulk_wait_read();    // last chunk's stores have read their tiles
     if (tid < CS) {
@@ -744,7 +758,8 @@ __global__ void __launch_bounds__(BNT, 1)
             make_uint4(pack_bf16(v[8 * k], v[8 * k + 1]), pack_bf16(v[8 * k + 2], v[8 * k + 3]),
                        pack_bf16(v[8 * k + 4], v[8 * k + 5]), pack_bf16(v[8 * k + 6], v[8 * k + 7]));
       float dot = 0.f;
-      if (j > 0) {   // S_out(c) = S_in(c+1): the other stage still holds its image
+      if (j == 0 && edge) ok = wait(&sm.edge, 0) && ok;
+      if (j > 0 || edge) {   // S_out(c) = S_in(c+1): the other stage holds its image
         const unsigned char* so = sm.stage[(j + 1) & 1].sin_;
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
@@ -793,8 +808,8 @@ __global__ void __launch_bounds__(BNT, 1)
                      tc::desc_mn_sw128(sm.edy0 + ks * 2048, BOX), id128, ks > 0 || j > 0 || have_fin);
       tc::commit(&sm.mma1);
     }
-    if (warp == 0 && c > 0) bwd_load_stage(sm, a, &tm_bc, &tm_proj, &tm_dy, b, h, c - 1, j + 1, lane);
-    if (c > 0) loads = j + 2;
+    if (warp == 0 && c > cb) bwd_load_stage(sm, a, &tm_bc, &tm_proj, &tm_dy, b, h, c - 1, j + 1, lane);
+    if (c > cb) loads = j + 2;
     // ---- epilogue A: P, dS, d cum -------------------------------------------------------------
     ok = wait(&sm.mma1, j & 1) && ok;
     tc::fence_after_sync();
@@ -1088,7 +1103,7 @@ __global__ void __launch_bounds__(BNT, 1)
     tc::tmem_ld16(tmem + lane_base + TB_CAR + c16, v);
     const int n = 32 * rb + lane;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) a.ds0[((size_t)bh * P + c16 + k) * N + n] = v[k];
+    for (int k = 0; k < 16; ++k) a.ds0[(slot * P + c16 + k) * N + n] = v[k];
   }
   __syncthreads();
   float* colsum = sm.seg;   // [2][N] (dead scratch)
@@ -1119,14 +1134,15 @@ __global__ void __launch_bounds__(BNT, 1)
   }
   __syncthreads();
   if (ok) {
-    if (tid < N) a.dCb[(size_t)bh * N + tid] = colsum[tid];
-    else if (tid < 2 * N) a.dBb[(size_t)bh * N + tid - N] = colsum[tid];
-    if (tid == 0) a.dD[bh] = sm.misc[0];
+    if (tid < N) a.dCb[slot * N + tid] = colsum[tid];
+    else if (tid < 2 * N) a.dBb[slot * N + tid - N] = colsum[tid];
+    if (tid == 0) a.dD[slot] = sm.misc[0];
   }
   if (!ok && tid == 0) {
     const int l = loads - 1;
     wait(&sm.full[l & 1], (l >> 1) & 1);
     if (l >= 1) wait(&sm.full[(l - 1) & 1], ((l - 1) >> 1) & 1);
+    if (edge) wait(&sm.edge, 0);
     if (a.status) atomicExch(a.status, 1);
   }
   if (tid == 0 && store_pending) tc::bulk_wait_all();
@@ -1162,7 +1178,12 @@ int m3_fwd_tc_launch(const M3TcFwd& f, cudaStream_t st) {
   a.states = reinterpret_cast<bf16*>(f.states);
   a.theta0 = f.theta0; a.s0 = f.s0; a.th_in = f.th_in; a.fin = f.fin; a.thf = f.thf; a.status = f.status;
   a.B = f.B; a.L = f.L; a.nh = f.nh; a.ldp = f.ldp; a.lds = f.lds; a.nc = (f.L + CS - 1) / CS;
-  if (f.B <= 0 || f.L <= 0) return 0;
+  a.nseg = f.nseg > 0 ? f.nseg : 1;
+  a.cps = (a.nc + a.nseg - 1) / a.nseg;
+  a.seg_lo = f.seg_lo;
+  a.seg_hi = f.seg_hi > 0 ? f.seg_hi : a.nseg;
+  if (f.B <= 0 || f.L <= 0 || a.seg_hi <= a.seg_lo) return 0;
+  if ((a.nseg - 1) * a.cps >= a.nc) return -5;   // every segment must own at least one chunk
   if ((reinterpret_cast<uintptr_t>(f.proj) | reinterpret_cast<uintptr_t>(f.bc) | reinterpret_cast<uintptr_t>(f.y) |
        reinterpret_cast<uintptr_t>(f.rate) | reinterpret_cast<uintptr_t>(f.states)) % 16 || f.ldp % 8)
     return -3;
@@ -1172,7 +1193,7 @@ int m3_fwd_tc_launch(const M3TcFwd& f, cudaStream_t st) {
     return -4;
   const int smem = (int)sizeof(Smem) + 1024;
   cudaFuncSetAttribute(m3_fwd_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  m3_fwd_tc_k<<<f.B * f.nh, NT, smem, st>>>(a, tm_bc, tm_proj, tm_y);
+  m3_fwd_tc_k<<<f.B * f.nh * (a.seg_hi - a.seg_lo), NT, smem, st>>>(a, tm_bc, tm_proj, tm_y);
   return (int)cudaGetLastError();
 }
 
@@ -1189,7 +1210,12 @@ int m3_bwd_tc_launch(const M3TcBwd& f, cudaStream_t st) {
   a.dthl = f.dthl; a.dthtot = f.dthtot; a.dgam = f.dgam; a.dscl = f.dscl; a.dadt = f.dadt;
   a.dD = f.dD; a.dCb = f.dCb; a.dBb = f.dBb; a.status = f.status;
   a.B = f.B; a.L = f.L; a.nh = f.nh; a.ldp = f.ldp; a.lds = f.lds; a.nc = (f.L + CS - 1) / CS;
-  if (f.B <= 0 || f.L <= 0) return 0;
+  a.nseg = f.nseg > 0 ? f.nseg : 1;
+  a.cps = (a.nc + a.nseg - 1) / a.nseg;
+  a.seg_lo = f.seg_lo;
+  a.seg_hi = f.seg_hi > 0 ? f.seg_hi : a.nseg;
+  if (f.B <= 0 || f.L <= 0 || a.seg_hi <= a.seg_lo) return 0;
+  if ((a.nseg - 1) * a.cps >= a.nc) return -5;
   if ((reinterpret_cast<uintptr_t>(f.proj) | reinterpret_cast<uintptr_t>(f.bc) | reinterpret_cast<uintptr_t>(f.dy) |
        reinterpret_cast<uintptr_t>(f.rate) | reinterpret_cast<uintptr_t>(f.states) |
        reinterpret_cast<uintptr_t>(f.theta0) | reinterpret_cast<uintptr_t>(f.dproj) |
@@ -1203,6 +1229,6 @@ int m3_bwd_tc_launch(const M3TcBwd& f, cudaStream_t st) {
     return -4;
   const int smem = (int)sizeof(BSmem) + 1024;
   cudaFuncSetAttribute(m3_bwd_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  m3_bwd_tc_k<<<f.B * f.nh, BNT, smem, st>>>(a, tm_bc, tm_proj, tm_dy, tm_dproj, tm_gq, tm_gk);
+  m3_bwd_tc_k<<<f.B * f.nh * (a.seg_hi - a.seg_lo), BNT, smem, st>>>(a, tm_bc, tm_proj, tm_dy, tm_dproj, tm_gq, tm_gk);
   return (int)cudaGetLastError();
 }

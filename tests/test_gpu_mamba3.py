@@ -114,6 +114,33 @@ def test_ssd_backward_walker_matches_chunk_parallel_kernels(B, L, H):
         assert rel(a, b) < 2e-2, (name, rel(a, b))
 
 
+@pytest.mark.parametrize("B,L,nseg", [(1, 1000, 3), (2, 4100, 5), (1, 300, 5)])
+def test_ssd_walkers_split_into_segments_match_one_walk(B, L, nseg, monkeypatch):
+    """Sequences cut into segments (walked in parallel, then re-walked from the carried state /
+    gradient) give the single walk's forward and backward outputs."""
+    from sigma0_b200.ops._ext import ext
+    C = ext()
+    m, d, proj = _walker_args(B, L, 512, 5)
+    dy = torch.randn(B, L, d.d_inner, device="cuda").to(torch.bfloat16)
+    common = (m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D)
+    res = {}
+    for k in (1, nseg):
+        monkeypatch.setenv("S0_M3_SEGMENTS", str(k))
+        out = C.m3_fwd(proj, B, L, d.n_heads, *common, m.A_floor, 1e-6, True, True)
+        y, st, fin, thf = out[:4]
+        res[k] = (y, fin, thf) + tuple(C.m3_bwd(proj, dy, *common, B, L, d.n_heads, m.A_floor, 1e-6,
+                                                 saved_states=st, saved_prep=list(out[4:])))
+    torch.cuda.synchronize()
+    assert int(C.m3_tc_status(proj).item()) == 0
+    names = ["y", "fin", "thf", "dproj", "dwB", "dwC", "ddt_bias", "dD", "dC_bias", "dB_bias"]
+    for name, a, b in zip(names, res[nseg], res[1]):
+        if name == "thf":
+            dth = torch.remainder(a - b + 3.14159265, 2 * 3.14159265) - 3.14159265
+            assert dth.abs().max().item() < 1e-3
+            continue
+        assert rel(a, b) < 1e-2, (name, rel(a, b))
+
+
 @pytest.mark.parametrize("L", [128, 150, 700])
 def test_ssd_backward_matches_oracle(L):
     from sigma0_b200.ops._ext import ext
