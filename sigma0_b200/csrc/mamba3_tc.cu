@@ -88,6 +88,10 @@ __device__ __forceinline__ uint32_t frag_off(int row, int col) {   // bf16 (row,
   return (uint32_t)(col >> 6) * BOX + swz(row, (col >> 3) & 7) + (uint32_t)(col & 7) * 2;
 }
 
+// theta table [64][32] fp32 with an xor swizzle on groups of 4 angles, so that the epilogue's
+// reads (8 rows x 4 angles per warp) and the build's float4 reads hit distinct banks
+__device__ __forceinline__ int th_idx(int row, int r) { return row * R + (r ^ ((row & 7) << 2)); }
+
 __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t ph) { return tc::mbar_wait(bar, ph, WAIT_LIMIT); }
 
 // loads of chunk c (the i-th of this walk) into stage i & 1 (V, rates, scalars); warp 0 calls it
@@ -208,7 +212,7 @@ __global__ void __launch_bounds__(NT, 2)
       for (int i = 0; i < 8; ++i) {
         const int row = warp * 8 + i;
         acc += st.rate[row * R + lane] * st.dt[row];
-        st.rate[row * R + lane] = acc;                    // local prefix, in place
+        st.rate[th_idx(row, lane)] = acc;                 // local prefix, in place (swizzled)
       }
       sm.seg[warp * 32 + lane] = acc;
     }
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(NT, 2)
       float base = sm.th[lane];
       for (int s = 0; s < warp; ++s) base += sm.seg[s * 32 + lane];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) st.rate[(warp * 8 + i) * R + lane] += base;   // theta (unreduced)
+      for (int i = 0; i < 8; ++i) st.rate[th_idx(warp * 8 + i, lane)] += base;   // theta (unreduced)
       if (warp == 7) {
         const float e = base + sm.seg[7 * 32 + lane];
         sm.thnext[lane] = e - TWO_PI_F * floorf(e * (1.f / TWO_PI_F));
@@ -253,7 +257,7 @@ __global__ void __launch_bounds__(NT, 2)
       for (int o = 1; o < 8; o <<= 1) qk += __shfl_xor_sync(0xffffffffu, qk, o);
       if (bch == 0) sm.qkp[half][row] = qk;
       if (half == 0) {
-        const float4 th4 = *reinterpret_cast<const float4*>(st.rate + row * R + 4 * bch);
+        const float4 th4 = *reinterpret_cast<const float4*>(st.rate + th_idx(row, 4 * bch));
         const float ths[4] = {th4.x, th4.y, th4.z, th4.w};
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
@@ -653,7 +657,7 @@ __global__ void __launch_bounds__(BNT, 1)
       for (int i = 0; i < 4; ++i) {
         const int row = warp * 4 + i;
         acc += st.rate[row * R + lane] * st.dt[row];
-        st.rate[row * R + lane] = acc;
+        st.rate[th_idx(row, lane)] = acc;
       }
       sm.seg[warp * 32 + lane] = acc;
     }
@@ -663,7 +667,7 @@ __global__ void __launch_bounds__(BNT, 1)
       float base = st.th0[lane];
       for (int s2 = 0; s2 < warp; ++s2) base += sm.seg[s2 * 32 + lane];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) st.rate[(warp * 4 + i) * R + lane] += base;
+      for (int i = 0; i < 4; ++i) st.rate[th_idx(warp * 4 + i, lane)] += base;
     }
     __syncthreads();
     const float cend = sm.cum[CS - 1];
@@ -721,7 +725,7 @@ __global__ void __launch_bounds__(BNT, 1)
       for (int o = 1; o < 8; o <<= 1) qk += __shfl_xor_sync(0xffffffffu, qk, o);
       if (bch == 0) sm.qkp[bhalf][row] = qk;
       if (bhalf == 0) {
-        const float4 th4 = *reinterpret_cast<const float4*>(st.rate + row * R + 4 * bch);
+        const float4 th4 = *reinterpret_cast<const float4*>(st.rate + th_idx(row, 4 * bch));
         const float ths[4] = {th4.x, th4.y, th4.z, th4.w};
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
@@ -881,6 +885,22 @@ __global__ void __launch_bounds__(BNT, 1)
       }
       tc::commit(&sm.mma2);
     }
+    // raw B rows of this thread's dQ / dK positions (global, L2-resident), fetched while the
+    // MMAs run
+    uint32_t braw[8];
+    {
+      const bf16* bcg = a.bc + ((size_t)b * a.L + t0) * (2 * N);
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int row = hr ? r1 : r0;
+        const bool live = t0 + row < a.L;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const int n = c16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq;
+          braw[hr * 4 + nt] = live ? __ldg(reinterpret_cast<const unsigned int*>(bcg + (size_t)row * 2 * N + n)) : 0u;
+        }
+      }
+    }
     ok = wait(&sm.mma2, j & 1) && ok;
     tc::fence_after_sync();
     const float e0 = __expf(cum0), e1 = __expf(cum1);
@@ -942,7 +962,6 @@ __global__ void __launch_bounds__(BNT, 1)
       tc::tmem_ld_frag16(tmem + lane_base + TB_DK + c16, ka);
       tc::tmem_ld_frag16(tmem + lane_base + TB_DK + 64 + c16, ka + 8);
       float* dth = reinterpret_cast<float*>(st.dy);
-      const bf16* bcg = a.bc + ((size_t)b * a.L + t0) * (2 * N);
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr) {
         const int row = hr ? r1 : r0;
@@ -955,15 +974,14 @@ __global__ void __launch_bounds__(BNT, 1)
           const int n = c16 + (nt >> 1) * 64 + (nt & 1) * 8 + 2 * tq;
           const int fi = (nt >> 1) * 8 + (nt & 1) * 4 + 2 * hr;     // register of this pair
           const float g0 = qa[fi], g1 = qa[fi + 1], k0g = ka[fi], k1g = ka[fi + 1];
-          const float2 bn = live ? unpack_bf16(*reinterpret_cast<const uint32_t*>(bcg + (size_t)row * 2 * N + n))
-                                 : make_float2(0.f, 0.f);
+          const float2 bn = unpack_bf16(braw[hr * 4 + nt]);
           const float b0 = bn.x + sm.bb[n], b1 = bn.y + sm.bb[n + 1];
           const uint32_t off = frag_off(row, n);
           const float2 qv = unpack_bf16(*reinterpret_cast<const uint32_t*>(st.cn + off));
           float dq0, dq1, dk0, dk1, cb0, cb1;
           if (nt < 2) {   // rotated columns
             const int r = n >> 1;
-            const float th = st.rate[row * R + r];
+            const float th = st.rate[th_idx(row, r)];
             float sn, cs;
             __sincosf(th - TWO_PI_F * floorf(th * (1.f / TWO_PI_F) + 0.5f), &sn, &cs);
             dq0 = g0 * cs + g1 * sn;
