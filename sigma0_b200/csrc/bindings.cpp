@@ -90,7 +90,14 @@ at::Tensor m3_status(const at::Tensor& like) {
   if (!per_dev[d].defined()) per_dev[d] = at::zeros({1}, like.options().dtype(at::kInt));
   return per_dev[d];
 }
-bool g_m3_tc = true;   // the tcgen05 chunk walker (false: the chunk-parallel mma.sync kernels)
+// SSD implementation: 1 the tcgen05 chunk walkers, 0 the chunk-parallel mma.sync kernels,
+// -1 (default) by occupancy: the walkers run one CTA per (sequence, head), so they are used when
+// there are at least as many (sequence, head) pairs as SMs; smaller batches (a single sequence of
+// the 75m recipe) keep every SM busy with the chunk-parallel kernels instead.
+int g_m3_tc = -1;
+bool m3_walker(const at::Tensor& like, int64_t B, int64_t nh) {
+  return g_m3_tc >= 0 ? g_m3_tc == 1 : B * nh >= num_sms(like);
+}
 
 // Segments per sequence for the walkers: one CTA walks one (sequence, head, segment).  With
 // fewer (sequence, head) pairs than CTA slots (two per SM forward, one backward) each sequence
@@ -119,12 +126,13 @@ std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh
                                double eps, bool want_final = false, bool return_prep = false) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
-  M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps, !g_m3_tc);
+  const bool walker = m3_walker(proj, B, nh);
+  M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps, !walker);
   int nc = m3_nchunks((int)L);
   at::Tensor fin, thf;
   if (want_final) fin = at::empty({B, nh, M3_P, M3_N}, proj.options().dtype(at::kFloat));
   auto y = at::empty({B, L, nh * M3_P}, proj.options());
-  if (g_m3_tc) {
+  if (walker) {
     if (want_final) thf = at::empty({B, nh, M3_R}, proj.options().dtype(at::kFloat));
     M3TcFwd f{};
     f.proj = proj.data_ptr(); f.bc = pre.bc.data_ptr();
@@ -282,7 +290,11 @@ std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
   req(dy, at::kBFloat16, "dy");
-  if (g_m3_tc) return m3_bwd_tc(proj, dy, wB, wC, dt_bias, Bb, Cb, D, B, L, nh, A_floor, eps, saved_states, saved_prep);
+  // the saved forward tensors say which implementation wrote them (6 prep tensors: the walker)
+  const bool walker = saved_prep.has_value() && saved_states.has_value() && saved_states->defined()
+                          ? saved_prep->size() == 6
+                          : m3_walker(proj, B, nh);
+  if (walker) return m3_bwd_tc(proj, dy, wB, wC, dt_bias, Bb, Cb, D, B, L, nh, A_floor, eps, saved_states, saved_prep);
   M3Pre pre;
   if (saved_prep.has_value() && saved_prep->size() == 7) {   // (bc, dt, adt, sig, rate, aend, theta0) of m3_fwd
     const auto& v = *saved_prep;
@@ -1065,11 +1077,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Mamba3 recurrent step over T tokens (proj rows [B*T, ldp]; states updated in place)");
   m.def("eng_process", &eng_process, "batched matching engine: apply [B, M, 8] messages, one warp per book");
   m.def("eng_l2", &eng_l2, "batched L2 extraction");
-  m.def("m3_use_tc_scan", [](bool on) { m3_use_tc_scan(on ? 1 : 0); }, "select the tcgen05 chunk-scan kernel");
-  m.def("m3_use_tc", [](bool on) { g_m3_tc = on; }, "select the tcgen05 chunk walker for the Mamba3 SSD");
+  m.def("m3_use_tc", [](c10::optional<bool> on) { g_m3_tc = on.has_value() ? (*on ? 1 : 0) : -1; },
+        py::arg("on") = py::none(),
+        "Mamba3 SSD: True the tcgen05 chunk walkers, False the chunk-parallel kernels, None by occupancy");
   m.def("m3_tc_status", [](at::Tensor like) { return m3_status(like); },
         "status word of the tcgen05 SSD kernels on the tensor's device (nonzero: a bounded wait gave up)");
-  m.def("m3_tc_error", []() { return m3_tc_error(); }, "nonzero if a tcgen05 bounded wait timed out");
   m.def("dp_fused_adam", &dp_fused_adam, "fused reduce-scatter + AdamW + all-gather over peer memory");
   m.def("gen_apply", &gen_apply, "generation: decode message tokens, match, L2 and next book image");
   m.def("gen_sample", &gen_sample, "syntax-masked argmax / Gumbel-max sampling from fp32 logits");

@@ -161,8 +161,6 @@ struct DpfArgs {
 };
 int dp_fused_adam_launch(const DpfArgs& a, int sms, cudaStream_t st);
 
-void m3_use_tc_scan(int on);   // select the tcgen05 chunk scan
-int m3_tc_error();             // nonzero once a bounded tcgen05 wait gave up
 void m3_decode_multi_launch(const void* proj, int B, int T, int ldp, int nh, const float* wB, const float* wC,
                             const float* dt_bias, const float* Bb, const float* Cb, const float* D, float A_floor,
                             float eps, float* ang, float* ssm, float* kprev, float* vprev, void* y,

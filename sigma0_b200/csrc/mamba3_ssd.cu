@@ -21,7 +21,6 @@
 // All matrix products are bf16 mma.m16n8k16 with fp32 accumulation.
 #include "common.cuh"
 #include "launchers.h"
-#include "tc_common.cuh"
 
 #include <cstdlib>
 
@@ -646,234 +645,6 @@ __global__ void __launch_bounds__(256)
       *reinterpret_cast<uint4*>(y + ((size_t)b * g.L + tt) * g.d_inner + h * P + ch * 8) =
           *reinterpret_cast<const uint4*>(sZ + r * LDP + ch * 8);
   }
-}
-
-// ---------------------------------------------------------------------------
-// F4 (tcgen05): chunk scan with the three contractions on the 5th-generation tensor
-// cores.  Operands live in K-major 128-byte-swizzled tiles (Q, K, S_in loaded and
-// rotated in place; V transposed; P written by the epilogue), accumulators in
-// tensor memory (S = Q K^T, Y_off = Q S_in^T, P V; M=64 tiles: row r sits in TMEM
-// lane 32*(r/16) + r%16).  One elected thread issues the MMAs and commits to an
-// mbarrier; epilogues read TMEM rows with tcgen05.ld.  ~107 KB of shared memory
-// and a 256-column TMEM allocation let two CTAs share an SM.
-// ---------------------------------------------------------------------------
-__device__ int g_tc_err;   // set (never cleared by kernels) when a bounded tcgen05 wait gives up
-
-__device__ __forceinline__ bf16* swz(unsigned char* tiles, int row, int n) {
-  return reinterpret_cast<bf16*>(tiles + (n >> 6) * (CS * 128) + tc::sw128_off(row, n & 63));
-}
-
-template <int NTH>
-__device__ __forceinline__ void load_rows_swz(const bf16* src_base, size_t row_stride, int col0, int ncols,
-                                              unsigned char* tiles, int t0, int L, int tid) {
-  const int per = ncols / 8;
-  for (int i = tid; i < CS * per; i += NTH) {
-    int r = i / per, ch = i % per;
-    int tt = t0 + r;
-    bool ok = tt < L;
-    cp_async16(swz(tiles, r, ch * 8), src_base + (size_t)(ok ? tt : 0) * row_stride + col0 + ch * 8, ok ? 16 : 0);
-  }
-}
-
-// build_qk on swizzled tiles (Q over Cn in tQ, K over Bn in tK), plus qkr.
-template <int NTH>
-__device__ __forceinline__ void build_qk_swz(unsigned char* tQ, unsigned char* tK, const float* sCos,
-                                             const float* sSin, const float* sScl, const float* sCbv,
-                                             const float* sBbv, float* sQKr, int tid) {
-  constexpr int TPR = NTH / CS;
-  {
-    int row = tid / TPR, part = tid % TPR;
-    constexpr int W = N / TPR;
-    float s = 0.f;
-    for (int n = part * W; n < part * W + W; n += 2) {
-      float2 c = unpack_bf16(*reinterpret_cast<const uint32_t*>(swz(tQ, row, n)));
-      float2 bb = unpack_bf16(*reinterpret_cast<const uint32_t*>(swz(tK, row, n)));
-      s += (c.x + sCbv[n]) * (bb.x + sBbv[n]) + (c.y + sCbv[n + 1]) * (bb.y + sBbv[n + 1]);
-    }
-#pragma unroll
-    for (int o = 1; o < TPR; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (part == 0) sQKr[row] = s;
-    __syncthreads();
-  }
-  {
-    constexpr int NSEG = NTH / 32, RPS = CS / NSEG;
-    int r = tid & 31, seg = tid >> 5;
-    for (int i = 0; i < RPS; ++i) {
-      int row = seg * RPS + i;
-      const float sn = sSin[row * RP + r], cs = sCos[row * RP + r];
-      uint32_t* qp = reinterpret_cast<uint32_t*>(swz(tQ, row, 2 * r));
-      uint32_t* kp = reinterpret_cast<uint32_t*>(swz(tK, row, 2 * r));
-      float2 c = unpack_bf16(*qp);
-      float c0 = c.x + sCbv[2 * r], c1 = c.y + sCbv[2 * r + 1];
-      *qp = pack_bf16(c0 * cs - c1 * sn, c0 * sn + c1 * cs);
-      float2 bb = unpack_bf16(*kp);
-      float b0 = bb.x + sBbv[2 * r], b1 = bb.y + sBbv[2 * r + 1];
-      float sc = sScl[row];
-      *kp = pack_bf16((b0 * cs - b1 * sn) * sc, (b0 * sn + b1 * cs) * sc);
-    }
-  }
-  for (int i = tid; i < CS * (N - 2 * R) / 2; i += NTH) {
-    int row = i / ((N - 2 * R) / 2);
-    int n = 2 * R + 2 * (i % ((N - 2 * R) / 2));
-    uint32_t* qp = reinterpret_cast<uint32_t*>(swz(tQ, row, n));
-    uint32_t* kp = reinterpret_cast<uint32_t*>(swz(tK, row, n));
-    float2 c = unpack_bf16(*qp);
-    *qp = pack_bf16(c.x + sCbv[n], c.y + sCbv[n + 1]);
-    float2 bb = unpack_bf16(*kp);
-    float sc = sScl[row];
-    *kp = pack_bf16((bb.x + sBbv[n]) * sc, (bb.y + sBbv[n + 1]) * sc);
-  }
-  __syncthreads();
-}
-
-constexpr size_t TSCAN_TILES = 3 * 16384 + 2 * 8192;     // Q, K, S_in (N-wide) + V^T, P
-constexpr size_t TSCAN_SMEM = 1024 + TSCAN_TILES + sizeof(bf16) * (2 * CS * LDP) +
-                              sizeof(float) * (2 * CS * RP + 2 * (CS + 4) + 5 * CS + 2 * N + 8 * 32 + 32);
-
-__global__ void __launch_bounds__(256, 2)
-    m3_chunk_scan_tc(ScanIn in, Geo g, const bf16* __restrict__ states, bf16* __restrict__ y) {
-  extern __shared__ unsigned char smem_raw[];
-  __shared__ uint64_t mbar;
-  __shared__ uint32_t tslot;
-  const uint32_t raw = tc::smem_u32(smem_raw);
-  unsigned char* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  unsigned char* tQ = base;
-  unsigned char* tK = base + 16384;
-  unsigned char* tS = base + 32768;
-  unsigned char* tVt = base + 49152;
-  unsigned char* tP = base + 57344;
-  bf16* sX = reinterpret_cast<bf16*>(base + TSCAN_TILES);
-  bf16* sZ = sX + CS * LDP;
-  float* sSin = reinterpret_cast<float*>(sZ + CS * LDP);
-  float* sCos = sSin + CS * RP;
-  float* sDT = sCos + CS * RP;
-  float* sSig = sDT + CS + 4;   // CS + 1 used; padded to keep later arrays 16-byte aligned
-  float* sADT = sSig + CS + 4;
-  float* sCum = sADT + CS;
-  float* sGam = sCum + CS;
-  float* sScl = sGam + CS;
-  float* sQKr = sScl + CS;
-  float* sCbv = sQKr + CS;
-  float* sBbv = sCbv + N;
-  float* sSeg = sBbv + N;
-  float* sTh0 = sSeg + 8 * 32;
-
-  const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = c * CS;
-  const size_t bh = (size_t)b * g.nh + h;
-  if (warp == 0) tc::tmem_alloc(&tslot, 256);
-  if (tid == 0) {
-    tc::mbar_init(&mbar, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  const bf16* bcb = in.bc + (size_t)b * g.L * 2 * N;
-  const bf16* pb = in.proj + (size_t)b * g.L * g.ldp;
-  load_rows_swz<256>(bcb, 2 * N, 0, N, tK, t0, g.L, tid);
-  load_rows_swz<256>(bcb, 2 * N, N, N, tQ, t0, g.L, tid);
-  load_rows<256>(pb, g.ldp, g.d_inner + h * P, P, sX, LDP, t0, g.L, tid);
-  load_rows<256>(pb, g.ldp, h * P, P, sZ, LDP, t0, g.L, tid);
-  {
-    const bf16* src = states + state_off(g, b, h, c);
-    for (int i = tid; i < P * N / 8; i += 256) {
-      int r = i / (N / 8), ch = i % (N / 8);
-      cp_async16(swz(tS, r, ch * 8), src + r * N + ch * 8);
-    }
-  }
-  cp_async_commit();
-  load_scalars<256>(in, g, b, h, t0, sDT, sADT, sSig, sSin, tid);
-  for (int i = tid; i < N; i += 256) {
-    sCbv[i] = in.Cb[h * N + i];
-    sBbv[i] = in.Bb[h * N + i];
-  }
-  if (tid < 32) sTh0[tid] = in.theta0[(bh * g.nc + c) * R + tid];
-  cp_async_wait_all();
-  __syncthreads();
-  row_scalars(sDT, sSig, sADT, sGam, sScl, sCum, tid);
-  chunk_angles<256>(sSin, sDT, sTh0, sCos, sSin, sSeg, tid);
-  build_qk_swz<256>(tQ, tK, sCos, sSin, sScl, sCbv, sBbv, sQKr, tid);
-  for (int i = tid; i < CS * P; i += 256) {       // V^T: B operand of P V (rows p, K = s)
-    int s_ = i / P, p = i % P;
-    *reinterpret_cast<bf16*>(tVt + tc::sw128_off(p, s_)) = sX[s_ * LDP + p];
-  }
-  tc::fence_proxy_async();
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = tslot;
-  const uint32_t id = tc::idesc_bf16(64, 64);
-  if (tid == 0) {
-    for (int ks = 0; ks < 8; ++ks)
-      tc::mma_bf16(tmem, tc::desc_sw128(tQ + (ks >> 2) * 8192, ks & 3), tc::desc_sw128(tK + (ks >> 2) * 8192, ks & 3),
-                   id, ks > 0);
-    for (int ks = 0; ks < 8; ++ks)
-      tc::mma_bf16(tmem + 64, tc::desc_sw128(tQ + (ks >> 2) * 8192, ks & 3),
-                   tc::desc_sw128(tS + (ks >> 2) * 8192, ks & 3), id, ks > 0);
-    tc::commit(&mbar);
-  }
-  bool ok = __syncthreads_and(tc::mbar_wait(&mbar, 0));    // block-uniform outcome
-  tc::fence_after_sync();
-  const int q = warp & 3, half = warp >> 2;
-  const int row = 16 * q + lane;                  // valid for lane < 16 (M=64 TMEM layout)
-  const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-  if (ok) {
-    float v[32];
-    tc::tmem_ld16(lane_base + half * 32, v);
-    tc::tmem_ld16(lane_base + half * 32 + 16, v + 16);
-    if (lane < 16) {
-      const float cr = sCum[row];
-#pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        const int s_ = half * 32 + j;
-        const float p0 = (s_ < row) ? v[j] * __expf(cr - sCum[s_]) : 0.f;
-        const float p1 = (s_ + 1 < row) ? v[j + 1] * __expf(cr - sCum[s_ + 1]) : 0.f;
-        *reinterpret_cast<uint32_t*>(tP + tc::sw128_off(row, s_)) = pack_bf16(p0, p1);
-      }
-    }
-  }
-  tc::fence_proxy_async();
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  if (tid == 0 && ok) {
-    for (int ks = 0; ks < 4; ++ks)
-      tc::mma_bf16(tmem + 128, tc::desc_sw128(tP, ks), tc::desc_sw128(tVt, ks), id, ks > 0);
-    tc::commit(&mbar);
-  }
-  ok = __syncthreads_and(ok && tc::mbar_wait(&mbar, 1));
-  tc::fence_after_sync();
-  if (ok) {
-    float yo[32], pv[32];
-    tc::tmem_ld16(lane_base + 64 + half * 32, yo);
-    tc::tmem_ld16(lane_base + 64 + half * 32 + 16, yo + 16);
-    tc::tmem_ld16(lane_base + 128 + half * 32, pv);
-    tc::tmem_ld16(lane_base + 128 + half * 32 + 16, pv + 16);
-    if (lane < 16) {
-      const float e = __expf(sCum[row]);
-      const float qd = in.D[h] + sQKr[row] * sGam[row];
-#pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        const int p = half * 32 + j;
-        float2 xv = unpack_bf16(*reinterpret_cast<const uint32_t*>(sX + row * LDP + p));
-        float2 zv = unpack_bf16(*reinterpret_cast<const uint32_t*>(sZ + row * LDP + p));
-        float a0 = (e * yo[j] + pv[j] + qd * xv.x) * zv.x * sigmoidf_(zv.x);
-        float a1 = (e * yo[j + 1] + pv[j + 1] + qd * xv.y) * zv.y * sigmoidf_(zv.y);
-        *reinterpret_cast<uint32_t*>(sZ + row * LDP + p) = pack_bf16(a0, a1);
-      }
-    }
-  } else if (tid == 0) {
-    atomicExch(&g_tc_err, 1);
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  for (int i = tid; i < CS * 8; i += 256) {
-    int r = i >> 3, ch = i & 7;
-    int tt = t0 + r;
-    if (tt < g.L)
-      *reinterpret_cast<uint4*>(y + ((size_t)b * g.L + tt) * g.d_inner + h * P + ch * 8) =
-          *reinterpret_cast<const uint4*>(sZ + r * LDP + ch * 8);
-  }
-  if (warp == 0) tc::tmem_dealloc(tmem, 256);
 }
 
 // ---------------------------------------------------------------------------
@@ -1712,30 +1483,9 @@ void m3_states_launch(const M3Geo& G, const M3Scan& S, void* states, cudaStream_
                                                                           final_state);
 }
 
-static int g_tc_scan = -1;   // -1: read S0_TC_SCAN once; else set by m3_use_tc_scan
-static int tc_scan_enabled() {
-  if (g_tc_scan < 0) {
-    const char* e = getenv("S0_TC_SCAN");
-    g_tc_scan = (e && e[0] == '1') ? 1 : 0;
-  }
-  return g_tc_scan;
-}
-void m3_use_tc_scan(int on) { g_tc_scan = on ? 1 : 0; }
-int m3_tc_error() {
-  int v = 0;
-  cudaMemcpyFromSymbol(&v, g_tc_err, sizeof(int));
-  return v;
-}
-
 void m3_scan_launch(const M3Geo& G, const M3Scan& S, const void* states, void* y, cudaStream_t st) {
   Geo g = make_geo(G);
   ScanIn in = make_in(S);
-  if (tc_scan_enabled()) {
-    set_smem(m3_chunk_scan_tc, TSCAN_SMEM);
-    m3_chunk_scan_tc<<<dim3(g.nh, g.nc, g.B), 256, TSCAN_SMEM, st>>>(in, g, reinterpret_cast<const bf16*>(states),
-                                                                     reinterpret_cast<bf16*>(y));
-    return;
-  }
   set_smem(m3_chunk_scan, SCAN_SMEM);
   m3_chunk_scan<<<dim3(g.nh, g.nc, g.B), 256, SCAN_SMEM, st>>>(in, g, reinterpret_cast<const bf16*>(states),
                                                                reinterpret_cast<bf16*>(y));

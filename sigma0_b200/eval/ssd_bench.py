@@ -160,12 +160,17 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--no_oracle_speed", action="store_true")
+    ap.add_argument("--impl", choices=["auto", "walker", "chunked"], default="auto",
+                    help="walker: the tcgen05 chunk walkers; chunked: the chunk-parallel mma.sync kernels; "
+                         "auto: the walkers when (sequences x heads) >= SMs")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("the SSD kernel bench needs a CUDA device")
+    from ..ops._ext import ext
+    ext().m3_use_tc(None if a.impl == "auto" else a.impl == "walker")
     par = parity(a.nh, a.parity_L)
     for L in a.L:
-        rec = {"nh": a.nh, "N": 128, "P": 64, "CS": 64, "B": a.B, "L": L, "parity_L": a.parity_L,
+        rec = {"impl": a.impl, "nh": a.nh, "N": 128, "P": 64, "CS": 64, "B": a.B, "L": L, "parity_L": a.parity_L,
                "parity_rel_l2": par}
         rec.update(speed(a.nh, L, a.B, a.warmup, a.iters, oracle=not a.no_oracle_speed))
         print(json.dumps(rec), flush=True)

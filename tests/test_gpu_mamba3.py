@@ -76,7 +76,7 @@ def test_ssd_forward_walker_matches_chunk_parallel_kernels(B, L, H):
         C.m3_use_tc(True)
         y1, _, f1, th1 = C.m3_fwd(*args)[:4]
     finally:
-        C.m3_use_tc(True)
+        C.m3_use_tc(None)
     torch.cuda.synchronize()
     assert int(st.item()) == 0
     assert torch.isfinite(y1.float()).all()
@@ -105,7 +105,7 @@ def test_ssd_backward_walker_matches_chunk_parallel_kernels(B, L, H):
         got = C.m3_bwd(proj, dy, *common, B, L, d.n_heads, m.A_floor, 1e-6, saved_states=out[1],
                        saved_prep=list(out[4:]))
     finally:
-        C.m3_use_tc(True)
+        C.m3_use_tc(None)
     torch.cuda.synchronize()
     assert int(st.item()) == 0
     names = ["dproj", "dwB", "dwC", "ddt_bias", "dD", "dC_bias", "dB_bias"]
@@ -124,12 +124,16 @@ def test_ssd_walkers_split_into_segments_match_one_walk(B, L, nseg, monkeypatch)
     dy = torch.randn(B, L, d.d_inner, device="cuda").to(torch.bfloat16)
     common = (m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D)
     res = {}
-    for k in (1, nseg):
-        monkeypatch.setenv("S0_M3_SEGMENTS", str(k))
-        out = C.m3_fwd(proj, B, L, d.n_heads, *common, m.A_floor, 1e-6, True, True)
-        y, st, fin, thf = out[:4]
-        res[k] = (y, fin, thf) + tuple(C.m3_bwd(proj, dy, *common, B, L, d.n_heads, m.A_floor, 1e-6,
-                                                 saved_states=st, saved_prep=list(out[4:])))
+    C.m3_use_tc(True)
+    try:
+        for k in (1, nseg):
+            monkeypatch.setenv("S0_M3_SEGMENTS", str(k))
+            out = C.m3_fwd(proj, B, L, d.n_heads, *common, m.A_floor, 1e-6, True, True)
+            y, st, fin, thf = out[:4]
+            res[k] = (y, fin, thf) + tuple(C.m3_bwd(proj, dy, *common, B, L, d.n_heads, m.A_floor, 1e-6,
+                                                     saved_states=st, saved_prep=list(out[4:])))
+    finally:
+        C.m3_use_tc(None)
     torch.cuda.synchronize()
     assert int(C.m3_tc_status(proj).item()) == 0
     names = ["y", "fin", "thf", "dproj", "dwB", "dwC", "ddt_bias", "dD", "dC_bias", "dB_bias"]
