@@ -325,10 +325,12 @@ def test_glu_residual_backward_matches_fp32(T, D):
     assert rel(db, bf.grad) < 1e-4, rel(db, bf.grad)
 
 
-def test_ssd_backward_with_saved_forward_tensors_matches_recompute():
+@pytest.mark.parametrize("walker", [False, True])
+def test_ssd_backward_with_saved_forward_tensors_matches_recompute(walker):
     """m3_bwd given the forward's passed states and prep tensors matches m3_bwd recomputing them."""
     from sigma0_b200.ops._ext import ext
     C = ext()
+    C.m3_use_tc(walker)
     m = _layer(seed=4)
     B, L = 2, 333
     d = m.dims
@@ -336,11 +338,15 @@ def test_ssd_backward_with_saved_forward_tensors_matches_recompute():
     proj = (torch.randn(B * L, ldp, device="cuda") * 0.5).to(torch.bfloat16)
     dy = torch.randn(B, L, d.d_inner, device="cuda").to(torch.bfloat16)
     args = (m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D)
-    out = C.m3_fwd(proj, B, L, d.n_heads, *args, m.A_floor, 1e-6, return_prep=True)
-    assert len(out) == 10            # y, states, final state, final angle, 6 prep tensors
-    full = C.m3_bwd(proj, dy, *args, B, L, d.n_heads, m.A_floor, 1e-6)
-    saved = C.m3_bwd(proj, dy, *args, B, L, d.n_heads, m.A_floor, 1e-6, saved_states=out[1],
-                     saved_prep=list(out[4:]))
+    try:
+        out = C.m3_fwd(proj, B, L, d.n_heads, *args, m.A_floor, 1e-6, return_prep=True)
+        # y, states, final state, final angle + the prep (6 tensors for the walker, 7 otherwise)
+        assert len(out) == (10 if walker else 11)
+        full = C.m3_bwd(proj, dy, *args, B, L, d.n_heads, m.A_floor, 1e-6)
+        saved = C.m3_bwd(proj, dy, *args, B, L, d.n_heads, m.A_floor, 1e-6, saved_states=out[1],
+                         saved_prep=list(out[4:]))
+    finally:
+        C.m3_use_tc(None)
     # equal up to the summation order of the kernels' shared-memory atomics
     for a, b in zip(full, saved):
         assert rel(a, b) < 1e-3, rel(a, b)
