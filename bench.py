@@ -55,6 +55,9 @@ def parse():
     p.add_argument("--no_graphs", action="store_true")
     p.add_argument("--dp_impl", choices=["fused", "nccl", "nccl_sharded"], default="fused",
                    help="N>1 gradient sync: fused peer-memory RS+AdamW+AG kernel, or NCCL all-reduce / RS+AG")
+    p.add_argument("--tp", type=int, default=1,
+                   help="tensor-parallel size (heads split over --tp consecutive ranks, batch over the rest)")
+    p.add_argument("--accum_steps", type=int, default=1, help="micro-batches per optimizer step")
     p.add_argument("--extras", choices=["auto", "on", "off"], default="auto",
                    help="after the headline region, time the published 75m recipe config and the "
                         "generation workload as extra keys (auto: on one GPU only)")
@@ -374,16 +377,19 @@ def main():
         args.n_messages = a.n_messages
     Bm, nm = args.micro_bsz, args.n_messages
     trainer = Trainer(args, device=dev, world=world, rank=rank, total_steps=10_000, seed=0,
-                      sharded=a.dp_impl == "nccl_sharded", dp_impl="fused" if a.dp_impl == "fused" else "nccl")
+                      sharded=a.dp_impl == "nccl_sharded", dp_impl="fused" if a.dp_impl == "fused" else "nccl",
+                      tp=a.tp, accum_steps=a.accum_steps)
+    dp_world, dp_rank = trainer.world, trainer.rank          # with --tp the batch is split over dp only
+    Bm = Bm * a.accum_steps
 
-    # synthetic data: Bm sequences per rank, replayed through the engine
-    days = make_sequences(Bm, nm + 1, seed=1000 + rank)
+    # synthetic data: Bm sequences per dp rank, replayed through the engine
+    days = make_sequences(Bm, nm + 1, seed=1000 + dp_rank)
     ds = LobWindowDataset.from_days(days, nm, token_mode=args.token_mode)
     tokens, labels, book = collate([ds[i] for i in range(Bm)])
     host = tuple(t.pin_memory() for t in (tokens, labels, book))
     devb = tuple(t.to(dev) for t in host)
     L = tokens.shape[1]
-    tok_per_step = Bm * L * world
+    tok_per_step = Bm * L * dp_world
 
     def barrier():
         if world > 1:
@@ -450,7 +456,9 @@ def main():
             "dtype": "bf16", "data": "synthetic (seeded order flow through the matching engine), random-init weights",
             "config": {"model": f"mamba3-lob-{a.preset} ({n_params/1e6:.1f}M params, d_model {d_model}, "
                                 f"{nml}+{nbpre}+{nbpost}+{nl} layers)",
-                       "global_batch": Bm * world, "seq_len": L, "parallelism": f"dp{world}",
+                       "global_batch": Bm * dp_world, "seq_len": L,
+                       "parallelism": f"tp{a.tp}xdp{dp_world}" if a.tp > 1 else f"dp{world}",
+                       "accum_steps": a.accum_steps,
                        "grad_sync": (a.dp_impl if world > 1 else "none"),
                        "l2": "working set (weights + ~90 GB activations per step) far above L2; no flush needed",
                        "vocab": vocab, "token_mode": tmode},

@@ -51,6 +51,8 @@ def parse(argv=None):
     p.add_argument("--sharded", action="store_true")
     p.add_argument("--grad_wire_dtype", default="float32", choices=["float32", "bfloat16"])
     p.add_argument("--accum_steps", type=int, default=1)
+    p.add_argument("--tp", type=int, default=1,
+                   help="tensor-parallel size: heads split over groups of --tp consecutive ranks, batch over the rest")
     p.add_argument("--context_parallel", action="store_true",
                    help="split every sequence over the ranks (message-aligned segments) instead of the batch")
     p.add_argument("--seed", type=int, default=0)
@@ -91,9 +93,10 @@ def main(argv=None):
     args = model_args(a, **extra)
     trainer = Trainer(args, device=dev, world=world, rank=rank, total_steps=a.steps, seed=a.seed,
                       sharded=a.sharded, accum_steps=a.accum_steps, grad_wire_dtype=a.grad_wire_dtype,
-                      dp_impl=a.dp_impl, context_parallel=a.context_parallel)
-    # context parallelism: every rank draws the same batch and keeps its segment of it
-    drank, dworld = (0, 1) if a.context_parallel else (rank, world)
+                      dp_impl=a.dp_impl, context_parallel=a.context_parallel, tp=a.tp)
+    # context parallelism: every rank draws the same batch and keeps its segment of it; tensor
+    # parallelism: the ranks of one tp group draw the same batch (their dp rank's)
+    drank, dworld = (0, 1) if a.context_parallel else (trainer.rank, trainer.world)
     tickers = a.tickers.split(",") if a.tickers else None
     dr = tuple(a.train_date_range.split(",")) if a.train_date_range else None
     days = load_days(a.data_dir, a.synthetic, args.n_messages + 1, a.seed + 1000 * drank, tickers, dr)

@@ -24,6 +24,13 @@ PRESETS = {
                  mamba3_expand=2, n_message_layers=2, n_layers=44, n_book_pre_layers=1,
                  n_book_post_layers=1, token_mode="22tok", vocab_size=12288, msg_len=22,
                  n_messages=500, micro_bsz=8, dtype="bfloat16", d_book=503),
+    # GDN backbone ~1B, d_model 2048, 24 layers (2 message + 1 book pre + 1 book
+    # post + 20 fused), 16 heads of dim 128 (value dim 256), chunk 64; 1,000 messages x 22 tokens;
+    # run with tensor parallelism (--tp 4 on 8 GPUs: TP4 x DP2)
+    "gdn1b": dict(architecture="gdn", d_model=2048, gdn_head_dim=128, gdn_num_heads=16, gdn_expand_v=2,
+                  gdn_chunk_size=64, n_message_layers=2, n_layers=20, n_book_pre_layers=1,
+                  n_book_post_layers=1, token_mode="22tok", vocab_size=12288, msg_len=22,
+                  n_messages=1000, micro_bsz=4, dtype="float32", d_book=503),
     "75m": dict(architecture="mamba3", d_model=1024, mamba3_d_state=128, mamba3_headdim=64,
                 mamba3_expand=2, n_message_layers=2, n_layers=6, n_book_pre_layers=1,
                 n_book_post_layers=1, token_mode="26tok", vocab_size=2112, msg_len=26,

@@ -76,8 +76,13 @@ class Mesh:
 
 
 def mesh_shape(world: int, hierarchical: bool = False, tp_size: int = 1, gpus_per_node: Optional[int] = None,
-               allow_single_node_hierarchical: bool = False) -> Tuple[Tuple[str, ...], Tuple[int, ...]]:
-    """(axis names, shape) for ``world`` ranks, without creating groups."""
+               allow_single_node_hierarchical: bool = False,
+               per_gpu_processes: bool = False) -> Tuple[Tuple[str, ...], Tuple[int, ...]]:
+    """(axis names, shape) for ``world`` ranks, without creating groups.
+
+    ``per_gpu_processes``: every GPU is its own process (torchrun), which is the
+    reference's multi-process branch, where a (dp, tp) mesh is allowed on one node; its
+    single-process branch (one process driving all local GPUs) requires tp = all GPUs."""
     gpn = gpus_per_node or world
     if world % gpn:
         raise ValueError(f"world size {world} is not a multiple of gpus_per_node {gpn}")
@@ -85,7 +90,7 @@ def mesh_shape(world: int, hierarchical: bool = False, tp_size: int = 1, gpus_pe
     if tp_size > 1:
         if world % tp_size:
             raise ValueError(f"world size {world} must be divisible by tp_size {tp_size}")
-        if nodes == 1 and tp_size != world:
+        if nodes == 1 and tp_size != world and not per_gpu_processes:
             raise ValueError(f"on one node tp_size ({tp_size}) must equal the number of GPUs ({world})")
         dp = world // tp_size
         return (("tp",), (tp_size,)) if dp == 1 else (("dp", "tp"), (dp, tp_size))
@@ -95,10 +100,11 @@ def mesh_shape(world: int, hierarchical: bool = False, tp_size: int = 1, gpus_pe
 
 
 def create_mesh(hierarchical: bool = False, tp_size: int = 1, gpus_per_node: Optional[int] = None,
-                allow_single_node_hierarchical: bool = False) -> Mesh:
+                allow_single_node_hierarchical: bool = False, per_gpu_processes: bool = False) -> Mesh:
     """Build the mesh of the current process group and its per-axis groups."""
     world, rank = dist.get_world_size(), dist.get_rank()
-    names, shape = mesh_shape(world, hierarchical, tp_size, gpus_per_node, allow_single_node_hierarchical)
+    names, shape = mesh_shape(world, hierarchical, tp_size, gpus_per_node, allow_single_node_hierarchical,
+                              per_gpu_processes)
     ranks = np.arange(world).reshape(shape)
     m = Mesh(names, shape, rank)
     for ax, name in enumerate(names):

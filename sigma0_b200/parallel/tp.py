@@ -165,6 +165,11 @@ class Mamba3TP(nn.Module):
         self.fused_out = FusedRowParallel(max_rows, self.out_proj_kernel.shape[1], self.group,
                                           self.out_proj_kernel.device)
 
+    def tp_sharded_parameters(self) -> list:
+        """This rank's head slices (the B / C / angle columns and BCNorm scales are replicated)."""
+        return [self.in_proj_heads, self.dt_bias, self.B_bias, self.C_bias, self.D, self.out_norm_scale,
+                self.out_proj_kernel]
+
     def full_in_proj_grad(self):
         """This rank's in_proj gradient scattered into the full (H, d_in_proj) layout."""
         g = torch.zeros(self.in_proj_heads.shape[0], self.full_dims.d_in_proj, dtype=self.in_proj_heads.grad.dtype)
@@ -174,9 +179,13 @@ class Mamba3TP(nn.Module):
 
 
 def shard_model(model: nn.Module, group=None) -> nn.Module:
-    """Replace every ``Mamba3`` sub-module by its tensor-parallel slice."""
+    """Replace every ``Mamba3`` sub-module by its tensor-parallel slice (one whose head count
+    does not divide over the group stays whole and replicated)."""
+    T = dist.get_world_size(group)
     for name, mod in list(model.named_modules()):
         for cname, child in list(mod.named_children()):
+            if isinstance(child, Mamba3) and child.dims.n_heads % T:
+                continue
             if isinstance(child, Mamba3):
                 setattr(mod, cname, Mamba3TP(child, group))
     return model

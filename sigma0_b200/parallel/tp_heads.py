@@ -70,6 +70,11 @@ class _RowParallel:
     def _full_table(self) -> tuple:
         return self._FULL
 
+    def tp_sharded_parameters(self) -> list:
+        """This rank's slices (their gradients are partial per rank; the rest is replicated)."""
+        own = dict(self.named_parameters())
+        return [own[local] for local, _, dim in self._full_table() if dim is not None]
+
     def _reduce(self, y: torch.Tensor, w: torch.Tensor, group) -> torch.Tensor:
         if self.fused is not None and y.is_cuda:
             from .tp_fused import fused_row_parallel
@@ -320,9 +325,13 @@ class NSABlockTP(nn.Module, _RowParallel):
 
 def shard_heads(model: nn.Module, group=None) -> nn.Module:
     """Replace every ``GDN`` mixer, ``TransformerBlock`` and ``NSABlock`` of a model by its
-    slice."""
+    slice.  A GDN mixer whose head count does not divide over the group (the narrow book
+    layers) stays whole and replicated: every rank computes it on the same input."""
+    T = dist.get_world_size(group)
     for _, mod in list(model.named_modules()):
         for cname, child in list(mod.named_children()):
+            if isinstance(child, GDN) and child.nh % T:
+                continue
             if isinstance(child, GDN):
                 setattr(mod, cname, GDNTP(child, group))
             elif isinstance(child, NSABlock):

@@ -45,7 +45,7 @@ class FlatAdam:
     def __init__(self, model: nn.Module, lr: float, ssm_lr: float, weight_decay: float = 0.05,
                  max_grad_norm: float = 1.0, betas=(0.9, 0.999), eps: float = 1e-8,
                  opt_config: str = "standard", attention_model: bool = False,
-                 bf16_shadow: bool = True, pad_multiple: int = 128, alloc=None):
+                 bf16_shadow: bool = True, pad_multiple: int = 128, alloc=None, last=()):
         self.model = model
         self.b1, self.b2 = betas
         self.eps = eps
@@ -56,6 +56,11 @@ class FlatAdam:
         groups = {"ssm": [], "regular": []}
         for n, p in named:
             groups[leaf_group(n, opt_config, attention_model)].append((n, p))
+        # parameters in `last` (tensor-parallel slices) go to the end of their group, so each
+        # group's slices form one contiguous range [tail_lo[group], group end)
+        late = {id(p) for p in last}
+        for k in groups:
+            groups[k] = [x for x in groups[k] if id(x[1]) not in late] + [x for x in groups[k] if id(x[1]) in late]
         order = groups["ssm"] + groups["regular"]
         dev = order[0][1].device
         # every slice starts on a 128-element boundary so bf16/fp32 views are 256-byte
@@ -75,8 +80,15 @@ class FlatAdam:
         self.shadow = mk(total, torch.bfloat16, dev) if (bf16_shadow and dev.type == "cuda") else None
         self.names: List[str] = []
         self.slices: Dict[str, Tuple[int, int]] = {}
+        self.late_ranges: List[Tuple[int, int]] = []     # [lo, hi) of the `last` parameters per group
+        ends = {"ssm": self.n_ssm, "regular": total}
         off = 0
+        seen_late = set()
         for n, p in order:
+            g = "ssm" if off < self.n_ssm else "regular"
+            if id(p) in late and g not in seen_late:
+                seen_late.add(g)
+                self.late_ranges.append((off, ends[g]))
             k = p.numel()
             self.flat[off:off + k].copy_(p.detach().reshape(-1))
             p.data = self.flat[off:off + k].view_as(p)

@@ -42,10 +42,9 @@ class Trainer:
     def __init__(self, args, device: Optional[torch.device] = None, world: int = 1, rank: int = 0,
                  group=None, total_steps: int = 1000, seed: int = 0, sharded: bool = False,
                  accum_steps: int = 1, grad_wire_dtype: str = "float32", dp_impl: str = "nccl",
-                 context_parallel: bool = False):
+                 context_parallel: bool = False, tp: int = 1):
         self.args = args
         self.device = device or torch.device("cuda" if torch.cuda.is_available() else "cpu")
-        self.world, self.rank, self.group = world, rank, group
         set_token_mode(args.token_mode)
         self.tok = get_tokenizer(args.token_mode)
         torch.manual_seed(seed)
@@ -56,6 +55,30 @@ class Trainer:
             # identical initial parameters on every rank (broadcast_one_to_all in the reference)
             for p in self.model.parameters():
                 dist.broadcast(p.data, 0, group=group)
+        # tensor parallelism: a (dp, tp) mesh over the default group; the mixers' heads (and
+        # the attention blocks' FFN width) are split over the tp axis, the batch over dp
+        self.tp, self.tp_group, tp_slices = 1, None, []
+        if int(tp) > 1:
+            if world <= 1 or group is not None or context_parallel:
+                raise ValueError("tensor parallelism needs the default process group of >= 2 ranks and no "
+                                 "context parallelism")
+            from ..parallel.mesh import create_mesh
+            from ..parallel.tp import shard_model
+            from ..parallel.tp_heads import shard_heads
+            if sharded:
+                raise ValueError("tensor parallelism keeps replicated moments (no ZeRO sharding)")
+            mesh = create_mesh(tp_size=int(tp), per_gpu_processes=True)
+            self.mesh, self.tp, self.tp_group = mesh, int(tp), mesh.group("tp")
+            shard_heads(shard_model(self.model, self.tp_group), self.tp_group)
+            for mod in self.model.modules():
+                if hasattr(mod, "tp_sharded_parameters"):
+                    tp_slices += mod.tp_sharded_parameters()
+            dp = mesh.size("dp") if "dp" in mesh.axis_names else 1
+            group = mesh.group("dp") if dp > 1 else None
+            world, rank = dp, (mesh.coord("dp") if dp > 1 else 0)
+            if dp_impl == "fused":
+                dp_impl = "nccl"          # the fused sync spans the default group only
+        self.world, self.rank, self.group = world, rank, group
         lr_base = float(getattr(args, "ssm_lr_base", 1e-3))
         lr = lr_base * float(getattr(args, "lr_factor", 1.0))
         opt_cls = FlatAdam
@@ -70,7 +93,7 @@ class Trainer:
                             opt_config=str(getattr(args, "opt_config", "standard")),
                             attention_model=attn_only,
                             pad_multiple=128 * (world if ((sharded or dp_impl == "fused") and world > 1) else 1),
-                            alloc=self._alloc(dp_impl, world))
+                            alloc=self._alloc(dp_impl, world), last=tp_slices)
         self.total_steps = total_steps
         self.warmup_steps = int(round(float(getattr(args, "warmup_end", 0.01)) * total_steps))
         lr_min = float(getattr(args, "lr_min", 0.0) or 0.0)
@@ -116,6 +139,9 @@ class Trainer:
           gradient of its shard, global-norm from the shards' sums of squares,
           Adam on the shard, then all-gather of the updated parameters."""
         opt = self.opt
+        if self.tp > 1:
+            self._update_tp(lr_scale)
+            return
         if self.world == 1:
             opt.step(lr_scale=lr_scale)
             return
@@ -153,6 +179,31 @@ class Trainer:
         opt.step_shard(gs, ss, lr_scale=lr_scale)
         dist.all_gather_into_tensor(opt.flat, opt.flat[opt.lo:opt.hi].clone(), group=self.group)
         opt.refresh_shadow()
+
+    def _update_tp(self, lr_scale: float):
+        """Tensor parallel: average over the dp axis, then the global gradient norm -- each
+        rank's head slices summed over the tp axis, the replicated parameters (identical
+        gradients on every tp rank) counted once -- and the update."""
+        opt = self.opt
+        g = opt.grad
+        if self.world > 1:
+            g.div_(self.world)
+            dist.all_reduce(g, group=self.group)
+        parts = torch.zeros(2, dtype=torch.float32, device=g.device)   # (slices, everything)
+        if g.is_cuda:
+            from ..ops._ext import ext
+            C = ext()
+            for lo, hi in opt.late_ranges:
+                C.sumsq(g[lo:hi], parts[0:1])
+            C.sumsq(g, parts[1:2])
+        else:
+            for lo, hi in opt.late_ranges:
+                parts[0] += (g[lo:hi] * g[lo:hi]).sum()
+            parts[1] = (g * g).sum()
+        rep = parts[1:2] - parts[0:1]
+        sl = parts[0:1].clone()
+        dist.all_reduce(sl, group=self.tp_group)
+        opt.step(lr_scale=lr_scale, grad_sumsq=sl + rep)
 
     def step_device(self, tokens, labels, book=None):
         """One optimizer step on device tensors; with ``accum_steps > 1`` the batch is
