@@ -438,6 +438,10 @@ def main():
     peak_gb = torch.cuda.max_memory_allocated(dev) / 1e9
     head_cfg = (args.d_model, args.n_message_layers, args.n_book_pre_layers, args.n_book_post_layers,
                 args.n_layers, args.vocab_size, args.token_mode)
+    arch = args.architecture
+    if a.tp > 1:   # the model's size: the replicated parameters once, the head slices from every rank
+        from sigma0_b200.models import build_model
+        n_params = sum(p.numel() for p in build_model(args).parameters())
     extras = {}
     if a.extras == "on" or (a.extras == "auto" and world == 1):
         # outside the headline region: free the headline trainer first
@@ -449,12 +453,12 @@ def main():
     if rank == 0:
         d_model, nml, nbpre, nbpost, nl, vocab, tmode = head_cfg
         out = {
-            "metric": "train tokens/s (max over ranks) Mamba3 LOB",
+            "metric": "train tokens/s (max over ranks) " + ("Mamba3 LOB" if arch == "mamba3" else f"{arch} LOB"),
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded order flow through the matching engine), random-init weights",
-            "config": {"model": f"mamba3-lob-{a.preset} ({n_params/1e6:.1f}M params, d_model {d_model}, "
+            "config": {"model": f"{arch}-lob-{a.preset} ({n_params/1e6:.1f}M params, d_model {d_model}, "
                                 f"{nml}+{nbpre}+{nbpost}+{nl} layers)",
                        "global_batch": Bm * dp_world, "seq_len": L,
                        "parallelism": f"tp{a.tp}xdp{dp_world}" if a.tp > 1 else f"dp{world}",
@@ -464,8 +468,8 @@ def main():
                        "vocab": vocab, "token_mode": tmode},
             "loss": float(loss), "gpu_launches": launches, "clocks": clk, "e2e": e2e,
             "peak_mem_gb": peak_gb,
-            "baseline_note": ("the reference publishes no rate for this 350m configuration (vs_baseline null); "
-                              "its 75m recipe rate is compared like for like under published_75m_config"),
+            "baseline_note": (f"the reference publishes no rate for the {a.preset} configuration (vs_baseline "
+                              "null); its 75m recipe rate is compared like for like under published_75m_config"),
         }
         out.update(extras)
         print(json.dumps(out))
