@@ -123,10 +123,15 @@ at::Tensor m3_segment_decay(const at::Tensor& adt, int64_t B, int64_t nh, int64_
 // prep is (bc, dt, adt, sig, rate, theta0) and `states` holds the S_in images for the backward.
 std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh, at::Tensor wB, at::Tensor wC,
                                at::Tensor dt_bias, at::Tensor Bb, at::Tensor Cb, at::Tensor D, double A_floor,
-                               double eps, bool want_final = false, bool return_prep = false) {
+                               double eps, bool want_final = false, bool return_prep = false,
+                               c10::optional<at::Tensor> init_state = c10::nullopt,
+                               c10::optional<at::Tensor> init_angle = c10::nullopt) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
-  const bool walker = m3_walker(proj, B, nh);
+  // a sequence continued from a carried state / angle (context parallelism) runs the walker
+  const bool carried = (init_state.has_value() && init_state->defined()) ||
+                       (init_angle.has_value() && init_angle->defined());
+  const bool walker = carried || m3_walker(proj, B, nh);
   M3Pre pre = m3_prepare(proj, B, L, nh, wB, wC, dt_bias, A_floor, eps, !walker);
   int nc = m3_nchunks((int)L);
   at::Tensor fin, thf;
@@ -151,7 +156,19 @@ std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh
       f.states = states.data_ptr();
       f.theta0 = theta0.data_ptr<float>();
     }
-    const int nseg = m3_segments(proj, B, nh, nc, 2);
+    if (carried) {
+      if (init_state.has_value() && init_state->defined()) {
+        req(*init_state, at::kFloat, "init_state");
+        TORCH_CHECK(init_state->numel() == B * nh * M3_P * M3_N, "init_state must be [B, nh, P, N]");
+        f.s0 = init_state->data_ptr<float>();
+      }
+      if (init_angle.has_value() && init_angle->defined()) {
+        req(*init_angle, at::kFloat, "init_angle");
+        TORCH_CHECK(init_angle->numel() == B * nh * M3_R, "init_angle must be [B, nh, R]");
+        f.th_in = init_angle->data_ptr<float>();
+      }
+    }
+    const int nseg = carried ? 1 : m3_segments(proj, B, nh, nc, 2);
     if (nseg == 1) {
       const int rc = m3_fwd_tc_launch(f, stream());
       TORCH_CHECK(rc == 0, "m3_fwd_tc launch failed (", rc, ")");
@@ -211,7 +228,9 @@ std::vector<at::Tensor> m3_fwd(at::Tensor proj, int64_t B, int64_t L, int64_t nh
 std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias,
                                   at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B, int64_t L, int64_t nh,
                                   double A_floor, double eps, c10::optional<at::Tensor> saved_states,
-                                  c10::optional<std::vector<at::Tensor>> saved_prep) {
+                                  c10::optional<std::vector<at::Tensor>> saved_prep,
+                                  c10::optional<at::Tensor> d_final = c10::nullopt, bool want_d_init = false) {
+  const bool carried = (d_final.has_value() && d_final->defined()) || want_d_init;
   M3Geo g = m3_geo(proj, B, L, nh);
   const int nc = m3_nchunks((int)L);
   at::Tensor bc, dt, adt, sig, rate, theta0, states;
@@ -235,7 +254,7 @@ std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB,
   auto dthl = at::empty({B * L, nh, M3_R}, f32);
   auto dthtot = at::empty({B, nh, nc, M3_R}, f32);
   auto dgam = at::empty({B, nh, L}, f32), dscl = at::empty({B, nh, L}, f32), dadt = at::empty({B, nh, L}, f32);
-  const int nseg = m3_segments(proj, B, nh, nc, 1);
+  const int nseg = carried ? 1 : m3_segments(proj, B, nh, nc, 1);
   auto dD = at::empty({B, nh, nseg}, f32), dCb = at::empty({B, nh, nseg, M3_N}, f32),
        dBb = at::empty({B, nh, nseg, M3_N}, f32);
   M3TcBwd f{};
@@ -251,6 +270,16 @@ std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB,
   f.status = m3_status(proj).data_ptr<int>();
   f.B = (int)B; f.L = (int)L; f.nh = (int)nh; f.ldp = g.ldp; f.lds = (int)L;
   f.nseg = nseg;
+  at::Tensor dinit;
+  if (d_final.has_value() && d_final->defined()) {
+    req(*d_final, at::kFloat, "d_final");
+    TORCH_CHECK(d_final->numel() == B * nh * M3_P * M3_N, "d_final must be [B, nh, P, N]");
+    f.ds_fin = d_final->data_ptr<float>();
+  }
+  if (want_d_init) {
+    dinit = at::empty({B, nh, M3_P, M3_N}, f32);
+    f.ds0 = dinit.data_ptr<float>();
+  }
   if (nseg == 1) {
     const int rc = m3_bwd_tc_launch(f, stream());
     TORCH_CHECK(rc == 0, "m3_bwd_tc launch failed (", rc, ")");
@@ -279,22 +308,34 @@ std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB,
                      dadt.data_ptr<float>(), dproj.data_ptr(), dwB.data_ptr<float>(), dwC.data_ptr<float>(),
                      ddtb.data_ptr<float>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {dproj, dwB, dwC, ddtb, dD.sum(at::IntArrayRef{0, 2}), dCb.sum(at::IntArrayRef{0, 2}),
-          dBb.sum(at::IntArrayRef{0, 2})};
+  std::vector<at::Tensor> out = {dproj, dwB, dwC, ddtb, dD.sum(at::IntArrayRef{0, 2}),
+                                 dCb.sum(at::IntArrayRef{0, 2}), dBb.sum(at::IntArrayRef{0, 2})};
+  if (want_d_init) {
+    // the initial angle shifts every token's angle: its gradient is the whole-sequence dtheta sum
+    auto dth0 = dthl.view({B, L, nh, M3_R}).select(1, 0) + dthtot.select(2, 0);
+    out.push_back(dinit);
+    out.push_back(dth0);
+  }
+  return out;
 }
 
 std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at::Tensor wC, at::Tensor dt_bias,
                                at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B, int64_t L, int64_t nh,
                                double A_floor, double eps, c10::optional<at::Tensor> saved_states,
-                               c10::optional<std::vector<at::Tensor>> saved_prep) {
+                               c10::optional<std::vector<at::Tensor>> saved_prep,
+                               c10::optional<at::Tensor> d_final = c10::nullopt, bool want_d_init = false) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
   req(dy, at::kBFloat16, "dy");
   // the saved forward tensors say which implementation wrote them (6 prep tensors: the walker)
+  const bool carried = (d_final.has_value() && d_final->defined()) || want_d_init;
   const bool walker = saved_prep.has_value() && saved_states.has_value() && saved_states->defined()
                           ? saved_prep->size() == 6
-                          : m3_walker(proj, B, nh);
-  if (walker) return m3_bwd_tc(proj, dy, wB, wC, dt_bias, Bb, Cb, D, B, L, nh, A_floor, eps, saved_states, saved_prep);
+                          : (carried || m3_walker(proj, B, nh));
+  TORCH_CHECK(walker || !carried, "a carried state gradient needs the walker's saved forward tensors");
+  if (walker)
+    return m3_bwd_tc(proj, dy, wB, wC, dt_bias, Bb, Cb, D, B, L, nh, A_floor, eps, saved_states, saved_prep, d_final,
+                     want_d_init);
   M3Pre pre;
   if (saved_prep.has_value() && saved_prep->size() == 7) {   // (bc, dt, adt, sig, rate, aend, theta0) of m3_fwd
     const auto& v = *saved_prep;
@@ -1025,13 +1066,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sigma0_b200 sm_100a kernels";
   m.def("m3_fwd", &m3_fwd, py::arg("proj"), py::arg("B"), py::arg("L"), py::arg("nh"), py::arg("wB"), py::arg("wC"),
         py::arg("dt_bias"), py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("A_floor"), py::arg("eps"),
-        py::arg("want_final") = false, py::arg("return_prep") = false,
-        "Mamba3 SSD forward (prep, chunk states, passing, chunk scan) -> (y, states, final state, final angle"
-        "[, bc, dt, adt, sig, rate, aend, theta0])");
+        py::arg("want_final") = false, py::arg("return_prep") = false, py::arg("init_state") = py::none(),
+        py::arg("init_angle") = py::none(),
+        "Mamba3 SSD forward -> (y, states, final state, final angle[, prep...]); init_state [B, nh, P, N] and "
+        "init_angle [B, nh, R] continue a sequence from a carry");
   m.def("m3_bwd", &m3_bwd, py::arg("proj"), py::arg("dy"), py::arg("wB"), py::arg("wC"), py::arg("dt_bias"),
         py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("B"), py::arg("L"), py::arg("nh"), py::arg("A_floor"),
         py::arg("eps"), py::arg("saved_states") = py::none(), py::arg("saved_prep") = py::none(),
-        "Mamba3 SSD backward -> (dproj, dB_norm, dC_norm, ddt_bias, dD, dC_bias, dB_bias)");
+        py::arg("d_final") = py::none(), py::arg("want_d_init") = false,
+        "Mamba3 SSD backward -> (dproj, dB_norm, dC_norm, ddt_bias, dD, dC_bias, dB_bias[, d_init_state, "
+        "d_init_angle]); d_final: gradient of the final state");
   m.def("ln_fwd", &ln_fwd);
   m.def("ln_bwd", &ln_bwd);
   m.def("rms_fwd", &rms_fwd);

@@ -241,3 +241,47 @@ def mamba3_sequence_layer(x: torch.Tensor, layer) -> torch.Tensor:
     if x.shape[-1] % 8:
         raise NotImplementedError("the fused layer path needs d_model % 8 == 0")
     return _LayerFn.apply(x, layer, *_layer_params(layer))
+
+
+class _SSDCarryFn(torch.autograd.Function):
+    """The SSD on a projection buffer, continued from a carried state and angle (context
+    parallelism): ``(proj, init_state, init_angle, params) -> (y, final_state)``, with the
+    gradients of both inputs from the reverse walker (the gradient of the final state enters
+    as its initial carry)."""
+
+    @staticmethod
+    def forward(ctx, proj, s0, th0, m, B, L, wB, wC, dt_bias, Bb, Cb, D):
+        C = ext()
+        d = m.dims
+        out = C.m3_fwd(proj, B, L, d.n_heads, wB, wC, dt_bias, Bb, Cb, D, m.A_floor, m.B_norm.eps,
+                       want_final=True, return_prep=True, init_state=s0,
+                       init_angle=th0 if th0 is not None else torch.zeros(B, d.n_heads, d.R, device=proj.device))
+        y, states, fin = out[0], out[1], out[2]
+        ctx.m, ctx.B, ctx.L = m, B, L
+        ctx.has_s0, ctx.has_th0 = s0 is not None, th0 is not None
+        ctx.save_for_backward(proj, states, wB, wC, dt_bias, Bb, Cb, D, *out[4:])
+        return y, fin
+
+    @staticmethod
+    def backward(ctx, dy, dfin):
+        C = ext()
+        proj, states, wB, wC, dt_bias, Bb, Cb, D, *prep = ctx.saved_tensors
+        m, B, L = ctx.m, ctx.B, ctx.L
+        d = m.dims
+        if dy is None:
+            dy = torch.zeros(B, L, d.d_inner, dtype=torch.bfloat16, device=proj.device)
+        res = C.m3_bwd(proj, dy.to(torch.bfloat16).contiguous(), wB, wC, dt_bias, Bb, Cb, D, B, L, d.n_heads,
+                       m.A_floor, m.B_norm.eps, saved_states=states, saved_prep=list(prep),
+                       d_final=dfin.float().contiguous() if dfin is not None else None, want_d_init=True)
+        dproj, dwB, dwC, ddtb, dD, dCb, dBb, ds0, dth0 = res
+        return (dproj, ds0 if ctx.has_s0 else None, dth0 if ctx.has_th0 else None, None, None, None,
+                dwB, dwC, ddtb, dCb, dBb, dD)
+
+
+def mamba3_ssd_carry(proj, m, B, L, init_state=None, init_angle=None):
+    """SSD of ``proj`` ([B*L, ldp] bf16, the module's projection layout) continued from
+    ``init_state`` ([B, nh, P, N] fp32) and ``init_angle`` ([B, nh, R]); returns
+    ``(y [B, L, d_inner] bf16, final_state [B, nh, P, N] fp32)``, differentiable in all."""
+    _check_dims(m)
+    return _SSDCarryFn.apply(proj, init_state, init_angle, m, B, L, m.B_norm.scale, m.C_norm.scale, m.dt_bias,
+                             m.B_bias, m.C_bias, m.D)

@@ -21,6 +21,12 @@ the whole mixer runs segment-parallel with autograd:
 
 All collectives are ``torch.distributed.nn.functional.all_gather`` (gradients
 flow back through reduce-scatter), so the backward pass is exact too.
+
+On CUDA (the module's ``impl == "cuda"`` geometry) steps 2 and 4 are the tcgen05 chunk
+walkers continued from a carried state and angle (``ops.mamba3_layer.mamba3_ssd_carry``):
+each pass is one forward kernel and, in the backward, one reverse kernel whose initial
+carry is the final-state gradient; the per-token prep, the boundary terms and the
+recurrence over ranks stay small torch expressions.
 """
 from __future__ import annotations
 
@@ -51,6 +57,8 @@ class Mamba3CP(nn.Module):
         self.group = group
 
     def forward(self, u: torch.Tensor) -> torch.Tensor:
+        if self.inner._cuda_ok(u):
+            return self._forward_cuda(u)
         m, d = self.inner, self.inner.dims
         W = dist.get_world_size(self.group)
         r = dist.get_rank(self.group)
@@ -99,6 +107,56 @@ class Mamba3CP(nn.Module):
         y = ref.mamba3_ssd_chunked(Ch, Bh, x, ADTt, DTt, trt, ang, m.C_bias, m.B_bias, m.D, z,
                                    chunk_size=d.chunk_size, initial_state=S_init, angle_offset=off)
         return m._post(y)
+
+    def _forward_cuda(self, u: torch.Tensor) -> torch.Tensor:
+        from ..ops.mamba3_layer import mamba3_ssd_carry
+        m, d = self.inner, self.inner.dims
+        W = dist.get_world_size(self.group)
+        r = dist.get_rank(self.group)
+        Bt, L, Hm = u.shape
+        nh, P, N, R = d.n_heads, d.headdim, d.d_state, d.R
+        proj = m.in_proj(u, dtype=torch.bfloat16).reshape(Bt * L, -1)
+        ldp = (d.d_in_proj + 7) // 8 * 8
+        if ldp != d.d_in_proj:
+            proj = F.pad(proj, (0, ldp - d.d_in_proj))
+        proj = proj.contiguous()
+        z, x, Bc, Cc, dd_dt, dd_A, trap, ang = m.split_proj(proj[:, :d.d_in_proj].float().view(Bt, L, -1))
+        DT = F.softplus(dd_dt + m.dt_bias)                                                # (Bt, L, nh)
+        A = torch.clamp(-F.softplus(dd_A), max=-m.A_floor)
+        rate = torch.tanh(ang) * math.pi                                                   # (Bt, L, R)
+        # 1. starting angles
+        tot = torch.einsum("blr,blh->bhr", rate, DT)                                      # (Bt, nh, R)
+        sums = _gather(tot, self.group)
+        off = sums[:r].sum(0) if r > 0 else torch.zeros_like(tot)
+        off = off - TWO_PI * torch.floor(off / TWO_PI)
+        # 2. local pass from a zero state
+        _, S_loc = mamba3_ssd_carry(proj, m, Bt, L, None, off)                             # (Bt, nh, P, N)
+        delta = torch.exp((A * DT).sum(1))                                                 # (Bt, nh)
+        th_last = off + tot
+        Kb = m.B_norm(Bc[:, -1])[:, None, :] + m.B_bias[None]                             # (Bt, nh, N)
+        k_last = ref.apply_rope(Kb, torch.cos(th_last), torch.sin(th_last))
+        v_last = x[:, -1].reshape(Bt, nh, P)
+        w0 = (1.0 - torch.sigmoid(trap[:, 0])) * DT[:, 0]                                 # (Bt, nh)
+        parts = [S_loc.reshape(Bt, nh, -1), delta[..., None], k_last, v_last, w0[..., None]]
+        sizes = [p.shape[-1] for p in parts]
+        allp = _gather(torch.cat(parts, -1), self.group)
+        allS, allD, allK, allV, allw = torch.split(allp, sizes, -1)
+        allS = allS.reshape(W, Bt, nh, P, N)
+        allD, allw = allD[..., 0], allw[..., 0]
+        # 3. boundary recurrence over ranks 0..r-1
+        S_end = torch.zeros_like(S_loc)
+        for k in range(r):
+            c = torch.zeros_like(S_loc) if k == 0 else \
+                allw[k][..., None, None] * allV[k - 1][..., :, None] * allK[k - 1][..., None, :]
+            S_end = allD[k][..., None, None] * (S_end + c) + allS[k]
+        if r > 0:
+            S_init = S_end + w0[..., None, None] * allV[r - 1][..., :, None] * allK[r - 1][..., None, :]
+        else:
+            S_init = torch.zeros_like(S_loc)
+        S_init = S_init + 0.0 * (allp.sum() + sums.sum())
+        # 4. the segment from its true initial state
+        y, _ = mamba3_ssd_carry(proj, m, Bt, L, S_init.contiguous(), off.contiguous())
+        return m._post(y.view(Bt, L, nh, P))
 
 
 def shard_model_cp(model: nn.Module, group=None) -> nn.Module:

@@ -350,3 +350,50 @@ def test_ssd_backward_with_saved_forward_tensors_matches_recompute(walker):
     # equal up to the summation order of the kernels' shared-memory atomics
     for a, b in zip(full, saved):
         assert rel(a, b) < 1e-3, rel(a, b)
+
+
+def test_ssd_carry_split_matches_whole_sequence():
+    """A sequence run as two pieces -- the second continued from the first one's final state
+    (plus the trapezoid coupling of the boundary tokens) and angle -- gives the whole
+    sequence's outputs, final state and gradients (the context-parallel building block)."""
+    import math
+    import torch.nn.functional as F
+    from sigma0_b200.ops.mamba3_layer import mamba3_ssd_carry
+    from sigma0_b200.ops.reference import mamba3_ref as ref
+    m, d, proj0 = _walker_args(2, 700, 512, 6)
+    B, L, L1 = 2, 700, 300
+    nh, P = d.n_heads, d.headdim
+    g = torch.randn(B, L, d.d_inner, device="cuda")
+
+    def run(split):
+        proj = proj0.clone().requires_grad_(True)
+        pv = proj.view(B, L, -1)
+        if not split:
+            y, fin = mamba3_ssd_carry(proj, m, B, L)
+        else:
+            pa, pb = pv[:, :L1].reshape(B * L1, -1).contiguous(), pv[:, L1:].reshape(B * (L - L1), -1).contiguous()
+            ya, fa = mamba3_ssd_carry(pa, m, B, L1)
+            z, x, Bc, Cc, dd_dt, dd_A, trap, ang = m.split_proj(pv[..., :d.d_in_proj].float())
+            DT = F.softplus(dd_dt + m.dt_bias)
+            tot = torch.einsum("blr,blh->bhr", torch.tanh(ang[:, :L1]) * math.pi, DT[:, :L1])
+            th = tot - 2 * math.pi * torch.floor(tot / (2 * math.pi))
+            Kb = m.B_norm(Bc[:, L1 - 1])[:, None, :] + m.B_bias[None]
+            k_last = ref.apply_rope(Kb, torch.cos(th), torch.sin(th))
+            v_last = x[:, L1 - 1].reshape(B, nh, P)
+            w0 = (1.0 - torch.sigmoid(trap[:, L1])) * DT[:, L1]
+            s_in = fa + w0[..., None, None] * v_last[..., :, None] * k_last[..., None, :]
+            yb, fin = mamba3_ssd_carry(pb, m, B, L - L1, s_in.contiguous(), th.contiguous())
+            y = torch.cat([ya, yb], 1)
+        for p_ in (m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D):
+            p_.grad = None
+        ((y.float() * g).sum() + fin.sum() * 1e-3).backward()
+        grads = [p_.grad.clone() for p_ in (m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D)]
+        return y.detach(), fin.detach(), proj.grad.detach(), grads
+
+    yw, fw, gw, pw = run(False)
+    ys, fs, gs, ps = run(True)
+    assert rel(ys, yw) < 1e-2, rel(ys, yw)
+    assert rel(fs, fw) < 1e-2, rel(fs, fw)
+    assert rel(gs[:, :d.d_in_proj], gw[:, :d.d_in_proj]) < 3e-2, rel(gs, gw)
+    for a, b in zip(ps, pw):
+        assert rel(a, b) < 3e-2, rel(a, b)
