@@ -182,3 +182,58 @@ def test_gdn_tensor_parallel_fused_out_proj_matches_nccl(tmp_path):
     res = torch.load(out)
     for a, b in zip(res[True], res[False]):
         assert ((a - b).norm() / b.norm()).item() < 2e-2
+
+
+def _cp_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from sigma0_b200.models.mamba3 import Mamba3
+        from sigma0_b200.parallel.cp import Mamba3CP
+        torch.manual_seed(0)
+        m = Mamba3(512, impl="cuda").cuda()
+        with torch.no_grad():
+            m.B_bias.normal_(0, 0.5)
+            m.C_bias.normal_(0, 0.5)
+        B, L = 2, 1200
+        gen = torch.Generator(device="cuda").manual_seed(3)
+        x = torch.randn(B, L, 512, device="cuda", generator=gen)
+        gy = torch.randn(B, L, 512, device="cuda", generator=gen)
+        seg = L // world
+        xr = x[:, rank * seg:(rank + 1) * seg].clone().requires_grad_(True)
+        y = Mamba3CP(m, None)(xr)
+        (y.float() * gy[:, rank * seg:(rank + 1) * seg]).sum().backward()
+        grads = torch.cat([p.grad.reshape(-1) for p in m.parameters()])
+        dist.all_reduce(grads)
+        ys = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(ys, y.detach().contiguous())
+        gx = [torch.empty_like(xr.grad) for _ in range(world)]
+        dist.all_gather(gx, xr.grad.contiguous())
+        if rank == 0:
+            for p in m.parameters():
+                p.grad = None
+            xf = x.clone().requires_grad_(True)
+            yf = m(xf)                                    # one GPU, the whole sequence
+            (yf.float() * gy).sum().backward()
+            gref = torch.cat([p.grad.reshape(-1) for p in m.parameters()])
+            torch.save({"y": torch.cat(ys, 1).float().cpu(), "yf": yf.detach().float().cpu(),
+                        "gx": torch.cat(gx, 1).float().cpu(), "gxf": xf.grad.float().cpu(),
+                        "g": grads.float().cpu(), "gf": gref.float().cpu()}, out)
+    finally:
+        dist.destroy_process_group()
+
+
+@need2
+def test_mamba3_context_parallel_on_the_walkers_matches_one_gpu(tmp_path):
+    """Mamba3 context parallelism on 2 GPUs (CUDA chunk walkers carried across the segment
+    boundary) against the whole sequence on one GPU: outputs, input and parameter gradients."""
+    out = str(tmp_path / "cp.pt")
+    mp.spawn(_cp_worker, args=(2, _port(), out), nprocs=2, join=True)
+    r = torch.load(out)
+    rel = lambda a, b: ((a - b).norm() / b.norm()).item()
+    assert rel(r["y"], r["yf"]) < 2e-2, rel(r["y"], r["yf"])
+    assert rel(r["gx"], r["gxf"]) < 3e-2, rel(r["gx"], r["gxf"])
+    assert rel(r["g"], r["gf"]) < 3e-2, rel(r["g"], r["gf"])
