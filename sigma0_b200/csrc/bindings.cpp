@@ -229,7 +229,8 @@ std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB,
                                   at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B, int64_t L, int64_t nh,
                                   double A_floor, double eps, c10::optional<at::Tensor> saved_states,
                                   c10::optional<std::vector<at::Tensor>> saved_prep,
-                                  c10::optional<at::Tensor> d_final = c10::nullopt, bool want_d_init = false) {
+                                  c10::optional<at::Tensor> d_final = c10::nullopt, bool want_d_init = false,
+                                  c10::optional<at::Tensor> final_state = c10::nullopt) {
   const bool carried = (d_final.has_value() && d_final->defined()) || want_d_init;
   M3Geo g = m3_geo(proj, B, L, nh);
   const int nc = m3_nchunks((int)L);
@@ -274,7 +275,12 @@ std::vector<at::Tensor> m3_bwd_tc(at::Tensor proj, at::Tensor dy, at::Tensor wB,
   if (d_final.has_value() && d_final->defined()) {
     req(*d_final, at::kFloat, "d_final");
     TORCH_CHECK(d_final->numel() == B * nh * M3_P * M3_N, "d_final must be [B, nh, P, N]");
+    TORCH_CHECK(final_state.has_value() && final_state->defined(),
+                "d_final needs the forward's final state (its decay gradient)");
+    req(*final_state, at::kFloat, "final_state");
+    TORCH_CHECK(final_state->numel() == B * nh * M3_P * M3_N, "final_state must be [B, nh, P, N]");
     f.ds_fin = d_final->data_ptr<float>();
+    f.s_fin = final_state->data_ptr<float>();
   }
   if (want_d_init) {
     dinit = at::empty({B, nh, M3_P, M3_N}, f32);
@@ -323,7 +329,8 @@ std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at
                                at::Tensor Bb, at::Tensor Cb, at::Tensor D, int64_t B, int64_t L, int64_t nh,
                                double A_floor, double eps, c10::optional<at::Tensor> saved_states,
                                c10::optional<std::vector<at::Tensor>> saved_prep,
-                               c10::optional<at::Tensor> d_final = c10::nullopt, bool want_d_init = false) {
+                               c10::optional<at::Tensor> d_final = c10::nullopt, bool want_d_init = false,
+                               c10::optional<at::Tensor> final_state = c10::nullopt) {
   c10::cuda::CUDAGuard guard(proj.device());
   M3Geo g = m3_geo(proj, B, L, nh);
   req(dy, at::kBFloat16, "dy");
@@ -335,7 +342,7 @@ std::vector<at::Tensor> m3_bwd(at::Tensor proj, at::Tensor dy, at::Tensor wB, at
   TORCH_CHECK(walker || !carried, "a carried state gradient needs the walker's saved forward tensors");
   if (walker)
     return m3_bwd_tc(proj, dy, wB, wC, dt_bias, Bb, Cb, D, B, L, nh, A_floor, eps, saved_states, saved_prep, d_final,
-                     want_d_init);
+                     want_d_init, final_state);
   M3Pre pre;
   if (saved_prep.has_value() && saved_prep->size() == 7) {   // (bc, dt, adt, sig, rate, aend, theta0) of m3_fwd
     const auto& v = *saved_prep;
@@ -1073,7 +1080,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("m3_bwd", &m3_bwd, py::arg("proj"), py::arg("dy"), py::arg("wB"), py::arg("wC"), py::arg("dt_bias"),
         py::arg("Bb"), py::arg("Cb"), py::arg("D"), py::arg("B"), py::arg("L"), py::arg("nh"), py::arg("A_floor"),
         py::arg("eps"), py::arg("saved_states") = py::none(), py::arg("saved_prep") = py::none(),
-        py::arg("d_final") = py::none(), py::arg("want_d_init") = false,
+        py::arg("d_final") = py::none(), py::arg("want_d_init") = false, py::arg("final_state") = py::none(),
         "Mamba3 SSD backward -> (dproj, dB_norm, dC_norm, ddt_bias, dD, dC_bias, dB_bias[, d_init_state, "
         "d_init_angle]); d_final: gradient of the final state");
   m.def("ln_fwd", &ln_fwd);

@@ -53,6 +53,7 @@ struct M3TcBwd {
   const void* states;                       // the forward's S_in images
   const float* theta0;                      // the forward's chunk-start angles [B, nh, nc, R]
   const float* ds_fin;                      // [B, nh, P, N] gradient of the final state or null
+  const float* s_fin;                       // [B, nh, P, N] the final state (needed with ds_fin) or null
   float* ds0;                               // [B, nh, P, N] gradient of the initial state or null
   void* dproj;                              // [B, L, ldp] bf16: z and x columns written
   void *gQ, *gK;                            // [B, L, nh * N] bf16

@@ -517,6 +517,7 @@ struct BwdArgs {
   const bf16* states;            // the forward's S_in images
   const float* theta0;           // the forward's chunk-start angles
   const float* ds_fin;           // [B, nh, nseg, P, N] gradient of each segment's final state, or null
+  const float* s_fin;            // [B, nh, P, N] the final state (with ds_fin at the sequence end), or null
   float* ds0;                    // [B, nh, nseg, P, N] gradient of each segment's initial state, or null
   float *dthl, *dthtot, *dgam, *dscl, *dadt;
   float *dD, *dCb, *dBb;         // [B, nh, nseg], [B, nh, nseg, N] x2 (partial sums per segment)
@@ -763,6 +764,10 @@ __global__ void __launch_bounds__(BNT, 1)
                        pack_bf16(v[8 * k + 4], v[8 * k + 5]), pack_bf16(v[8 * k + 6], v[8 * k + 7]));
       float dot = 0.f;
       if (j == 0 && edge) ok = wait(&sm.edge, 0) && ok;
+      if (j == 0 && !edge && have_fin && a.s_fin) {   // S_out of the last chunk is the final state
+#pragma unroll
+        for (int k = 0; k < 16; ++k) dot += v[k] * a.s_fin[(slot * P + c16 + k) * N + n];
+      }
       if (j > 0 || edge) {   // S_out(c) = S_in(c+1): the other stage holds its image
         const unsigned char* so = sm.stage[(j + 1) & 1].sin_;
 #pragma unroll
@@ -1224,7 +1229,7 @@ int m3_bwd_tc_launch(const M3TcBwd& f, cudaStream_t st) {
   a.dt = f.dt; a.adt = f.adt; a.sig = f.sig; a.rate = f.rate;
   a.Bb = f.Bb; a.Cb = f.Cb; a.D = f.D;
   a.states = reinterpret_cast<const bf16*>(f.states);
-  a.theta0 = f.theta0; a.ds_fin = f.ds_fin; a.ds0 = f.ds0;
+  a.theta0 = f.theta0; a.ds_fin = f.ds_fin; a.s_fin = f.s_fin; a.ds0 = f.ds0;
   a.dthl = f.dthl; a.dthtot = f.dthtot; a.dgam = f.dgam; a.dscl = f.dscl; a.dadt = f.dadt;
   a.dD = f.dD; a.dCb = f.dCb; a.dBb = f.dBb; a.status = f.status;
   a.B = f.B; a.L = f.L; a.nh = f.nh; a.ldp = f.ldp; a.lds = f.lds; a.nc = (f.L + CS - 1) / CS;

@@ -259,23 +259,24 @@ class _SSDCarryFn(torch.autograd.Function):
         y, states, fin = out[0], out[1], out[2]
         ctx.m, ctx.B, ctx.L = m, B, L
         ctx.has_s0, ctx.has_th0 = s0 is not None, th0 is not None
-        ctx.save_for_backward(proj, states, wB, wC, dt_bias, Bb, Cb, D, *out[4:])
+        ctx.save_for_backward(proj, states, fin, wB, wC, dt_bias, Bb, Cb, D, *out[4:])
         return y, fin
 
     @staticmethod
     def backward(ctx, dy, dfin):
         C = ext()
-        proj, states, wB, wC, dt_bias, Bb, Cb, D, *prep = ctx.saved_tensors
+        proj, states, fin, wB, wC, dt_bias, Bb, Cb, D, *prep = ctx.saved_tensors
         m, B, L = ctx.m, ctx.B, ctx.L
         d = m.dims
         if dy is None:
             dy = torch.zeros(B, L, d.d_inner, dtype=torch.bfloat16, device=proj.device)
         res = C.m3_bwd(proj, dy.to(torch.bfloat16).contiguous(), wB, wC, dt_bias, Bb, Cb, D, B, L, d.n_heads,
                        m.A_floor, m.B_norm.eps, saved_states=states, saved_prep=list(prep),
-                       d_final=dfin.float().contiguous() if dfin is not None else None, want_d_init=True)
+                       d_final=dfin.float().contiguous() if dfin is not None else None, want_d_init=True,
+                       final_state=fin)
         dproj, dwB, dwC, ddtb, dD, dCb, dBb, ds0, dth0 = res
         return (dproj, ds0 if ctx.has_s0 else None, dth0 if ctx.has_th0 else None, None, None, None,
-                dwB, dwC, ddtb, dCb, dBb, dD)
+                dwB, dwC, ddtb, dBb, dCb, dD)
 
 
 def mamba3_ssd_carry(proj, m, B, L, init_state=None, init_angle=None):
