@@ -160,6 +160,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--no_oracle_speed", action="store_true")
+    ap.add_argument("--skip_parity", action="store_true", help="timings only (e.g. under a profiler)")
     ap.add_argument("--impl", choices=["auto", "walker", "chunked"], default="auto",
                     help="walker: the tcgen05 chunk walkers; chunked: the chunk-parallel mma.sync kernels; "
                          "auto: the walkers when (sequences x heads) >= SMs")
@@ -168,7 +169,7 @@ def main(argv=None):
         raise SystemExit("the SSD kernel bench needs a CUDA device")
     from ..ops._ext import ext
     ext().m3_use_tc(None if a.impl == "auto" else a.impl == "walker")
-    par = parity(a.nh, a.parity_L)
+    par = None if a.skip_parity else parity(a.nh, a.parity_L)
     for L in a.L:
         rec = {"impl": a.impl, "nh": a.nh, "N": 128, "P": 64, "CS": 64, "B": a.B, "L": L, "parity_L": a.parity_L,
                "parity_rel_l2": par}
