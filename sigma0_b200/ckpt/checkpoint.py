@@ -1,9 +1,12 @@
 """Checkpoint save / restore for the flat-buffer trainer.
 
-Directory layout and retention are modelled on the reference's Orbax manager
-(``run/base_model/runtime/train.py:538-578``); the array format is NOT Orbax: arrays
-are raw little-endian float32 files plus a JSON leaf table, so Orbax checkpoints are
-not read here.  ``export_params_npz`` exchanges weights by Flax path.  Files:
+Two formats under the reference's Orbax-manager directory layout and retention
+(``run/base_model/runtime/train.py:538-578``): ``fmt="native"`` (default) writes raw
+little-endian float32 flat buffers plus a JSON leaf table with SHA-256 hashes (fast,
+sharded moments); ``fmt="orbax"`` writes the Orbax ``StandardSave`` / ``JsonSave`` layout
+(zarr v2 arrays under Flax key paths, ``ckpt/orbax.py``).  ``restore`` reads either, by
+Flax path; Orbax checkpoints stored in OCDBT databases are refused (no codec here).
+``export_params_npz`` exchanges weights by Flax path.  Native files:
 
     <base>/<step>/state/params.f32          float32 flat parameter buffer
     <base>/<step>/state/adam_m.r<k>.f32     Adam first moment, rank k's shard
@@ -67,7 +70,10 @@ class CheckpointError(RuntimeError):
 
 class CheckpointManager:
     def __init__(self, base_dir: str, max_to_keep: int = 10, keep_period: int = 5, rank: int = 0, world: int = 1,
-                 barrier=None):
+                 barrier=None, fmt: str = "native"):
+        if fmt not in ("native", "orbax"):
+            raise ValueError(f"checkpoint format must be 'native' or 'orbax', not {fmt!r}")
+        self.fmt = fmt
         self.base = base_dir
         self.max_to_keep, self.keep_period = max_to_keep, keep_period
         self.rank, self.world = rank, world
@@ -101,6 +107,8 @@ class CheckpointManager:
              blocking: bool = False) -> str:
         """Snapshot ``trainer`` (flat params, Adam moments, step) as ``<base>/<step>``."""
         self.wait()
+        if self.fmt == "orbax":
+            return self._save_orbax(step, trainer, metrics, config)
         opt = trainer.opt
         tmp = os.path.join(self.base, f".{step}.tmp")
         final = os.path.join(self.base, str(step))
@@ -186,9 +194,45 @@ class CheckpointManager:
             if s not in keep and not (self.keep_period and s % self.keep_period == 0):
                 shutil.rmtree(os.path.join(self.base, str(s)), ignore_errors=True)
 
+    def _save_orbax(self, step: int, trainer, metrics, config) -> str:
+        """The step in the Orbax layout (``ckpt/orbax.py``): ``state`` = {params, step,
+        opt_state/{mu, nu} (unsharded optimizers)}, ``metadata`` = the JSON record."""
+        from . import orbax as ox
+        opt = trainer.opt
+        tmp = os.path.join(self.base, f".{step}.tmp")
+        final = os.path.join(self.base, str(step))
+        if self.rank == 0:
+            tree = ox.params_tree(trainer.model)
+            tree[("step",)] = np.asarray(opt.step_count, dtype=np.int64)
+            if not getattr(opt, "sharded", False):
+                for n, p in zip(opt.names, opt.params_in_order()):
+                    a, b = opt.slices[n]
+                    kp = tuple(flax_path(n).split("/"))[1:]
+                    tree[("opt_state", "mu") + kp] = opt.m[a:b].view(p.shape).detach().cpu().numpy()
+                    tree[("opt_state", "nu") + kp] = opt.v[a:b].view(p.shape).detach().cpu().numpy()
+            meta = {"step": int(step), "optimizer_step": int(opt.step_count), "trainer_step": int(trainer.step_idx),
+                    "global_batch": int(getattr(trainer, "global_batch", 0)), "world": self.world,
+                    "config": config or {}, "metrics": metrics or {}, "format": "orbax"}
+            shutil.rmtree(tmp, ignore_errors=True)
+            ox.write_step(tmp, tree, meta)
+            shutil.rmtree(final, ignore_errors=True)
+            os.replace(tmp, final)
+            self._retain()
+        self.barrier()
+        return final
+
     # -- restore ----------------------------------------------------------------------------
     def verify(self, step: int) -> bool:
         d = os.path.join(self.base, str(step))
+        from . import orbax as ox
+        if ox.is_orbax_step(d):      # no hashes in that layout: every listed array must have its header
+            try:
+                with open(os.path.join(d, "state", "_METADATA")) as f:
+                    import ast
+                    kps = [ast.literal_eval(k) for k in json.load(f)["tree_metadata"]]
+                return all(os.path.exists(os.path.join(d, "state", ".".join(kp), ".zarray")) for kp in kps)
+            except (OSError, KeyError, ValueError, SyntaxError):
+                return False
         try:
             with open(os.path.join(d, "metadata", "metadata")) as f:
                 meta = json.load(f)
@@ -216,6 +260,9 @@ class CheckpointManager:
         d = os.path.join(self.base, str(chosen))
         with open(os.path.join(d, "metadata", "metadata")) as f:
             meta = json.load(f)
+        from . import orbax as ox
+        if ox.is_orbax_step(d):
+            return self._restore_orbax(trainer, d, meta, chosen, params_only)
         with open(os.path.join(d, "state", "index.json")) as f:
             index = json.load(f)
         opt = trainer.opt
@@ -248,6 +295,29 @@ class CheckpointManager:
                                       int(meta["optimizer_step"]))
                 gb_new = int(getattr(trainer, "global_batch", 0))
                 trainer.step_idx = remap_step(int(meta["trainer_step"]), int(meta.get("global_batch", 0)), gb_new)
+        meta["restored_step"] = chosen
+        return meta
+
+    def _restore_orbax(self, trainer, d: str, meta: Dict, chosen: int, params_only: bool) -> Dict:
+        from . import orbax as ox
+        tree = ox.read_standard_item(os.path.join(d, "state"))
+        opt = trainer.opt
+        ox.load_params_into(trainer.model, {k: v for k, v in tree.items() if k[0] == "params"})
+        with torch.no_grad():
+            opt.refresh_shadow()
+            has_mom = any(k[:2] == ("opt_state", "mu") for k in tree)
+            if not params_only and has_mom:
+                m = torch.zeros(opt.numel, dtype=torch.float32)
+                v = torch.zeros(opt.numel, dtype=torch.float32)
+                for n in opt.names:
+                    a, b = opt.slices[n]
+                    kp = tuple(flax_path(n).split("/"))[1:]
+                    m[a:b] = torch.from_numpy(np.ascontiguousarray(tree[("opt_state", "mu") + kp])).reshape(-1)
+                    v[a:b] = torch.from_numpy(np.ascontiguousarray(tree[("opt_state", "nu") + kp])).reshape(-1)
+                opt.load_full_moments(m.to(opt.device), v.to(opt.device), int(meta.get("optimizer_step", 0)))
+            if not params_only:
+                trainer.step_idx = remap_step(int(meta.get("trainer_step", chosen)), int(meta.get("global_batch", 0)),
+                                              int(getattr(trainer, "global_batch", 0)))
         meta["restored_step"] = chosen
         return meta
 

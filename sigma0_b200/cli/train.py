@@ -43,6 +43,8 @@ def parse(argv=None):
     p.add_argument("--ignore_times", action="store_true")
     p.add_argument("--ckpt_dir", default=None)
     p.add_argument("--save_every", type=int, default=0)
+    p.add_argument("--ckpt_format", choices=["native", "orbax"], default="native",
+                   help="native flat buffers, or the Orbax StandardSave layout (zarr arrays by Flax path)")
     p.add_argument("--no_resume", action="store_true")
     p.add_argument("--log_every", type=int, default=100)
     p.add_argument("--watchdog_timeout", type=float, default=900.0)
@@ -110,6 +112,7 @@ def main(argv=None):
             yield collate([ds[i] for i in idx])
     cfg = LoopConfig(steps=a.steps, log_every=a.log_every, save_every=a.save_every, ckpt_dir=a.ckpt_dir,
                      resume=not a.no_resume, watchdog_timeout=a.watchdog_timeout, time_limit_s=a.time_limit_s,
+                     ckpt_format=a.ckpt_format,
                      config={k: v for k, v in vars(args).items() if isinstance(v, (int, float, str, bool))})
     log = (lambda r: print(json.dumps(r), flush=True)) if rank == 0 else (lambda r: None)
     res = fit(trainer, batches(), cfg, log=log)

@@ -112,6 +112,7 @@ class LoopConfig:
     time_limit_s: Optional[float] = None    # wall-clock budget; save this long before it
     save_margin_s: float = 300.0
     config: Dict = field(default_factory=dict)
+    ckpt_format: str = "native"           # "native" flat buffers or the Orbax StandardSave layout
 
 
 @dataclass
@@ -129,8 +130,8 @@ def fit(trainer, batches: Iterable, cfg: LoopConfig, log: Callable[[Dict], None]
     from ..models.flops import lob_model_flops, measured_bf16_peak
     log = log or (lambda rec: print(rec, flush=True))
     barrier = (lambda: torch.distributed.barrier()) if trainer.world > 1 else None
-    mgr = CheckpointManager(cfg.ckpt_dir, rank=trainer.rank, world=trainer.world, barrier=barrier) \
-        if cfg.ckpt_dir else None
+    mgr = CheckpointManager(cfg.ckpt_dir, rank=trainer.rank, world=trainer.world, barrier=barrier,
+                            fmt=cfg.ckpt_format) if cfg.ckpt_dir else None
     start = 0
     if mgr is not None and cfg.resume and mgr.latest_step() is not None:
         meta = mgr.restore(trainer)
