@@ -12,7 +12,8 @@ import torch
 def add_model_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--preset", default="350m", help="model preset (smoke, 75m, 350m)")
     p.add_argument("--architecture", default=None, help="backbone name; must match the checkpoint when restoring")
-    p.add_argument("--token_mode", default=None, help="22tok/23tok/24tok/26tok (default: the preset's)")
+    p.add_argument("--token_mode", default=None,
+                   help="22tok/23tok/24tok/26tok, or 1tok (the one-position-per-message model; default: the preset's)")
     p.add_argument("--n_layers", type=int, default=None)
     p.add_argument("--d_model", type=int, default=None)
     p.add_argument("--impl", default=None, help="cuda (kernels) or torch (reference path)")
@@ -26,8 +27,9 @@ def model_args(a: argparse.Namespace, **extra):
     kw.update(extra)
     if kw.get("token_mode"):
         from ..encoding import get_tokenizer
-        tok = get_tokenizer(kw["token_mode"])
-        kw.setdefault("msg_len", tok.MSG_LEN)
+        from ..encoding.tok1 import encoding_mode
+        tok = get_tokenizer(encoding_mode(kw["token_mode"]))
+        kw.setdefault("msg_len", 1 if kw["token_mode"] == "1tok" else tok.MSG_LEN)
     return preset_args(a.preset, **kw)
 
 

@@ -1067,6 +1067,53 @@ void dp_fused_adam(std::vector<int64_t> G, std::vector<int64_t> P, std::vector<i
   TORCH_CHECK(rc == 0, "dp_fused_adam launch failed: ", rc > 0 ? cudaGetErrorString((cudaError_t)rc) : "occupancy");
 }
 
+// ---- embedding gathers -------------------------------------------------------------------
+at::Tensor embed_sum_fwd(std::vector<at::Tensor> tables, at::Tensor idx) {
+  TORCH_CHECK(!tables.empty() && (int)tables.size() <= EMBED_MAX_FIELDS, "1..", EMBED_MAX_FIELDS, " tables");
+  req(idx, at::kLong, "idx");
+  c10::cuda::CUDAGuard guard(idx.device());
+  const int nf = (int)tables.size();
+  const int64_t D = tables[0].size(1);
+  TORCH_CHECK(idx.size(-1) == nf, "idx [..., n_fields]");
+  EmbedSumArgs a{};
+  for (int f = 0; f < nf; ++f) {
+    req(tables[f], at::kFloat, "table");
+    TORCH_CHECK(tables[f].dim() == 2 && tables[f].size(1) == D, "tables [rows, D] with one D");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(tables[f].data_ptr()) % 16 == 0, "tables must be 16-byte aligned");
+    a.tab[f] = tables[f].data_ptr<float>();
+    a.rows[f] = (int)tables[f].size(0);
+  }
+  const int64_t T = idx.numel() / nf;
+  auto sizes = idx.sizes().vec();
+  sizes.back() = D;
+  auto out = at::empty(sizes, tables[0].options());
+  a.nf = nf; a.D = (int)D; a.idx = reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()); a.out = out.data_ptr<float>(); a.T = T;
+  const int rc = embed_sum_fwd_launch(a, stream());
+  TORCH_CHECK(rc == 0, "embed_sum_fwd failed (", rc, "): D must be a multiple of 4");
+  return out;
+}
+
+void embed_sum_bwd(std::vector<at::Tensor> grads, at::Tensor dout, at::Tensor idx) {
+  req(idx, at::kLong, "idx");
+  req(dout, at::kFloat, "dout");
+  c10::cuda::CUDAGuard guard(idx.device());
+  const int nf = (int)grads.size();
+  TORCH_CHECK(nf >= 1 && nf <= EMBED_MAX_FIELDS && idx.size(-1) == nf, "one gradient table per field");
+  const int64_t D = dout.size(-1);
+  EmbedSumBwdArgs a{};
+  for (int f = 0; f < nf; ++f) {
+    req(grads[f], at::kFloat, "grad");
+    TORCH_CHECK(grads[f].dim() == 2 && grads[f].size(1) == D, "gradient tables [rows, D]");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(grads[f].data_ptr()) % 16 == 0, "gradients must be 16-byte aligned");
+    a.gtab[f] = grads[f].data_ptr<float>();
+    a.rows[f] = (int)grads[f].size(0);
+  }
+  a.nf = nf; a.D = (int)D; a.idx = reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()); a.dout = dout.data_ptr<float>();
+  a.T = idx.numel() / nf;
+  const int rc = embed_sum_bwd_launch(a, stream());
+  TORCH_CHECK(rc == 0, "embed_sum_bwd failed (", rc, ")");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -1083,6 +1130,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("d_final") = py::none(), py::arg("want_d_init") = false, py::arg("final_state") = py::none(),
         "Mamba3 SSD backward -> (dproj, dB_norm, dC_norm, ddt_bias, dD, dC_bias, dB_bias[, d_init_state, "
         "d_init_angle]); d_final: gradient of the final state");
+  m.def("embed_sum_fwd", &embed_sum_fwd, "sum over fields of each field table's row: [..., nf] ids -> [..., D]");
+  m.def("embed_sum_bwd", &embed_sum_bwd, "scatter-add of the output gradient into each field table's gradient");
   m.def("ln_fwd", &ln_fwd);
   m.def("ln_bwd", &ln_bwd);
   m.def("rms_fwd", &rms_fwd);

@@ -82,6 +82,27 @@ void m3_prep_bwd_launch(const M3Geo& g, const void* proj, const float* wB, const
                         const float* dadt, void* dproj, float* dwB, float* dwC, float* ddt_bias,
                         cudaStream_t st);
 
+// ---- embedding gathers (embed.cu) --------------------------------------------------------
+#define EMBED_MAX_FIELDS 32
+struct EmbedSumArgs {
+  const float* tab[EMBED_MAX_FIELDS];   // one fp32 table [rows_f, D] per field
+  int rows[EMBED_MAX_FIELDS];
+  int nf, D;
+  const long long* idx;                 // [T, nf] row ids
+  float* out;                           // [T, D] = sum over fields of tab_f[idx[t, f]]
+  long long T;
+};
+struct EmbedSumBwdArgs {
+  float* gtab[EMBED_MAX_FIELDS];        // gradient of each table (accumulated)
+  int rows[EMBED_MAX_FIELDS];
+  int nf, D;
+  const long long* idx;
+  const float* dout;                    // [T, D]
+  long long T;
+};
+int embed_sum_fwd_launch(const EmbedSumArgs& a, cudaStream_t st);
+int embed_sum_bwd_launch(const EmbedSumBwdArgs& a, cudaStream_t st);
+
 // ---- fused row/elementwise ops, loss and optimizer (fused_ops.cu) -------------------
 void ln_fwd_launch(const float* x, const float* w, const float* b, void* y, float* mean, float* rstd, long T,
                    int D, float eps, int sms, cudaStream_t st);

@@ -35,7 +35,11 @@ class LobWindowDataset(torch.utils.data.Dataset):
                  token_mode: str = "22tok", book_depth: int = 500, use_book_data: bool = True,
                  stride: Optional[int] = None, return_raw_msgs: bool = False, mask="no_mask",
                  book_ablation: str = "real", seed: int = 0):
-        self.tok = get_tokenizer(token_mode)
+        from ..encoding.tok1 import encoding_mode
+        self.one_token = token_mode == "1tok"      # 24tok messages as one row of 24 field ids each
+        self.tok = get_tokenizer(encoding_mode(token_mode))
+        if self.one_token and mask == "no_mask":
+            mask = "no_mask_1tok"
         self.mask, self.book_ablation, self.seed = mask, book_ablation, seed
         self.n = n_messages
         self.book_depth = book_depth
@@ -74,6 +78,10 @@ class LobWindowDataset(torch.utils.data.Dataset):
             x = enc.reshape(-1)
             y = x.copy()
             x = np.concatenate([[START_TOK], x[:-1]])
+        elif self.mask == "no_mask_1tok":      # per-field local indices, shifted by one message
+            from ..encoding.tok1 import global_to_local
+            (x, _), y = M.no_mask_1tok(enc)
+            x, y = global_to_local(x), global_to_local(y)
         elif self.mask == "inference":
             (x, _), y = M.inference_mask(enc)
         else:

@@ -35,3 +35,9 @@ def global_to_local(tokens) -> np.ndarray:
 def local_to_global(tokens) -> np.ndarray:
     t = np.asarray(tokens)
     return np.where(t < N_SPECIAL, t, t + FIELD_OFFSETS - N_SPECIAL).astype(np.int32)
+
+
+def encoding_mode(token_mode: str) -> str:
+    """The message encoding under a run's ``token_mode``: the 1-token model reads 24tok
+    messages (and maps them to per-field local indices); other modes are themselves."""
+    return "24tok" if token_mode == "1tok" else token_mode

@@ -72,28 +72,41 @@ class Embed(nn.Module):
         self.embedding = nn.Parameter(torch.randn(n, d) / math.sqrt(d))
 
     def forward(self, idx):
-        if self.embedding.requires_grad and torch.is_grad_enabled() and idx.is_cuda:
-            return _EmbedGather.apply(self.embedding, idx)
+        if idx.is_cuda and self.embedding.dtype == torch.float32 and self.embedding.shape[1] % 4 == 0:
+            return _EmbedGather.apply(idx.long().unsqueeze(-1), self.embedding)
         return self.embedding[idx]
 
 
 class _EmbedGather(torch.autograd.Function):
-    """Row gather whose backward is one scatter-add (atomic index_add) instead of the
-    sort-based dense embedding backward, which is two orders of magnitude slower for
-    a 12k-row table and ~10^5 lookups."""
+    """Row gather of one or more tables summed (``csrc/embed.cu``: one warp per token in the
+    forward, a vector-atomic scatter-add in the backward -- the sort-based dense embedding
+    backward is two orders of magnitude slower for a 12k-row table and ~10^5 lookups)."""
 
     @staticmethod
-    def forward(ctx, weight, idx):
+    def forward(ctx, idx, *weights):
+        from ..ops._ext import ext
         ctx.save_for_backward(idx)
-        ctx.shape = weight.shape
-        return weight[idx]
+        ctx.shapes = [w.shape for w in weights]
+        return ext().embed_sum_fwd([w.contiguous() for w in weights], idx.contiguous())
 
     @staticmethod
     def backward(ctx, g):
+        from ..ops._ext import ext
         (idx,) = ctx.saved_tensors
-        gw = torch.zeros(ctx.shape, dtype=g.dtype, device=g.device)
-        gw.index_add_(0, idx.reshape(-1), g.reshape(-1, ctx.shape[1]))
-        return gw, None
+        gws = [torch.zeros(s, dtype=torch.float32, device=g.device) for s in ctx.shapes]
+        ext().embed_sum_bwd(gws, g.float().contiguous(), idx)
+        return (None,) + tuple(gws)
+
+
+def embed_sum(idx: torch.Tensor, weights) -> torch.Tensor:
+    """``sum_f weights[f][idx[..., f]]`` (CUDA kernel for fp32 tables on the GPU)."""
+    weights = list(weights)
+    if idx.is_cuda and all(w.dtype == torch.float32 for w in weights) and weights[0].shape[1] % 4 == 0:
+        return _EmbedGather.apply(idx.long(), *weights)
+    out = weights[0][idx[..., 0]]
+    for f in range(1, len(weights)):
+        out = out + weights[f][idx[..., f]]
+    return out
 
 
 def gelu_tanh(x):

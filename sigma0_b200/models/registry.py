@@ -373,6 +373,19 @@ def build_model(args: Any):
     from .lob_model import LobModel
     from .legacy_norm import apply_legacy_norm, legacy_norm_enabled
     bb = build_backbone(args)
+    if str(_arg(args, "token_mode", "")) == "1tok":      # the 1-token-per-message model family
+        from .lob_model_1tok import OneTokenLobModel
+        model = OneTokenLobModel(bb.factory_at, d_model=int(args.d_model), d_book=int(_arg(args, "d_book", 503)),
+                                 n_fused_layers=int(_arg(args, "n_layers", 6)),
+                                 n_book_pre_layers=int(_arg(args, "n_book_pre_layers", 1)),
+                                 n_book_post_layers=int(_arg(args, "n_book_post_layers", 1)),
+                                 activation=str(_arg(args, "activation_fn", "half_glu1")),
+                                 prenorm=bool(_arg(args, "prenorm", True)), dropout=float(_arg(args, "p_dropout", 0.0)),
+                                 use_book_data=bool(_arg(args, "use_book_data", True)),
+                                 attn_factory_at=bb.attn_factory_at, attn_layers=bb.attn_layers)
+        if str(_arg(args, "impl", "torch")) == "cuda" and hasattr(model, "book_encoder"):
+            model.book_encoder.compute_dtype = _compute_dtype(args)
+        return model
     model = LobModel(bb.factory_at, vocab_size=int(args.vocab_size), d_model=int(args.d_model),
                      d_book=int(_arg(args, "d_book", 503)),
                      n_message_layers=int(_arg(args, "n_message_layers", 2)),

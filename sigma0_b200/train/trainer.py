@@ -45,8 +45,9 @@ class Trainer:
                  context_parallel: bool = False, tp: int = 1):
         self.args = args
         self.device = device or torch.device("cuda" if torch.cuda.is_available() else "cpu")
-        set_token_mode(args.token_mode)
-        self.tok = get_tokenizer(args.token_mode)
+        from ..encoding.tok1 import encoding_mode
+        set_token_mode(encoding_mode(args.token_mode))
+        self.tok = get_tokenizer(encoding_mode(args.token_mode))
         torch.manual_seed(seed)
         self.model = build_model(args).to(self.device)
         arch = architecture_from_args(args)
