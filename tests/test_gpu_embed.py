@@ -26,7 +26,8 @@ def test_embed_sum_matches_torch(nf, D):
 def test_one_token_model_on_cuda_matches_torch_path():
     from sigma0_b200.models import preset_args, build_model
     from sigma0_b200.data import make_sequences, LobWindowDataset, collate
-    args = dict(token_mode="1tok", d_model=128, n_messages=20, micro_bsz=2, n_layers=1)
+    args = dict(token_mode="1tok", d_model=256, mamba3_d_state=128, mamba3_headdim=64, n_messages=20, micro_bsz=2,
+                n_layers=1, dtype="bfloat16")
     torch.manual_seed(0)
     mc = build_model(preset_args("smoke", impl="cuda", **args)).cuda()
     mt = build_model(preset_args("smoke", impl="torch", **args)).cuda()
