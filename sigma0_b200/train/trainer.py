@@ -42,7 +42,8 @@ class Trainer:
     def __init__(self, args, device: Optional[torch.device] = None, world: int = 1, rank: int = 0,
                  group=None, total_steps: int = 1000, seed: int = 0, sharded: bool = False,
                  accum_steps: int = 1, grad_wire_dtype: str = "float32", dp_impl: str = "nccl",
-                 context_parallel: bool = False, tp: int = 1):
+                 context_parallel: bool = False, tp: int = 1, hierarchical: bool = False,
+                 gpus_per_node: Optional[int] = None):
         self.args = args
         self.device = device or torch.device("cuda" if torch.cuda.is_available() else "cpu")
         from ..encoding.tok1 import encoding_mode
@@ -80,6 +81,16 @@ class Trainer:
             if dp_impl == "fused":
                 dp_impl = "nccl"          # the fused sync spans the default group only
         self.world, self.rank, self.group = world, rank, group
+        # hierarchical data parallelism: a (nodes, gpus) mesh; the gradient is reduce-scattered
+        # inside a node, all-reduced across nodes shard by shard, and all-gathered back
+        self.hier = None
+        if hierarchical and world > 1 and self.tp == 1:
+            if group is not None or context_parallel or sharded or dp_impl == "fused":
+                raise ValueError("the hierarchical step runs over the default group with replicated moments")
+            from ..parallel.mesh import create_mesh
+            mesh = create_mesh(hierarchical=True, gpus_per_node=gpus_per_node, allow_single_node_hierarchical=True)
+            self.mesh = mesh
+            self.hier = (mesh.group("nodes"), mesh.group("gpus"), mesh.size("gpus"))
         lr_base = float(getattr(args, "ssm_lr_base", 1e-3))
         lr = lr_base * float(getattr(args, "lr_factor", 1.0))
         opt_cls = FlatAdam
@@ -93,7 +104,8 @@ class Trainer:
                             max_grad_norm=float(getattr(args, "max_grad_norm", 1.0)),
                             opt_config=str(getattr(args, "opt_config", "standard")),
                             attention_model=attn_only,
-                            pad_multiple=128 * (world if ((sharded or dp_impl == "fused") and world > 1) else 1),
+                            pad_multiple=128 * (world if ((sharded or dp_impl == "fused" or hierarchical)
+                                                          and world > 1) else 1),
                             alloc=self._alloc(dp_impl, world), last=tp_slices)
         self.total_steps = total_steps
         self.warmup_steps = int(round(float(getattr(args, "warmup_end", 0.01)) * total_steps))
@@ -143,6 +155,9 @@ class Trainer:
         if self.tp > 1:
             self._update_tp(lr_scale)
             return
+        if self.hier is not None:
+            self._update_hier(lr_scale)
+            return
         if self.world == 1:
             opt.step(lr_scale=lr_scale)
             return
@@ -180,6 +195,25 @@ class Trainer:
         opt.step_shard(gs, ss, lr_scale=lr_scale)
         dist.all_gather_into_tensor(opt.flat, opt.flat[opt.lo:opt.hi].clone(), group=self.group)
         opt.refresh_shadow()
+
+    def _update_hier(self, lr_scale: float):
+        """Two-level gradient average (the reference's hierarchical step,
+        ``training/train_helpers.py:2069-2200``): reduce-scatter over the GPUs of a node,
+        all-reduce of each shard over the nodes (bf16 on the wire with
+        ``grad_wire_dtype="bfloat16"``), all-gather inside the node, then the update."""
+        nodes_g, gpus_g, gpn = self.hier
+        g = self.opt.grad
+        shard = torch.empty(g.numel() // gpn, dtype=g.dtype, device=g.device)
+        dist.reduce_scatter_tensor(shard, g, group=gpus_g)
+        if self.wire_bf16:
+            sb = shard.to(torch.bfloat16)
+            dist.all_reduce(sb, group=nodes_g)
+            shard.copy_(sb)
+        else:
+            dist.all_reduce(shard, group=nodes_g)
+        shard.div_(self.world)
+        dist.all_gather_into_tensor(g, shard, group=gpus_g)
+        self.opt.step(lr_scale=lr_scale)
 
     def _update_tp(self, lr_scale: float):
         """Tensor parallel: average over the dp axis, then the global gradient norm -- each

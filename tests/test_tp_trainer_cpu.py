@@ -69,3 +69,34 @@ def test_tp_trainer_matches_single_process(arch, world, tmp_path):
     tr = Trainer(_args(arch), device=torch.device("cpu"), total_steps=10, seed=0)
     ref = torch.tensor(_losses(tr, tok, lab, book))
     assert torch.allclose(got, ref, rtol=2e-4, atol=2e-4), (got, ref)
+
+
+def _hier_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=120))
+    try:
+        from sigma0_b200.train.trainer import Trainer
+        torch.set_num_threads(1)
+        res = {}
+        for hier in (False, True):
+            tr = Trainer(_args("mamba3"), device=torch.device("cpu"), world=world, rank=rank, total_steps=10, seed=0,
+                         hierarchical=hier, gpus_per_node=2)
+            tok, lab, book = _batch(4)
+            sl = slice(rank, rank + 1)
+            _losses(tr, tok[sl], lab[sl], book[sl])
+            res[hier] = tr.opt.flat.clone()
+        if rank == 0:
+            torch.save(res, out)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_hierarchical_step_matches_flat_data_parallel(tmp_path):
+    """Four ranks as 2 nodes x 2 GPUs: reduce-scatter in the node, all-reduce across nodes,
+    all-gather -- the same parameters as the flat all-reduce."""
+    out = str(tmp_path / "h.pt")
+    mp.spawn(_hier_worker, args=(4, _free_port(), out), nprocs=4, join=True)
+    r = torch.load(out)
+    n = min(r[False].numel(), r[True].numel())
+    assert torch.allclose(r[False][:n], r[True][:n], rtol=1e-5, atol=1e-6)
