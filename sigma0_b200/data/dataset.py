@@ -34,13 +34,16 @@ class LobWindowDataset(torch.utils.data.Dataset):
     def __init__(self, msgs: Sequence[np.ndarray], books: Sequence[np.ndarray], n_messages: int,
                  token_mode: str = "22tok", book_depth: int = 500, use_book_data: bool = True,
                  stride: Optional[int] = None, return_raw_msgs: bool = False, mask="no_mask",
-                 book_ablation: str = "real", seed: int = 0):
+                 book_ablation: str = "real", seed: int = 0, random_offsets: bool = False):
         from ..encoding.tok1 import encoding_mode
         self.one_token = token_mode == "1tok"      # 24tok messages as one row of 24 field ids each
         self.tok = get_tokenizer(encoding_mode(token_mode))
         if self.one_token and mask == "no_mask":
             mask = "no_mask_1tok"
         self.mask, self.book_ablation, self.seed = mask, book_ablation, seed
+        # random_offsets: every epoch shifts each day's windows by a seeded offset in
+        # [0, n_messages) (the reference's random_offsets_train), clipped to the day's end
+        self.random_offsets, self.epoch = random_offsets, 0
         self.n = n_messages
         self.book_depth = book_depth
         self.use_book = use_book_data
@@ -70,8 +73,14 @@ class LobWindowDataset(torch.utils.data.Dataset):
     def __len__(self):
         return len(self.index)
 
+    def set_epoch(self, epoch: int) -> None:
+        self.epoch = int(epoch)
+
     def __getitem__(self, i):
         f, s = self.index[i]
+        if self.random_offsets:
+            off = int(np.random.default_rng([self.seed, self.epoch, f]).integers(0, self.n))
+            s = min(s + off, self.msgs[f].shape[0] - self.n)
         raw = np.asarray(self.msgs[f][s:s + self.n])
         enc = self.tok.encode_msgs(raw)
         if self.mask == "no_mask":

@@ -54,6 +54,40 @@ class LayerNorm(nn.Module):
         return F.layer_norm(x.float(), (x.shape[-1],), self.scale, self.bias, self.eps)
 
 
+class BatchNorm(nn.Module):
+    """Batch normalisation over every axis but the last (the reference's ``--batchnorm``
+    choice of ``SequenceLayer`` norm, ``src/base_model/models/layers.py:81-83``): batch
+    statistics in training, averaged over the data-parallel ranks (the reference's
+    ``axis_name='batch'``); running averages ``r = momentum * r + (1 - momentum) * batch``
+    used in evaluation.  ``scale`` / ``bias`` carry the same names as ``LayerNorm``'s."""
+
+    def __init__(self, d: int, momentum: float = 0.9, eps: float = 1e-5, group=None):
+        super().__init__()
+        self.momentum, self.eps, self.group = momentum, eps, group
+        self.scale = nn.Parameter(torch.ones(d))
+        self.bias = nn.Parameter(torch.zeros(d))
+        self.register_buffer("mean", torch.zeros(d))
+        self.register_buffer("var", torch.ones(d))
+
+    def forward(self, x):
+        xf = x.float()
+        if self.training:
+            dims = tuple(range(xf.dim() - 1))
+            st = torch.cat([xf.mean(dims), (xf * xf).mean(dims)])
+            import torch.distributed as dist
+            if dist.is_available() and dist.is_initialized() and dist.get_world_size(self.group) > 1:
+                from torch.distributed.nn.functional import all_reduce
+                st = all_reduce(st, group=self.group) / dist.get_world_size(self.group)
+            m, m2 = st.split(xf.shape[-1])
+            var = (m2 - m * m).clamp_min(0.0)
+            with torch.no_grad():
+                self.mean.mul_(self.momentum).add_(m.detach(), alpha=1 - self.momentum)
+                self.var.mul_(self.momentum).add_(var.detach(), alpha=1 - self.momentum)
+        else:
+            m, var = self.mean, self.var
+        return (xf - m) * torch.rsqrt(var + self.eps) * self.scale + self.bias
+
+
 class RMSNorm(nn.Module):
     def __init__(self, d: int, eps: float = 1e-6):
         super().__init__()

@@ -17,6 +17,7 @@ from typing import Callable, Optional, Sequence
 
 import torch
 import torch.nn as nn
+import torch.utils.checkpoint
 import torch.nn.functional as F
 
 from .common import Dense, Embed, LayerNorm, gelu_tanh
@@ -45,7 +46,7 @@ class SequenceLayer(nn.Module):
     def _fused_ok(self, x) -> bool:
         from .mamba3 import Mamba3
         return (x.is_cuda and isinstance(self.seq, Mamba3) and self.seq.impl == "cuda"
-                and self.prenorm and self.activation == "half_glu1" and self.dropout == 0.0
+                and type(self.norm) is LayerNorm and self.prenorm and self.activation == "half_glu1" and self.dropout == 0.0
                 and self.d_model % 8 == 0)
 
     def _act(self, x):
@@ -133,6 +134,7 @@ class StackedEncoder(nn.Module):
         if attn_at and max(attn_at) >= n_layers:
             raise ValueError(f"attn_layers={tuple(sorted(attn_at))} out of range for n_layers={n_layers}")
         self.n_layers = n_layers
+        self.remat = False            # recompute each layer's activations in the backward pass
         for i in range(n_layers):
             mixer = attn_factory() if i in attn_at else factory()
             self.add_module(f"layers_{i}", SequenceLayer(mixer, d_model, activation, prenorm, dropout))
@@ -148,8 +150,9 @@ class StackedEncoder(nn.Module):
 
     def forward(self, x):
         x = self._encode(x)
+        remat = self.remat and self.training and torch.is_grad_enabled()
         for layer in self.layers:
-            x = layer(x)
+            x = torch.utils.checkpoint.checkpoint(layer, x, use_reentrant=False) if remat else layer(x)
         return x
 
     def initial_state(self, batch, device=None):

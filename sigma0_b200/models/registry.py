@@ -369,7 +369,27 @@ def build_backbone(args: Any, *, print_shapes: bool = False) -> BackboneBuild:
 
 
 def build_model(args: Any):
-    """Build the outer LOB model for ``args`` (an argparse namespace or similar)."""
+    """Build the outer LOB model for ``args`` (an argparse namespace or similar).  With
+    ``remat`` every sequence layer recomputes its activations in the backward pass (the
+    reference's ``--remat``, ``nn.remat`` of each layer); with ``batchnorm`` the sequence
+    layers normalise with ``BatchNorm`` (momentum ``bn_momentum``) instead of ``LayerNorm``."""
+    model = _build_model(args)
+    if bool(_arg(args, "batchnorm", False)):
+        from .common import BatchNorm
+        from .layers import SequenceLayer
+        mom = float(_arg(args, "bn_momentum", 0.9))
+        for m in model.modules():
+            if isinstance(m, SequenceLayer) and hasattr(m, "norm"):
+                m.norm = BatchNorm(m.d_model, momentum=mom)
+    if bool(_arg(args, "remat", False)):
+        from .layers import StackedEncoder
+        for m in model.modules():
+            if isinstance(m, StackedEncoder):
+                m.remat = True
+    return model
+
+
+def _build_model(args: Any):
     from .lob_model import LobModel
     from .legacy_norm import apply_legacy_norm, legacy_norm_enabled
     bb = build_backbone(args)

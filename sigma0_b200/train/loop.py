@@ -13,7 +13,11 @@ Mirrors the reference's ``train_epoch`` / ``train`` duties
 * a time limit (e.g. the scheduler's wall clock) -> save before it is reached;
 * periodic checkpoints and resume from the newest intact checkpoint, skipping
   the batches already consumed (resume-by-step at the sampler level);
-* periodic logs: loss, tokens/s, MFU, gradient norm, learning-rate scale.
+* periodic logs: loss, tokens/s, MFU, gradient norm, learning-rate scale;
+* validation on held-out batches every ``eval_every`` steps and at the end, with early
+  stopping and reduce-on-plateau of the learning rate (the reference's
+  ``early_stop_patience`` / ``lr_patience`` / ``reduce_factor``);
+* a profiler trace window over a range of steps and NVTX step ranges.
 
 The step itself never syncs the host; the loop reads the loss only every
 ``log_every`` steps (and for the NaN check at that cadence).
@@ -25,7 +29,7 @@ import os
 import threading
 import time
 from dataclasses import dataclass, field
-from typing import Callable, Dict, Iterable, List, Optional
+from typing import Callable, Dict, Iterable, List, Optional, Tuple
 
 import torch
 
@@ -113,19 +117,80 @@ class LoopConfig:
     save_margin_s: float = 300.0
     config: Dict = field(default_factory=dict)
     ckpt_format: str = "native"           # "native" flat buffers or the Orbax StandardSave layout
+    # trace window [start, stop) in optimizer steps (the reference's --enable_profiler: 2..20)
+    profile_steps: Optional[Tuple[int, int]] = None
+    profile_dir: str = "profile"
+    nvtx: bool = False                    # NVTX range around every step
+    # validation every eval_every steps (0: only at the end) over the val_batches callable's
+    # batches; early stop after early_stop_patience evaluations without improvement; the lr
+    # multiple drops by reduce_factor after lr_patience evaluations without improvement
+    eval_every: int = 0
+    early_stop_patience: int = 0
+    # resume from this step of ckpt_dir instead of the newest (the reference's
+    # --resume_from_step); or, when ckpt_dir holds nothing, initialise from another run's
+    # checkpoint (--restore / --restore_step), parameters only with partial_restore, with the
+    # step counter and lr schedule started over with reset_schedule
+    resume_step: Optional[int] = None
+    restore_dir: Optional[str] = None
+    restore_step: Optional[int] = None
+    partial_restore: bool = False
+    reset_schedule: bool = False
+    lr_patience: int = 0
+    reduce_factor: float = 0.9
 
 
 @dataclass
 class LoopResult:
     steps_done: int
     last_loss: float
-    stopped: str                       # "done" | "nan" | "time_limit"
+    stopped: str                       # "done" | "nan" | "time_limit" | "early_stop"
     history: List[Dict] = field(default_factory=list)
+    best_val: Optional[float] = None
+    trace_path: Optional[str] = None
+
+
+class _Plateau:
+    """Evaluation bookkeeping: best loss, evaluations since it, and the lr multiple."""
+
+    def __init__(self, early_stop_patience: int, lr_patience: int, reduce_factor: float):
+        self.best, self.since, self.since_lr = None, 0, 0
+        self.esp, self.lrp, self.factor = early_stop_patience, lr_patience, reduce_factor
+
+    def update(self, val: float, trainer) -> bool:
+        """Record one validation loss; returns True when training should stop."""
+        if self.best is None or val < self.best:
+            self.best, self.since, self.since_lr = val, 0, 0
+            return False
+        self.since += 1
+        self.since_lr += 1
+        if self.lrp > 0 and self.since_lr >= self.lrp:
+            trainer.lr_mult *= self.factor
+            self.since_lr = 0
+        return self.esp > 0 and self.since >= self.esp
+
+
+def evaluate(trainer, batches: Iterable) -> float:
+    """Mean loss over ``batches`` (averaged over the data-parallel ranks)."""
+    tot, n = None, 0
+    for b in batches:
+        loss = trainer.eval_loss(*b, sync=False)
+        tot = loss if tot is None else tot + loss
+        n += 1
+    if n == 0:
+        return float("nan")
+    val = (tot / n).reshape(1)
+    if trainer.world > 1 and not getattr(trainer, "cp", False):
+        torch.distributed.all_reduce(val)
+        val = val / torch.distributed.get_world_size()
+    return float(val)
 
 
 def fit(trainer, batches: Iterable, cfg: LoopConfig, log: Callable[[Dict], None] = None,
-        watchdog: Optional[StepWatchdog] = None) -> LoopResult:
-    """Train for ``cfg.steps`` optimizer steps over ``batches`` (host or device tuples)."""
+        watchdog: Optional[StepWatchdog] = None,
+        val_batches: Optional[Callable[[], Iterable]] = None) -> LoopResult:
+    """Train for ``cfg.steps`` optimizer steps over ``batches`` (host or device tuples);
+    ``val_batches()`` yields the held-out batches of one evaluation."""
+    from ..utils.step_profile import TraceWindow
     from ..ckpt import CheckpointManager
     from ..models.flops import lob_model_flops, measured_bf16_peak
     log = log or (lambda rec: print(rec, flush=True))
@@ -134,9 +199,17 @@ def fit(trainer, batches: Iterable, cfg: LoopConfig, log: Callable[[Dict], None]
                             fmt=cfg.ckpt_format) if cfg.ckpt_dir else None
     start = 0
     if mgr is not None and cfg.resume and mgr.latest_step() is not None:
-        meta = mgr.restore(trainer)
+        meta = mgr.restore(trainer, step=cfg.resume_step)
         start = trainer.step_idx
         log({"event": "resumed", "from_step": meta["restored_step"], "trainer_step": start})
+    elif cfg.restore_dir:
+        src = CheckpointManager(cfg.restore_dir, rank=trainer.rank, world=trainer.world, barrier=barrier)
+        meta = src.restore(trainer, step=cfg.restore_step, params_only=cfg.partial_restore)
+        if cfg.reset_schedule or cfg.partial_restore:
+            trainer.step_idx = 0
+        start = trainer.step_idx
+        log({"event": "restored", "from": cfg.restore_dir, "step": meta["restored_step"],
+             "params_only": cfg.partial_restore, "trainer_step": start})
     wd = watchdog or (StepWatchdog(cfg.watchdog_timeout) if cfg.watchdog_timeout > 0 else None)
     t_begin = time.time()
     flops_tok = lob_model_flops(trainer.args).train if hasattr(trainer.args, "mamba3_d_state") else None
@@ -149,13 +222,30 @@ def fit(trainer, batches: Iterable, cfg: LoopConfig, log: Callable[[Dict], None]
     t0, tok_count = time.time(), 0
     step = start
     stopped = "done"
+    tw = None
+    if cfg.profile_steps is not None or cfg.nvtx:
+        a, b = cfg.profile_steps if cfg.profile_steps is not None else (cfg.steps + 1, cfg.steps + 2)
+        tw = TraceWindow(a, b, cfg.profile_dir, rank=trainer.rank, nvtx=cfg.nvtx)
+    plateau = _Plateau(cfg.early_stop_patience, cfg.lr_patience, cfg.reduce_factor)
+
+    def validate():
+        v = evaluate(trainer, val_batches())
+        rec = {"step": step, "val_loss": v, "lr_mult": trainer.lr_mult}
+        log(rec)
+        hist.append(rec)
+        return plateau.update(v, trainer) if math.isfinite(v) else False
+
     while step < cfg.steps:
         batch = next(it)
         if wd:
             wd.arm(step)
         if batch[0].device.type == "cpu" and trainer.device.type == "cuda":
             batch = trainer.to_device(batch)
+        if tw:
+            tw.before(step)
         loss = trainer.step_device(*batch)
+        if tw:
+            tw.after(step)
         if wd and trainer.device.type == "cuda":
             ev = torch.cuda.Event()
             ev.record()
@@ -180,6 +270,11 @@ def fit(trainer, batches: Iterable, cfg: LoopConfig, log: Callable[[Dict], None]
                 break
         if wd:
             wd.disarm()
+        if val_batches is not None and cfg.eval_every and step % cfg.eval_every == 0 and step < cfg.steps:
+            if validate():
+                stopped = "early_stop"
+                log({"event": "early stop", "step": step, "best_val_loss": plateau.best})
+                break
         if mgr is not None and cfg.save_every and step % cfg.save_every == 0:
             mgr.save(step, trainer, metrics={"loss": last_loss}, config=cfg.config)
         if cfg.time_limit_s is not None and time.time() - t_begin > cfg.time_limit_s - cfg.save_margin_s:
@@ -187,9 +282,13 @@ def fit(trainer, batches: Iterable, cfg: LoopConfig, log: Callable[[Dict], None]
             break
     if wd:
         wd.disarm()
+    if tw:
+        tw.close()
+    if val_batches is not None and stopped in ("done", "time_limit"):
+        validate()
     if mgr is not None and stopped != "nan":
         if not math.isfinite(last_loss):
             last_loss = float(loss)
         mgr.save(step, trainer, metrics={"loss": last_loss}, config=cfg.config, blocking=True)
         mgr.wait()
-    return LoopResult(step, last_loss, stopped, hist)
+    return LoopResult(step, last_loss, stopped, hist, plateau.best, tw.path if tw else None)

@@ -34,10 +34,16 @@ SSM_LEAVES = {
 }
 
 
-def leaf_group(name: str, opt_config: str = "standard", attention_model: bool = False) -> str:
+def leaf_group(name: str, opt_config: str = "standard", attention_model: bool = False,
+               dt_global: bool = False) -> str:
+    """``ssm`` (Adam at the ssm lr, no decay) or ``regular`` (AdamW); with ``dt_global`` the
+    S5 ``log_step`` moves to the regular group (the reference's ``dt_global`` branch of the
+    standard configuration, ``training/train_helpers.py:541-547``)."""
     if attention_model:
         return "regular"
     leaf = name.split(".")[-1]
+    if dt_global and leaf == "log_step":
+        return "regular"
     return "ssm" if leaf in SSM_LEAVES.get(opt_config, SSM_LEAVES["standard"]) else "regular"
 
 
@@ -45,7 +51,7 @@ class FlatAdam:
     def __init__(self, model: nn.Module, lr: float, ssm_lr: float, weight_decay: float = 0.05,
                  max_grad_norm: float = 1.0, betas=(0.9, 0.999), eps: float = 1e-8,
                  opt_config: str = "standard", attention_model: bool = False,
-                 bf16_shadow: bool = True, pad_multiple: int = 128, alloc=None, last=()):
+                 bf16_shadow: bool = True, pad_multiple: int = 128, alloc=None, last=(), dt_global: bool = False):
         self.model = model
         self.b1, self.b2 = betas
         self.eps = eps
@@ -55,7 +61,7 @@ class FlatAdam:
         named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
         groups = {"ssm": [], "regular": []}
         for n, p in named:
-            groups[leaf_group(n, opt_config, attention_model)].append((n, p))
+            groups[leaf_group(n, opt_config, attention_model, dt_global)].append((n, p))
         # parameters in `last` (tensor-parallel slices) go to the end of their group, so each
         # group's slices form one contiguous range [tail_lo[group], group end)
         late = {id(p) for p in last}

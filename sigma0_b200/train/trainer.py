@@ -98,7 +98,9 @@ class Trainer:
         if str(getattr(args, "opt_config", "standard")) == "muon":
             from .muon import FlatMuon
             opt_cls = FlatMuon
-            extra_opt = dict(muon_lr=float(getattr(args, "muon_lr", 0.02)))
+            mwd = getattr(args, "muon_wd", None)
+            extra_opt = dict(muon_lr=float(getattr(args, "muon_lr", 0.02)),
+                             muon_wd=None if mwd is None else float(mwd))
         self.opt = opt_cls(self.model, lr=lr, ssm_lr=lr_base, **extra_opt,
                             weight_decay=float(getattr(args, "weight_decay", 0.05)),
                             max_grad_norm=float(getattr(args, "max_grad_norm", 1.0)),
@@ -106,11 +108,16 @@ class Trainer:
                             attention_model=attn_only,
                             pad_multiple=128 * (world if ((sharded or dp_impl == "fused" or hierarchical)
                                                           and world > 1) else 1),
-                            alloc=self._alloc(dp_impl, world), last=tp_slices)
+                            alloc=self._alloc(dp_impl, world), last=tp_slices,
+                            dt_global=bool(getattr(args, "dt_global", False)))
         self.total_steps = total_steps
         self.warmup_steps = int(round(float(getattr(args, "warmup_end", 0.01)) * total_steps))
         lr_min = float(getattr(args, "lr_min", 0.0) or 0.0)
         self.lr_min_frac = (lr_min / lr) if lr_min > 0 else 0.05
+        # cosine decay after the warmup (the reference's cosine_anneal), else a constant lr;
+        # lr_mult is the reduce-on-plateau factor the loop lowers (lr_patience / reduce_factor)
+        self.cosine = bool(getattr(args, "cosine_anneal", True))
+        self.lr_mult = 1.0
         self.ignore_times = bool(getattr(args, "ignore_times", False))
         if dp_impl not in ("nccl", "fused"):
             raise ValueError(f"dp_impl must be 'nccl' or 'fused', not {dp_impl!r}")
@@ -257,13 +264,20 @@ class Trainer:
                 loss, _ = self.model.loss(tc, bc, lc, ignore_times=self.ignore_times, tokenizer=self.tok)
                 (loss / k).backward()
                 total = total + loss.detach() / k
-        scale = cosine_schedule(self.step_idx + 1, self.warmup_steps, self.total_steps, self.lr_min_frac)
-        self._update(scale)
+        self._update(self.lr_scale(self.step_idx + 1))
         self.step_idx += 1
         if self.cp:
             dist.all_reduce(total, group=self.group)
             total = total / self.world
         return total
+
+    def lr_scale(self, step: int) -> float:
+        """The learning-rate multiple for optimizer step ``step`` (1-based)."""
+        if self.cosine:
+            s = cosine_schedule(step, self.warmup_steps, self.total_steps, self.lr_min_frac)
+        else:
+            s = step / self.warmup_steps if self.warmup_steps > 0 and step < self.warmup_steps else 1.0
+        return s * self.lr_mult
 
     def _segment(self, tokens, labels, book):
         """This rank's segment of every sequence (context parallelism)."""
@@ -287,7 +301,21 @@ class Trainer:
         return value
 
     @torch.no_grad()
-    def eval_loss(self, tokens, labels, book=None) -> float:
-        loss, _ = self.model.loss(tokens.to(self.device), book.to(self.device) if book is not None else None,
-                                  labels.to(self.device), ignore_times=self.ignore_times, tokenizer=self.tok)
-        return float(loss)
+    def eval_loss(self, tokens, labels, book=None, sync: bool = True):
+        """Mean loss of one batch without a parameter update (a float; a device scalar with
+        ``sync=False``).  Under context parallelism each rank scores its segment and the
+        segment means are averaged over the group."""
+        tokens, labels, book = self.to_device((tokens, labels, book))
+        was = self.model.training
+        self.model.eval()
+        try:
+            if self.cp:
+                tokens, labels, book = self._segment(tokens, labels, book)
+            loss, _ = self.model.loss(tokens, book, labels, ignore_times=self.ignore_times, tokenizer=self.tok)
+            loss = loss.detach().float()
+            if self.cp:
+                dist.all_reduce(loss, group=self.group)
+                loss = loss / self.world
+        finally:
+            self.model.train(was)
+        return float(loss) if sync else loss

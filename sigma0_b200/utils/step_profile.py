@@ -7,12 +7,61 @@ where a step's time goes; it is not a benchmark (the profiler adds overhead; tim
 steps with ``bench.py``).
 
     python -m sigma0_b200.utils.step_profile --preset 350m --top 30
+
+``TraceWindow`` is the training loop's trace hook: the reference starts a JAX profiler
+trace at step 2 and stops it at step 20 under ``--enable_profiler``
+(``training/train_helpers.py:1033-1034,1229-1231``); here a ``torch.profiler`` session
+covers the same optimizer-step window (CPU and CUDA activity) and writes one Chrome trace
+per rank, and NVTX ranges mark every step for an external timeline tool.
 """
 from __future__ import annotations
 
 import argparse
 import collections
-from typing import Dict, List, Tuple
+from typing import Dict, List, Optional, Tuple
+
+
+class TraceWindow:
+    """Profile optimizer steps ``[start, stop)``; ``trace_rank{r}.json`` goes to ``out_dir``."""
+
+    def __init__(self, start: int, stop: int, out_dir: str, rank: int = 0, nvtx: bool = False):
+        if stop <= start:
+            raise ValueError(f"empty profiler window [{start}, {stop})")
+        self.start, self.stop, self.out_dir, self.rank, self.nvtx = int(start), int(stop), out_dir, rank, nvtx
+        self.prof = None
+        self.path: Optional[str] = None
+
+    def before(self, step: int) -> None:
+        """Call before optimizer step ``step`` (0-based) is issued."""
+        import torch
+        if step == self.start and self.prof is None:
+            from torch.profiler import ProfilerActivity, profile
+            acts = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if torch.cuda.is_available() else [])
+            self.prof = profile(activities=acts, record_shapes=False)
+            self.prof.__enter__()
+        if self.nvtx and torch.cuda.is_available():
+            torch.cuda.nvtx.range_push(f"step {step}")
+
+    def after(self, step: int) -> None:
+        """Call after optimizer step ``step`` (0-based) has been issued."""
+        import torch
+        if self.nvtx and torch.cuda.is_available():
+            torch.cuda.nvtx.range_pop()
+        if self.prof is not None and step + 1 >= self.stop:
+            self.close()
+
+    def close(self) -> None:
+        import os
+        import torch
+        if self.prof is None:
+            return
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        self.prof.__exit__(None, None, None)
+        os.makedirs(self.out_dir, exist_ok=True)
+        self.path = os.path.join(self.out_dir, f"trace_rank{self.rank}.json")
+        self.prof.export_chrome_trace(self.path)
+        self.prof = None
 
 
 def profile_step(preset: str = "350m", micro_bsz: int = 0, n_messages: int = 0,
