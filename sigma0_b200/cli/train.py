@@ -382,6 +382,10 @@ def main(argv=None):
               val_batches=None if (val_fn is None or a.skip_test_eval and not cfg.eval_every) else val_fn)
     log({"event": "finished", "steps": res.steps_done, "stopped": res.stopped, "last_loss": res.last_loss,
          "best_val_loss": res.best_val, "trace": res.trace_path})
+    if a.ckpt_dir and rank == 0:
+        # how the run ended, for a supervising launcher (torchrun reports any failure as exit 1)
+        with open(os.path.join(a.ckpt_dir, "run_status.json"), "w") as f:
+            json.dump({"stopped": res.stopped, "steps": res.steps_done, "last_loss": res.last_loss}, f)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
