@@ -90,6 +90,78 @@ at::Tensor m3_status(const at::Tensor& like) {
   if (!per_dev[d].defined()) per_dev[d] = at::zeros({1}, like.options().dtype(at::kInt));
   return per_dev[d];
 }
+// status word of the tcgen05 GEMM on each device (1 once a bounded wait gave up)
+at::Tensor gemm_status(const at::Tensor& like) {
+  static std::vector<at::Tensor> per_dev(64);
+  const int d = like.device().index();
+  if (!per_dev[d].defined()) per_dev[d] = at::zeros({1}, like.options().dtype(at::kInt));
+  return per_dev[d];
+}
+
+// C (+)= A . B on the tcgen05 GEMM.  `a` is [M, K] (a_mn false) or [K, M] (a_mn true), `b` is
+// [K, N] (b_mn true) or [N, K] (b_mn false), both bf16 with unit column stride.  out_mode 0
+// returns a new bf16 [M, N]; 1 / 2 store / reduce-add fp32 into `out` (unit column stride; its
+// shape may be smaller than [M, N]: the rows / columns beyond it are dropped).
+at::Tensor gemm_tc(const at::Tensor& a, const at::Tensor& b, bool a_mn, bool b_mn, int64_t out_mode,
+                   c10::optional<at::Tensor> out, int64_t split_k) {
+  // operands may be row-strided views (a slice of a wider buffer); rows must be contiguous
+  auto rows_ok = [](const at::Tensor& t, at::ScalarType dt, const char* name) {
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(t.scalar_type() == dt, name, " has the wrong dtype");
+    TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, ": a 2-D tensor with unit column stride");
+  };
+  rows_ok(a, at::kBFloat16, "a");
+  rows_ok(b, at::kBFloat16, "b");
+  const int64_t M = a_mn ? a.size(1) : a.size(0), K = a_mn ? a.size(0) : a.size(1);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1), N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK(K == Kb, "gemm_tc: inner dimensions differ (", K, " vs ", Kb, ")");
+  TORCH_CHECK(M > 0 && N > 0 && K > 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31),
+              "gemm_tc: dimensions out of range");
+  TORCH_CHECK(split_k >= 1 && (split_k == 1 || out_mode == 2), "gemm_tc: K splits need out_mode 2");
+  TORCH_CHECK(out_mode >= 0 && out_mode <= 2, "gemm_tc: out_mode is 0, 1 or 2");
+  // the tensor maps want 16-byte aligned bases and row pitches
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0,
+              "gemm_tc: operand row pitches must be multiples of 16 bytes (8 bf16)");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0,
+              "gemm_tc: operands must start on 16-byte boundaries");
+  if (out_mode == 0) TORCH_CHECK(N % 8 == 0, "gemm_tc: bf16 output rows must be multiples of 16 bytes (N % 8)");
+  if (out_mode != 0) {
+    TORCH_CHECK(out.has_value(), "gemm_tc: fp32 modes write into `out`");
+    TORCH_CHECK((out->stride(0) * 4) % 16 == 0 && reinterpret_cast<uintptr_t>(out->data_ptr()) % 16 == 0,
+                "gemm_tc: out must start on a 16-byte boundary with a row pitch of a multiple of 4 floats");
+  }
+  at::Tensor c;
+  if (out_mode == 0) {
+    c = at::empty({M, N}, a.options());
+  } else {
+    TORCH_CHECK(out.has_value(), "gemm_tc: fp32 modes write into `out`");
+    c = *out;
+    rows_ok(c, at::kFloat, "out");
+    TORCH_CHECK(c.size(0) <= M && c.size(1) <= N, "gemm_tc: out larger than the product");
+  }
+  c10::cuda::CUDAGuard guard(a.device());
+  GemmArgs g{};
+  g.A = a.data_ptr();
+  g.B = b.data_ptr();
+  g.C = c.data_ptr();
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.lda = a.stride(0);
+  g.ldb = b.stride(0);
+  g.ldc = c.stride(0);
+  g.c_rows = (int)c.size(0);
+  g.c_cols = (int)c.size(1);
+  g.a_mn = a_mn;
+  g.b_mn = b_mn;
+  g.out_mode = (int)out_mode;
+  g.split_k = (int)split_k;
+  g.status = gemm_status(a).data_ptr<int>();
+  const int e = gemm_tc_launch(g, num_sms(a), stream());
+  TORCH_CHECK(e == 0, "gemm_tc launch failed: ", e);
+  return c;
+}
+
 // SSD implementation: 1 the tcgen05 chunk walkers, 0 the chunk-parallel mma.sync kernels,
 // -1 (default) by occupancy: the walkers run one CTA per (sequence, head), so they are used when
 // there are at least as many (sequence, head) pairs as SMs; smaller batches (a single sequence of
@@ -1180,6 +1252,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("m3_use_tc", [](c10::optional<bool> on) { g_m3_tc = on.has_value() ? (*on ? 1 : 0) : -1; },
         py::arg("on") = py::none(),
         "Mamba3 SSD: True the tcgen05 chunk walkers, False the chunk-parallel kernels, None by occupancy");
+  m.def("gemm_tc", &gemm_tc, "C (+)= A . B on the tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("a_mn"),
+        py::arg("b_mn"), py::arg("out_mode") = 0, py::arg("out") = c10::nullopt, py::arg("split_k") = 1);
+  m.def("gemm_status", [](at::Tensor like) { return gemm_status(like); }, "status word of the tcgen05 GEMM");
   m.def("m3_tc_status", [](at::Tensor like) { return m3_status(like); },
         "status word of the tcgen05 SSD kernels on the tensor's device (nonzero: a bounded wait gave up)");
   m.def("dp_fused_adam", &dp_fused_adam, "fused reduce-scatter + AdamW + all-gather over peer memory");

@@ -193,6 +193,26 @@ void ln_bwd_pipe_launch(const void* dy, const float* x, const float* mean, const
                         const float* dres, float* dx, float* dw, float* db, float* part, long T, int D, int sms,
                         cudaStream_t st);
 
+// dense bf16 GEMM on tcgen05 (gemm_tc.cu): C (+)= A . B with fp32 accumulation.
+// A is [M, K] K-major (row-major, leading dimension lda) or, with a_mn, stored [K, M] MN-major;
+// B is [N, K] K-major or, with b_mn, stored [K, N] MN-major.  C is written over its first
+// c_rows x c_cols entries (c_rows <= M, c_cols <= N; leading dimension ldc): out_mode 0 bf16
+// store, 1 fp32 store, 2 fp32 reduce-add (split_k > 1 only with 2).  Bases 16-byte aligned,
+// leading dimensions multiples of 16 bytes.
+struct GemmArgs {
+  const void* A;
+  const void* B;
+  void* C;
+  int M, N, K;
+  long lda, ldb, ldc;
+  int c_rows, c_cols;
+  int a_mn, b_mn;
+  int out_mode;
+  int split_k;
+  int* status;                 // 1: a pipeline wait timed out
+};
+int gemm_tc_launch(const GemmArgs& a, int sms, cudaStream_t st);
+
 // tensor-parallel row-parallel GEMM fused with its all-reduce over peer memory (tp_fused.cu)
 #define TPF_MAXW 8
 struct TpfArgs {
