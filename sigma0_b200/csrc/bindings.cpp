@@ -117,7 +117,7 @@ at::Tensor gemm_tc(const at::Tensor& a, const at::Tensor& b, bool a_mn, bool b_m
   TORCH_CHECK(K == Kb, "gemm_tc: inner dimensions differ (", K, " vs ", Kb, ")");
   TORCH_CHECK(M > 0 && N > 0 && K > 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31),
               "gemm_tc: dimensions out of range");
-  TORCH_CHECK(split_k >= 1 && (split_k == 1 || out_mode == 2), "gemm_tc: K splits need out_mode 2");
+  TORCH_CHECK(split_k >= 0 && (split_k <= 1 || out_mode == 2), "gemm_tc: K splits need out_mode 2");
   TORCH_CHECK(out_mode >= 0 && out_mode <= 2, "gemm_tc: out_mode is 0, 1 or 2");
   // the tensor maps want 16-byte aligned bases and row pitches
   TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0,
@@ -160,6 +160,34 @@ at::Tensor gemm_tc(const at::Tensor& a, const at::Tensor& b, bool a_mn, bool b_m
   const int e = gemm_tc_launch(g, num_sms(a), stream());
   TORCH_CHECK(e == 0, "gemm_tc launch failed: ", e);
   return c;
+}
+
+// the GLU block's fused GEMM epilogue: o = x . W with g = gelu(o) (both bf16); W is the [K, N]
+// kernel in bf16, N a multiple of 64.
+std::vector<at::Tensor> gemm_gelu_fwd(const at::Tensor& x, const at::Tensor& w) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+              "gemm_gelu_fwd: bf16 CUDA operands");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 && x.size(1) == w.size(0),
+              "gemm_gelu_fwd: x [M, K], w [K, N] with unit column stride");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(1);
+  TORCH_CHECK(N % 64 == 0 && (x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+              "gemm_gelu_fwd: N % 64 and 16-byte aligned rows");
+  auto o = at::empty({M, N}, x.options()), g = at::empty({M, N}, x.options());
+  c10::cuda::CUDAGuard guard(x.device());
+  GemmArgs a{};
+  a.A = x.data_ptr();
+  a.B = w.data_ptr();
+  a.C = o.data_ptr();
+  a.C2 = g.data_ptr();
+  a.M = (int)M; a.N = (int)N; a.K = (int)K;
+  a.lda = x.stride(0); a.ldb = w.stride(0); a.ldc = N; a.ldc2 = N;
+  a.c_rows = (int)M; a.c_cols = (int)N;
+  a.a_mn = 0; a.b_mn = 1; a.out_mode = 3; a.split_k = 1;
+  a.status = gemm_status(x).data_ptr<int>();
+  const int e = gemm_tc_launch(a, num_sms(x), stream());
+  TORCH_CHECK(e == 0, "gemm_gelu_fwd launch failed: ", e);
+  return {o, g};
 }
 
 // SSD implementation: 1 the tcgen05 chunk walkers, 0 the chunk-parallel mma.sync kernels,
@@ -1253,8 +1281,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("on") = py::none(),
         "Mamba3 SSD: True the tcgen05 chunk walkers, False the chunk-parallel kernels, None by occupancy");
   m.def("gemm_tc", &gemm_tc, "C (+)= A . B on the tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("a_mn"),
-        py::arg("b_mn"), py::arg("out_mode") = 0, py::arg("out") = c10::nullopt, py::arg("split_k") = 1);
+        py::arg("b_mn"), py::arg("out_mode") = 0, py::arg("out") = c10::nullopt, py::arg("split_k") = 1);  // split_k 0: auto
   m.def("gemm_status", [](at::Tensor like) { return gemm_status(like); }, "status word of the tcgen05 GEMM");
+  m.def("gemm_gelu_fwd", &gemm_gelu_fwd, "o = x . w and g = gelu(o) in one tcgen05 GEMM");
+  m.def("gemm_use_pair", [](bool on) { gemm_tc_set_pair(on ? 1 : 0); },
+        "two-SM (cta_group::2) GEMM tiles (default) or one-SM tiles");
   m.def("m3_tc_status", [](at::Tensor like) { return m3_status(like); },
         "status word of the tcgen05 SSD kernels on the tensor's device (nonzero: a bounded wait gave up)");
   m.def("dp_fused_adam", &dp_fused_adam, "fused reduce-scatter + AdamW + all-gather over peer memory");

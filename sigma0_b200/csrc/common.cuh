@@ -117,4 +117,17 @@ S0_DEV float warp_sum(float v) {
   return v;
 }
 
+// tanh-approximated GELU (flax's approximate gelu) and its derivative
+constexpr float K_GELU = 0.7978845608028654f;   // sqrt(2/pi)
+constexpr float C_GELU = 0.044715f;
+S0_DEV float gelu_t(float x) {
+  float u = K_GELU * (x + C_GELU * x * x * x);
+  return 0.5f * x * (1.f + tanhf(u));
+}
+S0_DEV float gelu_t_grad(float x) {
+  float u = K_GELU * (x + C_GELU * x * x * x);
+  float th = tanhf(u);
+  return 0.5f * (1.f + th) + 0.5f * x * (1.f - th * th) * K_GELU * (1.f + 3.f * C_GELU * x * x);
+}
+
 }  // namespace s0

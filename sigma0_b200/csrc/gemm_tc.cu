@@ -65,8 +65,83 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, int x,
                "r"(x), "r"(y), "r"(tc::smem_u32(src))
                : "memory");
 }
-// at most one of this thread's bulk stores may still be reading shared memory
+// at most one / none of this thread's bulk stores may still be reading shared memory
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+// Output modes: 0 bf16 store, 1 fp32 store, 2 fp32 reduce-add, 3 the GLU block's fused
+// epilogue: o = acc (bf16) and g = gelu(o) (bf16, through a second tensor map).
+constexpr int OUT_BF16 = 0, OUT_F32 = 1, OUT_F32_ADD = 2, OUT_GELU = 3;
+
+// One warp's share of an accumulator tile: rows row0..row0+31 (lane = row), columns
+// col0 .. col0 + min(BN, c_cols - col0); staged 128 bytes per row in swizzled shared memory
+// and written by TMA (partial boxes at the edges are clipped by the TMA unit).  Only chunks
+// that are stored are staged, so the two staging buffers strictly alternate.
+template <int OUT>
+__device__ __forceinline__ void epilogue_rows(const GemmArgs& a, const CUtensorMap* tmC, const CUtensorMap* tmC2,
+                                              unsigned char* mybuf, int lane, uint32_t tbase, int row0, int col0,
+                                              int cbeg, int cspan, int& nb) {
+  constexpr int CW = (OUT == OUT_F32 || OUT == OUT_F32_ADD) ? 32 : 64;   // output columns per 128-byte row
+  const int cols_left = a.c_cols - col0;
+  const int c_lim = cbeg + cspan < cols_left ? cbeg + cspan : cols_left;
+  const int c_end = row0 < a.c_rows ? c_lim : 0;
+#pragma unroll 1
+  for (int c = cbeg; c < c_end; c += CW, ++nb) {
+    unsigned char* buf = mybuf + (size_t)(nb & 1) * EPI_BUF;
+    unsigned char* buf2 = mybuf + (size_t)((nb + 1) & 1) * EPI_BUF;
+    if (lane == 0) {
+      if (OUT == OUT_GELU)
+        bulk_wait_read0();            // both buffers are written below
+      else
+        bulk_wait_read1();            // the store that used this buffer has read it
+    }
+    __syncwarp();
+    unsigned char* rp = buf + lane * 128;
+    unsigned char* rp2 = buf2 + lane * 128;
+    if (OUT == OUT_F32 || OUT == OUT_F32_ADD) {
+      float v[32];
+      tc::tmem_ld32(tbase + (uint32_t)c, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(rp + (((q ^ (lane & 7)) & 7) << 4)) =
+            make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float v[32];
+        tc::tmem_ld32(tbase + (uint32_t)(c + 32 * h), v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = 4 * h + q;
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) w4[e] = pack_bf16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+          *reinterpret_cast<uint4*>(rp + (((chunk ^ (lane & 7)) & 7) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          if (OUT == OUT_GELU) {
+            uint32_t g4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 ob = unpack_bf16(w4[e]);          // gelu of the stored (bf16) o
+              g4[e] = pack_bf16(gelu_t(ob.x), gelu_t(ob.y));
+            }
+            *reinterpret_cast<uint4*>(rp2 + (((chunk ^ (lane & 7)) & 7) << 4)) =
+                make_uint4(g4[0], g4[1], g4[2], g4[3]);
+          }
+        }
+      }
+    }
+    tc::fence_proxy_async();          // generic-proxy writes -> the TMA store's reads
+    __syncwarp();
+    if (lane == 0) {
+      if (OUT == OUT_F32_ADD)
+        tma_reduce_add_2d(tmC, col0 + c, row0, buf);
+      else
+        tma_store_2d(tmC, col0 + c, row0, buf);
+      if (OUT == OUT_GELU) tma_store_2d(tmC2, col0 + c, row0, buf2);
+      tc::bulk_commit();
+    }
+  }
+}
 
 struct Unit {
   int tm, tn, kb0, kb1;
@@ -86,7 +161,7 @@ __device__ __forceinline__ Unit unit_of(const GemmArgs& a, long u, int tiles_n, 
 template <bool AMN, bool BMN, int OUT>
 __global__ void __launch_bounds__(NT, 1)
     gemm_k(GemmArgs a, const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-           const __grid_constant__ CUtensorMap tmC) {
+           const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ uint64_t full[NS], empty[NS], acc_full[2], acc_empty[2];
   __shared__ uint32_t tslot;
@@ -196,48 +271,7 @@ __global__ void __launch_bounds__(NT, 1)
       tc::fence_after_sync();
       const int row0 = w.tm * BM + 32 * warp;
       const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(b * BN);
-      constexpr int CW = OUT == 0 ? 64 : 32;            // output columns per 128-byte staged row
-      // only chunks that are stored are staged: every staged chunk is followed by its store, so
-      // the two buffers strictly alternate and "at most one store pending" protects the reuse
-      const int cols_left = a.c_cols - w.tn * BN;
-      const int c_end = row0 < a.c_rows ? (cols_left < BN ? cols_left : BN) : 0;
-#pragma unroll 1
-      for (int c = 0; c < c_end; c += CW, ++nb) {
-        unsigned char* buf = epi + (size_t)(warp * 2 + (nb & 1)) * EPI_BUF;
-        if (lane == 0) bulk_wait_read1();             // the store that used this buffer has read it
-        __syncwarp();
-        unsigned char* row = buf + lane * 128;
-        if (OUT == 0) {
-          float v[32];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tc::tmem_ld32(tbase + (uint32_t)(c + 32 * h), v);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int chunk = 4 * h + q;
-              *reinterpret_cast<uint4*>(row + (((chunk ^ (lane & 7)) & 7) << 4)) =
-                  make_uint4(pack_bf16(v[8 * q + 0], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
-                             pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
-            }
-          }
-        } else {
-          float v[32];
-          tc::tmem_ld32(tbase + (uint32_t)c, v);
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4*>(row + (((q ^ (lane & 7)) & 7) << 4)) =
-                make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        }
-        tc::fence_proxy_async();                      // generic-proxy writes -> the TMA store's reads
-        __syncwarp();
-        if (lane == 0) {                              // a box reaching past the output is clipped by TMA
-          if (OUT == 2)
-            tma_reduce_add_2d(&tmC, w.tn * BN + c, row0, buf);
-          else
-            tma_store_2d(&tmC, w.tn * BN + c, row0, buf);
-          tc::bulk_commit();
-        }
-      }
+      epilogue_rows<OUT>(a, &tmC, &tmC2, epi + (size_t)warp * 2 * EPI_BUF, lane, tbase, row0, w.tn * BN, 0, BN, nb);
       tc::fence_before_sync();
       tc::mbar_arrive(&acc_empty[b]);                 // this thread's reads of accumulator b are done
     }
@@ -248,6 +282,218 @@ __global__ void __launch_bounds__(NT, 1)
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// Two-SM version: a cluster of 2 CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2.
+// CTA r of the pair holds rows 128r..128r+127 of the A tile and columns 128r..128r+127 of the
+// B tile in its own shared memory; the pair's leader (r = 0) issues M=256, N=256 MMAs that read
+// both CTAs' halves, and each CTA's tensor memory receives its 128 rows of the product.  Per SM a
+// 128 x 256 x 64 step stages 32 KB instead of 48 KB, which is what lets the tensor pipe outrun
+// the L2.  Both CTAs' TMA loads complete on the leader's full barrier (the .cta_group::2 form of
+// the load; no multicast qualifier anywhere), the leader's commits arrive on both CTAs' empty /
+// accumulator-full barriers (CTA mask 0b11), and the peer's epilogue releases the accumulator
+// with remote arrivals on the leader's barrier.
+// ---------------------------------------------------------------------------------------------
+// 6 warps: 0-3 epilogue (warp w reads TMEM lane quadrant w), 4 MMA issue (leader CTA only),
+// 5 TMA loads.  Six 32 KB stages: the pipeline depth is what the mainloop is sensitive to (five
+// stages measured 2-5% slower; eight epilogue warps gained nothing).
+constexpr int NS2 = 6;
+constexpr int NT2 = 192, EPI_WARPS2 = 4, MMA_WARP2 = 4, PROD_WARP2 = 5;
+constexpr int H_BYTES = 128 * BK * 2;                          // one CTA's half of A or B per stage
+constexpr int STAGE2 = 2 * H_BYTES;                            // 32 KB
+constexpr size_t SMEM2 = 1024 + (size_t)NS2 * STAGE2 + (size_t)EPI_WARPS2 * 2 * EPI_BUF;
+static_assert(SMEM2 <= 232448, "shared memory over the per-CTA limit");
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(tc::smem_u32(p)), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory completing on the pair leader's mbarrier
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t mbar_cl) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(tc::smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar_cl)
+      : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)acc));
+}
+// arrive once on the barrier at this offset in both CTAs of the pair when the leader's MMAs finish
+__device__ __forceinline__ void commit_pair(uint64_t* mbar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          tc::smem_u32(mbar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+__device__ __forceinline__ void arrive_remote(uint32_t mbar_cl) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(mbar_cl) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+template <bool AMN, bool BMN, int OUT>
+__global__ void __launch_bounds__(NT2, 1)
+    gemm2_k(GemmArgs a, const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint64_t full[NS2], empty[NS2], acc_full[2], acc_empty[2];
+  __shared__ uint32_t tslot;
+  const uint32_t raw = tc::smem_u32(smem_raw);
+  unsigned char* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  unsigned char* epi = base + (size_t)NS2 * STAGE2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();              // 0 = the pair's leader
+  const bool leader = rank == 0;
+  if (warp == 0) tmem_alloc_pair(&tslot, TMEM_COLS);
+  if (tid == 0) {
+    for (int i = 0; i < NS2; ++i) {
+      tc::mbar_init(&full[i], 1);
+      tc::mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&acc_full[i], 1);
+      tc::mbar_init(&acc_empty[i], 2 * EPI_WARPS2 * 32); // both CTAs' epilogue threads
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  tc::fence_before_sync();
+  cluster_sync();                                     // both CTAs' barriers exist before any remote use
+  tc::fence_after_sync();
+  const uint32_t tmem = tslot;
+  const int tiles_m = (a.M + 255) / 256, tiles_n = (a.N + 255) / 256, nkb = (a.K + BK - 1) / BK;
+  const long units = (long)tiles_m * tiles_n * a.split_k;
+  const long pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  bool ok = true;
+  if (warp == PROD_WARP2) {
+    if (lane == 0) {
+      long g = 0;
+      for (long u = pair; u < units && ok; u += npairs) {
+        const long t = u / a.split_k;
+        const int sk = (int)(u % a.split_k);
+        const int tm = (int)(t / tiles_n), tn = (int)(t % tiles_n);
+        const int kb0 = (int)((long)sk * nkb / a.split_k), kb1 = (int)((long)(sk + 1) * nkb / a.split_k);
+        const int ra = tm * 256 + 128 * (int)rank, rb = tn * 256 + 128 * (int)rank;
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
+          const int s = (int)(g % NS2);
+          if (g >= NS2 && !tc::mbar_wait(&empty[s], (uint32_t)(((g / NS2) - 1) & 1))) {
+            ok = false;
+            break;
+          }
+          unsigned char* sA = base + (size_t)s * STAGE2;
+          unsigned char* sB = sA + H_BYTES;
+          const uint32_t fb = map_to_rank(&full[s], 0);
+          if (leader) tc::mbar_expect_tx(&full[s], 2 * STAGE2);   // both CTAs' halves
+          if (!AMN) {
+            tma_load_2d_pair(sA, &tmA, kb * BK, ra, fb);
+          } else {
+            tma_load_2d_pair(sA, &tmA, ra, kb * BK, fb);
+            tma_load_2d_pair(sA + BOX, &tmA, ra + 64, kb * BK, fb);
+          }
+          if (!BMN) {
+            tma_load_2d_pair(sB, &tmB, kb * BK, rb, fb);
+          } else {
+            tma_load_2d_pair(sB, &tmB, rb, kb * BK, fb);
+            tma_load_2d_pair(sB + BOX, &tmB, rb + 64, kb * BK, fb);
+          }
+        }
+      }
+      // every issued load has landed once the MMAs that read it have committed: wait for the
+      // newest phase of each stage's empty barrier (bounded)
+      for (long h = g - NS2 > 0 ? g - NS2 : 0; h < g; ++h) tc::mbar_wait(&empty[h % NS2], (uint32_t)((h / NS2) & 1));
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP2) {
+    if (leader && lane == 0) {
+      const uint32_t idesc = tc::idesc_bf16(256, 256) | (AMN ? tc::IDESC_A_MN : 0u) | (BMN ? tc::IDESC_B_MN : 0u);
+      long g = 0;
+      int j = 0;
+      for (long u = pair; u < units && ok; u += npairs, ++j) {
+        const long t = u / a.split_k;
+        const int sk = (int)(u % a.split_k);
+        const int kb0 = (int)((long)sk * nkb / a.split_k), kb1 = (int)((long)(sk + 1) * nkb / a.split_k);
+        (void)t;
+        const int b = j & 1;
+        if (j >= 2 && !tc::mbar_wait(&acc_empty[b], (uint32_t)(((j >> 1) - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
+          const int s = (int)(g % NS2);
+          if (!tc::mbar_wait(&full[s], (uint32_t)((g / NS2) & 1))) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          unsigned char* sA = base + (size_t)s * STAGE2;
+          unsigned char* sB = sA + H_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks) {
+            const uint64_t ad = AMN ? tc::desc_mn_sw128(sA + ks * 2048, BOX) : tc::desc_sw128(sA, ks);
+            const uint64_t bd = BMN ? tc::desc_mn_sw128(sB + ks * 2048, BOX) : tc::desc_sw128(sB, ks);
+            mma_pair(acc, ad, bd, idesc, kb > kb0 || ks > 0);
+          }
+          commit_pair(&empty[s]);
+        }
+        if (!ok) break;
+        commit_pair(&acc_full[b]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue: CTA r, warp w, lane l holds row 128r + 32w + l of the 256-row tile
+    const uint32_t acc_empty_cl0 = map_to_rank(&acc_empty[0], 0), acc_empty_cl1 = map_to_rank(&acc_empty[1], 0);
+    int j = 0, nb = 0;
+    for (long u = pair; u < units; u += npairs, ++j) {
+      const long t = u / a.split_k;
+      const int tm = (int)(t / tiles_n), tn = (int)(t % tiles_n);
+      const int b = j & 1;
+      if (!tc::mbar_wait(&acc_full[b], (uint32_t)((j >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      const int row0 = tm * 256 + 128 * (int)rank + 32 * warp;
+      const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(b * BN);
+      epilogue_rows<OUT>(a, &tmC, &tmC2, epi + (size_t)warp * 2 * EPI_BUF, lane, tbase, row0, tn * BN, 0, BN, nb);
+      tc::fence_before_sync();
+      if (leader)
+        tc::mbar_arrive(&acc_empty[b]);
+      else
+        arrive_remote(b ? acc_empty_cl1 : acc_empty_cl0);   // the leader's MMA warp waits for both CTAs
+    }
+    if (lane == 0) tc::bulk_wait_all();
+    __syncwarp();
+  }
+  if (!ok) atomicExch(a.status, 1);
+  tc::fence_before_sync();
+  __syncthreads();
+  cluster_sync();                                       // the leader's MMAs may read this CTA's smem until here
+  if (warp == 0) tmem_dealloc_pair(tmem, TMEM_COLS);
 }
 
 }  // namespace gemm
@@ -278,8 +524,8 @@ int encode_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int esize
 template <bool AMN, bool BMN, int OUT>
 int launch_t(const GemmArgs& a, int sms, cudaStream_t st) {
   using namespace s0::gemm;
-  CUtensorMap tmA, tmB, tmC;
-  const bool f32 = OUT != 0;
+  CUtensorMap tmA, tmB, tmC, tmC2;
+  const bool f32 = OUT == 1 || OUT == 2;
   // A: K-major [M, K] (box 64 K x 128 rows) or MN-major [K, M] (box 64 M x 64 K)
   int e = AMN ? encode_2d(&tmA, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.lda, 64, 64)
               : encode_2d(&tmA, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.lda, 64, BM);
@@ -292,34 +538,118 @@ int launch_t(const GemmArgs& a, int sms, cudaStream_t st) {
   e = encode_2d(&tmC, a.C, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, f32 ? 4 : 2,
                 a.c_rows, a.c_cols, a.ldc, f32 ? 32 : 64, 32);
   if (e) return e;
+  tmC2 = tmC;
+  if (OUT == 3 && (e = encode_2d(&tmC2, a.C2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.c_rows, a.c_cols, a.ldc2, 64, 32)))
+    return e;
   auto* kern = gemm_k<AMN, BMN, OUT>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   const long units = (long)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * a.split_k;
   const int grid = (int)(units < sms ? units : sms);
-  kern<<<grid, NT, SMEM, st>>>(a, tmA, tmB, tmC);
+  kern<<<grid, NT, SMEM, st>>>(a, tmA, tmB, tmC, tmC2);
   return (int)cudaGetLastError();
+}
+template <bool AMN, bool BMN, int OUT>
+int launch_pair(const GemmArgs& a, int sms, cudaStream_t st) {
+  using namespace s0::gemm;
+  CUtensorMap tmA, tmB, tmC, tmC2;
+  const bool f32 = OUT == 1 || OUT == 2;
+  // each CTA loads a 128-row (K-major) or 2 x 64-column (MN-major) half of the A and B tiles
+  int e = AMN ? encode_2d(&tmA, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, a.lda, 64, 64)
+              : encode_2d(&tmA, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, a.lda, 64, 128);
+  if (e) return e;
+  e = BMN ? encode_2d(&tmB, a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, a.ldb, 64, 64)
+          : encode_2d(&tmB, a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.ldb, 64, 128);
+  if (e) return e;
+  e = encode_2d(&tmC, a.C, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, f32 ? 4 : 2,
+                a.c_rows, a.c_cols, a.ldc, f32 ? 32 : 64, 32);
+  if (e) return e;
+  tmC2 = tmC;
+  if (OUT == 3 && (e = encode_2d(&tmC2, a.C2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.c_rows, a.c_cols, a.ldc2, 64, 32)))
+    return e;
+  auto* kern = gemm2_k<AMN, BMN, OUT>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2);
+  const long units = (long)((a.M + 255) / 256) * ((a.N + 255) / 256) * a.split_k;
+  long pairs = units < sms / 2 ? units : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(NT2);
+  cfg.dynamicSmemBytes = SMEM2;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // persistent pairs must all be resident at once (a pair lives in one GPC): no more pairs than
+  // the device can hold together
+  int max_clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&max_clusters, (const void*)kern, &cfg) == cudaSuccess && max_clusters > 0 &&
+      pairs > max_clusters)
+    pairs = max_clusters;
+  if (pairs < 1) return -7;
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, a, tmA, tmB, tmC, tmC2);
+  return err == cudaSuccess ? 0 : (int)err;
 }
 }  // namespace
 
-int gemm_tc_launch(const GemmArgs& a, int sms, cudaStream_t st) {
+// 1: the two-SM kernel (default), 0: the one-SM kernel
+int g_gemm_pair = 1;
+void gemm_tc_set_pair(int on) { g_gemm_pair = on; }
+
+// K split for a reduce-add product: the split (1..16, at least 16 K-blocks per part) whose work
+// units fill the last wave of `slots` persistent workers best
+static int pick_split(long tiles, int K, int slots) {
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= 16; ++s) {
+    if (s > 1 && (K + BK - 1) / BK / s < 16) break;
+    const long units = tiles * s, waves = (units + slots - 1) / slots;
+    const double eff = (double)units / (double)(waves * slots);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+int gemm_tc_launch(const GemmArgs& a_in, int sms, cudaStream_t st) {
+  GemmArgs a = a_in;
+  if (a.split_k == 0) {        // auto: only for the reduce-add mode
+    if (a.out_mode != 2) {
+      a.split_k = 1;
+    } else if (g_gemm_pair) {
+      a.split_k = pick_split((long)((a.M + 255) / 256) * ((a.N + 255) / 256), a.K, sms / 2);
+    } else {
+      a.split_k = pick_split((long)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN), a.K, sms);
+    }
+  }
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.split_k < 1) return -1;
   if (a.split_k > 1 && a.out_mode != 2) return -2;          // K splits sum through the reduce-add
   // TMA: 16-byte aligned bases, leading dimensions multiples of 16 bytes
   if ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B) | reinterpret_cast<uintptr_t>(a.C)) % 16)
     return -3;
-  const int ce = a.out_mode == 0 ? 2 : 4;
+  const int ce = (a.out_mode == 1 || a.out_mode == 2) ? 4 : 2;
+  if (a.out_mode == 3) {      // fused epilogue: whole 64-column chunks, an aligned second output
+    if (a.c_cols % 64) return -8;
+    if (a.out_mode == 3 && (reinterpret_cast<uintptr_t>(a.C2) % 16 || (a.ldc2 * 2) % 16)) return -9;
+  }
   if ((a.lda * 2) % 16 || (a.ldb * 2) % 16 || ((long)a.ldc * ce) % 16) return -4;
   if (a.c_rows < 1 || a.c_cols < 1 || a.c_rows > a.M || a.c_cols > a.N) return -5;
   const int key = (a.a_mn ? 4 : 0) | (a.b_mn ? 2 : 0);
-#define S0_GEMM_CASE(AM, BMj, O)                             \
-  if (key == ((AM ? 4 : 0) | (BMj ? 2 : 0)) && a.out_mode == O) \
-    return launch_t<AM, BMj, O>(a, sms, st);
+#define S0_GEMM_CASE(AM, BMj, O)                                                                   \
+  if (key == ((AM ? 4 : 0) | (BMj ? 2 : 0)) && a.out_mode == O)                                       \
+    return g_gemm_pair ? launch_pair<AM, BMj, O>(a, sms, st) : launch_t<AM, BMj, O>(a, sms, st);
   S0_GEMM_CASE(false, true, 0)    // forward
   S0_GEMM_CASE(false, false, 0)   // input gradient
   S0_GEMM_CASE(true, true, 2)     // weight gradient, accumulated in fp32
   S0_GEMM_CASE(true, true, 1)     // weight gradient, stored in fp32
   S0_GEMM_CASE(false, true, 1)
   S0_GEMM_CASE(false, false, 1)
+  S0_GEMM_CASE(false, true, 3)    // o = x . W and g = gelu(o)
 #undef S0_GEMM_CASE
   return -6;
 }

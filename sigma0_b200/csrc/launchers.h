@@ -197,7 +197,7 @@ void ln_bwd_pipe_launch(const void* dy, const float* x, const float* mean, const
 // A is [M, K] K-major (row-major, leading dimension lda) or, with a_mn, stored [K, M] MN-major;
 // B is [N, K] K-major or, with b_mn, stored [K, N] MN-major.  C is written over its first
 // c_rows x c_cols entries (c_rows <= M, c_cols <= N; leading dimension ldc): out_mode 0 bf16
-// store, 1 fp32 store, 2 fp32 reduce-add (split_k > 1 only with 2).  Bases 16-byte aligned,
+// store, 1 fp32 store, 2 fp32 reduce-add (split_k > 1 only with 2), 3 bf16 store plus its GELU.  Bases 16-byte aligned,
 // leading dimensions multiples of 16 bytes.
 struct GemmArgs {
   const void* A;
@@ -210,8 +210,13 @@ struct GemmArgs {
   int out_mode;
   int split_k;
   int* status;                 // 1: a pipeline wait timed out
+  // out_mode 3 (the GLU block's fused epilogue) also writes C2 = gelu(C) (bf16, leading
+  // dimension ldc2)
+  void* C2;
+  long ldc2;
 };
 int gemm_tc_launch(const GemmArgs& a, int sms, cudaStream_t st);
+void gemm_tc_set_pair(int on);   // 1 (default): two-SM tcgen05 tiles, 0: one-SM tiles
 
 // tensor-parallel row-parallel GEMM fused with its all-reduce over peer memory (tp_fused.cu)
 #define TPF_MAXW 8

@@ -14,6 +14,7 @@ from __future__ import annotations
 import torch
 
 from ._ext import ext
+from . import gemm as G
 from . import weights as W
 
 CHUNK_ROWS = 8192
@@ -35,12 +36,17 @@ class _LinearCEMean(torch.autograd.Function):
         dh = torch.empty_like(hf)
         dW = torch.zeros(d, V, dtype=torch.float32, device=h.device)
         db = torch.zeros(V, dtype=torch.float32, device=h.device)
+        tc = G.USE_TC and V % 8 == 0 and d % 8 == 0
         for s in range(0, T, CHUNK_ROWS):
             e = min(T, s + CHUNK_ROWS)
-            logits = hf[s:e] @ wk
+            logits = G.mm(hf[s:e], wk) if tc else hf[s:e] @ wk
             loss_rows[s:e] = C.ce_fwd_bwd(logits, bias, lab[s:e], wr[s:e], V)
-            dh[s:e] = logits @ wk.t()
-            dW += torch.mm(hf[s:e].t(), logits, out_dtype=torch.float32)
+            if tc:
+                dh[s:e] = G.mm_nt(logits, wk)
+                G.mm_tn_acc(hf[s:e], logits, dW)          # fp32 accumulation across chunks
+            else:
+                dh[s:e] = logits @ wk.t()
+                dW += torch.mm(hf[s:e].t(), logits, out_dtype=torch.float32)
             db += logits.sum(0, dtype=torch.float32)
         loss = (loss_rows * wr).sum()
         ctx.save_for_backward(dh, dW, db)

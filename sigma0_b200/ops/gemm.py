@@ -13,17 +13,16 @@ The reference computes these as XLA dots inside ``nn.Dense``
 """
 from __future__ import annotations
 
+import os
+from typing import Optional
+
 import torch
 
 from ._ext import ext
 
-# weight gradients whose output tiles cannot fill the GPU are split along the long reduction
-# (tokens) into this many parts at most; the parts meet in the fp32 reduce-add
-_MAX_SPLIT = 8
-
-
-def _sms(t: torch.Tensor) -> int:
-    return torch.cuda.get_device_properties(t.device).multi_processor_count
+# S0_GEMM=cublas routes the model projections through torch.matmul instead (the comparison arm
+# of the step benchmarks); the default is this package's kernel
+USE_TC = os.environ.get("S0_GEMM", "tc") != "cublas"
 
 
 def _rows(t: torch.Tensor) -> torch.Tensor:
@@ -42,19 +41,70 @@ def mm_nt(dy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 
 def mm_tn_acc(x: torch.Tensor, dy: torch.Tensor, out: torch.Tensor, split_k: int = 0) -> torch.Tensor:
     """``out += x[T, M]^T @ dy[T, N]`` with ``out`` fp32 of shape ``[<= M, <= N]`` (the
-    rows / columns beyond it are dropped).  ``split_k`` 0 picks a split that gives every SM
-    a share of the output tiles."""
-    M, N = x.shape[1], dy.shape[1]
-    if split_k <= 0:
-        tiles = -(-M // 128) * -(-N // 256)
-        sms = _sms(x)
-        split_k = max(1, min(_MAX_SPLIT, sms // max(tiles, 1)))
-        while split_k > 1 and x.shape[0] // split_k < 64 * 4:
-            split_k -= 1
-    ext().gemm_tc(_rows(x), _rows(dy), True, True, 2, out, split_k)
+    rows / columns beyond it are dropped).  ``split_k`` 0 lets the launcher split the long
+    token reduction so the output tiles fill every SM (the parts meet in the reduce-add)."""
+    ext().gemm_tc(_rows(x), _rows(dy), True, True, 2, out, max(0, int(split_k)))
     return out
+
+
+def use_pair(on: bool = True) -> None:
+    """Two-SM (``cta_group::2``, 256 x 256) tiles (the default) or one-SM 128 x 256 tiles."""
+    ext().gemm_use_pair(bool(on))
 
 
 def status(like: torch.Tensor) -> int:
     """1 once a bounded wait of the GEMM gave up on this device (reads the device word)."""
     return int(ext().gemm_status(like).item())
+
+
+# ---- the model's projection products (the kernel, or torch.matmul under S0_GEMM=cublas) --------
+def proj(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x @ w`` (bf16)."""
+    return mm(x, w) if USE_TC else x @ w
+
+
+def proj_dx(dy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``dy @ w^T`` (bf16)."""
+    return mm_nt(dy, w) if USE_TC else dy @ w.t()
+
+
+def _fusable(*ts: torch.Tensor) -> bool:
+    return USE_TC and all(t.is_cuda and t.stride(-1) == 1 and t.data_ptr() % 16 == 0 for t in ts)
+
+
+def proj_gelu(x: torch.Tensor, w: torch.Tensor):
+    """``o = x @ w`` and ``g = gelu(o)`` (both bf16), one GEMM with the GELU in its epilogue."""
+    if _fusable(x, w) and w.shape[1] % 64 == 0:
+        o, g = ext().gemm_gelu_fwd(_rows(x), _rows(w))
+        return o, g
+    o = proj(x, w)
+    return o, ext().gelu_fwd(o)
+
+
+def _owns_grad(param: torch.Tensor) -> bool:
+    g = param.grad
+    return (getattr(param, "_s0_flat_grad", False) and g is not None and g.dtype == torch.float32
+            and g.stride(-1) == 1 and g.data_ptr() % 16 == 0 and (g.stride(0) * 4) % 16 == 0)
+
+
+def wgrad(param: torch.Tensor, x: torch.Tensor, dy: torch.Tensor) -> Optional[torch.Tensor]:
+    """The weight gradient ``x^T @ dy`` of ``param`` (its leading ``param.shape`` block).
+
+    For a parameter whose gradient lives in the flat float32 buffer of the optimizer (marked
+    ``_s0_flat_grad`` by it) the product is reduce-added straight into ``param.grad`` in fp32 and
+    None is returned: autograd has nothing left to accumulate.  Otherwise the gradient is returned
+    as a new float32 tensor."""
+    r, c = param.shape
+    if not USE_TC:
+        return (x.t() @ dy)[:r, :c].float()
+    if _owns_grad(param):
+        mm_tn_acc(x, dy, param.grad)
+        return None
+    # a separate fp32 result whose rows are padded to 16 bytes for the tensor map (odd widths such
+    # as the 503-wide book layers); the leading block is returned
+    cp = (c + 3) // 4 * 4
+    if cp > dy.shape[1] or r > x.shape[1]:
+        return (x.t() @ dy)[:r, :c].float()
+    out = torch.zeros(r, cp, dtype=torch.float32, device=x.device)
+    mm_tn_acc(x, dy, out)
+    return out[:, :c]

@@ -11,9 +11,10 @@ Two autograd functions:
 * :func:`mamba3_mixer` -- the mixer alone (in_proj ... out_proj), used where the
   residual wrapper is not fused (e.g. the book pre-layer at width 503).
 
-GEMMs are cuBLAS bf16 (``torch.matmul``; weight gradients with fp32 output);
-the SSD, its pre/post-processing and all row/elementwise work are the sm_100a
-kernels of ``csrc/``.  The projection buffer's row stride is padded to a
+GEMMs run on the package's tcgen05 kernel (``ops/gemm.py``): bf16 operands, fp32
+accumulation; weight gradients are reduce-added in fp32 straight into the flat gradient
+buffer.  The SSD, its pre/post-processing and all row/elementwise work are the sm_100a
+kernels of ``csrc/`` too.  The projection buffer's row stride is padded to a
 multiple of 8 elements so every kernel can use 16-byte accesses.
 """
 from __future__ import annotations
@@ -24,6 +25,7 @@ import torch
 import torch.nn.functional as F
 
 from ._ext import ext
+from . import gemm as G
 from . import weights as W
 
 EPS = 1e-6
@@ -39,12 +41,6 @@ def _pad8(n: int) -> int:
     return (n + 7) // 8 * 8
 
 
-def _mm_f32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """Weight gradient a @ b: bf16 operands, fp32 accumulation in the GEMM, bf16 result
-    (autograd widens it into the float32 gradient buffer)."""
-    return a @ b
-
-
 def _check_dims(m) -> None:
     d = m.dims
     if (d.d_state, d.headdim, d.chunk_size, d.R) != (128, 64, 64, 32):
@@ -57,7 +53,8 @@ class _Mamba3Core:
     """Forward/backward of in_proj -> SSD -> out_norm -> out_proj on flat rows."""
 
     @staticmethod
-    def forward(xn, B, L, m):
+    def forward(xn, B, L, m, want_gelu: bool = False):
+        """``want_gelu``: also return gelu(o) from the out_proj GEMM's epilogue."""
         C = ext()
         d = m.dims
         ldp = _pad8(d.d_in_proj)
@@ -67,16 +64,22 @@ class _Mamba3Core:
         if Hp != H:   # odd widths (the 503-wide book layers): pad K so the GEMM rows are 16-byte aligned
             xn = F.pad(xn, (0, Hp - H))
             w_in = F.pad(w_in, (0, 0, 0, Hp - H))
-        proj = xn @ w_in                                              # [T, ldp]
+        proj = G.proj(xn, w_in)                                       # [T, ldp]
         out = C.m3_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias,
                        m.C_bias, m.D, m.A_floor, m.B_norm.eps, return_prep=SAVE_STATES)
         y, states = out[0], out[1]
         prep = tuple(out[4:]) if SAVE_STATES else ()
         y2 = y.view(-1, d.d_inner)
         yn, yr = C.rms_fwd(y2, m.out_norm.scale, m.out_norm.eps)
-        o = yn @ W.bf16_padded(m.out_proj.kernel, Hp)                 # [T, Hp]
+        g = None
+        if want_gelu and Hp == H:
+            o, g = G.proj_gelu(yn, W.bf16_padded(m.out_proj.kernel, Hp))
+        else:
+            o = G.proj(yn, W.bf16_padded(m.out_proj.kernel, Hp))      # [T, Hp]
         if Hp != H:
             o = o[:, :H]
+        if want_gelu:
+            return o, g, proj, y2, yr, ((states,) + prep if SAVE_STATES else None)
         # the passed chunk states (bf16, B*nh*nc*P*N) and the per-token prep (BCNorm'd B/C,
         # dt, decay, gate, angle rates, chunk carries: ~1/8 of the states' size) are kept for
         # the backward unless the model is set to recompute them (memory for time)
@@ -98,16 +101,16 @@ class _Mamba3Core:
             xn = F.pad(xn, (0, Hp - H))
             w_in = F.pad(w_in, (0, 0, 0, Hp - H))
         yn, _ = C.rms_fwd(y2, m.out_norm.scale, m.out_norm.eps)
-        g_out_proj = _mm_f32(yn.t(), do)[:, :H]
-        dyn = do @ w_out.t()
+        g_out_proj = G.wgrad(m.out_proj.kernel, yn, do)
+        dyn = G.proj_dx(do, w_out)
         dy, g_out_norm = C.rms_bwd(dyn.contiguous(), y2, m.out_norm.scale, yr)
         saved_states = states[0] if states else None
         saved_prep = list(states[1:]) if states and len(states) in (7, 8) else None
         dproj, dwB, dwC, ddtb, dD, dCb, dBb = C.m3_bwd(
             proj, dy, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias, m.C_bias, m.D, B, L,
             d.n_heads, m.A_floor, m.B_norm.eps, saved_states=saved_states, saved_prep=saved_prep)
-        g_in = _mm_f32(xn.t(), dproj)[:H, :d.d_in_proj]
-        dxn = (dproj @ w_in.t())[:, :H]
+        g_in = G.wgrad(m.in_proj.kernel, xn, dproj)
+        dxn = G.proj_dx(dproj, w_in)[:, :H]
         grads = {m.out_proj.kernel: g_out_proj, m.out_norm.scale: g_out_norm, m.in_proj.kernel: g_in,
                  m.B_norm.scale: dwB, m.C_norm.scale: dwC, m.dt_bias: ddtb, m.D: dD,
                  m.C_bias: dCb, m.B_bias: dBb}
@@ -157,9 +160,10 @@ class _LayerFn(torch.autograd.Function):
         if xf.dtype != torch.float32 or not xf.is_contiguous():
             xf = xf.float().contiguous()
         xn, mu, rs = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)
-        o, proj, y2, yr, st = _Mamba3Core.forward(xn, B, L, m)
-        g = C.gelu_fwd(o)
-        h = g @ W.bf16(layer.out2.kernel)
+        o, g, proj, y2, yr, st = _Mamba3Core.forward(xn, B, L, m, want_gelu=True)
+        if g is None:
+            g = C.gelu_fwd(o)
+        h = G.proj(g, W.bf16(layer.out2.kernel))
         out = C.glu_res_fwd(xf, g, h, layer.out2.bias)
         ctx.layer, ctx.shape = layer, (B, L, H)
         ctx.n_st = 0 if st is None else len(st)
@@ -183,8 +187,8 @@ class _LayerFn(torch.autograd.Function):
             dout = dout.float().contiguous()
         g = g_s if ctx.saved_acts else C.gelu_fwd(o)
         dh, dgp, db2 = C.glu_res_bwd(dout, g, h, layer.out2.bias)
-        g_out2 = _mm_f32(g.t(), dh)
-        dgm = dh @ W.bf16(layer.out2.kernel).t()
+        g_out2 = G.wgrad(layer.out2.kernel, g, dh)
+        dgm = G.proj_dx(dh, W.bf16(layer.out2.kernel))
         do = C.gelu_bwd(o, dgp, dgm.contiguous())
         xn = xn_s if ctx.saved_acts else C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)[0]
         dxn, grads = _Mamba3Core.backward(do, xn, proj, y2, yr, B, L, m, st)

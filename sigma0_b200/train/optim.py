@@ -99,6 +99,7 @@ class FlatAdam:
             self.flat[off:off + k].copy_(p.detach().reshape(-1))
             p.data = self.flat[off:off + k].view_as(p)
             p.grad = self.grad[off:off + k].view_as(p)
+            p._s0_flat_grad = True      # fused weight-gradient GEMMs may accumulate into p.grad
             if self.shadow is not None:
                 W.register(p, self.shadow[off:off + k].view(p.shape))
             self.names.append(n)

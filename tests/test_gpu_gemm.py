@@ -78,3 +78,61 @@ def test_strided_operands():
     x = buf[:, 8:264]                        # [512, 256], row stride 400
     w = torch.randn(256, 384, device="cuda", generator=g).bfloat16()
     assert _rel(gemm.mm(x, w), x.float() @ w.float()) < 8e-3
+
+
+@cuda
+def test_trainer_gradients_match_the_library_gemm_arm():
+    """One training step of a small CUDA Mamba3 LOB model: the flat gradient with the tcgen05
+    projections (weight gradients reduce-added straight into the optimizer's buffer) equals the
+    one computed with torch.matmul."""
+    from sigma0_b200.data import LobWindowDataset, collate, make_sequences
+    from sigma0_b200.models import preset_args
+    from sigma0_b200.ops import gemm
+    from sigma0_b200.train.trainer import Trainer
+    args = preset_args("smoke", impl="cuda", d_model=256, mamba3_d_state=128, mamba3_headdim=64, n_messages=24,
+                       micro_bsz=2, n_layers=2, dtype="bfloat16")
+    days = make_sequences(2, args.n_messages + 1, seed=5)
+    ds = LobWindowDataset.from_days(days, args.n_messages, token_mode=args.token_mode)
+    batch = [t.cuda() for t in collate([ds[i] for i in range(2)])]
+    grads = []
+    saved = gemm.USE_TC
+    try:
+        for tc in (True, False):
+            gemm.USE_TC = tc
+            tr = Trainer(args, device=torch.device("cuda"), world=1, rank=0, total_steps=10, seed=0)
+            tr.opt.zero_grad()
+            loss, _ = tr.model.loss(batch[0], batch[2], batch[1])
+            loss.backward()
+            grads.append(tr.opt.grad.clone())
+    finally:
+        gemm.USE_TC = saved
+    assert torch.isfinite(grads[0]).all() and float(grads[0].abs().sum()) > 0
+    assert _rel(grads[0], grads[1]) < 2e-2
+
+
+@cuda
+def test_weight_gradient_of_an_odd_width_parameter():
+    """A 503-column weight (the book layers): the fp32 result rows are padded for the tensor
+    map and the leading block comes back."""
+    from sigma0_b200.ops import gemm
+    g = torch.Generator(device="cuda").manual_seed(6)
+    p = torch.nn.Parameter(torch.zeros(960, 503, device="cuda"))
+    x = torch.randn(2000, 960, device="cuda", generator=g).bfloat16()
+    dy = torch.randn(2000, 504, device="cuda", generator=g).bfloat16()
+    got = gemm.wgrad(p, x, dy)
+    assert got.shape == (960, 503)
+    assert _rel(got, (x.float().t() @ dy.float())[:, :503]) < 1e-5
+
+
+@cuda
+def test_fused_gelu_forward_epilogue():
+    import torch.nn.functional as F
+    from sigma0_b200.ops import gemm
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = (torch.randn(3000, 512, device="cuda", generator=g) * 0.1).bfloat16()
+    w = (torch.randn(512, 1024, device="cuda", generator=g) * 0.1).bfloat16()
+    o, gl = gemm.proj_gelu(x, w)
+    ref = x.float() @ w.float()
+    assert _rel(o, ref) < 8e-3
+    # g is the GELU of the stored bf16 o
+    assert _rel(gl, F.gelu(o.float(), approximate="tanh")) < 8e-3
