@@ -134,6 +134,18 @@ class CheckpointManager:
                 "global_batch": int(getattr(trainer, "global_batch", 0)), "world": self.world,
                 "config": config or {}, "metrics": metrics or {}}
         rank = self.rank
+        # FSDP-sharded kernels (parallel/fsdp.py): every rank takes part in gathering the full
+        # fp32 kernels, rank 0 writes them by Flax path; each rank writes its moment shards
+        fsdp = getattr(trainer, "fsdp", None)
+        fsdp_host = None
+        if fsdp is not None:
+            names = {id(p): n for n, p in trainer.model.named_parameters()}
+            full = fsdp.full_parameters()
+            fsdp_host = {"params": {flax_path(names[id(p)]): t.cpu().numpy() for p, t in full.items()}
+                         if self.rank == 0 else None,
+                         "m": torch.cat([u.m for u in fsdp.units]).cpu().numpy(),
+                         "v": torch.cat([u.v for u in fsdp.units]).cpu().numpy()}
+            meta["fsdp_step"] = int(fsdp.step_count)
 
         def write():
             try:
@@ -144,6 +156,15 @@ class CheckpointManager:
                     p = os.path.join(st, name)
                     h.numpy().tofile(p)
                     files[name] = _sha256(p)
+                if fsdp_host is not None:
+                    for key in ("m", "v"):
+                        name = f"fsdp_{key}.r{rank}.f32"
+                        fsdp_host[key].tofile(os.path.join(st, name))
+                        files[name] = _sha256(os.path.join(st, name))
+                    if fsdp_host["params"] is not None:
+                        name = "fsdp_params.npz"
+                        np.savez(os.path.join(st, name), **fsdp_host["params"])
+                        files[name] = _sha256(os.path.join(st, name))
                 with open(os.path.join(st, f"hashes.r{rank}.json"), "w") as f:
                     json.dump(files, f)
                 if rank == 0:
@@ -198,6 +219,9 @@ class CheckpointManager:
         """The step in the Orbax layout (``ckpt/orbax.py``): ``state`` = {params, step,
         opt_state/{mu, nu} (unsharded optimizers)}, ``metadata`` = the JSON record."""
         from . import orbax as ox
+        if getattr(trainer, "fsdp", None) is not None:
+            raise CheckpointError("the Orbax layout is written for replicated parameters; save FSDP runs with "
+                                  "fmt='native'")
         opt = trainer.opt
         tmp = os.path.join(self.base, f".{step}.tmp")
         final = os.path.join(self.base, str(step))
@@ -295,8 +319,36 @@ class CheckpointManager:
                                       int(meta["optimizer_step"]))
                 gb_new = int(getattr(trainer, "global_batch", 0))
                 trainer.step_idx = remap_step(int(meta["trainer_step"]), int(meta.get("global_batch", 0)), gb_new)
+        self._restore_fsdp(trainer, d, index, params_only)
+        if getattr(trainer, "fsdp", None) is not None and not params_only:
+            trainer.fsdp.step_count = int(meta.get("fsdp_step", 0))
         meta["restored_step"] = chosen
         return meta
+
+    def _restore_fsdp(self, trainer, d: str, index: Dict, params_only: bool) -> None:
+        """The FSDP-sharded kernels: full parameters by Flax path, re-sharded for this run; the
+        moment shards when the world size is the same."""
+        fsdp = getattr(trainer, "fsdp", None)
+        path = os.path.join(d, "state", "fsdp_params.npz")
+        if fsdp is None:
+            return
+        if not os.path.exists(path):
+            raise CheckpointError(f"{d} has no FSDP kernels (saved without FSDP?)")
+        arrs = np.load(path)
+        names = {id(p): n for n, p in trainer.model.named_parameters()}
+        full = {p: torch.from_numpy(arrs[flax_path(names[id(p)])]).to(fsdp.device)
+                for p in fsdp.sharded_parameters()}
+        fsdp.load_full_parameters(full)
+        mp = os.path.join(d, "state", f"fsdp_m.r{self.rank}.f32")
+        if not params_only and index.get("world") == self.world and os.path.exists(mp):
+            m = torch.from_numpy(np.fromfile(mp, dtype=np.float32)).to(fsdp.device)
+            v = torch.from_numpy(np.fromfile(os.path.join(d, "state", f"fsdp_v.r{self.rank}.f32"),
+                                             dtype=np.float32)).to(fsdp.device)
+            o = 0
+            for u in fsdp.units:
+                u.m.copy_(m[o:o + u.shard])
+                u.v.copy_(v[o:o + u.shard])
+                o += u.shard
 
     def _restore_orbax(self, trainer, d: str, meta: Dict, chosen: int, params_only: bool) -> Dict:
         from . import orbax as ox

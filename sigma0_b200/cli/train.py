@@ -184,6 +184,8 @@ def build_parser() -> argparse.ArgumentParser:
     # distributed
     p.add_argument("--dp_impl", choices=["nccl", "fused"], default="nccl")
     p.add_argument("--sharded", action="store_true")
+    p.add_argument("--fsdp", action="store_true",
+                   help="ZeRO-3: shard the fused layers' projection kernels, gather them per layer")
     p.add_argument("--grad_wire_dtype", default="float32", choices=["float32", "bfloat16"])
     p.add_argument("--accum_steps", "--grad_accum_steps", dest="accum_steps", type=int, default=1)
     p.add_argument("--tp", "--tp_size", dest="tp", type=int, default=1,
@@ -311,11 +313,11 @@ def main(argv=None):
     save_every = max(steps // 10, 1) if str(a.save_every) == "auto" else int(a.save_every)
 
     hier = bool(a.hierarchical) and world > 1 and tp == 1 and not cp and not diloco and not a.sharded \
-        and a.dp_impl == "nccl" and _nodes(world, a.gpus_per_node) > 1
+        and not a.fsdp and a.dp_impl == "nccl" and _nodes(world, a.gpus_per_node) > 1
     trainer = Trainer(args, device=dev, world=1 if diloco else world, rank=0 if diloco else rank,
                       total_steps=steps, seed=a.seed, sharded=a.sharded, accum_steps=a.accum_steps,
                       grad_wire_dtype=a.grad_wire_dtype, dp_impl=a.dp_impl, context_parallel=a.context_parallel,
-                      tp=a.tp, hierarchical=hier, gpus_per_node=a.gpus_per_node)
+                      tp=a.tp, hierarchical=hier, gpus_per_node=a.gpus_per_node, fsdp=a.fsdp)
     if diloco:
         from ..train.diloco import DiLoCo
         outer = DiLoCo(trainer, inner_steps=a.local_steps_k, outer_lr=a.diloco_outer_lr,

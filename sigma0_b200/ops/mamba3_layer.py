@@ -159,6 +159,9 @@ class _LayerFn(torch.autograd.Function):
         xf = x.reshape(-1, H)
         if xf.dtype != torch.float32 or not xf.is_contiguous():
             xf = xf.float().contiguous()
+        fs = getattr(layer, "_s0_fsdp", None)
+        if fs is not None:                # sharded kernels: gather this layer's (parallel/fsdp.py)
+            fs.before_forward(layer)
         xn, mu, rs = C.ln_fwd(xf, layer.norm.scale, layer.norm.bias, layer.norm.eps)
         o, g, proj, y2, yr, st = _Mamba3Core.forward(xn, B, L, m, want_gelu=True)
         if g is None:
@@ -182,6 +185,9 @@ class _LayerFn(torch.autograd.Function):
         layer = ctx.layer
         m = layer.seq
         B, L, H = ctx.shape
+        fs = getattr(layer, "_s0_fsdp", None)
+        if fs is not None:                # gather the kernels again, point their grads at the layer buffer
+            fs.before_backward(layer)
         dout = dout.reshape(-1, H)
         if dout.dtype != torch.float32 or not dout.is_contiguous():
             dout = dout.float().contiguous()
@@ -197,6 +203,8 @@ class _LayerFn(torch.autograd.Function):
         grads[layer.norm.bias] = dlb
         grads[layer.out2.kernel] = g_out2
         grads[layer.out2.bias] = db2
+        if fs is not None:                # reduce-scatter the layer's kernel gradients (side stream)
+            fs.after_backward(layer)
         return (dx.view(B, L, H), None) + tuple(grads[p] for p in _layer_params(layer))
 
 

@@ -51,14 +51,16 @@ class FlatAdam:
     def __init__(self, model: nn.Module, lr: float, ssm_lr: float, weight_decay: float = 0.05,
                  max_grad_norm: float = 1.0, betas=(0.9, 0.999), eps: float = 1e-8,
                  opt_config: str = "standard", attention_model: bool = False,
-                 bf16_shadow: bool = True, pad_multiple: int = 128, alloc=None, last=(), dt_global: bool = False):
+                 bf16_shadow: bool = True, pad_multiple: int = 128, alloc=None, last=(), dt_global: bool = False,
+                 exclude=()):
         self.model = model
         self.b1, self.b2 = betas
         self.eps = eps
         self.wd = weight_decay
         self.max_grad_norm = max_grad_norm
         self.base_lr = {"ssm": ssm_lr, "regular": lr}
-        named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+        skip = {id(p) for p in exclude}              # parameters another optimizer owns (FSDP shards)
+        named = [(n, p) for n, p in model.named_parameters() if p.requires_grad and id(p) not in skip]
         groups = {"ssm": [], "regular": []}
         for n, p in named:
             groups[leaf_group(n, opt_config, attention_model, dt_global)].append((n, p))

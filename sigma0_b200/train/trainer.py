@@ -43,7 +43,7 @@ class Trainer:
                  group=None, total_steps: int = 1000, seed: int = 0, sharded: bool = False,
                  accum_steps: int = 1, grad_wire_dtype: str = "float32", dp_impl: str = "nccl",
                  context_parallel: bool = False, tp: int = 1, hierarchical: bool = False,
-                 gpus_per_node: Optional[int] = None):
+                 gpus_per_node: Optional[int] = None, fsdp: bool = False):
         self.args = args
         self.device = device or torch.device("cuda" if torch.cuda.is_available() else "cpu")
         from ..encoding.tok1 import encoding_mode
@@ -93,6 +93,19 @@ class Trainer:
             self.hier = (mesh.group("nodes"), mesh.group("gpus"), mesh.size("gpus"))
         lr_base = float(getattr(args, "ssm_lr_base", 1e-3))
         lr = lr_base * float(getattr(args, "lr_factor", 1.0))
+        # ZeRO-3 over the fused layers' projection kernels (parallel/fsdp.py); the rest of the
+        # parameters stay replicated under the flat optimizer below
+        self.fsdp = None
+        if fsdp and world > 1:
+            if self.tp > 1 or context_parallel or sharded or self.hier is not None or dp_impl == "fused" or \
+                    accum_steps < 1:
+                raise ValueError("FSDP runs plain data parallelism over the default group")
+            if str(getattr(args, "opt_config", "standard")) == "muon":
+                raise ValueError("FSDP shards the AdamW state of the kernels; Muon is not supported with it")
+            from ..parallel.fsdp import FSDP
+            self.fsdp = FSDP(self.model, world, rank, group, lr=lr,
+                             weight_decay=float(getattr(args, "weight_decay", 0.05)),
+                             wire_bf16=grad_wire_dtype == "bfloat16")
         opt_cls = FlatAdam
         extra_opt = {}
         if str(getattr(args, "opt_config", "standard")) == "muon":
@@ -109,7 +122,8 @@ class Trainer:
                             pad_multiple=128 * (world if ((sharded or dp_impl == "fused" or hierarchical)
                                                           and world > 1) else 1),
                             alloc=self._alloc(dp_impl, world), last=tp_slices,
-                            dt_global=bool(getattr(args, "dt_global", False)))
+                            dt_global=bool(getattr(args, "dt_global", False)),
+                            exclude=self.fsdp.sharded_parameters() if self.fsdp is not None else ())
         self.total_steps = total_steps
         self.warmup_steps = int(round(float(getattr(args, "warmup_end", 0.01)) * total_steps))
         lr_min = float(getattr(args, "lr_min", 0.0) or 0.0)
@@ -165,6 +179,9 @@ class Trainer:
         if self.hier is not None:
             self._update_hier(lr_scale)
             return
+        if self.fsdp is not None:
+            self._update_fsdp(lr_scale)
+            return
         if self.world == 1:
             opt.step(lr_scale=lr_scale)
             return
@@ -202,6 +219,24 @@ class Trainer:
         opt.step_shard(gs, ss, lr_scale=lr_scale)
         dist.all_gather_into_tensor(opt.flat, opt.flat[opt.lo:opt.hi].clone(), group=self.group)
         opt.refresh_shadow()
+
+    def _update_fsdp(self, lr_scale: float):
+        """Replicated parameters: all-reduce and the flat AdamW; sharded kernels: their
+        gradient shards (reduce-scattered during the backward) and the sharded AdamW; one global
+        gradient norm over both for clipping."""
+        fs = self.fsdp
+        fs.sync()
+        g = self.opt.grad
+        if self.wire_bf16:
+            gb = g.to(torch.bfloat16)
+            dist.all_reduce(gb, group=self.group)
+            g.copy_(gb)
+        else:
+            dist.all_reduce(g, group=self.group)
+        g.div_(self.world)
+        total = fs.grad_sumsq() + (g * g).sum().reshape(1)
+        self.opt.step(lr_scale=lr_scale, grad_sumsq=total)
+        fs.step(lr_scale, total, self.opt.max_grad_norm)
 
     def _update_hier(self, lr_scale: float):
         """Two-level gradient average (the reference's hierarchical step,
@@ -251,6 +286,8 @@ class Trainer:
         """One optimizer step on device tensors; with ``accum_steps > 1`` the batch is
         split into micro-batches whose gradients accumulate before the update."""
         self.opt.zero_grad()
+        if self.fsdp is not None:
+            self.fsdp.zero_grad()
         if self.cp:
             tokens, labels, book = self._segment(tokens, labels, book)
         k = self.accum_steps

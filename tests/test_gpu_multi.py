@@ -238,3 +238,49 @@ def test_mamba3_context_parallel_on_the_walkers_matches_one_gpu(tmp_path):
     assert rel(r["gx"], r["gxf"]) < 3e-2, rel(r["gx"], r["gxf"])
     # parameter gradients: bf16 weight-gradient GEMMs on both sides, accumulated differently
     assert rel(r["g"], r["gf"]) < 6e-2, rel(r["g"], r["gf"])
+
+
+def _fsdp_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from sigma0_b200.train.trainer import Trainer
+        batch = _batch(rank)
+        res = {}
+        for mode in ("dp", "fsdp"):
+            tr = Trainer(_args(), device=torch.device("cuda", rank), world=world, rank=rank, total_steps=10,
+                         seed=0, dp_impl="nccl", fsdp=mode == "fsdp")
+            res[mode + "_loss"] = [float(tr.step_device(*batch)) for _ in range(3)]
+            if mode == "fsdp":
+                full = tr.fsdp.full_parameters()
+                names = {id(p): n for n, p in tr.model.named_parameters()}
+                res["fsdp_kernels"] = {names[id(p)]: t.cpu() for p, t in full.items()}
+                res["n_units"] = len(tr.fsdp.units)
+            else:
+                res["dp_params"] = {n: p.detach().float().cpu().clone() for n, p in tr.model.named_parameters()}
+            del tr
+            torch.cuda.empty_cache()
+        if rank == 0:
+            torch.save(res, out)
+    finally:
+        dist.destroy_process_group()
+
+
+@need2
+def test_fsdp_trains_like_replicated_data_parallelism(tmp_path):
+    """ZeRO-3 of the fused layers' kernels (gathered per layer, gradients reduce-scattered
+    during the backward, sharded AdamW) follows the replicated all-reduce trainer."""
+    out = str(tmp_path / "fsdp.pt")
+    mp.spawn(_fsdp_worker, args=(2, _port(), out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert r["n_units"] >= 2
+    for a, b in zip(r["dp_loss"], r["fsdp_loss"]):
+        assert abs(a - b) <= 2e-3 * abs(a), (r["dp_loss"], r["fsdp_loss"])
+    worst = 0.0
+    for n, t in r["fsdp_kernels"].items():
+        ref = r["dp_params"][n]
+        worst = max(worst, float((t - ref).norm() / ref.norm()))
+    assert worst < 1e-3, worst
