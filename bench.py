@@ -379,7 +379,7 @@ def main():
     Bm, nm = args.micro_bsz, args.n_messages
     trainer = Trainer(args, device=dev, world=world, rank=rank, total_steps=10_000, seed=0,
                       sharded=a.dp_impl == "nccl_sharded", dp_impl="fused" if a.dp_impl == "fused" else "nccl",
-                      tp=a.tp, accum_steps=a.accum_steps, fsdp=a.dp_impl == "fsdp")
+                      tp=a.tp, accum_steps=a.accum_steps, fsdp=a.dp_impl == "fsdp" and a.tp == 1)
     dp_world, dp_rank = trainer.world, trainer.rank          # with --tp the batch is split over dp only
     Bm = Bm * a.accum_steps
 
@@ -465,7 +465,8 @@ def main():
                        "parallelism": f"tp{a.tp}xdp{dp_world}" if a.tp > 1 else
                        (f"fsdp{world}" if trainer.fsdp is not None else f"dp{world}"),
                        "accum_steps": a.accum_steps,
-                       "grad_sync": (a.dp_impl if world > 1 else "none"),
+                       "grad_sync": ((a.dp_impl if (a.dp_impl != "fsdp" or a.tp == 1) else "nccl")
+                                     if world > 1 else "none"),
                        "l2": "working set (weights + ~90 GB activations per step) far above L2; no flush needed",
                        "vocab": vocab, "token_mode": tmode},
             "loss": float(loss), "gpu_launches": launches, "clocks": clk, "e2e": e2e,
