@@ -135,23 +135,93 @@ class BaseLOBEnv:
         return signed.sum(-1), -(signed * price).sum(-1)
 
 
-class MarketMakingEnv(BaseLOBEnv):
-    """One (or several) market makers quoting around the mid each step."""
+class _Quoting:
+    """Order management shared by the agents: each agent keeps up to K resting orders; a
+    step cancels those still resting and submits the new set (``envs/agents.py``)."""
+
+    def _init_live(self, n_agents: int, K: int):
+        self.live = torch.zeros(self.n, n_agents, K, 3, dtype=torch.long)   # (oid, side, price)
+        self.seq = 0
+
+    def _order_messages(self, a: int, tid: int, orders: torch.Tensor, market: Optional[torch.Tensor] = None,
+                        oid_block: int = 0) -> List[torch.Tensor]:
+        """Rows (n, 8) cancelling agent a's resting orders and placing ``orders`` (n, K, 3)
+        and the marketable ``market`` (n, 2) = (side, qty)."""
+        asks, bids = self.engine.sides()
+        in_b, in_a = torch.from_numpy(bids[:, :, 2]), torch.from_numpy(asks[:, :, 2])
+        rows = []
+        K = self.live.shape[2]
+        for k in range(K):
+            oid, side, price = self.live[:, a, k, 0], self.live[:, a, k, 1], self.live[:, a, k, 2]
+            resting = torch.where(side > 0, (in_b == oid[:, None]).any(1), (in_a == oid[:, None]).any(1))
+            # cancel only orders still resting: a failed lookup would fall back to another order
+            ok = resting & (oid != 0)
+            c = torch.stack([torch.full_like(oid, 3), torch.where(side > 0, 1, -1), torch.full_like(oid, 10**9),
+                             price, oid, torch.full_like(oid, tid), torch.zeros_like(oid), torch.zeros_like(oid)], -1)
+            c[~ok] = 0
+            rows.append(c)
+        self.seq += 1
+        self.live[:, a] = 0
+        for k in range(orders.shape[1]):
+            side, price, qty = orders[:, k, 0], orders[:, k, 1], orders[:, k, 2]
+            oid = torch.full_like(qty, AGENT_OID_BASE + (oid_block + a * K + k) * 10**6 + self.seq)
+            m = torch.stack([torch.ones_like(qty), side, qty, price, oid, torch.full_like(qty, tid),
+                             torch.zeros_like(qty), torch.zeros_like(qty)], -1)
+            ok = (qty > 0) & (side != 0)
+            m[~ok] = 0
+            rows.append(m)
+            if k < K:
+                self.live[:, a, k, 0] = torch.where(ok, oid, torch.zeros_like(oid))
+                self.live[:, a, k, 1] = side
+                self.live[:, a, k, 2] = price
+        if market is not None:
+            side, q = market[:, 0], market[:, 1]
+            # a marketable order executes against the opposite side: the message carries the resting
+            # side and an extreme limit (type 4: execution of visible liquidity)
+            far = torch.where(side > 0, torch.full_like(q, 10**9), torch.ones_like(q))
+            oid = torch.full_like(q, AGENT_OID_BASE + (oid_block + 90 + a) * 10**6 + self.seq)
+            m = torch.stack([torch.full_like(q, 4), -side, q, far, oid, torch.full_like(q, tid),
+                             torch.zeros_like(q), torch.zeros_like(q)], -1)
+            m[(q <= 0) | (side == 0)] = 0
+            rows.append(m)
+        return rows
+
+    def _state(self, inv: torch.Tensor) -> Dict[str, torch.Tensor]:
+        from .agents import touch
+        bb, ba, mid = touch(self.engine.l2(1).long().cpu(), self.tick)
+        return {"best_bid": bb, "best_ask": ba, "mid": mid, "inventory": inv,
+                "time_left": torch.full((self.n,), float(self.max_steps - self.t) / self.max_steps)}
+
+
+class MarketMakingEnv(_Quoting, BaseLOBEnv):
+    """One (or several) market makers.  ``action_space`` and ``reward_function`` select one
+    of the builders / rewards of ``envs/agents.py`` (the reference's config strings); the
+    default quotes one bid and one ask at mid -/+ an offset and is rewarded with the change
+    of mark-to-market PnL minus ``inventory_penalty`` per share held."""
 
     OFFSETS = (1, 2, 3, 5, 8)
 
-    def __init__(self, *a, quote_size: int = 100, inventory_penalty: float = 0.01, n_mm: int = 1, **kw):
+    def __init__(self, *a, quote_size: int = 100, inventory_penalty: float = 0.01, n_mm: int = 1,
+                 action_space: str = "offsets", reward_function: str = "pnl_inventory", inv_penalty: str = "linear",
+                 reference_price: str = "mid", eta: float = 0.5, gamma: float = 1.0, lam: float = 0.0,
+                 rebate_bps: float = 0.0, n_levels: int = 3, avst_k: float = 1.5, avst_var: float = 2.0, **kw):
+        from .agents import MM_ACTION_SPACES, MM_REWARDS
         super().__init__(*a, n_agents=n_mm, **kw)
+        if action_space not in MM_ACTION_SPACES or reward_function not in MM_REWARDS:
+            raise ValueError(f"action_space in {MM_ACTION_SPACES}, reward_function in {MM_REWARDS}")
         self.size, self.pen, self.n_mm = quote_size, inventory_penalty, n_mm
         self.tids = [1000 + i for i in range(n_mm)]
+        self.space, self.reward_fn, self.inv_pen_kind = action_space, reward_function, inv_penalty
+        self.ref_price, self.eta, self.gamma, self.lam, self.rebate = reference_price, eta, gamma, lam, rebate_bps
+        self.n_levels, self.avst_k, self.avst_var = n_levels, avst_k, avst_var
 
     def reset(self, idx=None):
         obs = super().reset(idx)
         z = lambda: torch.zeros(self.n, self.n_mm, dtype=torch.long)
         self.inv, self.cash = z(), z().double()
-        self.live = torch.zeros(self.n, self.n_mm, 2, 2, dtype=torch.long)   # [side][oid, price]
-        self.seq = 0
+        self._init_live(self.n_mm, 2 * self.n_levels if self.space == "fixed_prices" else 2)
         self.pnl_prev = torch.zeros(self.n, self.n_mm, dtype=torch.float64)
+        self.pv_prev = torch.zeros(self.n, self.n_mm, dtype=torch.float64)
         return self._obs(obs)
 
     def _obs(self, o):
@@ -159,97 +229,105 @@ class MarketMakingEnv(BaseLOBEnv):
         o["inventory"] = self.inv.clone()
         return o
 
-    def action_messages(self, actions: torch.Tensor, mid: torch.Tensor) -> torch.Tensor:
-        """actions (n, n_mm, 2) offset indices (bid, ask) -> (n, 4*n_mm, 8) messages."""
-        msgs = []
-        off = torch.tensor(self.OFFSETS)
-        asks, bids = self.engine.sides()
-        resting = {0: torch.from_numpy(bids[:, :, 2]), 1: torch.from_numpy(asks[:, :, 2])}
+    def action_messages(self, actions: torch.Tensor, mid: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """actions (n, n_mm[, d]) -> (n, m, 8) messages: every market maker's cancels, new
+        orders and marketable orders."""
+        from .agents import mm_orders
+        rows = []
         for a in range(self.n_mm):
-            tid = self.tids[a]
-            for side in (0, 1):        # 0 bid, 1 ask
-                oid, price = self.live[:, a, side, 0], self.live[:, a, side, 1]
-                # cancel only quotes still resting: a failed lookup would hit the engine's
-                # last-row fallback and disturb someone else's order
-                alive = (resting[side] == oid[:, None]).any(1) & (oid != 0)
-                oid = torch.where(alive, oid, torch.zeros_like(oid))
-                cancel = torch.stack([torch.full_like(oid, 3), torch.full_like(oid, 1 if side == 0 else -1),
-                                      torch.full_like(oid, 10**9), price, oid, torch.full_like(oid, tid),
-                                      torch.zeros_like(oid), torch.zeros_like(oid)], -1)
-                cancel[oid == 0] = 0                                  # nothing live yet: no-op row
-                msgs.append(cancel)
-            self.seq += 1
-            for side in (0, 1):
-                d = off[actions[:, a, side]] * self.tick
-                price = mid - d if side == 0 else mid + d
-                oid = torch.full_like(mid, AGENT_OID_BASE + (a * 2 + side) * 10**6 + self.seq)
-                new = torch.stack([torch.ones_like(mid), torch.full_like(mid, 1 if side == 0 else -1),
-                                   torch.full_like(mid, self.size), price, oid, torch.full_like(mid, tid),
-                                   torch.zeros_like(mid), torch.zeros_like(mid)], -1)
-                new[mid <= 0] = 0
-                msgs.append(new)
-                self.live[:, a, side, 0] = torch.where(mid > 0, oid, torch.zeros_like(oid))
-                self.live[:, a, side, 1] = price
-        return torch.stack(msgs, 1)
+            st = self._state(self.inv[:, a])
+            if mid is not None:
+                st["mid"] = mid
+            orders, market = mm_orders(self.space, actions[:, a], st, self.size, self.tick, self.n_levels,
+                                       self.avst_k, self.avst_var)
+            rows += self._order_messages(a, self.tids[a], orders,
+                                         market if self.space == "directional_trading" else None)
+        return torch.stack(rows, 1)
+
+    def _rewards(self, trades, mid0, obs):
+        from .agents import agent_trades, inventory_penalty, mm_reward, touch
+        bb, ba, _ = touch(obs["l2"], self.tick)
+        rew = torch.zeros(self.n, self.n_mm, dtype=torch.float64)
+        for a, tid in enumerate(self.tids):
+            bq, bv, sq, sv = agent_trades(trades, tid)
+            inv_prev = self.inv[:, a].clone()
+            self.inv[:, a] += bq - sq
+            self.cash[:, a] += (sv - bv).double()
+            if self.reward_fn == "pnl_inventory":
+                pnl = self.cash[:, a] + self.inv[:, a].double() * obs["mid"].double()
+                rew[:, a] = (pnl - self.pnl_prev[:, a]) / self.tick - self.pen * self.inv[:, a].double().abs()
+                self.pnl_prev[:, a] = pnl
+                continue
+            r, pv = mm_reward(self.reward_fn, buy_q=bq, buy_v=bv, sell_q=sq, sell_v=sv, inv_prev=inv_prev,
+                              inv=self.inv[:, a], cash=self.cash[:, a], mid0=mid0, mid1=obs["mid"], best_bid=bb,
+                              best_ask=ba, tick=self.tick, reference_price=self.ref_price, eta=self.eta,
+                              gamma=self.gamma, lam=self.lam, rebate_bps=self.rebate, pv_prev=self.pv_prev[:, a])
+            self.pv_prev[:, a] = pv
+            rew[:, a] = r + inventory_penalty(self.inv_pen_kind, self.inv[:, a], self.pen, self.size)
+        return rew
 
     def step(self, actions: torch.Tensor):
         obs0 = self.observe()
         trades, _ = self.step_messages(self.action_messages(actions, obs0["mid"]))
         obs = self.observe()
-        rew = torch.zeros(self.n, self.n_mm, dtype=torch.float64)
-        for a, tid in enumerate(self.tids):
-            q, c = self.fills(trades, tid)
-            self.inv[:, a] += q
-            self.cash[:, a] += c.double()
-            pnl = self.cash[:, a] + self.inv[:, a].double() * obs["mid"].double()
-            rew[:, a] = (pnl - self.pnl_prev[:, a]) / self.tick - self.pen * self.inv[:, a].double().abs()
-            self.pnl_prev[:, a] = pnl
+        rew = self._rewards(trades, obs0["mid"], obs)          # updates inventory and cash first
         return self._obs(obs), rew, self.done
 
 
-class ExecutionEnv(BaseLOBEnv):
-    """Buy (side=1) or sell (side=0) ``target`` shares before the episode ends."""
+class ExecutionEnv(_Quoting, BaseLOBEnv):
+    """Buy (side=1) or sell (side=0) ``target`` shares before the episode ends.
+    ``action_space`` / ``reward_function`` pick an execution builder / reward of
+    ``envs/agents.py``; the default sends a marketable child order of a size from a table
+    and is rewarded with the negative shortfall against the arrival mid.  The last step
+    sweeps what is left."""
 
     SIZES = (0, 50, 100, 200, 400)
 
-    def __init__(self, *a, target: int = 1000, side: int = 1, **kw):
+    def __init__(self, *a, target: int = 1000, side: int = 1, action_space: str = "sizes",
+                 reward_function: str = "slippage", clip: int = 100, lam: float = 1.0, **kw):
+        from .agents import EXEC_ACTION_SPACES, EXEC_REWARDS
         super().__init__(*a, n_agents=1, **kw)
+        if action_space not in EXEC_ACTION_SPACES or reward_function not in EXEC_REWARDS:
+            raise ValueError(f"action_space in {EXEC_ACTION_SPACES}, reward_function in {EXEC_REWARDS}")
         self.target, self.side, self.tid = target, side, 2000
+        self.space, self.reward_fn, self.clip, self.lam = action_space, reward_function, clip, lam
 
     def reset(self, idx=None):
         o = super().reset(idx)
         self.done_qty = torch.zeros(self.n, dtype=torch.long)
         self.cash = torch.zeros(self.n, dtype=torch.float64)
         self.arrival = o["mid"].clone()
-        self.seq = 0
+        self._init_live(1, 3)
         o["remaining"] = torch.full((self.n,), self.target)
         return o
 
     def step(self, actions: torch.Tensor):
-        """actions (n,) size indices; the last step sweeps what is left."""
-        rem = self.target - self.done_qty
-        q = torch.tensor(self.SIZES)[actions].clamp(max=rem)
+        """actions: (n,) indices, or (n, 4) sizes for ``fixed_prices``."""
+        from .agents import agent_trades, exec_orders, exec_reward
+        sell = self.side != 1
+        rem = (self.target - self.done_qty).clamp(min=0)
+        st = self._state(self.done_qty)
+        steps_left = self.max_steps - self.t
+        orders, take = exec_orders(self.space, actions, st, rem, self.clip, steps_left, sell, self.tick)
         if self.t == self.max_steps - 1:
-            q = rem
-        self.seq += 1
-        sgn = 1 if self.side == 1 else -1
-        far = torch.full_like(q, 10**9 if self.side == 1 else 1)
-        oid = torch.full_like(q, AGENT_OID_BASE + 50 * 10**6 + self.seq)
-        m = torch.stack([torch.full_like(q, 4), torch.full_like(q, -sgn), q, far, oid, torch.full_like(q, self.tid),
-                         torch.zeros_like(q), torch.zeros_like(q)], -1)[:, None]
-        # type 4 is the execution of a resting order on the *opposite* side: side flag is the
-        # resting side, so a buy execution hits the ask side (-1)
-        m[q <= 0] = 0
-        trades, _ = self.step_messages(m)
-        filled, cash = self.fills(trades, self.tid)
-        filled = filled * sgn
+            take = rem                                    # the last step sweeps what is left
+            orders = torch.zeros_like(orders)
+        sgn = -1 if sell else 1
+        market = torch.stack([torch.full_like(take, sgn), take], -1)
+        trades, _ = self.step_messages(torch.stack(self._order_messages(0, self.tid, orders, market, 50), 1))
+        bq, bv, sq, sv = agent_trades(trades, self.tid)
+        filled, value = (sq, sv) if sell else (bq, bv)
         self.done_qty += filled
-        self.cash += cash.double()
+        self.cash += (sv - bv).double()
+        # the rest of the market in this step (its VWAP for the vwap reward)
+        valid = trades[..., 0] >= 0
+        mine = (trades[..., 6] == self.tid) | (trades[..., 7] == self.tid)
+        other = valid & ~mine
+        oq = torch.where(other, trades[..., 1].abs(), torch.zeros_like(trades[..., 1])).long()
+        mq, mv = oq.sum(-1), (oq * trades[..., 0].long()).sum(-1)
         o = self.observe()
-        # shortfall vs arrival mid, in ticks per share
-        avg_px = (-self.cash * sgn) / self.done_qty.clamp(min=1).double()
-        short = (avg_px - self.arrival.double()) * sgn / self.tick
-        rew = torch.where(filled > 0, -short * filled.double() / self.target, torch.zeros_like(short))
+        rew = exec_reward(self.reward_fn, filled=filled, value=value, market_q=mq, market_v=mv,
+                          arrival=self.arrival, target=self.target, sell=sell, tick=self.tick, lam=self.lam)
         o["remaining"] = self.target - self.done_qty
         return o, rew, self.done
 
@@ -274,14 +352,7 @@ class MultiAgentEnv(MarketMakingEnv):
             msgs = torch.cat([msgs, m], 1)
         trades, _ = self.step_messages(msgs)
         obs = self.observe()
-        rew = torch.zeros(self.n, self.n_mm, dtype=torch.float64)
-        for a, tid in enumerate(self.tids):
-            q, c = self.fills(trades, tid)
-            self.inv[:, a] += q
-            self.cash[:, a] += c.double()
-            pnl = self.cash[:, a] + self.inv[:, a].double() * obs["mid"].double()
-            rew[:, a] = (pnl - self.pnl_prev[:, a]) / self.tick - self.pen * self.inv[:, a].double().abs()
-            self.pnl_prev[:, a] = pnl
+        rew = self._rewards(trades, obs0["mid"], obs)
         return self._obs(obs), rew, self.done
 
 
