@@ -53,7 +53,7 @@ def parse():
     p.add_argument("--books", type=int, default=512, help="gen: books per GPU")
     p.add_argument("--ctx_msgs", type=int, default=500, help="gen: conditioning messages per book")
     p.add_argument("--no_graphs", action="store_true")
-    p.add_argument("--dp_impl", choices=["fused", "nccl", "nccl_sharded", "fsdp"], default="fsdp",
+    p.add_argument("--dp_impl", choices=["fused", "nccl", "nccl_sharded", "fsdp", "fsdp_ag"], default="fsdp",
                    help="N>1 gradient sync: fused peer-memory RS+AdamW+AG kernel, NCCL all-reduce / RS+AG, or "
                         "FSDP (ZeRO-3 of the fused layers' kernels, parallel/fsdp.py)")
     p.add_argument("--tp", type=int, default=1,
@@ -379,7 +379,8 @@ def main():
     Bm, nm = args.micro_bsz, args.n_messages
     trainer = Trainer(args, device=dev, world=world, rank=rank, total_steps=10_000, seed=0,
                       sharded=a.dp_impl == "nccl_sharded", dp_impl="fused" if a.dp_impl == "fused" else "nccl",
-                      tp=a.tp, accum_steps=a.accum_steps, fsdp=a.dp_impl == "fsdp" and a.tp == 1)
+                      tp=a.tp, accum_steps=a.accum_steps, fsdp=a.dp_impl in ("fsdp", "fsdp_ag") and a.tp == 1,
+                      fsdp_fused_ag=a.dp_impl == "fsdp_ag")
     dp_world, dp_rank = trainer.world, trainer.rank          # with --tp the batch is split over dp only
     Bm = Bm * a.accum_steps
 
@@ -463,9 +464,10 @@ def main():
                                 f"{nml}+{nbpre}+{nbpost}+{nl} layers)",
                        "global_batch": Bm * dp_world, "seq_len": L,
                        "parallelism": f"tp{a.tp}xdp{dp_world}" if a.tp > 1 else
-                       (f"fsdp{world}" if trainer.fsdp is not None else f"dp{world}"),
+                       ((f"fsdp{world}" + ("_fused_ag" if trainer.fsdp.fused_ag else "")) if trainer.fsdp is not None
+                        else f"dp{world}"),
                        "accum_steps": a.accum_steps,
-                       "grad_sync": ((a.dp_impl if (a.dp_impl != "fsdp" or a.tp == 1) else "nccl")
+                       "grad_sync": ((a.dp_impl if (not a.dp_impl.startswith("fsdp") or a.tp == 1) else "nccl")
                                      if world > 1 else "none"),
                        "l2": "working set (weights + ~90 GB activations per step) far above L2; no flush needed",
                        "vocab": vocab, "token_mode": tmode},

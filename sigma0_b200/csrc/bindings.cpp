@@ -190,6 +190,47 @@ std::vector<at::Tensor> gemm_gelu_fwd(const at::Tensor& x, const at::Tensor& w) 
   return {o, g};
 }
 
+// y = x . W with W's rank row blocks all-gathered inside the GEMM (FSDP's first projection):
+// `wfull` is this GPU's [K, N] gathered buffer (filled by the kernel), `src` the address of
+// every rank's [K / world, N] row block (peer addresses), `ready` every rank's shard-version
+// flag (peer addresses), `counters` `world` zeroed ints on this GPU.
+at::Tensor gemm_ag(const at::Tensor& x, const at::Tensor& wfull, std::vector<int64_t> src, std::vector<int64_t> ready,
+                   const at::Tensor& counters, int64_t rank, int64_t seq, int64_t spin) {
+  TORCH_CHECK(x.is_cuda() && wfull.is_cuda() && x.scalar_type() == at::kBFloat16 && wfull.scalar_type() == at::kBFloat16,
+              "gemm_ag: bf16 CUDA operands");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && wfull.dim() == 2 && wfull.is_contiguous() && x.size(1) == wfull.size(0),
+              "gemm_ag: x [M, K] with unit column stride, wfull contiguous [K, N]");
+  const int64_t world = (int64_t)src.size();
+  TORCH_CHECK(world >= 2 && world <= 8 && (int64_t)ready.size() == world && counters.numel() >= world &&
+                  counters.scalar_type() == at::kInt,
+              "gemm_ag: 2..8 ranks, one source, flag and counter each");
+  const int64_t M = x.size(0), K = x.size(1), N = wfull.size(1);
+  TORCH_CHECK(K % (world * 64) == 0 && (x.stride(0) * 2) % 16 == 0 && (N * 2) % 16 == 0 && N % 8 == 0,
+              "gemm_ag: K a multiple of 64 x world, 16-byte rows");
+  auto y = at::empty({M, N}, x.options());
+  c10::cuda::CUDAGuard guard(x.device());
+  counters.zero_();
+  GemmArgs a{};
+  a.A = x.data_ptr();
+  a.B = wfull.data_ptr();
+  a.C = y.data_ptr();
+  a.M = (int)M; a.N = (int)N; a.K = (int)K;
+  a.lda = x.stride(0); a.ldb = N; a.ldc = N;
+  a.c_rows = (int)M; a.c_cols = (int)N;
+  a.a_mn = 0; a.b_mn = 1; a.out_mode = 0; a.split_k = 1;
+  a.status = gemm_status(x).data_ptr<int>();
+  a.ag_world = (int)world; a.ag_rank = (int)rank; a.ag_rows = (int)(K / world); a.ag_seq = (int)seq;
+  for (int64_t r = 0; r < world; ++r) {
+    a.ag_src[r] = reinterpret_cast<const void*>(src[r]);
+    a.ag_ready[r] = reinterpret_cast<const int*>(ready[r]);
+  }
+  a.ag_count = counters.data_ptr<int>();
+  a.ag_spin = spin;
+  const int e = gemm_tc_launch(a, num_sms(x), stream());
+  TORCH_CHECK(e == 0, "gemm_ag launch failed: ", e);
+  return y;
+}
+
 // SSD implementation: 1 the tcgen05 chunk walkers, 0 the chunk-parallel mma.sync kernels,
 // -1 (default) by occupancy: the walkers run one CTA per (sequence, head), so they are used when
 // there are at least as many (sequence, head) pairs as SMs; smaller batches (a single sequence of
@@ -1284,6 +1325,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b_mn"), py::arg("out_mode") = 0, py::arg("out") = c10::nullopt, py::arg("split_k") = 1);  // split_k 0: auto
   m.def("gemm_status", [](at::Tensor like) { return gemm_status(like); }, "status word of the tcgen05 GEMM");
   m.def("gemm_gelu_fwd", &gemm_gelu_fwd, "o = x . w and g = gelu(o) in one tcgen05 GEMM");
+  m.def("gemm_ag", &gemm_ag, "y = x . W with W's row blocks all-gathered from the ranks inside the tcgen05 GEMM",
+        py::arg("x"), py::arg("wfull"), py::arg("src"), py::arg("ready"), py::arg("counters"), py::arg("rank"),
+        py::arg("seq"), py::arg("spin"));
   m.def("gemm_use_pair", [](bool on) { gemm_tc_set_pair(on ? 1 : 0); },
         "two-SM (cta_group::2) GEMM tiles (default) or one-SM tiles");
   m.def("m3_tc_status", [](at::Tensor like) { return m3_status(like); },

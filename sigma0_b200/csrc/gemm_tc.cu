@@ -306,6 +306,58 @@ constexpr int STAGE2 = 2 * H_BYTES;                            // 32 KB
 constexpr size_t SMEM2 = 1024 + (size_t)NS2 * STAGE2 + (size_t)EPI_WARPS2 * 2 * EPI_BUF;
 static_assert(SMEM2 <= 232448, "shared memory over the per-CTA limit");
 
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Copy lanes (producer warp lanes 1..31 of every CTA) of the fused all-gather: this CTA's slice
+// of every rank's row block of B, own block first, each block counted once the slice has landed.
+__device__ void ag_copy(const GemmArgs& a, int lane) {
+  const int l = lane - 1, nl = 31;
+  bool ok = true;
+  for (int i = 0; i < a.ag_world; ++i) {
+    const int r = (a.ag_rank + i) % a.ag_world;
+    if (r != a.ag_rank && ok) {
+      long long it = 0;
+      while (ld_acquire_sys(a.ag_ready[r]) < a.ag_seq) {
+        if (++it > a.ag_spin) {
+          ok = false;
+          atomicExch(a.status, 3);            // a peer's shard never became current
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+    if (ok) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.ag_src[r]);
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(a.B)) +
+                                            (size_t)r * a.ag_rows * a.ldb);
+      const long n16 = (long)a.ag_rows * a.ldb / 8;
+      const long per = (n16 + gridDim.x - 1) / gridDim.x;
+      const long lo = (long)blockIdx.x * per, hi = lo + per < n16 ? lo + per : n16;
+      long j = lo + l;
+      for (; j + 3 * nl < hi; j += 4 * nl) {            // four loads in flight per lane
+        const uint4 v0 = src[j], v1 = src[j + nl], v2 = src[j + 2 * nl], v3 = src[j + 3 * nl];
+        dst[j] = v0;
+        dst[j + nl] = v1;
+        dst[j + 2 * nl] = v2;
+        dst[j + 3 * nl] = v3;
+      }
+      for (; j < hi; j += nl) dst[j] = src[j];
+    }
+    __threadfence();                            // the slice is visible GPU-wide before it is counted
+    __syncwarp(0xFFFFFFFEu);
+    if (l == 0) atomicAdd(a.ag_count + r, 1);   // counted even after a timeout: nobody waits forever
+  }
+}
+
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -388,7 +440,13 @@ __global__ void __launch_bounds__(NT2, 1)
   const long pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   bool ok = true;
   if (warp == PROD_WARP2) {
+    const bool ag = a.ag_world > 1;
+    if (ag && lane > 0) ag_copy(a, lane);
     if (lane == 0) {
+      // fused all-gather: k-blocks start at this rank's own row block (copied locally first);
+      // a block of another rank is loaded once every CTA has copied its slice of it
+      const int kb_rot = ag ? a.ag_rank * (a.ag_rows / BK) : 0;
+      uint32_t ready = 0;
       long g = 0;
       for (long u = pair; u < units && ok; u += npairs) {
         const long t = u / a.split_k;
@@ -396,11 +454,29 @@ __global__ void __launch_bounds__(NT2, 1)
         const int tm = (int)(t / tiles_n), tn = (int)(t % tiles_n);
         const int kb0 = (int)((long)sk * nkb / a.split_k), kb1 = (int)((long)(sk + 1) * nkb / a.split_k);
         const int ra = tm * 256 + 128 * (int)rank, rb = tn * 256 + 128 * (int)rank;
-        for (int kb = kb0; kb < kb1; ++kb, ++g) {
+        for (int kbi = kb0; kbi < kb1; ++kbi, ++g) {
+          const int kb = ag ? (kbi + kb_rot) % nkb : kbi;
           const int s = (int)(g % NS2);
           if (g >= NS2 && !tc::mbar_wait(&empty[s], (uint32_t)(((g / NS2) - 1) & 1))) {
             ok = false;
             break;
+          }
+          if (ag) {
+            const int owner = kb * BK / a.ag_rows;
+            if (!(ready >> owner & 1u)) {
+              long long it = 0;
+              while (ld_acquire_gpu(a.ag_count + owner) < (int)gridDim.x) {
+                if (++it > a.ag_spin) {
+                  ok = false;
+                  break;
+                }
+                __nanosleep(64);
+              }
+              if (!ok) break;
+              // generic-proxy stores (the copy lanes of every CTA) -> this thread's TMA reads
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+              ready |= 1u << owner;
+            }
           }
           unsigned char* sA = base + (size_t)s * STAGE2;
           unsigned char* sB = sA + H_BYTES;
@@ -633,6 +709,13 @@ int gemm_tc_launch(const GemmArgs& a_in, int sms, cudaStream_t st) {
   if ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B) | reinterpret_cast<uintptr_t>(a.C)) % 16)
     return -3;
   const int ce = (a.out_mode == 1 || a.out_mode == 2) ? 4 : 2;
+  if (a.ag_world > 1) {       // fused all-gather: two-SM kernel, MN-major B rows split in 64-row blocks
+    if (!g_gemm_pair || a.a_mn || !a.b_mn || a.split_k != 1 || a.ag_world > 8 || a.ag_rows % BK ||
+        (long)a.ag_rows * a.ag_world != a.K || a.ldb != a.N || a.ag_count == nullptr)
+      return -10;
+    for (int r = 0; r < a.ag_world; ++r)
+      if (reinterpret_cast<uintptr_t>(a.ag_src[r]) % 16 || a.ag_ready[r] == nullptr) return -11;
+  }
   if (a.out_mode == 3) {      // fused epilogue: whole 64-column chunks, an aligned second output
     if (a.c_cols % 64) return -8;
     if (a.out_mode == 3 && (reinterpret_cast<uintptr_t>(a.C2) % 16 || (a.ldc2 * 2) % 16)) return -9;

@@ -214,6 +214,16 @@ struct GemmArgs {
   // dimension ldc2)
   void* C2;
   long ldc2;
+  // fused all-gather of B (ag_world > 1; two-SM kernel, B MN-major): B is this GPU's full
+  // [K, N] buffer (leading dimension ldb == N), whose row block r (ag_rows rows) is copied in
+  // by the kernel from ag_src[r] -- rank r's shard, a peer address for r != ag_rank -- once
+  // ag_ready[r] (rank r's flag, a peer address) has reached ag_seq; ag_count (ag_world local
+  // ints, zeroed before the launch) counts the CTAs that finished each block
+  int ag_world, ag_rank, ag_rows, ag_seq;
+  const void* ag_src[8];
+  const int* ag_ready[8];
+  int* ag_count;
+  long long ag_spin;
 };
 int gemm_tc_launch(const GemmArgs& a, int sms, cudaStream_t st);
 void gemm_tc_set_pair(int on);   // 1 (default): two-SM tcgen05 tiles, 0: one-SM tiles

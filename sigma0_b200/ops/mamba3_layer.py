@@ -64,7 +64,8 @@ class _Mamba3Core:
         if Hp != H:   # odd widths (the 503-wide book layers): pad K so the GEMM rows are 16-byte aligned
             xn = F.pad(xn, (0, Hp - H))
             w_in = F.pad(w_in, (0, 0, 0, Hp - H))
-        proj = G.proj(xn, w_in)                                       # [T, ldp]
+        ag = getattr(m.in_proj.kernel, "_s0_ag", None)      # FSDP: in_proj gathered inside its GEMM
+        proj = ag(xn) if (ag is not None and Hp == H and ldp == d.d_in_proj) else G.proj(xn, w_in)   # [T, ldp]
         out = C.m3_fwd(proj, B, L, d.n_heads, m.B_norm.scale, m.C_norm.scale, m.dt_bias, m.B_bias,
                        m.C_bias, m.D, m.A_floor, m.B_norm.eps, return_prep=SAVE_STATES)
         y, states = out[0], out[1]

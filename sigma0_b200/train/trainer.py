@@ -43,7 +43,7 @@ class Trainer:
                  group=None, total_steps: int = 1000, seed: int = 0, sharded: bool = False,
                  accum_steps: int = 1, grad_wire_dtype: str = "float32", dp_impl: str = "nccl",
                  context_parallel: bool = False, tp: int = 1, hierarchical: bool = False,
-                 gpus_per_node: Optional[int] = None, fsdp: bool = False):
+                 gpus_per_node: Optional[int] = None, fsdp: bool = False, fsdp_fused_ag: bool = False):
         self.args = args
         self.device = device or torch.device("cuda" if torch.cuda.is_available() else "cpu")
         from ..encoding.tok1 import encoding_mode
@@ -105,7 +105,7 @@ class Trainer:
             from ..parallel.fsdp import FSDP
             self.fsdp = FSDP(self.model, world, rank, group, lr=lr,
                              weight_decay=float(getattr(args, "weight_decay", 0.05)),
-                             wire_bf16=grad_wire_dtype == "bfloat16")
+                             wire_bf16=grad_wire_dtype == "bfloat16", fused_ag=fsdp_fused_ag)
         opt_cls = FlatAdam
         extra_opt = {}
         if str(getattr(args, "opt_config", "standard")) == "muon":

@@ -65,9 +65,9 @@ def _worker(rank, world, port, out):
         for u in fs.units:
             shards = [torch.zeros_like(u.grad) for _ in range(world)]
             dist.all_gather(shards, u.grad)
-            flat = torch.cat(shards)
-            for p, o in zip(u.params, u.offsets):
-                full_g[id(p)] = flat[o:o + p.numel()].view(p.shape)
+            for k, p in enumerate(u.params):
+                n, so = p.numel() // world, u.soffsets[k]           # row blocks, rank order = row order
+                full_g[id(p)] = torch.cat([sh[so:so + n] for sh in shards]).view(p.shape)
         res["grad_ok"] = all(torch.allclose(full_g[k], g[k], rtol=1e-5, atol=1e-5) for k in g)
         # 3. one sharded AdamW step against the full-tensor update (averaged gradient)
         total = fs.grad_sumsq()

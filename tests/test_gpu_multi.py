@@ -250,10 +250,14 @@ def _fsdp_worker(rank, world, port, out):
         from sigma0_b200.train.trainer import Trainer
         batch = _batch(rank)
         res = {}
-        for mode in ("dp", "fsdp"):
+        for mode in ("dp", "fsdp", "fsdp_ag"):
             tr = Trainer(_args(), device=torch.device("cuda", rank), world=world, rank=rank, total_steps=10,
-                         seed=0, dp_impl="nccl", fsdp=mode == "fsdp")
+                         seed=0, dp_impl="nccl", fsdp=mode != "dp", fsdp_fused_ag=mode == "fsdp_ag")
             res[mode + "_loss"] = [float(tr.step_device(*batch)) for _ in range(3)]
+            if mode == "fsdp_ag":
+                from sigma0_b200.ops import gemm
+                res["ag_status"] = gemm.status(batch[0])
+                res["ag_used"] = tr.fsdp.fused_ag
             if mode == "fsdp":
                 full = tr.fsdp.full_parameters()
                 names = {id(p): n for n, p in tr.model.named_parameters()}
@@ -279,6 +283,10 @@ def test_fsdp_trains_like_replicated_data_parallelism(tmp_path):
     assert r["n_units"] >= 2
     for a, b in zip(r["dp_loss"], r["fsdp_loss"]):
         assert abs(a - b) <= 2e-3 * abs(a), (r["dp_loss"], r["fsdp_loss"])
+    # in_proj all-gathered inside its GEMM over peer memory: the same training
+    assert r["ag_used"] and r["ag_status"] == 0
+    for a, b in zip(r["fsdp_loss"], r["fsdp_ag_loss"]):
+        assert abs(a - b) <= 2e-3 * abs(a), (r["fsdp_loss"], r["fsdp_ag_loss"])
     worst = 0.0
     for n, t in r["fsdp_kernels"].items():
         ref = r["dp_params"][n]
