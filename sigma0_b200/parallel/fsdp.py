@@ -149,8 +149,9 @@ class FSDP:
         if self.fused_ag:
             import torch.distributed._symmetric_memory as symm
             torch.cuda.synchronize(dev)
-            h = symm.rendezvous(self._symm_bf16, group)
-            hr = symm.rendezvous(self._ready, group)
+            g = group if group is not None else dist.group.WORLD
+            h = symm.rendezvous(self._symm_bf16, g)
+            hr = symm.rendezvous(self._ready, g)
             base = int(h.buffer_ptrs[h.rank])
             self._peer_bf16 = [int(ptr) for ptr in h.buffer_ptrs]
             self._peer_ready = [int(ptr) + 4 * r for r, ptr in enumerate(hr.buffer_ptrs)]
