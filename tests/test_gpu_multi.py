@@ -258,10 +258,10 @@ def _fsdp_worker(rank, world, port, out):
                 from sigma0_b200.ops import gemm
                 res["ag_status"] = gemm.status(batch[0])
                 res["ag_used"] = tr.fsdp.fused_ag
-            if mode == "fsdp":
+            if mode != "dp":
                 full = tr.fsdp.full_parameters()
                 names = {id(p): n for n, p in tr.model.named_parameters()}
-                res["fsdp_kernels"] = {names[id(p)]: t.cpu() for p, t in full.items()}
+                res[mode + "_kernels"] = {names[id(p)]: t.cpu() for p, t in full.items()}
                 res["n_units"] = len(tr.fsdp.units)
             else:
                 res["dp_params"] = {n: p.detach().float().cpu().clone() for n, p in tr.model.named_parameters()}
@@ -287,8 +287,9 @@ def test_fsdp_trains_like_replicated_data_parallelism(tmp_path):
     assert r["ag_used"] and r["ag_status"] == 0
     for a, b in zip(r["fsdp_loss"], r["fsdp_ag_loss"]):
         assert abs(a - b) <= 2e-3 * abs(a), (r["fsdp_loss"], r["fsdp_ag_loss"])
-    worst = 0.0
-    for n, t in r["fsdp_kernels"].items():
-        ref = r["dp_params"][n]
-        worst = max(worst, float((t - ref).norm() / ref.norm()))
-    assert worst < 1e-3, worst
+    for mode in ("fsdp", "fsdp_ag"):
+        worst = 0.0
+        for n, t in r[mode + "_kernels"].items():
+            ref = r["dp_params"][n]
+            worst = max(worst, float((t - ref).norm() / ref.norm()))
+        assert worst < 1e-3, (mode, worst)
