@@ -287,9 +287,36 @@ def test_fsdp_trains_like_replicated_data_parallelism(tmp_path):
     assert r["ag_used"] and r["ag_status"] == 0
     for a, b in zip(r["fsdp_loss"], r["fsdp_ag_loss"]):
         assert abs(a - b) <= 2e-3 * abs(a), (r["fsdp_loss"], r["fsdp_ag_loss"])
-    for mode in ("fsdp", "fsdp_ag"):
+    # the fused gather starts every rank's in_proj GEMM at its own row block: the same products
+    # summed in another order, so bf16 rounding (and Adam's normalised first steps, ~lr per element
+    # where gradients are near zero) separate the runs slightly more than the plain FSDP run
+    for mode, tol in (("fsdp", 1e-3), ("fsdp_ag", 1e-2)):
         worst = 0.0
         for n, t in r[mode + "_kernels"].items():
             ref = r["dp_params"][n]
             worst = max(worst, float((t - ref).norm() / ref.norm()))
-        assert worst < 1e-3, (mode, worst)
+        assert worst < tol, (mode, worst)
+
+
+def _ag_gemm_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    import contextlib
+    import io
+    from sigma0_b200.eval import ag_gemm_bench
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        ag_gemm_bench.main(["--tokens", "4096", "--iters", "2", "--warmup", "1"])
+    if rank == 0:
+        import json
+        torch.save(json.loads(buf.getvalue().strip().splitlines()[-1]), out)
+
+
+@need2
+def test_fused_all_gather_gemm_gathers_exactly(tmp_path):
+    """The in-kernel all-gather leaves every rank's row block, bit for bit, in the local buffer,
+    and the product matches an fp32 reference."""
+    out = str(tmp_path / "ag.pt")
+    mp.spawn(_ag_gemm_worker, args=(2, _port(), out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert r["gathered_exact"] and r["status"] == 0 and r["rel_err"] < 1e-2
