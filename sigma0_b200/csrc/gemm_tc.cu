@@ -296,11 +296,11 @@ __global__ void __launch_bounds__(NT, 1)
 // accumulator-full barriers (CTA mask 0b11), and the peer's epilogue releases the accumulator
 // with remote arrivals on the leader's barrier.
 // ---------------------------------------------------------------------------------------------
-// 6 warps: 0-3 epilogue (warp w reads TMEM lane quadrant w), 4 MMA issue (leader CTA only),
-// 5 TMA loads.  Six 32 KB stages: the pipeline depth is what the mainloop is sensitive to (five
+// 7 warps: 0-3 epilogue (warp w reads TMEM lane quadrant w), 4 MMA issue (leader CTA only),
+// 5 TMA loads, 6 the fused all-gather's copies (idle otherwise).  Six 32 KB stages: the pipeline depth is what the mainloop is sensitive to (five
 // stages measured 2-5% slower; eight epilogue warps gained nothing).
 constexpr int NS2 = 6;
-constexpr int NT2 = 192, EPI_WARPS2 = 4, MMA_WARP2 = 4, PROD_WARP2 = 5;
+constexpr int NT2 = 224, EPI_WARPS2 = 4, MMA_WARP2 = 4, PROD_WARP2 = 5, COPY_WARP2 = 6;
 constexpr int H_BYTES = 128 * BK * 2;                          // one CTA's half of A or B per stage
 constexpr int STAGE2 = 2 * H_BYTES;                            // 32 KB
 constexpr size_t SMEM2 = 1024 + (size_t)NS2 * STAGE2 + (size_t)EPI_WARPS2 * 2 * EPI_BUF;
@@ -317,10 +317,11 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   return v;
 }
 
-// Copy lanes (producer warp lanes 1..31 of every CTA) of the fused all-gather: this CTA's slice
-// of every rank's row block of B, own block first, each block counted once the slice has landed.
+// The copy warp of the fused all-gather (warp 6 of every CTA): this CTA's slice of every rank's
+// row block of B, own block first, eight 16-byte loads in flight per lane; each block is counted
+// once the slice has landed.
 __device__ void ag_copy(const GemmArgs& a, int lane) {
-  const int l = lane - 1, nl = 31;
+  constexpr int nl = 32;
   bool ok = true;
   for (int i = 0; i < a.ag_world; ++i) {
     const int r = (a.ag_rank + i) % a.ag_world;
@@ -335,6 +336,7 @@ __device__ void ag_copy(const GemmArgs& a, int lane) {
         __nanosleep(128);
       }
     }
+    ok = __all_sync(0xFFFFFFFFu, ok);
     if (ok) {
       const uint4* src = reinterpret_cast<const uint4*>(a.ag_src[r]);
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(a.B)) +
@@ -342,19 +344,19 @@ __device__ void ag_copy(const GemmArgs& a, int lane) {
       const long n16 = (long)a.ag_rows * a.ldb / 8;
       const long per = (n16 + gridDim.x - 1) / gridDim.x;
       const long lo = (long)blockIdx.x * per, hi = lo + per < n16 ? lo + per : n16;
-      long j = lo + l;
-      for (; j + 3 * nl < hi; j += 4 * nl) {            // four loads in flight per lane
-        const uint4 v0 = src[j], v1 = src[j + nl], v2 = src[j + 2 * nl], v3 = src[j + 3 * nl];
-        dst[j] = v0;
-        dst[j + nl] = v1;
-        dst[j + 2 * nl] = v2;
-        dst[j + 3 * nl] = v3;
+      long j = lo + lane;
+      for (; j + 7 * nl < hi; j += 8 * nl) {
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = src[j + k * nl];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) dst[j + k * nl] = v[k];
       }
       for (; j < hi; j += nl) dst[j] = src[j];
     }
     __threadfence();                            // the slice is visible GPU-wide before it is counted
-    __syncwarp(0xFFFFFFFEu);
-    if (l == 0) atomicAdd(a.ag_count + r, 1);   // counted even after a timeout: nobody waits forever
+    __syncwarp();
+    if (lane == 0) atomicAdd(a.ag_count + r, 1);   // counted even after a timeout: nobody waits forever
   }
 }
 
@@ -439,9 +441,10 @@ __global__ void __launch_bounds__(NT2, 1)
   const long units = (long)tiles_m * tiles_n * a.split_k;
   const long pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   bool ok = true;
-  if (warp == PROD_WARP2) {
+  if (warp == COPY_WARP2) {
+    if (a.ag_world > 1) ag_copy(a, lane);
+  } else if (warp == PROD_WARP2) {
     const bool ag = a.ag_world > 1;
-    if (ag && lane > 0) ag_copy(a, lane);
     if (lane == 0) {
       // fused all-gather: k-blocks start at this rank's own row block (copied locally first);
       // a block of another rank is loaded once every CTA has copied its slice of it
