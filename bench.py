@@ -59,6 +59,8 @@ def parse():
     p.add_argument("--tp", type=int, default=1,
                    help="tensor-parallel size (heads split over --tp consecutive ranks, batch over the rest)")
     p.add_argument("--accum_steps", type=int, default=1, help="micro-batches per optimizer step")
+    p.add_argument("--tp_fused", choices=["on", "off"], default="on",
+                   help="with --tp: row-parallel out_proj + all-reduce as one peer-memory kernel")
     p.add_argument("--extras", choices=["auto", "on", "off"], default="auto",
                    help="after the headline region, time the published 75m recipe config and the "
                         "generation workload as extra keys (auto: on one GPU only)")
@@ -380,7 +382,7 @@ def main():
     trainer = Trainer(args, device=dev, world=world, rank=rank, total_steps=10_000, seed=0,
                       sharded=a.dp_impl == "nccl_sharded", dp_impl="fused" if a.dp_impl == "fused" else "nccl",
                       tp=a.tp, accum_steps=a.accum_steps, fsdp=a.dp_impl in ("fsdp", "fsdp_ag") and a.tp == 1,
-                      fsdp_fused_ag=a.dp_impl == "fsdp_ag")
+                      fsdp_fused_ag=a.dp_impl == "fsdp_ag", tp_fused_out=a.tp_fused == "on")
     dp_world, dp_rank = trainer.world, trainer.rank          # with --tp the batch is split over dp only
     Bm = Bm * a.accum_steps
 
@@ -463,6 +465,7 @@ def main():
             "config": {"model": f"{arch}-lob-{a.preset} ({n_params/1e6:.1f}M params, d_model {d_model}, "
                                 f"{nml}+{nbpre}+{nbpost}+{nl} layers)",
                        "global_batch": Bm * dp_world, "seq_len": L,
+                       "tp_fused_out_proj_modules": len(trainer.tp_fused),
                        "parallelism": f"tp{a.tp}xdp{dp_world}" if a.tp > 1 else
                        ((f"fsdp{world}" + ("_fused_ag" if trainer.fsdp.fused_ag else "")) if trainer.fsdp is not None
                         else f"dp{world}"),

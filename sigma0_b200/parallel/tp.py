@@ -152,7 +152,7 @@ class Mamba3TP(nn.Module):
         y = y.reshape(*lead, nhl * P)
         ss = all_reduce_both((y * y).sum(-1, keepdim=True), self.group)      # full-width RMS statistic
         yn = y * torch.rsqrt(ss / d.d_inner + self.eps) * self.out_norm_scale
-        if self.fused_out is not None and yn.is_cuda:
+        if self.fused_out is not None and yn.is_cuda and yn.numel() // yn.shape[-1] <= self.fused_out.M:
             from .tp_fused import fused_row_parallel
             out = fused_row_parallel(yn.reshape(-1, yn.shape[-1]), self.out_proj_kernel, self.fused_out)
             return out.reshape(*lead, -1).to(u.dtype)

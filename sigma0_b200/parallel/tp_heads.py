@@ -76,7 +76,7 @@ class _RowParallel:
         return [own[local] for local, _, dim in self._full_table() if dim is not None]
 
     def _reduce(self, y: torch.Tensor, w: torch.Tensor, group) -> torch.Tensor:
-        if self.fused is not None and y.is_cuda:
+        if self.fused is not None and y.is_cuda and y.numel() // y.shape[-1] <= self.fused.M:
             from .tp_fused import fused_row_parallel
             lead = y.shape[:-1]
             return fused_row_parallel(y.reshape(-1, y.shape[-1]), w, self.fused).reshape(*lead, -1)

@@ -43,7 +43,8 @@ class Trainer:
                  group=None, total_steps: int = 1000, seed: int = 0, sharded: bool = False,
                  accum_steps: int = 1, grad_wire_dtype: str = "float32", dp_impl: str = "nccl",
                  context_parallel: bool = False, tp: int = 1, hierarchical: bool = False,
-                 gpus_per_node: Optional[int] = None, fsdp: bool = False, fsdp_fused_ag: bool = False):
+                 gpus_per_node: Optional[int] = None, fsdp: bool = False, fsdp_fused_ag: bool = False,
+                 tp_fused_out: Optional[bool] = None):
         self.args = args
         self.device = device or torch.device("cuda" if torch.cuda.is_available() else "cpu")
         from ..encoding.tok1 import encoding_mode
@@ -60,6 +61,7 @@ class Trainer:
         # tensor parallelism: a (dp, tp) mesh over the default group; the mixers' heads (and
         # the attention blocks' FFN width) are split over the tp axis, the batch over dp
         self.tp, self.tp_group, tp_slices = 1, None, []
+        self.tp_fused: list = []          # TP modules whose out_proj runs the fused GEMM + all-reduce
         if int(tp) > 1:
             if world <= 1 or group is not None or context_parallel:
                 raise ValueError("tensor parallelism needs the default process group of >= 2 ranks and no "
@@ -75,6 +77,21 @@ class Trainer:
             for mod in self.model.modules():
                 if hasattr(mod, "tp_sharded_parameters"):
                     tp_slices += mod.tp_sharded_parameters()
+            # the row-parallel output projections + their all-reduce as one peer-memory kernel
+            # (csrc/tp_fused.cu); default on CUDA, a module whose width the kernel cannot tile
+            # keeps GEMM + NCCL
+            if tp_fused_out is None:
+                tp_fused_out = self.device.type == "cuda"
+            if tp_fused_out:
+                rows = int(getattr(args, "micro_bsz", 1)) * int(getattr(args, "n_messages", 1)) * \
+                    int(getattr(args, "msg_len", 1))
+                for mod in self.model.modules():
+                    if hasattr(mod, "use_fused_out_proj"):
+                        try:
+                            mod.use_fused_out_proj(rows)
+                            self.tp_fused.append(mod)
+                        except ValueError:
+                            pass
             dp = mesh.size("dp") if "dp" in mesh.axis_names else 1
             group = mesh.group("dp") if dp > 1 else None
             world, rank = dp, (mesh.coord("dp") if dp > 1 else 0)
@@ -335,6 +352,10 @@ class Trainer:
         value = float(loss.item())
         if self.fused is not None:      # the loss read synchronised: the status copy has landed
             self.fused.poll()
+        for mod in self.tp_fused:       # and every fused TP kernel's status word is final
+            helper = getattr(mod, "fused_out", None) or getattr(mod, "fused", None)
+            if helper is not None:
+                helper.check()
         return value
 
     @torch.no_grad()
