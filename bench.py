@@ -446,6 +446,11 @@ def main():
     if a.tp > 1:   # the model's size: the replicated parameters once, the head slices from every rank
         from sigma0_b200.models import build_model
         n_params = sum(p.numel() for p in build_model(args).parameters())
+    # labels read off the trainer before it is freed for the extras
+    n_tp_fused = len(trainer.tp_fused)
+    par_label = (f"tp{a.tp}xdp{dp_world}" if a.tp > 1 else
+                 ((f"fsdp{world}" + ("_fused_ag" if trainer.fsdp.fused_ag else "")) if trainer.fsdp is not None
+                  else f"dp{world}"))
     extras = {}
     if a.extras == "on" or (a.extras == "auto" and world == 1):
         # outside the headline region: free the headline trainer first
@@ -465,10 +470,8 @@ def main():
             "config": {"model": f"{arch}-lob-{a.preset} ({n_params/1e6:.1f}M params, d_model {d_model}, "
                                 f"{nml}+{nbpre}+{nbpost}+{nl} layers)",
                        "global_batch": Bm * dp_world, "seq_len": L,
-                       "tp_fused_out_proj_modules": len(trainer.tp_fused),
-                       "parallelism": f"tp{a.tp}xdp{dp_world}" if a.tp > 1 else
-                       ((f"fsdp{world}" + ("_fused_ag" if trainer.fsdp.fused_ag else "")) if trainer.fsdp is not None
-                        else f"dp{world}"),
+                       "tp_fused_out_proj_modules": n_tp_fused,
+                       "parallelism": par_label,
                        "accum_steps": a.accum_steps,
                        "grad_sync": ((a.dp_impl if (not a.dp_impl.startswith("fsdp") or a.tp == 1) else "nccl")
                                      if world > 1 else "none"),
