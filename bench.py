@@ -58,12 +58,16 @@ def parse():
                         "FSDP (ZeRO-3 of the fused layers' kernels, parallel/fsdp.py)")
     p.add_argument("--tp", type=int, default=1,
                    help="tensor-parallel size (heads split over --tp consecutive ranks, batch over the rest)")
-    p.add_argument("--accum_steps", type=int, default=1, help="micro-batches per optimizer step")
+    p.add_argument("--accum_steps", type=int, default=None,
+                   help="micro-batches per optimizer step (default: the preset's, else 1)")
     p.add_argument("--tp_fused", choices=["on", "off"], default="on",
                    help="with --tp: row-parallel out_proj + all-reduce as one peer-memory kernel")
+    p.add_argument("--cp", action="store_true",
+                   help="context parallelism over all N ranks (the long-context hybrid1b / nsa1b "
+                        "configuration): every rank holds a contiguous segment of every sequence")
     p.add_argument("--extras", choices=["auto", "on", "off"], default="auto",
                    help="after the headline region, time the published 75m recipe config and the "
-                        "generation workload as extra keys (auto: on one GPU only)")
+                        "generation workload as extra keys (auto: the 350m headline on one GPU only)")
     return p.parse_args()
 
 
@@ -347,6 +351,21 @@ def train_rate_75m(world, rank, dev, dp_impl, barrier, steps=20, warmup=5):
             "published_source": "docs/training.md:132 (0.072-0.075 s/step, 714k tok/s per 4xGH200 node)"}
 
 
+def cp_messages(args, world: int) -> int:
+    """Messages per sequence for a context-parallel run on ``world`` ranks: the preset's
+    length is its 8-rank shape, so each rank keeps the same segment (weak scaling) --
+    ``n_messages * world / 8``.  NSA segments must also start on a selection-block
+    boundary, so the per-rank message count is rounded up to make the segment a multiple
+    of that block."""
+    import math
+    per = max(1, args.n_messages // 8)
+    if args.architecture == "nsa":
+        sel = int(getattr(args, "nsa_select_block", args.msg_len))
+        step = sel // math.gcd(sel, args.msg_len)
+        per = -(-per // step) * step
+    return per * world
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -378,12 +397,22 @@ def main():
         args.micro_bsz = a.micro_bsz
     if a.n_messages:
         args.n_messages = a.n_messages
+    elif a.cp:
+        args.n_messages = cp_messages(args, world)
+    if a.cp and a.tp > 1:
+        raise SystemExit("--cp runs over all ranks; it does not combine with --tp")
     Bm, nm = args.micro_bsz, args.n_messages
+    if a.accum_steps is None:
+        a.accum_steps = int(getattr(args, "accum_steps", 1))
+    use_fsdp = a.dp_impl in ("fsdp", "fsdp_ag") and a.tp == 1 and not a.cp
     trainer = Trainer(args, device=dev, world=world, rank=rank, total_steps=10_000, seed=0,
-                      sharded=a.dp_impl == "nccl_sharded", dp_impl="fused" if a.dp_impl == "fused" else "nccl",
-                      tp=a.tp, accum_steps=a.accum_steps, fsdp=a.dp_impl in ("fsdp", "fsdp_ag") and a.tp == 1,
-                      fsdp_fused_ag=a.dp_impl == "fsdp_ag", tp_fused_out=a.tp_fused == "on")
-    dp_world, dp_rank = trainer.world, trainer.rank          # with --tp the batch is split over dp only
+                      sharded=a.dp_impl == "nccl_sharded" and not a.cp,
+                      dp_impl="fused" if a.dp_impl == "fused" and not a.cp else "nccl",
+                      tp=a.tp, accum_steps=a.accum_steps, fsdp=use_fsdp,
+                      fsdp_fused_ag=use_fsdp and a.dp_impl == "fsdp_ag", tp_fused_out=a.tp_fused == "on",
+                      context_parallel=a.cp)
+    # with --tp the batch is split over dp only; with --cp every rank takes the whole batch
+    dp_world, dp_rank = (1, 0) if a.cp else (trainer.world, trainer.rank)
     Bm = Bm * a.accum_steps
 
     # synthetic data: Bm sequences per dp rank, replayed through the engine
@@ -448,11 +477,11 @@ def main():
         n_params = sum(p.numel() for p in build_model(args).parameters())
     # labels read off the trainer before it is freed for the extras
     n_tp_fused = len(trainer.tp_fused)
-    par_label = (f"tp{a.tp}xdp{dp_world}" if a.tp > 1 else
+    par_label = (f"cp{world}" if trainer.cp else f"tp{a.tp}xdp{dp_world}" if a.tp > 1 else
                  ((f"fsdp{world}" + ("_fused_ag" if trainer.fsdp.fused_ag else "")) if trainer.fsdp is not None
                   else f"dp{world}"))
     extras = {}
-    if a.extras == "on" or (a.extras == "auto" and world == 1):
+    if a.extras == "on" or (a.extras == "auto" and world == 1 and a.preset == "350m" and not a.cp):
         # outside the headline region: free the headline trainer first
         del trainer, devb, host
         torch.cuda.empty_cache()
@@ -474,7 +503,9 @@ def main():
                        "parallelism": par_label,
                        "accum_steps": a.accum_steps,
                        "grad_sync": ((a.dp_impl if (not a.dp_impl.startswith("fsdp") or a.tp == 1) else "nccl")
-                                     if world > 1 else "none"),
+                                     if world > 1 and not a.cp else "nccl all-reduce (cp)" if world > 1
+                                     else "none"),
+                       "segment_tokens_per_rank": L // world if a.cp else None,
                        "l2": "working set (weights + ~90 GB activations per step) far above L2; no flush needed",
                        "vocab": vocab, "token_mode": tmode},
             "loss": float(loss), "gpu_launches": launches, "clocks": clk, "e2e": e2e,

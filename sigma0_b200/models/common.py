@@ -119,9 +119,10 @@ class _EmbedGather(torch.autograd.Function):
     @staticmethod
     def forward(ctx, idx, *weights):
         from ..ops._ext import ext
+        idx = idx.contiguous()          # a context-parallel segment is a strided view
         ctx.save_for_backward(idx)
         ctx.shapes = [w.shape for w in weights]
-        return ext().embed_sum_fwd([w.contiguous() for w in weights], idx.contiguous())
+        return ext().embed_sum_fwd([w.contiguous() for w in weights], idx)
 
     @staticmethod
     def backward(ctx, g):

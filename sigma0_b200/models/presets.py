@@ -10,6 +10,14 @@
   GPU (global batch 64 on 8 GPUs), bf16 compute with float32 master weights.
 * ``75m``: the reference's published recipe model (``docs/training.md:108-111``):
   d_model 1024, 2 message + 6 fused layers, 1 book pre + 1 book post layer.
+* ``hybrid1b`` / ``nsa1b``: the long-context configuration -- d_model 2048, 24 layers
+  (2 message + 1 book pre + 1 book post + 20 fused), 3,000 messages (66,000 tokens) per
+  sequence, 8 sequences per optimizer step (4 accumulated micro-batches of 2: the
+  activations of 8 whole sequences do not fit in 180 GB), meant to run context-parallel
+  over 8 GPUs.  ``hybrid1b`` is
+  hybrid_mamba3 with one attention block (16 heads of dim 128) after every four Mamba3
+  layers of the trunk; ``nsa1b`` is the NSA transformer with compression block 32,
+  selection block 64, top-16 selected blocks and a 512-token sliding window.
 """
 from __future__ import annotations
 
@@ -35,6 +43,16 @@ PRESETS = {
                 mamba3_expand=2, n_message_layers=2, n_layers=6, n_book_pre_layers=1,
                 n_book_post_layers=1, token_mode="26tok", vocab_size=2112, msg_len=26,
                 n_messages=500, micro_bsz=1, dtype="bfloat16", d_book=503),
+    "hybrid1b": dict(architecture="hybrid_mamba3", d_model=2048, mamba3_d_state=128, mamba3_headdim=64,
+                     mamba3_expand=2, n_message_layers=2, n_layers=20, n_book_pre_layers=1,
+                     n_book_post_layers=1, hybrid_attn_layers="4,9,14,19", hybrid_attn_heads=16,
+                     token_mode="22tok", vocab_size=12288, msg_len=22, n_messages=3000, micro_bsz=2,
+                     accum_steps=4,
+                     dtype="bfloat16", d_book=503),
+    "nsa1b": dict(architecture="nsa", d_model=2048, n_heads=16, nsa_strict_block=False, block_size=32,
+                  nsa_select_block=64, block_counts=16, window_size=512, n_message_layers=2, n_layers=20,
+                  n_book_pre_layers=1, n_book_post_layers=1, token_mode="22tok", vocab_size=12288,
+                  msg_len=22, n_messages=3000, micro_bsz=2, accum_steps=4, dtype="bfloat16", d_book=503),
 }
 
 _DEFAULTS = dict(activation_fn="half_glu1", prenorm=True, p_dropout=0.0, use_book_data=True,

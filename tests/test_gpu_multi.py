@@ -320,3 +320,41 @@ def test_fused_all_gather_gemm_gathers_exactly(tmp_path):
     mp.spawn(_ag_gemm_worker, args=(2, _port(), out), nprocs=2, join=True)
     r = torch.load(out)
     assert r["gathered_exact"] and r["status"] == 0 and r["rel_err"] < 1e-2
+
+
+def _hybrid_cp_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from sigma0_b200.data import make_sequences, LobWindowDataset, collate
+        from sigma0_b200.models import preset_args
+        from sigma0_b200.train.trainer import Trainer
+        args = preset_args("hybrid1b", d_model=256, n_layers=3, hybrid_attn_layers="1", hybrid_attn_heads=2,
+                           n_messages=32, micro_bsz=2, impl="cuda", warmup_end=0.0)
+        ds = LobWindowDataset.from_days(make_sequences(2, 33, seed=5), 32, token_mode="22tok")
+        batch = tuple(t.cuda() for t in collate([ds[0], ds[1]]))
+        tr = Trainer(args, device=torch.device("cuda", rank), world=world, rank=rank, total_steps=10, seed=0,
+                     context_parallel=True)
+        cp_loss = [float(tr.step_device(*batch)) for _ in range(2)]
+        del tr
+        if rank == 0:
+            one = Trainer(args, device=torch.device("cuda", rank), world=1, rank=0, total_steps=10, seed=0)
+            ref = [float(one.step_device(*batch)) for _ in range(2)]
+            torch.save({"cp": cp_loss, "ref": ref}, out)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@need2
+def test_hybrid_context_parallel_trainer_matches_one_gpu(tmp_path):
+    """hybrid_mamba3 (Mamba3 walkers carried across the segment boundary, attention over the
+    gathered key prefix with a query offset) on 2 GPUs takes the same two steps as one GPU."""
+    out = str(tmp_path / "hcp.pt")
+    mp.spawn(_hybrid_cp_worker, args=(2, _port(), out), nprocs=2, join=True)
+    r = torch.load(out)
+    for a, b in zip(r["cp"], r["ref"]):
+        assert abs(a - b) / abs(b) < 1e-2, (r["cp"], r["ref"])
