@@ -586,12 +586,16 @@ std::vector<at::Tensor> rms_fwd(at::Tensor x, at::Tensor w, double eps) {
   req(x, at::kBFloat16, "x");
   c10::cuda::CUDAGuard guard(x.device());
   int64_t D = x.size(-1), T = x.numel() / D;
-  TORCH_CHECK(D % 8 == 0 && D <= 2048, "RMSNorm width must be a multiple of 8, at most 2048");
+  TORCH_CHECK(D % 8 == 0 && D <= 8192, "RMSNorm width must be a multiple of 8, at most 8192");
   if (reinterpret_cast<uintptr_t>(w.data_ptr()) % 16) w = w.clone();   // the kernel reads w as float4
   auto y = at::empty_like(x);
   auto rstd = at::empty({T}, x.options().dtype(at::kFloat));
-  rms_fwd_launch(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), rstd.data_ptr<float>(), T, (int)D, (float)eps,
-                 num_sms(x), stream());
+  if (D > 2048)
+    rms_fwd_wide_launch(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), rstd.data_ptr<float>(), T, (int)D,
+                        (float)eps, num_sms(x), stream());
+  else
+    rms_fwd_launch(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), rstd.data_ptr<float>(), T, (int)D, (float)eps,
+                   num_sms(x), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {y, rstd};
 }
@@ -601,10 +605,17 @@ std::vector<at::Tensor> rms_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::T
   req(x, at::kBFloat16, "x");
   c10::cuda::CUDAGuard guard(x.device());
   int64_t D = x.size(-1), T = x.numel() / D;
-  TORCH_CHECK(D % 8 == 0 && D <= 2048, "RMSNorm width must be a multiple of 8, at most 2048");
+  TORCH_CHECK(D % 8 == 0 && D <= 8192, "RMSNorm width must be a multiple of 8, at most 8192");
   if (reinterpret_cast<uintptr_t>(w.data_ptr()) % 16) w = w.clone();   // the kernel reads w as float4
   auto dx = at::empty_like(x);
   auto dw = at::empty({D}, x.options().dtype(at::kFloat));
+  if (D > 2048) {
+    auto wpart = at::empty({(int64_t)rms_wide_blocks(T, num_sms(x)), D}, x.options().dtype(at::kFloat));
+    rms_bwd_wide_launch(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
+                        dw.data_ptr<float>(), wpart.data_ptr<float>(), T, (int)D, num_sms(x), stream());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return {dx, dw};
+  }
   auto part = at::empty({std::max<int64_t>(col_blocks(T, num_sms(x)), num_sms(x)), D}, x.options().dtype(at::kFloat));
   if (D > 1024 && D <= 2048 && T >= num_sms(x))
     rms_bwd_pipe_launch(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),

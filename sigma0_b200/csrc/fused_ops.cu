@@ -425,6 +425,142 @@ __global__ void __launch_bounds__(256, 2) rms_bwd_k(const bf16* __restrict__ dy,
   }
 }
 
+// RMSNorm for wide rows (2048 < D <= 1024 * PER): one 128-thread block per row, each
+// thread holding PER 16-byte chunks (columns tid + 128 j), the row sum reduced through
+// four shared-memory slots.  The backward keeps each thread's dw columns in registers
+// across its rows and writes one partial row per block for col_sum_k.
+constexpr int RW_NT = 128;
+template <int PER>
+__global__ void __launch_bounds__(RW_NT) rms_fwd_wide_k(const bf16* __restrict__ x, const float* __restrict__ w,
+                                                      bf16* __restrict__ y, float* __restrict__ rstd, int T, int D,
+                                                      float eps) {
+  __shared__ float red[RW_NT / 32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int nv = D / 8;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  for (int row = blockIdx.x; row < T; row += gridDim.x) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
+    uint4 u[PER];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = tid + RW_NT * j;
+      u[j] = c < nv ? xr[c] : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const uint32_t a[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) { const float2 f = unpack_bf16(a[k]); s += f.x * f.x + f.y * f.y; }
+    }
+    s = warp_sum(s);
+    if (lane == 0) red[wid] = s;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < RW_NT / 32; ++k) tot += red[k];
+    __syncthreads();                       // red is rewritten by the next row
+    const float r = rsqrtf(tot / D + eps);
+    uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * D);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = tid + RW_NT * j;
+      if (c < nv) {
+        const float4 wa = w4[2 * c], wb = w4[2 * c + 1];
+        const float ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t a[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = unpack_bf16(a[k]);
+          o[k] = pack_bf16(f.x * r * ws[2 * k], f.y * r * ws[2 * k + 1]);
+        }
+        yr[c] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    if (tid == 0) rstd[row] = r;
+  }
+}
+
+template <int PER>
+__global__ void __launch_bounds__(RW_NT) rms_bwd_wide_k(const bf16* __restrict__ dy, const bf16* __restrict__ x,
+                                                      const float* __restrict__ w, const float* __restrict__ rstd,
+                                                      bf16* __restrict__ dx, float* __restrict__ part, int T,
+                                                      int D) {
+  __shared__ float red[RW_NT / 32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int nv = D / 8;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float aw[PER * 8];
+#pragma unroll
+  for (int i = 0; i < PER * 8; ++i) aw[i] = 0.f;
+  for (int row = blockIdx.x; row < T; row += gridDim.x) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * D);
+    const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * D);
+    const float r = rstd[row];
+    uint4 ux[PER], ug[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = tid + RW_NT * j;
+      const bool ok = c < nv;
+      ux[j] = ok ? xr[c] : make_uint4(0u, 0u, 0u, 0u);
+      ug[j] = ok ? gr[c] : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = tid + RW_NT * j;
+      if (c < nv) {
+        const float4 wa = w4[2 * c], wb = w4[2 * c + 1];
+        const float ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t ax[4] = {ux[j].x, ux[j].y, ux[j].z, ux[j].w}, ag[4] = {ug[j].x, ug[j].y, ug[j].z, ug[j].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          m += fg.x * ws[2 * k] * fx.x + fg.y * ws[2 * k + 1] * fx.y;
+        }
+      }
+    }
+    m = warp_sum(m);
+    if (lane == 0) red[wid] = m;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < RW_NT / 32; ++k) tot += red[k];
+    __syncthreads();
+    const float r3m = r * r * r * (tot / D);
+    uint4* dr = reinterpret_cast<uint4*>(dx + (size_t)row * D);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int c = tid + RW_NT * j;
+      if (c < nv) {
+        const float4 wa = w4[2 * c], wb = w4[2 * c + 1];
+        const float ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t ax[4] = {ux[j].x, ux[j].y, ux[j].z, ux[j].w}, ag[4] = {ug[j].x, ug[j].y, ug[j].z, ug[j].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 fx = unpack_bf16(ax[k]), fg = unpack_bf16(ag[k]);
+          o[k] = pack_bf16(r * fg.x * ws[2 * k] - fx.x * r3m, r * fg.y * ws[2 * k + 1] - fx.y * r3m);
+          aw[j * 8 + 2 * k] += fg.x * fx.x * r;
+          aw[j * 8 + 2 * k + 1] += fg.y * fx.y * r;
+        }
+        dr[c] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  float* pr = part + (size_t)blockIdx.x * D;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int c = tid + RW_NT * j;
+    if (c < nv) {
+      *reinterpret_cast<float4*>(pr + c * 8) = make_float4(aw[j * 8], aw[j * 8 + 1], aw[j * 8 + 2], aw[j * 8 + 3]);
+      *reinterpret_cast<float4*>(pr + c * 8 + 4) =
+          make_float4(aw[j * 8 + 4], aw[j * 8 + 5], aw[j * 8 + 6], aw[j * 8 + 7]);
+    }
+  }
+}
+
 // RMSNorm backward, pipelined: each warp stages its NEXT row of x and dy in shared
 // memory with cp.async while it computes the current one, so every warp always has a
 // row in flight (the register version issues one row's loads, waits, computes, and
@@ -833,6 +969,30 @@ void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* 
   else if (nv <= 64) { allow_smem(rms_bwd_k<2>, sm); rms_bwd_k<2><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
   else if (nv <= 128) { allow_smem(rms_bwd_k<4>, sm); rms_bwd_k<4><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
   else { allow_smem(rms_bwd_k<8>, sm); rms_bwd_k<8><<<gr, 256, sm, st>>>(g, xp, w, rstd, o, part, (int)T, D); }
+  col_sum(part, gr, 1, D, dw, nullptr, st);
+}
+// wide rows (2048 < D <= 8192): one block per row; `part` holds >= rms_wide_blocks rows
+int rms_wide_blocks(long T, int sms) {
+  const long cap = 4L * sms;
+  return (int)(T < cap ? (T > 0 ? T : 1) : cap);
+}
+void rms_fwd_wide_launch(const void* x, const float* w, void* y, float* rstd, long T, int D, float eps, int sms,
+                         cudaStream_t st) {
+  const long cap = 16L * sms;
+  const int gr = (int)(T < cap ? (T > 0 ? T : 1) : cap);
+  const bf16* xp = reinterpret_cast<const bf16*>(x);
+  bf16* yp = reinterpret_cast<bf16*>(y);
+  if (D <= RW_NT * 8 * 4) rms_fwd_wide_k<4><<<gr, RW_NT, 0, st>>>(xp, w, yp, rstd, (int)T, D, eps);
+  else rms_fwd_wide_k<8><<<gr, RW_NT, 0, st>>>(xp, w, yp, rstd, (int)T, D, eps);
+}
+void rms_bwd_wide_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw,
+                         float* part, long T, int D, int sms, cudaStream_t st) {
+  const int gr = rms_wide_blocks(T, sms);
+  const bf16* g = reinterpret_cast<const bf16*>(dy);
+  const bf16* xp = reinterpret_cast<const bf16*>(x);
+  bf16* o = reinterpret_cast<bf16*>(dx);
+  if (D <= RW_NT * 8 * 4) rms_bwd_wide_k<4><<<gr, RW_NT, 0, st>>>(g, xp, w, rstd, o, part, (int)T, D);
+  else rms_bwd_wide_k<8><<<gr, RW_NT, 0, st>>>(g, xp, w, rstd, o, part, (int)T, D);
   col_sum(part, gr, 1, D, dw, nullptr, st);
 }
 // pipelined variant for wide rows (D > 1024): one block per SM; `part` holds >= sms rows

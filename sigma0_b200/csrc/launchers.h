@@ -187,6 +187,11 @@ void m3_decode_multi_launch(const void* proj, int B, int T, int ldp, int nh, con
                             const float* dt_bias, const float* Bb, const float* Cb, const float* D, float A_floor,
                             float eps, float* ang, float* ssm, float* kprev, float* vprev, void* y,
                             cudaStream_t st);
+int rms_wide_blocks(long T, int sms);
+void rms_fwd_wide_launch(const void* x, const float* w, void* y, float* rstd, long T, int D, float eps, int sms,
+                         cudaStream_t st);
+void rms_bwd_wide_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw,
+                         float* part, long T, int D, int sms, cudaStream_t st);
 void rms_bwd_pipe_launch(const void* dy, const void* x, const float* w, const float* rstd, void* dx, float* dw,
                          float* part, long T, int D, int sms, cudaStream_t st);
 void ln_bwd_pipe_launch(const void* dy, const float* x, const float* mean, const float* rstd, const float* w,

@@ -265,9 +265,10 @@ def test_odd_width_book_layer_paths_match_fp32():
     assert rel(y, y2) < 3e-2, rel(y, y2)
 
 
-@pytest.mark.parametrize("T,D", [(300, 2048), (5000, 2048), (257, 1024), (100, 2048), (40, 64)])
+@pytest.mark.parametrize("T,D", [(300, 2048), (5000, 2048), (257, 1024), (100, 2048), (40, 64), (3000, 4096),
+                                 (77, 4096), (500, 3072), (64, 8192)])
 def test_rmsnorm_kernels_match_fp32(T, D):
-    """rms_fwd / rms_bwd (register and pipelined variants) against fp32 autograd."""
+    """rms_fwd / rms_bwd (register, pipelined and wide-row variants) against fp32 autograd."""
     from sigma0_b200.ops._ext import ext
     C = ext()
     torch.manual_seed(D + T)
