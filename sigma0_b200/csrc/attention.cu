@@ -57,7 +57,7 @@ __device__ __forceinline__ void load_tile(bf16* s, const bf16* g, long row_strid
 // ------------------------------------------------------------------------------------------
 // forward
 // ------------------------------------------------------------------------------------------
-template <int HD>
+template <int HD, bool SEL>
 __global__ void __launch_bounds__(NT, HD == 64 ? 2 : 1) attn_fwd_k(AttnArgs a) {
   constexpr int BQ = 128, BKV = 64, LDS = HD + 8, KS = HD / 16;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -67,8 +67,14 @@ __global__ void __launch_bounds__(NT, HD == 64 ? 2 : 1) attn_fwd_k(AttnArgs a) {
   const int q0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const bf16* qg = a.q + b * a.sq_b + (long)q0 * a.sq_l + h * a.sq_h;
-  const bf16* kg = a.k + b * a.sk_b + h * a.sk_h;
-  const bf16* vg = a.v + b * a.sv_b + h * a.sv_h;
+  const long kb_b = SEL ? (long)(b / a.kb_ng) : (long)b;             // the batch the keys come from
+  const bf16* kg = a.k + kb_b * a.sk_b + h * a.sk_h;
+  const bf16* vg = a.v + kb_b * a.sv_b + h * a.sv_h;
+  // first source row of logical key block j (64 keys; block-indirect with SEL)
+  auto krow = [&](int j) -> long {
+    if constexpr (SEL) return (long)min(max(__ldg(a.kblk + (long)b * a.kb_n + j), 0), a.kb_max) * BKV;
+    else return (long)j * BKV;
+  };
   const int qoff = a.qoff ? a.qoff[b] : a.q_offset;
   const int* kp = a.kpos ? a.kpos + (long)b * a.Lk : nullptr;     // per-key positions (else the index)
   const int qlo = qoff + q0;                                         // smallest query position here
@@ -82,8 +88,8 @@ __global__ void __launch_bounds__(NT, HD == 64 ? 2 : 1) attn_fwd_k(AttnArgs a) {
 
   load_tile<HD>(sQ, qg, a.sq_l, BQ, a.Lq - q0, tid);
   if (kb0 < kb1) {
-    load_tile<HD>(sK, kg + (long)kb0 * BKV * a.sk_l, a.sk_l, BKV, a.Lk - kb0 * BKV, tid);
-    load_tile<HD>(sV, vg + (long)kb0 * BKV * a.sv_l, a.sv_l, BKV, a.Lk - kb0 * BKV, tid);
+    load_tile<HD>(sK, kg + krow(kb0) * a.sk_l, a.sk_l, BKV, a.Lk - kb0 * BKV, tid);
+    load_tile<HD>(sV, vg + krow(kb0) * a.sv_l, a.sv_l, BKV, a.Lk - kb0 * BKV, tid);
   }
   cp_async_commit();
 
@@ -99,8 +105,8 @@ __global__ void __launch_bounds__(NT, HD == 64 ? 2 : 1) attn_fwd_k(AttnArgs a) {
     const int st = (kb - kb0) & 1;
     if (kb + 1 < kb1) {
       const int n = (kb + 1) * BKV;
-      load_tile<HD>(sK + (st ^ 1) * BKV * LDS, kg + (long)n * a.sk_l, a.sk_l, BKV, a.Lk - n, tid);
-      load_tile<HD>(sV + (st ^ 1) * BKV * LDS, vg + (long)n * a.sv_l, a.sv_l, BKV, a.Lk - n, tid);
+      load_tile<HD>(sK + (st ^ 1) * BKV * LDS, kg + krow(kb + 1) * a.sk_l, a.sk_l, BKV, a.Lk - n, tid);
+      load_tile<HD>(sV + (st ^ 1) * BKV * LDS, vg + krow(kb + 1) * a.sv_l, a.sv_l, BKV, a.Lk - n, tid);
     }
     cp_async_commit();
     cp_async_wait_group<1>();
@@ -356,8 +362,23 @@ __global__ void __launch_bounds__(NT, 1) attn_bwd_k(AttnBwdArgs a) {
     qb1 = ihi > ilo ? (ihi + BR - 1) / BR : qb0;
   }
 
-  load_tile<HD>(sK, f.k + b * f.sk_b + (long)k0 * f.sk_l + h * f.sk_h, f.sk_l, BC, f.Lk - k0, tid);
-  load_tile<HD>(sV, f.v + b * f.sv_b + (long)k0 * f.sv_l + h * f.sv_h, f.sv_l, BC, f.Lk - k0, tid);
+  if (f.kblk) {
+    // block-indirect keys: the tile's two 64-key halves come from their own source blocks
+    const long kb_b = (long)(b / f.kb_ng);
+    const bf16* ks = f.k + kb_b * f.sk_b + h * f.sk_h;
+    const bf16* vs = f.v + kb_b * f.sv_b + h * f.sv_h;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int j = blockIdx.x * 2 + half;
+      const bool ok = j < f.kb_n;
+      const long row = ok ? (long)min(max(__ldg(f.kblk + (long)b * f.kb_n + j), 0), f.kb_max) * (BC / 2) : 0;
+      load_tile<HD>(sK + half * (BC / 2) * LDS, ks + row * f.sk_l, f.sk_l, BC / 2, ok ? BC / 2 : 0, tid);
+      load_tile<HD>(sV + half * (BC / 2) * LDS, vs + row * f.sv_l, f.sv_l, BC / 2, ok ? BC / 2 : 0, tid);
+    }
+  } else {
+    load_tile<HD>(sK, f.k + b * f.sk_b + (long)k0 * f.sk_l + h * f.sk_h, f.sk_l, BC, f.Lk - k0, tid);
+    load_tile<HD>(sV, f.v + b * f.sv_b + (long)k0 * f.sv_l + h * f.sv_h, f.sv_l, BC, f.Lk - k0, tid);
+  }
   auto load_q = [&](int qb, int st) {
     const int r0 = qb * BR;
     load_tile<HD>(sQ + st * BR * LDS, qg + (long)r0 * f.sq_l, f.sq_l, BR, f.Lq - r0, tid);
@@ -491,6 +512,32 @@ __global__ void __launch_bounds__(NT, 1) attn_bwd_k(AttnBwdArgs a) {
     __syncthreads();                                                 // stage st and dS^T free
   }
   cp_async_wait_group<0>();
+  if (f.kblk) {
+    // block-indirect keys: several entries select the same source block, so the gradients
+    // are added into the fp32 source-shaped buffers
+    const long rs = (long)f.nh * HD;                                 // row stride of the buffers
+    const long base = (long)(b / f.kb_ng) * a.kb_lsrc * rs + (long)h * HD;
+    const int ja = key_a >> 6, jb = key_b >> 6;                      // logical 64-key blocks
+    auto src_row = [&](int key, int j) -> long {
+      return key < f.Lk ? (long)min(max(__ldg(f.kblk + (long)b * f.kb_n + j), 0), f.kb_max) * 64 + (key & 63) : -1;
+    };
+    const long ra = src_row(key_a, ja), rb = src_row(key_b, jb);
+#pragma unroll
+    for (int nt = 0; nt < HD / 8; ++nt) {
+      const int c = nt * 8 + 2 * t;
+      if (ra >= 0) {
+        atomicAdd(reinterpret_cast<float2*>(a.dk_acc + base + ra * rs + c),
+                  make_float2(dk[nt][0] * a.scale, dk[nt][1] * a.scale));
+        atomicAdd(reinterpret_cast<float2*>(a.dv_acc + base + ra * rs + c), make_float2(dv[nt][0], dv[nt][1]));
+      }
+      if (rb >= 0) {
+        atomicAdd(reinterpret_cast<float2*>(a.dk_acc + base + rb * rs + c),
+                  make_float2(dk[nt][2] * a.scale, dk[nt][3] * a.scale));
+        atomicAdd(reinterpret_cast<float2*>(a.dv_acc + base + rb * rs + c), make_float2(dv[nt][2], dv[nt][3]));
+      }
+    }
+    return;
+  }
   // dK (scaled) and dV, bf16, straight from the accumulators
   bf16* dkg = a.dk + b * a.sdk_b + h * a.sdk_h;
   bf16* dvg = a.dv + b * a.sdv_b + h * a.sdv_h;
@@ -516,9 +563,14 @@ size_t bwd_smem() { return (size_t)(2 * 128 + 4 * 64) * (HD + 8) * 2 + (size_t)1
 template <int HD>
 int fwd_launch(const AttnArgs& a, cudaStream_t st) {
   const size_t sm = fwd_smem<HD>();
-  cudaFuncSetAttribute(attn_fwd_k<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   dim3 grid((a.Lq + 127) / 128, a.nh, a.B);
-  attn_fwd_k<HD><<<grid, NT, sm, st>>>(a);
+  if (a.kblk) {
+    cudaFuncSetAttribute(attn_fwd_k<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    attn_fwd_k<HD, true><<<grid, NT, sm, st>>>(a);
+  } else {
+    cudaFuncSetAttribute(attn_fwd_k<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    attn_fwd_k<HD, false><<<grid, NT, sm, st>>>(a);
+  }
   return (int)cudaGetLastError();
 }
 

@@ -790,6 +790,8 @@ static AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Te
   a.kpos = nullptr;
   a.qoff = nullptr;
   a.status = nullptr;
+  a.kblk = nullptr;
+  a.kb_n = 0; a.kb_ng = 1; a.kb_max = 0;
   if (kpos && kpos->defined()) {
     req(*kpos, at::kInt, "kpos");
     TORCH_CHECK(kpos->is_contiguous() && kpos->dim() == 2 && kpos->size(0) == k.size(0) && kpos->size(1) == k.size(1),
@@ -836,8 +838,98 @@ void attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor
   a.sdk_b = dk.stride(0); a.sdk_l = dk.stride(1); a.sdk_h = dk.stride(2);
   a.sdv_b = dv.stride(0); a.sdv_l = dv.stride(1); a.sdv_h = dv.stride(2);
   a.scale = (float)scale;
+  a.dk_acc = a.dv_acc = nullptr;
+  a.kb_lsrc = 0;
   const int rc = attn_bwd_launch(a, (int)hd, stream());
   TORCH_CHECK(rc == 0, "attn_bwd launch failed (", rc, ")");
+}
+
+// Block-indirect keys (NSA selected branch): entry e (query group) attends to the 64-key
+// blocks kblk[e] of source batch e / (E / B) of k / v [B, Lsrc, nh, hd], so the selected
+// blocks are never gathered; kpos [E, 64 kb_n] gives every logical key its absolute
+// position, qoff [E] every entry its first query position.
+static AttnArgs attn_sel_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                              const at::Tensor& lse, double scale, const at::Tensor& kblk, const at::Tensor& kpos,
+                              const at::Tensor& qoff) {
+  const int64_t hd = q.size(3);
+  TORCH_CHECK(hd == 64 || hd == 128, "attention head dim must be 64 or 128, got ", hd);
+  attn_check(q, "q", hd);
+  attn_check(k, "k", hd);
+  attn_check(v, "v", hd);
+  attn_check(o, "o", hd);
+  TORCH_CHECK(k.sizes() == v.sizes() && q.size(2) == k.size(2) && o.sizes() == q.sizes(),
+              "q/o [E, Lq, nh, hd] and k/v [B, Lsrc, nh, hd]");
+  const int64_t E = q.size(0), Bs = k.size(0);
+  TORCH_CHECK(Bs > 0 && E % Bs == 0, "entries must be a multiple of the source batch");
+  TORCH_CHECK(k.size(1) >= 64, "the source must hold at least one 64-key block");
+  req(kblk, at::kInt, "kblk");
+  TORCH_CHECK(kblk.is_contiguous() && kblk.dim() == 2 && kblk.size(0) == E && kblk.size(1) > 0, "kblk [E, nblk] int32");
+  const int64_t Lk = 64 * kblk.size(1);
+  req(kpos, at::kInt, "kpos");
+  TORCH_CHECK(kpos.is_contiguous() && kpos.dim() == 2 && kpos.size(0) == E && kpos.size(1) == Lk, "kpos [E, 64 nblk]");
+  req(qoff, at::kInt, "qoff");
+  TORCH_CHECK(qoff.is_contiguous() && qoff.numel() == E, "qoff [E] int32");
+  req(lse, at::kFloat, "lse");
+  TORCH_CHECK(lse.is_contiguous() && lse.numel() == E * q.size(2) * q.size(1), "lse [E, nh, Lq]");
+  AttnArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.sq_b = q.stride(0); a.sq_l = q.stride(1); a.sq_h = q.stride(2);
+  a.sk_b = k.stride(0); a.sk_l = k.stride(1); a.sk_h = k.stride(2);
+  a.sv_b = v.stride(0); a.sv_l = v.stride(1); a.sv_h = v.stride(2);
+  a.so_b = o.stride(0); a.so_l = o.stride(1); a.so_h = o.stride(2);
+  a.B = (int)E; a.nh = (int)q.size(2); a.Lq = (int)q.size(1); a.Lk = (int)Lk;
+  a.q_offset = 0; a.window = 0;
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.kpos = kpos.data_ptr<int>();
+  a.qoff = qoff.data_ptr<int>();
+  a.status = nullptr;
+  a.kblk = kblk.data_ptr<int>();
+  a.kb_n = (int)kblk.size(1); a.kb_ng = (int)(E / Bs); a.kb_max = (int)(k.size(1) / 64) - 1;
+  return a;
+}
+
+void attn_sel_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, double scale,
+                  at::Tensor kblk, at::Tensor kpos, at::Tensor qoff) {
+  c10::cuda::CUDAGuard guard(q.device());
+  const AttnArgs a = attn_sel_args(q, k, v, o, lse, scale, kblk, kpos, qoff);
+  const int rc = attn_fwd_launch(a, (int)q.size(3), stream());
+  TORCH_CHECK(rc == 0, "attn_sel_fwd launch failed (", rc, ")");
+}
+
+void attn_sel_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, at::Tensor dout,
+                  at::Tensor D, at::Tensor dq_acc, at::Tensor dk_acc, at::Tensor dv_acc, double scale, at::Tensor kblk,
+                  at::Tensor kpos, at::Tensor qoff) {
+  c10::cuda::CUDAGuard guard(q.device());
+  AttnBwdArgs a;
+  a.f = attn_sel_args(q, k, v, o, lse, scale, kblk, kpos, qoff);
+  const int64_t hd = q.size(3);
+  attn_check(dout, "dout", hd);
+  TORCH_CHECK(dout.sizes() == q.sizes(), "dout [E, Lq, nh, hd]");
+  req(D, at::kFloat, "D");
+  req(dq_acc, at::kFloat, "dq_acc");
+  req(dk_acc, at::kFloat, "dk_acc");
+  req(dv_acc, at::kFloat, "dv_acc");
+  TORCH_CHECK(D.is_contiguous() && D.numel() == lse.numel(), "D [E, nh, Lq]");
+  TORCH_CHECK(dq_acc.is_contiguous() && dq_acc.sizes() == q.sizes(), "dq_acc [E, Lq, nh, hd] fp32, contiguous");
+  TORCH_CHECK(dk_acc.is_contiguous() && dk_acc.sizes() == k.sizes() && dv_acc.is_contiguous() &&
+                  dv_acc.sizes() == v.sizes(),
+              "dk_acc / dv_acc [B, Lsrc, nh, hd] fp32, contiguous");
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.sd_b = dout.stride(0); a.sd_l = dout.stride(1); a.sd_h = dout.stride(2);
+  a.D = D.data_ptr<float>();
+  a.dq_acc = dq_acc.data_ptr<float>();
+  a.dk = a.dv = nullptr;
+  a.sdk_b = a.sdk_l = a.sdk_h = a.sdv_b = a.sdv_l = a.sdv_h = 0;
+  a.dk_acc = dk_acc.data_ptr<float>();
+  a.dv_acc = dv_acc.data_ptr<float>();
+  a.kb_lsrc = (int)k.size(1);
+  a.scale = (float)scale;
+  const int rc = attn_bwd_launch(a, (int)hd, stream());
+  TORCH_CHECK(rc == 0, "attn_sel_bwd launch failed (", rc, ")");
 }
 
 void attn_probsum(at::Tensor q, at::Tensor k, at::Tensor lse, at::Tensor imp, double scale, int64_t window,
@@ -1309,6 +1401,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dout"), py::arg("D"), py::arg("dq_acc"), py::arg("dk"), py::arg("dv"), py::arg("scale"),
         py::arg("window"), py::arg("q_offset"), py::arg("kpos") = py::none(), py::arg("qoff") = py::none(),
         "flash attention backward: dk, dv written, dq accumulated into the zeroed fp32 dq_acc (scaled)");
+  m.def("attn_sel_fwd", &attn_sel_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("scale"), py::arg("kblk"), py::arg("kpos"), py::arg("qoff"),
+        "flash attention forward over block-indirect keys: entry e reads the 64-key blocks kblk[e] of source "
+        "batch e / (E / B) (the NSA selected branch without a gather)");
+  m.def("attn_sel_bwd", &attn_sel_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("dout"), py::arg("D"), py::arg("dq_acc"), py::arg("dk_acc"), py::arg("dv_acc"), py::arg("scale"),
+        py::arg("kblk"), py::arg("kpos"), py::arg("qoff"),
+        "its backward: dq into the zeroed fp32 dq_acc, dk / dv added into the zeroed fp32 source-shaped buffers");
   m.def("attn_probsum", &attn_probsum, py::arg("q"), py::arg("k"), py::arg("lse"), py::arg("imp"), py::arg("scale"),
         py::arg("window"), py::arg("q_offset"), py::arg("kpos") = py::none(), py::arg("qoff") = py::none(),
         "head-summed softmax probabilities [B, Lq, Lk] of a finished forward (no gradient)");

@@ -266,6 +266,10 @@ struct AttnArgs {
   const int* kpos;                 // optional [B, Lk] absolute key positions (nullptr: the key index)
   const int* qoff;                 // optional [B] per-entry query offsets (nullptr: q_offset)
   int* status;                     // optional: set to 1 when a bounded wait of the tcgen05 forward timed out
+  // optional block-indirect keys (NSA selection): entry b's key block j (64 keys) is rows
+  // [64 kblk[b][j], 64 kblk[b][j] + 64) of source batch b / kb_ng of k / v; Lk = 64 kb_n
+  const int* kblk;                 // [B, kb_n] int32, or nullptr (indices clamped to [0, kb_max])
+  int kb_n, kb_ng, kb_max;
 };
 struct AttnBwdArgs {
   AttnArgs f;                      // the forward's tensors (o, lse as written by it)
@@ -276,6 +280,10 @@ struct AttnBwdArgs {
   __nv_bfloat16 *dk, *dv;          // [B, Lk, nh, HD] (strided)
   long sdk_b, sdk_l, sdk_h, sdv_b, sdv_l, sdv_h;
   float scale;                     // softmax scale
+  // with block-indirect keys: dK / dV are added (fp32 atomics) into the source-shaped,
+  // contiguous [B / kb_ng, kb_lsrc, nh, HD] buffers instead of dk / dv
+  float *dk_acc, *dv_acc;
+  int kb_lsrc;
 };
 int attn_fwd_launch(const AttnArgs& a, int hd, cudaStream_t st);
 int attn_bwd_launch(const AttnBwdArgs& a, int hd, cudaStream_t st);

@@ -111,14 +111,21 @@ class NSABlock(nn.Module):
         pad = ng * SB - Lq
         impg = torch.nn.functional.pad(imp_s, (0, 0, 0, pad)).reshape(B, ng, SB, nsb).mean(2)
         top = impg.topk(S, dim=-1).indices.clamp(0, max(nsb - 1, 0))                # (B, ng, S)
+        qg = torch.nn.functional.pad(q, (0, 0, 0, 0, 0, pad)).reshape(B, ng, SB, nh, hd)
+        off = torch.arange(S * SB, device=q.device)
+        kpos = top[..., off // SB] * SB + (off % SB)                                  # (B, ng, S*SB)
+        if SB == 64 and nsb >= 1 and kernel_supported(q, k, v):
+            # selection blocks of the kernels' key tile: read in place, no gathered copy
+            from ..ops.attention import flash_attention_blocks
+            qoff = (q_offset + torch.arange(ng, device=q.device) * SB).repeat(B)
+            o = flash_attention_blocks(qg.reshape(B * ng, SB, nh, hd), k, v, top.reshape(B * ng, S),
+                                       kpos.reshape(B * ng, S * SB), qoff, scale)
+            return o.reshape(B, ng * SB, nh, hd)[:, :Lq]
         kb = k[:, :nsb * SB].reshape(B, nsb, SB, nh, hd)
         vb = v[:, :nsb * SB].reshape(B, nsb, SB, nh, hd)
         bidx = torch.arange(B, device=q.device)[:, None, None]
         ksel = kb[bidx, top].reshape(B, ng, S * SB, nh, hd)
         vsel = vb[bidx, top].reshape(B, ng, S * SB, nh, hd)
-        qg = torch.nn.functional.pad(q, (0, 0, 0, 0, 0, pad)).reshape(B, ng, SB, nh, hd)
-        off = torch.arange(S * SB, device=q.device)
-        kpos = top[..., off // SB] * SB + (off % SB)                                  # (B, ng, S*SB)
         if kernel_supported(q, k, v):
             # flash kernels over the gathered blocks: every (batch, group) is one batch entry
             qoff = (q_offset + torch.arange(ng, device=q.device) * SB).repeat(B)

@@ -72,6 +72,51 @@ class _FlashAttn(torch.autograd.Function):
         return dq.to(torch.bfloat16), dk, dv, None, None, None, None, None
 
 
+class _FlashAttnSel(torch.autograd.Function):
+    """Attention of query groups over block-indirect keys (``attn_sel_fwd`` / ``attn_sel_bwd``):
+    the selected key / value blocks are read in place, and their gradients are added back into
+    source-shaped fp32 buffers by the kernel."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, kblk, kpos, qoff, scale):
+        from ._ext import ext
+        q, k, v = _kernel_ready(q), _kernel_ready(k), _kernel_ready(v)
+        E, Lq, nh, hd = q.shape
+        o = torch.empty_like(q, memory_format=torch.contiguous_format)
+        lse = torch.empty(E, nh, Lq, dtype=torch.float32, device=q.device)
+        ext().attn_sel_fwd(q, k, v, o, lse, scale, kblk, kpos, qoff)
+        ctx.save_for_backward(q, k, v, o, lse, kblk, kpos, qoff)
+        ctx.scale = scale
+        ctx.mark_non_differentiable(lse)
+        return o, lse
+
+    @staticmethod
+    def backward(ctx, do, _dlse):
+        from ._ext import ext
+        q, k, v, o, lse, kblk, kpos, qoff = ctx.saved_tensors
+        do = _kernel_ready(do.to(torch.bfloat16))
+        D = torch.empty_like(lse)
+        dq = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+        dk = torch.zeros(k.shape, dtype=torch.float32, device=k.device)
+        dv = torch.zeros(v.shape, dtype=torch.float32, device=v.device)
+        ext().attn_sel_bwd(q, k, v, o, lse, do, D, dq, dk, dv, ctx.scale, kblk, kpos, qoff)
+        return dq.to(torch.bfloat16), dk.to(torch.bfloat16), dv.to(torch.bfloat16), None, None, None, None
+
+
+def flash_attention_blocks(q, k, v, kblk, kpos, qoff, scale):
+    """Query groups over selected 64-key blocks without gathering them.
+
+    q [E, Lq, nh, hd] (E = B x groups), k / v [B, Lsrc, nh, hd]; entry e attends to the key
+    blocks ``kblk[e]`` (int [E, nblk], block j = source rows [64 j, 64 j + 64) of batch
+    e // (E // B)), whose keys sit at the absolute positions ``kpos`` [E, 64 nblk]; its queries
+    start at position ``qoff[e]``.  Block indices are clamped to the source."""
+    nb_max = k.shape[1] // 64 - 1
+    kb = kblk.to(device=q.device, dtype=torch.int32).clamp(0, nb_max).contiguous()
+    kp = kpos.to(device=q.device, dtype=torch.int32).contiguous()
+    qo = qoff.to(device=q.device, dtype=torch.int32).contiguous()
+    return _FlashAttnSel.apply(q, k, v, kb, kp, qo, float(scale))[0]
+
+
 _ENABLED = [True]
 
 

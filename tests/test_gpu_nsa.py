@@ -46,3 +46,35 @@ def test_nsa_block_forward_backward_runs_kernels():
     _ext.reset_launch_count()
     m(torch.randn(2, 500, 256, device="cuda")).sum().backward()
     assert _ext.launch_count() >= 4
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_block_indirect_attention_matches_the_gathered_blocks(hd):
+    """Query groups over selected 64-key blocks read in place (``flash_attention_blocks``)
+    against the same attention over a gathered copy of the blocks: outputs and q / k / v
+    gradients, with blocks shared between groups (their key gradients add up)."""
+    from sigma0_b200.ops.attention import flash_attention, flash_attention_blocks
+    torch.manual_seed(hd)
+    B, nblk, nh, ng, S = 2, 10, 2, 5, 4
+    Lsrc, E = nblk * 64, B * ng
+    k = torch.randn(B, Lsrc, nh, hd, device="cuda").to(torch.bfloat16)
+    v = torch.randn(B, Lsrc, nh, hd, device="cuda").to(torch.bfloat16)
+    q = torch.randn(E, 64, nh, hd, device="cuda").to(torch.bfloat16)
+    top = torch.stack([torch.randperm(nblk)[:S] for _ in range(E)]).cuda()
+    off = torch.arange(S * 64, device="cuda")
+    kpos = top[:, off // 64] * 64 + off % 64
+    qoff = (256 + torch.arange(ng, device="cuda") * 64).repeat(B)
+    scale = hd ** -0.5
+    xs = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    o1 = flash_attention_blocks(xs[0], xs[1], xs[2], top, kpos, qoff, scale)
+    ys = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    src = torch.arange(E, device="cuda") // ng
+    ksel = ys[1].reshape(B, nblk, 64, nh, hd)[src[:, None], top].reshape(E, S * 64, nh, hd)
+    vsel = ys[2].reshape(B, nblk, 64, nh, hd)[src[:, None], top].reshape(E, S * 64, nh, hd)
+    o2 = flash_attention(ys[0], ksel, vsel, scale=scale, kpos=kpos, qoff=qoff)
+    assert _rel(o1, o2) < 1e-2, _rel(o1, o2)
+    g = torch.randn(o2.shape, device="cuda")
+    (o1.float() * g).sum().backward()
+    (o2.float() * g).sum().backward()
+    for name, a, b in zip("qkv", xs, ys):
+        assert _rel(a.grad, b.grad) < 2e-2, (name, _rel(a.grad, b.grad))
