@@ -232,12 +232,17 @@ at::Tensor gemm_ag(const at::Tensor& x, const at::Tensor& wfull, std::vector<int
 }
 
 // SSD implementation: 1 the tcgen05 chunk walkers, 0 the chunk-parallel mma.sync kernels,
-// -1 (default) by occupancy: the walkers run one CTA per (sequence, head), so they are used when
-// there are at least as many (sequence, head) pairs as SMs; smaller batches (a single sequence of
-// the 75m recipe) keep every SM busy with the chunk-parallel kernels instead.
+// -1 (default) by occupancy: the walkers run one CTA per (sequence, head) and the backward one CTA
+// per SM, so they are used when the backward's waves of CTAs keep at least 3/4 of the SMs busy.
+// Measured training steps on one B200: 128 pairs (1 wave) 162.9 vs 173.8 ms with the walkers,
+// 256 pairs (2 waves) the walkers by 3%, 160 pairs (a second wave of 12 CTAs) 407.6 vs 397.8 ms
+// for the chunk-parallel kernels, which also win for a single sequence (32 pairs).
 int g_m3_tc = -1;
 bool m3_walker(const at::Tensor& like, int64_t B, int64_t nh) {
-  return g_m3_tc >= 0 ? g_m3_tc == 1 : B * nh >= num_sms(like);
+  if (g_m3_tc >= 0) return g_m3_tc == 1;
+  const int64_t pairs = B * nh, sms = num_sms(like);
+  const int64_t waves = (pairs + sms - 1) / sms;
+  return 4 * pairs >= 3 * waves * sms;
 }
 
 // Segments per sequence for the walkers: one CTA walks one (sequence, head, segment).  With
