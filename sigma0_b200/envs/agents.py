@@ -40,7 +40,9 @@ Rewards (``MM_REWARDS``), per step and agent, in ticks:
 ``complex``                spooner_asym_damped - lambda |inventory change|
 ``zero_inv``               -|inventory|
 ``pnl_inventory``          change of mark-to-market PnL at the mid (the default)
-and an inventory penalty (``none`` / ``linear`` / ``quadratic``) on top of any of them.
+and an inventory penalty (``none`` / ``linear`` / ``quadratic`` / ``threshold`` / ``exp4``) on
+top of any of them.  The reference price of the PnL terms is the mid after the step, the
+step's average mid (``mid_avg``), the far or the near touch.
 
 Execution action spaces (``EXEC_ACTION_SPACES``): ``sizes`` (a marketable child order of
 a size from a table), ``fixed_quants`` (a pair (aggressive, passive) of size multiples:
@@ -176,6 +178,8 @@ def mm_reward(name: str, *, buy_q, buy_v, sell_q, sell_v, inv_prev, inv, cash, m
     mid0, mid1 = mid0.to(d), mid1.to(d)
     if reference_price == "mid":
         ref_buy = ref_sell = ref = mid1
+    elif reference_price == "mid_avg":       # the step's average mid (before / after the step)
+        ref_buy = ref_sell = ref = (mid0 + mid1) / 2
     elif reference_price == "far_touch":
         ref_buy, ref_sell = best_ask.to(d), best_bid.to(d)
         ref = torch.where(inv > 0, best_bid.to(d), best_ask.to(d))
@@ -183,7 +187,7 @@ def mm_reward(name: str, *, buy_q, buy_v, sell_q, sell_v, inv_prev, inv, cash, m
         ref_buy, ref_sell = best_bid.to(d), best_ask.to(d)
         ref = torch.where(inv > 0, best_ask.to(d), best_bid.to(d))
     else:
-        raise ValueError(f"reference_price is mid, far_touch or near_touch, not {reference_price!r}")
+        raise ValueError(f"reference_price is mid, mid_avg, far_touch or near_touch, not {reference_price!r}")
     rebate = (buy_v + sell_v) / tick * (rebate_bps / 10_000.0)
     buy_pnl = (ref_buy * buy_q - buy_v) / tick
     sell_pnl = (sell_v - ref_sell * sell_q) / tick
@@ -209,7 +213,13 @@ def mm_reward(name: str, *, buy_q, buy_v, sell_q, sell_v, inv_prev, inv, cash, m
     return table[name](), pv
 
 
-def inventory_penalty(kind: str, inv: torch.Tensor, weight: float, size: int) -> torch.Tensor:
+INV_PENALTIES = ("none", "linear", "quadratic", "threshold", "exp4")
+
+
+def inventory_penalty(kind: str, inv: torch.Tensor, weight: float, size: int, threshold: float = 10.0) -> torch.Tensor:
+    """Inventory penalty in quote-size units q = inv / size (the reference's options,
+    ``mm_env.py:2435-2456``): linear -w|q|, quadratic -w q^2, threshold -w q^2 only where
+    |q| > ``threshold``, exp4 -w exp(4 q)."""
     q = inv.double() / size
     if kind == "none":
         return torch.zeros_like(q)
@@ -217,7 +227,36 @@ def inventory_penalty(kind: str, inv: torch.Tensor, weight: float, size: int) ->
         return -weight * q.abs()
     if kind == "quadratic":
         return -weight * q * q
-    raise ValueError(f"inv_penalty is none, linear or quadratic, not {kind!r}")
+    if kind == "threshold":
+        return torch.where(q.abs() > threshold, -weight * q * q, torch.zeros_like(q))
+    if kind == "exp4":
+        return -weight * torch.exp(4.0 * q)
+    raise ValueError(f"inv_penalty is one of {INV_PENALTIES}, not {kind!r}")
+
+
+UNWIND_PRICES = ("none", "mid", "mid_avg", "far_touch")
+
+
+def unwind_fill(kind: str, inv: torch.Tensor, mid0, mid1, best_bid, best_ask, tick: int, penalty_ticks: int = 0):
+    """The artificial end-of-episode trade that flattens ``inv`` (``mm_env.py:2206-2246``):
+    (buy_q, buy_v, sell_q, sell_v) of one fill of |inv| shares at the unwind price -- the
+    last mid, the step's average mid (here the mean of the mids before and after the step)
+    or the far touch -- moved ``penalty_ticks`` against the agent."""
+    zero = torch.zeros_like(inv)
+    if kind == "none":
+        return zero, zero, zero, zero
+    if kind == "mid":
+        p = mid1.long()
+    elif kind == "mid_avg":
+        p = (mid0.long() + mid1.long()) // 2
+    elif kind == "far_touch":
+        p = torch.where(inv > 0, best_bid.long(), best_ask.long())
+    else:
+        raise ValueError(f"unwind_price is one of {UNWIND_PRICES}, not {kind!r}")
+    p = torch.where(inv > 0, p - penalty_ticks * tick, p + penalty_ticks * tick)
+    sell_q = inv.clamp(min=0)
+    buy_q = (-inv).clamp(min=0)
+    return buy_q, buy_q * p, sell_q, sell_q * p
 
 
 EXEC_SIZES = (0, 50, 100, 200, 400)

@@ -18,7 +18,13 @@ Per step each environment:
 
 ``MarketMakingEnv`` quotes one bid and one ask per step at ``mid -/+ offset``
 ticks (discrete offsets), replacing the previous quotes; reward = change of
-mark-to-market PnL minus an inventory penalty.  ``ExecutionEnv`` must buy (or
+mark-to-market PnL minus an inventory penalty.  The reference's other options are
+keywords (or its config field names through ``from_reference_config``): the action
+spaces and rewards of ``envs/agents.py``, the end-of-episode unwind of the remaining
+inventory at the mid / average mid / far touch with a penalty in ticks, auto-liquidation
+above an inventory threshold, reward clipping, the market-share volume bonus, zero
+reward while the spread is extreme, and the ``basic`` / ``engineered`` observation
+vectors (``agent_observation``).  ``ExecutionEnv`` must buy (or
 sell) a target quantity within the episode; actions choose a child-order size,
 sent as a marketable order; reward = negative implementation shortfall against
 the arrival mid.  ``MultiAgentEnv`` runs several market makers and an executor
@@ -201,19 +207,72 @@ class MarketMakingEnv(_Quoting, BaseLOBEnv):
 
     OFFSETS = (1, 2, 3, 5, 8)
 
+    OBS_SPACES = ("basic", "engineered", "features")
+
     def __init__(self, *a, quote_size: int = 100, inventory_penalty: float = 0.01, n_mm: int = 1,
                  action_space: str = "offsets", reward_function: str = "pnl_inventory", inv_penalty: str = "linear",
                  reference_price: str = "mid", eta: float = 0.5, gamma: float = 1.0, lam: float = 0.0,
-                 rebate_bps: float = 0.0, n_levels: int = 3, avst_k: float = 1.5, avst_var: float = 2.0, **kw):
-        from .agents import MM_ACTION_SPACES, MM_REWARDS
+                 rebate_bps: float = 0.0, n_levels: int = 3, avst_k: float = 1.5, avst_var: float = 2.0,
+                 inv_threshold: float = 10.0, unwind_price: str = "none", unwind_penalty: int = 0,
+                 clip_reward: bool = False, volume_bonus: str = "none", exclude_extreme_spreads: bool = False,
+                 auto_liquidate_threshold: int = 0, auto_liquidate_alpha: float = 1.0,
+                 observation_space: str = "features", normalize: bool = True, **kw):
+        from .agents import INV_PENALTIES, MM_ACTION_SPACES, MM_REWARDS, UNWIND_PRICES
         super().__init__(*a, n_agents=n_mm, **kw)
         if action_space not in MM_ACTION_SPACES or reward_function not in MM_REWARDS:
             raise ValueError(f"action_space in {MM_ACTION_SPACES}, reward_function in {MM_REWARDS}")
+        if inv_penalty not in INV_PENALTIES or unwind_price not in UNWIND_PRICES:
+            raise ValueError(f"inv_penalty in {INV_PENALTIES}, unwind_price in {UNWIND_PRICES}")
+        if volume_bonus not in ("none", "market_share") or observation_space not in self.OBS_SPACES:
+            raise ValueError(f"volume_bonus in ('none', 'market_share'), observation_space in {self.OBS_SPACES}")
         self.size, self.pen, self.n_mm = quote_size, inventory_penalty, n_mm
         self.tids = [1000 + i for i in range(n_mm)]
         self.space, self.reward_fn, self.inv_pen_kind = action_space, reward_function, inv_penalty
         self.ref_price, self.eta, self.gamma, self.lam, self.rebate = reference_price, eta, gamma, lam, rebate_bps
         self.n_levels, self.avst_k, self.avst_var = n_levels, avst_k, avst_var
+        # reward shaping and episode-end options of the reference's market-making config
+        # (jaxob_config.py MarketMaking_EnvironmentConfig; mm_env.py:2206-2246 the unwind,
+        # :2435-2473 penalties, clipping, the market-share bonus, extreme spreads)
+        self.inv_threshold, self.unwind, self.unwind_pen = inv_threshold, unwind_price, unwind_penalty
+        self.clip, self.vol_bonus, self.no_extreme = clip_reward, volume_bonus, exclude_extreme_spreads
+        # auto-liquidation (mm_env.py:1086-1094): above |inventory| > threshold the quotes are replaced
+        # by an immediate-or-cancel order of alpha x inventory against the position
+        self.liq_thr, self.liq_alpha = auto_liquidate_threshold, auto_liquidate_alpha
+        self.obs_space, self.normalize = observation_space, normalize
+
+    # the reference's MarketMaking_EnvironmentConfig field -> keyword here
+    # (src/matching_engine/jaxob/jaxob_config.py:58-130)
+    REFERENCE_CONFIG = {
+        "action_space": "action_space", "reward_function": "reward_function", "inv_penalty": "inv_penalty",
+        "inv_penalty_lambda": "inventory_penalty", "inv_penalty_threshold": "inv_threshold",
+        "reference_price": "reference_price", "unwind_price": "unwind_price",
+        "unwind_price_penalty": "unwind_penalty", "clip_reward": "clip_reward",
+        "volume_traded_bonus": "volume_bonus", "exclude_extreme_spreads": "exclude_extreme_spreads",
+        "auto_liquidate_threshold": "auto_liquidate_threshold", "auto_liquidate_alpha": "auto_liquidate_alpha",
+        "observation_space": "observation_space", "normalize": "normalize", "inventoryPnL_eta": "eta",
+        "inventoryPnL_gamma": "gamma", "unrealizedPnL_lambda": "lam", "rebate_bps": "rebate_bps",
+        "avst_k_parameter": "avst_k", "avst_var_parameter": "avst_var", "fixed_quant_value": "quote_size",
+    }
+
+    @classmethod
+    def from_reference_config(cls, windows, n_envs: int, cfg: Dict, **kw):
+        """Build from the reference's market-making config (a dict of its field names).  Fields
+        without a counterpart here (debug and plotting switches, ``time_delay_obs_act``, the
+        message-token observation spaces) are returned unused in ``env.unused_config``."""
+        args, unused = {}, {}
+        for k, v in cfg.items():
+            if k in cls.REFERENCE_CONFIG:
+                args[cls.REFERENCE_CONFIG[k]] = v
+            else:
+                unused[k] = v
+        if args.get("reference_price") == "best_bid_ask":
+            args["reference_price"] = "far_touch"
+        if args.get("observation_space") not in (None,) + cls.OBS_SPACES:
+            unused["observation_space"] = args.pop("observation_space")
+        args.update(kw)
+        env = cls(windows, n_envs, **args)
+        env.unused_config = unused
+        return env
 
     def reset(self, idx=None):
         obs = super().reset(idx)
@@ -235,42 +294,86 @@ class MarketMakingEnv(_Quoting, BaseLOBEnv):
         from .agents import mm_orders
         rows = []
         for a in range(self.n_mm):
-            st = self._state(self.inv[:, a])
+            inv = self.inv[:, a]
+            st = self._state(inv)
             if mid is not None:
                 st["mid"] = mid
             orders, market = mm_orders(self.space, actions[:, a], st, self.size, self.tick, self.n_levels,
                                        self.avst_k, self.avst_var)
-            rows += self._order_messages(a, self.tids[a], orders,
-                                         market if self.space == "directional_trading" else None)
+            if self.space != "directional_trading":
+                market = torch.zeros(self.n, 2, dtype=torch.long) if self.liq_thr > 0 else None
+            if self.liq_thr > 0:
+                liq = inv.abs() > self.liq_thr
+                qty = (self.liq_alpha * inv.abs().double()).round().long()
+                orders = torch.where(liq[:, None, None], torch.zeros_like(orders), orders)
+                market = torch.where(liq[:, None], torch.stack([-inv.sign(), qty], -1), market)
+            rows += self._order_messages(a, self.tids[a], orders, market)
         return torch.stack(rows, 1)
 
-    def _rewards(self, trades, mid0, obs):
-        from .agents import agent_trades, inventory_penalty, mm_reward, touch
+    def agent_observation(self, obs: Dict[str, torch.Tensor]) -> torch.Tensor:
+        """(n, n_mm, d) observation vectors of the market makers (``observation_space``):
+        ``basic`` the inventory, ``engineered`` the inventory and the spread (price units),
+        each as (x - mean) / scale with the reference's constants when ``normalize``
+        (``mm_env.py:2881-2990``: inventory / 10, spread / 1e4; keys in sorted order), and
+        ``features`` the book features of ``features()``."""
+        if self.obs_space == "features":
+            return features(obs, self.n_mm)
+        inv = obs["inventory"].double()
+        cols = [inv / 10.0 if self.normalize else inv]
+        if self.obs_space == "engineered":
+            spread = (obs["spread"] * self.tick).double()[:, None].expand(-1, self.n_mm)
+            cols.append(spread / 1e4 if self.normalize else spread)
+        return torch.stack(cols, -1).float()
+
+    def _rewards(self, trades, mid0, obs, spread0=None):
+        from .agents import agent_trades, inventory_penalty, mm_reward, touch, unwind_fill
         bb, ba, _ = touch(obs["l2"], self.tick)
         rew = torch.zeros(self.n, self.n_mm, dtype=torch.float64)
+        valid = trades[..., 0] >= 0
+        step_volume = torch.where(valid, trades[..., 1].abs(), torch.zeros_like(trades[..., 1])).sum(-1)
+        self.unwound = torch.zeros(self.n, self.n_mm, dtype=torch.long)
         for a, tid in enumerate(self.tids):
             bq, bv, sq, sv = agent_trades(trades, tid)
+            traded = bq + sq
             inv_prev = self.inv[:, a].clone()
+            if self.unwind != "none" and self.done:
+                # the last step flattens what is left with one artificial fill
+                ubq, ubv, usq, usv = unwind_fill(self.unwind, inv_prev + bq - sq, mid0, obs["mid"], bb, ba, self.tick,
+                                                 self.unwind_pen)
+                bq, bv, sq, sv = bq + ubq, bv + ubv, sq + usq, sv + usv
+                self.unwound[:, a] = usq - ubq
             self.inv[:, a] += bq - sq
             self.cash[:, a] += (sv - bv).double()
             if self.reward_fn == "pnl_inventory":
                 pnl = self.cash[:, a] + self.inv[:, a].double() * obs["mid"].double()
-                rew[:, a] = (pnl - self.pnl_prev[:, a]) / self.tick - self.pen * self.inv[:, a].double().abs()
+                r = (pnl - self.pnl_prev[:, a]) / self.tick - self.pen * self.inv[:, a].double().abs()
                 self.pnl_prev[:, a] = pnl
-                continue
-            r, pv = mm_reward(self.reward_fn, buy_q=bq, buy_v=bv, sell_q=sq, sell_v=sv, inv_prev=inv_prev,
-                              inv=self.inv[:, a], cash=self.cash[:, a], mid0=mid0, mid1=obs["mid"], best_bid=bb,
-                              best_ask=ba, tick=self.tick, reference_price=self.ref_price, eta=self.eta,
-                              gamma=self.gamma, lam=self.lam, rebate_bps=self.rebate, pv_prev=self.pv_prev[:, a])
-            self.pv_prev[:, a] = pv
-            rew[:, a] = r + inventory_penalty(self.inv_pen_kind, self.inv[:, a], self.pen, self.size)
+            else:
+                r, pv = mm_reward(self.reward_fn, buy_q=bq, buy_v=bv, sell_q=sq, sell_v=sv, inv_prev=inv_prev,
+                                  inv=self.inv[:, a], cash=self.cash[:, a], mid0=mid0, mid1=obs["mid"], best_bid=bb,
+                                  best_ask=ba, tick=self.tick, reference_price=self.ref_price, eta=self.eta,
+                                  gamma=self.gamma, lam=self.lam, rebate_bps=self.rebate, pv_prev=self.pv_prev[:, a])
+                self.pv_prev[:, a] = pv
+                r = r + inventory_penalty(self.inv_pen_kind, self.inv[:, a], self.pen, self.size, self.inv_threshold)
+            if self.clip:
+                r = r.clamp(-10000.0, 10000.0)
+            if self.vol_bonus == "market_share":
+                share = traded.double() / step_volume.clamp(min=1).double()
+                r = r + r.abs() * share
+            if self.no_extreme:
+                # no reward while the spread exceeds 10% of the mid (before or after the step)
+                wide = (obs["spread"] * self.tick).double() > 0.1 * obs["mid"].double()
+                if spread0 is not None:
+                    wide |= (spread0 * self.tick).double() > 0.1 * mid0.double()
+                r = torch.where(wide, torch.zeros_like(r), r)
+            rew[:, a] = r
         return rew
 
     def step(self, actions: torch.Tensor):
         obs0 = self.observe()
         trades, _ = self.step_messages(self.action_messages(actions, obs0["mid"]))
         obs = self.observe()
-        rew = self._rewards(trades, obs0["mid"], obs)          # updates inventory and cash first
+        rew = self._rewards(trades, obs0["mid"], obs, obs0["spread"])   # updates inventory and cash first
         return self._obs(obs), rew, self.done
 
 
@@ -352,7 +455,7 @@ class MultiAgentEnv(MarketMakingEnv):
             msgs = torch.cat([msgs, m], 1)
         trades, _ = self.step_messages(msgs)
         obs = self.observe()
-        rew = self._rewards(trades, obs0["mid"], obs)
+        rew = self._rewards(trades, obs0["mid"], obs, obs0["spread"])
         return self._obs(obs), rew, self.done
 
 

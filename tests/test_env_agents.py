@@ -111,3 +111,80 @@ def test_agent_trades_splits_buys_and_sells():
     tr[0, 2] = -1
     bq, bv, sq, sv = agent_trades(tr, 7)
     assert (int(bq), int(bv), int(sq), int(sv)) == (4, 404, 5, 500)
+
+
+def test_episode_end_unwind_flattens_the_inventory_at_the_unwind_price():
+    """unwind_price: the last step adds one artificial fill of the remaining inventory at the
+    chosen price, moved unwind_penalty ticks against the agent."""
+    from sigma0_b200.envs.agents import unwind_fill
+    t = lambda *v: torch.tensor(v, dtype=torch.long)
+    bq, bv, sq, sv = unwind_fill("far_touch", t(300, -200, 0), t(10000, 10000, 10000), t(10100, 10100, 10100),
+                                 t(10000, 10000, 10000), t(10200, 10200, 10200), 100, penalty_ticks=2)
+    assert sq.tolist() == [300, 0, 0] and bq.tolist() == [0, 200, 0]
+    assert sv[0] == 300 * (10000 - 200) and bv[1] == 200 * (10200 + 200)
+    _, _, sq, sv = unwind_fill("mid_avg", t(10), t(10000), t(10200), t(0), t(0), 100)
+    assert sv[0] == 10 * 10100
+    env = MarketMakingEnv(_windows(), n_envs=3, msgs_per_step=5, seed=3, action_space="directional_trading",
+                          reward_function="spooner", unwind_price="mid")
+    env.reset()
+    for k in range(env.max_steps):
+        obs, rew, done = env.step(torch.ones(3, 1, dtype=torch.long) if k < 2 else torch.zeros(3, 1, dtype=torch.long))
+        assert torch.isfinite(rew).all()
+    assert done and (obs["inventory"] == 0).all() and (env.unwound[:, 0] > 0).all()
+
+
+def test_auto_liquidation_replaces_the_quotes_by_an_order_against_the_position():
+    env = MarketMakingEnv(_windows(), n_envs=2, msgs_per_step=1, seed=2, action_space="fixed_quants",
+                          auto_liquidate_threshold=50, auto_liquidate_alpha=0.5)
+    env.reset()
+    env.inv[:, 0] = torch.tensor([120, 10])
+    msgs = env.action_messages(torch.zeros(2, 1, dtype=torch.long))
+    new = msgs[..., 0] == 1
+    assert int(new[0].sum()) == 0 and int(new[1].sum()) > 0          # env 0 quotes nothing
+    mkt = msgs[0][msgs[0, :, 0] == 4]
+    assert mkt.shape[0] == 1 and int(mkt[0, 2]) == 60 and int(mkt[0, 1]) == 1   # sell 60 against the bids
+    assert int((msgs[1, :, 0] == 4).sum()) == 0
+
+
+def test_reward_shaping_options_and_observation_spaces():
+    from sigma0_b200.envs.agents import inventory_penalty
+    q = torch.tensor([0, 500, 1500])
+    assert inventory_penalty("threshold", q, 1.0, 100, threshold=10.0).tolist() == [0.0, 0.0, -225.0]
+    assert inventory_penalty("exp4", torch.tensor([0]), 2.0, 100).tolist() == [-2.0]
+    rng = torch.Generator().manual_seed(1)
+    for kw in (dict(clip_reward=True), dict(volume_bonus="market_share"), dict(exclude_extreme_spreads=True)):
+        env = MarketMakingEnv(_windows(), n_envs=2, msgs_per_step=5, seed=4, action_space="spread_skew",
+                              reward_function="spooner", **kw)
+        env.reset()
+        for _ in range(3):
+            _, rew, _ = env.step(_action("spread_skew", 2, rng)[:, None])
+            assert torch.isfinite(rew).all()
+            if "clip_reward" in kw:
+                assert rew.abs().max() <= 10000
+    env = MarketMakingEnv(_windows(), n_envs=2, msgs_per_step=5, seed=4, observation_space="engineered")
+    obs = env.reset()
+    obs["inventory"][:, 0] = torch.tensor([20, -30])
+    v = env.agent_observation(obs)
+    assert v.shape == (2, 1, 2) and v[:, 0, 0].tolist() == [2.0, -3.0]
+    assert torch.allclose(v[:, 0, 1].double(), (obs["spread"] * env.tick).double() / 1e4)
+    env.obs_space = "basic"
+    assert env.agent_observation(obs).shape == (2, 1, 1)
+
+
+def test_market_maker_from_the_reference_config_names():
+    cfg = {"action_space": "spread_skew", "reward_function": "spooner_asym_damped2", "inv_penalty": "threshold",
+           "inv_penalty_lambda": 0.5, "inv_penalty_threshold": 3.0, "unwind_price": "far_touch",
+           "unwind_price_penalty": 5, "reference_price": "mid_avg", "inventoryPnL_eta": 0.6,
+           "inventoryPnL_gamma": 0.5, "rebate_bps": 10.0, "clip_reward": True, "debug_mode": False,
+           "observation_space": "messages"}
+    env = MarketMakingEnv.from_reference_config(_windows(), 2, cfg, msgs_per_step=5, seed=1)
+    assert (env.space, env.reward_fn, env.inv_pen_kind, env.unwind, env.unwind_pen) == \
+        ("spread_skew", "spooner_asym_damped2", "threshold", "far_touch", 5)
+    assert env.pen == 0.5 and env.eta == 0.6 and env.clip and env.ref_price == "mid_avg"
+    assert set(env.unused_config) == {"debug_mode", "observation_space"}
+    env.reset()
+    rng = torch.Generator().manual_seed(0)
+    for _ in range(env.max_steps):
+        _, rew, done = env.step(_action("spread_skew", 2, rng)[:, None])
+        assert torch.isfinite(rew).all()
+    assert done
