@@ -48,10 +48,12 @@ Execution action spaces (``EXEC_ACTION_SPACES``): ``sizes`` (a marketable child 
 a size from a table), ``fixed_quants`` (a pair (aggressive, passive) of size multiples:
 marketable at the far touch, resting at the near touch), ``fixed_quants_1msg`` (one order,
 action picks size and aggressiveness), ``fixed_prices`` (sizes at the far touch, the mid,
-the near touch and one tick behind it), ``simplest_case`` (wait or take one clip at the far
-touch) and ``twap`` (the action is ignored: target / steps at the far touch every step).
+the near touch and one tick behind it), ``fixed_quants_complex`` (the reference's 13-action
+ladder: nothing, or 1, 2 or 5 clips at one of those four prices), ``simplest_case`` (wait or
+take one clip at the far touch) and ``twap`` (the action is ignored: target / steps at the far touch every step).
 Execution rewards: ``slippage`` (negative shortfall against the arrival mid per share of
-the target) and ``vwap`` (the reference's advantage over the market's VWAP of the step
+the target), the reference's ``normal``, ``finish_fast`` and ``simplest_case`` (see
+``exec_reward``) and ``vwap`` (the reference's advantage over the market's VWAP of the step
 plus lambda times the drift of that VWAP from the arrival price).
 """
 from __future__ import annotations
@@ -65,8 +67,9 @@ MM_ACTION_SPACES = ("offsets", "fixed_quants", "fixed_prices", "AvSt", "bobStrat
 MM_REWARDS = ("pnl_inventory", "portfolio_value", "delta_portfolio_value", "buy_sell_pnl", "spooner",
               "spooner_damped", "spooner_asym_damped", "spooner_asym_damped2", "spooner_scaled", "complex",
               "zero_inv")
-EXEC_ACTION_SPACES = ("sizes", "fixed_quants", "fixed_quants_1msg", "fixed_prices", "simplest_case", "twap")
-EXEC_REWARDS = ("slippage", "vwap")
+EXEC_ACTION_SPACES = ("sizes", "fixed_quants", "fixed_quants_1msg", "fixed_prices", "fixed_quants_complex",
+                      "simplest_case", "twap")
+EXEC_REWARDS = ("slippage", "vwap", "normal", "finish_fast", "simplest_case")
 
 OFFSETS = (1, 2, 3, 5, 8)
 FIXED_QUANTS = ((1, 1), (2, 1), (1, 2), (2, 2), (1, 0), (0, 1), (2, 0), (0, 2))
@@ -262,19 +265,26 @@ def unwind_fill(kind: str, inv: torch.Tensor, mid0, mid1, best_bid, best_ask, ti
 EXEC_SIZES = (0, 50, 100, 200, 400)
 EXEC_QUANTS = ((0, 0), (1, 0), (0, 1), (1, 1), (2, 0), (0, 2))
 EXEC_1MSG = ((0, 0), (1, 1), (2, 1), (1, 0), (2, 0))          # (size multiple, aggressive)
+# the 13-action ladder (exec_env.py:838-932): nothing, then the far touch / the mid / the near
+# touch / one level behind it at 1, 2 and 5 clips -- (level, multiple)
+EXEC_COMPLEX = ((0, 0),) + tuple((lvl, m) for m in (1, 2, 5) for lvl in range(4))
 
 
 def exec_orders(space: str, action: torch.Tensor, st: Dict[str, torch.Tensor], remaining: torch.Tensor,
-                clip: int, steps_left: int, sell: bool, tick: int):
+                clip: int, steps_left: int, sell, tick: int):
     """(resting orders (n, K, 3), marketable qty (n,)) of an executor working ``remaining``
-    shares; the far touch is the price that trades now (the ask for a buyer)."""
+    shares; the far touch is the price that trades now (the ask for a buyer).  ``sell`` is a
+    bool or a per-environment bool tensor."""
     bb, ba, mid = st["best_bid"], st["best_ask"], st["mid"]
-    far, near = (bb, ba) if sell else (ba, bb)
-    side = -1 if sell else 1
+    sell = torch.as_tensor(sell, dtype=torch.bool).expand(mid.shape)
+    near = torch.where(sell, ba, bb)
+    side = torch.where(sell, -1, 1)
     behind = near - side * tick                     # one tick less aggressive than the near touch
     one, zero = torch.ones_like(mid), torch.zeros_like(mid)
     a = action.long()
     take = zero.clone()
+    # the mid on the tick grid: floored for a buyer, rounded up for a seller
+    mid_px = torch.where(sell, -((-mid) // tick) * tick, (mid // tick) * tick)
     if space == "sizes":
         take = torch.tensor(EXEC_SIZES)[a]
         orders = _rows((zero, zero, zero))
@@ -289,9 +299,17 @@ def exec_orders(space: str, action: torch.Tensor, st: Dict[str, torch.Tensor], r
         orders = _rows((one * side, near, torch.where(t[:, 1] == 1, zero, q)))
     elif space == "fixed_prices":
         take = a[:, 0] * clip
-        mid_px = (mid // tick) * tick if not sell else -((-mid) // tick) * tick
         orders = _rows((one * side, mid_px, a[:, 1] * clip), (one * side, near, a[:, 2] * clip),
                        (one * side, behind, a[:, 3] * clip))
+    elif space == "fixed_quants_complex":
+        t = torch.tensor(EXEC_COMPLEX)[a]
+        lvl, q = t[:, 0], t[:, 1] * clip
+        # an order larger than what is left sends all of it to the far touch
+        over = q > remaining
+        take = torch.where(over, remaining, torch.where(lvl == 0, q, zero))
+        rest = torch.where(over | (lvl == 0), zero, q)
+        price = torch.where(lvl == 1, mid_px, torch.where(lvl == 2, near, behind))
+        orders = _rows((one * side, price, rest))
     elif space == "simplest_case":
         take = torch.where(a == 1, one * clip, zero)
         orders = _rows((zero, zero, zero))
@@ -310,13 +328,30 @@ def exec_orders(space: str, action: torch.Tensor, st: Dict[str, torch.Tensor], r
     return orders, take
 
 
-def exec_reward(name: str, *, filled, value, market_q, market_v, arrival, target: int, sell: bool, tick: int,
-                lam: float = 1.0):
+def exec_reward(name: str, *, filled, value, market_q, market_v, arrival, target: int, sell, tick: int,
+                lam: float = 1.0, remaining=None, mid_avg=None, scaling: float = 1.0):
     """Reward of the executor's fills of the step: ``filled`` shares for ``value`` (sum of
-    price x qty); ``market_q`` / ``market_v`` the other traders' volume and value (VWAP)."""
+    price x qty); ``market_q`` / ``market_v`` the other traders' volume and value (VWAP).
+
+    The reference's own rewards (``exec_env.py:1511-1758``, divided by ``scaling``, its
+    reward_scaling_quo): ``normal`` = advantage over the other traders' VWAP plus ``lam`` x
+    the drift of that VWAP from the arrival price, in ticks x shares (the VWAP falls back
+    to the step's average mid ``mid_avg`` when nobody else traded); ``finish_fast`` =
+    -(shares left after the step); ``simplest_case`` = the fills' price improvement over the
+    arrival price, in price units x shares."""
     d = torch.float64
     filled, value, arrival = filled.to(d), value.to(d), arrival.to(d)
-    sgn = -1.0 if sell else 1.0
+    sgn = torch.where(torch.as_tensor(sell, dtype=torch.bool).expand(filled.shape), -1.0, 1.0).to(d)
+    if name == "normal":
+        fb = (mid_avg if mid_avg is not None else arrival).to(d)
+        vwap = torch.where(market_q > 0, market_v.to(d) / market_q.to(d).clamp(min=1), fb) // tick
+        advantage = -sgn * (value / tick - vwap * filled)
+        drift = -sgn * filled * (vwap - arrival // tick)
+        return (advantage + lam * drift) / scaling
+    if name == "finish_fast":
+        return -remaining.to(d).abs() / scaling
+    if name == "simplest_case":
+        return -sgn * (value - arrival * filled) / scaling
     if name == "slippage":
         avg = value / filled.clamp(min=1)
         short = (avg - arrival) * sgn / tick

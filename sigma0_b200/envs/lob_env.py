@@ -378,60 +378,109 @@ class MarketMakingEnv(_Quoting, BaseLOBEnv):
 
 
 class ExecutionEnv(_Quoting, BaseLOBEnv):
-    """Buy (side=1) or sell (side=0) ``target`` shares before the episode ends.
-    ``action_space`` / ``reward_function`` pick an execution builder / reward of
+    """Buy or sell ``target`` shares before the episode ends (``task``: ``buy``, ``sell`` or
+    ``random`` -- a side drawn per environment at every reset; default from ``side``, 1 buy
+    / 0 sell).  ``action_space`` / ``reward_function`` pick an execution builder / reward of
     ``envs/agents.py``; the default sends a marketable child order of a size from a table
-    and is rewarded with the negative shortfall against the arrival mid.  The last step
-    sweeps what is left."""
+    and is rewarded with the negative shortfall against the arrival mid.  At the last step
+    (``end_fn``) either a marketable order sweeps what is left (``sweep``), or the rest is
+    booked as one artificial fill at the reference price moved ``doom_price_penalty`` ticks
+    against the agent (``unwind``: the step's average mid or the far touch, as the
+    reference's ``exec_env.py:1519-1560``).  ``self.info`` holds the step's statistics
+    (shares left, the unwound quantity, the other traders' VWAP, advantage, drift and their
+    running means over the episode)."""
 
     SIZES = (0, 50, 100, 200, 400)
 
     def __init__(self, *a, target: int = 1000, side: int = 1, action_space: str = "sizes",
-                 reward_function: str = "slippage", clip: int = 100, lam: float = 1.0, **kw):
+                 reward_function: str = "slippage", clip: int = 100, lam: float = 1.0, task: Optional[str] = None,
+                 end_fn: str = "sweep", reference_price: str = "mid", doom_price_penalty: int = 5,
+                 reward_scaling: float = 1.0, **kw):
         from .agents import EXEC_ACTION_SPACES, EXEC_REWARDS
         super().__init__(*a, n_agents=1, **kw)
         if action_space not in EXEC_ACTION_SPACES or reward_function not in EXEC_REWARDS:
             raise ValueError(f"action_space in {EXEC_ACTION_SPACES}, reward_function in {EXEC_REWARDS}")
-        self.target, self.side, self.tid = target, side, 2000
+        task = task or ("buy" if side == 1 else "sell")
+        if task not in ("buy", "sell", "random") or end_fn not in ("sweep", "unwind") or \
+                reference_price not in ("mid", "far_touch"):
+            raise ValueError("task in (buy, sell, random), end_fn in (sweep, unwind), reference_price in (mid, far_touch)")
+        self.target, self.side, self.tid, self.task = target, side, 2000, task
         self.space, self.reward_fn, self.clip, self.lam = action_space, reward_function, clip, lam
+        self.end_fn, self.ref_price, self.doom_pen, self.scaling = end_fn, reference_price, doom_price_penalty, \
+            reward_scaling
 
     def reset(self, idx=None):
         o = super().reset(idx)
+        if self.task == "random":
+            self.sell = torch.from_numpy(self.rng.integers(0, 2, size=self.n).astype(bool))
+        else:
+            self.sell = torch.full((self.n,), self.task == "sell", dtype=torch.bool)
         self.done_qty = torch.zeros(self.n, dtype=torch.long)
         self.cash = torch.zeros(self.n, dtype=torch.float64)
         self.arrival = o["mid"].clone()
         self._init_live(1, 3)
+        z = lambda: torch.zeros(self.n, dtype=torch.float64)
+        self.info = {"vwap_rm": z(), "slippage_rm": z(), "advantage_rm": z(), "drift_rm": z()}
         o["remaining"] = torch.full((self.n,), self.target)
+        o["is_sell"] = self.sell.clone()
         return o
 
     def step(self, actions: torch.Tensor):
         """actions: (n,) indices, or (n, 4) sizes for ``fixed_prices``."""
-        from .agents import agent_trades, exec_orders, exec_reward
-        sell = self.side != 1
+        from .agents import agent_trades, exec_orders, exec_reward, touch
+        sell = self.sell
         rem = (self.target - self.done_qty).clamp(min=0)
         st = self._state(self.done_qty)
         steps_left = self.max_steps - self.t
         orders, take = exec_orders(self.space, actions, st, rem, self.clip, steps_left, sell, self.tick)
-        if self.t == self.max_steps - 1:
+        last = self.t == self.max_steps - 1
+        if last and self.end_fn == "sweep":
             take = rem                                    # the last step sweeps what is left
             orders = torch.zeros_like(orders)
-        sgn = -1 if sell else 1
-        market = torch.stack([torch.full_like(take, sgn), take], -1)
+        sgn = torch.where(sell, -1, 1)
+        market = torch.stack([sgn * (take > 0), take], -1)
+        mid0 = st["mid"]
         trades, _ = self.step_messages(torch.stack(self._order_messages(0, self.tid, orders, market, 50), 1))
         bq, bv, sq, sv = agent_trades(trades, self.tid)
-        filled, value = (sq, sv) if sell else (bq, bv)
+        filled, value = torch.where(sell, sq, bq), torch.where(sell, sv, bv)
+        o = self.observe()
+        bb, ba, _ = touch(o["l2"], self.tick)
+        mid_avg = (mid0 + o["mid"]) // 2
+        unwound = torch.zeros_like(filled)
+        if last and self.end_fn == "unwind":
+            left = (rem - filled).clamp(min=0)
+            pen = self.doom_pen * self.tick
+            if self.ref_price == "mid":
+                px = torch.where(sell, mid_avg - pen, mid_avg + pen)
+            else:
+                px = torch.where(sell, bb - pen, ba + pen)
+            px = px // self.tick * self.tick
+            unwound = left
+            filled, value = filled + left, value + left * px
         self.done_qty += filled
-        self.cash += (sv - bv).double()
-        # the rest of the market in this step (its VWAP for the vwap reward)
+        self.cash += torch.where(sell, value, -value).double()
+        # the rest of the market in this step (its VWAP for the vwap rewards)
         valid = trades[..., 0] >= 0
         mine = (trades[..., 6] == self.tid) | (trades[..., 7] == self.tid)
         other = valid & ~mine
         oq = torch.where(other, trades[..., 1].abs(), torch.zeros_like(trades[..., 1])).long()
         mq, mv = oq.sum(-1), (oq * trades[..., 0].long()).sum(-1)
-        o = self.observe()
+        left = (self.target - self.done_qty).clamp(min=0)
         rew = exec_reward(self.reward_fn, filled=filled, value=value, market_q=mq, market_v=mv,
-                          arrival=self.arrival, target=self.target, sell=sell, tick=self.tick, lam=self.lam)
+                          arrival=self.arrival, target=self.target, sell=sell, tick=self.tick, lam=self.lam,
+                          remaining=left, mid_avg=mid_avg, scaling=self.scaling)
+        # step statistics and their running means (exec_env.py:1700-1760)
+        d = torch.float64
+        sg = torch.where(sell, 1.0, -1.0).to(d)
+        vwap = torch.where(mq > 0, mv.to(d) / mq.clamp(min=1).to(d), mid_avg.to(d)) / self.tick
+        adv = sg * (value.to(d) / self.tick - vwap * filled.to(d))
+        drift = sg * filled.to(d) * (vwap - self.arrival.to(d) / self.tick)
+        k = float(self.t)
+        for key, v in (("vwap_rm", vwap), ("advantage_rm", adv), ("drift_rm", drift), ("slippage_rm", adv + drift)):
+            self.info[key] = self.info[key] + (v - self.info[key]) / k
+        self.info.update(quant_left=left, doom_quant=unwound, p_vwap=vwap, advantage=adv, drift=drift)
         o["remaining"] = self.target - self.done_qty
+        o["is_sell"] = sell.clone()
         return o, rew, self.done
 
 

@@ -84,7 +84,7 @@ def test_every_execution_action_space_completes_the_target(space):
             act = torch.randint(0, 2, (3, 4), generator=rng)
         else:
             act = torch.randint(0, {"sizes": 5, "fixed_quants": 6, "fixed_quants_1msg": 5, "simplest_case": 2,
-                                    "twap": 1}[space], (3,), generator=rng)
+                                    "twap": 1, "fixed_quants_complex": 13}[space], (3,), generator=rng)
         obs, rew, done = env.step(act)
         assert torch.isfinite(rew).all()
     assert done
@@ -188,3 +188,29 @@ def test_market_maker_from_the_reference_config_names():
         _, rew, done = env.step(_action("spread_skew", 2, rng)[:, None])
         assert torch.isfinite(rew).all()
     assert done
+
+
+def test_execution_random_tasks_unwind_and_the_reference_rewards():
+    """task='random' draws a side per environment; end_fn='unwind' books what is left at the
+    far touch moved doom_price_penalty ticks against the agent; the reference's rewards."""
+    env = ExecutionEnv(_windows(), n_envs=8, msgs_per_step=5, target=400, seed=9, task="random",
+                       action_space="fixed_quants_complex", reward_function="normal", end_fn="unwind",
+                       reference_price="far_touch", doom_price_penalty=3)
+    obs = env.reset()
+    sells = obs["is_sell"].clone()
+    for _ in range(env.max_steps):
+        obs, rew, done = env.step(torch.zeros(8, dtype=torch.long))          # never trade
+        assert torch.isfinite(rew).all()
+    assert done and (obs["remaining"] == 0).all() and (env.info["doom_quant"] == 400).all()
+    # sellers receive cash, buyers pay it
+    assert ((env.cash > 0) == sells).all()
+    t = lambda *v: torch.tensor(v, dtype=torch.float64)
+    r = exec_reward("normal", filled=t(100), value=t(100 * 9900), market_q=t(50), market_v=t(50 * 10000),
+                    arrival=t(10000), target=400, sell=False, tick=100, lam=0.0)
+    assert float(r[0]) == 100.0                      # bought 1 tick below the VWAP, 100 shares
+    r = exec_reward("finish_fast", filled=t(0), value=t(0), market_q=t(0), market_v=t(0), arrival=t(1),
+                    target=1, sell=True, tick=100, remaining=torch.tensor([250]))
+    assert float(r[0]) == -250.0
+    r = exec_reward("simplest_case", filled=t(10), value=t(10 * 10100), market_q=t(0), market_v=t(0),
+                    arrival=t(10000), target=1, sell=True, tick=100)
+    assert float(r[0]) == 1000.0                     # sold 100 above the arrival price, 10 shares
