@@ -485,16 +485,89 @@ class ExecutionEnv(_Quoting, BaseLOBEnv):
 
 
 class MultiAgentEnv(MarketMakingEnv):
-    """Several market makers (and optionally an executor) trading on the same books."""
+    """Market makers and executors trading on the same books -- the reference's multi-agent
+    environment (``environment/jaxen/marl_env.py:212-470``).  Every agent builds its messages
+    from the book as it stands before the step; the step then applies all agents' cancels,
+    then their new orders (in a random order per environment and step with
+    ``shuffle_action_messages``), then the step's data messages.  Rewards are
+    (n, n_mm + n_exec): the market makers' (the ``MarketMakingEnv`` options) followed by the
+    executors' (the ``ExecutionEnv`` action spaces and rewards, ``exec_*`` keywords; the last
+    step sweeps what an executor has left).  ``exec_qty`` keeps the plain interface: a
+    marketable sell of that many shares by a trader outside the agents."""
 
-    def __init__(self, *a, n_mm: int = 2, exec_target: int = 0, **kw):
+    def __init__(self, *a, n_mm: int = 2, n_exec: int = 0, exec_target: int = 1000, exec_task: str = "sell",
+                 exec_action_space: str = "sizes", exec_reward: str = "slippage", exec_clip: int = 100,
+                 exec_lam: float = 1.0, shuffle_action_messages: bool = False, **kw):
+        from .agents import EXEC_ACTION_SPACES, EXEC_REWARDS
         super().__init__(*a, n_mm=n_mm, **kw)
-        self.exec_target = exec_target
-        self.exec_tid = 2000
+        if exec_action_space not in EXEC_ACTION_SPACES or exec_reward not in EXEC_REWARDS or \
+                exec_task not in ("buy", "sell", "random"):
+            raise ValueError(f"exec_action_space in {EXEC_ACTION_SPACES}, exec_reward in {EXEC_REWARDS}, "
+                             f"exec_task in (buy, sell, random)")
+        self.n_exec, self.exec_target, self.exec_task = n_exec, exec_target, exec_task
+        self.exec_space, self.exec_reward_fn, self.exec_clip, self.exec_lam = exec_action_space, exec_reward, \
+            exec_clip, exec_lam
+        self.exec_tids = [2000 + i for i in range(n_exec)]
+        self.exec_tid = 2000 + n_exec                 # the plain ``exec_qty`` seller
+        self.shuffle = shuffle_action_messages
+        self.n_agents = n_mm + n_exec
 
-    def step(self, actions: torch.Tensor, exec_qty: Optional[torch.Tensor] = None):
+    def reset(self, idx=None):
+        obs = super().reset(idx)
+        self._init_live(self.n_mm + self.n_exec, max(self.live.shape[2], 3))
+        E = self.n_exec
+        if self.exec_task == "random":
+            self.exec_sell = torch.from_numpy(self.rng.integers(0, 2, size=(self.n, E)).astype(bool))
+        else:
+            self.exec_sell = torch.full((self.n, E), self.exec_task == "sell", dtype=torch.bool)
+        self.exec_done = torch.zeros(self.n, E, dtype=torch.long)
+        self.exec_cash = torch.zeros(self.n, E, dtype=torch.float64)
+        self.exec_arrival = obs["mid"].clone()
+        return self._obs(obs)
+
+    def _obs(self, o):
+        o = super()._obs(o)
+        if hasattr(self, "exec_done"):
+            o["exec_remaining"] = self.exec_target - self.exec_done
+        return o
+
+    def _exec_messages(self, exec_actions: torch.Tensor) -> List[torch.Tensor]:
+        from .agents import exec_orders
+        rows = []
+        last = self.t == self.max_steps - 1
+        for e in range(self.n_exec):
+            rem = (self.exec_target - self.exec_done[:, e]).clamp(min=0)
+            st = self._state(self.exec_done[:, e])
+            sell = self.exec_sell[:, e]
+            orders, take = exec_orders(self.exec_space, exec_actions[:, e], st, rem, self.exec_clip,
+                                       self.max_steps - self.t, sell, self.tick)
+            if last:
+                take, orders = rem, torch.zeros_like(orders)
+            market = torch.stack([torch.where(sell, -1, 1) * (take > 0), take], -1)
+            rows += self._order_messages(self.n_mm + e, self.exec_tids[e], orders, market)
+        return rows
+
+    def _order(self, msgs: torch.Tensor) -> torch.Tensor:
+        """Cancels first, then the new orders (shuffled per environment if asked)."""
+        typ = msgs[..., 0]
+        key = torch.where(typ == 3, 0.0, 1.0).double()
+        if self.shuffle:
+            noise = torch.from_numpy(self.rng.random(size=tuple(typ.shape)))
+            key = key + torch.where(typ == 3, 0.0, 1.0).double() * noise
+        perm = torch.sort(key, dim=1, stable=True).indices
+        return torch.gather(msgs, 1, perm[..., None].expand_as(msgs))
+
+    def step(self, actions: torch.Tensor, exec_actions: Optional[torch.Tensor] = None,
+             exec_qty: Optional[torch.Tensor] = None):
+        """actions (n, n_mm[, d]) market-maker actions; exec_actions (n, n_exec[, d]) executor
+        actions; exec_qty (n,) shares the plain outside seller sends."""
+        from .agents import agent_trades, exec_reward
         obs0 = self.observe()
         msgs = self.action_messages(actions, obs0["mid"])
+        if self.n_exec:
+            if exec_actions is None:
+                raise ValueError("exec_actions (n, n_exec) are needed with n_exec > 0")
+            msgs = torch.cat([msgs, torch.stack(self._exec_messages(exec_actions), 1)], 1)
         if exec_qty is not None:
             q = exec_qty.long()
             m = torch.stack([torch.full_like(q, 4), torch.full_like(q, -1), q, torch.full_like(q, 10**9),
@@ -502,9 +575,29 @@ class MultiAgentEnv(MarketMakingEnv):
                              torch.zeros_like(q), torch.zeros_like(q)], -1)[:, None]
             m[q <= 0] = 0
             msgs = torch.cat([msgs, m], 1)
-        trades, _ = self.step_messages(msgs)
+        trades, _ = self.step_messages(self._order(msgs))
         obs = self.observe()
         rew = self._rewards(trades, obs0["mid"], obs, obs0["spread"])
+        if self.n_exec:
+            valid = trades[..., 0] >= 0
+            mine = torch.zeros_like(valid)
+            for tid in self.tids + self.exec_tids:
+                mine |= (trades[..., 6] == tid) | (trades[..., 7] == tid)
+            oq = torch.where(valid & ~mine, trades[..., 1].abs(), torch.zeros_like(trades[..., 1])).long()
+            mq, mv = oq.sum(-1), (oq * trades[..., 0].long()).sum(-1)
+            er = torch.zeros(self.n, self.n_exec, dtype=torch.float64)
+            for e, tid in enumerate(self.exec_tids):
+                bq, bv, sq, sv = agent_trades(trades, tid)
+                sell = self.exec_sell[:, e]
+                filled, value = torch.where(sell, sq, bq), torch.where(sell, sv, bv)
+                self.exec_done[:, e] += filled
+                self.exec_cash[:, e] += torch.where(sell, value, -value).double()
+                left = (self.exec_target - self.exec_done[:, e]).clamp(min=0)
+                er[:, e] = exec_reward(self.exec_reward_fn, filled=filled, value=value, market_q=mq, market_v=mv,
+                                       arrival=self.exec_arrival, target=self.exec_target, sell=sell,
+                                       tick=self.tick, lam=self.exec_lam, remaining=left,
+                                       mid_avg=(obs0["mid"] + obs["mid"]) // 2)
+            rew = torch.cat([rew, er], 1)
         return self._obs(obs), rew, self.done
 
 

@@ -63,3 +63,22 @@ def test_multi_agent_and_ppo():
     hist, pol = train_ippo(MarketMakingEnv(_windows(), n_envs=4, msgs_per_step=6, seed=7), iterations=2,
                            cfg=PPOConfig(epochs=2))
     assert len(hist) == 2 and all(np.isfinite(h["loss"]) for h in hist)
+
+
+def test_market_makers_and_executors_share_the_books():
+    """Two market makers and two executors (one buying, one selling at random per env) on the
+    same books: cancels go first, rewards come per agent, the executors finish their task."""
+    env = MultiAgentEnv(_windows(), n_envs=3, msgs_per_step=5, n_mm=2, n_exec=2, seed=8, exec_target=300,
+                        exec_task="random", exec_action_space="fixed_quants_complex", exec_reward="normal",
+                        action_space="spread_skew", reward_function="spooner", shuffle_action_messages=True)
+    obs = env.reset()
+    rng = torch.Generator().manual_seed(3)
+    msgs = env._order(env.action_messages(torch.randint(0, 5, (3, 2, 2), generator=rng), obs["mid"]))
+    typ = msgs[..., 0]
+    first_new = (typ != 3).float().argmax(1)
+    assert all(bool((typ[i, first_new[i]:] != 3).all()) for i in range(3))     # no cancel after a new order
+    while not env.done:
+        obs, rew, done = env.step(torch.randint(0, 5, (3, 2, 2), generator=rng),
+                                  exec_actions=torch.randint(0, 13, (3, 2), generator=rng))
+        assert rew.shape == (3, 4) and torch.isfinite(rew).all()
+    assert (obs["exec_remaining"] <= 300).all() and (env.exec_done > 0).any()
