@@ -101,3 +101,41 @@ def test_context_parallel_wrappers_keep_parameter_paths():
     plain = [flax_path(n) for n, _ in build().named_parameters()]
     wrapped = [flax_path(n) for n, _ in shard_model_cp(build()).named_parameters()]
     assert plain == wrapped
+
+
+def test_pinned_checkpoints_detect_drift(tmp_path):
+    """A pin names one step by its metadata hash: it resolves while the step is unchanged,
+    and a rewritten step, a damaged state file, a missing step or (when asked) a newer step
+    raise CheckpointDrift."""
+    from sigma0_b200.ckpt.pins import CheckpointDrift, PinRegistry, pin, resolve
+    a = _trainer()
+    mgr = CheckpointManager(str(tmp_path / "run"))
+    mgr.save(3, a, blocking=True)
+    mgr.save(6, a, blocking=True)
+    reg = PinRegistry(str(tmp_path / "pins.json"))
+    reg.add(pin("bg-flow", str(tmp_path / "run"), 3, role="background_order_flow", rationale="best KS"))
+    p = resolve(str(tmp_path / "pins.json"), "bg-flow")
+    assert p.step == 3 and p.role == "background_order_flow"
+    with pytest.raises(CheckpointDrift):
+        resolve(str(tmp_path / "pins.json"), "bg-flow", require_latest=True)     # step 6 is newer
+    with pytest.raises(KeyError):
+        reg.resolve("signal")
+    # a state file changed behind the pin's back
+    import glob
+    victim = sorted(glob.glob(str(tmp_path / "run" / "3" / "state" / "*")))[0]
+    with open(victim, "r+b") as f:
+        f.seek(0)
+        b = f.read(1)
+        f.seek(0)
+        f.write(bytes([b[0] ^ 0xFF]))
+    with pytest.raises(CheckpointDrift):
+        reg.resolve("bg-flow")
+    # the step saved again with other contents: new metadata, the pin no longer matches
+    mgr.save(3, a, metrics={"loss": 2.0}, blocking=True)
+    with pytest.raises(CheckpointDrift):
+        reg.resolve("bg-flow")
+    reg.add(pin("sig", str(tmp_path / "run"), 6))
+    import shutil
+    shutil.rmtree(str(tmp_path / "run" / "6"))
+    with pytest.raises(CheckpointDrift):
+        PinRegistry(str(tmp_path / "pins.json")).resolve("sig")

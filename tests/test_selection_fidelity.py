@@ -66,3 +66,45 @@ def test_fidelity_real_arm_is_exact_and_a_corrupted_stream_diverges():
     ghost[5] = [3, 1, 10, ghost[5, 3], 123_456_789, 0, ghost[5, 6], ghost[5, 7]]
     r = describe_stream(ghost, prior_ids=[])
     assert r.n_unresolvable_ids >= 1 and r.n_unresolved_positive >= 1
+
+
+def test_autopsy_finds_the_first_divergence_and_its_signature(tmp_path):
+    """A stream replayed against its own books never diverges; against books recorded for a
+    stream whose step k placed its order one tick away, the first divergence is step k, both
+    books moved at disjoint prices, and the run-directory reader gives the same answer."""
+    import pandas as pd
+    from sigma0_b200.data.synthetic import make_sequences
+    from sigma0_b200.sim import divergence as A
+    from sigma0_b200.sim.fidelity import replay_stream
+    d = make_sequences(1, 301, seed=5)[0]
+    after = np.asarray(d.books[1:, 3:], np.int64)
+    msgs = np.asarray(d.engine_msgs[:-1], np.int64)
+    init = np.asarray(d.l2_init, np.int64)
+    assert A.first_divergence(msgs, after, init)["first_step"] == -1
+    # the recorded books come from a stream whose k-th new order sat one tick deeper
+    news = np.nonzero(msgs[:, 0] == 1)[0]
+    # a new order that lands in the top three levels (deeper ones can fall off the compared book)
+    top = lambda i: set(after[i].reshape(-1, 4)[:3, [0, 2]].reshape(-1).tolist())
+    k = int(next(i for i in news[len(news) // 3:] if int(msgs[i, 3]) in top(i)))
+    moved = msgs.copy()
+    moved[k, 3] -= 100 * int(moved[k, 1])                 # a bid one tick lower, an ask one tick higher
+    ref, _ = replay_stream(moved, init, after.shape[1] // 4)
+    res = A.first_divergence(msgs, ref, init)
+    assert res["first_step"] == k and res["message"]["type_name"] == "NEW"
+    assert "DIFFERENT_PRICE" in res["signatures"] or "DIFFERENT_AMOUNT" in res["signatures"]
+    # the same window written in the generation runtime's CSV layout
+    for sub in ("data_cond", "data_gen"):
+        (tmp_path / sub).mkdir()
+    p = A.run_paths(str(tmp_path), "SYN", "2000-01-01", 7)
+    pd.DataFrame(np.stack([init, init])).to_csv(p["cond_book"], index=False)
+    pd.DataFrame({"time": [f"{s}.{ns:09d}" for s, ns in msgs[:, 6:8]], "event_type": msgs[:, 0],
+                  "order_id": msgs[:, 4], "size": msgs[:, 2], "price": msgs[:, 3],
+                  "direction": msgs[:, 1]}).to_csv(p["gen_msg"], index=False)
+    pd.DataFrame(ref).to_csv(p["gen_book"], index=False)
+    back = A.read_messages(p["gen_msg"])
+    assert np.array_equal(back[:, [0, 1, 2, 3, 4, 6, 7]], msgs[:, [0, 1, 2, 3, 4, 6, 7]])
+    w = A.autopsy_window(str(tmp_path), "SYN", "2000-01-01", 7)
+    assert w["first_step"] == k and w["signatures"] == res["signatures"]
+    assert A.autopsy_window(str(tmp_path), "SYN", "2000-01-01", 8) is None
+    assert A.signatures(np.array([4, 1, 1, 1, -999_999_999, 0, 0, 0]), {}, {("bid", 1): 1}, 10) == \
+        ["RECORDED_NOT_APPLIED", "AGGRESSIVE_EXECUTION", "MISS_SENTINEL"]
