@@ -82,3 +82,21 @@ def test_market_makers_and_executors_share_the_books():
                                   exec_actions=torch.randint(0, 13, (3, 2), generator=rng))
         assert rew.shape == (3, 4) and torch.isfinite(rew).all()
     assert (obs["exec_remaining"] <= 300).all() and (env.exec_done > 0).any()
+
+
+def test_ippo_per_agent_type_with_multi_discrete_and_autoregressive_heads():
+    """IPPO trains one actor-critic per agent type: two market makers on a two-dimensional
+    action space (autoregressive heads) and an executor on the 13-action ladder share the
+    books; an executor alone trains too."""
+    from sigma0_b200.envs.ippo import PPOConfig, action_dims, train_ippo
+    assert action_dims("mm", "spread_skew") == (5, 5) and action_dims("mm", "fixed_prices", 2) == (3,) * 4
+    env = MultiAgentEnv(_windows(), n_envs=3, msgs_per_step=5, n_mm=2, n_exec=1, seed=4, exec_target=200,
+                        exec_task="random", exec_action_space="fixed_quants_complex", exec_reward="normal",
+                        action_space="spread_skew", reward_function="spooner")
+    cfg = PPOConfig(epochs=2, minibatches=2, autoregressive=True, anneal_lr=True, per_type={"exe": {"lr": 1e-4}})
+    hist, pols = train_ippo(env, iterations=2, cfg=cfg)
+    assert set(pols) == {"mm", "exe"} and pols["mm"].dims == (5, 5) and pols["exe"].dims == (13,)
+    assert all(np.isfinite(h["mm_loss"]) and np.isfinite(h["exe_loss"]) for h in hist)
+    ex = ExecutionEnv(_windows(), n_envs=3, msgs_per_step=5, target=300, seed=4, action_space="fixed_prices")
+    hist, pol = train_ippo(ex, iterations=1, cfg=PPOConfig(epochs=1))
+    assert pol.dims == (3, 3, 3, 3) and np.isfinite(hist[0]["loss"])
