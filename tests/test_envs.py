@@ -100,3 +100,16 @@ def test_ippo_per_agent_type_with_multi_discrete_and_autoregressive_heads():
     ex = ExecutionEnv(_windows(), n_envs=3, msgs_per_step=5, target=300, seed=4, action_space="fixed_prices")
     hist, pol = train_ippo(ex, iterations=1, cfg=PPOConfig(epochs=1))
     assert pol.dims == (3, 3, 3, 3) and np.isfinite(hist[0]["loss"])
+
+
+def test_multiplicative_weights_bandit_baseline():
+    from sigma0_b200.envs.baselines import MultiplicativeWeights, run_bandit
+    b = MultiplicativeWeights(4, eta=0.5, n_envs=2, n_agents=1, seed=0)
+    b.last = torch.tensor([[3], [0]])
+    b.update(torch.tensor([[2.0], [-2.0]]))
+    assert torch.allclose(b.w.sum(-1), torch.ones(2, 1, dtype=torch.float64))
+    assert b.w[0, 0].argmax() == 3 and b.w[1, 0, 0] < b.w[1, 0, 1]
+    env = MarketMakingEnv(_windows(), n_envs=3, msgs_per_step=5, seed=2, action_space="fixed_quants",
+                          reward_function="spooner")
+    res = run_bandit(env, MultiplicativeWeights(8, eta=0.05, n_envs=3, seed=1))
+    assert np.isfinite(res["reward_mean"]) and 1 / 8 <= res["weights_max_mean"] <= 1
