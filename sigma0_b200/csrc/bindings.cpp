@@ -665,7 +665,7 @@ std::vector<at::Tensor> glu_res_bwd(at::Tensor dout, at::Tensor g, at::Tensor h,
   if (reinterpret_cast<uintptr_t>(b.data_ptr()) % 16) b = b.clone();   // read as float4
   auto dgp = at::empty_like(dout);
   auto db = at::empty({D}, dout.options());
-  auto part = at::empty({(int64_t)col_blocks(T, num_sms(dout)), D}, dout.options());
+  auto part = at::empty({(int64_t)glu_bwd_blocks(T, num_sms(dout)), D}, dout.options());
   glu_res_bwd_launch(dout.data_ptr<float>(), g.data_ptr(), h.data_ptr(), b.data_ptr<float>(), dh.data_ptr(),
                      dgp.data_ptr<float>(), db.data_ptr<float>(), part.data_ptr<float>(), T, (int)D, num_sms(dout),
                      stream());

@@ -117,6 +117,7 @@ void rms_bwd_launch(const void* dy, const void* x, const float* w, const float* 
 void gelu_fwd_launch(const void* o, void* g, long n, int sms, cudaStream_t st);
 void glu_res_fwd_launch(const float* x, const void* g, const void* h, const float* b, float* out, long n, int D,
                         int sms, cudaStream_t st);
+int glu_bwd_blocks(long T, int sms);
 void glu_res_bwd_launch(const float* dout, const void* g, const void* h, const float* b, void* dh, float* dgp,
                         float* db, float* part, long T, int D, int sms, cudaStream_t st);
 void gelu_bwd_launch(const void* o, const float* dgp, const void* dgm, void* dout, long n, int sms,
