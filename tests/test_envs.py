@@ -113,3 +113,35 @@ def test_multiplicative_weights_bandit_baseline():
                           reward_function="spooner")
     res = run_bandit(env, MultiplicativeWeights(8, eta=0.05, n_envs=3, seed=1))
     assert np.isfinite(res["reward_mean"]) and 1 / 8 <= res["weights_max_mean"] <= 1
+
+
+def _ippo_rank(rank, world, port, out):
+    import os
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from sigma0_b200.envs.ippo import PPOConfig, train_ippo
+        torch.set_num_threads(1)
+        # each rank runs its own environments (different windows), the same initial policy
+        env = MarketMakingEnv(_windows(), n_envs=2, msgs_per_step=6, seed=10 + rank, action_space="bobRL")
+        _, pol = train_ippo(env, iterations=2, cfg=PPOConfig(epochs=1), seed=0)
+        flat = torch.cat([p.detach().reshape(-1) for p in pol.parameters()])
+        allp = [torch.zeros_like(flat) for _ in range(world)]
+        dist.all_gather(allp, flat)
+        if rank == 0:
+            torch.save({"same": all(torch.equal(allp[0], x) for x in allp)}, out)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ippo_ranks_average_gradients_and_stay_identical(tmp_path):
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    out = str(tmp_path / "r.pt")
+    mp.spawn(_ippo_rank, args=(2, port, out), nprocs=2, join=True)
+    assert torch.load(out)["same"]
