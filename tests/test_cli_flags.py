@@ -136,3 +136,24 @@ def test_epochs_and_debug_overfit(capsys):
     ev = _events(capsys)
     steps = [e for e in ev if "loss" in e and "step" in e]
     assert ev[-1]["steps"] == 4 and len(steps) == 4          # 2 epochs x 2 batches of 2 windows
+
+
+def test_rl_runtime_reads_the_reference_ippo_keys(tmp_path):
+    """``cli rl`` builds market makers and an executor on shared books from the reference's
+    IPPO config keys and agent config field names, trains, and writes the policies."""
+    import json
+    from sigma0_b200.cli import rl
+    cfg = {"NUM_ENVS": 2, "NUM_STEPS": 6, "TOTAL_TIMESTEPS": 24, "UPDATE_EPOCHS": 1, "NUM_MINIBATCHES": 2,
+           "GAMMA": 0.99, "GAE_LAMBDA": 0.95, "CLIP_EPS": 0.2, "ENT_COEF": 0.01, "VF_COEF": 0.5,
+           "GRU_HIDDEN_DIM": 16, "SEED": 3, "LR": [3e-4, 1e-4], "MAX_GRAD_NORM": [0.5, 1.0],
+           "ANNEAL_LR": [True, False], "NUM_AGENTS_PER_TYPE": [2, 1], "MSGS_PER_STEP": 4, "WANDB_MODE": "off",
+           "AGENT_CONFIGS": {"MarketMaking": {"action_space": "spread_skew", "reward_function": "spooner_damped",
+                                              "inv_penalty": "quadratic", "unwind_price": "mid"},
+                             "Execution": {"action_space": "fixed_quants_complex", "task": "random",
+                                           "task_size": 200, "reward_function": "normal"}}}
+    path = tmp_path / "ippo.json"
+    path.write_text(json.dumps(cfg))
+    assert rl.main(["--config", str(path), "--synthetic", "2", "--out", str(tmp_path / "out")]) == 0
+    rec = json.loads((tmp_path / "out" / "history.json").read_text())
+    assert rec["agent_types"] == ["mm", "exe"] and rec["iterations"] == 2 and rec["unused_config"] == ["WANDB_MODE"]
+    assert (tmp_path / "out" / "policy_mm.pt").exists() and (tmp_path / "out" / "policy_exe.pt").exists()
