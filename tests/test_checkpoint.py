@@ -104,38 +104,35 @@ def test_context_parallel_wrappers_keep_parameter_paths():
 
 
 def test_pinned_checkpoints_detect_drift(tmp_path):
-    """A pin names one step by its metadata hash: it resolves while the step is unchanged,
-    and a rewritten step, a damaged state file, a missing step or (when asked) a newer step
-    raise CheckpointDrift."""
-    from sigma0_b200.ckpt.pins import CheckpointDrift, PinRegistry, pin, resolve
+    """A pinned name fixes one step by its metadata hash: it resolves while the step is
+    unchanged, and a damaged state file, a rewritten step, a removed step or (when asked) a
+    newer step raise ModelStoreError."""
+    import glob
+    import shutil
+    from sigma0_b200.pipeline.model_store import ModelStoreError, pin, resolve
     a = _trainer()
     mgr = CheckpointManager(str(tmp_path / "run"))
     mgr.save(3, a, blocking=True)
     mgr.save(6, a, blocking=True)
-    reg = PinRegistry(str(tmp_path / "pins.json"))
-    reg.add(pin("bg-flow", str(tmp_path / "run"), 3, role="background_order_flow", rationale="best KS"))
-    p = resolve(str(tmp_path / "pins.json"), "bg-flow")
-    assert p.step == 3 and p.role == "background_order_flow"
-    with pytest.raises(CheckpointDrift):
-        resolve(str(tmp_path / "pins.json"), "bg-flow", require_latest=True)     # step 6 is newer
-    with pytest.raises(KeyError):
-        reg.resolve("signal")
-    # a state file changed behind the pin's back
-    import glob
+    store = str(tmp_path / "pins.json")
+    pin(store, "bg-flow", str(tmp_path / "run"), 3, role="background_order_flow", rationale="best KS")
+    e = resolve(store, "bg-flow")
+    assert e["step"] == 3 and e["role"] == "background_order_flow"
+    with pytest.raises(ModelStoreError):
+        resolve(store, "bg-flow", require_latest=True)                  # step 6 is newer
+    with pytest.raises(ModelStoreError):
+        resolve(store, "signal")
     victim = sorted(glob.glob(str(tmp_path / "run" / "3" / "state" / "*")))[0]
-    with open(victim, "r+b") as f:
-        f.seek(0)
+    with open(victim, "r+b") as f:                      # a state file changed behind the pin's back
         b = f.read(1)
         f.seek(0)
         f.write(bytes([b[0] ^ 0xFF]))
-    with pytest.raises(CheckpointDrift):
-        reg.resolve("bg-flow")
-    # the step saved again with other contents: new metadata, the pin no longer matches
-    mgr.save(3, a, metrics={"loss": 2.0}, blocking=True)
-    with pytest.raises(CheckpointDrift):
-        reg.resolve("bg-flow")
-    reg.add(pin("sig", str(tmp_path / "run"), 6))
-    import shutil
+    with pytest.raises(ModelStoreError):
+        resolve(store, "bg-flow")
+    mgr.save(3, a, metrics={"loss": 2.0}, blocking=True)   # saved again with other contents
+    with pytest.raises(ModelStoreError):
+        resolve(store, "bg-flow")
+    pin(store, "sig", str(tmp_path / "run"), 6)
     shutil.rmtree(str(tmp_path / "run" / "6"))
-    with pytest.raises(CheckpointDrift):
-        PinRegistry(str(tmp_path / "pins.json")).resolve("sig")
+    with pytest.raises(ModelStoreError):
+        resolve(store, "sig")
