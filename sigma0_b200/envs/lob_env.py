@@ -87,6 +87,7 @@ class BaseLOBEnv:
         T = self.max_steps * self.k
         self.data = torch.from_numpy(np.stack([w.engine_msgs[:T] for w in ws]).astype(np.int32))
         self.t = 0
+        self.last_data = torch.zeros(self.n, self.k, 8, dtype=torch.int32)
         self.clock = torch.from_numpy(np.array([w.t0 for w in ws], dtype=np.int64))
         self._clear_trades()
         return self.observe()
@@ -112,6 +113,7 @@ class BaseLOBEnv:
         else:
             msgs = data
         self.engine.process(msgs.to(self.engine.device) if self.engine.on_gpu else msgs)
+        self.last_data = data
         self.t += 1
         self.clock = data[:, -1, 6:8].long()
         return torch.from_numpy(self.engine.trade_rows()), data
@@ -207,7 +209,7 @@ class MarketMakingEnv(_Quoting, BaseLOBEnv):
 
     OFFSETS = (1, 2, 3, 5, 8)
 
-    OBS_SPACES = ("basic", "engineered", "features")
+    OBS_SPACES = ("basic", "engineered", "features", "messages")
 
     def __init__(self, *a, quote_size: int = 100, inventory_penalty: float = 0.01, n_mm: int = 1,
                  action_space: str = "offsets", reward_function: str = "pnl_inventory", inv_penalty: str = "linear",
@@ -315,9 +317,15 @@ class MarketMakingEnv(_Quoting, BaseLOBEnv):
         ``basic`` the inventory, ``engineered`` the inventory and the spread (price units),
         each as (x - mean) / scale with the reference's constants when ``normalize``
         (``mm_env.py:2881-2990``: inventory / 10, spread / 1e4; keys in sorted order), and
-        ``features`` the book features of ``features()``."""
+        ``features`` the book features of ``features()``, ``messages`` the step's data
+        messages (engine rows, flattened)."""
         if self.obs_space == "features":
             return features(obs, self.n_mm)
+        if self.obs_space == "messages":
+            # the step's data messages as engine rows (the reference's raw "messages" space),
+            # zeros before the first step; every market maker sees the same rows
+            m = self.last_data.reshape(self.n, -1).float()
+            return m[:, None].expand(-1, self.n_mm, -1).contiguous()
         inv = obs["inventory"].double()
         cols = [inv / 10.0 if self.normalize else inv]
         if self.obs_space == "engineered":

@@ -169,6 +169,10 @@ def test_reward_shaping_options_and_observation_spaces():
     assert torch.allclose(v[:, 0, 1].double(), (obs["spread"] * env.tick).double() / 1e4)
     env.obs_space = "basic"
     assert env.agent_observation(obs).shape == (2, 1, 1)
+    env.obs_space = "messages"
+    assert env.agent_observation(obs).shape == (2, 1, 40) and not env.agent_observation(obs).any()
+    obs, _, _ = env.step(torch.zeros(2, 1, 2, dtype=torch.long))
+    assert torch.equal(env.agent_observation(obs)[:, 0], env.data[:, :5].reshape(2, -1).float())
 
 
 def test_market_maker_from_the_reference_config_names():
@@ -176,7 +180,7 @@ def test_market_maker_from_the_reference_config_names():
            "inv_penalty_lambda": 0.5, "inv_penalty_threshold": 3.0, "unwind_price": "far_touch",
            "unwind_price_penalty": 5, "reference_price": "mid_avg", "inventoryPnL_eta": 0.6,
            "inventoryPnL_gamma": 0.5, "rebate_bps": 10.0, "clip_reward": True, "debug_mode": False,
-           "observation_space": "messages"}
+           "observation_space": "messages_new_tokenizer"}
     env = MarketMakingEnv.from_reference_config(_windows(), 2, cfg, msgs_per_step=5, seed=1)
     assert (env.space, env.reward_fn, env.inv_pen_kind, env.unwind, env.unwind_pen) == \
         ("spread_skew", "spooner_asym_damped2", "threshold", "far_touch", 5)
