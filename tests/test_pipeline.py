@@ -97,3 +97,22 @@ def test_snapshots_and_ce_by_position():
     snap = make_snapshots(d.books, [t[5], t[5] + 1])
     assert np.array_equal(snap[0], d.books[6, 3:]) and np.array_equal(snap[1], d.books[6, 3:])
     assert main(["--preset", "smoke", "--impl", "torch", "--n_messages", "4", "--max_batches", "1"]) == 0
+
+
+def test_evidence_declared_assertions_and_self_test(tmp_path, capsys):
+    """Declarative assertions are re-evaluated from the record itself, and the self-test
+    plants every kind of defect and sees each one go red."""
+    from sigma0_b200.pipeline import integrity as I
+    src = tmp_path / "s.py"
+    src.write_text("a = 1\n")
+    ev = str(tmp_path / "ev.json")
+    I.record_evidence(ev, [str(src)], {}, metrics={"bench": {"ic": [0.8, 0.6]}},
+                      declared=[{"name": "ic holds", "metric": "bench.ic.1", "op": ">=", "value": 0.5}])
+    assert I.audit(ev) == {"changed": [], "missing": [], "failed": []}
+    import json
+    rec = json.load(open(ev))
+    rec["metrics"]["bench"]["ic"][1] = 0.4                # a number edited after the fact
+    json.dump(rec, open(ev, "w"))
+    assert I.audit(ev)["failed"] and I.main([ev]) == 1
+    assert I.self_test() == 0 and I.main(["--self-test"]) == 0
+    assert "self-test passed" in capsys.readouterr().out
