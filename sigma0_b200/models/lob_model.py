@@ -143,20 +143,23 @@ class LobModel(nn.Module):
         ``ignore_times`` the absolute-time tokens of every message are dropped."""
         h = self.hidden(tokens, book)
         B, L = labels.shape
-        keep = torch.ones(L, dtype=torch.bool, device=labels.device)
+        # the kept positions are known on the host: no device round trip in the step
+        keep = torch.ones(L, dtype=torch.bool)
         if ignore_times:
-            pos = torch.arange(L, device=labels.device) % self.msg_len
+            pos = torch.arange(L) % self.msg_len
             keep = (pos < tokenizer.TIME_START_I) | (pos > tokenizer.TIME_END_I)
+        n_keep = int(keep.sum())
+        idx = None if n_keep == L else keep.nonzero()[:, 0].to(labels.device, non_blocking=True)
         if h.is_cuda:
             from ..ops.cross_entropy import linear_cross_entropy_mean
-            w = keep.float().expand(B, L) / (B * int(keep.sum()))
+            w = keep.to(labels.device, non_blocking=True).float().expand(B, L) / (B * n_keep)
             loss, ce = linear_cross_entropy_mean(h, self.decoder.kernel, self.decoder.bias, labels, w)
         else:
             logits = self.decoder(h).float()
             ce = F.cross_entropy(logits.reshape(-1, logits.shape[-1]), labels.reshape(-1),
                                  reduction="none").reshape(labels.shape)
-            loss = ce[:, keep].mean()
-        ce_pos = ce[:, keep].mean(0)
+            loss = (ce if idx is None else ce.index_select(1, idx)).mean()
+        ce_pos = (ce if idx is None else ce.index_select(1, idx)).mean(0)
         return loss, ce_pos
 
     # -- decode ------------------------------------------------------------------------
