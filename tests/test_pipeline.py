@@ -116,3 +116,31 @@ def test_evidence_declared_assertions_and_self_test(tmp_path, capsys):
     assert I.audit(ev)["failed"] and I.main([ev]) == 1
     assert I.self_test() == 0 and I.main(["--self-test"]) == 0
     assert "self-test passed" in capsys.readouterr().out
+
+
+def test_injection_report_with_reference_arms(tmp_path):
+    """Off, on and a repeated off run of the same generation: J4 gates, J0 / J1 / J2 / J5 hold
+    for deterministic argmax sampling on the CPU, and the written report re-audits clean; a
+    tampered verdict is caught."""
+    from sigma0_b200.cli.infer import main
+    from sigma0_b200.pipeline import injection as J
+    base = ["--preset", "smoke", "--impl", "torch", "--synthetic", "2", "--n_sequences", "2", "--batch_size", "2",
+            "--n_cond_msgs", "4", "--n_gen_msgs", "5", "--sample_top_n", "1"]
+    inj = ["--inject_step", "2", "--inject_event_type", "1", "--inject_side", "1", "--inject_qty", "37",
+           "--inject_price_offset_ticks", "-1"]
+    runs = {}
+    for name, extra in (("p", []), ("p2", []), ("o", []), ("i", inj)):
+        runs[name] = str(tmp_path / name)
+        assert main(base + ["--save_dir", runs[name]] + extra) == 0
+    rep = J.verify_arms(runs["i"], 2, 1, 37, -1, dir_o=runs["o"], dir_p=runs["p"], dir_p2=runs["p2"])
+    assert rep["overall_pass"] == 1 and rep["j4_book_injection"]["n_windows"] == 2
+    assert rep["j0_determinism"]["pass"] == 1 and rep["j1_off_means_off"]["pass"] == 1
+    assert rep["j2_prefix"]["pass"] == 1 and rep["j5_divergence"]["pass"] == 1
+    path = str(tmp_path / "report.json")
+    assert J.main(["--dir_i", runs["i"], "--dir_o", runs["o"], "--step", "2", "--side", "1", "--qty", "37",
+                   "--offset_ticks", "-1", "--out", path]) == 0
+    assert J.check_report(path) == []
+    r = json.load(open(path))
+    r["overall_pass"] = 0
+    json.dump(r, open(path, "w"))
+    assert J.check_report(path) and J.main(["--check", path]) == 1
