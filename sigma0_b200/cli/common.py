@@ -41,15 +41,13 @@ def dist_env():
 
 def load_days(data_dir: Optional[str], synthetic: int, n_msgs: int, seed: int, tickers=None, date_range=None):
     """Day arrays from ``data_dir`` (``*_message.npy`` / ``*_book.npy``) or synthetic days."""
-    from ..data.lobster import LobDay, raw_to_engine, resolve_day_files
+    from ..data.lobster import MappedLobDay, resolve_day_files
+    from ..data.masks import load_npy
     if data_dir:
         files = resolve_day_files(data_dir, tickers, date_range)
         if not files:
             raise FileNotFoundError(f"no *_message.npy / *_book.npy day files under {data_dir}")
-        days = []
-        for mf, bf in files:
-            m, b = np.load(mf), np.load(bf)
-            days.append(LobDay(m, b, raw_to_engine(m), b[0, 3:].astype(np.int64)))
-        return days
+        # memory-mapped: a window's rows are read when it is sampled, not at start-up
+        return [MappedLobDay(load_npy(mf), load_npy(bf)) for mf, bf in files]
     from ..data.synthetic import make_sequences
     return make_sequences(synthetic, n_msgs, seed=seed)

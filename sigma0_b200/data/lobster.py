@@ -14,7 +14,7 @@
 * ``save_day`` / ``LobWindowDataset.from_dir`` use ``<ticker>_<date>_message.npy``
   and ``..._book.npy``.
 * ``resolve_day_files`` picks days by ticker and date range
-  (``data/data_files.py:18``); ``select_levels`` cuts a wide (L500) book to L
+  (``data/data_files.py:18``), from the data index ``build_index`` writes when one exists; ``select_levels`` cuts a wide (L500) book to L
   levels (``D5``); ``WindowSampler`` is the rank-interleaved, resumable,
   seeded sampler of ``data/dataloading.py:297``.
 """
@@ -38,6 +38,23 @@ class LobDay:
     books: np.ndarray         # (n, 3 + 4L) book before each message
     engine_msgs: np.ndarray   # (n, 8)
     l2_init: np.ndarray       # (4L,)
+
+
+class MappedLobDay:
+    """A day whose message and book arrays stay memory-mapped on disk (windows are read when
+    a sample is drawn); the engine rows are built on first use only (training never needs
+    them)."""
+
+    def __init__(self, msgs: np.ndarray, books: np.ndarray):
+        self.msgs, self.books = msgs, books
+        self._engine = None
+        self.l2_init = np.asarray(books[0, 3:], np.int64)
+
+    @property
+    def engine_msgs(self) -> np.ndarray:
+        if self._engine is None:
+            self._engine = raw_to_engine(np.asarray(self.msgs))
+        return self._engine
 
 
 def raw_to_engine(raw: np.ndarray) -> np.ndarray:
@@ -143,10 +160,69 @@ def select_levels(wide: np.ndarray, levels: int) -> np.ndarray:
 _DAY = re.compile(r"^(?P<ticker>[A-Za-z0-9.]+)_(?P<date>\d{4}-\d{2}-\d{2})_.*message.*\.npy$")
 
 
+INDEX_NAME = "index.json"
+
+
+def _walk_day_files(root: str) -> List[str]:
+    out = []
+    for d, _, files in os.walk(root):
+        for f in files:
+            if _DAY.match(f):
+                out.append(os.path.relpath(os.path.join(d, f), root))
+    return sorted(out)
+
+
+def build_index(root: str) -> Dict:
+    """Write ``<root>/index.json``: every day file's relative path and array shape (read from
+    the ``.npy`` header, no data loaded), so later runs find their days without walking the
+    tree -- the reference's baked data index (``data/lobster_dataloader.py:55-114``), for
+    filesystems where listing thousands of files is slow or forbidden."""
+    files = {}
+    for rel in _walk_day_files(root):
+        for f in (rel, rel.replace("message", "book")):
+            p = os.path.join(root, f)
+            if os.path.exists(p):
+                files[f] = list(np.load(p, mmap_mode="r").shape)
+    idx = {"schema": "sigma0_b200.data_index.v1", "shapes": files}
+    tmp = os.path.join(root, INDEX_NAME + ".tmp")
+    import json
+    with open(tmp, "w") as fh:
+        json.dump(idx, fh, indent=0, sort_keys=True)
+    os.replace(tmp, os.path.join(root, INDEX_NAME))
+    return idx
+
+
+def load_index(root: str) -> Optional[Dict]:
+    """The data index of ``root``: ``<root>/index.json``, else the file named by
+    ``$DATA_INDEX_JSON``; None when there is none."""
+    import json
+    for p in (os.path.join(root, INDEX_NAME), os.environ.get("DATA_INDEX_JSON") or ""):
+        if p and os.path.isfile(p):
+            with open(p) as fh:
+                return json.load(fh)
+    return None
+
+
 def resolve_day_files(root: str, tickers: Optional[Sequence[str]] = None,
                       date_range: Optional[Tuple[str, str]] = None) -> List[Tuple[str, str]]:
     """Paired ``(message.npy, book.npy)`` paths under ``root`` (recursive), filtered by
-    ticker and inclusive ISO date range, ordered by (date, ticker)."""
+    ticker and inclusive ISO date range, ordered by (date, ticker).  With a data index the
+    paths come from it and the tree is not walked."""
+    idx = load_index(root)
+    if idx is not None:
+        out = []
+        for rel in sorted(idx["shapes"]):
+            f = os.path.basename(rel)
+            m = _DAY.match(f)
+            if not m or (tickers and m["ticker"] not in tickers):
+                continue
+            if date_range and not (date_range[0] <= m["date"] <= date_range[1]):
+                continue
+            brel = rel.replace("message", "book")
+            if brel in idx["shapes"]:
+                out.append((m["date"], m["ticker"], os.path.join(root, rel), os.path.join(root, brel)))
+        out.sort()
+        return [(a, b) for _, _, a, b in out]
     out = []
     for d, _, files in os.walk(root):
         for f in files:
@@ -222,3 +298,17 @@ def make_snapshots(books: np.ndarray, times_ns: Sequence[int]) -> np.ndarray:
     idx = np.searchsorted(t, np.asarray(times_ns, dtype=np.int64), side="right")
     idx = np.clip(idx, 0, len(b) - 1)
     return b[idx, 3:]
+
+
+def main(argv=None) -> int:
+    import argparse
+    ap = argparse.ArgumentParser(description="LOBSTER day files: write the data index of a directory tree")
+    ap.add_argument("--build_index", required=True, metavar="ROOT")
+    a = ap.parse_args(argv)
+    idx = build_index(a.build_index)
+    print(f"{len(idx['shapes'])} files indexed in {os.path.join(a.build_index, INDEX_NAME)}")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

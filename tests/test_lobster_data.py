@@ -72,3 +72,25 @@ def test_window_sampler_interleave_and_resume():
     assert sorted(order.tolist()) == list(range(6))
     first = [["A", "A", "A", "B", "B", "C"][i] for i in order[:3]]
     assert sorted(first) == ["A", "B", "C"]
+
+
+def test_data_index_and_memory_mapped_days(tmp_path, monkeypatch):
+    """With a data index the day files come from it (the tree is not walked), and the CLI's
+    day loader memory-maps the arrays and builds engine rows only when asked."""
+    import sigma0_b200.data.lobster as L
+    from sigma0_b200.cli.common import load_days
+    from sigma0_b200.data.synthetic import make_sequences
+    d = make_sequences(1, 50, seed=3)[0]
+    day = L.LobDay(d.msgs, d.books, d.engine_msgs, d.l2_init)
+    for t, date in (("GOOG", "2022-01-03"), ("GOOG", "2022-01-05"), ("MSFT", "2022-01-04")):
+        save_day(day, str(tmp_path / t), t, date)
+    walked = resolve_day_files(str(tmp_path))
+    idx = L.build_index(str(tmp_path))
+    assert len(idx["shapes"]) == 6 and list(idx["shapes"].values())[0][0] == 50
+    monkeypatch.setattr(L.os, "walk", lambda *a, **k: (_ for _ in ()).throw(AssertionError("walked")))
+    assert resolve_day_files(str(tmp_path)) == walked
+    assert len(resolve_day_files(str(tmp_path), tickers=["MSFT"])) == 1
+    days = load_days(str(tmp_path), 0, 0, 0)
+    assert len(days) == 3 and isinstance(days[0].msgs, np.memmap) and days[0]._engine is None
+    assert np.array_equal(days[0].engine_msgs, raw_to_engine(np.asarray(d.msgs)))
+    assert np.array_equal(days[0].l2_init, np.asarray(d.books[0, 3:], np.int64))
