@@ -17,7 +17,10 @@ generator evaluation, ``src/base_model/inference/evaluation.py:14-430``).
 
 Books are rows ``[ask_p, ask_v, bid_p, bid_v] x levels`` (empty levels at the engine's
 sentinel prices or non-positive); messages the package's 14-column rows (event type in
-column 1, size in column 5).
+column 1, size in column 5) or engine rows (type 0, size 2).
+
+``python -m sigma0_b200.eval.gen_metrics --run_dir RUN --stock SYN`` scores a generation run
+(``cli/infer.py`` layout) over the windows' common number of generated steps.
 """
 from __future__ import annotations
 
@@ -131,15 +134,22 @@ def moments_ci(rets: np.ndarray, n_boot: int = 500, ci: float = 0.95, seed: int 
     return {k: bootstrap_ci(x, lambda y, k=k: moments(y)[k], n_boot, ci, seed) for k in moments(x)}
 
 
+def _cols(m: np.ndarray) -> Tuple[int, int]:
+    """(event type, size) columns: the 14-column message rows or the 8-column engine rows."""
+    return (0, 2) if m.shape[-1] == 8 else (1, 5)
+
+
 def liquidity(msgs: np.ndarray) -> Tuple[np.ndarray, np.ndarray]:
     """Cumulative volume provided (new orders) and taken (cancels, deletes, executions)."""
     m = np.asarray(msgs, np.int64)
-    etype, size = m[..., 1], m[..., 5]
+    te, sz = _cols(m)
+    etype, size = m[..., te], m[..., sz]
     return np.cumsum(np.where(etype == 1, size, 0), -1), np.cumsum(np.where(etype > 1, size, 0), -1)
 
 
 def event_type_counts(msgs: np.ndarray, types=(1, 2, 3, 4)) -> Dict[int, int]:
-    e = np.asarray(msgs, np.int64)[..., 1].ravel()
+    m = np.asarray(msgs, np.int64)
+    e = m[..., _cols(m)[0]].ravel()
     return {int(t): int((e == t).sum()) for t in types}
 
 
@@ -162,3 +172,50 @@ def evaluate(gen_books: np.ndarray, real_books: np.ndarray, gen_msgs: np.ndarray
             "return_corr": return_corr(rg, rr).tolist(), "return_corr_ci": [lo.tolist(), hi.tolist()],
             "moments_gen": moments(rg[:, -1]), "moments_real": moments(rr[:, -1]),
             "events_gen": event_type_counts(gen_msgs), "events_real": event_type_counts(real_msgs)}
+
+
+def evaluate_run(root: str, stock: str, n_levels: int = 10, tick: int = 100, limit: int = 10 ** 6,
+                 n_boot: int = 200) -> Dict:
+    """``evaluate`` over the windows of a generation run, cut to their common length."""
+    from ..sim.divergence import read_books, read_messages, run_paths
+    from ..sim.frozen import run_windows
+    gb, rb, gm, rm, m0 = [], [], [], [], []
+    for date, i in run_windows(root, stock, limit):
+        p = run_paths(root, stock, date, i)
+        gb.append(read_books(p["gen_book"]))
+        rb.append(read_books(p["real_book"]))
+        gm.append(read_messages(p["gen_msg"]))
+        rm.append(read_messages(p["real_msg"]))
+        m0.append(float(_mid(read_books(p["cond_book"])[-1:])[0]))
+    if not gb:
+        raise FileNotFoundError(f"no generated windows under {root}/data_gen")
+    S = min(min(len(x) for x in gb), min(len(x) for x in rb))
+    w = min(b.shape[1] for b in gb + rb)
+    cut = lambda xs, c=None: np.stack([x[:S, :c] if c else x[:S] for x in xs])
+    res = evaluate(cut(gb, w), cut(rb, w), cut(gm), cut(rm), np.array(m0), n_levels, tick, n_boot)
+    res.update(n_windows=len(gb), n_steps=S)
+    return res
+
+
+def main(argv=None) -> int:
+    import argparse
+    import json
+    ap = argparse.ArgumentParser(description="generator metrics of a generation run against the real continuations")
+    ap.add_argument("--run_dir", required=True)
+    ap.add_argument("--stock", default="SYN")
+    ap.add_argument("--n_levels", type=int, default=10)
+    ap.add_argument("--tick", type=int, default=100)
+    ap.add_argument("--n_boot", type=int, default=200)
+    ap.add_argument("--out", default=None)
+    a = ap.parse_args(argv)
+    res = evaluate_run(a.run_dir, a.stock, a.n_levels, a.tick, n_boot=a.n_boot)
+    text = json.dumps(res, indent=1)
+    print(text)
+    if a.out:
+        with open(a.out, "w") as f:
+            f.write(text)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

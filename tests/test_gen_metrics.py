@@ -66,3 +66,15 @@ def test_evaluate_on_a_generated_and_real_path():
     assert res["events_gen"] == res["events_real"]
     same = G.evaluate(real, real, rm, rm, mid0, n_boot=20)
     assert max(same["book_loss_l1"]) == 0.0 and max(same["mid_loss_l1_ticks"]) == 0.0
+
+
+def test_gen_metrics_on_a_generation_run(tmp_path):
+    """The metrics over a run written by the generation CLI."""
+    from sigma0_b200.cli.infer import main
+    out = str(tmp_path / "run")
+    assert main(["--preset", "smoke", "--impl", "torch", "--synthetic", "3", "--n_sequences", "3", "--batch_size", "3",
+                 "--n_cond_msgs", "4", "--n_gen_msgs", "6", "--sample_top_n", "1", "--save_dir", out]) == 0
+    res = G.evaluate_run(out, "SYN", n_boot=10)
+    assert res["n_windows"] == 3 and res["n_steps"] == 6 and len(res["book_loss_l1"]) == 6
+    assert sum(res["events_gen"].values()) == 18 and sum(res["events_real"].values()) == 18
+    assert G.main(["--run_dir", out, "--n_boot", "5"]) == 0
