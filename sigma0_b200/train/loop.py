@@ -137,6 +137,8 @@ class LoopConfig:
     reset_schedule: bool = False
     lr_patience: int = 0
     reduce_factor: float = 0.9
+    # log records also carry the gradient norm per optimizer group and the CE per message field
+    detailed_logs: bool = True
 
 
 @dataclass
@@ -258,6 +260,11 @@ def fit(trainer, batches: Iterable, cfg: LoopConfig, log: Callable[[Dict], None]
             gn = trainer.opt.last_grad_norm
             rec = {"step": step, "loss": last_loss, "tokens_per_s": tok_count / max(dt, 1e-9),
                    "grad_norm": math.sqrt(float(gn)) if gn is not None else None}
+            if hasattr(trainer, "current_lr"):
+                rec["lr"] = trainer.current_lr()
+            if cfg.detailed_logs and hasattr(trainer, "field_ce"):
+                rec["grad_norm_by_group"] = trainer.opt.group_grad_norms()
+                rec["ce_by_field"] = trainer.field_ce()
             if flops_tok:
                 rec["mfu"] = flops_tok * rec["tokens_per_s"] / (peak * trainer.world)
             log(rec)

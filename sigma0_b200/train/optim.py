@@ -196,6 +196,15 @@ class FlatAdam:
             v.mul_(self.b2).addcmul_(g, g, value=1 - self.b2)
             p.sub_(lr * ((m / bc1) / ((v / bc2).sqrt() + self.eps) + wd * p))
 
+    def group_grad_norms(self) -> Dict[str, float]:
+        """L2 norm of this rank's gradient buffer per optimizer group (ssm / regular), as the
+        reference logs grad norms by group (``training/train_helpers.py:290``)."""
+        out = {}
+        for name, (a, b) in (("ssm", (0, self.n_ssm)), ("regular", (self.n_ssm, self.numel))):
+            if b > a:
+                out[name] = float(self.grad[a:b].float().norm())
+        return out
+
     def step(self, lr_scale: float = 1.0, grad_sumsq: Optional[torch.Tensor] = None):
         """One update.  ``grad_sumsq`` overrides the local sum of squares (sharded optimizers)."""
         self.step_count += 1

@@ -28,8 +28,9 @@ from __future__ import annotations
 
 import math
 import time
-from typing import Optional
+from typing import Dict, Optional
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -309,21 +310,49 @@ class Trainer:
             tokens, labels, book = self._segment(tokens, labels, book)
         k = self.accum_steps
         if k == 1:
-            loss, _ = self.model.loss(tokens, book, labels, ignore_times=self.ignore_times, tokenizer=self.tok)
+            loss, ce_pos = self.model.loss(tokens, book, labels, ignore_times=self.ignore_times, tokenizer=self.tok)
             loss.backward()
             total = loss.detach()
+            self.last_ce_pos = ce_pos.detach()
         else:
             total = torch.zeros((), device=tokens.device)
+            ce_sum = None
             for tc, lc, bc in zip(tokens.chunk(k), labels.chunk(k), book.chunk(k) if book is not None else [None] * k):
-                loss, _ = self.model.loss(tc, bc, lc, ignore_times=self.ignore_times, tokenizer=self.tok)
+                loss, ce_pos = self.model.loss(tc, bc, lc, ignore_times=self.ignore_times, tokenizer=self.tok)
                 (loss / k).backward()
                 total = total + loss.detach() / k
+                ce_sum = ce_pos.detach() / k if ce_sum is None else ce_sum + ce_pos.detach() / k
+            self.last_ce_pos = ce_sum
         self._update(self.lr_scale(self.step_idx + 1))
         self.step_idx += 1
         if self.cp:
             dist.all_reduce(total, group=self.group)
             total = total / self.world
         return total
+
+    def field_ce(self) -> Dict[str, float]:
+        """Mean cross-entropy of the last step per message field (the reference logs it per
+        field): the per-position CE of the last batch grouped by the field each position of
+        a message belongs to.  Empty for encodings without per-token fields (1tok)."""
+        ce = getattr(self, "last_ce_pos", None)
+        tok = self.tok
+        lens = np.asarray(getattr(tok, "TOK_LENS", []), np.int64)
+        msg_len = int(getattr(self.model, "msg_len", 0))
+        if ce is None or not len(lens) or int(lens.sum()) != msg_len:
+            return {}
+        field_of = np.repeat(np.arange(len(lens)), lens)               # offset in a message -> field
+        offs = np.arange(msg_len)
+        if self.ignore_times:
+            offs = offs[(offs < tok.TIME_START_I) | (offs > tok.TIME_END_I)]
+        vals = ce.float().cpu().numpy()
+        if len(vals) % len(offs):
+            return {}
+        f = field_of[np.tile(offs, len(vals) // len(offs))]
+        return {str(tok.FIELDS[i]): float(vals[f == i].mean()) for i in np.unique(f)}
+
+    def current_lr(self) -> float:
+        """The regular group's learning rate of the next step."""
+        return float(self.opt.base_lr["regular"]) * self.lr_scale(self.step_idx + 1)
 
     def lr_scale(self, step: int) -> float:
         """The learning-rate multiple for optimizer step ``step`` (1-based)."""

@@ -124,3 +124,24 @@ def test_watchdog_covers_work_still_running_after_the_host_returns():
     done["v"] = True
     time.sleep(0.2)
     assert not ok and wd2.pending() == 0
+
+
+def test_log_records_carry_lr_group_norms_and_field_ce():
+    """Log records carry the learning rate, the gradient norm of each optimizer group and the
+    cross-entropy per message field; the field means reproduce the step's mean loss."""
+    import math
+    import numpy as np
+    recs = []
+    tr = _trainer()
+    fit(tr, _batches(2), LoopConfig(steps=2, log_every=1, watchdog_timeout=0), log=recs.append)
+    r = recs[-1]
+    assert r["lr"] > 0 and set(r["grad_norm_by_group"]) == {"ssm", "regular"}
+    g = r["grad_norm_by_group"]
+    assert all(math.isfinite(v) and v > 0 for v in g.values())
+    fields = r["ce_by_field"]
+    assert "event_type" in fields or len(fields) >= 5
+    # per-field means weighted by the field widths give back the mean over positions
+    lens = dict(zip(tr.tok.FIELDS, tr.tok.TOK_LENS))
+    w = np.array([lens[f] for f in fields])
+    mean = float((np.array(list(fields.values())) * w).sum() / w.sum())
+    assert abs(mean - float(tr.last_ce_pos.mean())) < 1e-4
