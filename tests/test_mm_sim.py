@@ -72,3 +72,36 @@ def test_frozen_episodes_signal_curve_and_the_replay_gate(tmp_path):
     assert F.run_windows(root, "SYN", 10) == [("2000-01-01", 3), ("2000-01-01", 9)]
     gate = F.replay_gate(root, "SYN")
     assert all(r["exact_mid_frac"] == 1.0 for r in gate.values()) and len(gate) == 2
+
+
+def test_closed_loop_policy_against_a_frozen_episode():
+    """The touch-quoting baseline trades against the background flow with exact accounting;
+    a policy that never quotes ends flat at zero; one that raises ends its episode with an
+    error; the inventory cap holds."""
+    from sigma0_b200.sim import closed_loop as C
+    from sigma0_b200.sim import frozen as F
+    from sigma0_b200.data.synthetic import make_sequences
+    d = make_sequences(1, 1500, seed=4)[0]
+    msgs = np.asarray(d.engine_msgs[:-1], np.int64)
+    ep = F.build_episode(F.EpisodeSpec(1, "SYN", "2000-01-01", 0, (0,)), np.asarray(d.l2_init, np.int64), msgs,
+                         {"mid_mean": np.array([1.0, 2.0])})
+    cfg = C.SimConfig(n_steps=30, warmup_s=0.0, size_cap=50, inventory_cap=120)
+    t = C.run_frozen_episode(C.symmetric_touch, ep, cfg)
+    assert t.error is None and t.n_fills > 0 and len(t.steps) > 0
+    assert all(abs(s.inventory) <= cfg.inventory_cap + cfg.size_cap for s in t.steps)
+    inv = sum((f["qty"] if f["side"] > 0 else -f["qty"]) for s in t.steps for f in s.fills)
+    cash = -sum((f["qty"] if f["side"] > 0 else -f["qty"]) * f["px"] for s in t.steps for f in s.fills)
+    assert inv == t.final_inventory and abs(cash - t.steps[-1].cash) < 1e-6
+    assert abs(t.total_pnl - (t.realized_pnl + t.unwind_pnl)) < 1e-6
+    idle = C.run_frozen_episode(lambda o, s: {}, ep, cfg)
+    assert idle.n_fills == 0 and idle.total_pnl == 0.0
+    seen = {}
+    C.run_frozen_episode(lambda o, s: seen.setdefault("sig", o["signal"]) and {}, ep, cfg)
+    assert seen["sig"]["mid_mean"] == [1.0, 2.0]
+
+    def bad(o, s):
+        raise RuntimeError("boom")
+    err = C.run_frozen_episode(bad, ep, cfg)
+    assert err.error and "boom" in err.error
+    cmp = C.compare_to_baseline(C.symmetric_touch, [ep], cfg)
+    assert cmp["delta_mean"] == 0.0 and not cmp["errors"]
