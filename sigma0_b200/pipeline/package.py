@@ -6,6 +6,13 @@ not part of this image, so a run is packed into a deterministic tar (sorted
 members, zeroed owners and timestamps) with a SHA-256 manifest of every file;
 ``verify`` re-hashes an archive's members against the manifest and ``unpack``
 restores it (refusing members that would escape the target directory).
+
+``package_run`` binds a finished benchmark run into one archive with the layout of the
+reference's run package (``lobpipeline/pipeline/package_run.py``): ``manifest.json`` (run
+name, the metric names of the scores, the file inventory), ``scores.json`` and the
+predictions under ``predictions/`` copied verbatim, plus a sidecar ``index_<run>.json`` next
+to the archive so consumers can list its contents without opening it.  ``plan_package``
+validates the inputs and computes the paths without touching anything.
 """
 from __future__ import annotations
 
@@ -13,8 +20,10 @@ import hashlib
 import io
 import json
 import os
+import shutil
 import tarfile
-from typing import Dict
+import tempfile
+from typing import Dict, List
 
 MANIFEST = "MANIFEST.sha256.json"
 
@@ -67,3 +76,52 @@ def unpack(archive: str, dest: str) -> None:
             if not target.startswith(dest + os.sep):
                 raise ValueError(f"archive member escapes the target: {m.name}")
         tar.extractall(dest)
+
+
+def plan_package(run_name: str, predictions_root: str, scores_path: str, output_dir: str) -> Dict[str, str]:
+    """The package's paths after checking the inputs (no side effects)."""
+    if not run_name or os.sep in run_name:
+        raise ValueError(f"run_name must be a plain non-empty name, got {run_name!r}")
+    if not os.path.isdir(predictions_root):
+        raise FileNotFoundError(f"predictions directory not found: {predictions_root}")
+    if not os.path.isfile(scores_path):
+        raise FileNotFoundError(f"scores file not found: {scores_path}")
+    return {"run_name": run_name, "predictions_root": os.path.abspath(predictions_root),
+            "scores_path": os.path.abspath(scores_path),
+            "archive": os.path.join(output_dir, f"{run_name}.tar"),
+            "index": os.path.join(output_dir, f"index_{run_name}.json")}
+
+
+def _metric_names(scores) -> List[str]:
+    if isinstance(scores, dict):
+        inner = scores.get("scores", scores)
+        if isinstance(inner, dict):
+            return sorted(str(k) for k in inner)
+    return []
+
+
+def package_run(run_name: str, predictions_root: str, scores_path: str, output_dir: str) -> Dict:
+    """Stage ``manifest.json``, ``scores.json`` and ``predictions/`` and pack them into
+    ``<output_dir>/<run_name>.tar`` (``pack``: deterministic, SHA-256 manifest); write the
+    sidecar index.  Returns the index."""
+    plan = plan_package(run_name, predictions_root, scores_path, output_dir)
+    os.makedirs(output_dir, exist_ok=True)
+    with open(plan["scores_path"]) as f:
+        scores = json.load(f)
+    with tempfile.TemporaryDirectory() as stage:
+        shutil.copytree(plan["predictions_root"], os.path.join(stage, "predictions"))
+        shutil.copyfile(plan["scores_path"], os.path.join(stage, "scores.json"))
+        files = []
+        for d, dirs, fs in os.walk(os.path.join(stage, "predictions")):
+            dirs.sort()
+            files += sorted(os.path.relpath(os.path.join(d, f), stage).replace(os.sep, "/") for f in fs)
+        manifest = {"run_name": run_name, "metric_names": _metric_names(scores), "n_files": len(files),
+                    "files": files}
+        with open(os.path.join(stage, "manifest.json"), "w") as f:
+            json.dump(manifest, f, indent=1, sort_keys=True)
+        hashes = pack(stage, plan["archive"])
+    index = {"run_name": run_name, "archive": os.path.basename(plan["archive"]),
+             "metric_names": manifest["metric_names"], "members": sorted(hashes), "sha256": hashes}
+    with open(plan["index"], "w") as f:
+        json.dump(index, f, indent=1, sort_keys=True)
+    return index

@@ -144,3 +144,23 @@ def test_injection_report_with_reference_arms(tmp_path):
     r["overall_pass"] = 0
     json.dump(r, open(path, "w"))
     assert J.check_report(path) and J.main(["--check", path]) == 1
+
+
+def test_package_run_layout_and_index(run_dir, tmp_path):
+    """A scored run becomes one archive with manifest, scores and predictions, verified by its
+    SHA-256 manifest, plus a sidecar index listing it without opening the archive."""
+    from sigma0_b200.pipeline.lobbench import score_run
+    from sigma0_b200.pipeline.package import package_run, plan_package, unpack, verify
+    scores = tmp_path / "scores.json"
+    scores.write_text(json.dumps(score_run(run_dir, "uncond", n_boot=3)))
+    with pytest.raises(FileNotFoundError):
+        plan_package("r1", str(tmp_path / "nope"), str(scores), str(tmp_path / "pk"))
+    idx = package_run("r1", run_dir, str(scores), str(tmp_path / "pk"))
+    assert idx["archive"] == "r1.tar" and "manifest.json" in idx["members"] and "scores.json" in idx["members"]
+    assert any(m.startswith("predictions/data_gen/") for m in idx["members"]) and idx["metric_names"]
+    arc = str(tmp_path / "pk" / "r1.tar")
+    assert verify(arc) == {"mismatch": [], "missing": [], "extra": []}
+    unpack(arc, str(tmp_path / "out"))
+    man = json.load(open(tmp_path / "out" / "manifest.json"))
+    assert man["run_name"] == "r1" and man["n_files"] == len(man["files"])
+    assert json.load(open(tmp_path / "pk" / "index_r1.json"))["sha256"]["scores.json"]
