@@ -16,9 +16,11 @@ the parameter arrays back with TensorStore from the ``state`` item's ``_METADATA
 
 This module writes that layout with one chunk per array (zarr v2, C order, no compressor or
 zlib) and reads zarr v2 arrays with several chunks, missing chunks (fill value) and the
-``null`` / ``zlib`` / ``gzip`` compressors.  Arrays stored in an OCDBT database
-(``manifest.ocdbt``, Orbax's default since 0.5) or compressed with zstd / blosc are refused
-with a clear error: neither codec exists in this image.
+``null`` / ``zlib`` / ``gzip`` / ``zstd`` compressors, and zarr v3 arrays (``zarr.json``:
+regular chunk grid, ``default`` or ``v2`` chunk keys, the ``transpose`` / ``bytes`` /
+``zstd`` / ``gzip`` / ``crc32c`` codecs; zstd through the system libzstd when the zstandard
+module is absent).  Arrays stored in an OCDBT database (``manifest.ocdbt``) or with the
+``blosc`` codec or ``sharding_indexed`` chunks are refused with a clear error.
 """
 from __future__ import annotations
 
@@ -90,7 +92,82 @@ def _decode(buf: bytes, comp: Optional[dict]) -> bytes:
         return zlib.decompress(buf)
     if cid == "gzip":
         return gzip.decompress(buf)
-    raise OrbaxFormatError(f"compressor {cid!r} is not available in this image (only zlib / gzip / none)")
+    if cid == "zstd":
+        return _zstd_decompress(buf)
+    raise OrbaxFormatError(f"compressor {cid!r} is not available in this image (only zlib / gzip / zstd / none)")
+
+
+def _zstd_decompress(buf: bytes) -> bytes:
+    try:
+        import zstandard
+        return zstandard.ZstdDecompressor().decompressobj().decompress(buf)
+    except ImportError:
+        from ..utils import zstd
+        return zstd.decompress(buf)
+
+
+def read_zarr3(path: str) -> np.ndarray:
+    """A zarr v3 array (``zarr.json``) with a regular chunk grid and non-sharded chunks."""
+    with open(os.path.join(path, "zarr.json")) as f:
+        hdr = json.load(f)
+    if hdr.get("zarr_format") != 3 or hdr.get("node_type", "array") != "array":
+        raise OrbaxFormatError(f"{path}: not a zarr v3 array")
+    grid = hdr["chunk_grid"]
+    if grid.get("name") != "regular":
+        raise OrbaxFormatError(f"{path}: chunk grid {grid.get('name')!r} is not read here")
+    chunks = tuple(grid["configuration"]["chunk_shape"])
+    shape = tuple(hdr["shape"])
+    dt, bf16 = _parse_dtype({"bfloat16": "bfloat16", "float32": "<f4", "float64": "<f8", "float16": "<f2",
+                             "int8": "|i1", "int16": "<i2", "int32": "<i4", "int64": "<i8", "uint8": "|u1",
+                             "uint16": "<u2", "uint32": "<u4", "uint64": "<u8", "bool": "|b1"}.get(
+        hdr["data_type"], hdr["data_type"]))
+    enc = hdr.get("chunk_key_encoding", {"name": "default"})
+    sep = enc.get("configuration", {}).get("separator", "/" if enc.get("name") == "default" else ".")
+    codecs = hdr.get("codecs", [])
+    transpose, endian, byte_codecs = None, "little", []
+    for c in codecs:
+        name, conf = c["name"], c.get("configuration", {})
+        if name == "transpose":
+            transpose = tuple(conf["order"])
+        elif name == "bytes":
+            endian = conf.get("endian", "little")
+        elif name in ("zstd", "gzip", "crc32c"):
+            byte_codecs.append(name)
+        else:
+            raise OrbaxFormatError(f"{path}: zarr v3 codec {name!r} is not supported here")
+    fill = hdr.get("fill_value", 0)
+    out = np.full(shape, 0 if fill in (None, "NaN") else fill, dtype=dt)
+    if fill == "NaN":
+        out[...] = np.nan
+    sdt = dt.newbyteorder(">" if endian == "big" else "<") if dt.itemsize > 1 else dt
+    inner = tuple(chunks[i] for i in transpose) if transpose else chunks
+    n_grid = [-(-s // c) for s, c in zip(shape, chunks)] if shape else []
+    for idx in (np.ndindex(*n_grid) if shape else [()]):
+        if enc.get("name", "default") == "default":
+            key = sep.join(["c"] + [str(i) for i in idx])
+        else:
+            key = sep.join(str(i) for i in idx) if idx else "0"
+        fp = os.path.join(path, *key.split("/"))
+        if not os.path.exists(fp):
+            continue
+        with open(fp, "rb") as f:
+            raw = f.read()
+        for name in reversed(byte_codecs):           # decode in reverse codec order
+            if name == "zstd":
+                raw = _zstd_decompress(raw)
+            elif name == "gzip":
+                raw = gzip.decompress(raw)
+            elif name == "crc32c":
+                raw = raw[:-4]                        # the trailing checksum (not verified here)
+        blk = np.frombuffer(raw, dtype=sdt).astype(dt).reshape(inner if shape else ())
+        if transpose:
+            blk = np.transpose(blk, np.argsort(transpose))
+        if shape:
+            sl = tuple(slice(i * c, min((i + 1) * c, s)) for i, c, s in zip(idx, chunks, shape))
+            out[sl] = blk[tuple(slice(0, x.stop - x.start) for x in sl)]
+        else:
+            out[...] = blk
+    return _bf16_to_f32(out) if bf16 else out
 
 
 def read_zarr(path: str) -> np.ndarray:
@@ -156,8 +233,6 @@ def read_standard_item(item_dir: str, prefix: Optional[str] = None) -> Dict[KeyP
     if os.path.exists(mp):
         with open(mp) as f:
             meta = json.load(f)
-        if meta.get("use_zarr3"):
-            raise OrbaxFormatError(f"{item_dir}: zarr3 arrays are not read here")
         kps = [tuple(ast.literal_eval(k)) for k in meta["tree_metadata"]]
     else:                                           # older layouts: one directory per array
         kps = [tuple(d.split(".")) for d in os.listdir(item_dir)
@@ -169,6 +244,8 @@ def read_standard_item(item_dir: str, prefix: Optional[str] = None) -> Dict[KeyP
         d = os.path.join(item_dir, ".".join(kp))
         if os.path.exists(os.path.join(d, ".zarray")):
             out[kp] = read_zarr(d)
+        elif os.path.exists(os.path.join(d, "zarr.json")):
+            out[kp] = read_zarr3(d)
     return out
 
 

@@ -15,7 +15,7 @@ the book input by zeros, noise or a shuffled copy (seeded per window).
 
 Sources are either in-memory :class:`~sigma0_b200.data.synthetic.SyntheticDay`
 objects or ``.npy`` message/book file pairs (the reference's on-disk layout;
-``.npy.zst`` files load when the ``zstandard`` module is available).
+``.npy.zst`` files are decompressed with the ``zstandard`` module or the system libzstd).
 """
 from __future__ import annotations
 

@@ -157,7 +157,7 @@ def select_levels(wide: np.ndarray, levels: int) -> np.ndarray:
     return wide[..., :4 * levels]
 
 
-_DAY = re.compile(r"^(?P<ticker>[A-Za-z0-9.]+)_(?P<date>\d{4}-\d{2}-\d{2})_.*message.*\.npy$")
+_DAY = re.compile(r"^(?P<ticker>[A-Za-z0-9.]+)_(?P<date>\d{4}-\d{2}-\d{2})_.*message.*\.npy(\.zst)?$")
 
 
 INDEX_NAME = "index.json"
@@ -182,7 +182,8 @@ def build_index(root: str) -> Dict:
         for f in (rel, rel.replace("message", "book")):
             p = os.path.join(root, f)
             if os.path.exists(p):
-                files[f] = list(np.load(p, mmap_mode="r").shape)
+                from .masks import load_npy
+                files[f] = list(load_npy(p).shape)      # a header read for .npy, a decode for .npy.zst
     idx = {"schema": "sigma0_b200.data_index.v1", "shapes": files}
     tmp = os.path.join(root, INDEX_NAME + ".tmp")
     import json

@@ -150,7 +150,7 @@ def ablate_books(book: np.ndarray, mode: str, seed: Sequence[int]) -> np.ndarray
 
 def load_npy(path: str, mmap_mode: Optional[str] = "r") -> np.ndarray:
     """``.npy`` (memory-mapped) or ``.npy.zst``: the plain file wins when both exist; a
-    ``.npy.zst`` alone needs the ``zstandard`` module."""
+    ``.npy.zst`` is decompressed with the ``zstandard`` module, else the system libzstd."""
     plain = path[:-4] if path.endswith(".zst") else path
     import os
     if os.path.exists(plain):
@@ -158,12 +158,13 @@ def load_npy(path: str, mmap_mode: Optional[str] = "r") -> np.ndarray:
     zst = plain + ".zst"
     if not os.path.exists(zst):
         raise FileNotFoundError(plain)
+    import io
     try:
         import zstandard
-    except ImportError as e:
-        raise ImportError(f"{zst} is zstd-compressed and the zstandard module is not installed; "
-                          f"decompress it to {plain} (zstd -d) or install zstandard") from e
-    import io
-    with open(zst, "rb") as f:
-        data = zstandard.ZstdDecompressor().stream_reader(f).read()
+        with open(zst, "rb") as f:
+            data = zstandard.ZstdDecompressor().stream_reader(f).read()
+    except ImportError:                                # the system libzstd through ctypes
+        from ..utils import zstd
+        with open(zst, "rb") as f:
+            data = zstd.decompress(f.read())
     return np.load(io.BytesIO(data))
