@@ -1,7 +1,7 @@
 """Orbax StandardSave layout (zarr v2 arrays under Flax key paths) without Orbax: a model
 round-trips bit-exact through CheckpointManager(fmt="orbax"); a hand-built step directory
 in the documented layout (several chunks, zlib, a missing fill-value chunk, bfloat16, the
-reference's extra items) restores into a LobModel; OCDBT and zstd are refused clearly."""
+reference's extra items) restores into a LobModel; OCDBT and blosc are refused clearly."""
 import json
 import os
 import zlib
