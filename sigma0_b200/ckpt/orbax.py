@@ -18,9 +18,9 @@ This module writes that layout with one chunk per array (zarr v2, C order, no co
 zlib) and reads zarr v2 arrays with several chunks, missing chunks (fill value) and the
 ``null`` / ``zlib`` / ``gzip`` / ``zstd`` compressors, and zarr v3 arrays (``zarr.json``:
 regular chunk grid, ``default`` or ``v2`` chunk keys, the ``transpose`` / ``bytes`` /
-``zstd`` / ``gzip`` / ``crc32c`` codecs; zstd through the system libzstd when the zstandard
-module is absent).  Arrays stored in an OCDBT database (``manifest.ocdbt``) or with the
-``blosc`` codec or ``sharding_indexed`` chunks are refused with a clear error.
+``zstd`` / ``gzip`` / ``crc32c`` codecs, ``sharding_indexed`` shards; zstd through the
+system libzstd when the zstandard module is absent).  Arrays stored in an OCDBT database
+(``manifest.ocdbt``) or with the ``blosc`` codec are refused with a clear error.
 """
 from __future__ import annotations
 
@@ -30,7 +30,7 @@ import json
 import os
 import time
 import zlib
-from typing import Any, Dict, Iterable, Optional, Tuple
+from typing import List, Any, Dict, Iterable, Optional, Tuple
 
 import numpy as np
 
@@ -106,70 +106,6 @@ def _zstd_decompress(buf: bytes) -> bytes:
         return zstd.decompress(buf)
 
 
-def read_zarr3(path: str) -> np.ndarray:
-    """A zarr v3 array (``zarr.json``) with a regular chunk grid and non-sharded chunks."""
-    with open(os.path.join(path, "zarr.json")) as f:
-        hdr = json.load(f)
-    if hdr.get("zarr_format") != 3 or hdr.get("node_type", "array") != "array":
-        raise OrbaxFormatError(f"{path}: not a zarr v3 array")
-    grid = hdr["chunk_grid"]
-    if grid.get("name") != "regular":
-        raise OrbaxFormatError(f"{path}: chunk grid {grid.get('name')!r} is not read here")
-    chunks = tuple(grid["configuration"]["chunk_shape"])
-    shape = tuple(hdr["shape"])
-    dt, bf16 = _parse_dtype({"bfloat16": "bfloat16", "float32": "<f4", "float64": "<f8", "float16": "<f2",
-                             "int8": "|i1", "int16": "<i2", "int32": "<i4", "int64": "<i8", "uint8": "|u1",
-                             "uint16": "<u2", "uint32": "<u4", "uint64": "<u8", "bool": "|b1"}.get(
-        hdr["data_type"], hdr["data_type"]))
-    enc = hdr.get("chunk_key_encoding", {"name": "default"})
-    sep = enc.get("configuration", {}).get("separator", "/" if enc.get("name") == "default" else ".")
-    codecs = hdr.get("codecs", [])
-    transpose, endian, byte_codecs = None, "little", []
-    for c in codecs:
-        name, conf = c["name"], c.get("configuration", {})
-        if name == "transpose":
-            transpose = tuple(conf["order"])
-        elif name == "bytes":
-            endian = conf.get("endian", "little")
-        elif name in ("zstd", "gzip", "crc32c"):
-            byte_codecs.append(name)
-        else:
-            raise OrbaxFormatError(f"{path}: zarr v3 codec {name!r} is not supported here")
-    fill = hdr.get("fill_value", 0)
-    out = np.full(shape, 0 if fill in (None, "NaN") else fill, dtype=dt)
-    if fill == "NaN":
-        out[...] = np.nan
-    sdt = dt.newbyteorder(">" if endian == "big" else "<") if dt.itemsize > 1 else dt
-    inner = tuple(chunks[i] for i in transpose) if transpose else chunks
-    n_grid = [-(-s // c) for s, c in zip(shape, chunks)] if shape else []
-    for idx in (np.ndindex(*n_grid) if shape else [()]):
-        if enc.get("name", "default") == "default":
-            key = sep.join(["c"] + [str(i) for i in idx])
-        else:
-            key = sep.join(str(i) for i in idx) if idx else "0"
-        fp = os.path.join(path, *key.split("/"))
-        if not os.path.exists(fp):
-            continue
-        with open(fp, "rb") as f:
-            raw = f.read()
-        for name in reversed(byte_codecs):           # decode in reverse codec order
-            if name == "zstd":
-                raw = _zstd_decompress(raw)
-            elif name == "gzip":
-                raw = gzip.decompress(raw)
-            elif name == "crc32c":
-                raw = raw[:-4]                        # the trailing checksum (not verified here)
-        blk = np.frombuffer(raw, dtype=sdt).astype(dt).reshape(inner if shape else ())
-        if transpose:
-            blk = np.transpose(blk, np.argsort(transpose))
-        if shape:
-            sl = tuple(slice(i * c, min((i + 1) * c, s)) for i, c, s in zip(idx, chunks, shape))
-            out[sl] = blk[tuple(slice(0, x.stop - x.start) for x in sl)]
-        else:
-            out[...] = blk
-    return _bf16_to_f32(out) if bf16 else out
-
-
 def read_zarr(path: str) -> np.ndarray:
     with open(os.path.join(path, ".zarray")) as f:
         hdr = json.load(f)
@@ -202,6 +138,111 @@ def read_zarr(path: str) -> np.ndarray:
             out[sl] = blk[tuple(slice(0, x.stop - x.start) for x in sl)]
         else:
             out[...] = blk
+    return _bf16_to_f32(out) if bf16 else out
+
+
+_V3_TYPES = {"bfloat16": "bfloat16", "float32": "<f4", "float64": "<f8", "float16": "<f2", "int8": "|i1",
+             "int16": "<i2", "int32": "<i4", "int64": "<i8", "uint8": "|u1", "uint16": "<u2", "uint32": "<u4",
+             "uint64": "<u8", "bool": "|b1"}
+
+
+def _decode_v3(raw: bytes, codecs: List[dict], shape: Tuple[int, ...], dt: np.dtype, path: str) -> np.ndarray:
+    """One chunk through a zarr v3 codec chain (decoded in reverse order)."""
+    transpose, endian, byte_codecs = None, "little", []
+    for c in codecs:
+        name, conf = c["name"], c.get("configuration", {})
+        if name == "transpose":
+            transpose = tuple(conf["order"])
+        elif name == "bytes":
+            endian = conf.get("endian", "little")
+        elif name in ("zstd", "gzip", "crc32c"):
+            byte_codecs.append(name)
+        else:
+            raise OrbaxFormatError(f"{path}: zarr v3 codec {name!r} is not supported here")
+    for name in reversed(byte_codecs):
+        if name == "zstd":
+            raw = _zstd_decompress(raw)
+        elif name == "gzip":
+            raw = gzip.decompress(raw)
+        else:
+            raw = raw[:-4]                            # the trailing crc32c (not verified here)
+    sdt = dt.newbyteorder(">" if endian == "big" else "<") if dt.itemsize > 1 else dt
+    inner = tuple(shape[i] for i in transpose) if transpose else shape
+    blk = np.frombuffer(raw, dtype=sdt).astype(dt).reshape(inner)
+    return np.transpose(blk, np.argsort(transpose)) if transpose else blk
+
+
+def _place(out: np.ndarray, blk: np.ndarray, idx, chunks) -> None:
+    if not out.shape:
+        out[...] = blk
+        return
+    sl = tuple(slice(i * c, min((i + 1) * c, s)) for i, c, s in zip(idx, chunks, out.shape))
+    if any(x.start >= x.stop for x in sl):
+        return
+    out[sl] = blk[tuple(slice(0, x.stop - x.start) for x in sl)]
+
+
+def _shard_chunks(raw: bytes, conf: dict, shard_shape, dt, path: str):
+    """(inner chunk index, decoded inner chunk) of one ``sharding_indexed`` shard: the index is
+    a (n_inner, 2) uint64 array of (offset, nbytes) -- all ones marks an empty chunk -- encoded
+    with ``index_codecs`` at the start or the end of the shard."""
+    inner = tuple(conf["chunk_shape"])
+    grid = [s // c for s, c in zip(shard_shape, inner)]
+    n = int(np.prod(grid)) if grid else 1
+    icodecs = conf.get("index_codecs", [{"name": "bytes", "configuration": {"endian": "little"}},
+                                        {"name": "crc32c"}])
+    isize = 16 * n + (4 if any(c["name"] == "crc32c" for c in icodecs) else 0)
+    at_start = conf.get("index_location", "end") == "start"
+    ibytes = raw[:isize] if at_start else raw[-isize:]
+    index = _decode_v3(ibytes, icodecs, tuple(grid) + (2,), np.dtype("<u8"), path)
+    for j, idx in enumerate(np.ndindex(*grid)):
+        off, nb = int(index[idx][0]), int(index[idx][1])
+        if off == 2 ** 64 - 1 and nb == 2 ** 64 - 1:
+            continue
+        yield idx, _decode_v3(raw[off:off + nb], conf["codecs"], inner, dt, path)
+
+
+def read_zarr3(path: str) -> np.ndarray:
+    """A zarr v3 array (``zarr.json``) with a regular chunk grid, plain or ``sharding_indexed``
+    chunks."""
+    with open(os.path.join(path, "zarr.json")) as f:
+        hdr = json.load(f)
+    if hdr.get("zarr_format") != 3 or hdr.get("node_type", "array") != "array":
+        raise OrbaxFormatError(f"{path}: not a zarr v3 array")
+    grid = hdr["chunk_grid"]
+    if grid.get("name") != "regular":
+        raise OrbaxFormatError(f"{path}: chunk grid {grid.get('name')!r} is not read here")
+    chunks = tuple(grid["configuration"]["chunk_shape"])
+    shape = tuple(hdr["shape"])
+    dt, bf16 = _parse_dtype(_V3_TYPES.get(hdr["data_type"], hdr["data_type"]))
+    enc = hdr.get("chunk_key_encoding", {"name": "default"})
+    sep = enc.get("configuration", {}).get("separator", "/" if enc.get("name", "default") == "default" else ".")
+    codecs = hdr.get("codecs", [])
+    shard = codecs[0] if len(codecs) == 1 and codecs[0]["name"] == "sharding_indexed" else None
+    fill = hdr.get("fill_value", 0)
+    out = np.full(shape, 0 if fill in (None, "NaN") else fill, dtype=dt)
+    if fill == "NaN":
+        out[...] = np.nan
+    n_grid = [-(-s // c) for s, c in zip(shape, chunks)] if shape else []
+    for idx in (np.ndindex(*n_grid) if shape else [()]):
+        if enc.get("name", "default") == "default":
+            key = sep.join(["c"] + [str(i) for i in idx])
+        else:
+            key = sep.join(str(i) for i in idx) if idx else "0"
+        fp = os.path.join(path, *key.split("/"))
+        if not os.path.exists(fp):
+            continue
+        with open(fp, "rb") as f:
+            raw = f.read()
+        if shard is None:
+            _place(out, _decode_v3(raw, codecs, chunks if shape else (), dt, path), idx, chunks)
+            continue
+        conf = shard["configuration"]
+        inner = tuple(conf["chunk_shape"])
+        for j, blk in _shard_chunks(raw, conf, chunks, dt, path):
+            # inner chunk j of shard idx covers the global chunk idx * (shard / inner) + j
+            gidx = tuple(i * (c // k) + jj for i, c, k, jj in zip(idx, chunks, inner, j))
+            _place(out, blk, gidx, inner)
     return _bf16_to_f32(out) if bf16 else out
 
 

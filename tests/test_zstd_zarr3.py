@@ -89,3 +89,45 @@ def test_zarr3_and_zstd_arrays_of_an_orbax_item(tmp_path):
                "fill_value": 0, "order": "C", "filters": None}, open(d2 / ".zarray", "w"))
     (d2 / "0").write_bytes(Z.compress(np.arange(4, dtype=np.float32).tobytes()))
     assert np.array_equal(O.read_zarr(str(d2)), np.arange(4, dtype=np.float32))
+
+
+def test_zarr3_sharded_array(tmp_path):
+    """``sharding_indexed``: one shard file per (4, 4) block holding (2, 2) inner chunks, each
+    zstd-compressed, with the (offset, nbytes) index (crc32c-suffixed) at the shard's end and
+    one inner chunk left empty."""
+    import struct
+    import zlib
+    from sigma0_b200.ckpt import orbax as O
+    a = np.arange(6 * 8, dtype=np.float32).reshape(6, 8)
+    path = tmp_path / "arr"
+    os.makedirs(path)
+    inner_codecs = [{"name": "bytes", "configuration": {"endian": "little"}}, {"name": "zstd", "configuration": {}}]
+    idx_codecs = [{"name": "bytes", "configuration": {"endian": "little"}}, {"name": "crc32c"}]
+    hdr = {"zarr_format": 3, "node_type": "array", "shape": [6, 8], "data_type": "float32",
+           "chunk_grid": {"name": "regular", "configuration": {"chunk_shape": [4, 4]}},
+           "chunk_key_encoding": {"name": "default"}, "fill_value": -1.0,
+           "codecs": [{"name": "sharding_indexed", "configuration": {
+               "chunk_shape": [2, 2], "codecs": inner_codecs, "index_codecs": idx_codecs,
+               "index_location": "end"}}]}
+    json.dump(hdr, open(path / "zarr.json", "w"))
+    want = np.full((6, 8), -1.0, np.float32)
+    for si in range(2):
+        for sj in range(2):
+            body, index = b"", []
+            for ii in range(2):
+                for jj in range(2):
+                    r0, c0 = si * 4 + ii * 2, sj * 4 + jj * 2
+                    if (si, sj, ii, jj) == (1, 1, 0, 1) or r0 >= 6:
+                        index += [2 ** 64 - 1, 2 ** 64 - 1]          # empty inner chunk
+                        continue
+                    blk = a[r0:r0 + 2, c0:c0 + 2]
+                    want[r0:r0 + 2, c0:c0 + 2] = blk
+                    enc = Z.compress(np.ascontiguousarray(blk).tobytes())
+                    index += [len(body), len(enc)]
+                    body += enc
+            ib = struct.pack("<%dQ" % len(index), *index)
+            ib += struct.pack("<I", zlib.crc32(ib))                   # checksum bytes (not verified)
+            fp = path / "c" / str(si) / str(sj)
+            os.makedirs(fp.parent, exist_ok=True)
+            fp.write_bytes(body + ib)
+    assert np.array_equal(O.read_zarr3(str(path)), want)
