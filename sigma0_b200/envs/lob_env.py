@@ -125,7 +125,9 @@ class BaseLOBEnv:
         mid = torch.where(ok, (ap + bp) // 2 // self.tick * self.tick, torch.zeros_like(ap))   # tick-floored
         spread = torch.where(ok, (ap - bp) // self.tick, torch.zeros_like(ap))
         imb = (bv - av).float() / (bv + av).clamp(min=1).float()
-        return {"l2": l2, "mid": mid, "spread": spread, "imbalance": imb,
+        # an empty side of the book makes the step's prices meaningless: the reference reports
+        # it as abort_episode (marl_env.py:360) and so does every observation here
+        return {"l2": l2, "mid": mid, "spread": spread, "imbalance": imb, "abort_episode": ~ok,
                 "time_left": torch.full((self.n,), float(self.max_steps - self.t) / self.max_steps)}
 
     @property

@@ -145,3 +145,17 @@ def test_ippo_ranks_average_gradients_and_stay_identical(tmp_path):
     out = str(tmp_path / "r.pt")
     mp.spawn(_ippo_rank, args=(2, port, out), nprocs=2, join=True)
     assert torch.load(out)["same"]
+
+
+def test_observation_flags_an_empty_book_side():
+    env = MarketMakingEnv(_windows(), n_envs=2, msgs_per_step=5, seed=1)
+    obs = env.reset()
+    assert not obs["abort_episode"].any()
+    # wipe the bid side of env 0 with deletes of every resting bid
+    asks, bids = env.engine.sides()
+    rows = [[3, 1, int(q), int(p), int(oid), 0, 0, 0] for p, q, oid, *_ in bids[0] if q > 0]
+    msgs = torch.zeros(2, len(rows), 8, dtype=torch.int32)
+    msgs[0] = torch.tensor(rows, dtype=torch.int32)
+    env.engine.process(msgs.numpy() if not env.engine.on_gpu else msgs)
+    o = env.observe()
+    assert bool(o["abort_episode"][0]) and not bool(o["abort_episode"][1])
