@@ -254,7 +254,8 @@ class CheckpointManager:
                 with open(os.path.join(d, "state", "_METADATA")) as f:
                     import ast
                     kps = [ast.literal_eval(k) for k in json.load(f)["tree_metadata"]]
-                return all(os.path.exists(os.path.join(d, "state", ".".join(kp), ".zarray")) for kp in kps)
+                return all(any(os.path.exists(os.path.join(d, "state", ".".join(kp), h)) for h in (".zarray", "zarr.json"))
+                           for kp in kps)
             except (OSError, KeyError, ValueError, SyntaxError):
                 return False
         try:

@@ -136,3 +136,26 @@ def test_pinned_checkpoints_detect_drift(tmp_path):
     shutil.rmtree(str(tmp_path / "run" / "6"))
     with pytest.raises(ModelStoreError):
         resolve(store, "sig")
+
+
+def test_checkpoint_inspector(tmp_path, capsys):
+    """The inspector summarises native and Orbax steps (layout, leaves and parameter counts per
+    top-level key, integrity, sampled arrays) and exits non-zero on a damaged step."""
+    import glob
+    import json
+    from sigma0_b200.ckpt.inspect import main, summarize
+    a = _trainer()
+    n_params = sum(p.numel() for p in a.model.parameters())
+    CheckpointManager(str(tmp_path / "nat")).save(2, a, config={"d_model": 64, "architecture": "mamba3"},
+                                                  blocking=True)
+    s = summarize(str(tmp_path / "nat"), sample_arrays=2)
+    assert s["layout"] == "native" and s["intact"] and s["step"] == 2 and s["d_model"] == 64
+    assert s["elements"]["params"] == n_params and len(s["samples"]) == 2 and s["samples"][0]["finite"]
+    CheckpointManager(str(tmp_path / "orb"), fmt="orbax").save(4, a, config={"d_model": 64}, blocking=True)
+    s = summarize(str(tmp_path / "orb" / "4"), sample_arrays=1)
+    assert s["layout"] == "orbax" and s["intact"] and s["elements"]["params"] == n_params
+    assert main([str(tmp_path / "orb"), "--json"]) == 0 and json.loads(capsys.readouterr().out)["step"] == 4
+    victim = sorted(glob.glob(str(tmp_path / "nat" / "2" / "state" / "*.f32")))[0]
+    with open(victim, "r+b") as f:
+        f.write(b"\xff\xff\xff\xff")
+    assert main([str(tmp_path / "nat")]) == 1
