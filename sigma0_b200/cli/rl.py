@@ -11,7 +11,9 @@ The config is a YAML or JSON mapping with the reference's IPPO keys
 ``NUM_AGENTS_PER_TYPE`` order, or one value for all) ``LR``, ``MAX_GRAD_NORM``,
 ``ANNEAL_LR``; ``NUM_AGENTS_PER_TYPE`` = [market makers, executors]; ``AGENT_CONFIGS``
 with a ``MarketMaking`` and an ``Execution`` block in the reference's environment
-config field names; ``MSGS_PER_STEP`` (data messages per environment step).  Keys this
+config field names; ``MSGS_PER_STEP`` (data messages per environment step);
+``world_config`` with ``ep_type`` (``fixed_steps``, or ``fixed_time`` windows of
+``episode_time`` seconds) and ``last_step_seconds``.  Keys this
 runtime does not use (logging, sweeps) are listed in the run record.
 
 Data: ``--data_dir`` (preprocessed ``*_message.npy`` / ``*_book.npy`` day files) or
@@ -30,7 +32,8 @@ import torch
 
 USED = {"NUM_ENVS", "NUM_STEPS", "TOTAL_TIMESTEPS", "UPDATE_EPOCHS", "NUM_MINIBATCHES", "GAMMA", "GAE_LAMBDA",
         "CLIP_EPS", "ENT_COEF", "VF_COEF", "GRU_HIDDEN_DIM", "SEED", "LR", "MAX_GRAD_NORM", "ANNEAL_LR",
-        "NUM_AGENTS_PER_TYPE", "AGENT_CONFIGS", "MSGS_PER_STEP", "AUTOREGRESSIVE"}
+        "NUM_AGENTS_PER_TYPE", "AGENT_CONFIGS", "MSGS_PER_STEP", "AUTOREGRESSIVE", "world_config", "WORLD_CONFIG",
+        "EP_TYPE", "EPISODE_TIME", "LAST_STEP_SECONDS"}
 
 EXEC_CONFIG = {"action_space": "exec_action_space", "reward_function": "exec_reward", "task": "exec_task",
                "task_size": "exec_target", "fixed_quant_value": "exec_clip", "reward_lambda": "exec_lam"}
@@ -49,6 +52,22 @@ def _per_type(v, i: int):
     return v[i] if isinstance(v, (list, tuple)) else v
 
 
+def episode_config(cfg: Dict) -> Dict:
+    """Episode keywords of the environments from the config's ``world_config`` section (the
+    reference's ``jaxob_config.py:233-240`` / ``config_io.py:96``): ``ep_type``
+    (``fixed_steps`` or ``fixed_time``), ``episode_time`` in seconds for fixed-time episodes
+    and ``last_step_seconds``; upper-case top-level keys are accepted too."""
+    world = dict(cfg.get("world_config", {}) or cfg.get("WORLD_CONFIG", {}) or {})
+    ep_type = world.get("ep_type", cfg.get("EP_TYPE", "fixed_steps"))
+    out = {"ep_type": ep_type}
+    if ep_type == "fixed_time":
+        out["episode_time"] = float(world.get("episode_time", cfg.get("EPISODE_TIME", 1800)))
+        lss = world.get("last_step_seconds", cfg.get("LAST_STEP_SECONDS"))
+        if lss is not None:
+            out["last_step_seconds"] = float(lss)
+    return out
+
+
 def build_env(cfg: Dict, windows, device: str = "cpu"):
     """The environment the config describes: market makers only, an executor only, or both
     on the same books."""
@@ -58,7 +77,7 @@ def build_env(cfg: Dict, windows, device: str = "cpu"):
     mm_cfg = dict(agents.get("MarketMaking", {}))
     ex_cfg = dict(agents.get("Execution", {}))
     common = dict(n_envs=int(cfg.get("NUM_ENVS", 8)), msgs_per_step=int(cfg.get("MSGS_PER_STEP", 5)),
-                  seed=int(cfg.get("SEED", 0)), device=device)
+                  seed=int(cfg.get("SEED", 0)), device=device, **episode_config(cfg))
     if n_mm == 0:
         kw = {"target": ex_cfg.pop("task_size", 500), "clip": ex_cfg.pop("fixed_quant_value", 10)}
         for k in ("action_space", "reward_function", "task", "reference_price"):
@@ -103,7 +122,11 @@ def main(argv=None) -> int:
     mps = int(cfg.get("MSGS_PER_STEP", 5))
     from .common import load_days
     days = load_days(a.data_dir, max(1, a.synthetic or 4), steps * mps * 4 + 1, int(cfg.get("SEED", 0)))
-    windows = windows_from_days(days, length=steps * mps)
+    ep = episode_config(cfg)
+    if ep["ep_type"] == "fixed_time":
+        windows = windows_from_days(days, length=int(ep["episode_time"]), ep_type="fixed_time", msgs_per_step=mps)
+    else:
+        windows = windows_from_days(days, length=steps * mps)
     env = build_env(cfg, windows, a.device)
     from ..envs.ippo import _groups, train_ippo
     types = [g.name for g in _groups(env)]

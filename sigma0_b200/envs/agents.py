@@ -271,10 +271,11 @@ EXEC_COMPLEX = ((0, 0),) + tuple((lvl, m) for m in (1, 2, 5) for lvl in range(4)
 
 
 def exec_orders(space: str, action: torch.Tensor, st: Dict[str, torch.Tensor], remaining: torch.Tensor,
-                clip: int, steps_left: int, sell, tick: int):
+                clip: int, steps_left, sell, tick: int):
     """(resting orders (n, K, 3), marketable qty (n,)) of an executor working ``remaining``
     shares; the far touch is the price that trades now (the ask for a buyer).  ``sell`` is a
-    bool or a per-environment bool tensor."""
+    bool or a per-environment bool tensor; ``steps_left`` an int or a per-environment tensor
+    (this step included)."""
     bb, ba, mid = st["best_bid"], st["best_ask"], st["mid"]
     sell = torch.as_tensor(sell, dtype=torch.bool).expand(mid.shape)
     near = torch.where(sell, ba, bb)
@@ -314,7 +315,7 @@ def exec_orders(space: str, action: torch.Tensor, st: Dict[str, torch.Tensor], r
         take = torch.where(a == 1, one * clip, zero)
         orders = _rows((zero, zero, zero))
     elif space == "twap":
-        take = -(-remaining // max(steps_left, 1))
+        take = -(-remaining // torch.as_tensor(steps_left).clamp(min=1))
         orders = _rows((zero, zero, zero))
     else:
         raise ValueError(f"unknown execution action space {space!r}; one of {EXEC_ACTION_SPACES}")

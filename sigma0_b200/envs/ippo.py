@@ -170,9 +170,13 @@ def train_ippo(env, iterations: int = 10, cfg: PPOConfig = PPOConfig(), seed: in
         obs = env.reset()
         n = env.n
         hs = {g.name: torch.zeros(n * g.n_agents, cfg.hidden) for g in groups}
-        buf = {g.name: {"x": [], "h": [], "a": [], "lp": [], "v": [], "r": []} for g in groups}
+        buf = {g.name: {"x": [], "h": [], "a": [], "lp": [], "v": [], "r": [], "live": [], "end": []}
+               for g in groups}
         with torch.no_grad():
             while not env.done:
+                # environments of different episode lengths (fixed-time episodes): a finished
+                # one is frozen; its samples are left out and its value is not bootstrapped
+                alive = ~env.ended if hasattr(env, "ended") else torch.ones(n, dtype=torch.bool)
                 acts = {}
                 for g in groups:
                     x = _obs(env, obs, g).reshape(n * g.n_agents, -1)
@@ -183,8 +187,11 @@ def train_ippo(env, iterations: int = 10, cfg: PPOConfig = PPOConfig(), seed: in
                     hs[g.name] = h2
                     acts[g.name] = _to_env(a, g, n, single)
                 obs, r, _ = _step(env, acts)
+                end = env.ended if hasattr(env, "ended") else torch.zeros(n, dtype=torch.bool)
                 for g in groups:
                     buf[g.name]["r"].append(r[:, g.cols].reshape(-1).float())
+                    buf[g.name]["live"].append(alive[:, None].expand(n, g.n_agents).reshape(-1))
+                    buf[g.name]["end"].append(end[:, None].expand(n, g.n_agents).reshape(-1).float())
         rec = {"iteration": it}
         for g in groups:
             b, pol, opt = buf[g.name], pols[g.name], opts[g.name]
@@ -192,25 +199,33 @@ def train_ippo(env, iterations: int = 10, cfg: PPOConfig = PPOConfig(), seed: in
             vals, rews = torch.stack(b["v"]), torch.stack(b["r"])
             adv = torch.zeros_like(rews)
             last = torch.zeros_like(rews[0])
+            ends = torch.stack(b["end"])
             for t in reversed(range(T)):
-                nv = vals[t + 1] if t + 1 < T else torch.zeros_like(vals[t])
-                last = rews[t] + cfg.gamma * nv - vals[t] + cfg.gamma * cfg.lam * last
+                cont = 1.0 - ends[t]                       # no bootstrap past an episode's end
+                nv = vals[t + 1] * cont if t + 1 < T else torch.zeros_like(vals[t])
+                last = rews[t] + cfg.gamma * nv - vals[t] + cfg.gamma * cfg.lam * cont * last
                 adv[t] = last
-            ret = (adv + vals).reshape(-1)
-            advn = ((adv - adv.mean()) / (adv.std() + 1e-8)).reshape(-1)
-            X, H = torch.stack(b["x"]).reshape(T * n * g.n_agents, -1), torch.stack(b["h"]).reshape(-1, cfg.hidden)
-            ACT, LP = torch.stack(b["a"]).reshape(-1, len(g.dims)), torch.stack(b["lp"]).reshape(-1)
+            keep = torch.stack(b["live"]).reshape(-1)
+            ret = (adv + vals).reshape(-1)[keep]
+            a_k = adv.reshape(-1)[keep]
+            advn = (a_k - a_k.mean()) / (a_k.std() + 1e-8)
+            X, H = torch.stack(b["x"]).reshape(T * n * g.n_agents, -1)[keep], \
+                torch.stack(b["h"]).reshape(-1, cfg.hidden)[keep]
+            ACT, LP = torch.stack(b["a"]).reshape(-1, len(g.dims))[keep], torch.stack(b["lp"]).reshape(-1)[keep]
             N = X.shape[0]
-            mb = max(1, N // max(1, cfg.minibatches))
             for _ in range(cfg.epochs):
                 perm = torch.randperm(N)
-                for s in range(0, N, mb):
-                    i = perm[s:s + mb]
-                    _, lp, ent, v, _ = pol(X[i], H[i], ACT[i])
-                    ratio = torch.exp(lp - LP[i])
-                    a = advn[i]
-                    pg = -torch.min(ratio * a, ratio.clamp(1 - cfg.clip, 1 + cfg.clip) * a).mean()
-                    loss = pg + cfg.vf_coef * ((v - ret[i]) ** 2).mean() - cfg.ent_coef * ent.mean()
+                # exactly NUM_MINIBATCHES updates per epoch on every rank (their sample counts
+                # differ with fixed-time episodes; the gradient all-reduce needs equal counts)
+                for i in torch.tensor_split(perm, max(1, cfg.minibatches)):
+                    if i.numel() == 0:
+                        loss = sum(p.sum() * 0.0 for p in pol.parameters())
+                    else:
+                        _, lp, ent, v, _ = pol(X[i], H[i], ACT[i])
+                        ratio = torch.exp(lp - LP[i])
+                        a = advn[i]
+                        pg = -torch.min(ratio * a, ratio.clamp(1 - cfg.clip, 1 + cfg.clip) * a).mean()
+                        loss = pg + cfg.vf_coef * ((v - ret[i]) ** 2).mean() - cfg.ent_coef * ent.mean()
                     opt.zero_grad()
                     loss.backward()
                     if world > 1:
@@ -221,7 +236,7 @@ def train_ippo(env, iterations: int = 10, cfg: PPOConfig = PPOConfig(), seed: in
                     nn.utils.clip_grad_norm_(pol.parameters(), scheds[g.name]["max_grad_norm"])
                     opt.step()
             rec[f"{g.name}_mean_return"] = float(rews.sum(0).mean())
-            rec[f"{g.name}_loss"] = float(loss)
+            rec[f"{g.name}_loss"] = float(loss.detach())
         # the first type's numbers under the plain keys
         rec["mean_return"], rec["loss"] = rec[f"{groups[0].name}_mean_return"], rec[f"{groups[0].name}_loss"]
         hist.append(rec)

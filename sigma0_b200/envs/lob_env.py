@@ -51,29 +51,66 @@ class EnvWindow:
     t0: tuple                  # (sec, ns) of the first message
 
 
-def windows_from_days(days, length: int, stride: Optional[int] = None) -> List[EnvWindow]:
+def windows_from_days(days, length: int, stride: Optional[int] = None, ep_type: str = "fixed_steps",
+                      msgs_per_step: int = 1) -> List[EnvWindow]:
+    """Episode windows of the days' message streams, each with the book before its first
+    message.  ``fixed_steps``: ``length`` messages every ``stride`` (default ``length``).
+    ``fixed_time``: the messages of consecutive ``length``-second intervals from the day's
+    first second, each cut to a whole number of ``msgs_per_step`` steps (intervals with less
+    than one step are left out), so windows differ in length (the reference's
+    ``matching_engine/jaxlobster/lobster_loader.py:415-490``)."""
+    if ep_type not in ("fixed_steps", "fixed_time"):
+        raise ValueError("ep_type is fixed_steps or fixed_time")
     out = []
     for d in days:
-        n = d.engine_msgs.shape[0]
-        for s in range(0, n - length + 1, stride or length):
-            out.append(EnvWindow(d.engine_msgs[s:s + length], np.asarray(d.books[s, 3:], np.int64),
+        msgs = d.engine_msgs
+        n = msgs.shape[0]
+        if ep_type == "fixed_steps":
+            starts = [(s, s + length) for s in range(0, n - length + 1, stride or length)]
+        else:
+            sec = msgs[:, 6].astype(np.int64)
+            edges = np.arange(int(sec[0]), int(sec[-1]) + 1 + length, length)
+            cut = np.searchsorted(sec, edges, side="left")
+            starts = []
+            for lo, hi in zip(cut[:-1], cut[1:]):
+                hi = lo + (hi - lo) // msgs_per_step * msgs_per_step
+                if hi > lo:
+                    starts.append((int(lo), int(hi)))
+        for s, e in starts:
+            out.append(EnvWindow(msgs[s:e], np.asarray(d.books[s, 3:], np.int64),
                                  (int(d.books[s, 1]), int(d.books[s, 2]))))
     return out
 
 
 class BaseLOBEnv:
-    """Replays data windows through batched books; agents add their own messages."""
+    """Replays data windows through batched books; agents add their own messages.
+
+    ``ep_type="fixed_steps"`` (default): every episode runs the same number of steps, the
+    shortest window's.  ``ep_type="fixed_time"``: the windows are ``episode_time``-second
+    intervals of different lengths (``windows_from_days(..., ep_type="fixed_time")``); each
+    environment runs its own window's steps, ``time_left`` is the fraction of
+    ``episode_time`` left on the data clock, an environment whose window has run out is
+    frozen (no data, its agents' messages dropped, zero reward) until all have ended, and its
+    last step comes at the end of its window or once at most ``last_step_seconds`` are left
+    (the reference's ``exec_env.py:1350-1356``)."""
 
     def __init__(self, windows: Sequence[EnvWindow], n_envs: int, msgs_per_step: int = 5, n_agents: int = 0,
                  cfg: EngineConfig = EngineConfig(n_trades=128, n_orders=128), device="cpu", tick: int = 100,
-                 seed: int = 0):
+                 seed: int = 0, ep_type: str = "fixed_steps", episode_time: Optional[float] = None,
+                 last_step_seconds: float = 5.0):
+        if ep_type not in ("fixed_steps", "fixed_time"):
+            raise ValueError("ep_type is fixed_steps or fixed_time")
+        if ep_type == "fixed_time" and not episode_time:
+            raise ValueError("fixed_time episodes need episode_time (seconds)")
         self.windows, self.n, self.k = list(windows), n_envs, msgs_per_step
         self.n_agents, self.cfg, self.tick = n_agents, cfg, tick
+        self.ep_type, self.episode_time, self.last_step_seconds = ep_type, episode_time, last_step_seconds
         self.dev = torch.device(device)
         self.rng = np.random.default_rng(seed)
         self.engine = BatchedEngine(n_envs, cfg, device=device)
-        L = min(w.engine_msgs.shape[0] for w in self.windows)
-        self.max_steps = L // msgs_per_step
+        lens = [w.engine_msgs.shape[0] for w in self.windows]
+        self.max_steps = (max(lens) if ep_type == "fixed_time" else min(lens)) // msgs_per_step
+        self.steps_env = torch.full((n_envs,), self.max_steps, dtype=torch.long)
 
     # -- episode control ------------------------------------------------------------------
     def reset(self, idx: Optional[Sequence[int]] = None):
@@ -84,13 +121,53 @@ class BaseLOBEnv:
         self.engine.reset()
         init = np.stack([init_msgs_from_l2(w.l2_start, self.cfg, w.t0) for w in ws])
         self.engine.process(init)
-        T = self.max_steps * self.k
-        self.data = torch.from_numpy(np.stack([w.engine_msgs[:T] for w in ws]).astype(np.int32))
+        if self.ep_type == "fixed_time":
+            self.steps_env = torch.tensor([w.engine_msgs.shape[0] // self.k for w in ws], dtype=torch.long)
+            T = int(self.steps_env.max()) * self.k
+            data = np.zeros((self.n, T, 8), np.int32)          # zero rows are no-ops
+            for i, w in enumerate(ws):
+                m = int(self.steps_env[i]) * self.k
+                data[i, :m] = w.engine_msgs[:m]
+            self.data = torch.from_numpy(data)
+        else:
+            T = self.max_steps * self.k
+            self.data = torch.from_numpy(np.stack([w.engine_msgs[:T] for w in ws]).astype(np.int32))
         self.t = 0
         self.last_data = torch.zeros(self.n, self.k, 8, dtype=torch.int32)
         self.clock = torch.from_numpy(np.array([w.t0 for w in ws], dtype=np.int64))
+        self.t_start = self.clock.clone()
+        self.prev_ended = torch.zeros(self.n, dtype=torch.bool)
         self._clear_trades()
         return self.observe()
+
+    def elapsed_seconds(self) -> torch.Tensor:
+        """(n,) data-clock seconds since each episode's first message."""
+        d = self.clock - self.t_start
+        return d[:, 0].double() + d[:, 1].double() * 1e-9
+
+    def time_left(self) -> torch.Tensor:
+        """(n,) fraction of the episode left: steps for ``fixed_steps``, the data clock
+        against ``episode_time`` for ``fixed_time``."""
+        if self.ep_type == "fixed_time":
+            return ((self.episode_time - self.elapsed_seconds()) / self.episode_time).clamp(0.0, 1.0).float()
+        return torch.full((self.n,), float(self.max_steps - self.t) / self.max_steps)
+
+    def steps_left(self) -> torch.Tensor:
+        """(n,) steps left in each environment's episode, this one included."""
+        return (self.steps_env - self.t).clamp(min=0)
+
+    def last_step(self) -> torch.Tensor:
+        """(n,) True where the coming step is the episode's last."""
+        last = self.steps_env - self.t == 1
+        if self.ep_type == "fixed_time":
+            live = self.t < self.steps_env
+            last |= live & (self.episode_time - self.elapsed_seconds() <= self.last_step_seconds)
+        return last
+
+    @property
+    def ended(self) -> torch.Tensor:
+        """(n,) True for environments whose episode is over."""
+        return self.t >= self.steps_env
 
     def _clear_trades(self):
         if self.engine.on_gpu:
@@ -104,18 +181,21 @@ class BaseLOBEnv:
         """agent_msgs (n, m, 8) or None; returns (trades (n, n_trades, 8) int64, data msgs of the step)."""
         self._clear_trades()
         data = self.data[:, self.t * self.k:(self.t + 1) * self.k]
+        over = self.ended
+        self.prev_ended = over
         # agent messages take the timestamp of the step's first data message
         if agent_msgs is not None and agent_msgs.shape[1]:
             am = agent_msgs.clone().to(torch.int32).cpu()
             am[:, :, 6] = data[:, :1, 6]
             am[:, :, 7] = data[:, :1, 7]
+            am[over] = 0                                    # a finished episode stays frozen
             msgs = torch.cat([am, data], 1)
         else:
             msgs = data
         self.engine.process(msgs.to(self.engine.device) if self.engine.on_gpu else msgs)
         self.last_data = data
         self.t += 1
-        self.clock = data[:, -1, 6:8].long()
+        self.clock = torch.where(over[:, None], self.clock, data[:, -1, 6:8].long())
         return torch.from_numpy(self.engine.trade_rows()), data
 
     def observe(self) -> Dict[str, torch.Tensor]:
@@ -128,11 +208,11 @@ class BaseLOBEnv:
         # an empty side of the book makes the step's prices meaningless: the reference reports
         # it as abort_episode (marl_env.py:360) and so does every observation here
         return {"l2": l2, "mid": mid, "spread": spread, "imbalance": imb, "abort_episode": ~ok,
-                "time_left": torch.full((self.n,), float(self.max_steps - self.t) / self.max_steps)}
+                "time_left": self.time_left()}
 
     @property
     def done(self) -> bool:
-        return self.t >= self.max_steps
+        return bool(self.ended.all())
 
     @staticmethod
     def fills(trades: torch.Tensor, tid: int):
@@ -199,8 +279,7 @@ class _Quoting:
     def _state(self, inv: torch.Tensor) -> Dict[str, torch.Tensor]:
         from .agents import touch
         bb, ba, mid = touch(self.engine.l2(1).long().cpu(), self.tick)
-        return {"best_bid": bb, "best_ask": ba, "mid": mid, "inventory": inv,
-                "time_left": torch.full((self.n,), float(self.max_steps - self.t) / self.max_steps)}
+        return {"best_bid": bb, "best_ask": ba, "mid": mid, "inventory": inv, "time_left": self.time_left()}
 
 
 class MarketMakingEnv(_Quoting, BaseLOBEnv):
@@ -342,14 +421,15 @@ class MarketMakingEnv(_Quoting, BaseLOBEnv):
         valid = trades[..., 0] >= 0
         step_volume = torch.where(valid, trades[..., 1].abs(), torch.zeros_like(trades[..., 1])).sum(-1)
         self.unwound = torch.zeros(self.n, self.n_mm, dtype=torch.long)
+        fin = self.ended & ~self.prev_ended              # episodes that ended with this step
         for a, tid in enumerate(self.tids):
             bq, bv, sq, sv = agent_trades(trades, tid)
             traded = bq + sq
             inv_prev = self.inv[:, a].clone()
-            if self.unwind != "none" and self.done:
+            if self.unwind != "none" and bool(fin.any()):
                 # the last step flattens what is left with one artificial fill
-                ubq, ubv, usq, usv = unwind_fill(self.unwind, inv_prev + bq - sq, mid0, obs["mid"], bb, ba, self.tick,
-                                                 self.unwind_pen)
+                u = unwind_fill(self.unwind, inv_prev + bq - sq, mid0, obs["mid"], bb, ba, self.tick, self.unwind_pen)
+                ubq, ubv, usq, usv = (torch.where(fin, x, torch.zeros_like(x)) for x in u)
                 bq, bv, sq, sv = bq + ubq, bv + ubv, sq + usq, sv + usv
                 self.unwound[:, a] = usq - ubq
             self.inv[:, a] += bq - sq
@@ -377,6 +457,7 @@ class MarketMakingEnv(_Quoting, BaseLOBEnv):
                     wide |= (spread0 * self.tick).double() > 0.1 * mid0.double()
                 r = torch.where(wide, torch.zeros_like(r), r)
             rew[:, a] = r
+        rew[self.prev_ended] = 0.0                       # frozen episodes earn nothing
         return rew
 
     def step(self, actions: torch.Tensor):
@@ -441,12 +522,11 @@ class ExecutionEnv(_Quoting, BaseLOBEnv):
         sell = self.sell
         rem = (self.target - self.done_qty).clamp(min=0)
         st = self._state(self.done_qty)
-        steps_left = self.max_steps - self.t
-        orders, take = exec_orders(self.space, actions, st, rem, self.clip, steps_left, sell, self.tick)
-        last = self.t == self.max_steps - 1
-        if last and self.end_fn == "sweep":
-            take = rem                                    # the last step sweeps what is left
-            orders = torch.zeros_like(orders)
+        orders, take = exec_orders(self.space, actions, st, rem, self.clip, self.steps_left(), sell, self.tick)
+        last = self.last_step()
+        if self.end_fn == "sweep":
+            take = torch.where(last, rem, take)           # the last step sweeps what is left
+            orders = torch.where(last[:, None, None], torch.zeros_like(orders), orders)
         sgn = torch.where(sell, -1, 1)
         market = torch.stack([sgn * (take > 0), take], -1)
         mid0 = st["mid"]
@@ -457,8 +537,8 @@ class ExecutionEnv(_Quoting, BaseLOBEnv):
         bb, ba, _ = touch(o["l2"], self.tick)
         mid_avg = (mid0 + o["mid"]) // 2
         unwound = torch.zeros_like(filled)
-        if last and self.end_fn == "unwind":
-            left = (rem - filled).clamp(min=0)
+        if self.end_fn == "unwind" and bool(last.any()):
+            left = torch.where(last, (rem - filled).clamp(min=0), torch.zeros_like(filled))
             pen = self.doom_pen * self.tick
             if self.ref_price == "mid":
                 px = torch.where(sell, mid_avg - pen, mid_avg + pen)
@@ -479,15 +559,17 @@ class ExecutionEnv(_Quoting, BaseLOBEnv):
         rew = exec_reward(self.reward_fn, filled=filled, value=value, market_q=mq, market_v=mv,
                           arrival=self.arrival, target=self.target, sell=sell, tick=self.tick, lam=self.lam,
                           remaining=left, mid_avg=mid_avg, scaling=self.scaling)
+        live = ~self.prev_ended
+        rew = torch.where(live, rew, torch.zeros_like(rew))
         # step statistics and their running means (exec_env.py:1700-1760)
         d = torch.float64
         sg = torch.where(sell, 1.0, -1.0).to(d)
         vwap = torch.where(mq > 0, mv.to(d) / mq.clamp(min=1).to(d), mid_avg.to(d)) / self.tick
         adv = sg * (value.to(d) / self.tick - vwap * filled.to(d))
         drift = sg * filled.to(d) * (vwap - self.arrival.to(d) / self.tick)
-        k = float(self.t)
+        k = torch.minimum(torch.full_like(self.steps_env, self.t), self.steps_env).clamp(min=1).to(d)
         for key, v in (("vwap_rm", vwap), ("advantage_rm", adv), ("drift_rm", drift), ("slippage_rm", adv + drift)):
-            self.info[key] = self.info[key] + (v - self.info[key]) / k
+            self.info[key] = torch.where(live, self.info[key] + (v - self.info[key]) / k, self.info[key])
         self.info.update(quant_left=left, doom_quant=unwound, p_vwap=vwap, advantage=adv, drift=drift)
         o["remaining"] = self.target - self.done_qty
         o["is_sell"] = sell.clone()
@@ -544,15 +626,15 @@ class MultiAgentEnv(MarketMakingEnv):
     def _exec_messages(self, exec_actions: torch.Tensor) -> List[torch.Tensor]:
         from .agents import exec_orders
         rows = []
-        last = self.t == self.max_steps - 1
+        last = self.last_step()
         for e in range(self.n_exec):
             rem = (self.exec_target - self.exec_done[:, e]).clamp(min=0)
             st = self._state(self.exec_done[:, e])
             sell = self.exec_sell[:, e]
             orders, take = exec_orders(self.exec_space, exec_actions[:, e], st, rem, self.exec_clip,
-                                       self.max_steps - self.t, sell, self.tick)
-            if last:
-                take, orders = rem, torch.zeros_like(orders)
+                                       self.steps_left(), sell, self.tick)
+            take = torch.where(last, rem, take)            # the last step sweeps what is left
+            orders = torch.where(last[:, None, None], torch.zeros_like(orders), orders)
             market = torch.stack([torch.where(sell, -1, 1) * (take > 0), take], -1)
             rows += self._order_messages(self.n_mm + e, self.exec_tids[e], orders, market)
         return rows
@@ -607,6 +689,7 @@ class MultiAgentEnv(MarketMakingEnv):
                                        arrival=self.exec_arrival, target=self.exec_target, sell=sell,
                                        tick=self.tick, lam=self.exec_lam, remaining=left,
                                        mid_avg=(obs0["mid"] + obs["mid"]) // 2)
+            er[self.prev_ended] = 0.0
             rew = torch.cat([rew, er], 1)
         return self._obs(obs), rew, self.done
 

@@ -157,3 +157,20 @@ def test_rl_runtime_reads_the_reference_ippo_keys(tmp_path):
     rec = json.loads((tmp_path / "out" / "history.json").read_text())
     assert rec["agent_types"] == ["mm", "exe"] and rec["iterations"] == 2 and rec["unused_config"] == ["WANDB_MODE"]
     assert (tmp_path / "out" / "policy_mm.pt").exists() and (tmp_path / "out" / "policy_exe.pt").exists()
+
+
+def test_rl_runtime_fixed_time_episodes(tmp_path):
+    """``world_config: {ep_type: fixed_time, episode_time}`` cuts the days into time windows and
+    trains on environments whose episodes differ in length."""
+    import json
+    from sigma0_b200.cli import rl
+    cfg = {"NUM_ENVS": 3, "NUM_STEPS": 4, "TOTAL_TIMESTEPS": 24, "UPDATE_EPOCHS": 1, "NUM_MINIBATCHES": 3,
+           "GRU_HIDDEN_DIM": 8, "SEED": 1, "NUM_AGENTS_PER_TYPE": [1, 0], "MSGS_PER_STEP": 4,
+           "world_config": {"ep_type": "fixed_time", "episode_time": 1, "last_step_seconds": 0}}
+    assert rl.episode_config(cfg) == {"ep_type": "fixed_time", "episode_time": 1.0, "last_step_seconds": 0.0}
+    assert rl.episode_config({}) == {"ep_type": "fixed_steps"}
+    path = tmp_path / "ippo.json"
+    path.write_text(json.dumps(cfg))
+    assert rl.main(["--config", str(path), "--synthetic", "2", "--out", str(tmp_path / "out")]) == 0
+    rec = json.loads((tmp_path / "out" / "history.json").read_text())
+    assert rec["unused_config"] == [] and rec["history"]

@@ -159,3 +159,65 @@ def test_observation_flags_an_empty_book_side():
     env.engine.process(msgs.numpy() if not env.engine.on_gpu else msgs)
     o = env.observe()
     assert bool(o["abort_episode"][0]) and not bool(o["abort_episode"][1])
+
+
+def _timed_day(seed=3, n=600):
+    """A synthetic day whose messages arrive at irregular times over about 30 seconds."""
+    from types import SimpleNamespace
+    d = make_sequences(1, n, seed=seed)[0]
+    rng = np.random.default_rng(seed)
+    t = np.cumsum(rng.exponential(0.05, size=n)) * (1 + 0.8 * np.sin(np.arange(n) / 40.0) ** 2)
+    t = np.maximum.accumulate(t)
+    msgs = d.engine_msgs.copy()
+    msgs[:, 6] = 34200 + t.astype(np.int64)
+    msgs[:, 7] = ((t % 1) * 1e9).astype(np.int64)
+    books = d.books.copy()
+    books[:, 1], books[:, 2] = msgs[:, 6], msgs[:, 7]
+    return SimpleNamespace(engine_msgs=msgs, books=books)
+
+
+def test_fixed_time_episodes():
+    day = _timed_day()
+    k = 5
+    ws = windows_from_days([day], length=3, ep_type="fixed_time", msgs_per_step=k)
+    lens = [w.engine_msgs.shape[0] for w in ws]
+    assert len(set(lens)) > 1 and all(n % k == 0 and n > 0 for n in lens)
+    for w in ws:                                   # one 3-second interval each
+        sec = w.engine_msgs[:, 6]
+        assert (sec - 34200) .min() // 3 == (sec - 34200).max() // 3
+    order = np.argsort(lens)
+    idx = [int(order[0]), int(order[-1]), int(order[len(order) // 2]), int(order[1])]
+    env = MarketMakingEnv(ws, n_envs=4, msgs_per_step=k, seed=1, ep_type="fixed_time", episode_time=3,
+                          unwind_price="mid", last_step_seconds=0.5)
+    obs = env.reset(idx)
+    steps = env.steps_env.clone()
+    assert steps.tolist() == [lens[i] // k for i in idx]
+    assert torch.all(obs["time_left"] <= 1.0)
+    prev_tl = obs["time_left"].clone()
+    n_steps, books_at_end = 0, {}
+    while not env.done:
+        obs, r, _ = env.step(torch.zeros(4, 1, 2, dtype=torch.long))
+        n_steps += 1
+        assert torch.all(obs["time_left"] <= prev_tl + 1e-6)
+        prev_tl = obs["time_left"].clone()
+        for e in range(4):
+            if n_steps == int(steps[e]):
+                books_at_end[e] = obs["l2"][e].clone()
+                assert env.inv[e, 0] == 0                        # the unwind flattened it
+            elif n_steps > int(steps[e]):
+                assert r[e].abs().sum() == 0                     # frozen: no reward
+                assert torch.equal(obs["l2"][e], books_at_end[e])  # and no book change
+    assert n_steps == int(steps.max())
+    # execution: TWAP spreads the target over each environment's own steps; the last step sweeps
+    ex = ExecutionEnv(ws, n_envs=4, msgs_per_step=k, seed=1, ep_type="fixed_time", episode_time=3,
+                      target=200, action_space="twap", task="buy", last_step_seconds=0.0)
+    ex.reset(idx)
+    while not ex.done:
+        _, r, _ = ex.step(torch.zeros(4, dtype=torch.long))
+    assert torch.all(ex.done_qty == 200) and torch.all(ex.info["quant_left"] == 0)
+    try:
+        MarketMakingEnv(ws, n_envs=2, ep_type="fixed_time")
+    except ValueError as e:
+        assert "episode_time" in str(e)
+    else:
+        raise AssertionError("fixed_time without episode_time accepted")
