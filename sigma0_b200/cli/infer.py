@@ -49,6 +49,8 @@ def parse(argv=None):
     p.add_argument("--stock", default="SYN")
     p.add_argument("--date", default="2000-01-01")
     p.add_argument("--n_sequences", type=int, default=8)
+    p.add_argument("--window_starts_file", default=None,
+                   help="JSON of explicit (file_idx, seq_start) windows (python -m sigma0_b200.eval.trade_anchors)")
     p.add_argument("--batch_size", type=int, default=8)
     p.add_argument("--n_cond_msgs", type=int, default=500)
     p.add_argument("--n_gen_msgs", type=int, default=100)
@@ -86,10 +88,19 @@ def main(argv=None):
     need = a.n_cond_msgs + a.n_gen_msgs + 1
     days = load_days(a.data_dir, a.synthetic or a.n_sequences, need, a.seed)
     windows = []
-    for di, d in enumerate(days):
-        for s in range(0, d.msgs.shape[0] - need + 1, need):
-            windows.append((di, s))
-    windows = windows[:a.n_sequences]
+    if a.window_starts_file:
+        from ..data.lobster import resolve_day_files
+        from ..eval.trade_anchors import load_window_starts
+        files = [mf for mf, _ in resolve_day_files(a.data_dir)] if a.data_dir else None
+        windows = load_window_starts(a.window_starts_file, files)
+        for di, s in windows:
+            if not (0 <= di < len(days) and 0 <= s and s + need <= min(days[di].msgs.shape[0] + 1, days[di].books.shape[0])):
+                raise ValueError(f"window ({di}, {s}) does not fit its day")
+    else:
+        for di, d in enumerate(days):
+            for s in range(0, d.msgs.shape[0] - need + 1, need):
+                windows.append((di, s))
+        windows = windows[:a.n_sequences]
     mine = [i for i in range(len(windows)) if i % world == rank]
     for sub in ("data_cond", "data_gen", "data_real"):
         os.makedirs(os.path.join(a.save_dir, sub), exist_ok=True)

@@ -135,3 +135,74 @@ def test_diagnostics_cli_writes_every_breakdown(tmp_path):
     pos = json.load(open(out / "position.json"))
     assert pos["origin"]["experiment"] == "smoke" and pos["c"] == 4
     assert all(v is None or abs(v) < 1e-9 for v in pos["ws_tau"])
+
+
+def test_model_zoo_ce_scores_every_checkpoint_on_one_sample(tmp_path, capsys):
+    """Every complete checkpoint step is scored on the same fixed held-out sample; the record
+    carries CE, accuracy, the iso-CE selection; config drift and missing steps are errors."""
+    from sigma0_b200.cli.train import main as train
+    from sigma0_b200.eval import model_zoo_ce as zoo
+    ck = tmp_path / "ck"
+    assert train(["--preset", "smoke", "--impl", "torch", "--synthetic", "2", "--n_messages", "4", "--micro_bsz",
+                  "2", "--log_every", "1", "--watchdog_timeout", "0", "--ckpt_dir", str(ck), "--steps", "2",
+                  "--save_every", "1"]) == 0
+    out = tmp_path / "zoo.json"
+    base = ["--checkpoint_root", str(ck), "--synthetic", "2", "--batch_size", "2", "--max_batches", "2",
+            "--device", "cpu", "--targets", "9.5,9.0"]
+    assert zoo.main(base + ["--output", str(out), "--expected_architecture", "mamba3"]) == 0
+    rec = json.loads(out.read_text())
+    assert [r["step"] for r in rec["results"]] == [1, 2]
+    assert all(np.isfinite(r["validation_ce"]) and 0 <= r["validation_accuracy"] <= 1 for r in rec["results"])
+    assert rec["selection"]["best_validation"]["step"] in (1, 2) and set(rec["selection"]["iso_ce"]) == {"9.5", "9"}
+    assert rec["validation"]["sequences"] == 4
+    # the same sample every time: a second run of one step reproduces its CE exactly
+    assert zoo.main(base + ["--output", str(tmp_path / "one.json"), "--steps", "2"]) == 0
+    one = json.loads((tmp_path / "one.json").read_text())["results"][0]
+    assert one["validation_ce"] == rec["results"][1]["validation_ce"]
+    with pytest.raises(ValueError, match="missing"):
+        zoo.main(base + ["--output", str(tmp_path / "x.json"), "--steps", "7"])
+    with pytest.raises(ValueError, match="architecture mismatch"):
+        zoo.main(base + ["--output", str(tmp_path / "x.json"), "--expected_architecture", "gdn"])
+    meta = ck / "2" / "metadata" / "metadata"
+    m = json.loads(meta.read_text())
+    m["config"]["d_model"] = 64
+    meta.write_text(json.dumps(m))
+    with pytest.raises(ValueError, match="drift at step 2: d_model"):
+        zoo.main(base + ["--output", str(tmp_path / "x.json")])
+
+
+def test_trade_anchors_feed_inference(tmp_path):
+    """Anchored windows end on a trade, balance the two directions, skip a day stored twice,
+    and inference runs exactly those windows."""
+    from sigma0_b200.cli.infer import main as infer
+    from sigma0_b200.data.lobster import save_day
+    from sigma0_b200.data.synthetic import make_sequences
+    from sigma0_b200.eval import trade_anchors as ta
+    days = make_sequences(3, 300, seed=4)
+    data = tmp_path / "days"
+    save_day(days[0], str(data), "GOOG", "2025-12-01")
+    save_day(days[1], str(data), "GOOG", "2025-12-02")
+    save_day(days[2], str(data), "GOOG", "2025-12-03")
+    dup = days[1]                               # the same session again under another time range
+    np.save(data / "GOOG_2025-12-02_24900000_57900000_message.npy", dup.msgs)
+    np.save(data / "GOOG_2025-12-02_24900000_57900000_book.npy", dup.books)
+    out = tmp_path / "anchors.json"
+    assert ta.main(["--data_dir", str(data), "--out", str(out), "--n_cond_msgs", "6", "--n_gen_msgs", "4",
+                    "--n_samples", "20", "--seed", "1"]) == 0
+    rec = json.loads(out.read_text())
+    files = rec["message_files"]
+    assert len(files) == 4 and rec["distinct_days_drawn_from"] == 3 and len(rec["windows"]) == 20
+    same_day = {i for i, f in enumerate(files) if "2025-12-02" in f}
+    assert len(same_day) == 2 and len(same_day & {i for i, _ in rec["windows"]}) == 1   # one file per day
+    for (i, s), d in zip(rec["windows"], rec["anchor_direction"]):
+        m = np.load(files[i])
+        assert m[s + 5, 1] == 4 and m[s + 5, 2] == d          # the last conditioning message is the trade
+    assert abs(rec["anchor_direction"].count(0) - rec["anchor_direction"].count(1)) <= 2
+    run = tmp_path / "gen"
+    assert infer(["--preset", "smoke", "--impl", "torch", "--data_dir", str(data), "--window_starts_file", str(out),
+                  "--batch_size", "10", "--n_cond_msgs", "6", "--n_gen_msgs", "4", "--sample_top_n", "1",
+                  "--save_dir", str(run)]) == 0
+    got = json.loads((run / "sample_indices_rank0.json").read_text())["windows"]
+    assert got == rec["windows"]
+    cond = sorted(glob.glob(str(run / "data_cond" / "*_message_real_id_*.csv")))
+    assert len(cond) == 20
