@@ -33,7 +33,7 @@ import torch
 USED = {"NUM_ENVS", "NUM_STEPS", "TOTAL_TIMESTEPS", "UPDATE_EPOCHS", "NUM_MINIBATCHES", "GAMMA", "GAE_LAMBDA",
         "CLIP_EPS", "ENT_COEF", "VF_COEF", "GRU_HIDDEN_DIM", "SEED", "LR", "MAX_GRAD_NORM", "ANNEAL_LR",
         "NUM_AGENTS_PER_TYPE", "AGENT_CONFIGS", "MSGS_PER_STEP", "AUTOREGRESSIVE", "world_config", "WORLD_CONFIG",
-        "EP_TYPE", "EPISODE_TIME", "LAST_STEP_SECONDS"}
+        "EP_TYPE", "EPISODE_TIME", "LAST_STEP_SECONDS", "FIXED_ACTIONS"}
 
 EXEC_CONFIG = {"action_space": "exec_action_space", "reward_function": "exec_reward", "task": "exec_task",
                "task_size": "exec_target", "fixed_quant_value": "exec_clip", "reward_lambda": "exec_lam"}
@@ -115,6 +115,10 @@ def main(argv=None) -> int:
     p.add_argument("--synthetic", type=int, default=0)
     p.add_argument("--out", required=True)
     p.add_argument("--device", default="cpu", help="engine device: cpu (oracle) or cuda (batched kernel)")
+    p.add_argument("--baseline_only", action="store_true",
+                   help="no training: every combination of the config's FIXED_ACTIONS per agent type, "
+                        "written to baselines.json / baselines.csv")
+    p.add_argument("--episodes", type=int, default=1, help="episodes per combination with --baseline_only")
     a = p.parse_args(argv)
     cfg = load_config(a.config)
     from ..envs import windows_from_days
@@ -130,6 +134,8 @@ def main(argv=None) -> int:
     env = build_env(cfg, windows, a.device)
     from ..envs.ippo import _groups, train_ippo
     types = [g.name for g in _groups(env)]
+    if a.baseline_only:
+        return _baseline_only(cfg, env, types, a)
     iters = max(1, int(cfg.get("TOTAL_TIMESTEPS", steps * env.n)) // (steps * env.n))
     os.makedirs(a.out, exist_ok=True)
     hist, pol = train_ippo(env, iterations=iters, cfg=ppo_config(cfg, types), seed=int(cfg.get("SEED", 0)),
@@ -140,6 +146,31 @@ def main(argv=None) -> int:
     with open(os.path.join(a.out, "history.json"), "w") as f:
         json.dump({"history": hist, "agent_types": types, "iterations": iters,
                    "unused_config": sorted(k for k in cfg if k not in USED)}, f, indent=1)
+    return 0
+
+
+def _baseline_only(cfg: Dict, env, types: List[str], a) -> int:
+    """FIXED_ACTIONS: a list in agent-type order or a {type: ...} map; per type a list of the
+    actions to try (each an int or one int per action dimension), or one bare int."""
+    from ..envs.baselines import fixed_action_sweep
+    fa = cfg.get("FIXED_ACTIONS")
+    if fa is None:
+        raise ValueError("--baseline_only needs FIXED_ACTIONS in the config")
+    per = fa if isinstance(fa, dict) else {t: fa[i] for i, t in enumerate(types) if i < len(fa)}
+    per = {t: (v if isinstance(v, (list, tuple)) else [v]) for t, v in per.items()}
+    rows = fixed_action_sweep(env, per, episodes=a.episodes)
+    os.makedirs(a.out, exist_ok=True)
+    with open(os.path.join(a.out, "baselines.json"), "w") as f:
+        json.dump({"agent_types": types, "episodes": a.episodes, "rows": rows}, f, indent=1)
+    import csv
+    keys = list(rows[0])
+    with open(os.path.join(a.out, "baselines.csv"), "w", newline="") as f:
+        w = csv.DictWriter(f, fieldnames=keys)
+        w.writeheader()
+        for r in rows:
+            w.writerow({k: (" ".join(map(str, v)) if isinstance(v, list) else v) for k, v in r.items()})
+    for r in rows:
+        print(json.dumps(r), flush=True)
     return 0
 
 

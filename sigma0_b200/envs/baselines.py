@@ -16,7 +16,7 @@
 from __future__ import annotations
 
 import math
-from typing import Callable, Dict
+from typing import Callable, Dict, List, Sequence
 
 import numpy as np
 import torch
@@ -99,3 +99,54 @@ def run_bandit(env, bandit: MultiplicativeWeights, episodes: int = 1) -> Dict[st
         rews.append(total.numpy())
     rews = np.concatenate(rews)
     return {"reward_mean": float(rews.mean()), "weights_max_mean": float(bandit.w.max(-1).values.mean())}
+
+
+def fixed_action_sweep(env, fixed_actions: Dict[str, Sequence], episodes: int = 1) -> List[Dict]:
+    """Every combination of fixed actions across the agent types: the reference's
+    baseline-only evaluation (``environment/jaxrl/MARL/baseline_eval/baseline_only_JAXMARL.py:140-520``,
+    a fixed-action network per type; ``plotting_combinations.py`` tabulates the
+    combinations).  ``fixed_actions`` maps a type (``mm``, ``exe``) to the actions to try,
+    each an int or one int per action dimension; every agent of the type plays it at every
+    step.  One row per combination: the actions and, per type, the mean episode return over
+    agents, environments and episodes (plus the market makers' mean absolute inventory and
+    the executors' mean executed quantity)."""
+    import itertools
+
+    from .ippo import _groups, _step
+    groups = _groups(env)
+    names = [g.name for g in groups]
+    missing = [n for n in names if n not in fixed_actions]
+    if missing:
+        raise ValueError(f"fixed actions needed for the agent types {missing}")
+    choices = [[tuple(np.atleast_1d(a).astype(int).tolist()) for a in fixed_actions[n]] for n in names]
+    for g, cs in zip(groups, choices):
+        for c in cs:
+            if len(c) != len(g.dims) or any(not 0 <= x < d for x, d in zip(c, g.dims)):
+                raise ValueError(f"action {c} does not fit the {g.name} action dimensions {g.dims}")
+    rows = []
+    for combo in itertools.product(*choices):
+        rets = {n: [] for n in names}
+        extra = {"mm_abs_inventory": [], "exe_executed": []}
+        for _ in range(episodes):
+            env.reset()
+            total = None
+            while not env.done:
+                acts = {}
+                for g, c in zip(groups, combo):
+                    a = torch.tensor(c, dtype=torch.long).expand(env.n, g.n_agents, len(c))
+                    a = a[..., 0] if len(c) == 1 else a
+                    acts[g.name] = a[:, 0] if names == ["exe"] else a
+                _, r, _ = _step(env, acts)
+                total = r.double() if total is None else total + r.double()
+            for g in groups:
+                rets[g.name].append(total[:, g.cols].mean().item())
+            if hasattr(env, "inv"):
+                extra["mm_abs_inventory"].append(env.inv.abs().double().mean().item())
+            done = getattr(env, "exec_done", getattr(env, "done_qty", None))
+            if done is not None and "exe" in names:
+                extra["exe_executed"].append(done.double().mean().item())
+        row = {f"{n}_action": list(c) for n, c in zip(names, combo)}
+        row.update({f"{n}_return": float(np.mean(v)) for n, v in rets.items()})
+        row.update({k: float(np.mean(v)) for k, v in extra.items() if v})
+        rows.append(row)
+    return rows

@@ -3,6 +3,7 @@ options on CPU (``sigma0_b200/cli/train.py``)."""
 import json
 import os
 
+import numpy as np
 import pytest
 import torch
 
@@ -174,3 +175,27 @@ def test_rl_runtime_fixed_time_episodes(tmp_path):
     assert rl.main(["--config", str(path), "--synthetic", "2", "--out", str(tmp_path / "out")]) == 0
     rec = json.loads((tmp_path / "out" / "history.json").read_text())
     assert rec["unused_config"] == [] and rec["history"]
+
+
+def test_rl_baseline_only_sweeps_fixed_action_combinations(tmp_path):
+    """``cli rl --baseline_only``: every combination of the per-type fixed actions, one row
+    each with per-type returns, to JSON and CSV."""
+    import json
+    from sigma0_b200.cli import rl
+    cfg = {"NUM_ENVS": 2, "NUM_STEPS": 5, "SEED": 2, "NUM_AGENTS_PER_TYPE": [1, 1], "MSGS_PER_STEP": 4,
+           "AGENT_CONFIGS": {"MarketMaking": {}, "Execution": {"action_space": "fixed_quants_complex",
+                                                               "task_size": 100}},
+           "FIXED_ACTIONS": [[[0, 0], [1, 1], [2, 2]], [0, 4]]}
+    path = tmp_path / "b.json"
+    path.write_text(json.dumps(cfg))
+    out = tmp_path / "out"
+    assert rl.main(["--config", str(path), "--synthetic", "2", "--out", str(out), "--baseline_only"]) == 0
+    rec = json.loads((out / "baselines.json").read_text())
+    assert rec["agent_types"] == ["mm", "exe"] and len(rec["rows"]) == 6
+    assert {tuple(r["mm_action"]) for r in rec["rows"]} == {(0, 0), (1, 1), (2, 2)}
+    assert all(np.isfinite(r["mm_return"]) and np.isfinite(r["exe_return"]) for r in rec["rows"])
+    assert (out / "baselines.csv").read_text().count("\n") == 7
+    cfg["FIXED_ACTIONS"] = [[[0, 99]], [0]]
+    path.write_text(json.dumps(cfg))
+    with pytest.raises(ValueError, match="does not fit"):
+        rl.main(["--config", str(path), "--synthetic", "2", "--out", str(out), "--baseline_only"])
