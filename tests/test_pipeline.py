@@ -164,3 +164,40 @@ def test_package_run_layout_and_index(run_dir, tmp_path):
     man = json.load(open(tmp_path / "out" / "manifest.json"))
     assert man["run_name"] == "r1" and man["n_files"] == len(man["files"])
     assert json.load(open(tmp_path / "pk" / "index_r1.json"))["sha256"]["scores.json"]
+
+
+def test_packed_tree_overlay_resolve_cat_listing(tmp_path):
+    """A packed tree is patched through its overlay (an override, a whiteout) without
+    repacking; ``resolve`` yields the merged directory and cleans up; ``cat`` / ``listing``
+    read the archive without unpacking; a directory resolves to itself."""
+    from sigma0_b200.pipeline import package as pk
+    tree = tmp_path / "run"
+    (tree / "data_gen").mkdir(parents=True)
+    (tree / "data_gen" / "a.csv").write_text("a")
+    (tree / "data_gen" / "b.csv").write_text("b")
+    (tree / "scores.json").write_text("{}")
+    pk.pack(str(tree), pk.image_for(str(tree)))
+    assert pk.listing(pk.image_for(str(tree))) == ["data_gen/a.csv", "data_gen/b.csv", "scores.json"]
+    assert pk.cat(pk.image_for(str(tree)), "data_gen/b.csv") == b"b"
+    with pk.resolve(str(tree)) as d:
+        assert d == str(tree)                                  # a directory is used as it is
+    import shutil
+    shutil.rmtree(tree)
+    pk.overlay_override(str(tree), "data_gen/a.csv", "A2")
+    pk.overlay_exclude(str(tree), "data_gen/b.csv")
+    pk.overlay_override(str(tree), "extra/new.txt", b"n")
+    with pk.resolve(str(tree), tmp_root=str(tmp_path)) as d:
+        got = sorted(os.path.relpath(os.path.join(r, f), d) for r, _, fs in os.walk(d) for f in fs)
+        assert got == ["data_gen/a.csv", "extra/new.txt", "scores.json"]
+        assert open(os.path.join(d, "data_gen", "a.csv")).read() == "A2"
+        merged = d
+    assert not os.path.exists(merged)
+    pk.overlay_override(str(tree), "data_gen/b.csv", "B2")      # an override lifts the whiteout
+    with pk.resolve(pk.image_for(str(tree))) as d:
+        assert open(os.path.join(d, "data_gen", "b.csv")).read() == "B2"
+    assert pk.verify(pk.image_for(str(tree))) == {"mismatch": [], "missing": [], "extra": []}
+    with pytest.raises(FileNotFoundError):
+        with pk.resolve(str(tmp_path / "nothing")):
+            pass
+    with pk.resolve(str(tmp_path / "nothing"), require=False) as d:
+        assert d == str(tmp_path / "nothing")
